@@ -1,0 +1,158 @@
+"""The state-fork visibility equivalence check with fault injection.
+
+Answers with numbers (the reference's `equivalence.py:1-12` contract):
+
+  1. does the noised stream equal the oracle (an unforked forward per block, block-causal mask)?
+  2. does the clean stream equal the unforked block-causal forward?
+  3. perturbation: does x_t block k ignore x_t block k-1 and x_0 block k, and react to x_0 block k-1?
+  4. does every deliberate fault (concat-causal-gdn / mask-leak / no-conv-prefix) turn check 1 red?
+
+Exit 0 = every check passed AND every fault was detected; 1 = a check failed or a fault went
+undetected; 2 = could not measure. The candidate runs through the op layer (CUDA kernels for
+``--device cuda``); the oracle always runs the fp32 reference ops with the token-by-token delta
+rule, on the host when the candidate is on the GPU.
+
+    python -m dllm_qwen38_b200.equivalence [--model tiny] [--block 32 --nblocks 4] [--device cuda]
+"""
+
+from __future__ import annotations
+
+import argparse
+import copy
+import json
+import sys
+import time
+
+import torch
+
+from . import ops
+from .models.blockdiff import FAULTS, BreakMode, block_diffusion_forward
+from .models.oracle import reference_block_logits, reference_clean_logits
+
+
+def _maxdiff(a, b) -> float:
+    return float((a.float().cpu() - b.float().cpu()).abs().max())
+
+
+def run(model, *, block: int, nblocks: int, layers: int | None, tol: float, change_floor: float, seed: int,
+        device: str, oracle_model=None, batch: int = 1, oracle_gdn: str = "recurrent") -> dict:
+    """Checks + faults on `model` (on `device`); the oracle runs on `oracle_model` (default: the
+    same model) on its own device, in fp32 reference ops."""
+    oracle_model = oracle_model or model
+    odev = next(oracle_model.parameters()).device
+    torch.manual_seed(seed)
+    L = block * nblocks
+    vocab = model.config.vocab_size
+    x0 = torch.randint(0, vocab, (batch, L))
+    xt = x0.clone()
+    mask_id = vocab - 1  # visibility does not depend on which id plays [MASK]
+    xt[torch.rand(batch, L) < 0.5] = mask_id
+    dx0, dxt = x0.to(device), xt.to(device)
+
+    def cand(a, b, fault=None):
+        with torch.no_grad():
+            return block_diffusion_forward(model, a.to(device), b.to(device), block, layers=layers, fault=fault)[0]
+
+    checks: list = []
+    t0 = time.time()
+    with torch.no_grad():
+        lt, l0 = block_diffusion_forward(model, dx0, dxt, block, layers=layers)
+        ref_t = reference_block_logits(oracle_model, x0.to(odev), xt.to(odev), block, layers=layers, gdn=oracle_gdn)
+        ref_0 = reference_clean_logits(oracle_model, x0.to(odev), block, layers=layers, gdn=oracle_gdn)
+    impl = ops.last_impl()
+    d = _maxdiff(lt, ref_t)
+    checks.append({"name": "noised-stream-vs-oracle", "max_abs_diff": d, "tol": tol, "pass": d <= tol})
+    d = _maxdiff(l0, ref_0)
+    checks.append({"name": "clean-stream-vs-oracle", "max_abs_diff": d, "tol": tol, "pass": d <= tol})
+    if nblocks >= 2:
+        worst_xt, worst_x0k, weakest = 0.0, 0.0, float("inf")
+        for k in range(1, nblocks):
+            sl, prev = slice(k * block, (k + 1) * block), slice((k - 1) * block, k * block)
+            xt2 = xt.clone()
+            xt2[:, prev] = torch.randint(0, vocab, (batch, block))
+            worst_xt = max(worst_xt, _maxdiff(lt[:, sl], cand(x0, xt2)[:, sl]))
+            x02 = x0.clone()
+            x02[:, sl] = torch.randint(0, vocab, (batch, block))
+            worst_x0k = max(worst_x0k, _maxdiff(lt[:, sl], cand(x02, xt)[:, sl]))
+            x03 = x0.clone()
+            x03[:, prev] = torch.randint(0, vocab, (batch, block))
+            weakest = min(weakest, _maxdiff(lt[:, sl], cand(x03, xt)[:, sl]))
+        checks.append({"name": "xt-block-k-ignores-xt-block-k-1", "max_abs_diff": worst_xt, "tol": tol, "pass": worst_xt <= tol})
+        checks.append({"name": "xt-block-k-ignores-x0-block-k", "max_abs_diff": worst_x0k, "tol": tol, "pass": worst_x0k <= tol})
+        checks.append({"name": "xt-block-k-reacts-to-x0-block-k-1", "min_abs_diff": weakest, "floor": change_floor,
+                       "pass": weakest >= change_floor})
+    faults = []
+    for name in FAULTS:
+        d = _maxdiff(cand(x0, xt, BreakMode(name)), ref_t)
+        faults.append({"fault": name, "max_abs_diff": d, "tol": tol, "detected": d > tol})
+    cfg = model.config
+    n_layers = layers if layers is not None else cfg.num_hidden_layers
+    return {
+        "block": block, "nblocks": nblocks, "seq_len": L, "batch": batch, "layers": n_layers,
+        "layer_types": list(cfg.layer_types[:n_layers]),
+        "dtype": str(model.text_model.embed_tokens.weight.dtype), "device": device,
+        "seconds": round(time.time() - t0, 2), "checks": checks, "faults": faults,
+        "checks_passed": sum(c["pass"] for c in checks), "checks_total": len(checks),
+        "faults_detected": sum(f["detected"] for f in faults), "faults_total": len(faults),
+        "candidate_impl": impl, "oracle": f"reference-ops/{oracle_gdn}",
+    }
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--model", default="tiny", help="preset (tiny, tiny_ref, 0.8b, 27b) or HF checkpoint dir")
+    p.add_argument("--layers", type=int, default=None)
+    p.add_argument("--block", type=int, default=32)
+    p.add_argument("--nblocks", type=int, default=4)
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--tol", type=float, default=None, help="max |dlogit| (default fp32 1e-3, bf16 0.25)")
+    p.add_argument("--change-floor", type=float, default=None, help="default 10 x tol")
+    p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
+    p.add_argument("--device", default="cpu")
+    p.add_argument("--oracle-gdn", default="recurrent", choices=["recurrent", "chunk"])
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--json", default=None)
+    a = p.parse_args(argv)
+    dtype = torch.float32 if a.dtype == "float32" else torch.bfloat16
+    tol = a.tol if a.tol is not None else (1e-3 if dtype == torch.float32 else 0.25)
+    floor = a.change_floor if a.change_floor is not None else 10 * tol
+    if a.nblocks < 1:
+        print("COULD-NOT-MEASURE nblocks < 1", file=sys.stderr)
+        return 2
+    try:
+        from .io.hf_load import load_model, spare_rows
+
+        model, tok = load_model(a.model, dtype=dtype, device=a.device, layers=a.layers, seed=a.seed)
+        spare = spare_rows(model, tok) if tok is not None else None
+    except Exception as e:  # noqa: BLE001
+        print(f"COULD-NOT-MEASURE model load failed: {type(e).__name__}: {e}", file=sys.stderr)
+        return 2
+    if a.layers is not None and a.layers > model.config.num_hidden_layers:
+        print("COULD-NOT-MEASURE --layers exceeds the model", file=sys.stderr)
+        return 2
+    oracle_model = model
+    if a.device != "cpu":  # the oracle runs the fp32 reference ops on the host
+        oracle_model = copy.deepcopy(model).to("cpu", torch.float32)
+    rep = run(model, block=a.block, nblocks=a.nblocks, layers=None, tol=tol, change_floor=floor, seed=a.seed,
+              device=a.device, oracle_model=oracle_model, batch=a.batch, oracle_gdn=a.oracle_gdn)
+    rep["model"] = a.model
+    if spare:
+        rep["vocab"] = spare
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(rep, f, indent=1)
+    for c in rep["checks"]:
+        val = c.get("max_abs_diff", c.get("min_abs_diff"))
+        print(f"{'PASS' if c['pass'] else 'FAIL'}\t{c['name']}\t{val:.3e}")
+    for f in rep["faults"]:
+        print(f"{'DETECTED' if f['detected'] else 'UNDETECTED'}\tfault:{f['fault']}\t{f['max_abs_diff']:.3e}")
+    print(f"CHECKS\t{rep['checks_passed']}/{rep['checks_total']}\tFAULTS-DETECTED\t{rep['faults_detected']}/{rep['faults_total']}"
+          f"\tmodel={rep['model']} layers={rep['layers']} L={rep['seq_len']} dtype={rep['dtype']} oracle={rep['oracle']} {rep['seconds']}s")
+    if spare:
+        print(f"VOCAB\tembedding_rows={spare['embedding_rows']}\ttokenizer_len={spare['tokenizer_len']}\tspare_rows={spare['spare_rows']}")
+    ok = rep["checks_passed"] == rep["checks_total"] and rep["faults_detected"] == rep["faults_total"]
+    return 0 if ok else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,46 @@
+// Python bindings of the sm_100a kernels (one extension module, dllm_qwen38_b200._C).
+#include <torch/extension.h>
+
+namespace bdllm {
+void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
+          int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
+          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha);
+at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu);
+at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode);
+std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
+                                 int64_t block, int64_t mode);
+at::Tensor ce_rows_(at::Tensor& logits, const at::Tensor& tgt);
+void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
+                double b2, double eps, double wd, double coef, double bc1, double bc2);
+int64_t read_error_word(bool reset);
+at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w1, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w1, double eps);
+at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at::Tensor& w, double eps);
+std::vector<at::Tensor> gated_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& z,
+                                          const at::Tensor& w, double eps);
+at::Tensor qk_norm_rope_fwd(const at::Tensor& src, const at::Tensor& w1, const at::Tensor& cs, const at::Tensor& sn,
+                            double eps);
+std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& w1,
+                                         const at::Tensor& cs, const at::Tensor& sn, double eps);
+}  // namespace bdllm
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "dllm_qwen38_b200 sm_100a kernels";
+  m.def("gemm", &bdllm::gemm, "tcgen05 bf16 GEMM with fused epilogues", py::arg("a"), py::arg("a_mn"),
+        py::arg("lda"), py::arg("b"), py::arg("b_mn"), py::arg("ldb"), py::arg("M"), py::arg("N"), py::arg("K"),
+        py::arg("c"), py::arg("ldc"), py::arg("epi"), py::arg("r") = c10::nullopt, py::arg("ldr") = 0,
+        py::arg("gu") = c10::nullopt, py::arg("bn") = 256, py::arg("alpha") = 1.0);
+  m.def("dswiglu", &bdllm::dswiglu);
+  m.def("conv_fwd", &bdllm::conv_fwd);
+  m.def("conv_bwd", &bdllm::conv_bwd);
+  m.def("ce_rows_", &bdllm::ce_rows_);
+  m.def("adamw_step", &bdllm::adamw_step);
+  m.def("rmsnorm_fwd", &bdllm::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &bdllm::rmsnorm_bwd);
+  m.def("gated_rmsnorm_fwd", &bdllm::gated_rmsnorm_fwd);
+  m.def("gated_rmsnorm_bwd", &bdllm::gated_rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &bdllm::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &bdllm::qk_norm_rope_bwd);
+  m.def("read_error_word", &bdllm::read_error_word, "device error word (bounded-wait expiries)",
+        py::arg("reset") = false);
+}

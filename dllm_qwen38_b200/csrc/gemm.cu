@@ -1,0 +1,551 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a: TMA -> shared memory -> tcgen05.mma with
+// the fp32 accumulator in TMEM -> tcgen05.ld epilogue with fused element-wise ops.
+//
+//   C[m, n] = sum_k A(m, k) * B(n, k)
+//
+// Operands are either K-major (A stored [M, K], B stored [N, K]) or MN-major (A stored [K, M],
+// B stored [K, N]); that covers y = x W^T (K,K), dx = dy W (K,MN) and dW = dy^T x (MN,MN)
+// without transposing anything in memory.
+//
+// CTA = 6 warps: warp 0 issues TMA loads, warp 1 allocates TMEM and issues MMAs (one elected
+// lane), warps 2..5 drain TMEM (warp w owns TMEM lanes 32*(w%4)..+31). Tiles 128 x BN x 64,
+// STAGES-deep smem ring, two TMEM accumulators so the epilogue of tile i overlaps the MMAs of
+// tile i+1. One CTA per SM, grid = min(#tiles, #SMs), grouped tile raster for L2 reuse.
+// TMA loads never use cluster multicast.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace bdllm {
+
+enum Epi : int {
+  EPI_BF16 = 0,      // C (bf16) = acc
+  EPI_F32 = 1,       // C (fp32) = acc
+  EPI_ADD_BF16 = 2,  // C (bf16) = acc + R (bf16; R may alias C)
+  EPI_ACC_F32 = 3,   // C (fp32) += acc
+  EPI_SWIGLU = 4,    // B rows [j, F + j] interleaved per tile; C = silu(gate) * up, optional GU store
+};
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int NUM_THREADS = 192;
+
+struct GemmArgs {
+  int M, N, K;       // N = output columns (for SWIGLU: F, the activation width)
+  void* C;           // output
+  int ldc;           // elements
+  const void* R;     // residual (EPI_ADD_BF16)
+  int ldr;
+  __nv_bfloat16* GU;  // SWIGLU: optional [M, 2F] store of (gate | up)
+  int ldgu;
+  int* err;     // device error word
+  float alpha;  // accumulator scale applied before the epilogue op
+};
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+struct Cfg {
+  static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  constexpr int G = 8;  // m-tiles per raster group
+  int group_size = G * tiles_n;
+  int g = t / group_size;
+  int first_m = g * G;
+  int rows = min(G, tiles_m - first_m);
+  int r = t % group_size;
+  tm = first_m + r % rows;
+  tn = r / rows;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs args) {
+  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  constexpr int STAGES = C_::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * C_::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tiles_m = (args.M + BM - 1) / BM;
+  const int tiles_n = (args.N + C_::BN_OUT - 1) / C_::BN_OUT;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);  // one arrive per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C_::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    int stage = 0;
+    uint32_t round = 0;
+    uint32_t armed_mask = 0;  // stages with a load in flight or landed (bit s)
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int m0 = tm * BM, n0 = tn * C_::BN_OUT;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[stage], C_::STAGE_BYTES);
+        armed_mask |= 1u << stage;
+        const int k0 = kb * BK;
+        uint8_t* a_dst = sa + stage * C_::A_BYTES;
+        uint8_t* b_dst = sb + stage * C_::B_BYTES;
+        if constexpr (!A_MN) {
+          tma_load_2d(a_dst, &map_a, &full[stage], k0, m0);
+        } else {
+          tma_load_2d(a_dst, &map_a, &full[stage], m0, k0);
+          tma_load_2d(a_dst + 8192, &map_a, &full[stage], m0 + 64, k0);
+        }
+        if constexpr (EPI == EPI_SWIGLU) {
+          tma_load_2d(b_dst, &map_b, &full[stage], k0, n0);
+          tma_load_2d(b_dst + (BN / 2) * 128, &map_b, &full[stage], k0, args.N + n0);
+        } else if constexpr (!B_MN) {
+          tma_load_2d(b_dst, &map_b, &full[stage], k0, n0);
+        } else {
+#pragma unroll
+          for (int i = 0; i < BN / 64; ++i) tma_load_2d(b_dst + i * 8192, &map_b, &full[stage], n0 + i * 64, k0);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          ++round;
+        }
+      }
+    }
+    if (!ok) {
+      // drain: every load this thread armed must land before the CTA's smem is released. Stage s
+      // was last armed in round (round - 1) if s >= stage, else in the current round.
+      for (int s = 0; s < STAGES; ++s)
+        if (armed_mask & (1u << s))
+          mbar_wait(&full[s], (s < stage ? round : round - 1) & 1, args.err, ERR_GEMM_WAIT, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer
+    int stage = 0;
+    uint32_t round = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = it >> 1;
+      if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], round & 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sa + stage * C_::A_BYTES);
+        const uint32_t b_addr = smem_u32(sb + stage * C_::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          uint64_t ad, bd;
+          if constexpr (!A_MN)
+            ad = smem_desc(a_addr + k * 32, 16, 1024);
+          else
+            ad = smem_desc(a_addr + k * 2048, 8192, 1024);
+          if constexpr (!B_MN || EPI == EPI_SWIGLU)
+            bd = smem_desc(b_addr + k * 32, 16, 1024);
+          else
+            bd = smem_desc(b_addr + k * 2048, 8192, 1024);
+          mma_bf16(d_tmem, ad, bd, C_::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[stage]);  // frees this smem stage once these MMAs have read it
+        if (++stage == STAGES) {
+          stage = 0;
+          ++round;
+        }
+      }
+      if (ok) mma_commit(&tfull[acc]);  // accumulator ready for the epilogue
+    }
+    if (!ok) {
+      // aborted: wait (bounded) until every MMA already issued has finished reading smem and
+      // writing TMEM, so the dealloc below never races an in-flight MMA
+      mma_commit(drain);
+      mbar_wait(drain, 0, args.err, ERR_GEMM_WAIT, nullptr);
+    }
+  } else if (warp >= 2) {
+    // ---------------------------------------------------------------- epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = it >> 1;
+      if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int row = tm * BM + row_in_tile;
+      const int n0 = tn * C_::BN_OUT;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      const bool row_ok = row < args.M;
+#pragma unroll 1
+      for (int c = 0; c < C_::BN_OUT / 32; ++c) {
+        float v[32];
+        tmem_ld32(t_row + c * 32, v);
+        if (args.alpha != 1.f) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
+        }
+        const int col0 = n0 + c * 32;
+        if constexpr (EPI == EPI_SWIGLU) {
+          float u[32];
+          tmem_ld32(t_row + BN / 2 + c * 32, u);
+          if (row_ok) {
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
+            __nv_bfloat16* gu = args.GU ? args.GU + (size_t)row * args.ldgu + col0 : nullptr;
+            if (col0 + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk, pg, pu;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+                __nv_bfloat162* g2 = reinterpret_cast<__nv_bfloat162*>(&pg);
+                __nv_bfloat162* u2 = reinterpret_cast<__nv_bfloat162*>(&pu);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  // the activation uses the bf16-rounded gate/up so that backward (which reads the
+                  // stored bf16 gate/up) differentiates exactly the function forward computed
+                  __nv_bfloat162 gb = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+                  __nv_bfloat162 ub = __floats2bfloat162_rn(u[j + 2 * e], u[j + 2 * e + 1]);
+                  float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
+                  p2[e] = __floats2bfloat162_rn(silu_f(gf.x) * uf.x, silu_f(gf.y) * uf.y);
+                  g2[e] = gb;
+                  u2[e] = ub;
+                }
+                *reinterpret_cast<uint4*>(out + j) = pk;
+                if (gu) {
+                  *reinterpret_cast<uint4*>(gu + j) = pg;
+                  *reinterpret_cast<uint4*>(gu + args.N + j) = pu;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < args.N) {
+                  float g = __bfloat162float(__float2bfloat16(v[j])), uu = __bfloat162float(__float2bfloat16(u[j]));
+                  out[j] = __float2bfloat16(silu_f(g) * uu);
+                  if (gu) {
+                    gu[j] = __float2bfloat16(g);
+                    gu[args.N + j] = __float2bfloat16(uu);
+                  }
+                }
+              }
+            }
+          }
+        } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
+          if (row_ok) {
+            float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col0;
+            if (col0 + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                if constexpr (EPI == EPI_ACC_F32) {
+                  float4 p = *reinterpret_cast<float4*>(out + j);
+                  o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
+                }
+                *reinterpret_cast<float4*>(out + j) = o;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) out[j] = (EPI == EPI_ACC_F32 ? out[j] : 0.f) + v[j];
+            }
+          }
+        } else {  // EPI_BF16 / EPI_ADD_BF16
+          if (row_ok) {
+            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
+            const __nv_bfloat16* res =
+                (EPI == EPI_ADD_BF16) ? reinterpret_cast<const __nv_bfloat16*>(args.R) + (size_t)row * args.ldr + col0
+                                      : nullptr;
+            if (col0 + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                uint4 pk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+                if constexpr (EPI == EPI_ADD_BF16) {
+                  uint4 rr = *reinterpret_cast<const uint4*>(res + j);
+                  const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    float2 rf = __bfloat1622float2(r2[e]);
+                    p2[e] = __floats2bfloat162_rn(v[j + 2 * e] + rf.x, v[j + 2 * e + 1] + rf.y);
+                  }
+                } else {
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+                }
+                *reinterpret_cast<uint4*>(out + j) = pk;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (col0 + j < args.N) {
+                  float r = (EPI == EPI_ADD_BF16) ? __bfloat162float(res[j]) : 0.f;
+                  out[j] = __float2bfloat16(v[j] + r);
+                }
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------------------------- host
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows, `ld` elements between rows,
+// box {box_inner, box_outer}, 128-byte swizzle, zero fill out of bounds. Written through a pointer:
+// CUtensorMap is a 64-byte-aligned type and is never passed or returned by value on the host
+// (a by-value copy made the host code depend on the calling thread's stack alignment).
+void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                   uint32_t box_outer) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(m) % 64 == 0, "tensor map storage must be 64-byte aligned");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(ptr) % 16 == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes (ld % 8 == 0)");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+}
+
+// Kernel parameters assembled in 64-byte-aligned thread-local storage and handed to
+// cudaLaunchKernel by pointer (the runtime copies them at launch).
+struct alignas(64) GemmLaunch {
+  CUtensorMap ma;
+  CUtensorMap mb;
+  GemmArgs args;
+};
+static thread_local GemmLaunch tls_launch;
+
+// cuTensorMapEncodeTiled is a driver-API call and needs a current context in the calling thread.
+// A thread that has only touched cached allocations (autograd's worker threads do exactly that)
+// may have none: torch skips cudaSetDevice when the device index is unchanged. Bind the device's
+// primary context once per thread before the first encode.
+void bind_context(int dev) {
+  static thread_local int bound = -1;
+  if (bound != dev) {
+    C10_CUDA_CHECK(cudaSetDevice(dev));
+    C10_CUDA_CHECK(cudaFree(nullptr));
+    bound = dev;
+  }
+}
+
+// BDLLM_GEMM_TRACE=1 prints host-side checkpoints of every GEMM call to stderr (diagnostics).
+static bool trace_on() {
+  static int on = -1;
+  if (on < 0) on = getenv("BDLLM_GEMM_TRACE") != nullptr;
+  return on == 1;
+}
+#define GTRACE(msg)                                                    \
+  do {                                                                 \
+    if (trace_on()) {                                                  \
+      fprintf(stderr, "[gemm] %s\n", msg);                            \
+      fflush(stderr);                                                  \
+    }                                                                  \
+  } while (0)
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    C10_CUDA_CHECK(cudaGetDevice(&dev));
+    C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static void launch(GemmLaunch* L, cudaStream_t st) {
+  using C_ = Cfg<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, EPI>;
+  GTRACE("maps ok");
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM));
+    attr = true;
+  }
+  GTRACE("attr ok");
+  const GemmArgs& args = L->args;
+  const int tiles = ((args.M + BM - 1) / BM) * ((args.N + C_::BN_OUT - 1) / C_::BN_OUT);
+  const int grid = std::max(1, std::min(tiles, num_sms()));
+  void* kargs[3] = {&L->ma, &L->mb, &L->args};
+  C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), kargs,
+                                  C_::SMEM, st));
+  GTRACE("launched");
+}
+
+// C = A B^T-style contraction with operand majors; see the file header for the conventions.
+// a: K-major -> [M, K] (lda); MN-major -> [K, M] (lda). b: K-major -> [N, K]; MN-major -> [K, N].
+void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
+          int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
+          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha) {
+  GTRACE("enter");
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors expected");
+  bind_context(a.get_device());
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  TORCH_CHECK(M > 0 && N > 0 && K > 0, "gemm: empty problem");
+  c10::cuda::CUDAGuard guard(a.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  GTRACE("stream ok");
+  GemmLaunch* L = &tls_launch;
+  L->args = GemmArgs{(int)M, (int)N, (int)K, c.data_ptr(), (int)ldc, nullptr, (int)ldr, nullptr, 0, error_word_ptr(),
+                     (float)alpha};
+  GemmArgs& args = L->args;
+  if (epi == EPI_ADD_BF16) {
+    TORCH_CHECK(r.has_value(), "EPI_ADD_BF16 needs a residual");
+    args.R = r->data_ptr();
+  }
+  if (epi == EPI_SWIGLU && gu.has_value()) {
+    args.GU = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
+    args.ldgu = (int)(2 * N);
+  }
+  const bool f32_out = (epi == EPI_F32 || epi == EPI_ACC_F32);
+  TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype does not match the epilogue");
+  // the epilogue stores (and reads the residual) in 16-byte vectors: rows must stay 16-byte aligned
+  const int64_t esz = f32_out ? 4 : 2;
+  // (an output narrower than 32 columns only ever takes the scalar tail path)
+  const bool vec = N >= 32;
+  TORCH_CHECK(!vec || ((ldc * esz) % 16 == 0 && reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0),
+              "gemm: output rows must be 16-byte aligned");
+  if (args.R)
+    TORCH_CHECK(!vec || ((ldr * 2) % 16 == 0 && reinterpret_cast<uintptr_t>(args.R) % 16 == 0),
+                "gemm: residual rows must be 16-byte aligned");
+  if (args.GU)
+    TORCH_CHECK((N % 8) == 0 && reinterpret_cast<uintptr_t>(args.GU) % 16 == 0, "gemm: gate/up store misaligned");
+  TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: dims exceed int32");
+
+  GTRACE("args ok");
+  if (a_mn)
+    make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);
+  else
+    make_map_bf16(&L->ma, a.data_ptr(), K, M, lda, 64, 128);
+  const int BN = (bn == 128) ? 128 : 256;
+  if (epi == EPI_SWIGLU) {
+    TORCH_CHECK(!a_mn && !b_mn, "swiglu epilogue: K-major operands only");
+    make_map_bf16(&L->mb, b.data_ptr(), K, 2 * N, ldb, 64, BN / 2);
+  } else if (b_mn) {
+    make_map_bf16(&L->mb, b.data_ptr(), N, K, ldb, 64, 64);
+  } else {
+    make_map_bf16(&L->mb, b.data_ptr(), K, N, ldb, 64, BN);
+  }
+
+#define BDLLM_GEMM_CASE(BN_, AM, BMN, E)                                       \
+  if (BN == BN_ && a_mn == AM && b_mn == BMN && epi == E) {                     \
+    launch<BN_, AM, BMN, E>(L, st);                                             \
+    return;                                                                     \
+  }
+  BDLLM_GEMM_CASE(256, false, false, EPI_BF16)
+  BDLLM_GEMM_CASE(256, false, false, EPI_F32)
+  BDLLM_GEMM_CASE(256, false, false, EPI_ADD_BF16)
+  BDLLM_GEMM_CASE(256, false, false, EPI_SWIGLU)
+  BDLLM_GEMM_CASE(256, false, true, EPI_BF16)
+  BDLLM_GEMM_CASE(256, false, true, EPI_ADD_BF16)
+  BDLLM_GEMM_CASE(256, false, true, EPI_F32)
+  BDLLM_GEMM_CASE(256, true, true, EPI_F32)
+  BDLLM_GEMM_CASE(256, true, true, EPI_ACC_F32)
+  BDLLM_GEMM_CASE(256, true, true, EPI_BF16)
+  BDLLM_GEMM_CASE(128, false, false, EPI_BF16)
+  BDLLM_GEMM_CASE(128, false, false, EPI_F32)
+  BDLLM_GEMM_CASE(128, false, true, EPI_BF16)
+  BDLLM_GEMM_CASE(128, true, true, EPI_F32)
+  BDLLM_GEMM_CASE(128, true, true, EPI_ACC_F32)
+#undef BDLLM_GEMM_CASE
+  TORCH_CHECK(false, "gemm: unsupported combination bn=", BN, " a_mn=", a_mn, " b_mn=", b_mn, " epi=", epi);
+}
+
+int* error_word_ptr() {
+  static int* ptrs[64] = {nullptr};
+  int dev;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!ptrs[dev]) {
+    C10_CUDA_CHECK(cudaMalloc(&ptrs[dev], sizeof(int)));
+    C10_CUDA_CHECK(cudaMemset(ptrs[dev], 0, sizeof(int)));
+  }
+  return ptrs[dev];
+}
+
+int64_t read_error_word(bool reset) {
+  int v = 0;
+  int* p = error_word_ptr();
+  C10_CUDA_CHECK(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) C10_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+  return v;
+}
+
+}  // namespace bdllm

@@ -1,0 +1,431 @@
+// Memory-bound kernels of the training step:
+//   dswiglu        dgate/dup from d(act) and the stored bf16 (gate | up)
+//   conv_fwd/bwd   the state-fork short causal conv + SiLU over the [B, 2L, C] two-stream layout
+//   ce_rows        per-row log-sum-exp over the vocabulary, loss, and dlogits written in place
+//   adamw          fused clip-scale + AdamW on fp32 master weights, bf16 parameter write-back
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace bdllm {
+
+static inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+static inline const __nv_bfloat16* cbf(const at::Tensor& t) {
+  return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
+}
+static inline __nv_bfloat16* bfp(at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+// ------------------------------------------------------------------------------- dswiglu
+// act = silu(g) * u; dg = dact * u * silu'(g), du = dact * silu(g). gu rows [g (F) | u (F)].
+__global__ void dswiglu_kernel(const __nv_bfloat16* __restrict__ dact, const __nv_bfloat16* __restrict__ gu,
+                               __nv_bfloat16* __restrict__ dgu, int64_t rows, int F) {
+  const int64_t n = rows * (int64_t)(F / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (F / 8);
+    const int c = (int)(i % (F / 8)) * 8;
+    uint4 da = *reinterpret_cast<const uint4*>(dact + r * F + c);
+    uint4 gg = *reinterpret_cast<const uint4*>(gu + r * 2 * F + c);
+    uint4 uu = *reinterpret_cast<const uint4*>(gu + r * 2 * F + F + c);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&da);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gg);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uu);
+    uint4 og, ou;
+    __nv_bfloat162* og2 = reinterpret_cast<__nv_bfloat162*>(&og);
+    __nv_bfloat162* ou2 = reinterpret_cast<__nv_bfloat162*>(&ou);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 d = __bfloat1622float2(d2[e]), g = __bfloat1622float2(g2[e]), u = __bfloat1622float2(u2[e]);
+      float sx = sigmoid_f(g.x), sy = sigmoid_f(g.y);
+      float dgx = d.x * u.x * sx * (1.f + g.x * (1.f - sx));
+      float dgy = d.y * u.y * sy * (1.f + g.y * (1.f - sy));
+      og2[e] = __floats2bfloat162_rn(dgx, dgy);
+      ou2[e] = __floats2bfloat162_rn(d.x * g.x * sx, d.y * g.y * sy);
+    }
+    *reinterpret_cast<uint4*>(dgu + r * 2 * F + c) = og;
+    *reinterpret_cast<uint4*>(dgu + r * 2 * F + F + c) = ou;
+  }
+}
+
+at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu) {
+  const int F = dact.size(-1);
+  TORCH_CHECK(F % 8 == 0 && gu.size(-1) == 2 * F, "dswiglu: shapes");
+  auto d = dact.to(at::kBFloat16).contiguous();
+  auto g = gu.contiguous();
+  const int64_t rows = d.numel() / F;
+  auto out = at::empty({rows, 2 * F}, gu.options());
+  if (rows == 0) return out;
+  c10::cuda::CUDAGuard guard(gu.device());
+  const int64_t n = rows * (F / 8);
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  dswiglu_kernel<<<grid, 256, 0, stream()>>>(cbf(d), cbf(g), bfp(out), rows, F);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+// ------------------------------------------------------------------------------- conv
+// raw [B, 2L, C] (row stride ld), w [C, K] fp32. Source position of tap j for output token t:
+//   q = t - (K-1) + j in the stream's own coordinates; see source_of().
+enum ConvMode : int { CONV_FORK = 0, CONV_NOPREFIX = 1, CONV_CONCAT = 2 };
+
+// returns the [B, 2L] row index that tap q of output row t reads, or -1 for a zero
+__device__ __forceinline__ int source_of(int t, int q_off, int L, int block, int mode) {
+  if (mode == CONV_CONCAT) {
+    int q = t + q_off;
+    return q >= 0 ? q : -1;
+  }
+  if (t >= L) {  // clean stream: plain causal from a zero start
+    int p = t - L + q_off;
+    return p >= 0 ? L + p : -1;
+  }
+  int q = t + q_off;  // noised stream
+  int s = (t / block) * block;
+  if (q >= s) return q;
+  if (mode == CONV_FORK && q >= 0) return L + q;  // the clean prefix before the block
+  return -1;
+}
+
+template <int K>
+__global__ void conv_fwd_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ w,
+                                __nv_bfloat16* __restrict__ y, int B, int T2, int C, int L, int block, int mode) {
+  const int cv = C / 8;
+  const int64_t n = (int64_t)B * T2 * cv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cv) * 8;
+    const int64_t bt = i / cv;
+    const int t = (int)(bt % T2);
+    const int b = (int)(bt / T2);
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      int src = source_of(t, j - (K - 1), L, block, mode);
+      if (src < 0) continue;
+      uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(p2[e]);
+        acc[2 * e] += w[(c + 2 * e) * K + j] * f.x;
+        acc[2 * e + 1] += w[(c + 2 * e + 1) * K + j] * f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(silu_f(acc[2 * e]), silu_f(acc[2 * e + 1]));
+    *reinterpret_cast<uint4*>(y + ((int64_t)b * T2 + t) * C + c) = o;
+  }
+}
+
+// dpre = dy * silu'(pre), pre recomputed; one thread per (b, t, 8 channels). Stored fp32 so the
+// gather below accumulates without a second rounding.
+template <int K>
+__global__ void conv_dpre_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ w,
+                                 const __nv_bfloat16* __restrict__ dy, float* __restrict__ dpre, int B, int T2,
+                                 int C, int L, int block, int mode) {
+  const int cv = C / 8;
+  const int64_t n = (int64_t)B * T2 * cv;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % cv) * 8;
+    const int64_t bt = i / cv;
+    const int t = (int)(bt % T2);
+    const int b = (int)(bt / T2);
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      int src = source_of(t, j - (K - 1), L, block, mode);
+      if (src < 0) continue;
+      uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(p2[e]);
+        acc[2 * e] += w[(c + 2 * e) * K + j] * f.x;
+        acc[2 * e + 1] += w[(c + 2 * e + 1) * K + j] * f.y;
+      }
+    }
+    uint4 g = *reinterpret_cast<const uint4*>(dy + ((int64_t)b * T2 + t) * C + c);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
+    float* out = dpre + ((int64_t)b * T2 + t) * C + c;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 gf = __bfloat1622float2(g2[e]);
+      float s0 = sigmoid_f(acc[2 * e]), s1 = sigmoid_f(acc[2 * e + 1]);
+      out[2 * e] = gf.x * s0 * (1.f + acc[2 * e] * (1.f - s0));
+      out[2 * e + 1] = gf.y * s1 * (1.f + acc[2 * e + 1] * (1.f - s1));
+    }
+  }
+}
+
+// draw[b, q, c] = sum over (t, j) with source_of(t, j-(K-1)) == q of dpre[b, t, c] * w[c, j].
+// A source row q is read only by output rows t in [q, q + K - 1] (its own stream) and, in fork
+// mode, by noised rows t in [q - L, q - L + K - 1] (clean source q >= L read as a block prefix).
+template <int K>
+__global__ void conv_dx_kernel(const float* __restrict__ dpre, const float* __restrict__ w,
+                               __nv_bfloat16* __restrict__ draw, int64_t ldd, int B, int T2, int C, int L, int block,
+                               int mode) {
+  const int64_t n = (int64_t)B * T2 * C;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % C);
+    const int64_t bq = i / C;
+    const int q = (int)(bq % T2);
+    const int b = (int)(bq / T2);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int t = q + (K - 1) - j;  // same-stream consumer
+      if (t < T2 && source_of(t, j - (K - 1), L, block, mode) == q)
+        acc += dpre[((int64_t)b * T2 + t) * C + c] * w[c * K + j];
+      if (mode == CONV_FORK && q >= L) {  // noised consumer reading this clean row as a prefix
+        const int tn = q - L + (K - 1) - j;
+        if (tn < L && source_of(tn, j - (K - 1), L, block, mode) == q)
+          acc += dpre[((int64_t)b * T2 + tn) * C + c] * w[c * K + j];
+      }
+    }
+    draw[((int64_t)b * T2 + q) * ldd + c] = __float2bfloat16(acc);
+  }
+}
+
+// dw partials: block handles a token range for 32 channels x K taps; grid.y over channel groups.
+template <int K>
+__global__ void conv_dw_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ dpre,
+                               float* __restrict__ part, int B, int T2, int C, int L, int block, int mode,
+                               int tokens_per_block) {
+  const int c = blockIdx.y * 32 + (threadIdx.x & 31);
+  const int sub = threadIdx.x >> 5;  // 8 token lanes
+  if (c >= C) return;
+  float acc[K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) acc[j] = 0.f;
+  const int64_t total = (int64_t)B * T2;
+  const int64_t r0 = (int64_t)blockIdx.x * tokens_per_block;
+  const int64_t r1 = min(total, r0 + tokens_per_block);
+  for (int64_t r = r0 + sub; r < r1; r += 8) {
+    const int t = (int)(r % T2);
+    const int b = (int)(r / T2);
+    const float d = dpre[r * C + c];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      int src = source_of(t, j - (K - 1), L, block, mode);
+      if (src >= 0) acc[j] += d * __bfloat162float(raw[((int64_t)b * T2 + src) * ld + c]);
+    }
+  }
+  __shared__ float red[8][32][K];
+#pragma unroll
+  for (int j = 0; j < K; ++j) red[sub][threadIdx.x & 31][j] = acc[j];
+  __syncthreads();
+  if (sub == 0) {
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      float s = 0.f;
+      for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x & 31][j];
+      part[((int64_t)blockIdx.x * C + c) * K + j] = s;
+    }
+  }
+}
+
+__global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int64_t n, float* __restrict__ out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float s = 0.f;
+    for (int p = 0; p < nparts; ++p) s += part[p * n + i];
+    out[i] = s;
+  }
+}
+
+static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
+
+at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode) {
+  TORCH_CHECK(raw.dim() == 3 && raw.stride(-1) == 1 && raw.scalar_type() == at::kBFloat16, "conv: raw [B, 2L, C] bf16");
+  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2), K = w.size(1);
+  TORCH_CHECK(T2 == 2 * L && C % 8 == 0 && raw.stride(1) % 8 == 0 && raw.stride(0) == (int64_t)T2 * raw.stride(1),
+              "conv: layout");
+  TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
+  auto wf = w.to(at::kFloat).contiguous();
+  auto y = at::empty({B, T2, C}, raw.options());
+  c10::cuda::CUDAGuard g(raw.device());
+  const int64_t n = (int64_t)B * T2 * (C / 8);
+  conv_fwd_kernel<4><<<grid_for(n), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(), bfp(y), B, T2,
+                                                        C, (int)L, (int)block, (int)mode);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
+std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
+                                 int64_t block, int64_t mode) {
+  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2), K = w.size(1);
+  TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
+  auto wf = w.to(at::kFloat).contiguous();
+  auto d = dy.to(at::kBFloat16).contiguous();
+  c10::cuda::CUDAGuard g(raw.device());
+  auto dpre = at::empty({B, T2, C}, raw.options().dtype(at::kFloat));
+  const int64_t nv = (int64_t)B * T2 * (C / 8);
+  conv_dpre_kernel<4><<<grid_for(nv), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(), cbf(d),
+                                                          dpre.data_ptr<float>(), B, T2, C, (int)L, (int)block,
+                                                          (int)mode);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto draw = at::empty({B, T2, C}, raw.options());
+  const int64_t n = (int64_t)B * T2 * C;
+  conv_dx_kernel<4><<<grid_for(n), 256, 0, stream()>>>(dpre.data_ptr<float>(), wf.data_ptr<float>(), bfp(draw), C, B,
+                                                       T2, C, (int)L, (int)block, (int)mode);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const int64_t total = (int64_t)B * T2;
+  const int tpb = (int)std::max<int64_t>(64, (total + 127) / 128);
+  const int nb = (int)((total + tpb - 1) / tpb);
+  auto part = at::empty({nb, C, K}, raw.options().dtype(at::kFloat));
+  dim3 grid(nb, (C + 31) / 32);
+  conv_dw_kernel<4><<<grid, 256, 0, stream()>>>(cbf(raw), raw.stride(1), dpre.data_ptr<float>(), part.data_ptr<float>(),
+                                                B, T2, C, (int)L, (int)block, (int)mode, tpb);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  auto dw = at::empty({C, K}, raw.options().dtype(at::kFloat));
+  sum_parts_kernel<<<grid_for((int64_t)C * K), 256, 0, stream()>>>(part.data_ptr<float>(), nb, (int64_t)C * K,
+                                                                    dw.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {draw, dw};
+}
+
+// ------------------------------------------------------------------------------- CE
+// One CTA per row of `logits` [n, V] (bf16, row stride ld). Pass 1: online max / sum-exp in fp32.
+// Pass 2 (row is L2-resident): dlogits = exp(x - lse) - onehot(target), written over the logits.
+// loss[row] = lse - x[target].
+__global__ void ce_rows_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, const int64_t* __restrict__ tgt,
+                               float* __restrict__ loss, int V) {
+  const int64_t row = blockIdx.x;
+  __nv_bfloat16* x = logits + row * ld;
+  float m = -INFINITY, s = 0.f;
+  for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
+    uint4 p = *reinterpret_cast<const uint4*>(x + c);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(p2[e]);
+      v[2 * e] = f.x, v[2 * e + 1] = f.y;
+    }
+    float mx = v[0];
+#pragma unroll
+    for (int e = 1; e < 8; ++e) mx = fmaxf(mx, v[e]);
+    float nm = fmaxf(m, mx);
+    s *= __expf(m - nm);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) s += __expf(v[e] - nm);
+    m = nm;
+  }
+  // block reduction of (m, s)
+  __shared__ float sm[32], ss[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  if (lane == 0) sm[warp] = m, ss[warp] = s;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x / 32;
+    m = lane < nw ? sm[lane] : -INFINITY;
+    s = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+      float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      m = nm;
+    }
+    if (lane == 0) sm[0] = m + logf(s);
+  }
+  __syncthreads();
+  const float lse = sm[0];
+  const int64_t t = tgt[row];
+  if (threadIdx.x == 0) loss[row] = lse - __bfloat162float(x[t]);
+  __syncthreads();  // the target logit is read before pass 2 overwrites it
+  for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
+    uint4 p = *reinterpret_cast<const uint4*>(x + c);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(p2[e]);
+      float a = __expf(f.x - lse) - (c + 2 * e == t ? 1.f : 0.f);
+      float b = __expf(f.y - lse) - (c + 2 * e + 1 == t ? 1.f : 0.f);
+      o2[e] = __floats2bfloat162_rn(a, b);
+    }
+    *reinterpret_cast<uint4*>(x + c) = o;
+  }
+}
+
+at::Tensor ce_rows_(at::Tensor& logits, const at::Tensor& tgt) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.size(1) % 8 == 0 && logits.stride(0) % 8 == 0,
+              "ce_rows: logits [n, V], V % 8 == 0");
+  const int64_t n = logits.size(0);
+  auto loss = at::empty({n}, logits.options().dtype(at::kFloat));
+  if (n == 0) return loss;
+  auto t = tgt.to(at::kLong).contiguous();
+  c10::cuda::CUDAGuard g(logits.device());
+  ce_rows_kernel<<<n, 512, 0, stream()>>>(bfp(logits), logits.stride(0), t.data_ptr<int64_t>(), loss.data_ptr<float>(),
+                                          (int)logits.size(1));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return loss;
+}
+
+// ------------------------------------------------------------------------------- AdamW
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ void store_as(float* p, float x) { *p = x; }
+__device__ __forceinline__ void store_as(__nv_bfloat16* p, float x) { *p = __float2bfloat16(x); }
+
+// w (fp32 master, or the fp32 param itself), p (param storage, bf16 or fp32), g (grad, any of
+// bf16/fp32), m, v fp32. coef = clip coefficient applied to g. bc1/bc2 = bias corrections.
+template <typename TP, typename TG>
+__global__ void adamw_kernel(float* __restrict__ w, TP* __restrict__ p, const TG* __restrict__ g,
+                             float* __restrict__ m, float* __restrict__ v, int64_t n, float lr, float b1, float b2,
+                             float eps, float wd, float coef, float bc1, float bc2) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float gi = to_f(g[i]) * coef;
+    float wi = w[i];
+    if (wd != 0.f) wi *= 1.f - lr * wd;
+    float mi = b1 * m[i] + (1.f - b1) * gi;
+    float vi = b2 * v[i] + (1.f - b2) * gi * gi;
+    m[i] = mi;
+    v[i] = vi;
+    wi -= lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+    w[i] = wi;
+    if (p != nullptr) store_as(p + i, wi);
+  }
+}
+
+void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
+                double b2, double eps, double wd, double coef, double bc1, double bc2) {
+  TORCH_CHECK(w.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "adamw: contiguous");
+  TORCH_CHECK(w.scalar_type() == at::kFloat, "adamw: fp32 master");
+  const int64_t n = w.numel();
+  if (n == 0) return;
+  c10::cuda::CUDAGuard gd(w.device());
+  const bool same = p.data_ptr() == w.data_ptr();
+  const int grid = grid_for(n);
+#define ADAMW(TP, TG, PP, GP)                                                                                        \
+  adamw_kernel<TP, TG><<<grid, 256, 0, stream()>>>(w.data_ptr<float>(), PP, GP, m.data_ptr<float>(),                  \
+                                                   v.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2,          \
+                                                   (float)eps, (float)wd, (float)coef, (float)bc1, (float)bc2)
+  const bool gbf = g.scalar_type() == at::kBFloat16;
+  if (same || p.scalar_type() == at::kFloat) {
+    float* pp = same ? nullptr : p.data_ptr<float>();
+    if (gbf) ADAMW(float, __nv_bfloat16, pp, cbf(g));
+    else ADAMW(float, float, pp, g.data_ptr<float>());
+  } else {
+    TORCH_CHECK(p.scalar_type() == at::kBFloat16 && p.is_contiguous(), "adamw: bf16 param");
+    if (gbf) ADAMW(__nv_bfloat16, __nv_bfloat16, bfp(p), cbf(g));
+    else ADAMW(__nv_bfloat16, float, bfp(p), g.data_ptr<float>());
+  }
+#undef ADAMW
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace bdllm

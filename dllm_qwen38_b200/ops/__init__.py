@@ -21,8 +21,23 @@ def _record(op: str, impl: str) -> None:
     _LAST[op] = impl
 
 
+_PENDING_TORCH_CUDA: set = set()
+
+
+def _record_ref(op: str) -> None:
+    """Record the torch path: 'torch-cuda' if use_native just routed a CUDA call here, else
+    'reference' (host tensors)."""
+    if op in _PENDING_TORCH_CUDA:
+        _PENDING_TORCH_CUDA.discard(op)
+        _LAST[op] = "torch-cuda"
+    else:
+        _LAST[op] = "reference"
+
+
 def last_impl(op: str | None = None):
-    """Which implementation each op used on its most recent call ('native' or 'reference')."""
+    """Which implementation each op used on its most recent call: 'native' (sm_100a kernel),
+    'reference' (fp32 torch on the host) or 'torch-cuda' (torch on the device: an op whose kernel
+    is not written yet)."""
     return dict(_LAST) if op is None else _LAST.get(op)
 
 
@@ -30,16 +45,21 @@ def reset_impl_record() -> None:
     _LAST.clear()
 
 
-def _native():
-    from . import _native as nat
+def _nat():
+    import importlib
 
-    return nat
+    return importlib.import_module(__name__ + "._native")
 
 
-def use_native(*tensors: torch.Tensor) -> bool:
-    """True when the op must run the CUDA kernel (any CUDA input). Raises if it is not built."""
+def use_native(*tensors: torch.Tensor, op: str | None = None) -> bool:
+    """True when the op must run the CUDA kernel (any CUDA input). Raises if the extension is not
+    built. An op listed in ``ops.cuda.TORCH_ON_CUDA`` has no kernel yet: it runs the reference on
+    the device and is recorded as 'torch-cuda' so no report mistakes it for a native path."""
     if any(t is not None and t.is_cuda for t in tensors):
-        _native().require()
+        _nat().require()
+        if op is not None and op in _nat().TORCH_ON_CUDA:
+            _PENDING_TORCH_CUDA.add(op)
+            return False
         return True
     return False
 
@@ -48,36 +68,36 @@ def use_native(*tensors: torch.Tensor) -> bool:
 
 
 def rmsnorm(x, w, eps: float):
-    if use_native(x):
+    if use_native(x, op="rmsnorm"):
         _record("rmsnorm", "native")
-        return _native().rmsnorm(x, w, eps)
-    _record("rmsnorm", "reference")
+        return _nat().rmsnorm(x, w, eps)
+    _record_ref("rmsnorm")
     return ref.rmsnorm(x, w, eps)
 
 
 def linear(x, w):
     """y = x @ w^T for x [..., K], w [N, K] (nn.Linear layout)."""
-    if use_native(x):
+    if use_native(x, op="linear"):
         _record("linear", "native")
-        return _native().linear(x, w)
-    _record("linear", "reference")
+        return _nat().linear(x, w)
+    _record_ref("linear")
     return ref.linear(x, w)
 
 
 def swiglu_mlp(x, w_gate, w_up, w_down):
     """down(silu(gate x) * up x)."""
-    if use_native(x):
+    if use_native(x, op="mlp"):
         _record("mlp", "native")
-        return _native().swiglu_mlp(x, w_gate, w_up, w_down)
-    _record("mlp", "reference")
+        return _nat().swiglu_mlp(x, w_gate, w_up, w_down)
+    _record_ref("mlp")
     return ref.linear(ref.swiglu(ref.linear(x, w_gate), ref.linear(x, w_up)), w_down)
 
 
 def gated_rmsnorm(x, z, w, eps: float):
-    if use_native(x):
+    if use_native(x, op="gated_rmsnorm"):
         _record("gated_rmsnorm", "native")
-        return _native().gated_rmsnorm(x, z, w, eps)
-    _record("gated_rmsnorm", "reference")
+        return _nat().gated_rmsnorm(x, z, w, eps)
+    _record_ref("gated_rmsnorm")
     return ref.gated_rmsnorm(x, z, w, eps)
 
 
@@ -85,26 +105,26 @@ def gated_rmsnorm(x, z, w, eps: float):
 
 
 def conv_blockdiff(raw, w, L: int, block: int, mode: str = ref.CONV_FORK):
-    if use_native(raw):
+    if use_native(raw, op="conv"):
         _record("conv", "native")
-        return _native().conv_blockdiff(raw, w, L, block, mode)
-    _record("conv", "reference")
+        return _nat().conv_blockdiff(raw, w, L, block, mode)
+    _record_ref("conv")
     return ref.conv_blockdiff(raw, w, L, block, mode)
 
 
 def gdn_gates(a, b, A_log, dt_bias):
-    if use_native(a):
+    if use_native(a, op="gdn_gates"):
         _record("gdn_gates", "native")
-        return _native().gdn_gates(a, b, A_log, dt_bias)
-    _record("gdn_gates", "reference")
+        return _nat().gdn_gates(a, b, A_log, dt_bias)
+    _record_ref("gdn_gates")
     return ref.gdn_gates(a, b, A_log, dt_bias)
 
 
 def gdn_core_blockdiff(q, k, v, g, beta, L: int, block: int, chunk: int, mode: str = ref.GDN_FORK):
-    if use_native(q):
+    if use_native(q, op="gdn_core"):
         _record("gdn_core", "native")
-        return _native().gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode)
-    _record("gdn_core", "reference")
+        return _nat().gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode)
+    _record_ref("gdn_core")
     return ref.gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode)
 
 
@@ -113,26 +133,30 @@ def gdn_core_blockdiff(q, k, v, g, beta, L: int, block: int, chunk: int, mode: s
 
 def attention_blockdiff(q, k, v, L: int, block: int, scale: float, leak_xt_prefix: bool = False):
     """Complementary-mask attention over the [B, 2L] layout (mask computed, never stored)."""
-    if use_native(q):
+    if use_native(q, op="attention"):
         _record("attention", "native")
-        return _native().attention_blockdiff(q, k, v, L, block, scale, leak_xt_prefix)
-    _record("attention", "reference")
+        return _nat().attention_blockdiff(q, k, v, L, block, scale, leak_xt_prefix)
+    _record_ref("attention")
     allowed = ref.complementary_allowed(L, block, q.device, leak_xt_prefix)
+    if q.is_cuda:  # device path until the native kernel covers it: no O(T^2) fp32 scores
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), attn_mask=allowed, scale=scale, enable_gqa=True)
+        return o.transpose(1, 2)
     return ref.attention(q, k, v, allowed, scale)
 
 
 def attention_masked(q, k, v, allowed, scale: float):
     """Attention under an explicit [T, T] bool mask (oracles and the plain forward)."""
-    _record("attention_masked", "reference")
+    _record_ref("attention_masked")
     return ref.attention(q, k, v, allowed, scale)
 
 
 def qk_norm_rope(q, k, wq, wk, eps: float, cos, sin):
     """Per-head RMSNorm(1+w) of q and k, then partial RoPE on both."""
-    if use_native(q):
+    if use_native(q, op="qk_norm_rope"):
         _record("qk_norm_rope", "native")
-        return _native().qk_norm_rope(q, k, wq, wk, eps, cos, sin)
-    _record("qk_norm_rope", "reference")
+        return _nat().qk_norm_rope(q, k, wq, wk, eps, cos, sin)
+    _record_ref("qk_norm_rope")
     return ref.apply_rope(ref.rmsnorm(q, wq, eps), cos, sin), ref.apply_rope(ref.rmsnorm(k, wk, eps), cos, sin)
 
 
@@ -141,16 +165,16 @@ def qk_norm_rope(q, k, wq, wk, eps: float, cos, sin):
 
 def masked_ce_sum(hidden, w, targets):
     """Sum over rows of fp32 CE(hidden @ w^T, targets); never holds the full-vocab logits on GPU."""
-    if use_native(hidden):
+    if use_native(hidden, op="masked_ce"):
         _record("masked_ce", "native")
-        return _native().masked_ce_sum(hidden, w, targets)
-    _record("masked_ce", "reference")
+        return _nat().masked_ce_sum(hidden, w, targets)
+    _record_ref("masked_ce")
     return ref.masked_ce_sum(hidden, w, targets)
 
 
 def embedding(ids, table):
-    if use_native(ids):
+    if use_native(ids, op="embedding"):
         _record("embedding", "native")
-        return _native().embedding(ids, table)
-    _record("embedding", "reference")
+        return _nat().embedding(ids, table)
+    _record_ref("embedding")
     return torch.nn.functional.embedding(ids, table)

@@ -1,0 +1,310 @@
+"""Autograd-aware wrappers around the sm_100a kernels (``dllm_qwen38_b200._C``).
+
+Conventions of the GEMM entry (``_C.gemm``): C[m, n] = sum_k A(m, k) B(n, k); A is K-major
+([M, K]) or MN-major ([K, M]); B is K-major ([N, K]) or MN-major ([K, N]). With those two bits
+the three GEMMs of a linear layer need no transposes:
+
+    forward  y  = x  W^T : A = x  (K-major), B = W (K-major)
+    dgrad    dx = dy W   : A = dy (K-major), B = W (MN-major, rows = out features)
+    wgrad    dW = dy^T x : A = dy (MN-major), B = x (MN-major)
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _C
+
+EPI_BF16, EPI_F32, EPI_ADD_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
+
+# ops that have no sm_100a kernel yet; on CUDA tensors they run the torch reference and are
+# recorded as 'torch-cuda' by ops.last_impl()
+TORCH_ON_CUDA = {"gdn_gates", "gdn_core", "attention", "embedding"}
+
+
+# native kernel launches issued through this module (benchmarks report the count of a region)
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def _c2(t: torch.Tensor) -> torch.Tensor:
+    """Flatten to 2-D with a unit inner stride (no copy when already so)."""
+    t2 = t.reshape(-1, t.shape[-1])
+    if t2.stride(-1) != 1 or (t2.stride(0) % 8) or (t2.data_ptr() % 16):
+        t2 = t2.contiguous()
+    return t2
+
+
+def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+            residual: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ b[N, K]^T (both K-major). residual: out = a b^T + residual (bf16).
+    accumulate: fp32 out += a b^T."""
+    a2, b2 = _c2(a), _c2(b)
+    M, K = a2.shape
+    N = b2.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    if accumulate:
+        epi = EPI_ACC_F32
+    elif residual is not None:
+        epi = EPI_ADD_BF16
+    else:
+        epi = EPI_F32 if out.dtype == torch.float32 else EPI_BF16
+    r = _c2(residual) if residual is not None else None
+    _C.gemm(a2, False, a2.stride(0), b2, False, b2.stride(0), M, N, K, out, out.stride(0), epi,
+            r, r.stride(0) if r is not None else 0)
+    _count()
+    return out
+
+
+def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+            residual: torch.Tensor | None = None, alpha: float = 1.0) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ b[K, N] (b MN-major: row-major [K, N])."""
+    a2, b2 = _c2(a), _c2(b)
+    M, K = a2.shape
+    N = b2.shape[1]
+    if out is None:
+        out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    epi = EPI_ADD_BF16 if residual is not None else (EPI_F32 if out.dtype == torch.float32 else EPI_BF16)
+    r = _c2(residual) if residual is not None else None
+    _C.gemm(a2, False, a2.stride(0), b2, True, b2.stride(0), M, N, K, out, out.stride(0), epi,
+            r, r.stride(0) if r is not None else 0, None, 256, alpha)
+    _count()
+    return out
+
+
+def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.float32,
+            accumulate: bool = False, alpha: float = 1.0) -> torch.Tensor:
+    """out[M, N] = a[K, M]^T @ b[K, N] (both MN-major) -- the weight-gradient GEMM."""
+    a2, b2 = _c2(a), _c2(b)
+    K, M = a2.shape
+    N = b2.shape[1]
+    if out is None:
+        out = torch.zeros(M, N, device=a.device, dtype=out_dtype) if accumulate else torch.empty(
+            M, N, device=a.device, dtype=out_dtype)
+    epi = EPI_ACC_F32 if accumulate else (EPI_F32 if out.dtype == torch.float32 else EPI_BF16)
+    _C.gemm(a2, True, a2.stride(0), b2, True, b2.stride(0), M, N, K, out, out.stride(0), epi, None, 0, None, 256,
+            alpha)
+    _count()
+    return out
+
+
+def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, F: int, store_gu: bool):
+    """act[M, F] = silu(x Wg^T) * (x Wu^T) with w_gate_up = [Wg; Wu] ([2F, K], contiguous rows).
+    Returns (act, gu) where gu [M, 2F] holds the bf16 (gate | up) when store_gu."""
+    x2 = _c2(x)
+    M, K = x2.shape
+    act = torch.empty(M, F, device=x.device, dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * F, device=x.device, dtype=torch.bfloat16) if store_gu else None
+    _C.gemm(x2, False, x2.stride(0), w_gate_up, False, w_gate_up.stride(0), M, F, K, act, act.stride(0), EPI_SWIGLU,
+            None, 0, gu)
+    _count()
+    return act, gu
+
+
+# ----------------------------------------------------------------------------- linear
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.save_for_backward(x, w)
+        y = gemm_nt(x, w)
+        return y.reshape(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w = ctx.saved_tensors
+        dy2 = _c2(dy.to(torch.bfloat16))
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm_nn(dy2, w).reshape(x.shape)
+        if ctx.needs_input_grad[1]:
+            dw = gemm_tn(dy2, _c2(x), out_dtype=torch.float32).to(w.dtype)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise TypeError(f"native linear runs bf16 operands (got {x.dtype}, {w.dtype})")
+    return _Linear.apply(x, w)
+
+
+# ----------------------------------------------------------------------------- norms
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        w1 = 1.0 + w.float()
+        ctx.save_for_backward(x, w1)
+        ctx.eps, ctx.wdtype = eps, w.dtype
+        _count()
+        return _C.rmsnorm_fwd(x, w1, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w1 = ctx.saved_tensors
+        dx, dw = _C.rmsnorm_bwd(dy, x, w1, ctx.eps)
+        _count(2)
+        return dx, dw.to(ctx.wdtype), None
+
+
+def rmsnorm(x, w, eps):
+    return _RMSNorm.apply(x, w, eps)
+
+
+class _GatedRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, z, w, eps):
+        ctx.save_for_backward(x, z, w)
+        ctx.eps = eps
+        _count()
+        return _C.gated_rmsnorm_fwd(x, z, w, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, z, w = ctx.saved_tensors
+        dx, dz, dw = _C.gated_rmsnorm_bwd(dy, x, z, w, ctx.eps)
+        _count(2)
+        return dx, dz, dw.to(w.dtype), None
+
+
+def gated_rmsnorm(x, z, w, eps):
+    return _GatedRMSNorm.apply(x, z, w, eps)
+
+
+class _QKNormRope(torch.autograd.Function):
+    """q/k [B, T2, H, Dh] strided views (q is a slice of the q|gate projection)."""
+
+    @staticmethod
+    def forward(ctx, q, k, wq, wk, eps, cos, sin):
+        wq1, wk1 = 1.0 + wq.float(), 1.0 + wk.float()
+        ctx.save_for_backward(q, k, wq1, wk1, cos, sin)
+        ctx.eps, ctx.dt = eps, wq.dtype
+        _count(2)
+        return _C.qk_norm_rope_fwd(q, wq1, cos, sin, eps), _C.qk_norm_rope_fwd(k, wk1, cos, sin, eps)
+
+    @staticmethod
+    def backward(ctx, dq, dk):
+        q, k, wq1, wk1, cos, sin = ctx.saved_tensors
+        dqs, dwq = _C.qk_norm_rope_bwd(dq, q, wq1, cos, sin, ctx.eps)
+        dks, dwk = _C.qk_norm_rope_bwd(dk, k, wk1, cos, sin, ctx.eps)
+        _count(4)
+        return dqs, dks, dwq.to(ctx.dt), dwk.to(ctx.dt), None, None, None
+
+
+def qk_norm_rope(q, k, wq, wk, eps, cos, sin):
+    return _QKNormRope.apply(q, k, wq, wk, eps, cos, sin)
+
+
+# ----------------------------------------------------------------------------- MLP
+
+
+class _SwiGLUMLP(torch.autograd.Function):
+    """down(silu(x Wg^T) * (x Wu^T)): one GEMM for gate|up with the SwiGLU epilogue (keeping the
+    bf16 gate|up for backward), one for down. Backward: d(act) = dy Wd, the SwiGLU derivative
+    kernel, then dx = dgu [Wg; Wu] and the two weight-gradient GEMMs."""
+
+    @staticmethod
+    def forward(ctx, x, w_gate, w_up, w_down):
+        F = w_gate.shape[0]
+        w_gu = torch.cat([w_gate, w_up], 0)
+        need = torch.is_grad_enabled() or any(ctx.needs_input_grad)
+        act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
+        y = gemm_nt(act, w_down)
+        ctx.save_for_backward(x, w_gu, w_down, act, gu)
+        ctx.F = F
+        return y.reshape(*x.shape[:-1], w_down.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w_gu, w_down, act, gu = ctx.saved_tensors
+        dy2 = _c2(dy.to(torch.bfloat16))
+        x2 = _c2(x)
+        dact = gemm_nn(dy2, w_down)
+        dgu = _C.dswiglu(dact, gu)
+        _count()
+        dx = gemm_nn(dgu, w_gu).reshape(x.shape)
+        dw_gu = gemm_tn(dgu, x2, out_dtype=torch.float32).to(w_gu.dtype)
+        dw_down = gemm_tn(dy2, act, out_dtype=torch.float32).to(w_down.dtype)
+        return dx, dw_gu[: ctx.F], dw_gu[ctx.F :], dw_down
+
+
+def swiglu_mlp(x, w_gate, w_up, w_down):
+    return _SwiGLUMLP.apply(x, w_gate, w_up, w_down)
+
+
+# ----------------------------------------------------------------------------- conv
+
+_CONV_MODE = {"fork": 0, "no-prefix": 1, "concat": 2}
+
+
+class _Conv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, raw, w, L, block, mode):
+        ctx.save_for_backward(raw, w)
+        ctx.cfg = (L, block, _CONV_MODE[mode])
+        _count()
+        return _C.conv_fwd(raw, w, L, block, _CONV_MODE[mode])
+
+    @staticmethod
+    def backward(ctx, dy):
+        raw, w = ctx.saved_tensors
+        draw, dw = _C.conv_bwd(dy, raw, w, *ctx.cfg)
+        _count(4)
+        return draw, dw.to(w.dtype), None, None, None
+
+
+def conv_blockdiff(raw, w, L, block, mode):
+    if raw.stride(-1) != 1 or raw.stride(1) % 8:
+        raw = raw.contiguous()
+    return _Conv.apply(raw, w, L, block, mode)
+
+
+# ----------------------------------------------------------------------------- loss
+
+
+class _MaskedCE(torch.autograd.Function):
+    """sum_rows CE(h W^T, t). Forward: logits by GEMM (bf16, [n, V]), one row kernel writes the
+    per-row loss and overwrites the logits with (softmax - onehot). Backward: dh = g * dlogits W,
+    dW = g * dlogits^T h (the GEMM epilogue applies g)."""
+
+    @staticmethod
+    def forward(ctx, h, w, tgt):
+        h2 = _c2(h)
+        logits = gemm_nt(h2, w)
+        loss = _C.ce_rows_(logits, tgt)
+        _count()
+        ctx.save_for_backward(h2, w, logits)
+        return loss.sum()
+
+    @staticmethod
+    def backward(ctx, g):
+        h2, w, dlogits = ctx.saved_tensors
+        gs = float(g)
+        dh = gemm_nn(dlogits, w, alpha=gs) if ctx.needs_input_grad[0] else None
+        dw = gemm_tn(dlogits, h2, out_dtype=torch.float32, alpha=gs).to(w.dtype) if ctx.needs_input_grad[1] else None
+        return dh, dw, None
+
+
+def masked_ce_sum(hidden, w, targets):
+    return _MaskedCE.apply(hidden, w, targets)
+
+
+def adamw_step(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
+    _C.adamw_step(w, p, g.contiguous(), m, v, lr, b1, b2, eps, wd, coef, bc1, bc2)
+    _count()
+
+
+def error_word(reset: bool = False) -> int:
+    return int(_C.read_error_word(reset))
+
+
+def check_errors() -> None:
+    e = error_word(reset=True)
+    if e:
+        raise RuntimeError(f"a bounded device wait expired (error code {e}); see csrc/common.cuh")

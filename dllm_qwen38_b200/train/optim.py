@@ -50,8 +50,9 @@ class MasterAdamW:
             if p.grad is None:
                 continue
             w = self.master[i] if self.master[i] is not None else p.data
-            if p.is_cuda and ops._native().available():
-                ops._native().adamw_step(w, p.data, p.grad, self.exp_avg[i], self.exp_avg_sq[i], self.lr, b1, b2,
+            native = getattr(ops._nat(), "adamw_step", None) if p.is_cuda else None
+            if native is not None:
+                native(w, p.data, p.grad, self.exp_avg[i], self.exp_avg_sq[i], self.lr, b1, b2,
                                          self.eps, self.wd, coef, bc1, bc2)
                 continue
             g = p.grad.float() * coef

@@ -22,6 +22,16 @@ at::Tensor qk_norm_rope_fwd(const at::Tensor& src, const at::Tensor& w1, const a
                             double eps);
 std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& w1,
                                          const at::Tensor& cs, const at::Tensor& sn, double eps);
+std::vector<at::Tensor> gdn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                const at::Tensor& beta, int64_t L, int64_t C, bool concat);
+std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S_in, int64_t L,
+                                int64_t C, bool concat);
+std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L,
+                                 int64_t block, double scale, bool leak);
+std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                 const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, int64_t L,
+                                 int64_t block, double scale, bool leak);
 }  // namespace bdllm
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -35,6 +45,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_bwd", &bdllm::conv_bwd);
   m.def("ce_rows_", &bdllm::ce_rows_);
   m.def("adamw_step", &bdllm::adamw_step);
+  m.def("gdn_fwd", &bdllm::gdn_fwd, "state-fork chunked gated delta rule forward");
+  m.def("gdn_bwd", &bdllm::gdn_bwd, "state-fork chunked gated delta rule backward");
+  m.def("attn_fwd", &bdllm::attn_fwd, "complementary-mask flash attention forward");
+  m.def("attn_bwd", &bdllm::attn_bwd, "complementary-mask flash attention backward");
   m.def("rmsnorm_fwd", &bdllm::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &bdllm::rmsnorm_bwd);
   m.def("gated_rmsnorm_fwd", &bdllm::gated_rmsnorm_fwd);

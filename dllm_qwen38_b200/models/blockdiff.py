@@ -73,10 +73,10 @@ def gdn_mixer(m, n: torch.Tensor, L: int, block: int, chunk: int, fault: BreakMo
     Same math as the reference's two `gdn_mixer_forward` calls (`gdn.py:193-233`,
     `blockdiff.py:159-177`), done as one pass over the two-stream layout."""
     B, T2, _ = n.shape
-    raw = ops.linear(n, m.in_proj_qkv.weight)  # [B, 2L, conv_dim] (pre-conv, the prefix source)
-    z = ops.linear(n, m.in_proj_z.weight)
-    b = ops.linear(n, m.in_proj_b.weight)
-    a = ops.linear(n, m.in_proj_a.weight)
+    # one GEMM for the four input projections (qkv | z | b | a)
+    w_in = torch.cat([m.in_proj_qkv.weight, m.in_proj_z.weight, m.in_proj_b.weight, m.in_proj_a.weight], 0)
+    proj = ops.linear(n, w_in)
+    raw, z, b, a = torch.split(proj, [m.conv_dim, m.value_dim, m.num_v_heads, m.num_v_heads], dim=-1)
     if fault.concat_causal_gdn:
         conv_mode, core_mode = ref.CONV_CONCAT, ref.GDN_CONCAT
     else:
@@ -97,10 +97,13 @@ def attn_mixer(m, n: torch.Tensor, L: int, block: int, cos, sin, fault: BreakMod
     """Output-gated GQA attention under the complementary mask. n [B, 2L, D] -> [B, 2L, D]."""
     B, T2, _ = n.shape
     Hq, Hk, Dh = m.num_heads, m.num_kv_heads, m.head_dim
-    qg = ops.linear(n, m.q_proj.weight).reshape(B, T2, Hq, 2 * Dh)
+    # one GEMM for q|gate, k, v
+    proj = ops.linear(n, torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight], 0))
+    qg, k, v = torch.split(proj, [2 * Hq * Dh, Hk * Dh, Hk * Dh], dim=-1)
+    qg = qg.reshape(B, T2, Hq, 2 * Dh)
     q, gate = qg[..., :Dh], qg[..., Dh:]
-    k = ops.linear(n, m.k_proj.weight).reshape(B, T2, Hk, Dh)
-    v = ops.linear(n, m.v_proj.weight).reshape(B, T2, Hk, Dh)
+    k = k.reshape(B, T2, Hk, Dh)
+    v = v.reshape(B, T2, Hk, Dh)
     cos2, sin2 = torch.cat([cos, cos], 0), torch.cat([sin, sin], 0)
     q, k = ops.qk_norm_rope(q, k, m.q_norm.weight, m.k_norm.weight, m.q_norm.eps, cos2, sin2)
     o = ops.attention_blockdiff(q, k, v, L, block, Dh ** -0.5, fault.leak_xt_prefix)

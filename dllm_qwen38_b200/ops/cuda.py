@@ -19,7 +19,7 @@ EPI_BF16, EPI_F32, EPI_ADD_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
 
 # ops that have no sm_100a kernel yet; on CUDA tensors they run the torch reference and are
 # recorded as 'torch-cuda' by ops.last_impl()
-TORCH_ON_CUDA = {"gdn_gates", "gdn_core", "attention", "embedding"}
+TORCH_ON_CUDA = {"gdn_gates", "embedding"}
 
 
 # native kernel launches issued through this module (benchmarks report the count of a region)
@@ -293,6 +293,78 @@ class _MaskedCE(torch.autograd.Function):
 
 def masked_ce_sum(hidden, w, targets):
     return _MaskedCE.apply(hidden, w, targets)
+
+
+# ----------------------------------------------------------------------------- GDN
+
+
+class _GDNCore(torch.autograd.Function):
+    """State-fork chunked gated delta rule over the [B, 2L] layout (chunk = block). q, k
+    [B, 2L, Hk, Dk] and v [B, 2L, Hv, Dv] may be strided views of the conv output; g, beta
+    [B, 2L, Hv]. Saves the fp32 chunk-entry states for backward."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, L, block, concat):
+        gf = g.float().contiguous()
+        bf = beta.float().contiguous()
+        o, S_in, _ = _C.gdn_fwd(q, k, v, gf, bf, L, block, concat)
+        _count(3)
+        ctx.save_for_backward(q, k, v, gf, bf, S_in)
+        ctx.cfg = (L, block, concat)
+        ctx.dtypes = (g.dtype, beta.dtype)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, gf, bf, S_in = ctx.saved_tensors
+        L, block, concat = ctx.cfg
+        dq, dk, dv, dg, db = _C.gdn_bwd(do, q, k, v, gf, bf, S_in, L, block, concat)
+        _count(3 if concat else 4)
+        Hk, Hv = q.shape[2], v.shape[2]
+        if Hv != Hk:  # the kernel returns per-v-head gradients; sum each repeat group
+            B, T2, _, Dk = dq.shape
+            dq = dq.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(q.dtype)
+            dk = dk.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(k.dtype)
+        return dq, dk, dv, dg.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None, None, None
+
+
+def gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode):
+    """chunk is the host reference's chunking; the kernels chunk at the block (<= 32)."""
+    del chunk
+    if block > 32 or L % block:
+        raise ValueError(f"native GDN needs block <= 32 dividing L (got block={block}, L={L})")
+    return _GDNCore.apply(q, k, v, g, beta, L, block, mode == "concat")
+
+
+# ----------------------------------------------------------------------------- attention
+
+
+class _Attention(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, L, block, scale, leak):
+        o, lse = _C.attn_fwd(q, k, v, L, block, scale, leak)
+        _count()
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.cfg = (L, block, scale, leak)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = _C.attn_bwd(do, q, k, v, o, lse, *ctx.cfg)
+        _count(2)
+        return dq, dk, dv, None, None, None, None
+
+
+def _rows16(t):
+    ok = t.stride(-1) == 1 and t.stride(2) == t.shape[3] and t.stride(1) % 8 == 0 and t.data_ptr() % 16 == 0 \
+        and t.stride(0) == t.shape[1] * t.stride(1)
+    return t if ok else t.contiguous()
+
+
+def attention_blockdiff(q, k, v, L, block, scale, leak_xt_prefix=False):
+    """q [B, 2L, Hq, D], k/v [B, 2L, Hk, D] (strided token rows allowed) -> o [B, 2L, Hq, D]."""
+    return _Attention.apply(_rows16(q), _rows16(k), _rows16(v), L, block, float(scale), bool(leak_xt_prefix))
 
 
 def adamw_step(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):

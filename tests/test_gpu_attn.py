@@ -1,0 +1,39 @@
+"""Complementary-mask flash attention (forward and backward) against the fp32 reference."""
+
+import pytest
+import torch
+
+from dllm_qwen38_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))
+
+
+@pytest.mark.parametrize("leak", [False, True])
+@pytest.mark.parametrize("B,L,block,Hq,Hk,D", [(2, 64, 16, 4, 2, 32), (1, 96, 32, 6, 2, 128), (1, 128, 32, 4, 1, 256),
+                                               (2, 24, 8, 4, 2, 16)])
+def test_attention_fwd_bwd(leak, B, L, block, Hq, Hk, D):
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(0)
+    T2 = 2 * L
+    q = torch.randn(B, T2, Hq, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    kv = torch.randn(B, T2, 2 * Hk * D + 8, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = kv[..., : Hk * D].reshape(B, T2, Hk, D)
+    v = kv[..., Hk * D : 2 * Hk * D].reshape(B, T2, Hk, D)
+    o = Cu.attention_blockdiff(q, k, v, L, block, D ** -0.5, leak)
+    do = torch.randn_like(o)
+    o.backward(do)
+    qf = q.detach().float().requires_grad_(True)
+    kvf = kv.detach().float().requires_grad_(True)
+    kf = kvf[..., : Hk * D].reshape(B, T2, Hk, D)
+    vf = kvf[..., Hk * D : 2 * Hk * D].reshape(B, T2, Hk, D)
+    allowed = ref.complementary_allowed(L, block, "cuda", leak)
+    orf = ref.attention(qf, kf, vf, allowed, D ** -0.5)
+    orf.backward(do.float())
+    assert _rel(o, orf) < 1e-2, _rel(o, orf)
+    assert _rel(q.grad, qf.grad) < 2e-2, _rel(q.grad, qf.grad)
+    assert _rel(kv.grad, kvf.grad) < 2e-2, _rel(kv.grad, kvf.grad)

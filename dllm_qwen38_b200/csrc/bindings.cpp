@@ -11,7 +11,8 @@ std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, co
                                  int64_t block, int64_t mode);
 at::Tensor ce_rows_(at::Tensor& logits, const at::Tensor& tgt);
 void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
-                double b2, double eps, double wd, double coef, double bc1, double bc2);
+                double b2, double eps, double wd, double coef, const c10::optional<at::Tensor>& coef_dev, double bc1,
+                double bc2);
 int64_t read_error_word(bool reset);
 at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w1, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w1, double eps);

@@ -386,7 +386,9 @@ __device__ __forceinline__ void store_as(__nv_bfloat16* p, float x) { *p = __flo
 template <typename TP, typename TG>
 __global__ void adamw_kernel(float* __restrict__ w, TP* __restrict__ p, const TG* __restrict__ g,
                              float* __restrict__ m, float* __restrict__ v, int64_t n, float lr, float b1, float b2,
-                             float eps, float wd, float coef, float bc1, float bc2) {
+                             float eps, float wd, float coef, const float* __restrict__ coef_dev, float bc1,
+                             float bc2) {
+  if (coef_dev != nullptr) coef *= *coef_dev;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float gi = to_f(g[i]) * coef;
     float wi = w[i];
@@ -402,7 +404,9 @@ __global__ void adamw_kernel(float* __restrict__ w, TP* __restrict__ p, const TG
 }
 
 void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
-                double b2, double eps, double wd, double coef, double bc1, double bc2) {
+                double b2, double eps, double wd, double coef, const c10::optional<at::Tensor>& coef_dev, double bc1,
+                double bc2) {
+  const float* cd = coef_dev.has_value() ? coef_dev->data_ptr<float>() : nullptr;
   TORCH_CHECK(w.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "adamw: contiguous");
   TORCH_CHECK(w.scalar_type() == at::kFloat, "adamw: fp32 master");
   const int64_t n = w.numel();
@@ -413,7 +417,7 @@ void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m
 #define ADAMW(TP, TG, PP, GP)                                                                                        \
   adamw_kernel<TP, TG><<<grid, 256, 0, stream()>>>(w.data_ptr<float>(), PP, GP, m.data_ptr<float>(),                  \
                                                    v.data_ptr<float>(), n, (float)lr, (float)b1, (float)b2,          \
-                                                   (float)eps, (float)wd, (float)coef, (float)bc1, (float)bc2)
+                                                   (float)eps, (float)wd, (float)coef, cd, (float)bc1, (float)bc2)
   const bool gbf = g.scalar_type() == at::kBFloat16;
   if (same || p.scalar_type() == at::kFloat) {
     float* pp = same ? nullptr : p.data_ptr<float>();

@@ -74,7 +74,9 @@ def gdn_mixer(m, n: torch.Tensor, L: int, block: int, chunk: int, fault: BreakMo
     `blockdiff.py:159-177`), done as one pass over the two-stream layout."""
     B, T2, _ = n.shape
     # one GEMM for the four input projections (qkv | z | b | a)
-    w_in = torch.cat([m.in_proj_qkv.weight, m.in_proj_z.weight, m.in_proj_b.weight, m.in_proj_a.weight], 0)
+    w_in = getattr(m, "fused_in_weight", None)  # a sharding engine may supply the contiguous block
+    if w_in is None:
+        w_in = torch.cat([m.in_proj_qkv.weight, m.in_proj_z.weight, m.in_proj_b.weight, m.in_proj_a.weight], 0)
     proj = ops.linear(n, w_in)
     raw, z, b, a = torch.split(proj, [m.conv_dim, m.value_dim, m.num_v_heads, m.num_v_heads], dim=-1)
     if fault.concat_causal_gdn:
@@ -98,7 +100,10 @@ def attn_mixer(m, n: torch.Tensor, L: int, block: int, cos, sin, fault: BreakMod
     B, T2, _ = n.shape
     Hq, Hk, Dh = m.num_heads, m.num_kv_heads, m.head_dim
     # one GEMM for q|gate, k, v
-    proj = ops.linear(n, torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight], 0))
+    w_qkv = getattr(m, "fused_qkv_weight", None)
+    if w_qkv is None:
+        w_qkv = torch.cat([m.q_proj.weight, m.k_proj.weight, m.v_proj.weight], 0)
+    proj = ops.linear(n, w_qkv)
     qg, k, v = torch.split(proj, [2 * Hq * Dh, Hk * Dh, Hk * Dh], dim=-1)
     qg = qg.reshape(B, T2, Hq, 2 * Dh)
     q, gate = qg[..., :Dh], qg[..., Dh:]
@@ -112,6 +117,9 @@ def attn_mixer(m, n: torch.Tensor, L: int, block: int, cos, sin, fault: BreakMod
 
 
 def mlp(m, x: torch.Tensor) -> torch.Tensor:
+    w_gu = getattr(m, "fused_gate_up_weight", None)
+    if w_gu is not None:
+        return ops.swiglu_mlp_fused(x, w_gu, m.down_proj.weight)
     return ops.swiglu_mlp(x, m.gate_proj.weight, m.up_proj.weight, m.down_proj.weight)
 
 

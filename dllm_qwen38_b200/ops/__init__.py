@@ -93,6 +93,32 @@ def swiglu_mlp(x, w_gate, w_up, w_down):
     return ref.linear(ref.swiglu(ref.linear(x, w_gate), ref.linear(x, w_up)), w_down)
 
 
+def swiglu_mlp_fused(x, w_gate_up, w_down):
+    """down(silu(x Wg^T) * (x Wu^T)) with w_gate_up = [Wg; Wu] one contiguous [2F, D] weight."""
+    if use_native(x, op="mlp"):
+        _record("mlp", "native")
+        return _nat().swiglu_mlp_fused(x, w_gate_up, w_down)
+    _record_ref("mlp")
+    F = w_gate_up.shape[0] // 2
+    return ref.linear(ref.swiglu(ref.linear(x, w_gate_up[:F]), ref.linear(x, w_gate_up[F:])), w_down)
+
+
+def adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
+    """Fused AdamW over flat fp32 master w, bf16 param p, grad g, moments m, v. coef is the clip
+    coefficient (float or 0-d device tensor, read on the device)."""
+    if w.is_cuda:
+        _record("adamw", "native")
+        return _nat().adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2)
+    _record_ref("adamw")
+    gg = g.float() * (coef if not torch.is_tensor(coef) else coef.float())
+    if wd:
+        w.mul_(1 - lr * wd)
+    m.mul_(b1).add_(gg, alpha=1 - b1)
+    v.mul_(b2).addcmul_(gg, gg, value=1 - b2)
+    w.addcdiv_(m, (v / bc2).sqrt_().add_(eps), value=-lr / bc1)
+    p.copy_(w)
+
+
 def gated_rmsnorm(x, z, w, eps: float):
     if use_native(x, op="gated_rmsnorm"):
         _record("gated_rmsnorm", "native")

@@ -205,19 +205,17 @@ def qk_norm_rope(q, k, wq, wk, eps, cos, sin):
 
 
 class _SwiGLUMLP(torch.autograd.Function):
-    """down(silu(x Wg^T) * (x Wu^T)): one GEMM for gate|up with the SwiGLU epilogue (keeping the
-    bf16 gate|up for backward), one for down. Backward: d(act) = dy Wd, the SwiGLU derivative
-    kernel, then dx = dgu [Wg; Wu] and the two weight-gradient GEMMs."""
+    """down(silu(x Wg^T) * (x Wu^T)) with w_gu = [Wg; Wu]: one GEMM for gate|up with the SwiGLU
+    epilogue (keeping the bf16 gate|up for backward), one for down. Backward: d(act) = dy Wd,
+    the SwiGLU derivative kernel, then dx = dgu [Wg; Wu] and the two weight-gradient GEMMs."""
 
     @staticmethod
-    def forward(ctx, x, w_gate, w_up, w_down):
-        F = w_gate.shape[0]
-        w_gu = torch.cat([w_gate, w_up], 0)
-        need = torch.is_grad_enabled() or any(ctx.needs_input_grad)
+    def forward(ctx, x, w_gu, w_down):
+        F = w_gu.shape[0] // 2
+        need = any(ctx.needs_input_grad)
         act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
         y = gemm_nt(act, w_down)
         ctx.save_for_backward(x, w_gu, w_down, act, gu)
-        ctx.F = F
         return y.reshape(*x.shape[:-1], w_down.shape[0])
 
     @staticmethod
@@ -231,11 +229,15 @@ class _SwiGLUMLP(torch.autograd.Function):
         dx = gemm_nn(dgu, w_gu).reshape(x.shape)
         dw_gu = gemm_tn(dgu, x2, out_dtype=torch.float32).to(w_gu.dtype)
         dw_down = gemm_tn(dy2, act, out_dtype=torch.float32).to(w_down.dtype)
-        return dx, dw_gu[: ctx.F], dw_gu[ctx.F :], dw_down
+        return dx, dw_gu, dw_down
 
 
 def swiglu_mlp(x, w_gate, w_up, w_down):
-    return _SwiGLUMLP.apply(x, w_gate, w_up, w_down)
+    return _SwiGLUMLP.apply(x, torch.cat([w_gate, w_up], 0), w_down)
+
+
+def swiglu_mlp_fused(x, w_gu, w_down):
+    return _SwiGLUMLP.apply(x, w_gu, w_down)
 
 
 # ----------------------------------------------------------------------------- conv
@@ -368,7 +370,14 @@ def attention_blockdiff(q, k, v, L, block, scale, leak_xt_prefix=False):
 
 
 def adamw_step(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
-    _C.adamw_step(w, p, g.contiguous(), m, v, lr, b1, b2, eps, wd, coef, bc1, bc2)
+    _C.adamw_step(w, p, g.contiguous(), m, v, lr, b1, b2, eps, wd, coef, None, bc1, bc2)
+    _count()
+
+
+def adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
+    dev_coef = coef.float().reshape(1) if torch.is_tensor(coef) else None
+    _C.adamw_step(w, p, g, m, v, lr, b1, b2, eps, wd, 1.0 if dev_coef is not None else float(coef), dev_coef,
+                  bc1, bc2)
     _count()
 
 

@@ -1,0 +1,420 @@
+"""Fully-sharded data-parallel training engine (ZeRO-3) for the block-diffusion step.
+
+Units: the embedding table, each decoder layer, and the head (final norm, plus lm_head when it
+is not tied to the embedding). A unit's parameters live flattened, in module order, in one bf16
+buffer; rank r owns elements [r*S, (r+1)*S) (S = ceil(numel / world)) together with their fp32
+master copy and fp32 AdamW moments.
+
+Per step and per layer unit:
+  forward   all-gather the unit into one of two gathered buffers (the next unit's gather is issued
+            on the communication stream while this one computes), run the layer under no_grad,
+            keep only its input (activation checkpointing);
+  backward  re-gather (prefetching the previous layer), recompute the layer with grad enabled on
+            leaf views of the gathered buffer whose .grad are pre-set views of one flat gradient
+            buffer (autograd accumulates in place), then reduce-scatter the flat gradient.
+Weight groups that one GEMM consumes (GDN qkv|z|b|a, attention q|k|v, MLP gate|up) are adjacent
+in the flat buffer, so each is ONE leaf and one contiguous slice -- no concatenation copies.
+After backward, one fused AdamW launch per unit updates the fp32 master shard and rewrites the
+bf16 shard; the clip coefficient is computed on the device from one all-reduced scalar, so the
+step has no host synchronisation.
+
+This replaces the reference's FSDP2 wrapping of a `LayerStep` (`fsdp_train.py:86-171`): the
+state fork calls submodules directly, which FSDP hooks cannot see (`fsdp_train.py:3-10`); here
+parameters are gathered explicitly per unit, so there is no hook to bypass. Reduction semantics
+match the reference: each rank's loss is its CE sum over the GLOBAL target count and gradients
+are averaged over ranks (`fsdp_train.py:39-44,162,207-221`), so AdamW sees
+(1/world) * grad(global mean CE), as in the reference.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..models.blockdiff import BreakMode, layer_step, rope_tables
+
+# weight groups consumed by one GEMM: attribute set on the submodule -> member parameter names
+FUSED_GROUPS = {
+    "linear_attn": ("fused_in_weight", ("in_proj_qkv.weight", "in_proj_z.weight", "in_proj_b.weight",
+                                        "in_proj_a.weight")),
+    "self_attn": ("fused_qkv_weight", ("q_proj.weight", "k_proj.weight", "v_proj.weight")),
+    "mlp": ("fused_gate_up_weight", ("gate_proj.weight", "up_proj.weight")),
+}
+
+
+def _world():
+    return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
+
+
+class Unit:
+    """A flat, sharded group of parameters of one module."""
+
+    def __init__(self, name: str, module: torch.nn.Module, world: int, rank: int, device, dtype=torch.bfloat16):
+        self.name, self.world, self.rank, self.device = name, world, rank, device
+        self.entries = []  # (param name, shape, offset, numel), module order
+        off, seen = 0, set()
+        for pname, p in module.named_parameters():
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            self.entries.append((pname, tuple(p.shape), off, p.numel()))
+            off += p.numel()
+        self.numel = off
+        self.shard = (off + world - 1) // world
+        self.padded = self.shard * world
+        self.p = torch.zeros(self.shard, dtype=dtype, device=device)
+        self.master = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.g = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        self.groups = self._groups()
+
+    def _groups(self):
+        """Fused groups present in this unit: (submodule path, attr, first offset, numel, rows, cols)."""
+        by_name = {n: (s, o, k) for n, s, o, k in self.entries}
+        out = []
+        for n, _, _, _ in self.entries:
+            for kind, (attr, members) in FUSED_GROUPS.items():
+                pre = n.split(kind + ".")[0] + kind + "." if (kind + ".") in n else None
+                if pre is None or n != pre + members[0]:
+                    continue
+                names = [pre + m for m in members]
+                if not all(x in by_name for x in names):
+                    continue
+                offs = [by_name[x][1] for x in names]
+                sizes = [by_name[x][2] for x in names]
+                if any(offs[i] + sizes[i] != offs[i + 1] for i in range(len(offs) - 1)):
+                    continue
+                cols = by_name[names[0]][0][1]
+                rows = sum(by_name[x][0][0] for x in names)
+                out.append((pre[:-1], attr, offs[0], sum(sizes), rows, cols))
+        return out
+
+    @torch.no_grad()
+    def load_full(self, flat: torch.Tensor) -> None:
+        lo = self.rank * self.shard
+        hi = min(self.numel, lo + self.shard)
+        self.master.zero_()
+        if hi > lo:
+            self.master[: hi - lo].copy_(flat[lo:hi].to(self.device, torch.float32))
+        self.p.copy_(self.master)
+
+    def flat_of(self, module: torch.nn.Module) -> torch.Tensor:
+        own = dict(module.named_parameters())
+        return torch.cat([own[n].detach().reshape(-1) for n, _, _, _ in self.entries])
+
+    def views(self, buf: torch.Tensor) -> dict:
+        return {n: buf[o : o + k].view(s) for n, s, o, k in self.entries}
+
+    def gather_into(self, out: torch.Tensor) -> None:
+        if self.world == 1:
+            out[: self.shard].copy_(self.p)
+        else:
+            dist.all_gather_into_tensor(out[: self.padded], self.p)
+
+    def reduce_scatter_from(self, flat_grad: torch.Tensor) -> None:
+        """flat_grad [>= padded] -> self.g (fp32), averaged over ranks (overwrites self.g)."""
+        src = flat_grad[: self.padded]
+        if self.world == 1:
+            self.g.copy_(src[: self.shard])
+        else:
+            dist.reduce_scatter_tensor(self.g, src.float() if src.dtype != torch.float32 else src,
+                                       op=dist.ReduceOp.AVG)
+
+
+class FSDPEngine:
+    """Sharded training of a `BlockDiffusionLM`.
+
+    `model` must hold the initial weights (identical on every rank, e.g. `build_model` with one
+    seed); the engine copies each rank's shards and then releases the model's parameter storage
+    (the module tree stays, on the meta device, as the structure the layer code reads)."""
+
+    def __init__(self, model, *, lr: float = 1e-5, betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.0,
+                 grad_clip: float = 1.0):
+        self.cfg = model.config
+        self.world, self.rank = _world()
+        p0 = next(model.parameters())
+        self.device, self.dtype = p0.device, p0.dtype
+        self.lr, self.betas, self.eps, self.wd, self.grad_clip = lr, betas, eps, weight_decay, grad_clip
+        self.step_count = 0
+        tm = model.text_model
+        self.tied = self.cfg.tie_word_embeddings
+        mk = lambda name, mod: Unit(name, mod, self.world, self.rank, self.device, self.dtype)  # noqa: E731
+        self.embed = mk("embed", tm.embed_tokens)
+        self.layers = [mk(f"layers.{i}", tm.layers[i]) for i in range(self.cfg.num_hidden_layers)]
+        head_mod = torch.nn.ModuleDict({"norm": tm.norm} if self.tied else {"norm": tm.norm, "lm_head": model.lm_head})
+        self.head = mk("head", head_mod)
+        self.units = [self.embed] + self.layers + [self.head]
+        for u, mod in zip(self.units, [tm.embed_tokens] + list(tm.layers) + [head_mod]):
+            u.load_full(u.flat_of(mod))
+        self.model = model.to("meta")
+        if self.tied:
+            self.model.lm_head.weight = self.model.text_model.embed_tokens.weight
+        n = max(u.padded for u in self.units)
+        self.bufs = [torch.empty(n, dtype=self.dtype, device=self.device) for _ in range(2)]
+        self.owner = [None, None]
+        self.ready = [None, None]
+        self.lru = 0
+        self.grad = torch.empty(max(u.padded for u in self.layers + [self.head]), dtype=self.dtype,
+                                device=self.device)
+        self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
+        self.comm = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
+        self.anchor = torch.zeros((), device=self.device, requires_grad=True)
+
+    # ------------------------------------------------------------------ gathers
+    def gather(self, unit: Unit, prefetch: bool = False) -> torch.Tensor:
+        for i in range(2):
+            if self.owner[i] is unit:
+                if self.ready[i] is not None:
+                    torch.cuda.current_stream(self.device).wait_event(self.ready[i])
+                    self.ready[i] = None
+                self.lru = 1 - i
+                return self.bufs[i]
+        i = self.lru
+        self.lru = 1 - i
+        self.owner[i] = unit
+        buf = self.bufs[i]
+        if prefetch and self.comm is not None:
+            self.comm.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(self.comm):
+                unit.gather_into(buf)
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+            self.ready[i] = ev
+        else:
+            unit.gather_into(buf)
+            self.ready[i] = None
+        return buf
+
+    def reduce_scatter(self, unit: Unit, flat_grad: torch.Tensor) -> None:
+        unit.reduce_scatter_from(flat_grad)
+
+    # ------------------------------------------------------------------ layer parameter binding
+    def leaves(self, unit: Unit, buf: torch.Tensor, grad: torch.Tensor | None):
+        """Parameter tensors for `unit` over gathered `buf`. With `grad`, fused groups and the other
+        parameters are leaves whose .grad are views of `grad` (autograd accumulates in place).
+        Returns (params by name, fused attrs {submodule path: (attr, tensor)})."""
+        params, fused = {}, {}
+        for path, attr, off, numel, rows, cols in unit.groups:
+            t = buf[off : off + numel].view(rows, cols)
+            if grad is not None:
+                t = t.detach().requires_grad_(True)
+                t.grad = grad[off : off + numel].view(rows, cols)
+            fused[path] = (attr, t)
+            for n, s, o, k in unit.entries:
+                if off <= o < off + numel:
+                    params[n] = t.detach()[(o - off) // cols : (o - off + k) // cols].view(s) if grad is not None \
+                        else buf[o : o + k].view(s)
+        for n, s, o, k in unit.entries:
+            if n in params:
+                continue
+            t = buf[o : o + k].view(s)
+            if grad is not None:
+                t = t.detach().requires_grad_(True)
+                t.grad = grad[o : o + k].view(s)
+            params[n] = t
+        return params, fused
+
+    # ------------------------------------------------------------------ step
+    def forward_hidden(self, x0_2, xt_2, block: int, fault: BreakMode | None = None):
+        fault = fault or BreakMode()
+        B, L = x0_2.shape
+        ids = torch.cat([xt_2, x0_2], 1)
+        h = _EmbedFn.apply(ids, self.anchor, self)
+        cos, sin = rope_tables(self.cfg, L, self.dtype, ids.device)
+        for i in range(len(self.layers)):
+            h = _LayerFn.apply(h, self.anchor, self, i, L, block, cos, sin, fault)
+        return h
+
+    def step(self, x0, prompt_len, valid_len, *, block: int, mask_id: int, n_global, gstep: int):
+        """One optimizer step on this rank's rows. n_global: the global scored-target count (python
+        number, or a 0-d device tensor). Returns this rank's loss contribution (device tensor);
+        summed over ranks it is the global mean CE."""
+        from ..train.objective import complementary_step_inputs
+
+        self.step_count += 1
+        gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
+        x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
+        n_local = int((valid_len - prompt_len).clamp(min=0).sum()) if not x0.is_cuda else None
+        h = self.forward_hidden(x0_2, xt_2, block)
+        L = x0.shape[1]
+        self.table_grad.zero_()
+        loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
+        loss.backward()
+        self._optimizer_step()
+        return loss.detach()
+
+    @torch.no_grad()
+    def _optimizer_step(self):
+        sq = torch.zeros((), device=self.device, dtype=torch.float32)
+        for u in self.units:
+            sq += u.g.pow(2).sum()
+        if self.world > 1:
+            dist.all_reduce(sq)
+        norm = sq.sqrt()
+        coef = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0)
+        b1, b2 = self.betas
+        bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
+        for u in self.units:
+            ops.adamw_flat(u.master, u.p, u.g, u.m, u.v, self.lr, b1, b2, self.eps, self.wd, coef, bc1, bc2)
+        self.last_grad_norm = norm
+
+    # ------------------------------------------------------------------ inspection
+    @torch.no_grad()
+    def full_state(self) -> dict:
+        """Gather every unit's full bf16 parameters (collective). {our key: tensor} on this device."""
+        out = {}
+        prefixes = {"embed": "text_model.embed_tokens.", "head": ""}
+        for u in self.units:
+            buf = torch.empty(u.padded, dtype=self.dtype, device=self.device)
+            u.gather_into(buf)
+            for n, s, o, k in u.entries:
+                if u.name == "head":
+                    key = ("text_model." + n) if n.startswith("norm.") else n
+                elif u.name == "embed":
+                    key = prefixes["embed"] + n
+                else:
+                    key = f"text_model.{u.name}.{n}"
+                out[key] = buf[o : o + k].view(s).clone()
+        return out
+
+
+# ---------------------------------------------------------------------------- autograd units
+
+
+class _EmbedFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, anchor, engine):
+        buf = engine.gather(engine.embed)
+        table = engine.embed.views(buf)["weight"]
+        h = torch.nn.functional.embedding(ids, table)
+        ctx.save_for_backward(ids)
+        ctx.engine = engine
+        if engine.layers:
+            engine.gather(engine.layers[0], prefetch=True)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        (ids,) = ctx.saved_tensors
+        engine = ctx.engine
+        V, D = engine.cfg.vocab_size, engine.cfg.hidden_size
+        tg = engine.table_grad[: V * D].view(V, D)  # already holds the tied head's gradient, if any
+        tg.index_add_(0, ids.reshape(-1), dh.reshape(-1, D).float())
+        engine.reduce_scatter(engine.embed, engine.table_grad)
+        return None, None, None
+
+
+def _bind(layer, fused):
+    for path, (attr, t) in fused.items():
+        sub = layer.get_submodule(path) if path else layer
+        object.__setattr__(sub, attr, t)
+
+
+def _unbind(layer, fused):
+    for path, (attr, _) in fused.items():
+        sub = layer.get_submodule(path) if path else layer
+        object.__delattr__(sub, attr)
+
+
+class _LayerFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, anchor, engine, i, L, block, cos, sin, fault):
+        unit = engine.layers[i]
+        buf = engine.gather(unit)
+        if i + 1 < len(engine.layers):
+            engine.gather(engine.layers[i + 1], prefetch=True)
+        layer = engine.model.text_model.layers[i]
+        params, fused = engine.leaves(unit, buf, None)
+        _bind(layer, fused)
+        try:
+            with torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
+                out = layer_step(layer, engine.cfg.layer_types[i], h, L, block, engine.cfg.gdn_chunk_size, cos, sin,
+                                 fault)
+        finally:
+            _unbind(layer, fused)
+        ctx.save_for_backward(h, cos, sin)
+        ctx.meta = (engine, i, L, block, fault)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        h, cos, sin = ctx.saved_tensors
+        engine, i, L, block, fault = ctx.meta
+        unit = engine.layers[i]
+        buf = engine.gather(unit)
+        if i > 0:
+            engine.gather(engine.layers[i - 1], prefetch=True)
+        grad = engine.grad[: unit.padded]
+        grad.zero_()
+        params, fused = engine.leaves(unit, buf, grad)
+        layer = engine.model.text_model.layers[i]
+        hx = h.detach().requires_grad_(True)
+        _bind(layer, fused)
+        try:
+            with torch.enable_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
+                out = layer_step(layer, engine.cfg.layer_types[i], hx, L, block, engine.cfg.gdn_chunk_size, cos, sin,
+                                 fault)
+            torch.autograd.backward(out, dout)
+        finally:
+            _unbind(layer, fused)
+        engine.reduce_scatter(unit, grad)
+        return hx.grad, None, None, None, None, None, None, None, None
+
+
+def _head_loss(engine, ht, m, x0, norm_w, head_w, n_global, n_local):
+    hn = ops.rmsnorm(ht, norm_w, engine.cfg.rms_norm_eps)
+    flat = m.reshape(-1)
+    idx = torch.nonzero_static(flat, size=n_local).squeeze(1) if n_local is not None else flat.nonzero().squeeze(1)
+    rows = hn.reshape(-1, hn.shape[-1]).index_select(0, idx)
+    tgt = x0.reshape(-1).index_select(0, idx)
+    return ops.masked_ce_sum(rows, head_w, tgt) / n_global
+
+
+class _HeadFn(torch.autograd.Function):
+    """final norm + masked-row lm_head + CE sum / global target count."""
+
+    @staticmethod
+    def forward(ctx, ht, m, x0, anchor, engine, n_global, n_local):
+        u = engine.head
+        buf = engine.gather(u)
+        v = u.views(buf)
+        if engine.tied:
+            head_w = engine.embed.views(engine.gather(engine.embed))["weight"]
+            buf = engine.gather(u)  # both resident: the two gathered slots hold head and embed
+            v = u.views(buf)
+        else:
+            head_w = v["lm_head.weight"]
+        ctx.meta = (engine, n_global, n_local)
+        ctx.save_for_backward(ht, m, x0)
+        with torch.no_grad():
+            return _head_loss(engine, ht, m, x0, v["norm.weight"], head_w, n_global, n_local)
+
+    @staticmethod
+    def backward(ctx, g):
+        engine, n_global, n_local = ctx.meta
+        ht, m, x0 = ctx.saved_tensors
+        u = engine.head
+        grad = engine.grad[: u.padded]
+        grad.zero_()
+        buf = engine.gather(u)
+        params, _ = engine.leaves(u, buf, grad)
+        if engine.tied:
+            ebuf = engine.gather(engine.embed)
+            e = engine.embed.entries[0]
+            tgrad = torch.zeros(e[1], dtype=ebuf.dtype, device=ebuf.device)
+            head_w = ebuf[e[2] : e[2] + e[3]].view(e[1]).detach().requires_grad_(True)
+            head_w.grad = tgrad
+            buf = engine.gather(u)
+            params, _ = engine.leaves(u, buf, grad)
+        else:
+            head_w = params["lm_head.weight"]
+        hx = ht.detach().requires_grad_(True)
+        with torch.enable_grad():
+            loss = _head_loss(engine, hx, m, x0, params["norm.weight"], head_w, n_global, n_local)
+        torch.autograd.backward(loss, g)
+        engine.reduce_scatter(u, grad)
+        if engine.tied:
+            engine.table_grad[: tgrad.numel()].copy_(tgrad.reshape(-1).float())
+        return hx.grad, None, None, None, None, None, None

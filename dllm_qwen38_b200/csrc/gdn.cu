@@ -819,3 +819,111 @@ std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, con
 }
 
 }  // namespace bdllm
+
+// ============================================================================ no-allocation entry
+// The forward above, with its working memory taken from a fixed array instead of allocated
+// tensors. Declared (and its contract described) in gdn_noalloc.h.
+#include <atomic>
+#include <cstdio>
+
+#include "gdn_noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) unsigned char g_gdn_noalloc_scratch[BDLLM_GDN_NOALLOC_SCRATCH_BYTES];
+
+// this device's address of the array, looked up on the first call made with the device current
+static std::atomic<void*> g_gdn_noalloc_addr[64];
+
+int noalloc_fail(char* err, int err_len, int code, const char* msg) {
+  if (err != nullptr && err_len > 0) snprintf(err, (size_t)err_len, "%s", msg);
+  return code;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+template <int D>
+int noalloc_run(bdllm::gdn::Args a, unsigned char* base, size_t cap, cudaStream_t stream, char* err, int err_len) {
+  using namespace bdllm::gdn;
+  const size_t units = (size_t)a.B * a.nb * a.Hv;
+  const size_t C = (size_t)a.C;
+  size_t off = 0;
+  auto take = [&](size_t floats) {
+    float* p = reinterpret_cast<float*>(base + off);
+    off = align256(off + floats * sizeof(float));
+    return p;
+  };
+  a.U = take(units * C * D);
+  a.W = take(units * C * D);
+  a.Kt = take(units * C * D);
+  a.Ec = take(units);
+  a.S_in = take(units * D * D);
+  a.Vp = take(units * C * D);
+  if (off > cap) {
+    char msg[160];
+    snprintf(msg, sizeof msg, "problem needs %zu bytes of scratch; the fixed array holds %zu", off, cap);
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_TOO_LARGE, msg);
+  }
+  const int BH = a.B * a.Hv;
+  const int big = Smem<D, D>::floats * 4;
+  const int rec = (3 * 32 * D + 32 * 32 + D * 32) * 4;
+  if (cudaFuncSetAttribute(fwd_prep_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess ||
+      cudaFuncSetAttribute(fwd_recur_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, rec) != cudaSuccess ||
+      cudaFuncSetAttribute(fwd_out_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "cudaFuncSetAttribute failed");
+  fwd_prep_kernel<D, D><<<dim3(a.nb, BH), NT, big, stream>>>(a);
+  fwd_recur_kernel<D, D><<<dim3(BH, (D + 31) / 32), NT, rec, stream>>>(a);
+  fwd_out_kernel<D, D><<<dim3(2 * a.nb, BH), NT, big, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "kernel launch failed");
+  return BDLLM_NOALLOC_OK;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int bdllm_gdn_forward_noalloc(
+    const void* q, const void* k, const void* v, int64_t ld_qk, int64_t ld_v, const float* g, const float* beta,
+    void* o, int B, int L, int Hk, int Hv, int D, int block, cudaStream_t stream, char* err, int err_len) {
+  if (q == nullptr || k == nullptr || v == nullptr || g == nullptr || beta == nullptr || o == nullptr)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "null pointer argument");
+  if (B < 1 || L < 1 || Hk < 1 || Hv < 1 || Hv % Hk != 0 || block < 1 || block > 32 || L % block != 0)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "need block <= 32 dividing L and Hv % Hk == 0");
+  if (D != 16 && D != 32 && D != 64 && D != 128)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "head dim must be 16, 32, 64 or 128");
+  if (ld_qk % 8 != 0 || ld_v % 8 != 0 || ld_qk < 2 * (int64_t)Hk * D || ld_v < (int64_t)Hv * D)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "token strides too small or not multiples of 8");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "cudaGetDevice failed");
+  void* base = g_gdn_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (base == nullptr) {  // first call on this device: look up the array's device address
+    if (cudaGetSymbolAddress(&base, g_gdn_noalloc_scratch) != cudaSuccess || base == nullptr)
+      return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "cudaGetSymbolAddress failed");
+    g_gdn_noalloc_addr[dev].store(base, std::memory_order_release);
+  }
+  bdllm::gdn::Args a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q);
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k);
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v);
+  a.ldqk = ld_qk;
+  a.ldv = ld_v;
+  a.g = g;
+  a.beta = beta;
+  a.B = B;
+  a.L = L;
+  a.Hk = Hk;
+  a.Hv = Hv;
+  a.C = block;
+  a.concat = 0;
+  a.nb = L / block;
+  a.scale = 1.f / sqrtf((float)D);
+  a.o = reinterpret_cast<__nv_bfloat16*>(o);
+  unsigned char* s = reinterpret_cast<unsigned char*>(base);
+  const size_t cap = BDLLM_GDN_NOALLOC_SCRATCH_BYTES;
+  switch (D) {
+    case 16: return noalloc_run<16>(a, s, cap, stream, err, err_len);
+    case 32: return noalloc_run<32>(a, s, cap, stream, err, err_len);
+    case 64: return noalloc_run<64>(a, s, cap, stream, err, err_len);
+    default: return noalloc_run<128>(a, s, cap, stream, err, err_len);
+  }
+}

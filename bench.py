@@ -109,7 +109,13 @@ def run_native(a, rank, world):
     dev = torch.device("cuda", torch.cuda.current_device())
     cfg = preset(a.model, layers=a.layers)
     model = build_model(cfg, seed=a.seed, device=dev, dtype=torch.bfloat16)
-    if world > 1:
+    if a.engine == "fsdp":
+        from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+
+        trainer = FSDPTrainer(model, block=a.block, mask_id=cfg.mask_id, lr=a.lr)
+        del model
+        parallel = f"fsdp{world}"
+    elif world > 1:
         from dllm_qwen38_b200.parallel.dp import ReplicatedDP
 
         trainer = ReplicatedDP(model, block=a.block, mask_id=cfg.mask_id, lr=a.lr, checkpointing=not a.no_ckpt,
@@ -119,6 +125,7 @@ def run_native(a, rank, world):
         trainer = Trainer(model, block=a.block, mask_id=cfg.mask_id, lr=a.lr, checkpointing=not a.no_ckpt,
                           seed=a.seed, rank=rank)
         parallel = "single"
+    torch.cuda.empty_cache()
     g = torch.Generator().manual_seed(a.seed + rank)
     B, L = a.micro_batch, a.seq_len
     host_x = [torch.randint(0, cfg.mask_id, (B, L), generator=g).pin_memory() for _ in range(2)]
@@ -287,6 +294,8 @@ def main(argv=None) -> int:
     p.add_argument("--micro-batch", type=int, default=1)
     p.add_argument("--lr", type=float, default=1e-5)
     p.add_argument("--no-ckpt", action="store_true")
+    p.add_argument("--engine", default="fsdp", choices=["fsdp", "module"],
+                   help="native arm: the sharded engine (default, every N) or the module trainer")
     p.add_argument("--seed", type=int, default=0)
     a = p.parse_args(argv)
     if a.warmup < 3:

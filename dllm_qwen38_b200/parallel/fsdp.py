@@ -67,7 +67,9 @@ class Unit:
         self.master = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
-        self.g = torch.zeros(self.shard, dtype=torch.float32, device=device)
+        # the reduce-scattered gradient: fp32 when ranks are summed, the local (model dtype)
+        # gradient itself at world 1 (no reduction, and half the memory of an fp32 copy)
+        self.g = torch.zeros(self.shard, dtype=torch.float32 if world > 1 else dtype, device=device)
         self.groups = self._groups()
 
     def _groups(self):
@@ -151,7 +153,7 @@ class FSDPEngine:
         self.model = model.to("meta")
         if self.tied:
             self.model.lm_head.weight = self.model.text_model.embed_tokens.weight
-        n = max(u.padded for u in self.units)
+        n = max(u.padded for u in self.units) if self.world > 1 else 0
         self.bufs = [torch.empty(n, dtype=self.dtype, device=self.device) for _ in range(2)]
         self.owner = [None, None]
         self.ready = [None, None]
@@ -164,6 +166,8 @@ class FSDPEngine:
 
     # ------------------------------------------------------------------ gathers
     def gather(self, unit: Unit, prefetch: bool = False) -> torch.Tensor:
+        if self.world == 1:  # the shard is the whole unit
+            return unit.p
         for i in range(2):
             if self.owner[i] is unit:
                 if self.ready[i] is not None:
@@ -227,16 +231,16 @@ class FSDPEngine:
             h = _LayerFn.apply(h, self.anchor, self, i, L, block, cos, sin, fault)
         return h
 
-    def step(self, x0, prompt_len, valid_len, *, block: int, mask_id: int, n_global, gstep: int):
-        """One optimizer step on this rank's rows. n_global: the global scored-target count (python
-        number, or a 0-d device tensor). Returns this rank's loss contribution (device tensor);
-        summed over ranks it is the global mean CE."""
+    def step(self, x0, prompt_len, valid_len, *, block: int, mask_id: int, n_local: int, n_global, gstep: int):
+        """One optimizer step on this rank's rows (already on the device). n_local: this rank's
+        scored-target count (host int); n_global: the global count (python number or 0-d device
+        tensor). Returns this rank's loss contribution (device tensor); summed over ranks it is the
+        global mean CE."""
         from ..train.objective import complementary_step_inputs
 
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
         x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
-        n_local = int((valid_len - prompt_len).clamp(min=0).sum()) if not x0.is_cuda else None
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
@@ -259,6 +263,12 @@ class FSDPEngine:
         for u in self.units:
             ops.adamw_flat(u.master, u.p, u.g, u.m, u.v, self.lr, b1, b2, self.eps, self.wd, coef, bc1, bc2)
         self.last_grad_norm = norm
+        self.invalidate()
+
+    def invalidate(self) -> None:
+        """Forget gathered copies (their shards changed)."""
+        self.owner = [None, None]
+        self.ready = [None, None]
 
     # ------------------------------------------------------------------ inspection
     @torch.no_grad()
@@ -418,3 +428,34 @@ class _HeadFn(torch.autograd.Function):
         if engine.tied:
             engine.table_grad[: tgrad.numel()].copy_(tgrad.reshape(-1).float())
         return hx.grad, None, None, None, None, None, None
+
+
+class FSDPTrainer:
+    """Public step API over the sharded engine, same call as `train.trainer.Trainer.step`."""
+
+    def __init__(self, model, *, block: int, mask_id: int, lr: float = 1e-5, grad_clip: float = 1.0,
+                 uniform_rows: bool = True, **_ignored):
+        self.engine = FSDPEngine(model, lr=lr, grad_clip=grad_clip)
+        self.block, self.mask_id = block, mask_id
+        self.uniform_rows = uniform_rows
+        self.gstep = 0
+        self.world, self.rank = self.engine.world, self.engine.rank
+
+    def step(self, x0, prompt_len, valid_len, n_targets: int | None = None):
+        """x0 [b, L] this rank's rows (host or device); returns this rank's loss contribution."""
+        self.gstep += 1
+        if n_targets is None:
+            n_targets = int((valid_len - prompt_len).clamp(min=0).sum())
+        dev = self.engine.device
+        x0 = x0.to(dev, non_blocking=True)
+        prompt_len = prompt_len.to(dev, non_blocking=True)
+        valid_len = valid_len.to(dev, non_blocking=True)
+        if self.world == 1 or self.uniform_rows:
+            n_global = n_targets * self.world  # every rank scores the same count (no communication)
+        else:
+            n_global = torch.tensor(float(n_targets), device=dev)
+            dist.all_reduce(n_global)
+        if n_targets == 0:
+            raise ValueError("a step with zero scored targets on this rank; pass uniform rows or skip it")
+        return self.engine.step(x0, prompt_len, valid_len, block=self.block, mask_id=self.mask_id,
+                                n_local=n_targets, n_global=n_global, gstep=self.gstep)

@@ -1,0 +1,94 @@
+"""FSDP engine on CPU: world 1 against the single-device trainer, world 2 (gloo ranks) against
+replicated data parallelism with the same masks and reduction semantics."""
+
+import copy
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dllm_qwen38_b200.config import preset
+from dllm_qwen38_b200.models.qwen35 import build_model
+
+
+def _batches(B, L, vocab, seed, n=3):
+    g = torch.Generator().manual_seed(seed)
+    return [(torch.randint(0, vocab - 1, (B, L), generator=g), torch.zeros(B, dtype=torch.long),
+             torch.full((B,), L, dtype=torch.long)) for _ in range(n)]
+
+
+def _flat(sd):
+    return {k: v.detach().float().cpu() for k, v in sd.items()}
+
+
+@pytest.mark.parametrize("name", ["tiny_ref", "tiny"])  # untied head / tied head
+def test_world1_fsdp_matches_single_device_trainer(name):
+    from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+    from dllm_qwen38_b200.train.trainer import Trainer
+
+    torch.manual_seed(0)
+    cfg = preset(name)
+    m1 = build_model(cfg, seed=0)
+    m2 = copy.deepcopy(m1)
+    if cfg.tie_word_embeddings:
+        m2.lm_head.weight = m2.text_model.embed_tokens.weight
+    t1 = Trainer(m1, block=8, mask_id=cfg.mask_id, lr=1e-3, checkpointing=False)
+    t2 = FSDPTrainer(m2, block=8, mask_id=cfg.mask_id, lr=1e-3)
+    for x0, pl, vl in _batches(2, 32, cfg.vocab_size, 1):
+        l1 = t1.step(x0, pl, vl)
+        l2 = t2.step(x0, pl, vl)
+        assert abs(float(l1) - float(l2)) < 1e-4 * max(1.0, abs(float(l1)))
+    ref = _flat({f"text_model.{k}" if not k.startswith("lm_head") else k: v
+                 for k, v in {**{("text_model." + k)[len("text_model."):]: v for k, v in m1.text_model.state_dict().items()},
+                              "lm_head.weight": m1.lm_head.weight}.items()})
+    got = _flat(t2.engine.full_state())
+    for k, v in got.items():
+        assert k in ref, k
+        assert float((v - ref[k]).abs().max()) < 1e-4, k
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from dllm_qwen38_b200.parallel.dp import ReplicatedDP
+        from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+
+        torch.manual_seed(0)
+        cfg = preset("tiny_ref")
+        m1 = build_model(cfg, seed=0)
+        m2 = copy.deepcopy(m1)
+        dp = ReplicatedDP(m1, block=8, mask_id=cfg.mask_id, lr=1e-3, checkpointing=False, rank=rank, world=world)
+        fs = FSDPTrainer(m2, block=8, mask_id=cfg.mask_id, lr=1e-3)
+        losses = []
+        for x0, pl, vl in _batches(2 * world, 32, cfg.vocab_size, 2):
+            sl = slice(rank * 2, (rank + 1) * 2)
+            a = dp.step(x0[sl], pl[sl], vl[sl])
+            b = fs.step(x0[sl], pl[sl], vl[sl])
+            losses.append((float(a), float(b)))
+        got = _flat(fs.engine.full_state())
+        ref = {("text_model." + k): v.detach().float() for k, v in m1.text_model.state_dict().items()}
+        ref["lm_head.weight"] = m1.lm_head.weight.detach().float()
+        worst = max(float((v - ref[k]).abs().max()) for k, v in got.items())
+        out.put((rank, losses, worst))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_world2_fsdp_matches_replicated_dp_on_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29000 + os.getpid() % 2000
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, losses, worst in res:
+        for a, b in losses:
+            assert abs(a - b) < 1e-4 * max(1.0, abs(a)), (rank, losses)
+        assert worst < 1e-4, (rank, worst)

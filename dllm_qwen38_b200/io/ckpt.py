@@ -1,0 +1,252 @@
+"""Checkpoints: resumable sharded saves of the FSDP engine, exports and imports.
+
+Resumable save (`save_engine` / `load_engine`), the reference's contract (`fsdp_train.py:352-517`):
+  * directory ``<ckpt_dir>/step-%08d`` written by torch.distributed.checkpoint (every rank writes
+    its own shards into ``step-N.tmp``); after a barrier rank 0 renames it to ``step-N`` (the rename
+    is the commit point: a run killed mid-save leaves only a ``.tmp``), then keeps the last two;
+  * contents: {"model": flat bf16 parameter shards, "optim": fp32 master + AdamW moments + step,
+    "step", "seq_tokens"}; each unit's shard is stored as a DTensor sharded on dim 0 over the
+    world, so a checkpoint written at one world size loads at another (DCP reshards);
+  * optional per-rank SHA256 fingerprints of the model and optimizer shards, written to
+    ``fingerprints/step-N.tsv`` as ``rank \\t model-fp \\t opt-fp`` at save and verified at load;
+    a missing or unparseable file fails closed (all-reduced, identical on every rank);
+  * no RNG state: masks are a pure function of (global step, rank), so a resumed window replays
+    the uninterrupted run's masks (`fsdp_train.py:418-422,607`).
+
+Exports/imports:
+  * `export_safetensors`: full parameters under our keys (``text_model.<HF text key>``,
+    ``lm_head.weight``) -- the reference's single-device layout (`train.py:270-276`);
+  * `reference_dcp_tensors` + `plain_fqn`: read a reference FSDP checkpoint (per-parameter
+    DTensors named ``text_model.layers.N.layer.<...>``, `gsm8k_eval.py:249-285`) as plain tensors.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import os
+import re
+import shutil
+
+import torch
+import torch.distributed as dist
+
+
+def ckpt_path(ckpt_dir: str, gstep: int) -> str:
+    return os.path.join(ckpt_dir, f"step-{gstep:08d}")
+
+
+def latest_checkpoint(ckpt_dir: str) -> int | None:
+    """Highest committed step-N (a `.tmp` left by an interrupted save does not count)."""
+    try:
+        entries = os.listdir(ckpt_dir)
+    except FileNotFoundError:
+        return None
+    ns = []
+    for e in entries:
+        if e.startswith("step-") and not e.endswith(".tmp"):
+            try:
+                ns.append(int(e.split("-")[1]))
+            except ValueError:
+                pass
+    return max(ns) if ns else None
+
+
+def fingerprint(tensors: dict) -> str:
+    """SHA256 over the raw bytes of a flat {name: tensor} map (sorted), first 16 hex digits."""
+    h = hashlib.sha256()
+    for k in sorted(tensors):
+        t = tensors[k]
+        h.update(f"{k}\x1f".encode())
+        if torch.is_tensor(t):
+            u = t.detach().contiguous().cpu()
+            h.update(f"{tuple(u.shape)}\x1f{u.dtype}\x1f".encode())
+            h.update(u.reshape(-1).view(torch.uint8).numpy().tobytes())
+        else:
+            h.update(repr(t).encode())
+    return h.hexdigest()[:16]
+
+
+def _world():
+    return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
+
+
+def _barrier():
+    if dist.is_initialized():
+        dist.barrier()
+
+
+def _local_maps(engine):
+    model = {f"{u.name}": u.p for u in engine.units}
+    optim = {}
+    for u in engine.units:
+        optim[f"{u.name}.master"] = u.master
+        optim[f"{u.name}.exp_avg"] = u.m
+        optim[f"{u.name}.exp_avg_sq"] = u.v
+    return model, optim
+
+
+def _as_dtensor(t: torch.Tensor, world: int):
+    """Wrap this rank's dim-0 shard as a DTensor over all ranks (single-process: plain tensor)."""
+    if world == 1 or not dist.is_initialized():
+        return t
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import DTensor, Shard
+
+    mesh = init_device_mesh(t.device.type, (world,))
+    return DTensor.from_local(t, mesh, [Shard(0)], run_check=False, shape=torch.Size([t.numel() * world]),
+                              stride=(1,))
+
+
+def save_engine(engine, ckpt_dir: str, gstep: int, seq_tokens: int, *, fingerprint_save: bool = True,
+                keep: int = 2) -> str:
+    """Collective: every rank writes its shards, rank 0 commits by rename and prunes."""
+    import torch.distributed.checkpoint as dcp
+
+    world, rank = _world()
+    model, optim = _local_maps(engine)
+    if fingerprint_save:
+        fp = f"{fingerprint(model)} {fingerprint(optim)}"
+        fps = [None] * world
+        if world > 1:
+            dist.all_gather_object(fps, fp)
+        else:
+            fps = [fp]
+        if rank == 0:
+            os.makedirs(os.path.join(ckpt_dir, "fingerprints"), exist_ok=True)
+            with open(os.path.join(ckpt_dir, "fingerprints", f"step-{gstep}.tsv"), "w") as f:
+                for r, s in enumerate(fps):
+                    mfp, ofp = s.split()
+                    f.write(f"{r}\t{mfp}\t{ofp}\n")
+    state = {
+        "model": {k: _as_dtensor(v, world) for k, v in model.items()},
+        "optim": {**{k: _as_dtensor(v, world) for k, v in optim.items()},
+                  "step": torch.tensor(engine.step_count, dtype=torch.int64)},
+        "step": torch.tensor(gstep, dtype=torch.int64),
+        "seq_tokens": torch.tensor(seq_tokens, dtype=torch.int64),
+    }
+    tmp = ckpt_path(ckpt_dir, gstep) + ".tmp"
+    dcp.save(state, checkpoint_id=tmp, no_dist=not dist.is_initialized())
+    _barrier()
+    if rank == 0:
+        final = ckpt_path(ckpt_dir, gstep)
+        if os.path.exists(final):
+            shutil.rmtree(final)
+        os.rename(tmp, final)
+        kept = sorted((int(e.split("-")[1]), e) for e in os.listdir(ckpt_dir)
+                      if e.startswith("step-") and not e.endswith(".tmp"))
+        for _, e in kept[:-keep]:
+            shutil.rmtree(os.path.join(ckpt_dir, e))
+    _barrier()
+    return ckpt_path(ckpt_dir, gstep)
+
+
+def load_engine(engine, ckpt_dir: str, gstep: int, *, verify: bool = True) -> dict:
+    """Restore shards in place. Returns {"seq_tokens", "step", "fp_ok"}; fp_ok is False on every
+    rank when any rank's restored state fails (or cannot be) verified against the saved
+    fingerprints (fail closed)."""
+    import torch.distributed.checkpoint as dcp
+
+    world, rank = _world()
+    model, optim = _local_maps(engine)
+    state = {
+        "model": {k: _as_dtensor(v, world) for k, v in model.items()},
+        "optim": {**{k: _as_dtensor(v, world) for k, v in optim.items()},
+                  "step": torch.zeros((), dtype=torch.int64)},
+        "step": torch.zeros((), dtype=torch.int64),
+        "seq_tokens": torch.zeros((), dtype=torch.int64),
+    }
+    dcp.load(state, checkpoint_id=ckpt_path(ckpt_dir, gstep), no_dist=not dist.is_initialized())
+    engine.step_count = int(state["optim"]["step"])
+    engine.invalidate()
+    fp_ok = True
+    if verify:
+        got = f"{fingerprint(model)} {fingerprint(optim)}"
+        expected = None
+        fp_file = os.path.join(ckpt_dir, "fingerprints", f"step-{gstep}.tsv")
+        if os.path.exists(fp_file):
+            for ln in open(fp_file):
+                parts = ln.rstrip("\n").split("\t")
+                if len(parts) >= 3 and parts[0] == str(rank):
+                    expected = parts[1] + " " + parts[2]
+        bad = expected is None or expected != got
+        flag = torch.tensor([1.0 if bad else 0.0], device=engine.device)
+        if world > 1:
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+        fp_ok = float(flag) == 0.0
+    return {"seq_tokens": int(state["seq_tokens"]), "step": int(state["step"]), "fp_ok": fp_ok}
+
+
+# ----------------------------------------------------------------------------- exports / imports
+
+
+@torch.no_grad()
+def export_safetensors(engine_or_model, path: str) -> None:
+    """Full parameters under `text_model.*` / `lm_head.weight` (collective for an engine; rank 0
+    writes)."""
+    from safetensors.torch import save_file
+
+    if hasattr(engine_or_model, "full_state"):
+        state = engine_or_model.full_state()
+        if engine_or_model.tied and "lm_head.weight" not in state:
+            state["lm_head.weight"] = state["text_model.embed_tokens.weight"]
+    else:
+        m = engine_or_model
+        state = {f"text_model.{k}": v for k, v in m.text_model.state_dict().items()}
+        state["lm_head.weight"] = m.lm_head.weight
+    _, rank = _world()
+    if rank == 0:
+        save_file({k: v.detach().cpu().contiguous().clone() for k, v in state.items()}, path)
+    _barrier()
+
+
+def plain_fqn(dcp_fqn: str) -> str | None:
+    """Reference checkpoint FQN -> our key; None = not a model key. Strips the LayerStep `.layer.`
+    hop: `text_model.layers.7.layer.mlp.x` -> `text_model.layers.7.mlp.x` (`gsm8k_eval.py:249-261`)."""
+    if dcp_fqn.startswith("text_model."):
+        m = re.match(r"^text_model\.(layers\.\d+)\.layer\.(.+)$", dcp_fqn)
+        return f"text_model.{m.group(1)}.{m.group(2)}" if m else dcp_fqn
+    if dcp_fqn.startswith("lm_head."):
+        return dcp_fqn
+    return None
+
+
+def reference_dcp_tensors(path: str) -> tuple[dict, int, int]:
+    """The 'model' half of a reference FSDP checkpoint as plain CPU tensors (resharding read with
+    no process group), plus (step, seq_tokens)."""
+    from torch.distributed.checkpoint import FileSystemReader, load as dcp_load
+
+    reader = FileSystemReader(path)
+    md = reader.read_metadata()
+    model = {}
+    for key, meta in md.state_dict_metadata.items():
+        if not key.startswith("model."):
+            continue
+        if not hasattr(meta, "size"):
+            raise ValueError(f"{path}: non-tensor entry under 'model': {key}")
+        model[key[len("model."):]] = torch.empty(tuple(meta.size), dtype=meta.properties.dtype)
+    step, seq = torch.zeros((), dtype=torch.int64), torch.zeros((), dtype=torch.int64)
+    dcp_load({"model": model, "step": step, "seq_tokens": seq}, storage_reader=reader, no_dist=True)
+    return model, int(step), int(seq)
+
+
+def restore_into(model, tensors: dict, ctx: str = "ckpt") -> None:
+    """Load {reference or our FQN: tensor} into a `BlockDiffusionLM`; any missing, unexpected or
+    foreign key raises (a partial restore would score silently wrong, `gsm8k_eval.py:306-328`)."""
+    own = dict(model.named_parameters(remove_duplicate=False))
+    seen, bad = set(), []
+    for fqn, t in tensors.items():
+        k = plain_fqn(fqn)
+        if k is None:
+            bad.append("ckpt?" + fqn)
+            continue
+        if k not in own:
+            bad.append("model?" + k)
+            continue
+        with torch.no_grad():
+            own[k].copy_(t.to(own[k].dtype))
+        seen.add(k)
+    tied = model.config.tie_word_embeddings
+    missing = [k for k in own if k not in seen and not (tied and k == "lm_head.weight")]
+    bad += ["model:" + k for k in missing]
+    if bad:
+        raise ValueError(f"{ctx}: restore incomplete ({len(bad)} problems, first 10: {bad[:10]})")

@@ -18,7 +18,8 @@
 //   bwd_prep   clean chunks: P^T dO, K~, q~ = diag(E) q^, W, e^gam_C                -> scratch
 //   bwd_recur  reverse recurrence: dS_out[c] (gradient of the state after chunk c), dV'_c
 //   bwd_chunk  clean chunks, parallel: input gradients
-// Math is fp32 in shared memory with 4x4 register tiles (CUDA cores).
+// The per-chunk products run on tensor cores (mma.sync TF32 with fp32 accumulation) when they tile
+// into 16 x 32 x 8, and in fp32 on CUDA cores otherwise (small test shapes).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -94,16 +95,126 @@ __device__ __forceinline__ void mm(int M, int N, int K, const float* A, int lda,
   }
 }
 
-// tile selection: 4 when the dimension allows it
+// Tensor-core path: each warp owns 16 x 32 output tiles and runs mma.sync m16n8k8 with TF32
+// operands (rounded from the fp32 shared tiles, cvt.rna) and fp32 accumulation. Fragment layout
+// (g = lane / 4, t = lane % 4): A a0 (g, t) a1 (g+8, t) a2 (g, t+4) a3 (g+8, t+4); B b0 (t, g)
+// b1 (t+4, g); C c0 (g, 2t) c1 (g, 2t+1) c2 (g+8, 2t) c3 (g+8, 2t+1).
+__device__ __forceinline__ uint32_t tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+template <bool AT, bool BT, typename Epi>
+__device__ __forceinline__ void mm_tc(int M, int N, int K, const float* A, int lda, const float* B, int ldb, Epi epi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int tiles_n = N / 32, tiles = (M / 16) * tiles_n;
+  for (int tile = warp; tile < tiles; tile += NT / 32) {
+    const int m0 = (tile / tiles_n) * 16, n0 = (tile % tiles_n) * 32;
+    float c[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      auto Aget = [&](int m, int k) { return AT ? A[k * lda + m] : A[m * lda + k]; };
+      const uint32_t a0 = tf32(Aget(m0 + g, k0 + t)), a1 = tf32(Aget(m0 + g + 8, k0 + t));
+      const uint32_t a2 = tf32(Aget(m0 + g, k0 + t + 4)), a3 = tf32(Aget(m0 + g + 8, k0 + t + 4));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = n0 + j * 8 + g;
+        const uint32_t b0 = tf32(BT ? B[n * ldb + k0 + t] : B[(k0 + t) * ldb + n]);
+        const uint32_t b1 = tf32(BT ? B[n * ldb + k0 + t + 4] : B[(k0 + t + 4) * ldb + n]);
+        asm volatile(
+            "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[j][0]), "+f"(c[j][1]), "+f"(c[j][2]), "+f"(c[j][3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + j * 8 + 2 * t;
+      epi(m0 + g, n, c[j][0]);
+      epi(m0 + g, n + 1, c[j][1]);
+      epi(m0 + g + 8, n, c[j][2]);
+      epi(m0 + g + 8, n + 1, c[j][3]);
+    }
+  }
+}
+
+// tensor cores when the shape tiles into 16 x 32 x 8, else fp32 CUDA cores (4x4 register tiles)
 template <bool AT, bool BT, typename Epi>
 __device__ __forceinline__ void matmul(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
                                        Epi epi) {
-  if (M % 4 == 0 && N % 4 == 0)
+  if (M % 16 == 0 && N % 32 == 0 && K % 8 == 0)
+    mm_tc<AT, BT>(M, N, K, A, lda, B, ldb, epi);
+  else if (M % 4 == 0 && N % 4 == 0)
     mm<4, 4, AT, BT>(M, N, K, A, lda, B, ldb, epi);
   else if (N % 4 == 0)
     mm<1, 4, AT, BT>(M, N, K, A, lda, B, ldb, epi);
   else
     mm<1, 1, AT, BT>(M, N, K, A, lda, B, ldb, epi);
+}
+
+// out[m] += sum_n f(m, n, (A B)_mn) for an M x N product. On tensor cores the four lanes that share
+// a row reduce with shuffles first, so each warp tile issues one shared atomic per row.
+template <bool AT, bool BT, typename F>
+__device__ __forceinline__ void matmul_rowsum(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
+                                              F f, float* out) {
+  if (M % 16 == 0 && N % 32 == 0 && K % 8 == 0) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int tiles_n = N / 32, tiles = (M / 16) * tiles_n;
+    for (int tile = warp; tile < tiles; tile += NT / 32) {
+      const int m0 = (tile / tiles_n) * 16, n0 = (tile % tiles_n) * 32;
+      float c[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+      for (int k0 = 0; k0 < K; k0 += 8) {
+        auto Aget = [&](int m, int k) { return AT ? A[k * lda + m] : A[m * lda + k]; };
+        const uint32_t a0 = tf32(Aget(m0 + g, k0 + t)), a1 = tf32(Aget(m0 + g + 8, k0 + t));
+        const uint32_t a2 = tf32(Aget(m0 + g, k0 + t + 4)), a3 = tf32(Aget(m0 + g + 8, k0 + t + 4));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int n = n0 + j * 8 + g;
+          const uint32_t b0 = tf32(BT ? B[n * ldb + k0 + t] : B[(k0 + t) * ldb + n]);
+          const uint32_t b1 = tf32(BT ? B[n * ldb + k0 + t + 4] : B[(k0 + t + 4) * ldb + n]);
+          asm volatile(
+              "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+              "{%0,%1,%2,%3};"
+              : "+f"(c[j][0]), "+f"(c[j][1]), "+f"(c[j][2]), "+f"(c[j][3])
+              : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+        }
+      }
+      float r0 = 0.f, r1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = n0 + j * 8 + 2 * t;
+        r0 += f(m0 + g, n, c[j][0]) + f(m0 + g, n + 1, c[j][1]);
+        r1 += f(m0 + g + 8, n, c[j][2]) + f(m0 + g + 8, n + 1, c[j][3]);
+      }
+      r0 += __shfl_xor_sync(0xffffffffu, r0, 1);
+      r0 += __shfl_xor_sync(0xffffffffu, r0, 2);
+      r1 += __shfl_xor_sync(0xffffffffu, r1, 1);
+      r1 += __shfl_xor_sync(0xffffffffu, r1, 2);
+      if (t == 0) {
+        atomicAdd(&out[m0 + g], r0);
+        atomicAdd(&out[m0 + g + 8], r1);
+      }
+    }
+  } else {
+    matmul<AT, BT>(M, N, K, A, lda, B, ldb, [&](int m, int n, float x) { atomicAdd(&out[m], f(m, n, x)); });
+  }
+}
+
+// out[i] += sum_d X[i][d] * Y[i][d] over C rows of D, warp per row
+__device__ __forceinline__ void rowdot(int C, int D, const float* X, int ldx, const float* Y, int ldy, float* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < C; i += NT / 32) {
+    float acc = 0.f;
+    for (int d = lane; d < D; d += 32) acc += X[i * ldx + d] * Y[i * ldy + d];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) out[i] += acc;
+  }
 }
 
 __device__ __forceinline__ float wsum(float v) {
@@ -119,23 +230,53 @@ __device__ __forceinline__ int64_t tok(const Args& a, int b, int stream, int c, 
   return (int64_t)b * 2 * a.L + ((stream && !a.concat) ? a.L : 0) + (int64_t)c * a.C + i;
 }
 
+// ------------------------------------------------------------------ shared-tile strides
+// Row strides of the fp32 shared tiles are padded by 4 floats: with that, every TF32 fragment read
+// pattern of mm_tc (lanes spanning 8 rows x 4 columns or 4 rows x 8 columns) hits 32 distinct banks.
+template <int D>
+struct Ld {
+  static constexpr int v = D + 4;
+};
+constexpr int LDC = 36;  // [C][C] tiles (C <= 32)
+
 // ------------------------------------------------------------------ per-chunk loads
 // sQ/sK [C][Dk] l2-normalised (q scaled), sV [C][Dv], sgam[C] = cumsum g, sbeta[C].
 template <int Dk, int Dv>
 __device__ void load_chunk(const Args& a, int b, int stream, int c, int h, float* sQ, float* sK, float* sV,
                            float* sgam, float* sbeta, bool need_q, bool need_v) {
+  constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
   const int C = a.C;
   const int hk = h / (a.Hv / a.Hk);
-  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-    const int i = idx / Dk, d = idx % Dk;
+  for (int idx = threadIdx.x; idx < C * (Dk / 8); idx += NT) {
+    const int i = idx / (Dk / 8), d = (idx % (Dk / 8)) * 8;
     const int64_t t = tok(a, b, stream, c, i);
-    sK[i * Dk + d] = __bfloat162float(a.k[t * a.ldqk + hk * Dk + d]);
-    if (need_q) sQ[i * Dk + d] = __bfloat162float(a.q[t * a.ldqk + hk * Dk + d]);
+    uint4 kk = *reinterpret_cast<const uint4*>(a.k + t * a.ldqk + hk * Dk + d);
+    const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kk);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __bfloat1622float2(k2[e]);
+      sK[i * KD + d + 2 * e] = f.x, sK[i * KD + d + 2 * e + 1] = f.y;
+    }
+    if (need_q) {
+      uint4 qq = *reinterpret_cast<const uint4*>(a.q + t * a.ldqk + hk * Dk + d);
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qq);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(q2[e]);
+        sQ[i * KD + d + 2 * e] = f.x, sQ[i * KD + d + 2 * e + 1] = f.y;
+      }
+    }
   }
   if (need_v)
-    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
-      const int i = idx / Dv, d = idx % Dv;
-      sV[i * Dv + d] = __bfloat162float(a.v[tok(a, b, stream, c, i) * a.ldv + h * Dv + d]);
+    for (int idx = threadIdx.x; idx < C * (Dv / 8); idx += NT) {
+      const int i = idx / (Dv / 8), d = (idx % (Dv / 8)) * 8;
+      uint4 vv = *reinterpret_cast<const uint4*>(a.v + tok(a, b, stream, c, i) * a.ldv + h * Dv + d);
+      const __nv_bfloat162* v2 = reinterpret_cast<const __nv_bfloat162*>(&vv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(v2[e]);
+        sV[i * VD + d + 2 * e] = f.x, sV[i * VD + d + 2 * e + 1] = f.y;
+      }
     }
   if (threadIdx.x < 32) {
     const int i = threadIdx.x;
@@ -145,19 +286,17 @@ __device__ void load_chunk(const Args& a, int b, int stream, int c, int h, float
       gv = a.g[t * a.Hv + h];
       bv = a.beta[t * a.Hv + h];
     }
-    // inclusive prefix sum over the chunk (C <= 32)
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
+    for (int o = 1; o < 32; o <<= 1) {  // inclusive prefix sum over the chunk (C <= 32)
       float y = __shfl_up_sync(0xffffffffu, gv, o);
       if (i >= o) gv += y;
     }
     if (i < C) sgam[i] = gv, sbeta[i] = bv;
   }
   __syncthreads();
-  // l2 normalisation, one warp per row
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int r = warp; r < (need_q ? 2 * C : C); r += NT / 32) {
-    float* row = (r < C) ? sK + r * Dk : sQ + (r - C) * Dk;
+  for (int r = warp; r < (need_q ? 2 * C : C); r += NT / 32) {  // l2 normalisation, warp per row
+    float* row = (r < C) ? sK + r * KD : sQ + (r - C) * KD;
     float ss = 0.f;
     for (int d = lane; d < Dk; d += 32) ss += row[d] * row[d];
     ss = wsum(ss);
@@ -168,46 +307,47 @@ __device__ void load_chunk(const Args& a, int b, int stream, int c, int h, float
 }
 
 // sT = (I + A)^-1 with A = strict_lower(beta_i KK_ij Gam_ij); sKK = k^ k^T must be ready.
+// All [C][C] tiles use row stride LDC.
 __device__ void ut_transform(int C, const float* sKK, const float* sgam, const float* sbeta, float* sA, float* sT) {
   for (int idx = threadIdx.x; idx < C * C; idx += NT) {
     const int i = idx / C, j = idx % C;
-    sA[idx] = j < i ? sbeta[i] * sKK[idx] * __expf(sgam[i] - sgam[j]) : 0.f;
+    sA[i * LDC + j] = j < i ? sbeta[i] * sKK[i * LDC + j] * __expf(sgam[i] - sgam[j]) : 0.f;
   }
   __syncthreads();
   if (threadIdx.x < 32) {  // forward substitution, lane = column (C <= 32)
     const int col = threadIdx.x;
     for (int i = 0; i < C; ++i) {
       float v = (i == col) ? 1.f : 0.f;
-      for (int j = 0; j < i; ++j) v -= sA[i * C + j] * sT[j * C + col];
-      if (col < C) sT[i * C + col] = v;
+      for (int j = 0; j < i; ++j) v -= sA[i * LDC + j] * sT[j * LDC + col];
+      if (col < C) sT[i * LDC + col] = v;
       __syncwarp();
     }
   }
   __syncthreads();
 }
 
-// ------------------------------------------------------------------ smem layout helper
+// ------------------------------------------------------------------ forward smem layout
 template <int Dk, int Dv>
 struct Smem {
-  float *Q, *K, *V, *W, *X, *Y, *S, *KK, *A, *T, *P, *gam, *beta, *red;
-  __device__ Smem(float* base, int C) {
+  static constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v, MD = (KD > VD ? KD : VD);
+  float *Q, *K, *V, *W, *X, *Y, *S, *KK, *A, *T, *P, *gam, *beta;
+  __device__ Smem(float* base, int) {
     float* p = base;
-    Q = p; p += 32 * Dk;
-    K = p; p += 32 * Dk;
-    V = p; p += 32 * Dv;
-    W = p; p += 32 * Dk;
-    X = p; p += 32 * (Dk > Dv ? Dk : Dv);
-    Y = p; p += 32 * (Dk > Dv ? Dk : Dv);
-    S = p; p += Dk * Dv;
-    KK = p; p += 32 * 32;
-    A = p; p += 32 * 32;
-    T = p; p += 32 * 32;
-    P = p; p += 32 * 32;
+    Q = p; p += 32 * KD;
+    K = p; p += 32 * KD;
+    V = p; p += 32 * VD;
+    W = p; p += 32 * KD;
+    X = p; p += 32 * MD;
+    Y = p; p += 32 * MD;
+    S = p; p += Dk * VD;
+    KK = p; p += 32 * LDC;
+    A = p; p += 32 * LDC;
+    T = p; p += 32 * LDC;
+    P = p; p += 32 * LDC;
     gam = p; p += 32;
     beta = p; p += 32;
-    red = p; p += 4 * 32;
   }
-  static constexpr int floats = 6 * 32 * 128 + Dk * Dv + 4 * 1024 + 64 + 128;
+  static constexpr int floats = 3 * 32 * KD + 32 * VD + 2 * 32 * MD + Dk * VD + 4 * 32 * LDC + 64;
 };
 
 // ================================================================== forward
@@ -216,9 +356,10 @@ template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) fwd_prep_kernel(Args a) {
   extern __shared__ float sm[];
   Smem<Dk, Dv> s(sm, a.C);
+  constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
   const int c = blockIdx.x, bh = blockIdx.y, b = bh / a.Hv, h = bh % a.Hv, C = a.C;
   load_chunk<Dk, Dv>(a, b, 1, c, h, s.Q, s.K, s.V, s.gam, s.beta, false, true);
-  matmul<false, true>(C, C, Dk, s.K, Dk, s.K, Dk, [&](int i, int j, float x) { s.KK[i * C + j] = x; });
+  matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
   __syncthreads();
   ut_transform(C, s.KK, s.gam, s.beta, s.A, s.T);
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
@@ -226,61 +367,66 @@ __global__ void __launch_bounds__(NT) fwd_prep_kernel(Args a) {
   float* Wg = a.W + base * C * Dk;
   float* Kt = a.Kt + base * C * Dk;
   // U = T diag(beta) V ; W = T diag(beta E) k^
-  for (int idx = threadIdx.x; idx < C * Dv; idx += NT) s.X[idx] = s.beta[idx / Dv] * s.V[idx];
+  for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
+    const int i = idx / Dv, d = idx % Dv;
+    s.X[i * VD + d] = s.beta[i] * s.V[i * VD + d];
+  }
   for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-    const int i = idx / Dk;
-    s.Y[idx] = s.beta[i] * __expf(s.gam[i]) * s.K[idx];
-    Kt[idx] = __expf(s.gam[C - 1] - s.gam[i]) * s.K[idx];
+    const int i = idx / Dk, d = idx % Dk;
+    s.Y[i * KD + d] = s.beta[i] * __expf(s.gam[i]) * s.K[i * KD + d];
+    Kt[i * Dk + d] = __expf(s.gam[C - 1] - s.gam[i]) * s.K[i * KD + d];
   }
   __syncthreads();
-  matmul<false, false>(C, Dv, C, s.T, C, s.X, Dv, [&](int i, int d, float x) { U[i * Dv + d] = x; });
-  matmul<false, false>(C, Dk, C, s.T, C, s.Y, Dk, [&](int i, int d, float x) { Wg[i * Dk + d] = x; });
+  matmul<false, false>(C, Dv, C, s.T, LDC, s.X, VD, [&](int i, int d, float x) { U[i * Dv + d] = x; });
+  matmul<false, false>(C, Dk, C, s.T, LDC, s.Y, KD, [&](int i, int d, float x) { Wg[i * Dk + d] = x; });
   if (threadIdx.x == 0) a.Ec[base] = __expf(s.gam[C - 1]);
 }
 
-// sequential state recurrence: CTA per (b, h, 32 value columns); the state slice lives in
-// registers (Dk x 32 / NT per thread), the chunk operands stream through smem.
+// sequential state recurrence: CTA per (b, h, 32 value columns); the chunk operands stream
+// through smem.
 template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) fwd_recur_kernel(Args a) {
   extern __shared__ float sm[];
+  constexpr int KD = Ld<Dk>::v;
   const int C = a.C;
-  float* sW = sm;              // [C][Dk]
-  float* sKt = sW + 32 * Dk;   // [C][Dk]
-  float* sVp = sKt + 32 * Dk;  // [C][32]
-  float* sS = sVp + 32 * 32;   // [Dk][32]
+  float* sW = sm;               // [C][KD]
+  float* sKt = sW + 32 * KD;    // [C][KD]
+  float* sVp = sKt + 32 * KD;   // [C][LDC]
+  float* sS = sVp + 32 * LDC;   // [Dk][LDC]
   const int bh = blockIdx.x, b = bh / a.Hv, h = bh % a.Hv;
   const int col0 = blockIdx.y * 32;
   const int ncols = min(32, Dv - col0);
-  for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) sS[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) sS[idx] = 0.f;
   __syncthreads();
   for (int c = 0; c < a.nb; ++c) {
     const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
     float* Sin = a.S_in + base * Dk * Dv;
     for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
       const int r = idx / 32, cc = idx % 32;
-      if (cc < ncols) Sin[r * Dv + col0 + cc] = sS[idx];
+      if (cc < ncols) Sin[r * Dv + col0 + cc] = sS[r * LDC + cc];
     }
     const float* Wg = a.W + base * C * Dk;
     const float* Kt = a.Kt + base * C * Dk;
     const float* U = a.U + base * C * Dv;
-    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) sW[idx] = Wg[idx], sKt[idx] = Kt[idx];
+    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
+      const int i = idx / Dk, d = idx % Dk;
+      sW[i * KD + d] = Wg[idx], sKt[i * KD + d] = Kt[idx];
+    }
     __syncthreads();
-    // V' = U - W S   [C x ncols]
     float* Vp = a.Vp + base * C * Dv;
-    matmul<false, false>(C, 32, Dk, sW, Dk, sS, 32, [&](int i, int j, float x) {
+    matmul<false, false>(C, 32, Dk, sW, KD, sS, LDC, [&](int i, int j, float x) {  // V' = U - W S
       if (j < ncols) {
         const float v = U[i * Dv + col0 + j] - x;
-        sVp[i * 32 + j] = v;
+        sVp[i * LDC + j] = v;
         Vp[i * Dv + col0 + j] = v;
       } else {
-        sVp[i * 32 + j] = 0.f;
+        sVp[i * LDC + j] = 0.f;
       }
     });
     __syncthreads();
-    // S = Ec S + K~^T V'   [Dk x 32]
     const float ec = a.Ec[base];
-    matmul<true, false>(Dk, 32, C, sKt, Dk, sVp, 32, [&](int r, int j, float x) {
-      sS[r * 32 + j] = ec * sS[r * 32 + j] + x;
+    matmul<true, false>(Dk, 32, C, sKt, KD, sVp, LDC, [&](int r, int j, float x) {  // S = Ec S + K~^T V'
+      sS[r * LDC + j] = ec * sS[r * LDC + j] + x;
     });
     __syncthreads();
   }
@@ -291,6 +437,7 @@ template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
   extern __shared__ float sm[];
   Smem<Dk, Dv> s(sm, a.C);
+  constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
   const int C = a.C;
   const int stream = (a.concat || blockIdx.x >= a.nb) ? 1 : 0;
   const int c = blockIdx.x - ((stream && !a.concat) ? a.nb : 0);
@@ -298,44 +445,53 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
   load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.V, s.gam, s.beta, true, stream == 0);
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
   const float* Sin = a.S_in + base * Dk * Dv;
-  for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) s.S[idx] = Sin[idx];
-  // P = q^ k^T * Gam (incl)
-  matmul<false, true>(C, C, Dk, s.Q, Dk, s.K, Dk, [&](int i, int j, float x) {
-    s.P[i * C + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
-  });
-  if (stream == 0) {
-    matmul<false, true>(C, C, Dk, s.K, Dk, s.K, Dk, [&](int i, int j, float x) { s.KK[i * C + j] = x; });
+  for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
+    const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
+    *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(Sin + r * Dv + d);
   }
+  matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {  // P = q^ k^T * Gam (incl)
+    s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
+  });
+  if (stream == 0)
+    matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
   __syncthreads();
-  float* sVp = s.X;  // [C][Dv]
+  float* sVp = s.X;  // [C][VD]
   if (stream == 0) {
     ut_transform(C, s.KK, s.gam, s.beta, s.A, s.T);
-    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) s.V[idx] *= s.beta[idx / Dv];
+    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
+      const int i = idx / Dv, d = idx % Dv;
+      s.V[i * VD + d] *= s.beta[i];
+    }
     for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-      const int i = idx / Dk;
-      s.Y[idx] = s.beta[i] * __expf(s.gam[i]) * s.K[idx];
+      const int i = idx / Dk, d = idx % Dk;
+      s.Y[i * KD + d] = s.beta[i] * __expf(s.gam[i]) * s.K[i * KD + d];
     }
     __syncthreads();
-    matmul<false, false>(C, Dk, C, s.T, C, s.Y, Dk, [&](int i, int d, float x) { s.W[i * Dk + d] = x; });
-    matmul<false, false>(C, Dv, C, s.T, C, s.V, Dv, [&](int i, int d, float x) { sVp[i * Dv + d] = x; });
+    matmul<false, false>(C, Dk, C, s.T, LDC, s.Y, KD, [&](int i, int d, float x) { s.W[i * KD + d] = x; });
+    matmul<false, false>(C, Dv, C, s.T, LDC, s.V, VD, [&](int i, int d, float x) { sVp[i * VD + d] = x; });
     __syncthreads();
-    matmul<false, false>(C, Dv, Dk, s.W, Dk, s.S, Dv, [&](int i, int d, float x) { sVp[i * Dv + d] -= x; });
+    matmul<false, false>(C, Dv, Dk, s.W, KD, s.S, VD, [&](int i, int d, float x) { sVp[i * VD + d] -= x; });
   } else {
     const float* Vp = a.Vp + base * C * Dv;
-    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) sVp[idx] = Vp[idx];
+    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
+      const int i = idx / Dv, d = idx % Dv;
+      sVp[i * VD + d] = Vp[idx];
+    }
   }
   __syncthreads();
   // O = diag(E) q^ S + P V'
-  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) s.Q[idx] *= __expf(s.gam[idx / Dk]);
+  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
+    const int i = idx / Dk, d = idx % Dk;
+    s.Q[i * KD + d] *= __expf(s.gam[i]);
+  }
   __syncthreads();
   float* sO = s.Y;
-  matmul<false, false>(C, Dv, C, s.P, C, sVp, Dv, [&](int i, int d, float x) { sO[i * Dv + d] = x; });
+  matmul<false, false>(C, Dv, C, s.P, LDC, sVp, VD, [&](int i, int d, float x) { sO[i * VD + d] = x; });
   __syncthreads();
-  matmul<false, false>(C, Dv, Dk, s.Q, Dk, s.S, Dv, [&](int i, int d, float x) {
-    a.o[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(x + sO[i * Dv + d]);
+  matmul<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD, [&](int i, int d, float x) {
+    a.o[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(x + sO[i * VD + d]);
   });
 }
-
 
 // ================================================================== backward
 // With R = diag(beta) (V - diag(E) k^ S) the UT identities give V' = T R and dT = dV' R^T, so the
@@ -346,33 +502,39 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
 //   dE_i = sum_b (q^ S)_ib dO_ib - beta_i sum_b dR_ib (k^ S)_ib,  dF_i = sum_b (k^ dS_out)_ib V'_ib
 //   dA = strict_lower(-T^T dT T^T),  dKK = dA * beta_i * Gam
 //   dS_in = e^gam_C dS_out + (diag(E) q^)^T dO - k^T diag(beta E) dR
+// The T-path (dT, dA, dKK) runs right after dR, after which the dV' tile is dead and holds the
+// dq^ accumulator: 8 [C][D] tiles + S + 5 [C][C] tiles fit in 227 KB with padded strides.
 template <int Dk, int Dv>
 struct BSmem {
-  float *Q, *K, *R0, *dO, *Vp, *dVp, *dR, *dQ, *dK, *S, *KK, *T, *P, *X, *gam, *beta, *dgam, *dE, *dF, *red;
+  static constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
+  float *Q, *K, *R0, *dO, *Vp, *dVp, *dR, *dK, *S, *KK, *T, *P, *X, *Y, *gam, *beta, *dgam, *dE, *dF, *red;
+  float* dQ;  // aliases dVp once the T-path is done
   __device__ BSmem(float* base) {
     float* p = base;
-    Q = p; p += 32 * Dk;
-    K = p; p += 32 * Dk;
-    R0 = p; p += 32 * Dv;
-    dO = p; p += 32 * Dv;
-    Vp = p; p += 32 * Dv;
-    dVp = p; p += 32 * Dv;
-    dR = p; p += 32 * Dv;
-    dQ = p; p += 32 * Dk;
-    dK = p; p += 32 * Dk;
-    S = p; p += Dk * Dv;
-    KK = p; p += 32 * 32;
-    T = p; p += 32 * 32;
-    P = p; p += 32 * 32;
-    X = p; p += 32 * 32;
+    Q = p; p += 32 * KD;
+    K = p; p += 32 * KD;
+    R0 = p; p += 32 * VD;
+    dO = p; p += 32 * VD;
+    Vp = p; p += 32 * VD;
+    dVp = p; p += 32 * (VD > KD ? VD : KD);
+    dR = p; p += 32 * VD;
+    dK = p; p += 32 * KD;
+    S = p; p += Dk * VD;
+    KK = p; p += 32 * LDC;
+    T = p; p += 32 * LDC;
+    P = p; p += 32 * LDC;
+    X = p; p += 32 * LDC;
+    Y = p; p += 32 * LDC;
     gam = p; p += 32;
     beta = p; p += 32;
     dgam = p; p += 32;
     dE = p; p += 32;
     dF = p; p += 32;
     red = p; p += 32;
+    dQ = dVp;
   }
-  static constexpr int floats = 4 * 32 * Dk + 5 * 32 * Dv + Dk * Dv + 4 * 1024 + 6 * 32;
+  static constexpr int floats =
+      3 * 32 * KD + 4 * 32 * VD + 32 * (VD > KD ? VD : KD) + Dk * VD + 5 * 32 * LDC + 6 * 32;
 };
 
 // mode 0: noised block (dS_out = 0, dV' = P^T dO, writes dS_inj[c]); mode 1: clean chunk
@@ -381,6 +543,7 @@ template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   extern __shared__ float sm[];
   BSmem<Dk, Dv> s(sm);
+  constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
   const int C = a.C;
   const int stream = mode == 0 ? 0 : 1;
   const int c = blockIdx.x;
@@ -389,135 +552,160 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   // ---- loads: q^, k^, V (into R0), gam, beta, S, dO
   load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.R0, s.gam, s.beta, true, true);
   const float* Sin = a.S_in + base * Dk * Dv;
-  for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) s.S[idx] = Sin[idx];
+  for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
+    const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
+    *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(Sin + r * Dv + d);
+  }
   for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
     const int i = idx / Dv, d = idx % Dv;
-    s.dO[idx] = __bfloat162float(a.dout[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d]);
+    s.dO[i * VD + d] = __bfloat162float(a.dout[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d]);
   }
   if (threadIdx.x < 32) {
     s.dgam[threadIdx.x] = 0.f, s.dE[threadIdx.x] = 0.f, s.dF[threadIdx.x] = 0.f, s.red[threadIdx.x] = 0.f;
   }
-  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) s.dQ[idx] = 0.f, s.dK[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
+    const int i = idx / Dk, d = idx % Dk;
+    s.dK[i * KD + d] = 0.f;
+  }
   // ---- KK, P (with Gam, incl), T
-  matmul<false, true>(C, C, Dk, s.K, Dk, s.K, Dk, [&](int i, int j, float x) { s.KK[i * C + j] = x; });
-  matmul<false, true>(C, C, Dk, s.Q, Dk, s.K, Dk, [&](int i, int j, float x) {
-    s.P[i * C + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
+  matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
+  matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {
+    s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
   });
   __syncthreads();
   ut_transform(C, s.KK, s.gam, s.beta, s.X, s.T);  // X is scratch for A here
   // ---- R0 = V - diag(E) k^ S (in place over V)
-  matmul<false, false>(C, Dv, Dk, s.K, Dk, s.S, Dv, [&](int i, int d, float x) {
-    s.R0[i * Dv + d] -= __expf(s.gam[i]) * x;
+  matmul<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
+    s.R0[i * VD + d] -= __expf(s.gam[i]) * x;
   });
   __syncthreads();
   // ---- V' = (T diag(beta)) R0
-  for (int idx = threadIdx.x; idx < C * C; idx += NT) s.X[idx] = s.T[idx] * s.beta[idx % C];
+  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
+    const int i = idx / C, j = idx % C;
+    s.X[i * LDC + j] = s.T[i * LDC + j] * s.beta[j];
+  }
   __syncthreads();
-  matmul<false, false>(C, Dv, C, s.X, C, s.R0, Dv, [&](int i, int d, float x) { s.Vp[i * Dv + d] = x; });
+  matmul<false, false>(C, Dv, C, s.X, LDC, s.R0, VD, [&](int i, int d, float x) { s.Vp[i * VD + d] = x; });
   __syncthreads();
   // ---- dV'
   if (mode == 0) {
-    matmul<true, false>(C, Dv, C, s.P, C, s.dO, Dv, [&](int i, int d, float x) { s.dVp[i * Dv + d] = x; });
+    matmul<true, false>(C, Dv, C, s.P, LDC, s.dO, VD, [&](int i, int d, float x) { s.dVp[i * VD + d] = x; });
   } else {
     const float* gdv = a.dVp + base * C * Dv;
-    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) s.dVp[idx] = gdv[idx];
+    for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
+      const int i = idx / Dv, d = idx % Dv;
+      s.dVp[i * VD + d] = gdv[idx];
+    }
   }
   __syncthreads();
   // ---- dR = T^T dV' ; dV = diag(beta) dR -> global
-  matmul<true, false>(C, Dv, C, s.T, C, s.dVp, Dv, [&](int i, int d, float x) {
-    s.dR[i * Dv + d] = x;
+  matmul<true, false>(C, Dv, C, s.T, LDC, s.dVp, VD, [&](int i, int d, float x) {
+    s.dR[i * VD + d] = x;
     a.dv[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(s.beta[i] * x);
   });
+  // ---- T-path: dT = dV' R^T (R = diag(beta) R0) -> Y ; dA = strict_lower(-T^T dT T^T) -> Y
+  matmul<false, true>(C, C, Dv, s.dVp, VD, s.R0, VD, [&](int i, int j, float x) { s.Y[i * LDC + j] = x * s.beta[j]; });
+  __syncthreads();
+  matmul<false, true>(C, C, C, s.Y, LDC, s.T, LDC, [&](int i, int j, float x) { s.X[i * LDC + j] = x; });
+  __syncthreads();
+  matmul<true, false>(C, C, C, s.T, LDC, s.X, LDC, [&](int i, int j, float x) { s.Y[i * LDC + j] = j < i ? -x : 0.f; });
+  __syncthreads();
+  // dbeta += sum_j dA_ij KK_ij Gam_ij ; dKK = dA * beta_i * Gam (-> X) ; H2 = dA beta KK Gam (-> P2)
+  // with dgam += rowsum(H2) - colsum(H2): one thread per row, then one per column (no atomics)
+  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
+    const int i = idx / C, j = idx % C;
+    const float gm = j < i ? __expf(s.gam[i] - s.gam[j]) : 0.f;
+    const float dA = s.Y[i * LDC + j];
+    s.X[i * LDC + j] = dA * s.beta[i] * gm;
+    s.Y[i * LDC + j] = dA * s.KK[i * LDC + j] * gm;  // dA KK Gam (H2 / beta_i)
+  }
+  __syncthreads();
+  if (threadIdx.x < C) {
+    const int i = threadIdx.x;
+    float rs = 0.f, cs = 0.f;
+    for (int j = 0; j < C; ++j) rs += s.Y[i * LDC + j], cs += s.beta[j] * s.Y[j * LDC + i];
+    s.red[i] += rs;
+    s.dgam[i] += s.beta[i] * rs - cs;
+  }
+  __syncthreads();
+  // dK += dKK k^ + dKK^T k^ ; dV' is dead from here on: its tile becomes the dq^ accumulator
+  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  __syncthreads();
+  matmul<true, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
+    const int i = idx / Dk, d = idx % Dk;
+    s.dQ[i * KD + d] = 0.f;
+  }
   __syncthreads();
   // ---- products with S: dQ += diag(E) dO S^T ; dK -= diag(beta E) dR S^T ; dE terms ; dbeta part
-  matmul<false, true>(C, Dk, Dv, s.dO, Dv, s.S, Dv, [&](int i, int d, float x) {
-    s.dQ[i * Dk + d] += __expf(s.gam[i]) * x;
+  matmul<false, true>(C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) {
+    s.dQ[i * KD + d] += __expf(s.gam[i]) * x;
   });
-  matmul<false, true>(C, Dk, Dv, s.dR, Dv, s.S, Dv, [&](int i, int d, float x) {
-    s.dK[i * Dk + d] -= s.beta[i] * __expf(s.gam[i]) * x;
+  matmul<false, true>(C, Dk, Dv, s.dR, VD, s.S, VD, [&](int i, int d, float x) {
+    s.dK[i * KD + d] -= s.beta[i] * __expf(s.gam[i]) * x;
   });
-  matmul<false, false>(C, Dv, Dk, s.Q, Dk, s.S, Dv, [&](int i, int d, float x) {
-    atomicAdd(&s.dE[i], x * s.dO[i * Dv + d]);
-  });
-  matmul<false, false>(C, Dv, Dk, s.K, Dk, s.S, Dv, [&](int i, int d, float x) {
-    atomicAdd(&s.dE[i], -s.beta[i] * x * s.dR[i * Dv + d]);
-  });
-  for (int idx = threadIdx.x; idx < C * Dv; idx += NT) atomicAdd(&s.red[idx / Dv], s.dR[idx] * s.R0[idx]);
+  matmul_rowsum<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD,
+                               [&](int i, int d, float x) { return x * s.dO[i * VD + d]; }, s.dE);
+  matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
+                               [&](int i, int d, float x) { return -s.beta[i] * x * s.dR[i * VD + d]; }, s.dE);
   __syncthreads();
-  // ---- dP = dO V'^T ; dPm = dP * Gam (incl) -> X ; dgam += rowsum(dP*P) - colsum(dP*P)
-  matmul<false, true>(C, C, Dv, s.dO, Dv, s.Vp, Dv, [&](int i, int j, float x) {
+  rowdot(C, Dv, s.dR, VD, s.R0, VD, s.red);
+  __syncthreads();
+  // ---- dP = dO V'^T ; dPm = dP * Gam (incl) -> X ; G1 = dP * P -> Y ; dgam += rowsum(G1) - colsum(G1)
+  matmul<false, true>(C, C, Dv, s.dO, VD, s.Vp, VD, [&](int i, int j, float x) {
     const float gm = j <= i ? __expf(s.gam[i] - s.gam[j]) : 0.f;
-    s.X[i * C + j] = x * gm;
-    const float g1 = x * s.P[i * C + j];
-    atomicAdd(&s.dgam[i], g1);
-    atomicAdd(&s.dgam[j], -g1);
+    s.X[i * LDC + j] = x * gm;
+    s.Y[i * LDC + j] = x * s.P[i * LDC + j];
   });
   __syncthreads();
-  // dQ += dPm k^ ; dK += dPm^T q^
-  matmul<false, false>(C, Dk, C, s.X, C, s.K, Dk, [&](int i, int d, float x) { s.dQ[i * Dk + d] += x; });
-  matmul<true, false>(C, Dk, C, s.X, C, s.Q, Dk, [&](int i, int d, float x) { s.dK[i * Dk + d] += x; });
+  if (threadIdx.x < C) {
+    const int i = threadIdx.x;
+    float rs = 0.f, cs = 0.f;
+    for (int j = 0; j < C; ++j) rs += s.Y[i * LDC + j], cs += s.Y[j * LDC + i];
+    s.dgam[i] += rs - cs;
+  }
+  __syncthreads();
+  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dQ[i * KD + d] += x; });
+  matmul<true, false>(C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   __syncthreads();
   // ---- state gradient
   if (mode == 0) {
-    // dS_inj = (diag(E) q^)^T dO - k^T diag(beta E) dR ; dO and dR are consumed here (scaled in place)
+    // dS_inj = (diag(E) q^)^T dO - k^T diag(beta E) dR ; dO and dR are consumed (scaled in place)
     for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
-      const int i = idx / Dv;
+      const int i = idx / Dv, d = idx % Dv;
       const float e = __expf(s.gam[i]);
-      s.dO[idx] *= e;
-      s.dR[idx] *= s.beta[i] * e;
+      s.dO[i * VD + d] *= e;
+      s.dR[i * VD + d] *= s.beta[i] * e;
     }
     __syncthreads();
-    matmul<true, false>(Dk, Dv, C, s.Q, Dk, s.dO, Dv, [&](int r, int d, float x) { s.S[r * Dv + d] = x; });
+    matmul<true, false>(Dk, Dv, C, s.Q, KD, s.dO, VD, [&](int r, int d, float x) { s.S[r * VD + d] = x; });
     __syncthreads();
     float* dSi = a.dS_inj + base * Dk * Dv;
-    matmul<true, false>(Dk, Dv, C, s.K, Dk, s.dR, Dv, [&](int r, int d, float x) {
-      dSi[r * Dv + d] = s.S[r * Dv + d] - x;
+    matmul<true, false>(Dk, Dv, C, s.K, KD, s.dR, VD, [&](int r, int d, float x) {
+      dSi[r * Dv + d] = s.S[r * VD + d] - x;
     });
     __syncthreads();
   } else {
     // dEc = sum S * dS_out (S still in smem, dS_out from global) ; then S <- dS_out
     const float* dSo = a.dS_out + base * Dk * Dv;
     float part = 0.f;
-    for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) part += s.S[idx] * dSo[idx];
+    for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) part += s.S[(idx / Dv) * VD + idx % Dv] * dSo[idx];
     part = wsum(part);
     if ((threadIdx.x & 31) == 0) atomicAdd(&s.dgam[C - 1], part * __expf(s.gam[C - 1]));  // dEc * Ec
     __syncthreads();
-    for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) s.S[idx] = dSo[idx];
+    for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
+      const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
+      *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(dSo + r * Dv + d);
+    }
     __syncthreads();
     // dK += diag(F) V' dS_out^T ; dF_i = sum_b (k^ dS_out)_ib V'_ib
-    matmul<false, true>(C, Dk, Dv, s.Vp, Dv, s.S, Dv, [&](int i, int d, float x) {
-      s.dK[i * Dk + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
+    matmul<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
+      s.dK[i * KD + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
     });
-    matmul<false, false>(C, Dv, Dk, s.K, Dk, s.S, Dv, [&](int i, int d, float x) {
-      atomicAdd(&s.dF[i], x * s.Vp[i * Dv + d]);
-    });
+    matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
+                                 [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
     __syncthreads();
   }
-  // ---- dT = dV' R^T with R = diag(beta) R0 -> P (P no longer needed)
-  matmul<false, true>(C, C, Dv, s.dVp, Dv, s.R0, Dv, [&](int i, int j, float x) { s.P[i * C + j] = x * s.beta[j]; });
-  __syncthreads();
-  // dA = strict_lower(-T^T dT T^T): M = dT T^T -> X, then -T^T M -> P (masked)
-  matmul<false, true>(C, C, C, s.P, C, s.T, C, [&](int i, int j, float x) { s.X[i * C + j] = x; });
-  __syncthreads();
-  matmul<true, false>(C, C, C, s.T, C, s.X, C, [&](int i, int j, float x) { s.P[i * C + j] = j < i ? -x : 0.f; });
-  __syncthreads();
-  // dbeta += sum_j dA_ij KK_ij Gam_ij ; dKK = dA * beta_i * Gam (-> X) ; dgam from H2
-  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
-    const int i = idx / C, j = idx % C;
-    const float gm = j < i ? __expf(s.gam[i] - s.gam[j]) : 0.f;
-    const float dA = s.P[idx];
-    const float h2 = dA * s.beta[i] * s.KK[idx] * gm;
-    atomicAdd(&s.red[i], dA * s.KK[idx] * gm);
-    atomicAdd(&s.dgam[i], h2);
-    atomicAdd(&s.dgam[j], -h2);
-    s.X[idx] = dA * s.beta[i] * gm;
-  }
-  __syncthreads();
-  // dK += dKK k^ + dKK^T k^
-  matmul<false, false>(C, Dk, C, s.X, C, s.K, Dk, [&](int i, int d, float x) { s.dK[i * Dk + d] += x; });
-  __syncthreads();
-  matmul<true, false>(C, Dk, C, s.X, C, s.K, Dk, [&](int i, int d, float x) { s.dK[i * Dk + d] += x; });
-  __syncthreads();
   // ---- gates: dgam += dE E - dF F ; dgam[C-1] += sum dF F ; dg = reverse cumsum ; dbeta
   if (threadIdx.x < 32) {
     const int i = threadIdx.x;
@@ -549,7 +737,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     const int i = isq ? r - C : r;
     const int64_t t = tok(a, b, stream, c, i);
     const __nv_bfloat16* src = (isq ? a.q : a.k) + t * a.ldqk + hk * Dk;
-    const float* dy = (isq ? s.dQ : s.dK) + i * Dk;
+    const float* dy = (isq ? s.dQ : s.dK) + i * KD;
     const float sc = isq ? a.scale : 1.f;
     float ss = 0.f, xd = 0.f;
     for (int d = lane; d < Dk; d += 32) {
@@ -573,33 +761,34 @@ template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) bwd_prep_kernel(Args a) {
   extern __shared__ float sm[];
   Smem<Dk, Dv> s(sm, a.C);
+  constexpr int KD = Ld<Dk>::v, VD = Ld<Dv>::v;
   const int C = a.C;
   const int c = blockIdx.x, bh = blockIdx.y, b = bh / a.Hv, h = bh % a.Hv;
   load_chunk<Dk, Dv>(a, b, 1, c, h, s.Q, s.K, s.V, s.gam, s.beta, true, false);
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
   for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
     const int i = idx / Dv, d = idx % Dv;
-    s.X[idx] = __bfloat162float(a.dout[tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + d]);
+    s.X[i * VD + d] = __bfloat162float(a.dout[tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + d]);
   }
-  matmul<false, true>(C, C, Dk, s.K, Dk, s.K, Dk, [&](int i, int j, float x) { s.KK[i * C + j] = x; });
-  matmul<false, true>(C, C, Dk, s.Q, Dk, s.K, Dk, [&](int i, int j, float x) {
-    s.P[i * C + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
+  matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
+  matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {
+    s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
   });
   __syncthreads();
   ut_transform(C, s.KK, s.gam, s.beta, s.A, s.T);
   float* PtdO = a.PtdO + base * C * Dv;
-  matmul<true, false>(C, Dv, C, s.P, C, s.X, Dv, [&](int i, int d, float x) { PtdO[i * Dv + d] = x; });
+  matmul<true, false>(C, Dv, C, s.P, LDC, s.X, VD, [&](int i, int d, float x) { PtdO[i * Dv + d] = x; });
   float* Kt = a.Kt + base * C * Dk;
   float* Qt = a.Qt + base * C * Dk;
   for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-    const int i = idx / Dk;
-    Kt[idx] = __expf(s.gam[C - 1] - s.gam[i]) * s.K[idx];
-    Qt[idx] = __expf(s.gam[i]) * s.Q[idx];
-    s.Y[idx] = s.beta[i] * __expf(s.gam[i]) * s.K[idx];
+    const int i = idx / Dk, d = idx % Dk;
+    Kt[idx] = __expf(s.gam[C - 1] - s.gam[i]) * s.K[i * KD + d];
+    Qt[idx] = __expf(s.gam[i]) * s.Q[i * KD + d];
+    s.Y[i * KD + d] = s.beta[i] * __expf(s.gam[i]) * s.K[i * KD + d];
   }
   __syncthreads();
   float* Wg = a.W + base * C * Dk;
-  matmul<false, false>(C, Dk, C, s.T, C, s.Y, Dk, [&](int i, int d, float x) { Wg[i * Dk + d] = x; });
+  matmul<false, false>(C, Dk, C, s.T, LDC, s.Y, KD, [&](int i, int d, float x) { Wg[i * Dk + d] = x; });
   if (threadIdx.x == 0) a.Ec[base] = __expf(s.gam[C - 1]);
 }
 
@@ -608,58 +797,61 @@ __global__ void __launch_bounds__(NT) bwd_prep_kernel(Args a) {
 template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) bwd_recur_kernel(Args a, int has_inj) {
   extern __shared__ float sm[];
+  constexpr int KD = Ld<Dk>::v;
   const int C = a.C;
-  float* sW = sm;               // [C][Dk]
-  float* sKt = sW + 32 * Dk;    // [C][Dk]
-  float* sQt = sKt + 32 * Dk;   // [C][Dk]
-  float* sdVp = sQt + 32 * Dk;  // [C][32]
-  float* sdO = sdVp + 32 * 32;  // [C][32]
-  float* sS = sdO + 32 * 32;    // [Dk][32]
+  float* sW = sm;                // [C][KD]
+  float* sKt = sW + 32 * KD;     // [C][KD]
+  float* sQt = sKt + 32 * KD;    // [C][KD]
+  float* sdVp = sQt + 32 * KD;   // [C][LDC]
+  float* sdO = sdVp + 32 * LDC;  // [C][LDC]
+  float* sS = sdO + 32 * LDC;    // [Dk][LDC]
   const int bh = blockIdx.x, b = bh / a.Hv, h = bh % a.Hv;
   const int col0 = blockIdx.y * 32;
   const int ncols = min(32, Dv - col0);
-  for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) sS[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) sS[idx] = 0.f;
   __syncthreads();
   for (int c = a.nb - 1; c >= 0; --c) {
     const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
     float* dSo = a.dS_out + base * Dk * Dv;
     for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
       const int r = idx / 32, cc = idx % 32;
-      if (cc < ncols) dSo[r * Dv + col0 + cc] = sS[idx];
+      if (cc < ncols) dSo[r * Dv + col0 + cc] = sS[r * LDC + cc];
     }
     const float* Wg = a.W + base * C * Dk;
     const float* Kt = a.Kt + base * C * Dk;
     const float* Qt = a.Qt + base * C * Dk;
-    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) sW[idx] = Wg[idx], sKt[idx] = Kt[idx], sQt[idx] = Qt[idx];
+    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
+      const int i = idx / Dk, d = idx % Dk;
+      sW[i * KD + d] = Wg[idx], sKt[i * KD + d] = Kt[idx], sQt[i * KD + d] = Qt[idx];
+    }
     for (int idx = threadIdx.x; idx < C * 32; idx += NT) {
       const int i = idx / 32, cc = idx % 32;
-      sdO[idx] = cc < ncols ? __bfloat162float(a.dout[tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + col0 + cc])
-                            : 0.f;
+      sdO[i * LDC + cc] =
+          cc < ncols ? __bfloat162float(a.dout[tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + col0 + cc]) : 0.f;
     }
     __syncthreads();
     const float* PtdO = a.PtdO + base * C * Dv;
     float* dVp = a.dVp + base * C * Dv;
-    matmul<false, false>(C, 32, Dk, sKt, Dk, sS, 32, [&](int i, int j, float x) {
+    matmul<false, false>(C, 32, Dk, sKt, KD, sS, LDC, [&](int i, int j, float x) {
       if (j < ncols) {
         const float v = PtdO[i * Dv + col0 + j] + x;
-        sdVp[i * 32 + j] = v;
+        sdVp[i * LDC + j] = v;
         dVp[i * Dv + col0 + j] = v;
       } else {
-        sdVp[i * 32 + j] = 0.f;
+        sdVp[i * LDC + j] = 0.f;
       }
     });
     __syncthreads();
     const float ec = a.Ec[base];
     const float* inj = has_inj ? a.dS_inj + base * Dk * Dv : nullptr;
-    // dS = Ec dS + Qt^T dO - W^T dV' (+ inj): two products into registers via the epilogue
-    matmul<true, false>(Dk, 32, C, sQt, Dk, sdO, 32, [&](int r, int j, float x) {
-      sS[r * 32 + j] = ec * sS[r * 32 + j] + x;
+    matmul<true, false>(Dk, 32, C, sQt, KD, sdO, LDC, [&](int r, int j, float x) {
+      sS[r * LDC + j] = ec * sS[r * LDC + j] + x;
     });
     __syncthreads();
-    matmul<true, false>(Dk, 32, C, sW, Dk, sdVp, 32, [&](int r, int j, float x) {
-      float v = sS[r * 32 + j] - x;
+    matmul<true, false>(Dk, 32, C, sW, KD, sdVp, LDC, [&](int r, int j, float x) {
+      float v = sS[r * LDC + j] - x;
       if (inj != nullptr && j < ncols) v += inj[r * Dv + col0 + j];
-      sS[r * 32 + j] = v;
+      sS[r * LDC + j] = v;
     });
     __syncthreads();
   }
@@ -738,7 +930,7 @@ static std::vector<at::Tensor> forward_t(const at::Tensor& q, const at::Tensor& 
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   const int BH = a.B * a.Hv;
   launch(fwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
-  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 3 * 32 * Dk + 32 * 32 + Dk * 32, a);
+  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 2 * 32 * Ld<Dk>::v + 32 * LDC + Dk * LDC, a);
   // noised blocks (x < nb) only exist with the fork
   const int ngrid = concat ? a.nb : 2 * a.nb;
   launch(fwd_out_kernel<Dk, Dv>, dim3(ngrid, BH), Smem<Dk, Dv>::floats, a);
@@ -784,7 +976,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   const int BH = a.B * a.Hv;
   if (!concat) launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
   launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
-  launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 3 * 32 * Dk + 2 * 32 * 32 + Dk * 32, a,
+  launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 3 * 32 * Ld<Dk>::v + 2 * 32 * LDC + Dk * LDC, a,
           concat ? 0 : 1);
   launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
   return {dq, dk, dv, dg, db};
@@ -866,7 +1058,7 @@ int noalloc_run(bdllm::gdn::Args a, unsigned char* base, size_t cap, cudaStream_
   }
   const int BH = a.B * a.Hv;
   const int big = Smem<D, D>::floats * 4;
-  const int rec = (3 * 32 * D + 32 * 32 + D * 32) * 4;
+  const int rec = (2 * 32 * Ld<D>::v + 32 * LDC + D * LDC) * 4;
   if (cudaFuncSetAttribute(fwd_prep_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess ||
       cudaFuncSetAttribute(fwd_recur_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, rec) != cudaSuccess ||
       cudaFuncSetAttribute(fwd_out_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess)

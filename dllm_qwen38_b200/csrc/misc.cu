@@ -86,79 +86,92 @@ __device__ __forceinline__ int source_of(int t, int q_off, int L, int block, int
   return -1;
 }
 
+// grid: x over 8-channel vectors, y over groups of CONV_ROWS rows (b * T2 + t). A thread keeps
+// its 8 channels' taps (32 floats) in registers and walks its rows.
+constexpr int CONV_ROWS = 16;
+
+template <int K>
+__device__ __forceinline__ void load_taps(const float* __restrict__ w, int c, float (&wr)[8][K]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float4 t = *reinterpret_cast<const float4*>(w + (c + e) * K);
+    wr[e][0] = t.x, wr[e][1] = t.y, wr[e][2] = t.z, wr[e][3] = t.w;
+  }
+}
+
+template <int K>
+__device__ __forceinline__ void conv_row(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float (&wr)[8][K],
+                                         int b, int t, int c, int T2, int L, int block, int mode, float (&acc)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int src = source_of(t, j - (K - 1), L, block, mode);
+    if (src < 0) continue;
+    const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(p2[e]);
+      acc[2 * e] += wr[2 * e][j] * f.x;
+      acc[2 * e + 1] += wr[2 * e + 1][j] * f.y;
+    }
+  }
+}
+
 template <int K>
 __global__ void conv_fwd_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ w,
                                 __nv_bfloat16* __restrict__ y, int B, int T2, int C, int L, int block, int mode) {
-  const int cv = C / 8;
-  const int64_t n = (int64_t)B * T2 * cv;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % cv) * 8;
-    const int64_t bt = i / cv;
-    const int t = (int)(bt % T2);
-    const int b = (int)(bt / T2);
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= C) return;
+  float wr[8][K];
+  load_taps<K>(w, c, wr);
+  const int r1 = min(B * T2, (int)(blockIdx.y + 1) * CONV_ROWS);
+  for (int row = blockIdx.y * CONV_ROWS; row < r1; ++row) {
+    const int t = row % T2, b = row / T2;
     float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      int src = source_of(t, j - (K - 1), L, block, mode);
-      if (src < 0) continue;
-      uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __bfloat1622float2(p2[e]);
-        acc[2 * e] += w[(c + 2 * e) * K + j] * f.x;
-        acc[2 * e + 1] += w[(c + 2 * e + 1) * K + j] * f.y;
-      }
-    }
+    conv_row<K>(raw, ld, wr, b, t, c, T2, L, block, mode, acc);
     uint4 o;
     __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(silu_f(acc[2 * e]), silu_f(acc[2 * e + 1]));
-    *reinterpret_cast<uint4*>(y + ((int64_t)b * T2 + t) * C + c) = o;
+    *reinterpret_cast<uint4*>(y + (int64_t)row * C + c) = o;
   }
 }
 
-// dpre = dy * silu'(pre), pre recomputed; one thread per (b, t, 8 channels). Stored fp32 so the
-// gather below accumulates without a second rounding.
+// dpre = dy * silu'(pre), pre recomputed; stored fp32 so the gather below accumulates without a
+// second rounding.
 template <int K>
 __global__ void conv_dpre_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ w,
                                  const __nv_bfloat16* __restrict__ dy, float* __restrict__ dpre, int B, int T2,
                                  int C, int L, int block, int mode) {
-  const int cv = C / 8;
-  const int64_t n = (int64_t)B * T2 * cv;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % cv) * 8;
-    const int64_t bt = i / cv;
-    const int t = (int)(bt % T2);
-    const int b = (int)(bt / T2);
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c >= C) return;
+  float wr[8][K];
+  load_taps<K>(w, c, wr);
+  const int r1 = min(B * T2, (int)(blockIdx.y + 1) * CONV_ROWS);
+  for (int row = blockIdx.y * CONV_ROWS; row < r1; ++row) {
+    const int t = row % T2, b = row / T2;
     float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
-#pragma unroll
-    for (int j = 0; j < K; ++j) {
-      int src = source_of(t, j - (K - 1), L, block, mode);
-      if (src < 0) continue;
-      uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float2 f = __bfloat1622float2(p2[e]);
-        acc[2 * e] += w[(c + 2 * e) * K + j] * f.x;
-        acc[2 * e + 1] += w[(c + 2 * e + 1) * K + j] * f.y;
-      }
-    }
-    uint4 g = *reinterpret_cast<const uint4*>(dy + ((int64_t)b * T2 + t) * C + c);
+    conv_row<K>(raw, ld, wr, b, t, c, T2, L, block, mode, acc);
+    const uint4 g = *reinterpret_cast<const uint4*>(dy + (int64_t)row * C + c);
     const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&g);
-    float* out = dpre + ((int64_t)b * T2 + t) * C + c;
+    float4 o0, o1;
+    float* op[2] = {&o0.x, &o1.x};
+    (void)op;
+    float out[8];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float2 gf = __bfloat1622float2(g2[e]);
-      float s0 = sigmoid_f(acc[2 * e]), s1 = sigmoid_f(acc[2 * e + 1]);
+      const float2 gf = __bfloat1622float2(g2[e]);
+      const float s0 = sigmoid_f(acc[2 * e]), s1 = sigmoid_f(acc[2 * e + 1]);
       out[2 * e] = gf.x * s0 * (1.f + acc[2 * e] * (1.f - s0));
       out[2 * e + 1] = gf.y * s1 * (1.f + acc[2 * e + 1] * (1.f - s1));
     }
+    o0 = make_float4(out[0], out[1], out[2], out[3]);
+    o1 = make_float4(out[4], out[5], out[6], out[7]);
+    float* dst = dpre + (int64_t)row * C + c;
+    *reinterpret_cast<float4*>(dst) = o0;
+    *reinterpret_cast<float4*>(dst + 4) = o1;
   }
 }
 
@@ -169,12 +182,10 @@ template <int K>
 __global__ void conv_dx_kernel(const float* __restrict__ dpre, const float* __restrict__ w,
                                __nv_bfloat16* __restrict__ draw, int64_t ldd, int B, int T2, int C, int L, int block,
                                int mode) {
-  const int64_t n = (int64_t)B * T2 * C;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const int64_t bq = i / C;
-    const int q = (int)(bq % T2);
-    const int b = (int)(bq / T2);
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  for (int row = blockIdx.y; row < B * T2; row += gridDim.y) {
+    const int q = row % T2, b = row / T2;
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < K; ++j) {
@@ -238,6 +249,7 @@ __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int
 }
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
+static dim3 row_grid(int per_row, int rows) { return dim3((per_row + 255) / 256, std::min(rows, 65535)); }
 
 at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode) {
   TORCH_CHECK(raw.dim() == 3 && raw.stride(-1) == 1 && raw.scalar_type() == at::kBFloat16, "conv: raw [B, 2L, C] bf16");
@@ -248,9 +260,8 @@ at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64
   auto wf = w.to(at::kFloat).contiguous();
   auto y = at::empty({B, T2, C}, raw.options());
   c10::cuda::CUDAGuard g(raw.device());
-  const int64_t n = (int64_t)B * T2 * (C / 8);
-  conv_fwd_kernel<4><<<grid_for(n), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(), bfp(y), B, T2,
-                                                        C, (int)L, (int)block, (int)mode);
+  conv_fwd_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(),
+                                                                   bfp(y), B, T2, C, (int)L, (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return y;
 }
@@ -263,15 +274,13 @@ std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, co
   auto d = dy.to(at::kBFloat16).contiguous();
   c10::cuda::CUDAGuard g(raw.device());
   auto dpre = at::empty({B, T2, C}, raw.options().dtype(at::kFloat));
-  const int64_t nv = (int64_t)B * T2 * (C / 8);
-  conv_dpre_kernel<4><<<grid_for(nv), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(), cbf(d),
-                                                          dpre.data_ptr<float>(), B, T2, C, (int)L, (int)block,
-                                                          (int)mode);
+  conv_dpre_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(),
+                                                                    cbf(d), dpre.data_ptr<float>(), B, T2, C, (int)L,
+                                                                    (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto draw = at::empty({B, T2, C}, raw.options());
-  const int64_t n = (int64_t)B * T2 * C;
-  conv_dx_kernel<4><<<grid_for(n), 256, 0, stream()>>>(dpre.data_ptr<float>(), wf.data_ptr<float>(), bfp(draw), C, B,
-                                                       T2, C, (int)L, (int)block, (int)mode);
+  conv_dx_kernel<4><<<row_grid(C, B * T2), 256, 0, stream()>>>(dpre.data_ptr<float>(), wf.data_ptr<float>(),
+                                                                bfp(draw), C, B, T2, C, (int)L, (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int64_t total = (int64_t)B * T2;
   const int tpb = (int)std::max<int64_t>(64, (total + 127) / 128);

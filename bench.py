@@ -168,6 +168,12 @@ def run_native(a, rank, world):
     _barrier()
     e2e_s = _max_over_ranks((time.perf_counter() - t0) / a.steps)
     del loss_host
+    if dist.is_initialized():  # each rank's loss is its share of the global mean CE
+        t = torch.tensor([loss_last], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t)
+        loss_last = float(t.item())
+    if hasattr(trainer, "engine"):
+        trainer.engine.close()
     h2d = host_x[0].numel() * host_x[0].element_size() + pl.numel() * 8 + vl.numel() * 8
     return {
         "ms_per_step": ms, "e2e_s_per_step": e2e_s, "launches": launches, "clocks": clocks, "cfg": cfg,

@@ -33,6 +33,22 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                  const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, int64_t L,
                                  int64_t block, double scale, bool leak);
+namespace peer {
+int64_t alloc(int64_t bytes);
+at::Tensor handle(int64_t ptr);
+int64_t open(const at::Tensor& h);
+void close(int64_t ptr);
+void release(int64_t ptr);
+at::Tensor view(int64_t ptr, int64_t numel, const at::Tensor& like);
+void signal(const std::vector<int64_t>& peers, int64_t rank, int64_t slot, int64_t value);
+void all_gather(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes, at::Tensor& out,
+                int64_t epoch, int64_t max_blocks, double timeout_s);
+void reduce_scatter(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard, bool in_f32,
+                    at::Tensor& out, double scale, const c10::optional<at::Tensor>& sq, int64_t seq,
+                    int64_t max_blocks, double timeout_s);
+void allreduce_f32(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& vals, at::Tensor& out,
+                   int64_t seq, double timeout_s);
+}  // namespace peer
 }  // namespace bdllm
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -56,6 +72,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_rmsnorm_bwd", &bdllm::gated_rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &bdllm::qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &bdllm::qk_norm_rope_bwd);
+  m.def("peer_alloc", &bdllm::peer::alloc, "symmetric heap: zeroed device region");
+  m.def("peer_handle", &bdllm::peer::handle, "CUDA IPC handle of a heap (64-byte CPU tensor)");
+  m.def("peer_open", &bdllm::peer::open, "map a peer's heap from its IPC handle");
+  m.def("peer_close", &bdllm::peer::close);
+  m.def("peer_release", &bdllm::peer::release);
+  m.def("peer_view", &bdllm::peer::view, "non-owning tensor over heap memory");
+  m.def("peer_signal", &bdllm::peer::signal);
+  m.def("peer_all_gather", &bdllm::peer::all_gather, "all-gather of heap shards by peer loads");
+  m.def("peer_reduce_scatter", &bdllm::peer::reduce_scatter,
+        "reduce-scatter by peer loads, fused fp32 cast, scale and sum of squares", py::arg("peers"),
+        py::arg("rank"), py::arg("src_off"), py::arg("shard"), py::arg("in_f32"), py::arg("out"), py::arg("scale"),
+        py::arg("sq"), py::arg("seq"), py::arg("max_blocks"), py::arg("timeout_s"));
+  m.def("peer_allreduce_f32", &bdllm::peer::allreduce_f32);
   m.def("read_error_word", &bdllm::read_error_word, "device error word (bounded-wait expiries)",
         py::arg("reset") = false);
 }

@@ -11,7 +11,7 @@
 // lane), warps 2..5 drain TMEM (warp w owns TMEM lanes 32*(w%4)..+31). Tiles 128 x BN x 64,
 // STAGES-deep smem ring, two TMEM accumulators so the epilogue of tile i overlaps the MMAs of
 // tile i+1. One CTA per SM, grid = min(#tiles, #SMs), grouped tile raster for L2 reuse.
-// TMA loads never use cluster multicast.
+// Every TMA load copies into the issuing CTA only.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>

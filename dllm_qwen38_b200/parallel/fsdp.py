@@ -18,6 +18,16 @@ After backward, one fused AdamW launch per unit updates the fp32 master shard an
 bf16 shard; the clip coefficient is computed on the device from one all-reduced scalar, so the
 step has no host synchronisation.
 
+Communication. On CUDA with more than one rank the engine keeps every parameter shard and both
+flat gradient buffers in a symmetric peer heap (`parallel/peer.py`): a gather is one launch that
+reads the peers' shards over NVLink into the gathered buffer, and a gradient reduce-scatter is one
+launch that reads the peers' gradient slices, sums them in fp32, scales by 1/world, writes the
+fp32 gradient shard and accumulates its sum of squares for the clip; it runs on the communication
+stream, overlapped with the next layer's backward (the two gradient buffers alternate). The
+global norm is one peer all-reduce launch; after the AdamW launches each rank publishes a
+parameter epoch that the next step's gathers wait for. Set BDLLM_COMM=nccl (or run on CPU/gloo)
+for the same steps over torch.distributed collectives.
+
 This replaces the reference's FSDP2 wrapping of a `LayerStep` (`fsdp_train.py:86-171`): the
 state fork calls submodules directly, which FSDP hooks cannot see (`fsdp_train.py:3-10`); here
 parameters are gathered explicitly per unit, so there is no hook to bypass. Reduction semantics
@@ -27,6 +37,8 @@ are averaged over ranks (`fsdp_train.py:39-44,162,207-221`), so AdamW sees
 """
 
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -50,7 +62,8 @@ def _world():
 class Unit:
     """A flat, sharded group of parameters of one module."""
 
-    def __init__(self, name: str, module: torch.nn.Module, world: int, rank: int, device, dtype=torch.bfloat16):
+    def __init__(self, name: str, module: torch.nn.Module, world: int, rank: int, device, dtype=torch.bfloat16,
+                 alloc=None):
         self.name, self.world, self.rank, self.device = name, world, rank, device
         self.entries = []  # (param name, shape, offset, numel), module order
         off, seen = 0, set()
@@ -62,8 +75,13 @@ class Unit:
             off += p.numel()
         self.numel = off
         self.shard = (off + world - 1) // world
+        if world > 1:  # 16-byte aligned slices of bf16 and fp32 buffers for the peer kernels
+            self.shard = (self.shard + 63) // 64 * 64
         self.padded = self.shard * world
-        self.p = torch.zeros(self.shard, dtype=dtype, device=device)
+        if alloc is not None:  # in the symmetric heap: peers read it directly
+            self.p, self.p_off = alloc(self.shard, dtype)
+        else:
+            self.p, self.p_off = torch.zeros(self.shard, dtype=dtype, device=device), None
         self.master = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.m = torch.zeros(self.shard, dtype=torch.float32, device=device)
         self.v = torch.zeros(self.shard, dtype=torch.float32, device=device)
@@ -142,13 +160,19 @@ class FSDPEngine:
         self.step_count = 0
         tm = model.text_model
         self.tied = self.cfg.tie_word_embeddings
-        mk = lambda name, mod: Unit(name, mod, self.world, self.rank, self.device, self.dtype)  # noqa: E731
-        self.embed = mk("embed", tm.embed_tokens)
-        self.layers = [mk(f"layers.{i}", tm.layers[i]) for i in range(self.cfg.num_hidden_layers)]
         head_mod = torch.nn.ModuleDict({"norm": tm.norm} if self.tied else {"norm": tm.norm, "lm_head": model.lm_head})
-        self.head = mk("head", head_mod)
-        self.units = [self.embed] + self.layers + [self.head]
-        for u, mod in zip(self.units, [tm.embed_tokens] + list(tm.layers) + [head_mod]):
+        mods = [("embed", tm.embed_tokens)] + [(f"layers.{i}", tm.layers[i]) for i in range(self.cfg.num_hidden_layers)]
+        mods.append(("head", head_mod))
+        self.peer = None
+        if self.world > 1 and self.device.type == "cuda" and os.environ.get("BDLLM_COMM", "peer") == "peer":
+            from .peer import SymmetricHeap
+
+            self.peer = SymmetricHeap(self._heap_bytes([m for _, m in mods]), self.device)
+        alloc = self.peer.alloc if self.peer is not None else None
+        mk = lambda name, mod: Unit(name, mod, self.world, self.rank, self.device, self.dtype, alloc)  # noqa: E731
+        self.units = [mk(name, mod) for name, mod in mods]
+        self.embed, self.layers, self.head = self.units[0], self.units[1:-1], self.units[-1]
+        for u, (_, mod) in zip(self.units, mods):
             u.load_full(u.flat_of(mod))
         self.model = model.to("meta")
         if self.tied:
@@ -158,11 +182,41 @@ class FSDPEngine:
         self.owner = [None, None]
         self.ready = [None, None]
         self.lru = 0
-        self.grad = torch.empty(max(u.padded for u in self.layers + [self.head]), dtype=self.dtype,
-                                device=self.device)
-        self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
+        gmax = max(u.padded for u in self.layers + [self.head])
+        if self.peer is not None:  # two alternating gradient buffers: one is reduce-scattered while
+            # the next layer's backward fills the other
+            self.grads, self.grad_offs = zip(*[self.peer.alloc(gmax, self.dtype) for _ in range(2)])
+            self.table_grad, self.table_off = self.peer.alloc(self.embed.padded, torch.float32)
+            self.sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+            self.sq_all = torch.zeros(1, dtype=torch.float32, device=self.device)
+        else:
+            self.grads = (torch.empty(gmax, dtype=self.dtype, device=self.device),)
+            self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
+        self.grad_i = 0
+        self.rs_done = [None] * len(self.grads)
+        self.epoch = 0
         self.comm = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.anchor = torch.zeros((), device=self.device, requires_grad=True)
+        if self.peer is not None:  # every shard written before any peer reads one
+            torch.cuda.synchronize(self.device)
+            dist.barrier()
+
+    def _heap_bytes(self, modules) -> int:
+        """Bytes of the symmetric heap: every unit's bf16 shard, two bf16 gradient buffers of the
+        largest layer/head unit and the fp32 embedding-table gradient (256-byte aligned each)."""
+        w = self.world
+        esz = torch.empty(0, dtype=self.dtype).element_size()
+
+        def shard(mod):
+            n = sum(p.numel() for p in {id(p): p for p in mod.parameters()}.values())
+            return ((n + w - 1) // w + 63) // 64 * 64
+
+        a = lambda b: (b + 255) // 256 * 256  # noqa: E731
+        shards = [shard(m) for m in modules]
+        total = sum(a(s * esz) for s in shards)
+        total += 2 * a(max(shards[1:]) * w * esz)
+        total += a(shards[0] * w * 4)
+        return total + 4096
 
     # ------------------------------------------------------------------ gathers
     def gather(self, unit: Unit, prefetch: bool = False) -> torch.Tensor:
@@ -182,17 +236,48 @@ class FSDPEngine:
         if prefetch and self.comm is not None:
             self.comm.wait_stream(torch.cuda.current_stream(self.device))
             with torch.cuda.stream(self.comm):
-                unit.gather_into(buf)
+                self.gather_into(unit, buf)
                 ev = torch.cuda.Event()
                 ev.record(self.comm)
             self.ready[i] = ev
         else:
-            unit.gather_into(buf)
+            self.gather_into(unit, buf)
             self.ready[i] = None
         return buf
 
+    def gather_into(self, unit: Unit, out: torch.Tensor) -> None:
+        if self.peer is not None:
+            self.peer.all_gather(unit.p_off, unit.shard * unit.p.element_size(), out, self.epoch)
+        else:
+            unit.gather_into(out)
+
+    def grad_buffer(self, unit: Unit) -> torch.Tensor:
+        """A zeroed flat gradient buffer for `unit` (waits until its previous reduce-scatter ended)."""
+        j = self.grad_i
+        self.grad_i = (j + 1) % len(self.grads)
+        if self.rs_done[j] is not None:
+            torch.cuda.current_stream(self.device).wait_event(self.rs_done[j])
+            self.rs_done[j] = None
+        g = self.grads[j][: unit.padded]
+        g.zero_()
+        return g
+
     def reduce_scatter(self, unit: Unit, flat_grad: torch.Tensor) -> None:
-        unit.reduce_scatter_from(flat_grad)
+        if self.peer is None:
+            unit.reduce_scatter_from(flat_grad)
+            return
+        if flat_grad.data_ptr() == self.table_grad.data_ptr():
+            j, off, f32 = None, self.table_off, True
+        else:
+            j = next(k for k, g in enumerate(self.grads) if g.data_ptr() == flat_grad.data_ptr())
+            off, f32 = self.grad_offs[j], False
+        self.comm.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.comm):
+            self.peer.reduce_scatter(off, unit.shard, f32, unit.g, 1.0 / self.world, self.sq)
+            if j is not None:
+                ev = torch.cuda.Event()
+                ev.record(self.comm)
+                self.rs_done[j] = ev
 
     # ------------------------------------------------------------------ layer parameter binding
     def leaves(self, unit: Unit, buf: torch.Tensor, grad: torch.Tensor | None):
@@ -244,6 +329,8 @@ class FSDPEngine:
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
+        if self.peer is not None:
+            self.sq.zero_()
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
         loss.backward()
         self._optimizer_step()
@@ -251,12 +338,17 @@ class FSDPEngine:
 
     @torch.no_grad()
     def _optimizer_step(self):
-        sq = torch.zeros((), device=self.device, dtype=torch.float32)
-        for u in self.units:
-            sq += u.g.pow(2).sum()
-        if self.world > 1:
-            dist.all_reduce(sq)
-        norm = sq.sqrt()
+        if self.peer is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.comm)
+            self.peer.allreduce_f32(self.sq, self.sq_all)
+            norm = self.sq_all[0].sqrt()
+        else:
+            sq = torch.zeros((), device=self.device, dtype=torch.float32)
+            for u in self.units:
+                sq += u.g.pow(2).sum()
+            if self.world > 1:
+                dist.all_reduce(sq)
+            norm = sq.sqrt()
         coef = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0)
         b1, b2 = self.betas
         bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
@@ -266,9 +358,21 @@ class FSDPEngine:
         self.invalidate()
 
     def invalidate(self) -> None:
-        """Forget gathered copies (their shards changed)."""
+        """Forget gathered copies (their shards changed) and, with the peer heap, publish the new
+        parameter epoch that peers' next gathers wait for."""
         self.owner = [None, None]
         self.ready = [None, None]
+        self.epoch += 1
+        if self.peer is not None:
+            self.peer.publish_epoch(self.epoch)
+
+    def close(self) -> None:
+        """Release the peer heap (collective; the engine is unusable afterwards)."""
+        if self.peer is not None:
+            torch.cuda.synchronize(self.device)
+            dist.barrier()
+            self.peer.close()
+            self.peer = None
 
     # ------------------------------------------------------------------ inspection
     @torch.no_grad()
@@ -278,7 +382,7 @@ class FSDPEngine:
         prefixes = {"embed": "text_model.embed_tokens.", "head": ""}
         for u in self.units:
             buf = torch.empty(u.padded, dtype=self.dtype, device=self.device)
-            u.gather_into(buf)
+            self.gather_into(u, buf)
             for n, s, o, k in u.entries:
                 if u.name == "head":
                     key = ("text_model." + n) if n.startswith("norm.") else n
@@ -356,8 +460,7 @@ class _LayerFn(torch.autograd.Function):
         buf = engine.gather(unit)
         if i > 0:
             engine.gather(engine.layers[i - 1], prefetch=True)
-        grad = engine.grad[: unit.padded]
-        grad.zero_()
+        grad = engine.grad_buffer(unit)
         params, fused = engine.leaves(unit, buf, grad)
         layer = engine.model.text_model.layers[i]
         hx = h.detach().requires_grad_(True)
@@ -406,8 +509,7 @@ class _HeadFn(torch.autograd.Function):
         engine, n_global, n_local = ctx.meta
         ht, m, x0 = ctx.saved_tensors
         u = engine.head
-        grad = engine.grad[: u.padded]
-        grad.zero_()
+        grad = engine.grad_buffer(u)
         buf = engine.gather(u)
         params, _ = engine.leaves(u, buf, grad)
         if engine.tied:

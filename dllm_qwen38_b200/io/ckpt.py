@@ -229,6 +229,63 @@ def reference_dcp_tensors(path: str) -> tuple[dict, int, int]:
     return model, int(step), int(seq)
 
 
+def engine_unit_layout(cfg) -> dict:
+    """{unit name: [(our key, shape, offset, numel)]} of the sharded engine's flat units, in the
+    engine's order (module registration order, shared parameters once)."""
+    from ..models.qwen35 import BlockDiffusionLM
+
+    with torch.device("meta"):
+        m = BlockDiffusionLM(cfg)
+    tm = m.text_model
+    units = [("embed", "text_model.embed_tokens.", tm.embed_tokens)]
+    units += [(f"layers.{i}", f"text_model.layers.{i}.", layer) for i, layer in enumerate(tm.layers)]
+    head = {"norm": tm.norm} if cfg.tie_word_embeddings else {"norm": tm.norm, "lm_head": m.lm_head}
+    units.append(("head", "", torch.nn.ModuleDict(head)))
+    out = {}
+    for name, prefix, mod in units:
+        off, ent, seen = 0, [], set()
+        for n, p in mod.named_parameters():
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            key = prefix + n
+            if name == "head" and n.startswith("norm."):
+                key = "text_model." + n
+            ent.append((key, tuple(p.shape), off, p.numel()))
+            off += p.numel()
+        out[name] = ent
+    return out
+
+
+def any_dcp_tensors(path: str, cfg) -> tuple[dict, int, int]:
+    """Full parameters {our or reference key: tensor} from either checkpoint kind: this
+    repository's engine (flat per-unit shards under 'model.<unit>') or the reference's FSDP
+    layout (per-parameter entries under 'model.text_model...' / 'model.lm_head...')."""
+    from torch.distributed.checkpoint import FileSystemReader, load as dcp_load
+
+    md = FileSystemReader(path).read_metadata()
+    keys = [k for k in md.state_dict_metadata if k.startswith("model.")]
+    if any(k.startswith("model.text_model.") or k.startswith("model.lm_head.") for k in keys):
+        return reference_dcp_tensors(path)
+    flat = {}
+    for k in keys:
+        meta = md.state_dict_metadata[k]
+        flat[k[len("model."):]] = torch.empty(tuple(meta.size), dtype=meta.properties.dtype)
+    step, seq = torch.zeros((), dtype=torch.int64), torch.zeros((), dtype=torch.int64)
+    dcp_load({"model": flat, "step": step, "seq_tokens": seq}, storage_reader=FileSystemReader(path), no_dist=True)
+    out = {}
+    for unit, entries in engine_unit_layout(cfg).items():
+        if unit not in flat:
+            raise ValueError(f"{path}: unit {unit} missing (checkpoint of another model shape?)")
+        buf = flat[unit]
+        need = sum(e[3] for e in entries)
+        if buf.numel() < need:
+            raise ValueError(f"{path}: unit {unit} holds {buf.numel()} elements, the model needs {need}")
+        for key, shape, off, n in entries:
+            out[key] = buf[off : off + n].view(shape).clone()
+    return out, int(step), int(seq)
+
+
 def restore_into(model, tensors: dict, ctx: str = "ckpt") -> None:
     """Load {reference or our FQN: tensor} into a `BlockDiffusionLM`; any missing, unexpected or
     foreign key raises (a partial restore would score silently wrong, `gsm8k_eval.py:306-328`)."""

@@ -40,3 +40,21 @@ def test_gdn_core_fwd_bwd(mode, B, L, block, Hk, Hv, D):
     assert _rel(g.grad, gf.grad) < 2e-2, _rel(g.grad, gf.grad)
     assert _rel(beta.grad, bf.grad) < 2e-2, _rel(beta.grad, bf.grad)
     Cu.check_errors()
+
+
+def test_kernel_diff_probe_on_a_real_mixer():
+    from dllm_qwen38_b200.config import preset
+    from dllm_qwen38_b200.models.qwen35 import build_model
+    from dllm_qwen38_b200.ops import kernel_diff
+    from dllm_qwen38_b200.ops import reference as ref
+
+    cfg = preset("tiny", hidden_size=256, linear_key_head_dim=64, linear_value_head_dim=64, linear_num_key_heads=2,
+                 linear_num_value_heads=4, layers=1)
+    model = build_model(cfg, seed=0, device="cuda", dtype=torch.bfloat16)
+    ids = torch.randint(0, cfg.mask_id, (1, 512), device="cuda", generator=torch.Generator(device="cuda").manual_seed(0))
+    layer = model.text_model.layers[0]
+    n = ref.rmsnorm(model.text_model.embed_tokens(ids), layer.input_layernorm.weight, layer.input_layernorm.eps)
+    res = kernel_diff.mixer_diff(layer.linear_attn, n, 256, 32)
+    assert res["impl"] == "native"
+    assert res["out_max_abs_diff"] < 2e-2 * max(1.0, res["out_max_abs"]), res
+    assert res["states_max_abs_diff"] < 2e-2 * max(1.0, res["states_max_abs"]), res

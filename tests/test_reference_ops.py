@@ -67,3 +67,14 @@ def test_complementary_mask_components():
             assert not bool(a[L + i, j])  # x_0 never sees x_t
     leak = ref.complementary_allowed(L, block, "cpu", leak_xt_prefix=True)
     assert bool(leak[block, 0]) and not bool(a[block, 0])
+
+
+def test_kernel_diff_refuses_without_the_native_kernel():
+    import pytest
+
+    from dllm_qwen38_b200.ops import kernel_diff
+
+    q = torch.zeros(1, 64, 1, 16)
+    g = torch.zeros(1, 64, 1)
+    with pytest.raises(RuntimeError, match="cannot run"):
+        kernel_diff.core_diff(q, q, q, g, g, 32, 32)

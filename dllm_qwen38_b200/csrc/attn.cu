@@ -37,9 +37,16 @@ struct Args {
   __nv_bfloat16* dq;            // [B, T2, Hq, D]
   __nv_bfloat16* dk;            // [B, T2, Hk, D]
   __nv_bfloat16* dv;            // [B, T2, Hk, D]
-  int B, T2, L, Hq, Hk, block, leak;
+  int B, T2, L, Hq, Hk, block, leak;  // leak 2: every key visible (decode over a KV cache)
   float scale, scale_log2;
+  // forward only: keys may be a separate, longer sequence (a KV cache) with their own batch
+  // strides; the key count is Tk, or *tk_dev when set (read on the device, graph-capturable)
+  int Tk;
+  int64_t q_bat, k_bat, v_bat;
+  const int* tk_dev;
 };
+
+constexpr int LEAK_ALL = 2;
 
 __device__ __forceinline__ bool allowed(int i, int j, int L, int block, int leak) {
   const bool it = i < L, jt = j < L;
@@ -178,9 +185,11 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
   const int i0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
-  const __nv_bfloat16* qb = a.q + (int64_t)b * a.T2 * a.q_tok + h * D;
-  const __nv_bfloat16* kb = a.k + (int64_t)b * a.T2 * a.k_tok + hk * D;
-  const __nv_bfloat16* vb = a.v + (int64_t)b * a.T2 * a.v_tok + hk * D;
+  const __nv_bfloat16* qb = a.q + (int64_t)b * a.q_bat + h * D;
+  const __nv_bfloat16* kb = a.k + (int64_t)b * a.k_bat + hk * D;
+  const __nv_bfloat16* vb = a.v + (int64_t)b * a.v_bat + hk * D;
+  const int Tk = a.tk_dev != nullptr ? *a.tk_dev : a.Tk;
+  const bool all = a.leak == LEAK_ALL;
   load_tile<D>(sQ, qb, a.q_tok, i0, a.T2);
   cp_commit();
   const int r0 = i0 + warp * 16 + g, r1 = r0 + 8;
@@ -189,11 +198,11 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   const int i1 = min(i0 + TILE - 1, a.T2 - 1);
-  for (int j0 = 0; j0 < a.T2; j0 += TILE) {
-    if (!tile_may(i0, i1, j0, min(j0 + TILE - 1, a.T2 - 1), a.L, a.block, a.leak)) continue;
+  for (int j0 = 0; j0 < Tk; j0 += TILE) {
+    if (!all && !tile_may(i0, i1, j0, min(j0 + TILE - 1, Tk - 1), a.L, a.block, a.leak)) continue;
     __syncthreads();
-    load_tile<D>(sK, kb, a.k_tok, j0, a.T2);
-    load_tile<D>(sV, vb, a.v_tok, j0, a.T2);
+    load_tile<D>(sK, kb, a.k_tok, j0, Tk);
+    load_tile<D>(sV, vb, a.v_tok, j0, Tk);
     cp_commit();
     cp_wait_all();
     __syncthreads();
@@ -206,7 +215,7 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
       for (int e = 0; e < 4; ++e) {
         const int row = e < 2 ? r0 : r1, col = j0 + n * 8 + t4 * 2 + (e & 1);
         float v = s[n][e] * a.scale_log2;
-        if (row >= a.T2 || col >= a.T2 || !allowed(row, col, a.L, a.block, a.leak)) v = NEG_INF;
+        if (row >= a.T2 || col >= Tk || !(all || allowed(row, col, a.L, a.block, a.leak))) v = NEG_INF;
         s[n][e] = v;
         mx[e >> 1] = fmaxf(mx[e >> 1], v);
       }
@@ -456,6 +465,11 @@ static Args make_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor
   a.scale = (float)scale;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   TORCH_CHECK(a.T2 == 2 * L && a.Hq % a.Hk == 0, "attn: shapes");
+  a.Tk = a.T2;
+  a.q_bat = (int64_t)a.T2 * a.q_tok;
+  a.k_bat = (int64_t)a.T2 * a.k_tok;
+  a.v_bat = (int64_t)a.T2 * a.v_tok;
+  a.tk_dev = nullptr;
   return a;
 }
 
@@ -464,6 +478,44 @@ static void go(K kern, dim3 grid, int bytes, const Args& a) {
   C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   kern<<<grid, NTH, bytes, at::cuda::getCurrentCUDAStream()>>>(a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// q [B, Tq, Hq, D] attends to every key of k/v [B, Tmax, Hk, D] rows [0, Tk) (Tk from `tk`, a
+// device int32, when given; else `tk_host`). Output [B, Tq, Hq, D]; no lse.
+template <int D>
+static at::Tensor prefix_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t tk_host,
+                           const c10::optional<at::Tensor>& tk, double scale) {
+  TORCH_CHECK(q.stride(3) == 1 && q.stride(2) == D && k.stride(3) == 1 && k.stride(2) == D && v.stride(3) == 1 &&
+                  v.stride(2) == D,
+              "attn_prefix: heads packed in a token row");
+  for (const at::Tensor* t : {&q, &k, &v})
+    TORCH_CHECK(t->stride(1) % 8 == 0 && t->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0,
+                "attn_prefix: 16-byte aligned rows");
+  Args a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  a.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  a.q_tok = q.stride(1), a.k_tok = k.stride(1), a.v_tok = v.stride(1);
+  a.q_bat = q.stride(0), a.k_bat = k.stride(0), a.v_bat = v.stride(0);
+  a.B = q.size(0), a.T2 = q.size(1), a.L = a.T2, a.Hq = q.size(2), a.Hk = k.size(2), a.block = 1;
+  a.leak = LEAK_ALL;
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.Tk = (int)tk_host;
+  a.tk_dev = nullptr;
+  if (tk.has_value()) {
+    TORCH_CHECK(tk->is_cuda() && tk->scalar_type() == at::kInt, "attn_prefix: tk is a device int32");
+    a.tk_dev = tk->data_ptr<int>();
+  } else {
+    TORCH_CHECK(tk_host >= 1 && tk_host <= k.size(1) && tk_host <= v.size(1), "attn_prefix: 1 <= Tk <= cache rows");
+  }
+  TORCH_CHECK(a.Hq % a.Hk == 0 && k.size(0) == a.B && v.size(0) == a.B, "attn_prefix: shapes");
+  auto o = at::empty({a.B, a.T2, a.Hq, D}, q.options());
+  auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.lse2 = lse.data_ptr<float>();
+  go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 3 * TILE * D * 2, a);
+  return o;
 }
 
 template <int D>
@@ -530,4 +582,13 @@ std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, co
   return {};
 }
 
+}  // namespace bdllm
+
+namespace bdllm {
+at::Tensor attn_prefix(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t tk_host,
+                       const c10::optional<at::Tensor>& tk, double scale) {
+  c10::cuda::CUDAGuard guard(q.device());
+  ATTN_DISPATCH(prefix_t, q, k, v, tk_host, tk, scale)
+  return {};
+}
 }  // namespace bdllm

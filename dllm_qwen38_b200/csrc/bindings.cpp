@@ -33,6 +33,15 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                  const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, int64_t L,
                                  int64_t block, double scale, bool leak);
+at::Tensor attn_prefix(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t tk_host,
+                       const c10::optional<at::Tensor>& tk, double scale);
+std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                 const at::Tensor& beta, const at::Tensor& S0, const c10::optional<at::Tensor>& S_final,
+                                 int64_t C);
+at::Tensor conv_tail(const at::Tensor& raw, at::Tensor& tail, const at::Tensor& w, bool update_tail);
+void confidence(const at::Tensor& logits, at::Tensor& conf, at::Tensor& pick);
+void commit(const at::Tensor& conf, const at::Tensor& pick, at::Tensor& masked, at::Tensor& ids, double threshold,
+            int64_t sub_block, at::Tensor& forwards, at::Tensor& remaining);
 namespace peer {
 int64_t alloc(int64_t bytes);
 at::Tensor handle(int64_t ptr);
@@ -72,6 +81,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_rmsnorm_bwd", &bdllm::gated_rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &bdllm::qk_norm_rope_fwd);
   m.def("qk_norm_rope_bwd", &bdllm::qk_norm_rope_bwd);
+  m.def("attn_prefix", &bdllm::attn_prefix, "attention of a query block over a KV cache (every key visible)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("tk_host"), py::arg("tk") = c10::nullopt, py::arg("scale"));
+  m.def("gdn_rows", &bdllm::gdn_rows, "gated delta rule over decode rows from a cached state", py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta"), py::arg("S0"), py::arg("S_final") = c10::nullopt,
+        py::arg("C"));
+  m.def("conv_tail", &bdllm::conv_tail, "short causal conv + SiLU of a block over a cached conv tail");
+  m.def("confidence", &bdllm::confidence, "softmax max probability and argmax per logits row");
+  m.def("commit", &bdllm::commit, "confidence-threshold commit rule per batch row, on the device");
   m.def("peer_alloc", &bdllm::peer::alloc, "symmetric heap: zeroed device region");
   m.def("peer_handle", &bdllm::peer::handle, "CUDA IPC handle of a heap (64-byte CPU tensor)");
   m.def("peer_open", &bdllm::peer::open, "map a peer's heap from its IPC handle");

@@ -50,6 +50,8 @@ struct Args {
   float* Vp;    // [B, nb, Hv, C, Dv]
   __nv_bfloat16* o;  // [B, 2L, Hv, Dv]
   int concat;        // 1: one causal run over the 2L sequence (the concat fault), no fork
+  const float* S0;   // optional [B, Hv, Dk, Dv] state before the first chunk (decode rows)
+  float* S_final;    // optional [B, Hv, Dk, Dv] state after the last chunk (may alias S0)
   // backward
   const __nv_bfloat16* dout;  // [B, 2L, Hv, Dv]
   float* dS_inj;   // [B, nb, Hv, Dk, Dv]
@@ -396,7 +398,10 @@ __global__ void __launch_bounds__(NT) fwd_recur_kernel(Args a) {
   const int bh = blockIdx.x, b = bh / a.Hv, h = bh % a.Hv;
   const int col0 = blockIdx.y * 32;
   const int ncols = min(32, Dv - col0);
-  for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) sS[idx] = 0.f;
+  for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) {
+    const int r = idx / LDC, cc = idx % LDC;
+    sS[idx] = (a.S0 != nullptr && cc < ncols) ? a.S0[((int64_t)bh * Dk + r) * Dv + col0 + cc] : 0.f;
+  }
   __syncthreads();
   for (int c = 0; c < a.nb; ++c) {
     const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
@@ -430,6 +435,11 @@ __global__ void __launch_bounds__(NT) fwd_recur_kernel(Args a) {
     });
     __syncthreads();
   }
+  if (a.S_final != nullptr)
+    for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
+      const int r = idx / 32, cc = idx % 32;
+      if (cc < ncols) a.S_final[((int64_t)bh * Dk + r) * Dv + col0 + cc] = sS[r * LDC + cc];
+    }
 }
 
 // output for chunk blockIdx.x of the noised stream (x < nb) or clean stream (x >= nb).
@@ -886,7 +896,8 @@ static Args make_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor
   TORCH_CHECK(g.is_contiguous() && beta.is_contiguous() && g.scalar_type() == at::kFloat &&
                   beta.scalar_type() == at::kFloat,
               "gdn: g, beta fp32 contiguous [B, 2L, Hv]");
-  TORCH_CHECK(C <= 32 && C >= 1 && (2 * L) % C == 0 && L % C == 0, "gdn: chunk (= block) must be <= 32 and divide L");
+  TORCH_CHECK(C <= 32 && C >= 1 && (2 * L) % C == 0 && (concat || L % C == 0),
+              "gdn: chunk (= block) must be <= 32 and divide L");
   Args a{};
   a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
@@ -935,6 +946,46 @@ static std::vector<at::Tensor> forward_t(const at::Tensor& q, const at::Tensor& 
   const int ngrid = concat ? a.nb : 2 * a.nb;
   launch(fwd_out_kernel<Dk, Dv>, dim3(ngrid, BH), Smem<Dk, Dv>::floats, a);
   return {o, S_in, Vp};
+}
+
+// Decode rows: q, k [B, T, Hk, Dk], v [B, T, Hv, Dv] (T even, chunked by C), one causal run per
+// row starting from S0 [B, Hv, Dk, Dv] (fp32); writes the final state into S_final when given
+// (S_final may be S0: each CTA reads its slice before it writes it). Returns o [B, T, Hv, Dv].
+template <int Dk, int Dv>
+static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                      const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S0,
+                                      const c10::optional<at::Tensor>& S_final, int64_t C) {
+  const int64_t T = q.size(1);
+  TORCH_CHECK(T % 2 == 0 && T % C == 0, "gdn_rows: T even and a multiple of the chunk");
+  Args a = make_args(q, k, v, g, beta, T / 2, C, true);
+  TORCH_CHECK(S0.is_contiguous() && S0.scalar_type() == at::kFloat && S0.numel() == (int64_t)a.B * a.Hv * Dk * Dv,
+              "gdn_rows: S0 fp32 [B, Hv, Dk, Dv]");
+  auto f32 = q.options().dtype(at::kFloat);
+  auto U = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
+  auto W = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
+  auto Kt = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
+  auto Ec = at::empty({a.B, a.nb, a.Hv}, f32);
+  auto S_in = at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
+  auto Vp = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
+  auto o = at::empty({a.B, T, a.Hv, Dv}, q.options());
+  a.U = U.data_ptr<float>();
+  a.W = W.data_ptr<float>();
+  a.Kt = Kt.data_ptr<float>();
+  a.Ec = Ec.data_ptr<float>();
+  a.S_in = S_in.data_ptr<float>();
+  a.Vp = Vp.data_ptr<float>();
+  a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  a.S0 = S0.data_ptr<float>();
+  if (S_final.has_value()) {
+    TORCH_CHECK(S_final->is_contiguous() && S_final->scalar_type() == at::kFloat && S_final->numel() == S0.numel(),
+                "gdn_rows: S_final like S0");
+    a.S_final = S_final->data_ptr<float>();
+  }
+  const int BH = a.B * a.Hv;
+  launch(fwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
+  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 2 * 32 * Ld<Dk>::v + 32 * LDC + Dk * LDC, a);
+  launch(fwd_out_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
+  return {o};
 }
 
 // Backward. Returns {dq, dk (per v-head), dv, dg, dbeta}.
@@ -1007,6 +1058,14 @@ std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, con
                                 int64_t C, bool concat) {
   c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(backward_t, dout, q, k, v, g, beta, S_in, L, C, concat)
+  return {};
+}
+
+std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                 const at::Tensor& beta, const at::Tensor& S0, const c10::optional<at::Tensor>& S_final,
+                                 int64_t C) {
+  c10::cuda::CUDAGuard guard(q.device());
+  GDN_DISPATCH(rows_t, q, k, v, g, beta, S0, S_final, C)
   return {};
 }
 

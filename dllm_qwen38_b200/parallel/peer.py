@@ -26,6 +26,12 @@ import torch.distributed as dist
 
 from ..ops import _native
 
+
+def _count() -> None:
+    from ..ops import cuda
+
+    cuda.LAUNCHES[0] += 1
+
 HEADER_BYTES = 64 * 1024
 SLOT_EPOCH = 0
 
@@ -81,20 +87,24 @@ class SymmetricHeap:
                    max_blocks: int = 148) -> None:
         self.C.peer_all_gather(self.ptrs, self.rank, off, shard_bytes, out,
                                self.epoch if epoch is None else epoch, max_blocks, self.timeout)
+        _count()
 
     def reduce_scatter(self, off: int, shard: int, in_f32: bool, out: torch.Tensor, scale: float,
                        sq: torch.Tensor | None = None, max_blocks: int = 64) -> None:
         self.rs_seq += 1
         self.C.peer_reduce_scatter(self.ptrs, self.rank, off, shard, in_f32, out, scale, sq, self.rs_seq,
                                    max_blocks, self.timeout)
+        _count()
 
     def allreduce_f32(self, vals: torch.Tensor, out: torch.Tensor) -> None:
         self.ar_seq += 1
         self.C.peer_allreduce_f32(self.ptrs, self.rank, vals, out, self.ar_seq, self.timeout)
+        _count()
 
     def publish_epoch(self, epoch: int) -> None:
         self.epoch = epoch
         self.C.peer_signal(self.ptrs, self.rank, SLOT_EPOCH, epoch)
+        _count()
 
     def close(self) -> None:
         """Unmap peers and free the heap (call after every kernel using it has finished)."""

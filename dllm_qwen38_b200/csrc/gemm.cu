@@ -27,7 +27,15 @@ enum Epi : int {
   EPI_ADD_BF16 = 2,  // C (bf16) = acc + R (bf16; R may alias C)
   EPI_ACC_F32 = 3,   // C (fp32) += acc
   EPI_SWIGLU = 4,    // B rows [j, F + j] interleaved per tile; C = silu(gate) * up, optional GU store
+  EPI_PEER_F32 = 5,  // tensor parallel: fp32 partial rows stored into the owner rank's slot (peer memory)
 };
+
+// Tensor-parallel hooks (peer memory; see csrc/tp.cu for the other half of each collective).
+// Counters in `ctr` (this rank's device memory): sequence numbers advanced on the device so that
+// a captured CUDA graph replays with fresh values.
+enum TpCtr : int { CTR_RS = 0, CTR_RS_ARRIVE = 1, CTR_AGC = 2, CTR_AGC_ARRIVE = 3 };
+enum TpSlot : int { TP_SLOT_RS = 8, TP_SLOT_AG = 9, TP_SLOT_CONF = 10 };
+constexpr int TP_MAX = 8;
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -43,7 +51,28 @@ struct GemmArgs {
   int ldgu;
   int* err;     // device error word
   float alpha;  // accumulator scale applied before the epilogue op
+  // tensor parallel (EPI_PEER_F32 and/or wait_ag)
+  int64_t peers[TP_MAX];  // symmetric heap bases of the TP ranks
+  int world, rank;
+  int rows_per_rank;      // EPI_PEER_F32: output row r belongs to rank r / rows_per_rank
+  int64_t part_off;       // EPI_PEER_F32: byte offset of the owners' fp32 partial slots [world][rows][ldc]
+  int64_t flag_off;       // byte offset of the flag rows (u32 [16 slots][16 ranks]) in every heap
+  unsigned* ctr;          // this rank's TP counters
+  int wait_ag;            // the producer waits until every rank pushed the gathered A rows
+  uint64_t timeout_ns;
 };
+
+__device__ __forceinline__ void tp_st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned tp_ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned* tp_flag(int64_t base, int64_t flag_off, int slot, int src) {
+  return reinterpret_cast<unsigned*>(base + flag_off) + slot * 16 + src;
+}
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 struct Cfg {
@@ -121,6 +150,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t round = 0;
     uint32_t armed_mask = 0;  // stages with a load in flight or landed (bit s)
     bool ok = true;
+    if (args.wait_ag) {  // fused all-gather: A's rows are pushed by every rank; wait for all of them
+      const unsigned target = args.ctr[CTR_AGC] + 1u;
+      const uint64_t t0 = globaltimer();
+      for (int p = 0; p < args.world && ok; ++p) {
+        const unsigned* f = tp_flag(args.peers[args.rank], args.flag_off, TP_SLOT_AG, p);
+        while (static_cast<int>(tp_ld_acquire(f) - target) < 0) {
+          if (globaltimer() - t0 > args.timeout_ns || *reinterpret_cast<volatile int*>(args.err) != 0) {
+            record_error(args.err, ERR_COMM_WAIT);
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          __nanosleep(64);
+        }
+      }
+      asm volatile("fence.proxy.async.global;" ::: "memory");  // peers' generic writes -> our TMA reads
+    }
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
       tile_coords(t, tiles_m, tiles_n, tm, tn);
@@ -282,6 +328,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               }
             }
           }
+        } else if constexpr (EPI == EPI_PEER_F32) {
+          if (row_ok) {
+            const int owner = row / args.rows_per_rank, lr = row - owner * args.rows_per_rank;
+            float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
+                         ((int64_t)args.rank * args.rows_per_rank + lr) * args.ldc + col0;
+            if (col0 + 32 <= args.N) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) out[j] = v[j];
+            }
+          }
         } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
           if (row_ok) {
             float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col0;
@@ -344,10 +405,29 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
   }
   tc_fence_before();
+  if constexpr (EPI == EPI_PEER_F32) __threadfence_system();  // this thread's peer stores
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C_::TMEM_COLS);
+  }
+  if ((EPI == EPI_PEER_F32 || args.wait_ag) && threadIdx.x == 0) {
+    // the last CTA to finish advances the device counters and, for EPI_PEER_F32, tells every
+    // owner that this rank's partial rows have landed
+    __threadfence_system();
+    const int arrive = EPI == EPI_PEER_F32 ? CTR_RS_ARRIVE : CTR_AGC_ARRIVE;
+    const unsigned prev = atomicAdd(&args.ctr[arrive], 1u);
+    if (prev == gridDim.x - 1) {
+      args.ctr[arrive] = 0u;
+      if (args.wait_ag) args.ctr[CTR_AGC] += 1u;
+      if constexpr (EPI == EPI_PEER_F32) {
+        const unsigned seq = args.ctr[CTR_RS] + 1u;
+        args.ctr[CTR_RS] = seq;
+        __threadfence_system();
+        for (int p = 0; p < args.world; ++p)
+          tp_st_release(tp_flag(args.peers[p], args.flag_off, TP_SLOT_RS, args.rank), seq);
+      }
+    }
   }
 }
 
@@ -452,9 +532,51 @@ static void launch(GemmLaunch* L, cudaStream_t st) {
 
 // C = A B^T-style contraction with operand majors; see the file header for the conventions.
 // a: K-major -> [M, K] (lda); MN-major -> [K, M] (lda). b: K-major -> [N, K]; MN-major -> [K, N].
+struct TpHook {
+  const std::vector<int64_t>* peers;
+  int rank, rows_per_rank, wait_ag;
+  int64_t part_off, flag_off;
+  unsigned* ctr;
+  double timeout_s;
+};
+
+static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
+                      int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
+                      const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
+                      double alpha, const TpHook* tp);
+
 void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
           int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
           int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha) {
+  TORCH_CHECK(epi != EPI_PEER_F32, "gemm: the peer epilogue goes through gemm_tp");
+  gemm_impl(a, a_mn, lda, b, b_mn, ldb, M, N, K, c, ldc, epi, r, ldr, gu, bn, alpha, nullptr);
+}
+
+// Tensor-parallel GEMM: y = a b^T (K-major operands) with the collective hooks. epi EPI_PEER_F32:
+// output rows go to their owner's fp32 partial slot in peer memory (c is only the shape/stride
+// template, [M, N] fp32); other epilogues write c locally. wait_ag: wait for every rank's pushed
+// A rows first (the gathered A lives in this rank's heap).
+void gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
+             const std::vector<int64_t>& peers, int64_t rank, int64_t rows_per_rank, int64_t part_off,
+             int64_t flag_off, const at::Tensor& ctr, bool wait_ag, double timeout_s, int64_t bn) {
+  TORCH_CHECK(peers.size() >= 1 && peers.size() <= (size_t)TP_MAX, "gemm_tp: 1..8 ranks");
+  TORCH_CHECK(ctr.is_cuda() && ctr.scalar_type() == at::kInt && ctr.numel() >= 4, "gemm_tp: int32 counters [>= 4]");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_tp: 2-D K-major operands");
+  const int64_t M = a.size(0), K = a.size(1), N = (epi == EPI_SWIGLU) ? b.size(0) / 2 : b.size(0);
+  if (epi == EPI_PEER_F32)
+    TORCH_CHECK(rows_per_rank > 0 && M % rows_per_rank == 0 && M / rows_per_rank == (int64_t)peers.size() &&
+                    c.scalar_type() == at::kFloat && c.size(1) == N && (c.stride(0) * 4) % 16 == 0,
+                "gemm_tp: peer epilogue needs M = world * rows_per_rank and an fp32 [M, N] template");
+  TpHook h{&peers, (int)rank, (int)rows_per_rank, wait_ag ? 1 : 0, part_off, flag_off,
+           reinterpret_cast<unsigned*>(ctr.data_ptr<int>()), timeout_s};
+  gemm_impl(a, false, a.stride(0), b, false, b.stride(0), M, N, K, c, c.stride(0), epi, c10::nullopt, 0, gu, bn, 1.0,
+            &h);
+}
+
+static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
+                      int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
+                      const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
+                      double alpha, const TpHook* tp) {
   GTRACE("enter");
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors expected");
   bind_context(a.get_device());
@@ -475,7 +597,19 @@ void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool
     args.GU = reinterpret_cast<__nv_bfloat16*>(gu->data_ptr());
     args.ldgu = (int)(2 * N);
   }
-  const bool f32_out = (epi == EPI_F32 || epi == EPI_ACC_F32);
+  if (tp != nullptr) {
+    const int w = (int)tp->peers->size();
+    for (int i = 0; i < w; ++i) args.peers[i] = (*tp->peers)[i];
+    args.world = w;
+    args.rank = tp->rank;
+    args.rows_per_rank = tp->rows_per_rank;
+    args.part_off = tp->part_off;
+    args.flag_off = tp->flag_off;
+    args.ctr = tp->ctr;
+    args.wait_ag = tp->wait_ag;
+    args.timeout_ns = (uint64_t)(tp->timeout_s * 1e9);
+  }
+  const bool f32_out = (epi == EPI_F32 || epi == EPI_ACC_F32 || epi == EPI_PEER_F32);
   TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype does not match the epilogue");
   // the epilogue stores (and reads the residual) in 16-byte vectors: rows must stay 16-byte aligned
   const int64_t esz = f32_out ? 4 : 2;
@@ -514,6 +648,9 @@ void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool
   BDLLM_GEMM_CASE(256, false, false, EPI_F32)
   BDLLM_GEMM_CASE(256, false, false, EPI_ADD_BF16)
   BDLLM_GEMM_CASE(256, false, false, EPI_SWIGLU)
+  BDLLM_GEMM_CASE(256, false, false, EPI_PEER_F32)
+  BDLLM_GEMM_CASE(128, false, false, EPI_PEER_F32)
+  BDLLM_GEMM_CASE(128, false, false, EPI_SWIGLU)
   BDLLM_GEMM_CASE(256, false, true, EPI_BF16)
   BDLLM_GEMM_CASE(256, false, true, EPI_ADD_BF16)
   BDLLM_GEMM_CASE(256, false, true, EPI_F32)

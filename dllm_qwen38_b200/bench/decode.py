@@ -47,6 +47,18 @@ def main(argv=None) -> int:
     from dllm_qwen38_b200.models.qwen35 import build_model
 
     cfg = preset(a.model, layers=a.layers)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:  # tensor parallel: one process per GPU (torchrun)
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
+        if a.impl != "native":
+            raise SystemExit("the reference decoder is single-GPU")
     dev = "cuda"
     g = torch.Generator().manual_seed(a.seed)
     prompts = [torch.randint(0, cfg.mask_id, (a.prompt_len,), generator=g).tolist() for _ in range(a.batch)]
@@ -60,6 +72,17 @@ def main(argv=None) -> int:
 
         def run():
             out = cached.generate(model, prompts, **kw)
+            return sum(t.generated for t in out), sum(t.forwards for t in out)
+    elif a.impl == "native" and world > 1:
+        from dllm_qwen38_b200.infer.tp import TPDecodeEngine
+
+        eng = TPDecodeEngine(model, a.batch, a.prompt_len + (n_blocks + 1) * a.block, a.block,
+                             threshold=a.threshold, sub_block=a.sub_block, graphs=not a.no_graphs)
+        del model
+        torch.cuda.empty_cache()
+
+        def run():
+            out = eng.generate(prompts, n_blocks=n_blocks)
             return sum(t.generated for t in out), sum(t.forwards for t in out)
     elif a.impl == "native":
         from dllm_qwen38_b200.infer.engine import DecodeEngine
@@ -125,8 +148,19 @@ def main(argv=None) -> int:
     e1.record()
     torch.cuda.synchronize()
     s = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the slowest rank's device time
+        s = float(t.item())
+        eng.close()
+        dist.destroy_process_group()
+        if rank != 0:
+            return 0
     print(json.dumps({"metric": "dLLM decode tok/s", "value": round(gen / s, 2), "unit": "tok/s", "impl": a.impl, "engine": a.engine if a.impl == "native" else "golden",
-                      "generated": gen, "forwards": fw, "seconds": round(s, 3), "batch": a.batch,
+                      "generated": gen, "forwards": fw, "seconds": round(s, 3), "batch": a.batch, "n_gpus": world,
+                      "parallelism": f"tp{world}" if world > 1 else "single",
                       "config": {"model": a.model, "layers": cfg.num_hidden_layers, "prompt_len": a.prompt_len,
                                  "new_tokens": a.new_tokens, "block": a.block, "sub_block": a.sub_block,
                                  "threshold": a.threshold, "data": "random ids, random weights"}}))

@@ -51,6 +51,12 @@ void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_
 void tp_confidence(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& logits, int64_t v0,
                    int64_t conf_off, int64_t flag_off, at::Tensor& ctr, at::Tensor& conf, at::Tensor& pick,
                    double timeout_s);
+at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& table);
+void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh);
+std::vector<at::Tensor> gdn_gates_fwd(const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
+                                      const at::Tensor& dt_bias);
+std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& dbeta, const at::Tensor& a,
+                                      const at::Tensor& b, const at::Tensor& A_log, const at::Tensor& dt_bias);
 namespace peer {
 int64_t alloc(int64_t bytes);
 at::Tensor handle(int64_t ptr);
@@ -106,6 +112,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm_push", &bdllm::tp_reduce_norm_push,
         "owner rows: sum peers' partials + residual, RMSNorm, push to every rank's gathered buffer");
   m.def("tp_confidence", &bdllm::tp_confidence, "vocab-parallel confidence: per-slice push + rank-order merge");
+  m.def("embed_fwd", &bdllm::embed_fwd, "embedding row gather");
+  m.def("embed_bwd_", &bdllm::embed_bwd_, "embedding gradient scatter-add into an fp32 table");
+  m.def("gdn_gates_fwd", &bdllm::gdn_gates_fwd, "beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)");
+  m.def("gdn_gates_bwd", &bdllm::gdn_gates_bwd);
   m.def("peer_alloc", &bdllm::peer::alloc, "symmetric heap: zeroed device region");
   m.def("peer_handle", &bdllm::peer::handle, "CUDA IPC handle of a heap (64-byte CPU tensor)");
   m.def("peer_open", &bdllm::peer::open, "map a peer's heap from its IPC handle");

@@ -441,4 +441,166 @@ void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------- embedding
+// out[i] = table[ids[i]] (bf16 rows, 16-byte vectors); one warp per row
+__global__ void embed_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int D,
+                                 int64_t V, __nv_bfloat16* __restrict__ out, int64_t N, int* err) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= N) return;
+  const int64_t id = ids[row];
+  if (id < 0 || id >= V) {  // out of range: record, write zeros (never read outside the table)
+    if ((threadIdx.x & 31) == 0) record_error(err, ERR_BOUNDS);
+    for (int c = (threadIdx.x & 31) * 8; c < D; c += 256)
+      *reinterpret_cast<uint4*>(out + row * D + c) = make_uint4(0, 0, 0, 0);
+    return;
+  }
+  for (int c = (threadIdx.x & 31) * 8; c < D; c += 256)
+    *reinterpret_cast<uint4*>(out + row * D + c) = *reinterpret_cast<const uint4*>(table + id * D + c);
+}
+
+// grad[ids[i]] += dh[i] (fp32 accumulate); one warp per row
+__global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ dh, int D,
+                                 int64_t V, float* __restrict__ grad, int64_t N) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (row >= N) return;
+  const int64_t id = ids[row];
+  if (id < 0 || id >= V) return;
+  for (int c = (threadIdx.x & 31) * 8; c < D; c += 256) {
+    const uint4 p = *reinterpret_cast<const uint4*>(dh + row * D + c);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(p2[e]);
+      atomicAdd(grad + id * D + c + 2 * e, f.x);
+      atomicAdd(grad + id * D + c + 2 * e + 1, f.y);
+    }
+  }
+}
+
+at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& table) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embed: int64 ids");
+  TORCH_CHECK(table.dim() == 2 && table.is_contiguous() && table.scalar_type() == at::kBFloat16 &&
+                  table.size(1) % 8 == 0,
+              "embed: bf16 table [V, D], D % 8 == 0");
+  const int64_t N = ids.numel(), V = table.size(0);
+  const int D = table.size(1);
+  auto sizes = ids.sizes().vec();
+  sizes.push_back(D);
+  auto out = at::empty(sizes, table.options());
+  if (N == 0) return out;
+  c10::cuda::CUDAGuard g(table.device());
+  embed_fwd_kernel<<<(int)((N + 7) / 8), 256, 0, stream()>>>(ids.data_ptr<int64_t>(), cbf(table), D, V, bfp(out), N,
+                                                             error_word_ptr());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
+void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh) {
+  TORCH_CHECK(grad.dim() == 2 && grad.is_contiguous() && grad.scalar_type() == at::kFloat, "embed_bwd: fp32 [V, D]");
+  TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embed_bwd: int64 ids");
+  const int64_t N = ids.numel(), V = grad.size(0);
+  const int D = grad.size(1);
+  auto d = dh.to(at::kBFloat16).contiguous();
+  TORCH_CHECK(d.numel() == N * D && D % 8 == 0, "embed_bwd: dh [N, D]");
+  if (N == 0) return;
+  c10::cuda::CUDAGuard g(grad.device());
+  embed_bwd_kernel<<<(int)((N + 7) / 8), 256, 0, stream()>>>(ids.data_ptr<int64_t>(), cbf(d), D, V,
+                                                             grad.data_ptr<float>(), N);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------- GDN gates
+// beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) (softplus linear above 20, as torch's)
+__device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+// a, b: [rows, H] views with row stride lda / ldb (bf16); g, beta: [rows, H] fp32
+__global__ void gates_fwd_kernel(const __nv_bfloat16* __restrict__ a, int64_t lda, const __nv_bfloat16* __restrict__ b,
+                                 int64_t ldb, const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                 int H, int64_t rows, float* __restrict__ g, float* __restrict__ beta) {
+  const int64_t n = rows * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H;
+    const int h = (int)(i - r * H);
+    const float x = __bfloat162float(a[r * lda + h]) + dt_bias[h];
+    g[i] = -__expf(A_log[h]) * softplus_f(x);
+    beta[i] = sigmoid_f(__bfloat162float(b[r * ldb + h]));
+  }
+}
+
+// da = dg * (-exp(A_log)) * sigmoid(a + dt_bias); db = dbeta * beta (1 - beta);
+// d dt_bias[h] = sum_r da; d A_log[h] = sum_r dg * g  (per-head sums: block partials + atomics)
+__global__ void gates_bwd_kernel(const __nv_bfloat16* __restrict__ a, int64_t lda, const __nv_bfloat16* __restrict__ b,
+                                 int64_t ldb, const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+                                 const float* __restrict__ dg, const float* __restrict__ dbeta, int H, int64_t rows,
+                                 __nv_bfloat16* __restrict__ da, __nv_bfloat16* __restrict__ db,
+                                 float* __restrict__ dA_log, float* __restrict__ ddt) {
+  extern __shared__ float red[];  // [2 * H]
+  for (int i = threadIdx.x; i < 2 * H; i += blockDim.x) red[i] = 0.f;
+  __syncthreads();
+  const int64_t n = rows * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / H;
+    const int h = (int)(i - r * H);
+    const float x = __bfloat162float(a[r * lda + h]) + dt_bias[h];
+    const float ea = __expf(A_log[h]);
+    const float gv = -ea * softplus_f(x);
+    const float dav = dg[i] * (-ea) * sigmoid_f(x);
+    const float be = sigmoid_f(__bfloat162float(b[r * ldb + h]));
+    da[i] = __float2bfloat16(dav);
+    db[i] = __float2bfloat16(dbeta[i] * be * (1.f - be));
+    atomicAdd(&red[h], dav);
+    atomicAdd(&red[H + h], dg[i] * gv);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    atomicAdd(&ddt[i], red[i]);
+    atomicAdd(&dA_log[i], red[H + i]);
+  }
+}
+
+static void check_gate_view(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.stride(-1) == 1, "gdn_gates: ", name, " bf16 with unit inner stride");
+  TORCH_CHECK(t.dim() >= 2, "gdn_gates: ", name, " [..., H]");
+  for (int d = 0; d < t.dim() - 2; ++d)
+    TORCH_CHECK(t.stride(d) == t.size(d + 1) * t.stride(d + 1), "gdn_gates: ", name, " rows must merge");
+}
+
+std::vector<at::Tensor> gdn_gates_fwd(const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
+                                      const at::Tensor& dt_bias) {
+  check_gate_view(a, "a");
+  check_gate_view(b, "b");
+  const int H = a.size(-1);
+  const int64_t rows = a.numel() / H;
+  auto Af = A_log.to(at::kFloat).contiguous(), df = dt_bias.to(at::kFloat).contiguous();
+  auto g = at::empty(a.sizes(), a.options().dtype(at::kFloat));
+  auto beta = at::empty(a.sizes(), a.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard gd(a.device());
+  gates_fwd_kernel<<<grid_for(rows * H), 256, 0, stream()>>>(cbf(a), a.stride(-2), cbf(b), b.stride(-2),
+                                                             Af.data_ptr<float>(), df.data_ptr<float>(), H, rows,
+                                                             g.data_ptr<float>(), beta.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {g, beta};
+}
+
+std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& dbeta, const at::Tensor& a,
+                                      const at::Tensor& b, const at::Tensor& A_log, const at::Tensor& dt_bias) {
+  check_gate_view(a, "a");
+  check_gate_view(b, "b");
+  const int H = a.size(-1);
+  const int64_t rows = a.numel() / H;
+  auto Af = A_log.to(at::kFloat).contiguous(), df = dt_bias.to(at::kFloat).contiguous();
+  auto dgc = dg.to(at::kFloat).contiguous(), dbc = dbeta.to(at::kFloat).contiguous();
+  auto da = at::empty(a.sizes(), a.options());
+  auto db = at::empty(a.sizes(), a.options());
+  auto dA = at::zeros({H}, a.options().dtype(at::kFloat));
+  auto ddt = at::zeros({H}, a.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard gd(a.device());
+  const int grid = std::min<int64_t>(grid_for(rows * H), 148 * 4);
+  gates_bwd_kernel<<<grid, 256, 2 * H * sizeof(float), stream()>>>(
+      cbf(a), a.stride(-2), cbf(b), b.stride(-2), Af.data_ptr<float>(), df.data_ptr<float>(), dgc.data_ptr<float>(),
+      dbc.data_ptr<float>(), H, rows, bfp(da), bfp(db), dA.data_ptr<float>(), ddt.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {da, db, dA, ddt};
+}
+
 }  // namespace bdllm

@@ -106,8 +106,8 @@ class DecodeEngine:
         q = q.view(B, T, m.num_k_heads, m.head_k_dim)
         k = k.view(B, T, m.num_k_heads, m.head_k_dim)
         v = v.view(B, T, m.num_v_heads, m.head_v_dim)
-        g, beta = ref.gdn_gates(a, b, m.A_log, m.dt_bias)
-        (o,) = C.gdn_rows(q, k, v, g.float().contiguous(), beta.float().contiguous(), e["S"],
+        g, beta = C.gdn_gates_fwd(a, b, m.A_log, m.dt_bias)
+        (o,) = C.gdn_rows(q, k, v, g, beta, e["S"],
                           e["S"] if commit else None, T)
         y = Cu.gated_rmsnorm(o, z.reshape(B, T, m.num_v_heads, m.head_v_dim), m.norm.weight, m.norm.eps)
         return y.reshape(B * T, m.value_dim), m.out_proj.weight

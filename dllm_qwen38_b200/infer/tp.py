@@ -91,7 +91,7 @@ class TPDecodeEngine:
                 rows_k = slice(kd + r * hk * Dk, kd + (r + 1) * hk * Dk)
                 rows_v = slice(2 * kd + r * hv * Dv, 2 * kd + (r + 1) * hv * Dv)
                 cw = m.conv1d.weight[:, 0, :]
-                e.update(m=m, hk=hk, hv=hv, Dk=Dk, Dv=Dv,
+                e.update(hk=hk, hv=hv, Dk=Dk, Dv=Dv,
                          w_in=torch.cat([qkv[rows_q], qkv[rows_k], qkv[rows_v],
                                          m.in_proj_z.weight[r * hv * Dv:(r + 1) * hv * Dv],
                                          m.in_proj_b.weight[r * hv:(r + 1) * hv],
@@ -99,7 +99,7 @@ class TPDecodeEngine:
                          conv_w=torch.cat([cw[rows_q], cw[rows_k], cw[rows_v]], 0).float().contiguous(),
                          A_log=m.A_log[r * hv:(r + 1) * hv].detach().clone(),
                          dt_bias=m.dt_bias[r * hv:(r + 1) * hv].detach().clone(),
-                         norm_w=m.norm.weight.detach(), norm_eps=m.norm.eps,
+                         norm_w=m.norm.weight.detach().clone(), norm_eps=m.norm.eps,
                          w_out=m.out_proj.weight[:, r * hv * Dv:(r + 1) * hv * Dv].contiguous(),
                          S=torch.zeros(B, hv, Dk, Dv, device=dev),
                          tail=torch.zeros(B, m.conv_kernel_size - 1, 2 * hk * Dk + hv * Dv, device=dev, dtype=self.dt))
@@ -110,7 +110,8 @@ class TPDecodeEngine:
                 kv0, kv1 = (r * hq) // grp, ((r + 1) * hq - 1) // grp + 1
                 if hq % (kv1 - kv0):
                     raise ValueError("TP decode: local q heads must split evenly over the local kv heads")
-                e.update(m=m, hq=hq, hk=kv1 - kv0, Dh=Dh,
+                e.update(qn=m.q_norm.weight.detach().clone(), kn=m.k_norm.weight.detach().clone(), qk_eps=m.q_norm.eps,
+                         hq=hq, hk=kv1 - kv0, Dh=Dh,
                          w_qkv=torch.cat([m.q_proj.weight[r * hq * 2 * Dh:(r + 1) * hq * 2 * Dh],
                                           m.k_proj.weight[kv0 * Dh:kv1 * Dh],
                                           m.v_proj.weight[kv0 * Dh:kv1 * Dh]], 0).contiguous(),
@@ -122,7 +123,7 @@ class TPDecodeEngine:
             self.layers.append(e)
         self.final_w1 = (1.0 + tm.norm.weight.float()).contiguous()
         self.final_eps = tm.norm.eps
-        self.embed = tm.embed_tokens.weight
+        self.embed = tm.embed_tokens.weight.detach()
         self.Vl = V // W
         self.head = model.lm_head.weight[r * self.Vl:(r + 1) * self.Vl].contiguous()
         self.cos_t, self.sin_t = ref.rope_cos_sin(torch.arange(self.max_len), cfg.rotary_dim, cfg.rope_theta,
@@ -202,7 +203,7 @@ class TPDecodeEngine:
         raw, z, b, a = torch.split(proj, [cd, hv * Dv, hv, hv], -1)
         mixed = C.conv_tail(raw, e["tail"], e["conv_w"], commit)
         q, k, v = torch.split(mixed, [hk * Dk, hk * Dk, hv * Dv], dim=-1)
-        g, beta = ref.gdn_gates(a, b, e["A_log"], e["dt_bias"])
+        g, beta = C.gdn_gates_fwd(a, b, e["A_log"], e["dt_bias"])
         (o,) = C.gdn_rows(q.view(B, T, hk, Dk), k.view(B, T, hk, Dk), v.view(B, T, hv, Dv), g.float().contiguous(),
                           beta.float().contiguous(), e["S"], e["S"] if commit else None, T)
         y = Cu.gated_rmsnorm(o, z.reshape(B, T, hv, Dv), e["norm_w"], e["norm_eps"])
@@ -210,12 +211,12 @@ class TPDecodeEngine:
 
     def _attn(self, e, cos, sin):
         C, Cu, B, T = self.C, self.Cu, self.B, self.T
-        m, hq, hk, Dh = e["m"], e["hq"], e["hk"], e["Dh"]
+        hq, hk, Dh = e["hq"], e["hk"], e["Dh"]
         proj = self._col(e["w_qkv"]).view(B, T, -1)
         qg, k, v = torch.split(proj, [2 * hq * Dh, hk * Dh, hk * Dh], dim=-1)
         qg = qg.view(B, T, hq, 2 * Dh)
         q, gate = qg[..., :Dh], qg[..., Dh:]
-        q, k = Cu.qk_norm_rope(q, k.view(B, T, hk, Dh), m.q_norm.weight, m.k_norm.weight, m.q_norm.eps, cos, sin)
+        q, k = Cu.qk_norm_rope(q, k.view(B, T, hk, Dh), e["qn"], e["kn"], e["qk_eps"], cos, sin)
         e["K"].index_copy_(1, self.pos, k)
         e["V"].index_copy_(1, self.pos, v.view(B, T, hk, Dh))
         o = C.attn_prefix(q, e["K"], e["V"], 0, self.tk, Dh ** -0.5) * torch.sigmoid(gate)

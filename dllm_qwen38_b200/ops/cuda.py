@@ -19,7 +19,7 @@ EPI_BF16, EPI_F32, EPI_ADD_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
 
 # ops that have no sm_100a kernel yet; on CUDA tensors they run the torch reference and are
 # recorded as 'torch-cuda' by ops.last_impl()
-TORCH_ON_CUDA = {"gdn_gates", "embedding"}
+TORCH_ON_CUDA: set = set()
 
 
 # native kernel launches issued through this module (benchmarks report the count of a region)
@@ -328,6 +328,58 @@ class _GDNCore(torch.autograd.Function):
             dq = dq.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(q.dtype)
             dk = dk.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(k.dtype)
         return dq, dk, dv, dg.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None, None, None
+
+
+class _Gates(torch.autograd.Function):
+    """beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias), both fp32 (a, b bf16 views)."""
+
+    @staticmethod
+    def forward(ctx, a, b, A_log, dt_bias):
+        g, beta = _C.gdn_gates_fwd(a, b, A_log, dt_bias)
+        ctx.save_for_backward(a, b, A_log, dt_bias)
+        _count()
+        return g, beta
+
+    @staticmethod
+    def backward(ctx, dg, dbeta):
+        a, b, A_log, dt_bias = ctx.saved_tensors
+        if dg is None:
+            dg = torch.zeros(a.shape, device=a.device, dtype=torch.float32)
+        if dbeta is None:
+            dbeta = torch.zeros(a.shape, device=a.device, dtype=torch.float32)
+        da, db, dA, ddt = _C.gdn_gates_bwd(dg, dbeta, a, b, A_log, dt_bias)
+        _count()
+        return da, db, dA.to(A_log.dtype), ddt.to(dt_bias.dtype)
+
+
+def gdn_gates(a, b, A_log, dt_bias):
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        a, b = a.to(torch.bfloat16), b.to(torch.bfloat16)
+    return _Gates.apply(a, b, A_log, dt_bias)
+
+
+class _Embedding(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, ids, table):
+        ids_c = ids.contiguous()
+        ctx.save_for_backward(ids_c)
+        ctx.shape, ctx.dt = table.shape, table.dtype
+        _count()
+        return _C.embed_fwd(ids_c, table.contiguous())
+
+    @staticmethod
+    def backward(ctx, dh):
+        (ids,) = ctx.saved_tensors
+        grad = torch.zeros(ctx.shape, device=dh.device, dtype=torch.float32)
+        _C.embed_bwd_(grad, ids, dh)
+        _count()
+        return None, grad.to(ctx.dt)
+
+
+def embedding(ids, table):
+    if table.dtype != torch.bfloat16:
+        raise TypeError("native embedding: bf16 table")
+    return _Embedding.apply(ids, table)
 
 
 def gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode):

@@ -402,7 +402,12 @@ class _EmbedFn(torch.autograd.Function):
     def forward(ctx, ids, anchor, engine):
         buf = engine.gather(engine.embed)
         table = engine.embed.views(buf)["weight"]
-        h = torch.nn.functional.embedding(ids, table)
+        if ids.is_cuda:
+            from ..ops import _native
+
+            h = _native.require().embed_fwd(ids.contiguous(), table)
+        else:
+            h = torch.nn.functional.embedding(ids, table)
         ctx.save_for_backward(ids)
         ctx.engine = engine
         if engine.layers:
@@ -415,7 +420,12 @@ class _EmbedFn(torch.autograd.Function):
         engine = ctx.engine
         V, D = engine.cfg.vocab_size, engine.cfg.hidden_size
         tg = engine.table_grad[: V * D].view(V, D)  # already holds the tied head's gradient, if any
-        tg.index_add_(0, ids.reshape(-1), dh.reshape(-1, D).float())
+        if tg.is_cuda:
+            from ..ops import _native
+
+            _native.require().embed_bwd_(tg, ids.reshape(-1).contiguous(), dh.reshape(-1, D))
+        else:
+            tg.index_add_(0, ids.reshape(-1), dh.reshape(-1, D).float())
         engine.reduce_scatter(engine.embed, engine.table_grad)
         return None, None, None
 

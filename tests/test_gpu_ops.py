@@ -83,3 +83,43 @@ def test_adamw_matches_reference_update():
         og.step(clip=1.0)
         oc.step(clip=1.0)
     assert _rel(og.master[0].cpu(), p_cpu.detach()) < 1e-5
+
+
+def test_gdn_gates_fwd_bwd_against_reference():
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(0)
+    B, T, H = 2, 64, 12
+    proj = torch.randn(B, T, 40 + 2 * H, device="cuda").bfloat16()
+    a, b = proj[..., 40:40 + H], proj[..., 40 + H:]
+    A_log = torch.randn(H, device="cuda") * 0.5
+    dt = torch.randn(H, device="cuda") * 0.5
+    ar, br = a.float().clone().requires_grad_(True), b.float().clone().requires_grad_(True)
+    Ar, dr = A_log.clone().requires_grad_(True), dt.clone().requires_grad_(True)
+    g_ref, beta_ref = ref.gdn_gates(ar, br, Ar, dr)
+    An, dn = A_log.clone().requires_grad_(True), dt.clone().requires_grad_(True)
+    an, bn = a.clone().requires_grad_(True), b.clone().requires_grad_(True)
+    g, beta = Cu.gdn_gates(an, bn, An, dn)
+    assert torch.allclose(g, g_ref, rtol=1e-4, atol=1e-5) and torch.allclose(beta, beta_ref, rtol=1e-4, atol=1e-5)
+    wg, wb = torch.randn_like(g), torch.randn_like(beta)
+    ((g_ref * wg).sum() + (beta_ref * wb).sum()).backward()
+    ((g * wg).sum() + (beta * wb).sum()).backward()
+    assert torch.allclose(an.grad.float(), ar.grad, rtol=2e-2, atol=2e-2)
+    assert torch.allclose(bn.grad.float(), br.grad, rtol=2e-2, atol=2e-2)
+    assert torch.allclose(An.grad, Ar.grad, rtol=1e-3, atol=1e-3)
+    assert torch.allclose(dn.grad, dr.grad, rtol=1e-3, atol=1e-3)
+
+
+def test_embedding_fwd_bwd_against_torch():
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(0)
+    table = torch.randn(300, 64, device="cuda").bfloat16().requires_grad_(True)
+    ids = torch.randint(0, 300, (3, 50), device="cuda")
+    ids[0, :5] = 7  # repeated rows accumulate
+    h = Cu.embedding(ids, table)
+    assert torch.equal(h, torch.nn.functional.embedding(ids, table.detach()))
+    dh = torch.randn_like(h)
+    h.backward(dh)
+    want = torch.zeros(300, 64, device="cuda").index_add_(0, ids.reshape(-1), dh.reshape(-1, 64).float())
+    assert torch.allclose(table.grad.float(), want, rtol=1e-2, atol=1e-2)

@@ -1,0 +1,215 @@
+"""Per-kernel benchmarks with roofline fractions (one op, one shape, one JSON line).
+
+    python -m dllm_qwen38_b200.bench.kernels gemm --M 8192 --N 5120 --K 5120
+    python -m dllm_qwen38_b200.bench.kernels gdn --L 8192 --block 32 [--impl reference]
+    python -m dllm_qwen38_b200.bench.kernels attn --L 4096 --block 32
+    python -m dllm_qwen38_b200.bench.kernels ce --rows 8192 --vocab 248320
+    python -m dllm_qwen38_b200.bench.kernels conv|rmsnorm|adamw ...
+
+Timing: CUDA events on the launching stream around each iteration, after warm-up, with a write of
+a buffer larger than L2 (256 MiB) before every timed iteration; the median is reported.
+Denominators are the measured copy bandwidth and cuBLAS bf16 rate in MEASURED_PEAKS.json at the
+repository root (fallback 6.65 TB/s and 1.59 PFLOP/s when absent). The GDN op is the state-fork
+sweep of the inference/training shapes (48 v heads / 16 qk heads, dk = dv = 128, rows =
+batch x (blocks + 1)); `--impl reference` runs the reference's own chunked torch function
+(`gdn.py:48-123`) the way its block-diffusion forward uses it (`blockdiff.py:159-177`).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]) * 1e9, float(p["bf16_tflops"]) * 1e12, "measured"
+    except Exception:  # noqa: BLE001
+        return 6.65e12, 1.59e15, "fallback"
+
+
+def timeit(fn, iters: int, warmup: int) -> float:
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for i in range(iters):
+        flush.fill_(i & 0xFF)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1))
+    return statistics.median(ts)
+
+
+def op_gemm(a):
+    from ..ops import cuda as Cu
+
+    x = torch.randn(a.M, a.K, device="cuda").bfloat16()
+    w = torch.randn(a.N, a.K, device="cuda").bfloat16()
+    fn = (lambda: torch.matmul(x, w.t())) if a.impl == "cublas" else (lambda: Cu.gemm_nt(x, w))
+    return fn, 2.0 * a.M * a.N * a.K, 2.0 * (a.M * a.K + a.N * a.K + a.M * a.N)
+
+
+def _gdn_inputs(a):
+    B, L, Hk, Hv, D = a.B, a.L, 16, 48, 128
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, 2 * L, Hv, D, device="cuda", generator=g).bfloat16()
+    beta = torch.sigmoid(torch.randn(B, 2 * L, Hv, device="cuda", generator=g))
+    lg = -torch.nn.functional.softplus(torch.randn(B, 2 * L, Hv, device="cuda", generator=g))
+    return q, k, v, lg, beta
+
+
+def op_gdn(a):
+    """forward + backward of the state-fork delta rule over [x_t || x_0] of length 2L."""
+    q, k, v, lg, beta = _gdn_inputs(a)
+    B, L, Hv, D = a.B, a.L, 48, 128
+    nb = L // a.block
+    if a.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from dllm_qwen38.gdn import chunk_gated_delta_rule_with_states as rf
+
+        def fn():
+            qq, kk, vv, gg, bb = (t.detach().requires_grad_(True) for t in (q, k, v, lg, beta))
+            rep = Hv // qq.shape[2]
+            qr, kr = qq.repeat_interleave(rep, 2), kk.repeat_interleave(rep, 2)
+            sl = slice(L, 2 * L)
+            o0, st = rf(qr[:, sl], kr[:, sl], vv[:, sl], gg[:, sl], bb[:, sl], a.block)
+            init = torch.cat([torch.zeros_like(st[:, :1]), st[:, :-1]], 1).reshape(B * nb, Hv, D, D)
+            rs = lambda x: x[:, :L].reshape(B * nb, a.block, *x.shape[2:])  # noqa: E731
+            ot, _ = rf(rs(qr), rs(kr), rs(vv), rs(gg), rs(bb), a.block, initial_state=init, need_states=False)
+            (o0.float().sum() + ot.float().sum()).backward()
+    else:
+        from ..ops import cuda as Cu
+
+        def fn():
+            qq, kk, vv, gg, bb = (t.detach().requires_grad_(True) for t in (q, k, v, lg, beta))
+            o = Cu.gdn_core_blockdiff(qq, kk, vv, gg, bb, L, a.block, 64, "fork")
+            o.float().sum().backward()
+    # model FLOPs of the chunked algebra per (chunk, head): forward 6 C D^2 (W S, q S, K~^T V') +
+    # 10 C^2 D (k k^T, q k^T, T X, T Y, P V'); backward about twice that
+    C = a.block
+    chunks = B * (2 * L // C)
+    flops = chunks * Hv * (18.0 * C * D * D + 30.0 * C * C * D)
+    byts = 2 * (q.numel() + k.numel() + 2 * v.numel()) * 2 + B * nb * Hv * D * D * 4 * 2
+    return fn, flops, byts
+
+
+def op_attn(a):
+    from ..ops import cuda as Cu
+
+    B, L, Hq, Hk, D = a.B, a.L, 24, 4, 256
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, 2 * L, Hq, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+
+    def fn():
+        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+        o = Cu.attention_blockdiff(qq, kk, vv, L, a.block, D ** -0.5)
+        o.float().sum().backward()
+    # allowed pairs of the complementary mask: x_t rows see their block + earlier clean blocks
+    # (~L^2/2 + L*block), x_0 rows the clean prefix (~L^2/2): ~L^2 pairs; fwd 4 D + bwd 10 D flops/pair
+    pairs = float(L) * L + L * a.block
+    flops = B * Hq * pairs * D * 14.0
+    byts = 2 * (q.numel() * 3 + k.numel() * 3 + v.numel() * 3)
+    return fn, flops, byts
+
+
+def op_ce(a):
+    from ..ops import cuda as Cu
+
+    h = torch.randn(a.rows, a.D, device="cuda").bfloat16()
+    w = (torch.randn(a.vocab, a.D, device="cuda") * 0.02).bfloat16()
+    t = torch.randint(0, a.vocab, (a.rows,), device="cuda")
+
+    def fn():
+        hh, ww = h.detach().requires_grad_(True), w.detach().requires_grad_(True)
+        Cu.masked_ce_sum(hh, ww, t).backward()
+    return fn, 6.0 * a.rows * a.vocab * a.D, 2.0 * (a.rows * a.vocab * 2 + a.vocab * a.D * 2)
+
+
+def op_conv(a):
+    from ..ops import cuda as Cu
+
+    C = 10240
+    raw = torch.randn(a.B, 2 * a.L, C, device="cuda").bfloat16()
+    w = torch.randn(C, 4, device="cuda") * 0.3
+
+    def fn():
+        rr, ww = raw.detach().requires_grad_(True), w.detach().requires_grad_(True)
+        Cu.conv_blockdiff(rr, ww, a.L, a.block, "fork").float().sum().backward()
+    n = raw.numel()
+    return fn, 16.0 * n, 2.0 * n * 5
+
+
+def op_rmsnorm(a):
+    from ..ops import cuda as Cu
+
+    x = torch.randn(a.rows, a.D, device="cuda").bfloat16()
+    w = torch.zeros(a.D, device="cuda").bfloat16()
+    return (lambda: Cu.rmsnorm(x, w, 1e-6)), 4.0 * x.numel(), 4.0 * x.numel()
+
+
+def op_adamw(a):
+    from ..ops import cuda as Cu
+
+    n = a.n
+    w = torch.randn(n, device="cuda")
+    p = w.bfloat16()
+    gr = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    return (lambda: Cu.adamw_flat(w, p, gr, m, v, 1e-5, 0.9, 0.95, 1e-8, 0.0, 1.0, 0.1, 0.05)), 12.0 * n, 30.0 * n
+
+
+OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm,
+       "adamw": op_adamw}
+
+
+def main(argv=None) -> int:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("op", choices=sorted(OPS))
+    p.add_argument("--impl", default="native", choices=["native", "reference", "cublas"])
+    p.add_argument("--M", type=int, default=8192)
+    p.add_argument("--N", type=int, default=5120)
+    p.add_argument("--K", type=int, default=5120)
+    p.add_argument("--B", type=int, default=1)
+    p.add_argument("--L", type=int, default=4096)
+    p.add_argument("--block", type=int, default=32)
+    p.add_argument("--rows", type=int, default=8192)
+    p.add_argument("--D", type=int, default=5120)
+    p.add_argument("--vocab", type=int, default=248320)
+    p.add_argument("--n", type=int, default=400_000_000)
+    p.add_argument("--iters", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    a = p.parse_args(argv)
+    sys.path.insert(0, ROOT)
+    fn, flops, byts = OPS[a.op](a)
+    ms = timeit(fn, a.iters, a.warmup)
+    bw, tf, src = peaks()
+    s = ms / 1e3
+    out = {"op": a.op, "impl": a.impl, "ms": round(ms, 4), "tflops": round(flops / s / 1e12, 2),
+           "gbs": round(byts / s / 1e9, 1), "frac_bf16_peak": round(flops / s / tf, 3),
+           "frac_hbm_peak": round(byts / s / bw, 3), "peaks": src,
+           "shape": {k: getattr(a, k) for k in ("M", "N", "K", "B", "L", "block", "rows", "D", "vocab", "n")}}
+    print(json.dumps(out))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

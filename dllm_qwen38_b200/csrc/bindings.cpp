@@ -57,6 +57,8 @@ std::vector<at::Tensor> gdn_gates_fwd(const at::Tensor& a, const at::Tensor& b, 
                                       const at::Tensor& dt_bias);
 std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& dbeta, const at::Tensor& a,
                                       const at::Tensor& b, const at::Tensor& A_log, const at::Tensor& dt_bias);
+void gemm_splitk(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, at::Tensor& ws, int64_t S,
+                 const c10::optional<at::Tensor>& residual);
 namespace peer {
 int64_t alloc(int64_t bytes);
 at::Tensor handle(int64_t ptr);
@@ -116,6 +118,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd_", &bdllm::embed_bwd_, "embedding gradient scatter-add into an fp32 table");
   m.def("gdn_gates_fwd", &bdllm::gdn_gates_fwd, "beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)");
   m.def("gdn_gates_bwd", &bdllm::gdn_gates_bwd);
+  m.def("gemm_splitk", &bdllm::gemm_splitk, "split-K tcgen05 GEMM for skinny problems (+ residual)",
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("ws"), py::arg("S"), py::arg("residual") = c10::nullopt);
   m.def("peer_alloc", &bdllm::peer::alloc, "symmetric heap: zeroed device region");
   m.def("peer_handle", &bdllm::peer::handle, "CUDA IPC handle of a heap (64-byte CPU tensor)");
   m.def("peer_open", &bdllm::peer::open, "map a peer's heap from its IPC handle");

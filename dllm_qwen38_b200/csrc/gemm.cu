@@ -60,6 +60,10 @@ struct GemmArgs {
   unsigned* ctr;          // this rank's TP counters
   int wait_ag;            // the producer waits until every rank pushed the gathered A rows
   uint64_t timeout_ns;
+  // split-K (EPI_F32 only): work item = (tile, split); split s covers k-blocks [s*kbs, (s+1)*kbs)
+  // and writes its fp32 partial at C + s * split_stride
+  int ksplit, kbs;
+  int64_t split_stride;
 };
 
 __device__ __forceinline__ void tp_st_release(unsigned* p, unsigned v) {
@@ -117,8 +121,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int tiles_m = (args.M + BM - 1) / BM;
   const int tiles_n = (args.N + C_::BN_OUT - 1) / C_::BN_OUT;
-  const int num_tiles = tiles_m * tiles_n;
-  const int kblocks = (args.K + BK - 1) / BK;
+  const int mn_tiles = tiles_m * tiles_n;
+  const int ksplit = args.ksplit > 1 ? args.ksplit : 1;
+  const int num_tiles = mn_tiles * ksplit;
+  const int kblocks_all = (args.K + BK - 1) / BK;
+  const int kbs = ksplit > 1 ? args.kbs : kblocks_all;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -169,9 +176,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      tile_coords(t % mn_tiles, tiles_m, tiles_n, tm, tn);
       const int m0 = tm * BM, n0 = tn * C_::BN_OUT;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      const int kb0 = (t / mn_tiles) * kbs, kb1 = min(kblocks_all, kb0 + kbs);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
           break;
@@ -224,7 +232,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      const int kb0 = (t / mn_tiles) * kbs, kb1 = min(kblocks_all, kb0 + kbs);
+      for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], round & 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
           break;
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bd = smem_desc(b_addr + k * 32, 16, 1024);
           else
             bd = smem_desc(b_addr + k * 2048, 8192, 1024);
-          mma_bf16(d_tmem, ad, bd, C_::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_bf16(d_tmem, ad, bd, C_::IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&empty[stage]);  // frees this smem stage once these MMAs have read it
         if (++stage == STAGES) {
@@ -270,7 +279,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      tile_coords(t % mn_tiles, tiles_m, tiles_n, tm, tn);
+      const int64_t split_off = (int64_t)(t / mn_tiles) * args.split_stride;
       const int row = tm * BM + row_in_tile;
       const int n0 = tn * C_::BN_OUT;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
@@ -345,7 +355,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
           if (row_ok) {
-            float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + col0;
+            float* out = reinterpret_cast<float*>(args.C) + split_off + (size_t)row * args.ldc + col0;
             if (col0 + 32 <= args.N) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
@@ -532,6 +542,30 @@ static void launch(GemmLaunch* L, cudaStream_t st) {
 
 // C = A B^T-style contraction with operand majors; see the file header for the conventions.
 // a: K-major -> [M, K] (lda); MN-major -> [K, M] (lda). b: K-major -> [N, K]; MN-major -> [K, N].
+// out (bf16) = sum_s ws[s] (+ residual), ws [S, M, N] fp32 contiguous
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int S, int64_t M, int N,
+                                     __nv_bfloat16* __restrict__ out, int64_t ldo,
+                                     const __nv_bfloat16* __restrict__ res, int64_t ldr) {
+  const int64_t nv = M * (N / 4);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / (N / 4);
+    const int n = (int)(i - m * (N / 4)) * 4;
+    float4 a = *reinterpret_cast<const float4*>(ws + m * N + n);
+    for (int s2 = 1; s2 < S; ++s2) {
+      const float4 b = *reinterpret_cast<const float4*>(ws + (int64_t)s2 * M * N + m * N + n);
+      a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+    }
+    if (res != nullptr) {
+      const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(res + m * ldr + n);
+      const float2 r0 = __bfloat1622float2(r2[0]), r1 = __bfloat1622float2(r2[1]);
+      a.x += r0.x, a.y += r0.y, a.z += r1.x, a.w += r1.y;
+    }
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(out + m * ldo + n);
+    o2[0] = __floats2bfloat162_rn(a.x, a.y);
+    o2[1] = __floats2bfloat162_rn(a.z, a.w);
+  }
+}
+
 struct TpHook {
   const std::vector<int64_t>* peers;
   int rank, rows_per_rank, wait_ag;
@@ -550,6 +584,59 @@ void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool
           int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha) {
   TORCH_CHECK(epi != EPI_PEER_F32, "gemm: the peer epilogue goes through gemm_tp");
   gemm_impl(a, a_mn, lda, b, b_mn, ldb, M, N, K, c, ldc, epi, r, ldr, gu, bn, alpha, nullptr);
+}
+
+// Split-K GEMM for skinny problems (few output tiles): out[M, N] (bf16) = a b^T (+ residual), both
+// K-major. `ws` is an fp32 workspace of >= S * M * N elements.
+void gemm_splitk(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, at::Tensor& ws, int64_t S,
+                 const c10::optional<at::Tensor>& residual) {
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_splitk: K-major 2-D");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(N % 4 == 0 && ws.is_contiguous() && ws.scalar_type() == at::kFloat && ws.numel() >= S * M * N,
+              "gemm_splitk: N % 4 == 0 and an fp32 workspace of S*M*N");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.stride(0) % 8 == 0, "gemm_splitk: out");
+  const int64_t kblocks = (K + BK - 1) / BK;
+  const int64_t kbs = (kblocks + S - 1) / S;
+  const int64_t splits = (kblocks + kbs - 1) / kbs;  // every split gets >= 1 k-block
+  at::Tensor w2 = ws.view({-1}).narrow(0, 0, splits * M * N).view({splits * M, N});
+  {
+    // reuse the plain path with the split fields set (EPI_F32, 256-wide tiles)
+    c10::cuda::CUDAGuard guard(a.device());
+    bind_context(a.get_device());
+    cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    GemmLaunch* L = &tls_launch;
+    L->args = GemmArgs{};
+    GemmArgs& g = L->args;
+    g.M = (int)M, g.N = (int)N, g.K = (int)K, g.C = w2.data_ptr(), g.ldc = (int)N, g.err = error_word_ptr();
+    g.alpha = 1.f, g.ksplit = (int)splits, g.kbs = (int)kbs, g.split_stride = M * N;
+    make_map_bf16(&L->ma, a.data_ptr(), K, M, a.stride(0), 64, 128);
+    make_map_bf16(&L->mb, b.data_ptr(), K, N, b.stride(0), 64, 256);
+    using C_ = Cfg<256, false, false, EPI_F32>;
+    auto kern = gemm_kernel<256, false, false, EPI_F32>;
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM));
+      attr = true;
+    }
+    const int tiles = (int)(((M + BM - 1) / BM) * ((N + 255) / 256) * splits);
+    const int grid = std::max(1, std::min(tiles, num_sms()));
+    void* kargs[3] = {&L->ma, &L->mb, &L->args};
+    C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(NUM_THREADS), kargs,
+                                    C_::SMEM, st));
+    const __nv_bfloat16* res = nullptr;
+    int64_t ldr = 0;
+    if (residual.has_value()) {
+      TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1, "gemm_splitk: residual");
+      res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+      ldr = residual->stride(0);
+    }
+    const int64_t nv = M * (N / 4);
+    const int rgrid = (int)std::min<int64_t>((nv + 255) / 256, 148 * 8);
+    splitk_reduce_kernel<<<rgrid, 256, 0, st>>>(w2.data_ptr<float>(), (int)splits, M, (int)N,
+                                                reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), res,
+                                                ldr);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
 }
 
 // Tensor-parallel GEMM: y = a b^T (K-major operands) with the collective hooks. epi EPI_PEER_F32:

@@ -51,13 +51,36 @@ def _nat():
     return importlib.import_module(__name__ + "._native")
 
 
+_LEVERS: set = set()
+
+
+class torch_on_cuda:
+    """Context manager: run the named ops through their torch path on the device (recorded as
+    'torch-cuda'). Used by the lever benchmark to measure what each native kernel buys; nothing
+    on a production path enters it."""
+
+    def __init__(self, *ops: str):
+        self.ops = set(ops)
+        self.prev: set = set()
+
+    def __enter__(self):
+        self.prev = set(_LEVERS)
+        _LEVERS.update(self.ops)
+        return self
+
+    def __exit__(self, *exc):
+        _LEVERS.clear()
+        _LEVERS.update(self.prev)
+        return False
+
+
 def use_native(*tensors: torch.Tensor, op: str | None = None) -> bool:
     """True when the op must run the CUDA kernel (any CUDA input). Raises if the extension is not
     built. An op listed in ``ops.cuda.TORCH_ON_CUDA`` has no kernel yet: it runs the reference on
     the device and is recorded as 'torch-cuda' so no report mistakes it for a native path."""
     if any(t is not None and t.is_cuda for t in tensors):
         _nat().require()
-        if op is not None and op in _nat().TORCH_ON_CUDA:
+        if op is not None and (op in _nat().TORCH_ON_CUDA or op in _LEVERS):
             _PENDING_TORCH_CUDA.add(op)
             return False
         return True

@@ -38,15 +38,36 @@ def _c2(t: torch.Tensor) -> torch.Tensor:
     return t2
 
 
+_NUM_SMS = [0]
+
+
+def _splits(M: int, N: int, K: int) -> int:
+    """k-splits for a skinny bf16 GEMM whose output tiles cannot fill the GPU (1 = no split)."""
+    if M > 256 or K < 2048 or N % 4:
+        return 1
+    if not _NUM_SMS[0]:
+        _NUM_SMS[0] = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    tiles = ((M + 127) // 128) * ((N + 255) // 256)
+    if 2 * tiles > _NUM_SMS[0]:
+        return 1
+    return max(1, min((K + 63) // 64 // 4, _NUM_SMS[0] // tiles))  # one wave of (tile, split) items
+
+
 def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
             residual: torch.Tensor | None = None, accumulate: bool = False) -> torch.Tensor:
     """out[M, N] = a[M, K] @ b[N, K]^T (both K-major). residual: out = a b^T + residual (bf16).
-    accumulate: fp32 out += a b^T."""
+    accumulate: fp32 out += a b^T. Skinny bf16 problems (decode) run split-K."""
     a2, b2 = _c2(a), _c2(b)
     M, K = a2.shape
     N = b2.shape[0]
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    S = _splits(M, N, K) if (out.dtype == torch.bfloat16 and not accumulate) else 1
+    if S > 1:
+        ws = torch.empty(S * M * N, device=a.device, dtype=torch.float32)
+        _C.gemm_splitk(a2, b2, out, ws, S, _c2(residual) if residual is not None else None)
+        _count(2)
+        return out
     if accumulate:
         epi = EPI_ACC_F32
     elif residual is not None:

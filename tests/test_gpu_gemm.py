@@ -89,3 +89,19 @@ def test_linear_autograd_matches_fp32():
     assert _rel(y, xf @ wf.t()) < 1e-2
     assert _rel(x.grad, xf.grad) < 1e-2
     assert _rel(w.grad, wf.grad) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 5120, 8192), (64, 1024, 4096), (16, 2048, 17408)])
+def test_splitk_skinny_gemm(M, N, K):
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(0)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    r = torch.randn(M, N, device="cuda").bfloat16()
+    assert Cu._splits(M, N, K) > 1
+    want = a.float() @ b.float().t()
+    got = Cu.gemm_nt(a, b)
+    assert float((got.float() - want).abs().max()) < 2e-2 * float(want.abs().max())
+    got_r = Cu.gemm_nt(a, b, residual=r)
+    assert float((got_r.float() - (want + r.float())).abs().max()) < 2e-2 * float(want.abs().max())

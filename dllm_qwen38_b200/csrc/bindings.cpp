@@ -42,12 +42,15 @@ at::Tensor conv_tail(const at::Tensor& raw, at::Tensor& tail, const at::Tensor& 
 void confidence(const at::Tensor& logits, at::Tensor& conf, at::Tensor& pick);
 void commit(const at::Tensor& conf, const at::Tensor& pick, at::Tensor& masked, at::Tensor& ids, double threshold,
             int64_t sub_block, at::Tensor& forwards, at::Tensor& remaining);
-void gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
-             const std::vector<int64_t>& peers, int64_t rank, int64_t rows_per_rank, int64_t part_off,
-             int64_t flag_off, const at::Tensor& ctr, bool wait_ag, double timeout_s, int64_t bn);
+int64_t gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t epi,
+                const c10::optional<at::Tensor>& gu, const std::vector<int64_t>& peers, int64_t rank,
+                int64_t rows_per_rank, int64_t part_off, int64_t flag_off, const at::Tensor& ctr, bool wait_ag,
+                double timeout_s, int64_t bn, int64_t ksplit);
+void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::optional<at::Tensor>& residual,
+                   bool swiglu);
 void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_t R, int64_t D, int64_t part_off,
                          at::Tensor& h, bool has_partials, const at::Tensor& w1, double eps, int64_t gather_off,
-                         int64_t flag_off, at::Tensor& ctr, double timeout_s, bool do_push);
+                         int64_t flag_off, at::Tensor& ctr, double timeout_s, bool do_push, int64_t nslots);
 void tp_confidence(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& logits, int64_t v0,
                    int64_t conf_off, int64_t flag_off, at::Tensor& ctr, at::Tensor& conf, at::Tensor& pick,
                    double timeout_s);
@@ -110,7 +113,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "tensor-parallel tcgen05 GEMM: fused all-gather wait in the producer, peer-store partial epilogue",
         py::arg("a"), py::arg("b"), py::arg("c"), py::arg("epi"), py::arg("gu"), py::arg("peers"), py::arg("rank"),
         py::arg("rows_per_rank"), py::arg("part_off"), py::arg("flag_off"), py::arg("ctr"), py::arg("wait_ag"),
-        py::arg("timeout_s"), py::arg("bn") = 256);
+        py::arg("timeout_s"), py::arg("bn") = 256, py::arg("ksplit") = 1);
+  m.def("splitk_reduce", &bdllm::splitk_reduce, "sum of k-split partials (+ residual, or SwiGLU of gate|up)",
+        py::arg("ws"), py::arg("S"), py::arg("out"), py::arg("residual") = c10::nullopt, py::arg("swiglu") = false);
   m.def("tp_reduce_norm_push", &bdllm::tp_reduce_norm_push,
         "owner rows: sum peers' partials + residual, RMSNorm, push to every rank's gathered buffer");
   m.def("tp_confidence", &bdllm::tp_confidence, "vocab-parallel confidence: per-slice push + rank-order merge");

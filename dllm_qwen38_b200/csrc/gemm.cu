@@ -341,8 +341,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         } else if constexpr (EPI == EPI_PEER_F32) {
           if (row_ok) {
             const int owner = row / args.rows_per_rank, lr = row - owner * args.rows_per_rank;
+            const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
             float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
-                         ((int64_t)args.rank * args.rows_per_rank + lr) * args.ldc + col0;
+                         (slot * args.rows_per_rank + lr) * args.ldc + col0;
             if (col0 + 32 <= args.N) {
 #pragma unroll
               for (int j = 0; j < 32; j += 4)
@@ -572,7 +573,17 @@ struct TpHook {
   int64_t part_off, flag_off;
   unsigned* ctr;
   double timeout_s;
+  int ksplit, kbs;
+  int64_t split_stride;
 };
+
+// k-split that gives every split >= 1 k-block: returns {splits, k-blocks per split}
+static std::pair<int, int> split_plan(int64_t K, int64_t S) {
+  const int64_t kblocks = (K + BK - 1) / BK;
+  S = std::max<int64_t>(1, std::min<int64_t>(S, kblocks));
+  const int64_t kbs = (kblocks + S - 1) / S;
+  return {(int)((kblocks + kbs - 1) / kbs), (int)kbs};
+}
 
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
                       int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
@@ -643,9 +654,13 @@ void gemm_splitk(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, at::
 // output rows go to their owner's fp32 partial slot in peer memory (c is only the shape/stride
 // template, [M, N] fp32); other epilogues write c locally. wait_ag: wait for every rank's pushed
 // A rows first (the gathered A lives in this rank's heap).
-void gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
-             const std::vector<int64_t>& peers, int64_t rank, int64_t rows_per_rank, int64_t part_off,
-             int64_t flag_off, const at::Tensor& ctr, bool wait_ag, double timeout_s, int64_t bn) {
+// ksplit > 1 (skinny problems): EPI_F32 writes split s at c + s * M * N (c is [S * M, N] fp32);
+// EPI_PEER_F32 writes split s of source rank r into the owner's slot r * S + s. Returns the number of
+// splits used (the consumer sums that many slots).
+int64_t gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t epi,
+                const c10::optional<at::Tensor>& gu, const std::vector<int64_t>& peers, int64_t rank,
+                int64_t rows_per_rank, int64_t part_off, int64_t flag_off, const at::Tensor& ctr, bool wait_ag,
+                double timeout_s, int64_t bn, int64_t ksplit) {
   TORCH_CHECK(peers.size() >= 1 && peers.size() <= (size_t)TP_MAX, "gemm_tp: 1..8 ranks");
   TORCH_CHECK(ctr.is_cuda() && ctr.scalar_type() == at::kInt && ctr.numel() >= 4, "gemm_tp: int32 counters [>= 4]");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1, "gemm_tp: 2-D K-major operands");
@@ -655,9 +670,65 @@ void gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t ep
                     c.scalar_type() == at::kFloat && c.size(1) == N && (c.stride(0) * 4) % 16 == 0,
                 "gemm_tp: peer epilogue needs M = world * rows_per_rank and an fp32 [M, N] template");
   TpHook h{&peers, (int)rank, (int)rows_per_rank, wait_ag ? 1 : 0, part_off, flag_off,
-           reinterpret_cast<unsigned*>(ctr.data_ptr<int>()), timeout_s};
+           reinterpret_cast<unsigned*>(ctr.data_ptr<int>()), timeout_s, 1, 0, 0};
+  if (ksplit > 1) {
+    TORCH_CHECK(epi == EPI_F32 || epi == EPI_PEER_F32, "gemm_tp: k-split with the fp32 or peer epilogue only");
+    auto [S, kbs] = split_plan(K, ksplit);
+    h.ksplit = S, h.kbs = kbs, h.split_stride = (epi == EPI_F32) ? M * N : 0;
+    if (epi == EPI_F32)
+      TORCH_CHECK(c.is_contiguous() && c.numel() >= (int64_t)S * M * N, "gemm_tp: fp32 workspace [S*M, N]");
+  }
   gemm_impl(a, false, a.stride(0), b, false, b.stride(0), M, N, K, c, c.stride(0), epi, c10::nullopt, 0, gu, bn, 1.0,
             &h);
+  return h.ksplit;
+}
+
+// Reductions of k-split partials: out (bf16) = sum_s ws[s] (+ residual); or, for the gate|up GEMM,
+// act = silu(sum_s gate) * (sum_s up) with ws [S, M, 2F].
+__global__ void splitk_swiglu_kernel(const float* __restrict__ ws, int S, int64_t M, int F,
+                                     __nv_bfloat16* __restrict__ act) {
+  const int64_t n = M * F;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / F;
+    const int j = (int)(i - m * F);
+    float g = 0.f, u = 0.f;
+    for (int s2 = 0; s2 < S; ++s2) {
+      const float* row = ws + ((int64_t)s2 * M + m) * 2 * F;
+      g += row[j];
+      u += row[F + j];
+    }
+    // same rounding as the SwiGLU epilogue: bf16 gate and up first
+    g = __bfloat162float(__float2bfloat16(g));
+    u = __bfloat162float(__float2bfloat16(u));
+    act[i] = __float2bfloat16(silu_f(g) * u);
+  }
+}
+
+void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::optional<at::Tensor>& residual,
+                   bool swiglu) {
+  TORCH_CHECK(ws.is_contiguous() && ws.scalar_type() == at::kFloat, "splitk_reduce: fp32 workspace");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1, "splitk_reduce: bf16 out");
+  const int64_t M = out.size(0), N = out.size(1);
+  c10::cuda::CUDAGuard g(ws.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (swiglu) {
+    TORCH_CHECK(out.is_contiguous() && ws.numel() >= S * M * 2 * N, "splitk_reduce: swiglu shapes");
+    const int grid = (int)std::min<int64_t>((M * N + 255) / 256, 148 * 8);
+    splitk_swiglu_kernel<<<grid, 256, 0, st>>>(ws.data_ptr<float>(), (int)S, M, (int)N,
+                                               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  } else {
+    TORCH_CHECK(N % 4 == 0 && ws.numel() >= S * M * N && out.stride(0) % 4 == 0, "splitk_reduce: shapes");
+    const __nv_bfloat16* res = nullptr;
+    int64_t ldr = 0;
+    if (residual.has_value()) {
+      res = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+      ldr = residual->stride(0);
+    }
+    const int grid = (int)std::min<int64_t>((M * (N / 4) + 255) / 256, 148 * 8);
+    splitk_reduce_kernel<<<grid, 256, 0, st>>>(ws.data_ptr<float>(), (int)S, M, (int)N,
+                                               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), res, ldr);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
@@ -695,6 +766,9 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
     args.ctr = tp->ctr;
     args.wait_ag = tp->wait_ag;
     args.timeout_ns = (uint64_t)(tp->timeout_s * 1e9);
+    args.ksplit = tp->ksplit;
+    args.kbs = tp->kbs;
+    args.split_stride = tp->split_stride;
   }
   const bool f32_out = (epi == EPI_F32 || epi == EPI_ACC_F32 || epi == EPI_PEER_F32);
   TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype does not match the epilogue");

@@ -81,7 +81,7 @@ __device__ bool last_block(unsigned* arrive) {
 __global__ void __launch_bounds__(256) reduce_norm_push_kernel(
     Peers P, int world, int rank, int R, int D, int64_t part_off, __nv_bfloat16* __restrict__ h, int has_partials,
     const float* __restrict__ w1, float eps, int64_t gather_off, int64_t flag_off, unsigned* ctr, int* err,
-    uint64_t tmo, int do_push) {
+    uint64_t tmo, int do_push, int nslots) {
   __shared__ int ok;
   __shared__ float red[8];
   const int row = blockIdx.x;
@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(256) reduce_norm_push_kernel(
       }
       if (has_partials) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int p = 0; p < world; ++p) {
+        for (int p = 0; p < nslots; ++p) {  // [source rank][k split], summed in that order
           const float* src = reinterpret_cast<const float*>(P.p[rank] + part_off) + ((int64_t)p * R + row) * D + v * 8;
           const float4 a = __ldcg(reinterpret_cast<const float4*>(src));
           const float4 b = __ldcg(reinterpret_cast<const float4*>(src + 4));
@@ -247,7 +247,7 @@ static Peers to_peers(const std::vector<int64_t>& v) {
 
 void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_t R, int64_t D, int64_t part_off,
                          at::Tensor& h, bool has_partials, const at::Tensor& w1, double eps, int64_t gather_off,
-                         int64_t flag_off, at::Tensor& ctr, double timeout_s, bool do_push) {
+                         int64_t flag_off, at::Tensor& ctr, double timeout_s, bool do_push, int64_t nslots) {
   TORCH_CHECK(h.is_contiguous() && h.scalar_type() == at::kBFloat16 && h.numel() == R * D, "tp: h [R, D] bf16");
   TORCH_CHECK(w1.is_contiguous() && w1.scalar_type() == at::kFloat && w1.numel() == D, "tp: w1 fp32 [D]");
   TORCH_CHECK(D % 8 == 0 && D <= 8 * 256 * 4, "tp: D % 8 == 0 and D <= 8192");
@@ -257,7 +257,7 @@ void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_
       tp::to_peers(peers), (int)peers.size(), (int)rank, (int)R, (int)D, part_off,
       reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), has_partials ? 1 : 0, w1.data_ptr<float>(), (float)eps,
       gather_off, flag_off, reinterpret_cast<unsigned*>(ctr.data_ptr<int>()), error_word_ptr(),
-      (uint64_t)(timeout_s * 1e9), do_push ? 1 : 0);
+      (uint64_t)(timeout_s * 1e9), do_push ? 1 : 0, (int)(nslots > 0 ? nslots : (int64_t)peers.size()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

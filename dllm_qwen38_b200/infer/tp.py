@@ -35,7 +35,7 @@ from ..ops import _native
 from ..ops import reference as ref
 from .golden import DecodeTrace
 
-EPI_BF16, EPI_SWIGLU, EPI_PEER_F32 = 0, 4, 5
+EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_PEER_F32 = 0, 1, 4, 5
 
 
 class TPDecodeEngine:
@@ -129,18 +129,21 @@ class TPDecodeEngine:
         self.cos_t, self.sin_t = ref.rope_cos_sin(torch.arange(self.max_len), cfg.rotary_dim, cfg.rope_theta,
                                                   self.dt, dev)
         # ---------------------------------------------------------------- peer heap
-        part_bytes = W * self.R * D * 4
+        self.SMAX = 8
+        self.n_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self._nslots = W
+        part_bytes = W * self.SMAX * self.R * D * 4
         gather_bytes = M * D * 2
         conf_bytes = W * M * 16
         if W > 1:
             self.heap = SymmetricHeap(part_bytes + gather_bytes + conf_bytes + 3 * 256, dev)
-            self.part, self.part_off = self.heap.alloc(W * self.R * D, torch.float32)
+            self.part, self.part_off = self.heap.alloc(W * self.SMAX * self.R * D, torch.float32)
             self.gather, self.gather_off = self.heap.alloc(M * D, self.dt)
             _, self.conf_off = self.heap.alloc(W * M * 4, torch.float32)
             self.peers = self.heap.ptrs
         else:
             self.heap = None
-        self.part2d = self.part.view(M, D) if W > 1 else None
+        self.part2d = self.part[: M * D].view(M, D) if W > 1 else None  # shape/stride template of the slots
         self.gather2d = self.gather.view(M, D) if W > 1 else None
         self.ctr = torch.zeros(16, dtype=torch.int32, device=dev)
         # ---------------------------------------------------------------- step buffers
@@ -160,27 +163,45 @@ class TPDecodeEngine:
             dist.barrier()
 
     # ------------------------------------------------------------------ collectives
-    def _col(self, w, epi=EPI_BF16, n_out=None):
-        """Column-parallel GEMM over the gathered rows (waits for every rank's push)."""
+    def _splits(self, N: int, K: int) -> int:
+        """k-splits so that a skinny GEMM (few output tiles) still runs one wave over the SMs."""
+        if self.M > 256 or N % 8 or K < 1024:
+            return 1
+        tiles = ((self.M + 127) // 128) * ((N + 255) // 256)
+        return max(1, min(self.SMAX, self.n_sms // tiles, K // 64 // 2))
+
+    def _col(self, w, epi=EPI_BF16):
+        """Column-parallel GEMM over the gathered rows (waits for every rank's push inside the GEMM)."""
         C = self.C
         N = w.shape[0] // 2 if epi == EPI_SWIGLU else w.shape[0]
-        out = torch.empty(self.M, N, dtype=self.dt, device=self.dev)
         if self.world == 1:
             if epi == EPI_SWIGLU:
                 return self.Cu.gemm_swiglu(self._a1, w, N, store_gu=False)[0]
             return self.Cu.gemm_nt(self._a1, w)
+        S = self._splits(w.shape[0], w.shape[1])
+        if S > 1:  # fp32 k-split partials, then one reduction (SwiGLU applied there)
+            ws = torch.empty(S * self.M * w.shape[0], dtype=torch.float32, device=self.dev)
+            S = C.gemm_tp(self.gather2d, w, ws.view(-1, w.shape[0]), EPI_F32, None, self.peers, self.rank, self.R,
+                          self.part_off, 0, self.ctr, True, self.timeout, 256, S)
+            out = torch.empty(self.M, N, dtype=self.dt, device=self.dev)
+            C.splitk_reduce(ws, S, out, None, epi == EPI_SWIGLU)
+            self.Cu._count(2)
+            return out
+        pad = -(-N // 8) * 8  # 16-byte output rows
+        out = torch.empty(self.M, pad, dtype=self.dt, device=self.dev)[:, :N]
         C.gemm_tp(self.gather2d, w, out, epi, None, self.peers, self.rank, self.R, self.part_off, 0, self.ctr, True,
-                  self.timeout, 256)
+                  self.timeout, 256, 1)
         self.Cu._count()
         return out
 
     def _row(self, x, w):
-        """Row-parallel GEMM: partial rows straight into the owners' slots."""
+        """Row-parallel GEMM: fp32 partial rows straight into the owners' slots (per k split)."""
         if self.world == 1:
             self._partial = self.Cu.gemm_nt(x, w)
             return
-        self.C.gemm_tp(x, w, self.part2d, EPI_PEER_F32, None, self.peers, self.rank, self.R, self.part_off, 0,
-                       self.ctr, False, self.timeout, 256)
+        S = self._splits(w.shape[0], w.shape[1])
+        self._nslots = self.world * self.C.gemm_tp(x, w, self.part2d, EPI_PEER_F32, None, self.peers, self.rank,
+                                                   self.R, self.part_off, 0, self.ctr, False, self.timeout, 256, S)
         self.Cu._count()
 
     def _reduce_norm(self, w1, eps, has_partials=True, push=True):
@@ -191,7 +212,8 @@ class TPDecodeEngine:
                 self._a1 = self.C.rmsnorm_fwd(self.h, w1, eps)
             return
         self.C.tp_reduce_norm_push(self.peers, self.rank, self.R, self.cfg.hidden_size, self.part_off, self.h,
-                                   has_partials, w1, eps, self.gather_off, 0, self.ctr, self.timeout, push)
+                                   has_partials, w1, eps, self.gather_off, 0, self.ctr, self.timeout, push,
+                                   self._nslots if has_partials else 0)
         self.Cu._count()
 
     # ------------------------------------------------------------------ mixers (local heads, all M rows)

@@ -46,6 +46,10 @@ int64_t gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t
                 const c10::optional<at::Tensor>& gu, const std::vector<int64_t>& peers, int64_t rank,
                 int64_t rows_per_rank, int64_t part_off, int64_t flag_off, const at::Tensor& ctr, bool wait_ag,
                 double timeout_s, int64_t bn, int64_t ksplit);
+void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
+             const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes,
+             at::Tensor& gathered, at::Tensor& ready, at::Tensor& claim, int64_t seq, int64_t epoch, int64_t flag_off,
+             double timeout_s);
 void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::optional<at::Tensor>& residual,
                    bool swiglu);
 void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_t R, int64_t D, int64_t part_off,
@@ -72,6 +76,8 @@ at::Tensor view(int64_t ptr, int64_t numel, const at::Tensor& like);
 void signal(const std::vector<int64_t>& peers, int64_t rank, int64_t slot, int64_t value);
 void all_gather(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes, at::Tensor& out,
                 int64_t epoch, int64_t max_blocks, double timeout_s);
+void gather_range(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes, at::Tensor& out,
+                  int64_t lo, int64_t hi, int64_t epoch, double timeout_s);
 void reduce_scatter(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard, bool in_f32,
                     at::Tensor& out, double scale, const c10::optional<at::Tensor>& sq, int64_t seq,
                     int64_t max_blocks, double timeout_s);
@@ -114,6 +120,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a"), py::arg("b"), py::arg("c"), py::arg("epi"), py::arg("gu"), py::arg("peers"), py::arg("rank"),
         py::arg("rows_per_rank"), py::arg("part_off"), py::arg("flag_off"), py::arg("ctr"), py::arg("wait_ag"),
         py::arg("timeout_s"), py::arg("bn") = 256, py::arg("ksplit") = 1);
+  m.def("gemm_ag", &bdllm::gemm_ag,
+        "fused FSDP all-gather -> GEMM: copy warps pull the unit's shards from the peers while the tiles wait per chunk");
   m.def("splitk_reduce", &bdllm::splitk_reduce, "sum of k-split partials (+ residual, or SwiGLU of gate|up)",
         py::arg("ws"), py::arg("S"), py::arg("out"), py::arg("residual") = c10::nullopt, py::arg("swiglu") = false);
   m.def("tp_reduce_norm_push", &bdllm::tp_reduce_norm_push,
@@ -133,6 +141,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_view", &bdllm::peer::view, "non-owning tensor over heap memory");
   m.def("peer_signal", &bdllm::peer::signal);
   m.def("peer_all_gather", &bdllm::peer::all_gather, "all-gather of heap shards by peer loads");
+  m.def("peer_gather_range", &bdllm::peer::gather_range, "bytes [lo, hi) of a gathered buffer from the owning shards");
   m.def("peer_reduce_scatter", &bdllm::peer::reduce_scatter,
         "reduce-scatter by peer loads, fused fp32 cast, scale and sum of squares", py::arg("peers"),
         py::arg("rank"), py::arg("src_off"), py::arg("shard"), py::arg("in_f32"), py::arg("out"), py::arg("scale"),

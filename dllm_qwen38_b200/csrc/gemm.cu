@@ -39,7 +39,9 @@ constexpr int TP_MAX = 8;
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int NUM_THREADS = 192;
+// warps 0..5 as described above; warps 6..7 copy the weight shards from the peers in the fused
+// all-gather variant (idle otherwise)
+constexpr int NUM_THREADS = 256;
 
 struct GemmArgs {
   int M, N, K;       // N = output columns (for SWIGLU: F, the activation width)
@@ -64,6 +66,17 @@ struct GemmArgs {
   // and writes its fp32 partial at C + s * split_stride
   int ksplit, kbs;
   int64_t split_stride;
+  // fused FSDP all-gather (ag_nchunks > 0): the B operand lives in `ag_dst`, the gathered buffer of a
+  // unit whose rank-p shard is at peers[p] + ag_src_off (ag_shard_bytes each). Warps 6-7 of every
+  // CTA claim 16-byte-aligned chunks of ag_chunk bytes (chunk k = shard k / cps, piece k % cps) in
+  // priority order starting at ag_first, copy them from the owning peer and publish ready[k] = seq;
+  // the TMA producer waits for the chunks under each B tile before loading it.
+  int ag_nchunks, ag_first, ag_world, ag_rank;
+  int64_t ag_src_off, ag_shard_bytes, ag_chunk, ag_b_off;
+  char* ag_dst;
+  unsigned* ag_ready;
+  unsigned* ag_claim;
+  unsigned ag_seq, ag_epoch;
 };
 
 __device__ __forceinline__ void tp_st_release(unsigned* p, unsigned v) {
@@ -99,6 +112,86 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   int r = t % group_size;
   tm = first_m + r % rows;
   tn = r / rows;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// fused all-gather, copy side (one warp): wait for the peers' parameter epoch, then claim and copy
+// chunks until none is left
+__device__ void ag_copy_warp(const GemmArgs& a, int lane, volatile int* abort_flag) {
+  int ok = 1;
+  if (lane == 0) {
+    const uint64_t t0 = globaltimer();
+    for (int p = 0; p < a.ag_world && ok; ++p) {
+      const unsigned* f = reinterpret_cast<const unsigned*>(a.peers[a.ag_rank] + a.flag_off) + p;  // slot 0: epoch
+      while (static_cast<int>(tp_ld_acquire(f) - a.ag_epoch) < 0) {
+        if (globaltimer() - t0 > a.timeout_ns || *abort_flag) {
+          record_error(a.err, ERR_COMM_WAIT);
+          *abort_flag = 1;
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (!ok) return;
+  const int64_t cps = (a.ag_shard_bytes + a.ag_chunk - 1) / a.ag_chunk;
+  for (;;) {
+    unsigned c = 0;
+    if (lane == 0) c = atomicAdd(a.ag_claim, 1u);
+    c = __shfl_sync(0xffffffffu, c, 0);
+    if (c >= (unsigned)a.ag_nchunks || *abort_flag) break;
+    const int64_t k = (a.ag_first + (int64_t)c) % a.ag_nchunks;
+    const int p = (int)(k / cps);
+    const int64_t lo = (k % cps) * a.ag_chunk, n = min(a.ag_chunk, a.ag_shard_bytes - lo);
+    const char* src = reinterpret_cast<const char*>(a.peers[p] + a.ag_src_off) + lo;
+    char* dst = a.ag_dst + (int64_t)p * a.ag_shard_bytes + lo;
+    constexpr int U = 8;
+    for (int64_t o = (int64_t)lane * 16; o < n; o += 32 * 16 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (o + u * 512 < n) v[u] = __ldcg(reinterpret_cast<const uint4*>(src + o + u * 512));
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (o + u * 512 < n) *reinterpret_cast<uint4*>(dst + o + u * 512) = v[u];
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // our generic stores -> later TMA reads
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) st_release_gpu(a.ag_ready + k, a.ag_seq);
+  }
+}
+
+// fused all-gather, consumer side (TMA producer thread): wait until every chunk overlapping the
+// gathered-buffer byte range [lo, hi) is published
+__device__ bool ag_wait_range(const GemmArgs& a, int64_t lo, int64_t hi, volatile int* abort_flag) {
+  const int64_t cps = (a.ag_shard_bytes + a.ag_chunk - 1) / a.ag_chunk;
+  auto chunk_of = [&](int64_t x) { return (x / a.ag_shard_bytes) * cps + (x % a.ag_shard_bytes) / a.ag_chunk; };
+  const int64_t k0 = chunk_of(lo), k1 = chunk_of(hi - 1);
+  const uint64_t t0 = globaltimer();
+  for (int64_t k = k0; k <= k1; ++k) {
+    while (static_cast<int>(ld_acquire_gpu(a.ag_ready + k) - a.ag_seq) < 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > a.timeout_ns) {
+        record_error(a.err, ERR_COMM_WAIT);
+        *abort_flag = 1;
+        return false;
+      }
+      __nanosleep(32);
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -179,6 +272,22 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tile_coords(t % mn_tiles, tiles_m, tiles_n, tm, tn);
       const int m0 = tm * BM, n0 = tn * C_::BN_OUT;
       const int kb0 = (t / mn_tiles) * kbs, kb1 = min(kblocks_all, kb0 + kbs);
+      if constexpr (!B_MN) {
+        if (args.ag_nchunks > 0) {  // the weight rows of this tile must have landed
+          const int64_t rb = (int64_t)args.K * 2;
+          const int rows = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+          const int n_rows = args.N;
+          bool got = ag_wait_range(args, args.ag_b_off + n0 * rb, args.ag_b_off + min(n0 + rows, n_rows) * rb,
+                                   abort_flag);
+          if (got && EPI == EPI_SWIGLU)
+            got = ag_wait_range(args, args.ag_b_off + (int64_t)(n_rows + n0) * rb,
+                                args.ag_b_off + (int64_t)(n_rows + min(n0 + rows, n_rows)) * rb, abort_flag);
+          if (!got) {
+            ok = false;
+            break;
+          }
+        }
+      }
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
@@ -268,6 +377,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mma_commit(drain);
       mbar_wait(drain, 0, args.err, ERR_GEMM_WAIT, nullptr);
     }
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------------- fused all-gather copies
+    if (args.ag_nchunks > 0) ag_copy_warp(args, lane, abort_flag);
   } else if (warp >= 2) {
     // ---------------------------------------------------------------- epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
@@ -575,6 +687,17 @@ struct TpHook {
   double timeout_s;
   int ksplit, kbs;
   int64_t split_stride;
+  // fused FSDP all-gather (ag_nchunks > 0): the B operand lives in `ag_dst`, the gathered buffer of a
+  // unit whose rank-p shard is at peers[p] + ag_src_off (ag_shard_bytes each). Warps 6-7 of every
+  // CTA claim 16-byte-aligned chunks of ag_chunk bytes (chunk k = shard k / cps, piece k % cps) in
+  // priority order starting at ag_first, copy them from the owning peer and publish ready[k] = seq;
+  // the TMA producer waits for the chunks under each B tile before loading it.
+  int ag_nchunks, ag_first, ag_world, ag_rank;
+  int64_t ag_src_off, ag_shard_bytes, ag_chunk, ag_b_off;
+  char* ag_dst;
+  unsigned* ag_ready;
+  unsigned* ag_claim;
+  unsigned ag_seq, ag_epoch;
 };
 
 // k-split that gives every split >= 1 k-block: returns {splits, k-blocks per split}
@@ -585,10 +708,21 @@ static std::pair<int, int> split_plan(int64_t K, int64_t S) {
   return {(int)((kblocks + kbs - 1) / kbs), (int)kbs};
 }
 
+struct AgHook {
+  const std::vector<int64_t>* peers;
+  int rank, nchunks, first;
+  int64_t src_off, shard_bytes, chunk, b_off, flag_off;
+  char* dst;
+  unsigned* ready;
+  unsigned* claim;
+  unsigned seq, epoch;
+  double timeout_s;
+};
+
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
                       int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
                       const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
-                      double alpha, const TpHook* tp);
+                      double alpha, const TpHook* tp, const AgHook* ag = nullptr);
 
 void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
           int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
@@ -731,10 +865,43 @@ void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Fused FSDP all-gather -> GEMM: y = a W^T where W ([N, K], or [2F, K] for the SwiGLU epilogue) is a
+// view into `gathered`, the unit's full buffer that this launch fills from the peers' shards while
+// it computes (see GemmArgs::ag_*). Every chunk of the unit is copied, not only W's, so the buffer
+// is complete when the kernel ends. `ready` (int32, >= chunks) holds per-chunk sequence numbers,
+// `claim` (int32) is the chunk claim counter (zeroed here).
+void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
+             const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes,
+             at::Tensor& gathered, at::Tensor& ready, at::Tensor& claim, int64_t seq, int64_t epoch, int64_t flag_off,
+             double timeout_s) {
+  const int world = (int)peers.size();
+  TORCH_CHECK(world >= 1 && world <= TP_MAX, "gemm_ag: 1..8 ranks");
+  TORCH_CHECK(a.dim() == 2 && w.dim() == 2 && a.stride(1) == 1 && w.stride(1) == 1, "gemm_ag: K-major 2-D operands");
+  TORCH_CHECK(shard_bytes % 16 == 0 && src_off % 16 == 0, "gemm_ag: 16-byte shards");
+  TORCH_CHECK(gathered.is_cuda() && gathered.numel() * gathered.element_size() >= shard_bytes * world,
+              "gemm_ag: gathered buffer too small");
+  char* base = reinterpret_cast<char*>(gathered.data_ptr());
+  const int64_t b_off = reinterpret_cast<char*>(w.data_ptr()) - base;
+  TORCH_CHECK(b_off >= 0 && b_off + w.numel() * 2 <= shard_bytes * world, "gemm_ag: W must lie in the gathered buffer");
+  int64_t chunk = std::max<int64_t>(256 * 1024, (shard_bytes * world + 8191) / 8192);
+  chunk = (chunk + 15) / 16 * 16;
+  const int64_t cps = (shard_bytes + chunk - 1) / chunk;
+  const int64_t nchunks = cps * world;
+  TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= nchunks, "gemm_ag: ready flags");
+  TORCH_CHECK(claim.is_cuda() && claim.scalar_type() == at::kInt && claim.numel() >= 1, "gemm_ag: claim counter");
+  C10_CUDA_CHECK(cudaMemsetAsync(claim.data_ptr(), 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
+  AgHook h{&peers, (int)rank, (int)nchunks, (int)((b_off / shard_bytes) * cps + (b_off % shard_bytes) / chunk),
+           src_off, shard_bytes, chunk, b_off, flag_off, base, reinterpret_cast<unsigned*>(ready.data_ptr<int>()),
+           reinterpret_cast<unsigned*>(claim.data_ptr<int>()), (unsigned)seq, (unsigned)epoch, timeout_s};
+  const int64_t M = a.size(0), K = a.size(1), N = (epi == EPI_SWIGLU) ? w.size(0) / 2 : w.size(0);
+  gemm_impl(a, false, a.stride(0), w, false, w.stride(0), M, N, K, c, c.stride(0), epi, c10::nullopt, 0, gu, 256, 1.0,
+            nullptr, &h);
+}
+
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
                       int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
                       const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
-                      double alpha, const TpHook* tp) {
+                      double alpha, const TpHook* tp, const AgHook* ag) {
   GTRACE("enter");
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors expected");
   bind_context(a.get_device());
@@ -769,6 +936,25 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
     args.ksplit = tp->ksplit;
     args.kbs = tp->kbs;
     args.split_stride = tp->split_stride;
+  }
+  if (ag != nullptr) {
+    const int w = (int)ag->peers->size();
+    for (int i = 0; i < w; ++i) args.peers[i] = (*ag->peers)[i];
+    args.flag_off = ag->flag_off;
+    args.timeout_ns = (uint64_t)(ag->timeout_s * 1e9);
+    args.ag_nchunks = ag->nchunks;
+    args.ag_first = ag->first;
+    args.ag_world = w;
+    args.ag_rank = ag->rank;
+    args.ag_src_off = ag->src_off;
+    args.ag_shard_bytes = ag->shard_bytes;
+    args.ag_chunk = ag->chunk;
+    args.ag_b_off = ag->b_off;
+    args.ag_dst = ag->dst;
+    args.ag_ready = ag->ready;
+    args.ag_claim = ag->claim;
+    args.ag_seq = ag->seq;
+    args.ag_epoch = ag->epoch;
   }
   const bool f32_out = (epi == EPI_F32 || epi == EPI_ACC_F32 || epi == EPI_PEER_F32);
   TORCH_CHECK(c.scalar_type() == (f32_out ? at::kFloat : at::kBFloat16), "gemm: output dtype does not match the epilogue");

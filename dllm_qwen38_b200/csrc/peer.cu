@@ -139,6 +139,22 @@ __global__ void __launch_bounds__(512) all_gather_kernel(Ptrs peers, int world, 
   }
 }
 
+// Bytes [lo, hi) (16-byte aligned) of the gathered buffer: byte x comes from rank x / shard_bytes.
+__global__ void gather_range_kernel(Ptrs peers, int world, int rank, int64_t src_off, int64_t shard_bytes, int64_t lo,
+                                    int64_t hi, char* __restrict__ out, unsigned epoch, int* err,
+                                    uint64_t timeout_ns) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = (*reinterpret_cast<volatile int*>(err) == 0) &&
+                             wait_all(flag_row(peers.p[rank], SLOT_EPOCH), world, epoch, err, timeout_ns);
+  __syncthreads();
+  if (!ok) return;
+  for (int64_t x = lo + ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 16; x < hi;
+       x += (int64_t)gridDim.x * blockDim.x * 16) {
+    const int p = (int)(x / shard_bytes);
+    *reinterpret_cast<uint4*>(out + x) = ldcg16(reinterpret_cast<const char*>(peers.p[p] + src_off) + x % shard_bytes);
+  }
+}
+
 // out[i] = scale * sum_p in_p[rank * shard + i] (fp32), sq += sum_i out[i]^2.
 template <typename TIn>
 __global__ void __launch_bounds__(512) reduce_scatter_kernel(Ptrs peers, int world, int rank, int64_t src_off,
@@ -318,6 +334,23 @@ void all_gather(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off
   all_gather_kernel<<<grid, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
       to_ptrs(peers), world, static_cast<int>(rank), src_off, nvec, reinterpret_cast<uint4*>(out.data_ptr()),
       static_cast<unsigned>(epoch), error_word_ptr(), static_cast<uint64_t>(timeout_s * 1e9));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gather_range(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes, at::Tensor& out,
+                  int64_t lo, int64_t hi, int64_t epoch, double timeout_s) {
+  lo = lo / 16 * 16;
+  hi = (hi + 15) / 16 * 16;
+  const int world = (int)peers.size();
+  TORCH_CHECK(shard_bytes % 16 == 0 && src_off % 16 == 0 && hi <= shard_bytes * world && lo >= 0 && lo < hi,
+              "gather_range: bounds");
+  TORCH_CHECK(out.is_cuda() && out.numel() * out.element_size() >= hi &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "gather_range: output");
+  const int grid = grid_for((hi - lo) / 16, 256, 64);
+  gather_range_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      to_ptrs(peers), world, (int)rank, src_off, shard_bytes, lo, hi, reinterpret_cast<char*>(out.data_ptr()),
+      (unsigned)epoch, error_word_ptr(), (uint64_t)(timeout_s * 1e9));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -40,6 +40,10 @@ def _c2(t: torch.Tensor) -> torch.Tensor:
 
 _NUM_SMS = [0]
 
+# set by the sharded engine while a layer's gather is pending: a callable (a, w, out) -> bool that
+# runs the fused all-gather -> GEMM when w lies in the pending gathered buffer
+AG_HOOK = [None]
+
 
 def _splits(M: int, N: int, K: int) -> int:
     """k-splits for a skinny bf16 GEMM whose output tiles cannot fill the GPU (1 = no split)."""
@@ -62,6 +66,10 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
     N = b2.shape[0]
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=out_dtype)
+    if AG_HOOK[0] is not None and residual is None and not accumulate and out.dtype == torch.bfloat16:
+        if AG_HOOK[0](a2, b2, out):  # the fused all-gather -> GEMM consumed this call
+            _count()
+            return out
     S = _splits(M, N, K) if (out.dtype == torch.bfloat16 and not accumulate) else 1
     if S > 1:
         ws = torch.empty(S * M * N, device=a.device, dtype=torch.float32)

@@ -195,6 +195,13 @@ class FSDPEngine:
         self.grad_i = 0
         self.rs_done = [None] * len(self.grads)
         self.epoch = 0
+        # fused all-gather -> first GEMM of each layer (peer heap only)
+        self.fused_ag = self.peer is not None and os.environ.get("BDLLM_FUSED_AG", "1") != "0"
+        if self.fused_ag:
+            self.ag_ready = [torch.zeros(8192 + 64, dtype=torch.int32, device=self.device) for _ in range(2)]
+            self.ag_claim = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.ag_seq = 0
+            self._pending = None
         self.comm = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.anchor = torch.zeros((), device=self.device, requires_grad=True)
         if self.peer is not None:  # every shard written before any peer reads one
@@ -219,9 +226,25 @@ class FSDPEngine:
         return total + 4096
 
     # ------------------------------------------------------------------ gathers
+    def _fused_plan(self, unit: Unit):
+        """(first-GEMM weight offset, pre-read byte range) of a layer unit, or None."""
+        plan = getattr(unit, "_ag_plan", False)
+        if plan is False:
+            plan = None
+            first = [g for g in unit.groups if g[1] in ("fused_in_weight", "fused_qkv_weight")]
+            ln1 = [e for e in unit.entries if e[0] == "input_layernorm.weight"]
+            if first and ln1:
+                esz = unit.p.element_size()
+                _, _, o, k = ln1[0]
+                plan = (first[0][2] * esz, (o * esz, (o + k) * esz))
+            unit._ag_plan = plan
+        return plan
+
     def gather(self, unit: Unit, prefetch: bool = False) -> torch.Tensor:
         if self.world == 1:  # the shard is the whole unit
             return unit.p
+        if self.fused_ag and self._fused_plan(unit) is not None:
+            return self._gather_fused(unit, prefetch)
         for i in range(2):
             if self.owner[i] is unit:
                 if self.ready[i] is not None:
@@ -244,6 +267,54 @@ class FSDPEngine:
             self.gather_into(unit, buf)
             self.ready[i] = None
         return buf
+
+    def _gather_fused(self, unit: Unit, prefetch: bool) -> torch.Tensor:
+        """Fused path: only the bytes read before the layer's first GEMM (its input norm weight)
+        are copied now; the first GEMM gathers the rest while it computes (`_C.gemm_ag`)."""
+        if prefetch:
+            return None  # nothing to prefetch: the gather happens inside the first GEMM
+        for i in range(2):
+            if self.owner[i] is unit and self._pending is None:
+                self.lru = 1 - i
+                return self.bufs[i]
+        i = self.lru
+        self.lru = 1 - i
+        self.owner[i] = unit
+        buf = self.bufs[i]
+        w_off, (lo, hi) = self._fused_plan(unit)
+        sb = unit.shard * unit.p.element_size()
+        self.peer.gather_range(unit.p_off, sb, buf, lo, hi, self.epoch)
+        self.ag_seq += 1
+        seq, ready = self.ag_seq, self.ag_ready[i]
+        lo_ptr, hi_ptr = buf.data_ptr() + w_off, buf.data_ptr() + unit.padded * buf.element_size()
+        C = self.peer.C
+        peer = self.peer
+
+        def hook(a, w, out):
+            if not (lo_ptr <= w.data_ptr() < hi_ptr):
+                return False
+            from ..ops import cuda as Cu
+
+            C.gemm_ag(a, w, out, Cu.EPI_BF16, None, peer.ptrs, peer.rank, unit.p_off, sb, buf, ready,
+                      self.ag_claim, seq, self.epoch, 0, peer.timeout)
+            Cu.AG_HOOK[0] = None
+            self._pending = None
+            return True
+
+        from ..ops import cuda as Cu
+
+        self._pending = unit
+        Cu.AG_HOOK[0] = hook
+        return buf
+
+    def check_gathered(self) -> None:
+        """Raise if a fused gather was set up but its GEMM never ran (the buffer would be stale)."""
+        if self.fused_ag and self._pending is not None:
+            from ..ops import cuda as Cu
+
+            Cu.AG_HOOK[0] = None
+            name, self._pending = self._pending.name, None
+            raise RuntimeError(f"fused all-gather of {name} was not consumed by a GEMM")
 
     def gather_into(self, unit: Unit, out: torch.Tensor) -> None:
         if self.peer is not None:
@@ -360,6 +431,8 @@ class FSDPEngine:
     def invalidate(self) -> None:
         """Forget gathered copies (their shards changed) and, with the peer heap, publish the new
         parameter epoch that peers' next gathers wait for."""
+        if self.fused_ag:
+            self.check_gathered()
         self.owner = [None, None]
         self.ready = [None, None]
         self.epoch += 1
@@ -458,6 +531,7 @@ class _LayerFn(torch.autograd.Function):
                                  fault)
         finally:
             _unbind(layer, fused)
+        engine.check_gathered()
         ctx.save_for_backward(h, cos, sin)
         ctx.meta = (engine, i, L, block, fault)
         return out
@@ -482,6 +556,7 @@ class _LayerFn(torch.autograd.Function):
             torch.autograd.backward(out, dout)
         finally:
             _unbind(layer, fused)
+        engine.check_gathered()
         engine.reduce_scatter(unit, grad)
         return hx.grad, None, None, None, None, None, None, None, None
 

@@ -89,6 +89,13 @@ class SymmetricHeap:
                                self.epoch if epoch is None else epoch, max_blocks, self.timeout)
         _count()
 
+    def gather_range(self, off: int, shard_bytes: int, out: torch.Tensor, lo: int, hi: int,
+                     epoch: int | None = None) -> None:
+        """Bytes [lo, hi) of the gathered buffer (rounded out to 16 bytes) from the owning shards."""
+        self.C.peer_gather_range(self.ptrs, self.rank, off, shard_bytes, out, lo, hi,
+                                 self.epoch if epoch is None else epoch, self.timeout)
+        _count()
+
     def reduce_scatter(self, off: int, shard: int, in_f32: bool, out: torch.Tensor, scale: float,
                        sq: torch.Tensor | None = None, max_blocks: int = 64) -> None:
         self.rs_seq += 1

@@ -62,6 +62,42 @@ def test_peer_wait_times_out_and_reports():
         dist.destroy_process_group()
 
 
+def test_fused_allgather_gemm_single_rank():
+    """gemm_ag with one rank: the copy warps fill the whole gathered buffer from the (own) shard
+    while the tiles wait per chunk; result and buffer against torch."""
+    from dllm_qwen38_b200.ops import _native
+    from dllm_qwen38_b200.parallel.peer import SymmetricHeap
+
+    C = _native.require()
+    torch.cuda.set_device(0)
+    store = dist.TCPStore("127.0.0.1", _port(), 1, True)
+    dist.init_process_group("gloo", store=store, rank=0, world_size=1)
+    try:
+        N, K, M, extra = 1536, 1024, 300, 777 * 64
+        numel = 4096 + N * K + extra  # [something | W | the rest of a unit]
+        heap = SymmetricHeap(numel * 2 + (1 << 20), torch.device("cuda", 0))
+        shard, off = heap.alloc(numel, torch.bfloat16)
+        shard.copy_(torch.randn(numel, device="cuda").to(torch.bfloat16) * 0.1)
+        gathered = torch.zeros(numel, dtype=torch.bfloat16, device="cuda")
+        w = gathered[4096 : 4096 + N * K].view(N, K)
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        ready = torch.zeros(8192 + 64, dtype=torch.int32, device="cuda")
+        claim = torch.zeros(1, dtype=torch.int32, device="cuda")
+        for seq in (1, 2):
+            gathered.zero_()
+            C.read_error_word(True)
+            C.gemm_ag(x, w, out, 0, None, heap.ptrs, 0, off, numel * 2, gathered, ready, claim, seq, 0, 0, 10.0)
+            torch.cuda.synchronize()
+            assert C.read_error_word(False) == 0
+            assert torch.equal(gathered, shard)
+            want = x.float() @ shard[4096 : 4096 + N * K].view(N, K).float().t()
+            assert float((out.float() - want).abs().max()) < 2e-2 * float(want.abs().max())
+        heap.close()
+    finally:
+        dist.destroy_process_group()
+
+
 def _collectives_worker(rank, world, port, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
@@ -161,11 +197,14 @@ def _engine_worker(rank, world, port, q):
         cfg = preset("tiny", hidden_size=256, intermediate_size=512, linear_key_head_dim=64, linear_value_head_dim=64,
                      head_dim=64)
         runs = {}
-        for comm in ("nccl", "peer"):
+        for comm, fused in (("nccl", "0"), ("peer", "0"), ("peer", "1")):
             os.environ["BDLLM_COMM"] = comm
+            os.environ["BDLLM_FUSED_AG"] = fused
             model = build_model(cfg, seed=0, device=dev, dtype=torch.bfloat16)
             tr = FSDPTrainer(model, block=32, mask_id=cfg.mask_id, lr=1e-4)
             assert (tr.engine.peer is not None) == (comm == "peer")
+            assert tr.engine.__dict__.get("fused_ag", False) == (comm == "peer" and fused == "1")
+            comm = comm + ("-fused" if fused == "1" else "")
             g = torch.Generator().manual_seed(7)
             losses = []
             for _ in range(3):
@@ -176,10 +215,14 @@ def _engine_worker(rank, world, port, q):
             runs[comm] = (losses, state, float(tr.engine.last_grad_norm))
             tr.engine.close()
         C.check_errors()
-        (la, sa, na), (lb, sb, nb) = runs["nccl"], runs["peer"]
-        dl = max(abs(a - b) / max(1.0, abs(a)) for a, b in zip(la, lb))
-        dp = max(float((sa[k] - sb[k]).abs().max()) for k in sa)
-        q.put((rank, dl, dp, abs(na - nb) / max(1e-6, na)))
+        (la, sa, na) = runs["nccl"]
+        dl = dp = dn = 0.0
+        for other in ("peer", "peer-fused"):
+            lb, sb, nb = runs[other]
+            dl = max(dl, max(abs(a - b) / max(1.0, abs(a)) for a, b in zip(la, lb)))
+            dp = max(dp, max(float((sa[k] - sb[k]).abs().max()) for k in sa))
+            dn = max(dn, abs(na - nb) / max(1e-6, na))
+        q.put((rank, dl, dp, dn))
     finally:
         dist.destroy_process_group()
 

@@ -45,6 +45,7 @@ import torch.distributed as dist
 
 from .. import ops
 from ..models.blockdiff import BreakMode, layer_step, rope_tables
+from ..utils.trace import nvtx
 
 # weight groups consumed by one GEMM: attribute set on the submodule -> member parameter names
 FUSED_GROUPS = {
@@ -343,7 +344,7 @@ class FSDPEngine:
             j = next(k for k, g in enumerate(self.grads) if g.data_ptr() == flat_grad.data_ptr())
             off, f32 = self.grad_offs[j], False
         self.comm.wait_stream(torch.cuda.current_stream(self.device))
-        with torch.cuda.stream(self.comm):
+        with torch.cuda.stream(self.comm), nvtx(f"rs.{unit.name}"):
             self.peer.reduce_scatter(off, unit.shard, f32, unit.g, 1.0 / self.world, self.sq)
             if j is not None:
                 ev = torch.cuda.Event()
@@ -526,7 +527,7 @@ class _LayerFn(torch.autograd.Function):
         params, fused = engine.leaves(unit, buf, None)
         _bind(layer, fused)
         try:
-            with torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
+            with nvtx(f"layer{i}.fwd"), torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], h, L, block, engine.cfg.gdn_chunk_size, cos, sin,
                                  fault)
         finally:
@@ -550,10 +551,11 @@ class _LayerFn(torch.autograd.Function):
         hx = h.detach().requires_grad_(True)
         _bind(layer, fused)
         try:
-            with torch.enable_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
+            with nvtx(f"layer{i}.bwd"), torch.enable_grad(), \
+                    torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], hx, L, block, engine.cfg.gdn_chunk_size, cos, sin,
                                  fault)
-            torch.autograd.backward(out, dout)
+                torch.autograd.backward(out, dout)
         finally:
             _unbind(layer, fused)
         engine.check_gathered()

@@ -80,7 +80,8 @@ void gather_range(const std::vector<int64_t>& peers, int64_t rank, int64_t src_o
                   int64_t lo, int64_t hi, int64_t epoch, double timeout_s);
 void reduce_scatter(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard, bool in_f32,
                     at::Tensor& out, double scale, const c10::optional<at::Tensor>& sq, int64_t seq,
-                    int64_t max_blocks, double timeout_s);
+                    int64_t max_blocks, double timeout_s, const std::vector<at::Tensor>& adam_state,
+                    const std::vector<double>& adam_hp);
 void allreduce_f32(const std::vector<int64_t>& peers, int64_t rank, const at::Tensor& vals, at::Tensor& out,
                    int64_t seq, double timeout_s);
 }  // namespace peer
@@ -145,7 +146,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_reduce_scatter", &bdllm::peer::reduce_scatter,
         "reduce-scatter by peer loads, fused fp32 cast, scale and sum of squares", py::arg("peers"),
         py::arg("rank"), py::arg("src_off"), py::arg("shard"), py::arg("in_f32"), py::arg("out"), py::arg("scale"),
-        py::arg("sq"), py::arg("seq"), py::arg("max_blocks"), py::arg("timeout_s"));
+        py::arg("sq"), py::arg("seq"), py::arg("max_blocks"), py::arg("timeout_s"),
+        py::arg("adam_state") = std::vector<at::Tensor>{}, py::arg("adam_hp") = std::vector<double>{});
   m.def("peer_allreduce_f32", &bdllm::peer::allreduce_f32);
   m.def("read_error_word", &bdllm::read_error_word, "device error word (bounded-wait expiries)",
         py::arg("reset") = false);

@@ -155,12 +155,35 @@ __global__ void gather_range_kernel(Ptrs peers, int world, int rank, int64_t src
   }
 }
 
-// out[i] = scale * sum_p in_p[rank * shard + i] (fp32), sq += sum_i out[i]^2.
+// AdamW fused into the reduce-scatter (runs without gradient clipping): the averaged gradient
+// never leaves registers; master/moments are fp32 shards, p the bf16 parameter shard.
+struct Adam {
+  float* w;
+  float* m;
+  float* v;
+  __nv_bfloat16* p;
+  float lr, b1, b2, eps, wd, bc1, bc2;
+};
+
+__device__ __forceinline__ void adam_update(const Adam& A, int64_t i, float g) {
+  float wi = A.w[i];
+  if (A.wd != 0.f) wi *= 1.f - A.lr * A.wd;
+  const float mi = A.b1 * A.m[i] + (1.f - A.b1) * g;
+  const float vi = A.b2 * A.v[i] + (1.f - A.b2) * g * g;
+  A.m[i] = mi;
+  A.v[i] = vi;
+  wi -= A.lr * (mi / A.bc1) / (sqrtf(vi / A.bc2) + A.eps);
+  A.w[i] = wi;
+  A.p[i] = __float2bfloat16(wi);
+}
+
+// out[i] = scale * sum_p in_p[rank * shard + i] (fp32), sq += sum_i out[i]^2; with A.w set, the
+// AdamW update of element i is applied right away instead (out may then be null).
 template <typename TIn>
 __global__ void __launch_bounds__(512) reduce_scatter_kernel(Ptrs peers, int world, int rank, int64_t src_off,
                                                              int64_t shard, float* __restrict__ out, float scale,
                                                              float* __restrict__ sq, unsigned seq, int* err,
-                                                             uint64_t timeout_ns) {
+                                                             uint64_t timeout_ns, Adam A) {
   constexpr int EPV = 16 / sizeof(TIn);  // elements per 16-byte vector
   __shared__ int ok;
   __shared__ float red[16];
@@ -198,14 +221,19 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(Ptrs peers, int wor
           }
         }
       }
-      float4* o = reinterpret_cast<float4*>(out + v * EPV);
 #pragma unroll
       for (int e = 0; e < EPV; ++e) {
         s[e] *= scale;
         acc2 += s[e] * s[e];
       }
-      o[0] = make_float4(s[0], s[1], s[2], s[3]);
-      if constexpr (EPV == 8) o[1] = make_float4(s[4], s[5], s[6], s[7]);
+      if (A.w != nullptr) {
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) adam_update(A, v * EPV + e, s[e]);
+      } else {
+        float4* o = reinterpret_cast<float4*>(out + v * EPV);
+        o[0] = make_float4(s[0], s[1], s[2], s[3]);
+        if constexpr (EPV == 8) o[1] = make_float4(s[4], s[5], s[6], s[7]);
+      }
     }
   }
   // block sum of squares
@@ -356,7 +384,21 @@ void gather_range(const std::vector<int64_t>& peers, int64_t rank, int64_t src_o
 
 void reduce_scatter(const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard, bool in_f32,
                     at::Tensor& out, double scale, const c10::optional<at::Tensor>& sq, int64_t seq,
-                    int64_t max_blocks, double timeout_s) {
+                    int64_t max_blocks, double timeout_s, const std::vector<at::Tensor>& adam_state,
+                    const std::vector<double>& adam_hp) {
+  Adam A{};
+  if (!adam_state.empty()) {  // {master, m, v, p} and {lr, b1, b2, eps, wd, bc1, bc2}
+    TORCH_CHECK(adam_state.size() == 4 && adam_hp.size() == 7, "reduce_scatter: adam state/hyper-parameters");
+    for (int i = 0; i < 3; ++i)
+      TORCH_CHECK(adam_state[i].scalar_type() == at::kFloat && adam_state[i].numel() >= shard, "adam: fp32 shards");
+    TORCH_CHECK(adam_state[3].scalar_type() == at::kBFloat16 && adam_state[3].numel() >= shard, "adam: bf16 shard");
+    A.w = adam_state[0].data_ptr<float>();
+    A.m = adam_state[1].data_ptr<float>();
+    A.v = adam_state[2].data_ptr<float>();
+    A.p = reinterpret_cast<__nv_bfloat16*>(adam_state[3].data_ptr());
+    A.lr = (float)adam_hp[0], A.b1 = (float)adam_hp[1], A.b2 = (float)adam_hp[2], A.eps = (float)adam_hp[3];
+    A.wd = (float)adam_hp[4], A.bc1 = (float)adam_hp[5], A.bc2 = (float)adam_hp[6];
+  }
   const int world = static_cast<int>(peers.size());
   const int esz = in_f32 ? 4 : 2;
   TORCH_CHECK((shard * esz) % 16 == 0 && src_off % 16 == 0, "reduce_scatter: 16-byte shards");
@@ -376,11 +418,11 @@ void reduce_scatter(const std::vector<int64_t>& peers, int64_t rank, int64_t src
   if (in_f32)
     reduce_scatter_kernel<float><<<grid, 512, 0, stream>>>(P, world, static_cast<int>(rank), src_off, shard,
                                                            out.data_ptr<float>(), static_cast<float>(scale), sqp,
-                                                           static_cast<unsigned>(seq), error_word_ptr(), tmo);
+                                                           static_cast<unsigned>(seq), error_word_ptr(), tmo, A);
   else
     reduce_scatter_kernel<__nv_bfloat16><<<grid, 512, 0, stream>>>(
         P, world, static_cast<int>(rank), src_off, shard, out.data_ptr<float>(), static_cast<float>(scale), sqp,
-        static_cast<unsigned>(seq), error_word_ptr(), tmo);
+        static_cast<unsigned>(seq), error_word_ptr(), tmo, A);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

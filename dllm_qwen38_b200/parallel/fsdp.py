@@ -344,8 +344,13 @@ class FSDPEngine:
             j = next(k for k, g in enumerate(self.grads) if g.data_ptr() == flat_grad.data_ptr())
             off, f32 = self.grad_offs[j], False
         self.comm.wait_stream(torch.cuda.current_stream(self.device))
+        adam = None
+        if not self.grad_clip:  # no global clip: AdamW runs inside the reduce-scatter, overlapped
+            b1, b2 = self.betas
+            adam = ((unit.master, unit.m, unit.v, unit.p),
+                    (self.lr, b1, b2, self.eps, self.wd, 1 - b1 ** self.step_count, 1 - b2 ** self.step_count))
         with torch.cuda.stream(self.comm), nvtx(f"rs.{unit.name}"):
-            self.peer.reduce_scatter(off, unit.shard, f32, unit.g, 1.0 / self.world, self.sq)
+            self.peer.reduce_scatter(off, unit.shard, f32, unit.g, 1.0 / self.world, self.sq, adam=adam)
             if j is not None:
                 ev = torch.cuda.Event()
                 ev.record(self.comm)
@@ -414,6 +419,10 @@ class FSDPEngine:
             torch.cuda.current_stream(self.device).wait_stream(self.comm)
             self.peer.allreduce_f32(self.sq, self.sq_all)
             norm = self.sq_all[0].sqrt()
+            if not self.grad_clip:  # the updates already ran inside the reduce-scatters
+                self.last_grad_norm = norm
+                self.invalidate()
+                return
         else:
             sq = torch.zeros((), device=self.device, dtype=torch.float32)
             for u in self.units:
@@ -421,7 +430,7 @@ class FSDPEngine:
             if self.world > 1:
                 dist.all_reduce(sq)
             norm = sq.sqrt()
-        coef = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0)
+        coef = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0) if self.grad_clip > 0 else torch.ones_like(norm)
         b1, b2 = self.betas
         bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count
         for u in self.units:

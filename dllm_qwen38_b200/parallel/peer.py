@@ -97,10 +97,13 @@ class SymmetricHeap:
         _count()
 
     def reduce_scatter(self, off: int, shard: int, in_f32: bool, out: torch.Tensor, scale: float,
-                       sq: torch.Tensor | None = None, max_blocks: int = 64) -> None:
+                       sq: torch.Tensor | None = None, max_blocks: int = 64, adam=None) -> None:
+        """adam = ((master, m, v, p_bf16), (lr, b1, b2, eps, wd, bc1, bc2)) applies AdamW to the
+        reduced gradient in the same launch (no clipping: the gradient is not stored)."""
         self.rs_seq += 1
+        st, hp = adam if adam is not None else ((), ())
         self.C.peer_reduce_scatter(self.ptrs, self.rank, off, shard, in_f32, out, scale, sq, self.rs_seq,
-                                   max_blocks, self.timeout)
+                                   max_blocks, self.timeout, list(st), [float(x) for x in hp])
         _count()
 
     def allreduce_f32(self, vals: torch.Tensor, out: torch.Tensor) -> None:

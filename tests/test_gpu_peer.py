@@ -197,14 +197,15 @@ def _engine_worker(rank, world, port, q):
         cfg = preset("tiny", hidden_size=256, intermediate_size=512, linear_key_head_dim=64, linear_value_head_dim=64,
                      head_dim=64)
         runs = {}
-        for comm, fused in (("nccl", "0"), ("peer", "0"), ("peer", "1")):
+        for comm, fused, clip in (("nccl", "0", 1.0), ("peer", "0", 1.0), ("peer", "1", 1.0), ("nccl", "0", 0.0),
+                                  ("peer", "1", 0.0)):
             os.environ["BDLLM_COMM"] = comm
             os.environ["BDLLM_FUSED_AG"] = fused
             model = build_model(cfg, seed=0, device=dev, dtype=torch.bfloat16)
-            tr = FSDPTrainer(model, block=32, mask_id=cfg.mask_id, lr=1e-4)
+            tr = FSDPTrainer(model, block=32, mask_id=cfg.mask_id, lr=1e-4, grad_clip=clip)
             assert (tr.engine.peer is not None) == (comm == "peer")
             assert tr.engine.__dict__.get("fused_ag", False) == (comm == "peer" and fused == "1")
-            comm = comm + ("-fused" if fused == "1" else "")
+            comm = comm + ("-fused" if fused == "1" else "") + ("-noclip" if clip == 0 else "")
             g = torch.Generator().manual_seed(7)
             losses = []
             for _ in range(3):
@@ -217,7 +218,8 @@ def _engine_worker(rank, world, port, q):
         C.check_errors()
         (la, sa, na) = runs["nccl"]
         dl = dp = dn = 0.0
-        for other in ("peer", "peer-fused"):
+        for base, other in (("nccl", "peer"), ("nccl", "peer-fused"), ("nccl-noclip", "peer-fused-noclip")):
+            la, sa, na = runs[base]
             lb, sb, nb = runs[other]
             dl = max(dl, max(abs(a - b) / max(1.0, abs(a)) for a, b in zip(la, lb)))
             dp = max(dp, max(float((sa[k] - sb[k]).abs().max()) for k in sa))

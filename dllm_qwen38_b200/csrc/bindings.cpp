@@ -49,7 +49,7 @@ int64_t gemm_tp(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t
 void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
              const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes,
              at::Tensor& gathered, at::Tensor& ready, at::Tensor& claim, int64_t seq, int64_t epoch, int64_t flag_off,
-             double timeout_s);
+             double timeout_s, int64_t lo, int64_t hi);
 void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::optional<at::Tensor>& residual,
                    bool swiglu);
 void tp_reduce_norm_push(const std::vector<int64_t>& peers, int64_t rank, int64_t R, int64_t D, int64_t part_off,
@@ -122,7 +122,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("rows_per_rank"), py::arg("part_off"), py::arg("flag_off"), py::arg("ctr"), py::arg("wait_ag"),
         py::arg("timeout_s"), py::arg("bn") = 256, py::arg("ksplit") = 1);
   m.def("gemm_ag", &bdllm::gemm_ag,
-        "fused FSDP all-gather -> GEMM: copy warps pull the unit's shards from the peers while the tiles wait per chunk");
+        "fused FSDP all-gather -> GEMM: copy warps pull the unit's shards from the peers while the tiles wait per chunk",
+        py::arg("a"), py::arg("w"), py::arg("c"), py::arg("epi"), py::arg("gu"), py::arg("peers"), py::arg("rank"),
+        py::arg("src_off"), py::arg("shard_bytes"), py::arg("gathered"), py::arg("ready"), py::arg("claim"),
+        py::arg("seq"), py::arg("epoch"), py::arg("flag_off"), py::arg("timeout_s"), py::arg("lo") = 0,
+        py::arg("hi") = 0);
   m.def("splitk_reduce", &bdllm::splitk_reduce, "sum of k-split partials (+ residual, or SwiGLU of gate|up)",
         py::arg("ws"), py::arg("S"), py::arg("out"), py::arg("residual") = c10::nullopt, py::arg("swiglu") = false);
   m.def("tp_reduce_norm_push", &bdllm::tp_reduce_norm_push,

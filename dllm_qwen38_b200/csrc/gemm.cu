@@ -71,7 +71,7 @@ struct GemmArgs {
   // CTA claim 16-byte-aligned chunks of ag_chunk bytes (chunk k = shard k / cps, piece k % cps) in
   // priority order starting at ag_first, copy them from the owning peer and publish ready[k] = seq;
   // the TMA producer waits for the chunks under each B tile before loading it.
-  int ag_nchunks, ag_first, ag_world, ag_rank;
+  int ag_nchunks, ag_first, ag_world, ag_rank;  // ag_nchunks: chunks this launch copies, from ag_first
   int64_t ag_src_off, ag_shard_bytes, ag_chunk, ag_b_off;
   char* ag_dst;
   unsigned* ag_ready;
@@ -150,7 +150,7 @@ __device__ void ag_copy_warp(const GemmArgs& a, int lane, volatile int* abort_fl
     if (lane == 0) c = atomicAdd(a.ag_claim, 1u);
     c = __shfl_sync(0xffffffffu, c, 0);
     if (c >= (unsigned)a.ag_nchunks || *abort_flag) break;
-    const int64_t k = (a.ag_first + (int64_t)c) % a.ag_nchunks;
+    const int64_t k = a.ag_first + (int64_t)c;
     const int p = (int)(k / cps);
     const int64_t lo = (k % cps) * a.ag_chunk, n = min(a.ag_chunk, a.ag_shard_bytes - lo);
     const char* src = reinterpret_cast<const char*>(a.peers[p] + a.ag_src_off) + lo;
@@ -692,7 +692,7 @@ struct TpHook {
   // CTA claim 16-byte-aligned chunks of ag_chunk bytes (chunk k = shard k / cps, piece k % cps) in
   // priority order starting at ag_first, copy them from the owning peer and publish ready[k] = seq;
   // the TMA producer waits for the chunks under each B tile before loading it.
-  int ag_nchunks, ag_first, ag_world, ag_rank;
+  int ag_nchunks, ag_first, ag_world, ag_rank;  // ag_nchunks: chunks this launch copies, from ag_first
   int64_t ag_src_off, ag_shard_bytes, ag_chunk, ag_b_off;
   char* ag_dst;
   unsigned* ag_ready;
@@ -873,7 +873,7 @@ void splitk_reduce(const at::Tensor& ws, int64_t S, at::Tensor& out, const c10::
 void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t epi, const c10::optional<at::Tensor>& gu,
              const std::vector<int64_t>& peers, int64_t rank, int64_t src_off, int64_t shard_bytes,
              at::Tensor& gathered, at::Tensor& ready, at::Tensor& claim, int64_t seq, int64_t epoch, int64_t flag_off,
-             double timeout_s) {
+             double timeout_s, int64_t lo, int64_t hi) {
   const int world = (int)peers.size();
   TORCH_CHECK(world >= 1 && world <= TP_MAX, "gemm_ag: 1..8 ranks");
   TORCH_CHECK(a.dim() == 2 && w.dim() == 2 && a.stride(1) == 1 && w.stride(1) == 1, "gemm_ag: K-major 2-D operands");
@@ -888,9 +888,16 @@ void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t ep
   const int64_t cps = (shard_bytes + chunk - 1) / chunk;
   const int64_t nchunks = cps * world;
   TORCH_CHECK(ready.is_cuda() && ready.scalar_type() == at::kInt && ready.numel() >= nchunks, "gemm_ag: ready flags");
+  (void)nchunks;
   TORCH_CHECK(claim.is_cuda() && claim.scalar_type() == at::kInt && claim.numel() >= 1, "gemm_ag: claim counter");
   C10_CUDA_CHECK(cudaMemsetAsync(claim.data_ptr(), 0, sizeof(int), at::cuda::getCurrentCUDAStream()));
-  AgHook h{&peers, (int)rank, (int)nchunks, (int)((b_off / shard_bytes) * cps + (b_off % shard_bytes) / chunk),
+  // chunks to copy: those overlapping gathered bytes [lo, hi) (default: the whole unit)
+  if (hi <= lo) lo = 0, hi = shard_bytes * world;
+  TORCH_CHECK(lo >= 0 && hi <= shard_bytes * world && lo <= b_off && b_off + w.numel() * 2 <= hi,
+              "gemm_ag: the copied range must cover W");
+  auto chunk_of = [&](int64_t x) { return (x / shard_bytes) * cps + (x % shard_bytes) / chunk; };
+  const int64_t k_lo = chunk_of(lo), k_hi = chunk_of(hi - 1);
+  AgHook h{&peers, (int)rank, (int)(k_hi - k_lo + 1), (int)k_lo,
            src_off, shard_bytes, chunk, b_off, flag_off, base, reinterpret_cast<unsigned*>(ready.data_ptr<int>()),
            reinterpret_cast<unsigned*>(claim.data_ptr<int>()), (unsigned)seq, (unsigned)epoch, timeout_s};
   const int64_t M = a.size(0), K = a.size(1), N = (epi == EPI_SWIGLU) ? w.size(0) / 2 : w.size(0);

@@ -231,7 +231,8 @@ def reference_dcp_tensors(path: str) -> tuple[dict, int, int]:
 
 def engine_unit_layout(cfg) -> dict:
     """{unit name: [(our key, shape, offset, numel)]} of the sharded engine's flat units, in the
-    engine's order (module registration order, shared parameters once)."""
+    engine's flat order (`parallel.fsdp.flat_order`: small non-GEMM parameters first, shared
+    parameters once)."""
     from ..models.qwen35 import BlockDiffusionLM
 
     with torch.device("meta"):
@@ -241,13 +242,12 @@ def engine_unit_layout(cfg) -> dict:
     units += [(f"layers.{i}", f"text_model.layers.{i}.", layer) for i, layer in enumerate(tm.layers)]
     head = {"norm": tm.norm} if cfg.tie_word_embeddings else {"norm": tm.norm, "lm_head": m.lm_head}
     units.append(("head", "", torch.nn.ModuleDict(head)))
+    from ..parallel.fsdp import flat_order
+
     out = {}
     for name, prefix, mod in units:
-        off, ent, seen = 0, [], set()
-        for n, p in mod.named_parameters():
-            if id(p) in seen:
-                continue
-            seen.add(id(p))
+        off, ent = 0, []
+        for n, p in flat_order(mod):
             key = prefix + n
             if name == "head" and n.startswith("norm."):
                 key = "text_model." + n

@@ -40,8 +40,9 @@ def _c2(t: torch.Tensor) -> torch.Tensor:
 
 _NUM_SMS = [0]
 
-# set by the sharded engine while a layer's gather is pending: a callable (a, w, out) -> bool that
-# runs the fused all-gather -> GEMM when w lies in the pending gathered buffer
+# set by the sharded engine while a layer's weights are being gathered: a callable
+# (a, w, out, epi, gu) -> bool that runs the fused all-gather -> GEMM when w is one of the layer's
+# weights not gathered yet
 AG_HOOK = [None]
 
 
@@ -67,7 +68,7 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
     if out is None:
         out = torch.empty(M, N, device=a.device, dtype=out_dtype)
     if AG_HOOK[0] is not None and residual is None and not accumulate and out.dtype == torch.bfloat16:
-        if AG_HOOK[0](a2, b2, out):  # the fused all-gather -> GEMM consumed this call
+        if AG_HOOK[0](a2, b2, out, EPI_BF16, None):  # this weight is gathered by this GEMM (fused)
             _count()
             return out
     S = _splits(M, N, K) if (out.dtype == torch.bfloat16 and not accumulate) else 1
@@ -128,6 +129,9 @@ def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, F: int, store_gu: bool
     M, K = x2.shape
     act = torch.empty(M, F, device=x.device, dtype=torch.bfloat16)
     gu = torch.empty(M, 2 * F, device=x.device, dtype=torch.bfloat16) if store_gu else None
+    if AG_HOOK[0] is not None and AG_HOOK[0](x2, w_gate_up, act, EPI_SWIGLU, gu):
+        _count()
+        return act, gu
     _C.gemm(x2, False, x2.stride(0), w_gate_up, False, w_gate_up.stride(0), M, F, K, act, act.stride(0), EPI_SWIGLU,
             None, 0, gu)
     _count()

@@ -56,6 +56,29 @@ FUSED_GROUPS = {
 }
 
 
+SMALL_NUMEL = 1 << 20
+
+
+def flat_order(module: torch.nn.Module) -> list:
+    """Unique (name, parameter) of a unit in flat-buffer order: parameters below 1M elements that
+    are not members of a fused weight group first (norm weights, conv taps, gate constants: what a
+    layer reads outside its GEMMs), then the rest in module order. The small region is gathered
+    before a layer runs; each GEMM weight after it can then be gathered by its own GEMM."""
+    members = {m for _, (_, ms) in FUSED_GROUPS.items() for m in ms}
+    uniq, seen = [], set()
+    for n, p in module.named_parameters():
+        if id(p) not in seen:
+            seen.add(id(p))
+            uniq.append((n, p))
+
+    def is_member(n):
+        return any(n == m or n.endswith("." + m) for m in members)
+
+    small = [(n, p) for n, p in uniq if p.numel() < SMALL_NUMEL and not is_member(n)]
+    ids = {id(p) for _, p in small}
+    return small + [(n, p) for n, p in uniq if id(p) not in ids]
+
+
 def _world():
     return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
 
@@ -66,14 +89,12 @@ class Unit:
     def __init__(self, name: str, module: torch.nn.Module, world: int, rank: int, device, dtype=torch.bfloat16,
                  alloc=None):
         self.name, self.world, self.rank, self.device = name, world, rank, device
-        self.entries = []  # (param name, shape, offset, numel), module order
-        off, seen = 0, set()
-        for pname, p in module.named_parameters():
-            if id(p) in seen:
-                continue
-            seen.add(id(p))
+        self.entries = []  # (param name, shape, offset, numel), flat_order
+        off = 0
+        for pname, p in flat_order(module):
             self.entries.append((pname, tuple(p.shape), off, p.numel()))
             off += p.numel()
+        self.small_numel = sum(k for n, _, _, k in self.entries if self._is_small(n, k))  # a prefix
         self.numel = off
         self.shard = (off + world - 1) // world
         if world > 1:  # 16-byte aligned slices of bf16 and fp32 buffers for the peer kernels
@@ -90,6 +111,11 @@ class Unit:
         # gradient itself at world 1 (no reduction, and half the memory of an fp32 copy)
         self.g = torch.zeros(self.shard, dtype=torch.float32 if world > 1 else dtype, device=device)
         self.groups = self._groups()
+
+    @staticmethod
+    def _is_small(name: str, numel: int) -> bool:
+        members = {m for _, (_, ms) in FUSED_GROUPS.items() for m in ms}
+        return numel < SMALL_NUMEL and not any(name == m or name.endswith("." + m) for m in members)
 
     def _groups(self):
         """Fused groups present in this unit: (submodule path, attr, first offset, numel, rows, cols)."""
@@ -228,16 +254,13 @@ class FSDPEngine:
 
     # ------------------------------------------------------------------ gathers
     def _fused_plan(self, unit: Unit):
-        """(first-GEMM weight offset, pre-read byte range) of a layer unit, or None."""
+        """Byte size of the unit's small-parameter prefix when its GEMM weights can be gathered by
+        their own GEMMs (layer units), else None."""
         plan = getattr(unit, "_ag_plan", False)
         if plan is False:
             plan = None
-            first = [g for g in unit.groups if g[1] in ("fused_in_weight", "fused_qkv_weight")]
-            ln1 = [e for e in unit.entries if e[0] == "input_layernorm.weight"]
-            if first and ln1:
-                esz = unit.p.element_size()
-                _, _, o, k = ln1[0]
-                plan = (first[0][2] * esz, (o * esz, (o + k) * esz))
+            if any(g[1] in ("fused_in_weight", "fused_qkv_weight") for g in unit.groups):
+                plan = unit.small_numel * unit.p.element_size()
             unit._ag_plan = plan
         return plan
 
@@ -270,52 +293,69 @@ class FSDPEngine:
         return buf
 
     def _gather_fused(self, unit: Unit, prefetch: bool) -> torch.Tensor:
-        """Fused path: only the bytes read before the layer's first GEMM (its input norm weight)
-        are copied now; the first GEMM gathers the rest while it computes (`_C.gemm_ag`)."""
+        """Fused path: the small-parameter prefix (norm weights, conv taps, gate constants) is
+        copied now; every GEMM weight of the unit is gathered by the first GEMM that reads it
+        (`_C.gemm_ag`), tile by tile, while that GEMM computes."""
         if prefetch:
-            return None  # nothing to prefetch: the gather happens inside the first GEMM
+            return None  # nothing to prefetch: the gathers happen inside the GEMMs
         for i in range(2):
             if self.owner[i] is unit and self._pending is None:
                 self.lru = 1 - i
                 return self.bufs[i]
+        self.check_gathered()
         i = self.lru
         self.lru = 1 - i
         self.owner[i] = unit
         buf = self.bufs[i]
-        w_off, (lo, hi) = self._fused_plan(unit)
-        sb = unit.shard * unit.p.element_size()
-        self.peer.gather_range(unit.p_off, sb, buf, lo, hi, self.epoch)
-        self.ag_seq += 1
-        seq, ready = self.ag_seq, self.ag_ready[i]
-        lo_ptr, hi_ptr = buf.data_ptr() + w_off, buf.data_ptr() + unit.padded * buf.element_size()
-        C = self.peer.C
-        peer = self.peer
+        esz = buf.element_size()
+        sb = unit.shard * esz
+        small = self._fused_plan(unit)
+        if small:
+            self.peer.gather_range(unit.p_off, sb, buf, 0, small, self.epoch)
+        # the GEMM weights still to gather: (byte lo, byte hi)
+        todo = []
+        for n, _, o, k in unit.entries:
+            if o * esz >= small:
+                todo.append((o * esz, (o + k) * esz))
+        for path, attr, off, numel, rows, cols in unit.groups:  # a fused group is one weight
+            todo = [r for r in todo if not (off * esz <= r[0] < (off + numel) * esz)]
+            todo.append((off * esz, (off + numel) * esz))
+        pending = {lo: hi for lo, hi in todo}
+        base = buf.data_ptr()
+        ready = self.ag_ready[i]
+        C, peer = self.peer.C, self.peer
 
-        def hook(a, w, out):
-            if not (lo_ptr <= w.data_ptr() < hi_ptr):
+        def hook(a, w, out, epi, gu):
+            lo = w.data_ptr() - base
+            hi = pending.get(lo)
+            if hi is None or hi != lo + w.numel() * esz:
                 return False
-            from ..ops import cuda as Cu
+            self.ag_seq += 1
+            C.gemm_ag(a, w, out, epi, gu, peer.ptrs, peer.rank, unit.p_off, sb, buf, ready, self.ag_claim,
+                      self.ag_seq, self.epoch, 0, peer.timeout, lo, hi)
+            del pending[lo]
+            if not pending:
+                from ..ops import cuda as Cu
 
-            C.gemm_ag(a, w, out, Cu.EPI_BF16, None, peer.ptrs, peer.rank, unit.p_off, sb, buf, ready,
-                      self.ag_claim, seq, self.epoch, 0, peer.timeout)
-            Cu.AG_HOOK[0] = None
-            self._pending = None
+                Cu.AG_HOOK[0] = None
+                self._pending = None
             return True
 
         from ..ops import cuda as Cu
 
-        self._pending = unit
+        self._pending = (unit, pending)
         Cu.AG_HOOK[0] = hook
         return buf
 
     def check_gathered(self) -> None:
-        """Raise if a fused gather was set up but its GEMM never ran (the buffer would be stale)."""
+        """Raise if a layer ran without gathering all of its GEMM weights (the buffer would be
+        incomplete for the next use)."""
         if self.fused_ag and self._pending is not None:
             from ..ops import cuda as Cu
 
             Cu.AG_HOOK[0] = None
-            name, self._pending = self._pending.name, None
-            raise RuntimeError(f"fused all-gather of {name} was not consumed by a GEMM")
+            (unit, left), self._pending = self._pending, None
+            raise RuntimeError(f"fused all-gather of {unit.name}: {len(left)} weights were never read by a GEMM")
 
     def gather_into(self, unit: Unit, out: torch.Tensor) -> None:
         if self.peer is not None:

@@ -154,6 +154,8 @@ def main(argv=None) -> int:
         t = torch.tensor([s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)  # the slowest rank's device time
         s = float(t.item())
+        if hasattr(eng, "timing") and os.environ.get("BDLLM_TP_TIMING") == "1":
+            print(json.dumps({"rank": rank, "tp_timing_ms": eng.timing()}), flush=True)
         eng.close()
         dist.destroy_process_group()
         if rank != 0:

@@ -37,6 +37,25 @@ from .golden import DecodeTrace
 
 EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_PEER_F32 = 0, 1, 4, 5
 
+TIMING = os.environ.get("BDLLM_TP_TIMING", "0") == "1"
+
+
+def _timed(name):
+    """Per-phase device time (CUDA events) when BDLLM_TP_TIMING=1 and graphs are off: a breakdown
+    of where a step's time goes, read with `TPDecodeEngine.timing()`."""
+    def deco(fn):
+        def wrap(self, *a, **k):
+            if not (TIMING and not self.graphs):
+                return fn(self, *a, **k)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(self, *a, **k)
+            e1.record()
+            self._events.append((name, e0, e1))
+            return r
+        return wrap
+    return deco
+
 
 class TPDecodeEngine:
     def __init__(self, model, batch: int, max_len: int, block: int, *, threshold: float = 0.9,
@@ -158,6 +177,7 @@ class TPDecodeEngine:
         self.left = torch.zeros(B, dtype=torch.int32, device=dev)
         self.mask_id_t = torch.full((), cfg.mask_id, dtype=torch.long, device=dev)
         self._g = {}
+        self._events = []
         if W > 1:
             torch.cuda.synchronize(dev)
             dist.barrier()
@@ -170,6 +190,7 @@ class TPDecodeEngine:
         tiles = ((self.M + 127) // 128) * ((N + 255) // 256)
         return max(1, min(self.SMAX, self.n_sms // tiles, K // 64 // 2))
 
+    @_timed("col_gemm")
     def _col(self, w, epi=EPI_BF16):
         """Column-parallel GEMM over the gathered rows (waits for every rank's push inside the GEMM)."""
         C = self.C
@@ -194,6 +215,7 @@ class TPDecodeEngine:
         self.Cu._count()
         return out
 
+    @_timed("row_gemm")
     def _row(self, x, w):
         """Row-parallel GEMM: fp32 partial rows straight into the owners' slots (per k split)."""
         if self.world == 1:
@@ -204,6 +226,7 @@ class TPDecodeEngine:
                                                    self.R, self.part_off, 0, self.ctr, False, self.timeout, 256, S)
         self.Cu._count()
 
+    @_timed("reduce_norm_push")
     def _reduce_norm(self, w1, eps, has_partials=True, push=True):
         if self.world == 1:
             if has_partials:
@@ -217,6 +240,7 @@ class TPDecodeEngine:
         self.Cu._count()
 
     # ------------------------------------------------------------------ mixers (local heads, all M rows)
+    @_timed("gdn_mixer_total")
     def _gdn(self, e, commit):
         C, Cu, B, T = self.C, self.Cu, self.B, self.T
         hk, hv, Dk, Dv = e["hk"], e["hv"], e["Dk"], e["Dv"]
@@ -231,6 +255,7 @@ class TPDecodeEngine:
         y = Cu.gated_rmsnorm(o, z.reshape(B, T, hv, Dv), e["norm_w"], e["norm_eps"])
         self._row(y.reshape(B * T, hv * Dv), e["w_out"])
 
+    @_timed("attn_mixer_total")
     def _attn(self, e, cos, sin):
         C, Cu, B, T = self.C, self.Cu, self.B, self.T
         hq, hk, Dh = e["hq"], e["hk"], e["Dh"]
@@ -376,6 +401,14 @@ class TPDecodeEngine:
             if all(done):
                 break
         return traces
+
+    def timing(self) -> dict:
+        """{phase: total ms} of the timed calls so far (BDLLM_TP_TIMING=1, graphs off)."""
+        torch.cuda.synchronize(self.dev)
+        out = {}
+        for name, e0, e1 in self._events:
+            out[name] = out.get(name, 0.0) + e0.elapsed_time(e1)
+        return {k: round(v, 2) for k, v in out.items()}
 
     def close(self) -> None:
         self._g.clear()

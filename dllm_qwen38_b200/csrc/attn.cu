@@ -84,8 +84,6 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool vali
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
-// all but the most recently committed group have landed (double buffering: the current tile is in)
-__device__ __forceinline__ void cp_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // 64 rows x D of a [B*T2, ...] tensor with token stride `tok` (elements) starting at row r0
 template <int D>
@@ -181,10 +179,9 @@ __device__ __forceinline__ void pv_tile(float (&acc)[DA / 8][4], const float (&p
 template <int D>
 __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
   extern __shared__ __align__(128) __nv_bfloat16 sm[];
-  // Q, then two K/V buffers: the next key tile streams in while this one is used
   __nv_bfloat16* sQ = sm;
-  __nv_bfloat16* sKb[2] = {sm + TILE * D, sm + 3 * TILE * D};
-  __nv_bfloat16* sVb[2] = {sm + 2 * TILE * D, sm + 4 * TILE * D};
+  __nv_bfloat16* sK = sm + TILE * D;
+  __nv_bfloat16* sV = sm + 2 * TILE * D;
   const int i0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
@@ -201,28 +198,14 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   const int i1 = min(i0 + TILE - 1, a.T2 - 1);
-  auto next = [&](int j) {  // first key tile >= j that this query tile may see
-    for (; j < Tk; j += TILE)
-      if (all || tile_may(i0, i1, j, min(j + TILE - 1, Tk - 1), a.L, a.block, a.leak)) break;
-    return j;
-  };
-  int j0 = next(0), cur = 0;
-  if (j0 < Tk) {
-    load_tile<D>(sKb[0], kb, a.k_tok, j0, Tk);
-    load_tile<D>(sVb[0], vb, a.v_tok, j0, Tk);
-  }
-  cp_commit();
-  while (j0 < Tk) {
-    const int jn = next(j0 + TILE);
-    if (jn < Tk) {
-      load_tile<D>(sKb[cur ^ 1], kb, a.k_tok, jn, Tk);
-      load_tile<D>(sVb[cur ^ 1], vb, a.v_tok, jn, Tk);
-    }
-    cp_commit();
-    cp_wait_prev();
+  for (int j0 = 0; j0 < Tk; j0 += TILE) {
+    if (!all && !tile_may(i0, i1, j0, min(j0 + TILE - 1, Tk - 1), a.L, a.block, a.leak)) continue;
     __syncthreads();
-    const __nv_bfloat16* sK = sKb[cur];
-    const __nv_bfloat16* sV = sVb[cur];
+    load_tile<D>(sK, kb, a.k_tok, j0, Tk);
+    load_tile<D>(sV, vb, a.v_tok, j0, Tk);
+    cp_commit();
+    cp_wait_all();
+    __syncthreads();
     float s[8][4];
     qk_tile<D>(s, sQ, warp * 16, sK);
     float mx[2] = {NEG_INF, NEG_INF};
@@ -269,9 +252,6 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
       o[n][2] *= alpha[1], o[n][3] *= alpha[1];
     }
     pv_tile<D, D>(o, s, sV, 0);
-    __syncthreads();  // every warp is done with this buffer before it is refilled
-    j0 = jn;
-    cur ^= 1;
   }
   // finalize
   const float inv0 = l[0] > 0.f ? 1.f / l[0] : 0.f, inv1 = l[1] > 0.f ? 1.f / l[1] : 0.f;
@@ -298,8 +278,8 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
   extern __shared__ __align__(128) __nv_bfloat16 sm[];
   __nv_bfloat16* sQ = sm;
   __nv_bfloat16* sdO = sm + TILE * D;
-  __nv_bfloat16* sKb[2] = {sm + 2 * TILE * D, sm + 4 * TILE * D};
-  __nv_bfloat16* sVb[2] = {sm + 3 * TILE * D, sm + 5 * TILE * D};
+  __nv_bfloat16* sK = sm + 2 * TILE * D;
+  __nv_bfloat16* sV = sm + 3 * TILE * D;
   const int i0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
@@ -336,28 +316,14 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
   const int i1 = min(i0 + TILE - 1, a.T2 - 1);
-  auto next = [&](int j) {
-    for (; j < a.T2; j += TILE)
-      if (tile_may(i0, i1, j, min(j + TILE - 1, a.T2 - 1), a.L, a.block, a.leak)) break;
-    return j;
-  };
-  int j0 = next(0), cur = 0;
-  if (j0 < a.T2) {
-    load_tile<D>(sKb[0], kb, a.k_tok, j0, a.T2);
-    load_tile<D>(sVb[0], vb, a.v_tok, j0, a.T2);
-  }
-  cp_commit();
-  while (j0 < a.T2) {
-    const int jn = next(j0 + TILE);
-    if (jn < a.T2) {
-      load_tile<D>(sKb[cur ^ 1], kb, a.k_tok, jn, a.T2);
-      load_tile<D>(sVb[cur ^ 1], vb, a.v_tok, jn, a.T2);
-    }
-    cp_commit();
-    cp_wait_prev();
+  for (int j0 = 0; j0 < a.T2; j0 += TILE) {
+    if (!tile_may(i0, i1, j0, min(j0 + TILE - 1, a.T2 - 1), a.L, a.block, a.leak)) continue;
     __syncthreads();
-    const __nv_bfloat16* sK = sKb[cur];
-    const __nv_bfloat16* sV = sVb[cur];
+    load_tile<D>(sK, kb, a.k_tok, j0, a.T2);
+    load_tile<D>(sV, vb, a.v_tok, j0, a.T2);
+    cp_commit();
+    cp_wait_all();
+    __syncthreads();
     float s[8][4], dp[8][4];
     qk_tile<D>(s, sQ, warp * 16, sK);
     qk_tile<D>(dp, sdO, warp * 16, sV);
@@ -371,9 +337,6 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
         s[n][e] = p * (dp[n][e] - (e < 2 ? d0 : d1));  // dS
       }
     pv_tile<D, D>(dq, s, sK, 0);
-    __syncthreads();
-    j0 = jn;
-    cur ^= 1;
   }
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) {
@@ -394,11 +357,10 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
   extern __shared__ __align__(128) __nv_bfloat16 sm[];
   __nv_bfloat16* sK = sm;
   __nv_bfloat16* sV = sm + TILE * D;
-  // two buffers of (Q, dO, lse2, delta): the next query tile streams in while this one is used
-  __nv_bfloat16* sQb[2] = {sm + 2 * TILE * D, sm + 4 * TILE * D};
-  __nv_bfloat16* sdOb[2] = {sm + 3 * TILE * D, sm + 5 * TILE * D};
-  float* sLb[2] = {reinterpret_cast<float*>(sm + 6 * TILE * D), reinterpret_cast<float*>(sm + 6 * TILE * D) + 2 * TILE};
-  float* sDb[2] = {sLb[0] + TILE, sLb[1] + TILE};
+  __nv_bfloat16* sQ = sm + 2 * TILE * D;
+  __nv_bfloat16* sdO = sm + 3 * TILE * D;
+  float* sL = reinterpret_cast<float*>(sm + 4 * TILE * D);  // [64] lse2
+  float* sD = sL + TILE;                                     // [64] delta
   const int j0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hk, hk = blockIdx.y % a.Hk;
   const int d0 = blockIdx.z * DA;
@@ -418,41 +380,23 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
   const int j1 = min(j0 + TILE - 1, a.T2 - 1);
   const int rep = a.Hq / a.Hk;
   const int64_t otok = (int64_t)a.Hq * D;
-  // work items: (q head of this kv head, query tile) in order, skipping tiles that see no key here
-  const int ntq = (a.T2 + TILE - 1) / TILE, nitems = rep * ntq;
-  auto next = [&](int it) {
-    for (; it < nitems; ++it) {
-      const int i0 = (it % ntq) * TILE;
-      if (tile_may(i0, min(i0 + TILE - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak)) break;
-    }
-    return it;
-  };
-  auto fetch = [&](int it, int buf) {  // async Q / dO tiles, plain lse / delta loads
-    const int hq = hk * rep + it / ntq, i0 = (it % ntq) * TILE;
-    load_tile<D>(sQb[buf], a.q + (int64_t)b * a.T2 * a.q_tok + hq * D, a.q_tok, i0, a.T2);
-    load_tile<D>(sdOb[buf], a.dout + (int64_t)b * a.T2 * otok + hq * D, otok, i0, a.T2);
+  for (int hq = hk * rep; hq < (hk + 1) * rep; ++hq) {
+    const __nv_bfloat16* qb = a.q + (int64_t)b * a.T2 * a.q_tok + hq * D;
+    const __nv_bfloat16* dob = a.dout + (int64_t)b * a.T2 * otok + hq * D;
     const float* lse = a.lse2 + ((int64_t)b * a.Hq + hq) * a.T2;
     const float* delta = a.delta + ((int64_t)b * a.Hq + hq) * a.T2;
-    for (int r = threadIdx.x; r < TILE; r += NTH) {
-      sLb[buf][r] = i0 + r < a.T2 ? lse[i0 + r] : 0.f;
-      sDb[buf][r] = i0 + r < a.T2 ? delta[i0 + r] : 0.f;
-    }
-  };
-  int it = next(0), cur = 0;
-  if (it < nitems) fetch(it, 0);
-  cp_commit();
-  while (it < nitems) {
-    const int itn = next(it + 1);
-    if (itn < nitems) fetch(itn, cur ^ 1);
-    cp_commit();
-    cp_wait_prev();
-    __syncthreads();
-    const int i0 = (it % ntq) * TILE;
-    const __nv_bfloat16* sQ = sQb[cur];
-    const __nv_bfloat16* sdO = sdOb[cur];
-    const float* sL = sLb[cur];
-    const float* sD = sDb[cur];
-    {
+    for (int i0 = 0; i0 < a.T2; i0 += TILE) {
+      if (!tile_may(i0, min(i0 + TILE - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak)) continue;
+      __syncthreads();
+      load_tile<D>(sQ, qb, a.q_tok, i0, a.T2);
+      load_tile<D>(sdO, dob, otok, i0, a.T2);
+      cp_commit();
+      for (int r = threadIdx.x; r < TILE; r += NTH) {
+        sL[r] = i0 + r < a.T2 ? lse[i0 + r] : 0.f;
+        sD[r] = i0 + r < a.T2 ? delta[i0 + r] : 0.f;
+      }
+      cp_wait_all();
+      __syncthreads();
       float s[8][4], dp[8][4];
       qk_tile<D>(s, sK, warp * 16, sQ);   // S^T: rows = keys, cols = queries
       qk_tile<D>(dp, sV, warp * 16, sdO);  // dP^T = V dO^T
@@ -469,9 +413,6 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
       pv_tile<D, DA>(dv, s, sdO, d0);
       pv_tile<D, DA>(dk, dp, sQ, d0);
     }
-    __syncthreads();  // this buffer (incl. lse / delta) is refilled next
-    it = itn;
-    cur ^= 1;
   }
 #pragma unroll
   for (int n = 0; n < DA / 8; ++n) {
@@ -573,7 +514,7 @@ static at::Tensor prefix_t(const at::Tensor& q, const at::Tensor& k, const at::T
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse2 = lse.data_ptr<float>();
-  go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 5 * TILE * D * 2, a);
+  go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 3 * TILE * D * 2, a);
   return o;
 }
 
@@ -585,7 +526,7 @@ static std::vector<at::Tensor> fwd_t(const at::Tensor& q, const at::Tensor& k, c
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse2 = lse.data_ptr<float>();
-  go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 5 * TILE * D * 2, a);
+  go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 3 * TILE * D * 2, a);
   return {o, lse};
 }
 
@@ -608,9 +549,9 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
   a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   const int nt = (a.T2 + TILE - 1) / TILE;
-  go(bwd_dq_kernel<D>, dim3(nt, a.B * a.Hq), 6 * TILE * D * 2, a);
+  go(bwd_dq_kernel<D>, dim3(nt, a.B * a.Hq), 4 * TILE * D * 2, a);
   constexpr int DA = D > 128 ? D / 2 : D;
-  go(bwd_dkv_kernel<D, DA>, dim3(nt, a.B * a.Hk, D / DA), 6 * TILE * D * 2 + 4 * TILE * 4, a);
+  go(bwd_dkv_kernel<D, DA>, dim3(nt, a.B * a.Hk, D / DA), 4 * TILE * D * 2 + 2 * TILE * 4, a);
   return {dq, dk, dv};
 }
 

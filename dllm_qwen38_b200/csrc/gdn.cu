@@ -29,7 +29,7 @@
 namespace bdllm {
 namespace gdn {
 
-constexpr int NT = 256;
+constexpr int NT = 512;
 
 struct Args {
   // inputs ([B, 2L, heads, dim] strided views; row stride = token stride)

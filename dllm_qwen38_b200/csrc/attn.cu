@@ -86,10 +86,10 @@ __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_grou
 __device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 // 64 rows x D of a [B*T2, ...] tensor with token stride `tok` (elements) starting at row r0
-template <int D>
+template <int D, int ROWS = TILE>
 __device__ __forceinline__ void load_tile(__nv_bfloat16* s, const __nv_bfloat16* base, int64_t tok, int r0, int T2) {
   constexpr int CH = D / 8;
-  for (int idx = threadIdx.x; idx < TILE * CH; idx += NTH) {
+  for (int idx = threadIdx.x; idx < ROWS * CH; idx += NTH) {
     const int r = idx / CH, c8 = idx % CH;
     const bool ok = r0 + r < T2;
     const __nv_bfloat16* src = base + (int64_t)(ok ? r0 + r : 0) * tok + c8 * 8;
@@ -138,17 +138,17 @@ __device__ __forceinline__ void frag_b_cols(uint32_t (&b)[4], const __nv_bfloat1
   ldsm4t(b, s + sw<D>(k0 + (mi & 1) * 8 + (lane & 7), (n0 >> 3) + (mi >> 1)));
 }
 
-// S[16 x 64] (8 n-tiles) = A(rows of sa starting at ra, all D) * B(rows of sb)^T
-template <int D>
-__device__ __forceinline__ void qk_tile(float (&s)[8][4], const __nv_bfloat16* sa, int ra, const __nv_bfloat16* sb) {
+// S[16 x 8*NN] (NN n-tiles) = A(rows of sa starting at ra, all D) * B(rows of sb)^T
+template <int D, int NN = 8>
+__device__ __forceinline__ void qk_tile(float (&s)[NN][4], const __nv_bfloat16* sa, int ra, const __nv_bfloat16* sb) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+  for (int n = 0; n < NN; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
   for (int kk = 0; kk < D; kk += 16) {
     uint32_t a[4];
     frag_a<D>(a, sa, ra, kk);
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
+    for (int p = 0; p < NN / 2; ++p) {
       uint32_t b[4];
       frag_b_rows<D>(b, sb, p * 16, kk);
       mma(s[2 * p], a, b[0], b[1]);
@@ -157,12 +157,12 @@ __device__ __forceinline__ void qk_tile(float (&s)[8][4], const __nv_bfloat16* s
   }
 }
 
-// acc[DA/8][4] += P(16 x 64, from registers) * B(rows k of sb = 64 keys, cols d0..d0+DA)
-template <int D, int DA>
-__device__ __forceinline__ void pv_tile(float (&acc)[DA / 8][4], const float (&p)[8][4], const __nv_bfloat16* sb,
+// acc[DA/8][4] += P(16 x 8*NN, from registers) * B(rows k of sb = 8*NN keys, cols d0..d0+DA)
+template <int D, int DA, int NN = 8>
+__device__ __forceinline__ void pv_tile(float (&acc)[DA / 8][4], const float (&p)[NN][4], const __nv_bfloat16* sb,
                                         int d0) {
 #pragma unroll
-  for (int kp = 0; kp < 4; ++kp) {
+  for (int kp = 0; kp < NN / 2; ++kp) {
     uint32_t a[4] = {pack(p[2 * kp][0], p[2 * kp][1]), pack(p[2 * kp][2], p[2 * kp][3]),
                      pack(p[2 * kp + 1][0], p[2 * kp + 1][1]), pack(p[2 * kp + 1][2], p[2 * kp + 1][3])};
 #pragma unroll
@@ -273,13 +273,15 @@ __global__ void __launch_bounds__(NTH, 1) fwd_kernel(Args a) {
 }
 
 // ================================================================== backward: dQ
+// key tiles of TK = 32 rows: Q, dO (64 rows) + K, V (32 rows) = 96 KB at D = 256, two CTAs per SM
+constexpr int TK = 32;
 template <int D>
-__global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
+__global__ void __launch_bounds__(NTH, 2) bwd_dq_kernel(Args a) {
   extern __shared__ __align__(128) __nv_bfloat16 sm[];
   __nv_bfloat16* sQ = sm;
   __nv_bfloat16* sdO = sm + TILE * D;
   __nv_bfloat16* sK = sm + 2 * TILE * D;
-  __nv_bfloat16* sV = sm + 3 * TILE * D;
+  __nv_bfloat16* sV = sm + 2 * TILE * D + TK * D;
   const int i0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t4 = lane & 3;
@@ -316,19 +318,19 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) dq[n][0] = dq[n][1] = dq[n][2] = dq[n][3] = 0.f;
   const int i1 = min(i0 + TILE - 1, a.T2 - 1);
-  for (int j0 = 0; j0 < a.T2; j0 += TILE) {
-    if (!tile_may(i0, i1, j0, min(j0 + TILE - 1, a.T2 - 1), a.L, a.block, a.leak)) continue;
+  for (int j0 = 0; j0 < a.T2; j0 += TK) {
+    if (!tile_may(i0, i1, j0, min(j0 + TK - 1, a.T2 - 1), a.L, a.block, a.leak)) continue;
     __syncthreads();
-    load_tile<D>(sK, kb, a.k_tok, j0, a.T2);
-    load_tile<D>(sV, vb, a.v_tok, j0, a.T2);
+    load_tile<D, TK>(sK, kb, a.k_tok, j0, a.T2);
+    load_tile<D, TK>(sV, vb, a.v_tok, j0, a.T2);
     cp_commit();
     cp_wait_all();
     __syncthreads();
-    float s[8][4], dp[8][4];
-    qk_tile<D>(s, sQ, warp * 16, sK);
-    qk_tile<D>(dp, sdO, warp * 16, sV);
+    float s[TK / 8][4], dp[TK / 8][4];
+    qk_tile<D, TK / 8>(s, sQ, warp * 16, sK);
+    qk_tile<D, TK / 8>(dp, sdO, warp * 16, sV);
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < TK / 8; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int row = e < 2 ? r0 : r1, col = j0 + n * 8 + t4 * 2 + (e & 1);
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
         const float p = ok ? exp2f(s[n][e] * a.scale_log2 - (e < 2 ? l0 : l1)) : 0.f;
         s[n][e] = p * (dp[n][e] - (e < 2 ? d0 : d1));  // dS
       }
-    pv_tile<D, D>(dq, s, sK, 0);
+    pv_tile<D, D, TK / 8>(dq, s, sK, 0);
   }
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) {
@@ -352,15 +354,17 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dq_kernel(Args a) {
 
 // ================================================================== backward: dK, dV
 // CTA = 64 keys of one kv head; blockIdx.z selects the head-dim slice [z*DA, (z+1)*DA) of dK/dV.
+// query tiles of TQ = 32 rows: K, V (64 rows) + Q, dO (32 rows) = 96 KB at D = 256, two CTAs per SM
+constexpr int TQ = 32;
 template <int D, int DA>
-__global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
+__global__ void __launch_bounds__(NTH, 2) bwd_dkv_kernel(Args a) {
   extern __shared__ __align__(128) __nv_bfloat16 sm[];
   __nv_bfloat16* sK = sm;
   __nv_bfloat16* sV = sm + TILE * D;
   __nv_bfloat16* sQ = sm + 2 * TILE * D;
-  __nv_bfloat16* sdO = sm + 3 * TILE * D;
-  float* sL = reinterpret_cast<float*>(sm + 4 * TILE * D);  // [64] lse2
-  float* sD = sL + TILE;                                     // [64] delta
+  __nv_bfloat16* sdO = sm + 2 * TILE * D + TQ * D;
+  float* sL = reinterpret_cast<float*>(sm + 2 * TILE * D + 2 * TQ * D);  // [TQ] lse2
+  float* sD = sL + TQ;                                                   // [TQ] delta
   const int j0 = blockIdx.x * TILE;
   const int b = blockIdx.y / a.Hk, hk = blockIdx.y % a.Hk;
   const int d0 = blockIdx.z * DA;
@@ -385,23 +389,23 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
     const __nv_bfloat16* dob = a.dout + (int64_t)b * a.T2 * otok + hq * D;
     const float* lse = a.lse2 + ((int64_t)b * a.Hq + hq) * a.T2;
     const float* delta = a.delta + ((int64_t)b * a.Hq + hq) * a.T2;
-    for (int i0 = 0; i0 < a.T2; i0 += TILE) {
-      if (!tile_may(i0, min(i0 + TILE - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak)) continue;
+    for (int i0 = 0; i0 < a.T2; i0 += TQ) {
+      if (!tile_may(i0, min(i0 + TQ - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak)) continue;
       __syncthreads();
-      load_tile<D>(sQ, qb, a.q_tok, i0, a.T2);
-      load_tile<D>(sdO, dob, otok, i0, a.T2);
+      load_tile<D, TQ>(sQ, qb, a.q_tok, i0, a.T2);
+      load_tile<D, TQ>(sdO, dob, otok, i0, a.T2);
       cp_commit();
-      for (int r = threadIdx.x; r < TILE; r += NTH) {
+      for (int r = threadIdx.x; r < TQ; r += NTH) {
         sL[r] = i0 + r < a.T2 ? lse[i0 + r] : 0.f;
         sD[r] = i0 + r < a.T2 ? delta[i0 + r] : 0.f;
       }
       cp_wait_all();
       __syncthreads();
-      float s[8][4], dp[8][4];
-      qk_tile<D>(s, sK, warp * 16, sQ);   // S^T: rows = keys, cols = queries
-      qk_tile<D>(dp, sV, warp * 16, sdO);  // dP^T = V dO^T
+      float s[TQ / 8][4], dp[TQ / 8][4];
+      qk_tile<D, TQ / 8>(s, sK, warp * 16, sQ);   // S^T: rows = keys, cols = queries
+      qk_tile<D, TQ / 8>(dp, sV, warp * 16, sdO);  // dP^T = V dO^T
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < TQ / 8; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int key = e < 2 ? k0 : k1, qi = n * 8 + t4 * 2 + (e & 1), row = i0 + qi;
@@ -410,8 +414,8 @@ __global__ void __launch_bounds__(NTH, 1) bwd_dkv_kernel(Args a) {
           s[n][e] = p;                       // P^T
           dp[n][e] = p * (dp[n][e] - sD[qi]);  // dS^T
         }
-      pv_tile<D, DA>(dv, s, sdO, d0);
-      pv_tile<D, DA>(dk, dp, sQ, d0);
+      pv_tile<D, DA, TQ / 8>(dv, s, sdO, d0);
+      pv_tile<D, DA, TQ / 8>(dk, dp, sQ, d0);
     }
   }
 #pragma unroll
@@ -549,9 +553,9 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
   a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   const int nt = (a.T2 + TILE - 1) / TILE;
-  go(bwd_dq_kernel<D>, dim3(nt, a.B * a.Hq), 4 * TILE * D * 2, a);
+  go(bwd_dq_kernel<D>, dim3(nt, a.B * a.Hq), (2 * TILE + 2 * TK) * D * 2, a);
   constexpr int DA = D > 128 ? D / 2 : D;
-  go(bwd_dkv_kernel<D, DA>, dim3(nt, a.B * a.Hk, D / DA), 4 * TILE * D * 2 + 2 * TILE * 4, a);
+  go(bwd_dkv_kernel<D, DA>, dim3(nt, a.B * a.Hk, D / DA), (2 * TILE + 2 * TQ) * D * 2 + 2 * TQ * 4, a);
   return {dq, dk, dv};
 }
 

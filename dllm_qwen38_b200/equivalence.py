@@ -8,9 +8,10 @@ Answers with numbers (the reference's `equivalence.py:1-12` contract):
   4. does every deliberate fault (concat-causal-gdn / mask-leak / no-conv-prefix) turn check 1 red?
 
 Exit 0 = every check passed AND every fault was detected; 1 = a check failed or a fault went
-undetected; 2 = could not measure. The candidate runs through the op layer (CUDA kernels for
-``--device cuda``); the oracle always runs the fp32 reference ops with the token-by-token delta
-rule, on the host when the candidate is on the GPU.
+undetected; 2 = could not measure. The candidate runs through the op layer (the sm_100a kernels
+for ``--device cuda --dtype bfloat16``; fp32 torch ops on the device for ``--dtype float32``,
+since the kernels compute in bf16); the oracle always runs the fp32 reference ops with the
+token-by-token delta rule on its own fp32 copy (``--oracle-device``, default the candidate's).
 
     python -m dllm_qwen38_b200.equivalence [--model tiny] [--block 32 --nblocks 4] [--device cuda]
 """
@@ -110,6 +111,7 @@ def main(argv=None) -> int:
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--device", default="cpu")
     p.add_argument("--oracle-gdn", default="recurrent", choices=["recurrent", "chunk"])
+    p.add_argument("--oracle-device", default=None, help="where the fp32 oracle runs (default: --device)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--json", default=None)
     a = p.parse_args(argv)
@@ -131,10 +133,18 @@ def main(argv=None) -> int:
         print("COULD-NOT-MEASURE --layers exceeds the model", file=sys.stderr)
         return 2
     oracle_model = model
-    if a.device != "cpu":  # the oracle runs the fp32 reference ops on the host
-        oracle_model = copy.deepcopy(model).to("cpu", torch.float32)
-    rep = run(model, block=a.block, nblocks=a.nblocks, layers=None, tol=tol, change_floor=floor, seed=a.seed,
-              device=a.device, oracle_model=oracle_model, batch=a.batch, oracle_gdn=a.oracle_gdn)
+    odev = a.oracle_device or a.device
+    if a.device != "cpu" or dtype != torch.float32:  # the oracle: fp32 reference ops on its own copy
+        oracle_model = copy.deepcopy(model).to(odev, torch.float32)
+    import contextlib
+
+    from . import ops
+
+    # the sm_100a kernels compute in bf16: an fp32 gate on a GPU runs the fp32 torch ops there
+    ctx = ops.torch_on_cuda(*ops.ALL_OPS) if (a.device != "cpu" and dtype == torch.float32) else contextlib.nullcontext()
+    with ctx:
+        rep = run(model, block=a.block, nblocks=a.nblocks, layers=None, tol=tol, change_floor=floor, seed=a.seed,
+                  device=a.device, oracle_model=oracle_model, batch=a.batch, oracle_gdn=a.oracle_gdn)
     rep["model"] = a.model
     if spare:
         rep["vocab"] = spare

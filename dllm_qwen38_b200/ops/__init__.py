@@ -53,6 +53,11 @@ def _nat():
 
 _LEVERS: set = set()
 
+# every op family with a native kernel (the native kernels compute in bf16; fp32 runs on a CUDA
+# device go through torch_on_cuda(*ALL_OPS))
+ALL_OPS = ("rmsnorm", "linear", "mlp", "gated_rmsnorm", "conv", "gdn_gates", "gdn_core", "attention",
+           "qk_norm_rope", "masked_ce", "embedding")
+
 
 class torch_on_cuda:
     """Context manager: run the named ops through their torch path on the device (recorded as

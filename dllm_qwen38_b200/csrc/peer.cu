@@ -165,17 +165,6 @@ struct Adam {
   float lr, b1, b2, eps, wd, bc1, bc2;
 };
 
-__device__ __forceinline__ void adam_update(const Adam& A, int64_t i, float g) {
-  float wi = A.w[i];
-  if (A.wd != 0.f) wi *= 1.f - A.lr * A.wd;
-  const float mi = A.b1 * A.m[i] + (1.f - A.b1) * g;
-  const float vi = A.b2 * A.v[i] + (1.f - A.b2) * g * g;
-  A.m[i] = mi;
-  A.v[i] = vi;
-  wi -= A.lr * (mi / A.bc1) / (sqrtf(vi / A.bc2) + A.eps);
-  A.w[i] = wi;
-  A.p[i] = __float2bfloat16(wi);
-}
 
 // out[i] = scale * sum_p in_p[rank * shard + i] (fp32), sq += sum_i out[i]^2; with A.w set, the
 // AdamW update of element i is applied right away instead (out may then be null).
@@ -226,9 +215,40 @@ __global__ void __launch_bounds__(512) reduce_scatter_kernel(Ptrs peers, int wor
         s[e] *= scale;
         acc2 += s[e] * s[e];
       }
-      if (A.w != nullptr) {
+      if (A.w != nullptr) {  // vectorised AdamW on EPV consecutive elements
+        const int64_t i0 = v * EPV;
+        float w[8], m[8], vv[8];
 #pragma unroll
-        for (int e = 0; e < EPV; ++e) adam_update(A, v * EPV + e, s[e]);
+        for (int q = 0; q < EPV / 4; ++q) {
+          const float4 a4 = reinterpret_cast<const float4*>(A.w + i0)[q];
+          const float4 m4 = reinterpret_cast<const float4*>(A.m + i0)[q];
+          const float4 v4 = reinterpret_cast<const float4*>(A.v + i0)[q];
+          w[4 * q] = a4.x, w[4 * q + 1] = a4.y, w[4 * q + 2] = a4.z, w[4 * q + 3] = a4.w;
+          m[4 * q] = m4.x, m[4 * q + 1] = m4.y, m[4 * q + 2] = m4.z, m[4 * q + 3] = m4.w;
+          vv[4 * q] = v4.x, vv[4 * q + 1] = v4.y, vv[4 * q + 2] = v4.z, vv[4 * q + 3] = v4.w;
+        }
+        __nv_bfloat16 pb[8];
+#pragma unroll
+        for (int e = 0; e < EPV; ++e) {
+          float wi = w[e];
+          if (A.wd != 0.f) wi *= 1.f - A.lr * A.wd;
+          m[e] = A.b1 * m[e] + (1.f - A.b1) * s[e];
+          vv[e] = A.b2 * vv[e] + (1.f - A.b2) * s[e] * s[e];
+          wi -= A.lr * (m[e] / A.bc1) / (sqrtf(vv[e] / A.bc2) + A.eps);
+          w[e] = wi;
+          pb[e] = __float2bfloat16(wi);
+        }
+#pragma unroll
+        for (int q = 0; q < EPV / 4; ++q) {
+          reinterpret_cast<float4*>(A.w + i0)[q] = make_float4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          reinterpret_cast<float4*>(A.m + i0)[q] = make_float4(m[4 * q], m[4 * q + 1], m[4 * q + 2], m[4 * q + 3]);
+          reinterpret_cast<float4*>(A.v + i0)[q] =
+              make_float4(vv[4 * q], vv[4 * q + 1], vv[4 * q + 2], vv[4 * q + 3]);
+        }
+        if constexpr (EPV == 8)
+          *reinterpret_cast<uint4*>(A.p + i0) = *reinterpret_cast<const uint4*>(pb);
+        else
+          *reinterpret_cast<uint2*>(A.p + i0) = *reinterpret_cast<const uint2*>(pb);
       } else {
         float4* o = reinterpret_cast<float4*>(out + v * EPV);
         o[0] = make_float4(s[0], s[1], s[2], s[3]);

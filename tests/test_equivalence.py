@@ -72,6 +72,9 @@ def test_model_matches_huggingface_qwen3_5():
     states on a plain block-causal forward: the model definition is HF's math."""
     import pytest
 
+    if torch.cuda.is_available():  # HF then routes CPU tensors to its Triton fast path
+        pytest.skip("host-only parity check")
+
     from dllm_qwen38_b200.models.oracle import hf_text_model, plain_forward
     from dllm_qwen38_b200.ops import reference as ref
 

@@ -98,10 +98,7 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  // the peer epilogue transposes each 32 x 32 fp32 block through smem (one buffer per epilogue
-  // warp) so that remote stores are whole 128-byte row segments
-  static constexpr int XPOSE = (EPI == EPI_PEER_F32) ? 4 * 32 * 33 * 4 : 0;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256 + XPOSE;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
 };
@@ -454,24 +451,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
           }
         } else if constexpr (EPI == EPI_PEER_F32) {
-          // lane = row holds 32 columns; write them to smem, then store row by row with lane =
-          // column: each store instruction is one contiguous 128-byte segment of one row
-          float* xp = reinterpret_cast<float*>(smem + STAGES * C_::STAGE_BYTES + 256) + (quad * 32) * 33;
+          // lane = row: 16-byte stores of this row's 32 columns into the owner's slot (a transposed,
+          // row-contiguous variant measured slower over NVLink)
+          if (row_ok) {
+            const int owner = row / args.rows_per_rank, lr = row - owner * args.rows_per_rank;
+            const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
+            float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
+                         (slot * args.rows_per_rank + lr) * args.ldc + col0;
+            if (col0 + 32 <= args.N) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) xp[lane * 33 + j] = v[j];
-          __syncwarp();
-          const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
-          const int row_base = tm * BM + quad * 32;
-          for (int r = 0; r < 32; ++r) {
-            const int rr = row_base + r;
-            if (rr < args.M && col0 + lane < args.N) {
-              const int owner = rr / args.rows_per_rank, lr = rr - owner * args.rows_per_rank;
-              float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
-                           (slot * args.rows_per_rank + lr) * args.ldc + col0;
-              out[lane] = xp[r * 33 + lane];
+              for (int j = 0; j < 32; j += 4)
+                *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.N) out[j] = v[j];
             }
           }
-          __syncwarp();
         } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
           if (row_ok) {
             float* out = reinterpret_cast<float*>(args.C) + split_off + (size_t)row * args.ldc + col0;

@@ -333,6 +333,50 @@ def masked_ce_sum(hidden, w, targets):
 # ----------------------------------------------------------------------------- GDN
 
 
+class ActStore:
+    """Selective activation saving across activation checkpointing: in "save" mode the GDN core
+    and attention forwards keep their outputs (and the state snapshots / log-sum-exps their
+    backward needs) per layer; in "reuse" mode the recomputation inside the backward returns them
+    instead of running those kernels again. Keyed by layer, consumed in call order."""
+
+    mode = None
+    key = None
+    data: dict = {}
+    pos = 0
+
+    @classmethod
+    def begin(cls, mode: str, key) -> None:
+        cls.mode, cls.key, cls.pos = mode, key, 0
+        if mode == "save":
+            cls.data[key] = []
+
+    @classmethod
+    def end(cls) -> None:
+        if cls.mode == "reuse":
+            cls.data.pop(cls.key, None)
+        cls.mode = cls.key = None
+
+    @classmethod
+    def take(cls):
+        if cls.mode != "reuse":
+            return None
+        saved = cls.data.get(cls.key)
+        if saved is None or cls.pos >= len(saved):
+            return None
+        cls.pos += 1
+        return saved[cls.pos - 1]
+
+    @classmethod
+    def put(cls, *ts) -> None:
+        if cls.mode == "save":
+            cls.data[cls.key].append(ts)
+
+    @classmethod
+    def clear(cls) -> None:
+        cls.data.clear()
+        cls.mode = cls.key = None
+
+
 class _GDNCore(torch.autograd.Function):
     """State-fork chunked gated delta rule over the [B, 2L] layout (chunk = block). q, k
     [B, 2L, Hk, Dk] and v [B, 2L, Hv, Dv] may be strided views of the conv output; g, beta
@@ -342,8 +386,13 @@ class _GDNCore(torch.autograd.Function):
     def forward(ctx, q, k, v, g, beta, L, block, concat):
         gf = g.float().contiguous()
         bf = beta.float().contiguous()
-        o, S_in, _ = _C.gdn_fwd(q, k, v, gf, bf, L, block, concat)
-        _count(3)
+        saved = ActStore.take()
+        if saved is not None:
+            o, S_in = saved
+        else:
+            o, S_in, _ = _C.gdn_fwd(q, k, v, gf, bf, L, block, concat)
+            _count(3)
+            ActStore.put(o, S_in)
         ctx.save_for_backward(q, k, v, gf, bf, S_in)
         ctx.cfg = (L, block, concat)
         ctx.dtypes = (g.dtype, beta.dtype)
@@ -429,8 +478,13 @@ def gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode):
 class _Attention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, L, block, scale, leak):
-        o, lse = _C.attn_fwd(q, k, v, L, block, scale, leak)
-        _count()
+        saved = ActStore.take()
+        if saved is not None:
+            o, lse = saved
+        else:
+            o, lse = _C.attn_fwd(q, k, v, L, block, scale, leak)
+            _count()
+            ActStore.put(o, lse)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.cfg = (L, block, scale, leak)
         return o

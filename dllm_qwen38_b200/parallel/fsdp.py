@@ -231,6 +231,13 @@ class FSDPEngine:
             self._pending = None
         self.comm = torch.cuda.Stream(device=self.device) if self.device.type == "cuda" else None
         self.anchor = torch.zeros((), device=self.device, requires_grad=True)
+        # keep the GDN core / attention outputs of the checkpointed forward for the backward's
+        # recomputation (about 0.5 GB per GDN layer at L 4096: the fp32 block states)
+        self.save_cores = self.device.type == "cuda" and os.environ.get("BDLLM_SAVE_CORES", "1") != "0"
+        if self.save_cores:
+            from ..ops import cuda as Cu
+
+            self.act_store = Cu.ActStore
         if self.peer is not None:  # every shard written before any peer reads one
             torch.cuda.synchronize(self.device)
             dist.barrier()
@@ -575,11 +582,16 @@ class _LayerFn(torch.autograd.Function):
         layer = engine.model.text_model.layers[i]
         params, fused = engine.leaves(unit, buf, None)
         _bind(layer, fused)
+        save = engine.save_cores and h.is_cuda
         try:
+            if save:
+                engine.act_store.begin("save", i)
             with nvtx(f"layer{i}.fwd"), torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], h, L, block, engine.cfg.gdn_chunk_size, cos, sin,
                                  fault)
         finally:
+            if save:
+                engine.act_store.end()
             _unbind(layer, fused)
         engine.check_gathered()
         ctx.save_for_backward(h, cos, sin)
@@ -599,13 +611,20 @@ class _LayerFn(torch.autograd.Function):
         layer = engine.model.text_model.layers[i]
         hx = h.detach().requires_grad_(True)
         _bind(layer, fused)
+        reuse = engine.save_cores and hx.is_cuda
         try:
+            if reuse:  # the recomputation takes the saved core outputs instead of rerunning them
+                engine.act_store.begin("reuse", i)
             with nvtx(f"layer{i}.bwd"), torch.enable_grad(), \
                     torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], hx, L, block, engine.cfg.gdn_chunk_size, cos, sin,
                                  fault)
+                if reuse:
+                    engine.act_store.end()
                 torch.autograd.backward(out, dout)
         finally:
+            if reuse:
+                engine.act_store.end()
             _unbind(layer, fused)
         engine.check_gathered()
         engine.reduce_scatter(unit, grad)

@@ -1,0 +1,41 @@
+"""The sharded engine on one GPU: keeping the GDN core / attention outputs of the checkpointed
+forward for the backward's recomputation changes nothing in the result."""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(save: str):
+    from dllm_qwen38_b200.config import preset
+    from dllm_qwen38_b200.models.qwen35 import build_model
+    from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+
+    os.environ["BDLLM_SAVE_CORES"] = save
+    cfg = preset("tiny", hidden_size=256, intermediate_size=512, linear_key_head_dim=64, linear_value_head_dim=64,
+                 head_dim=64)
+    tr = FSDPTrainer(build_model(cfg, seed=0, device="cuda", dtype=torch.bfloat16), block=32, mask_id=cfg.mask_id,
+                     lr=1e-4)
+    assert tr.engine.save_cores == (save == "1")
+    g = torch.Generator().manual_seed(11)
+    losses = []
+    for _ in range(3):
+        x0 = torch.randint(0, cfg.mask_id, (2, 128), generator=g)
+        losses.append(float(tr.step(x0, torch.zeros(2, dtype=torch.long), torch.full((2,), 128, dtype=torch.long))))
+    return losses, {k: v.float().cpu() for k, v in tr.engine.full_state().items()}
+
+
+def test_saved_core_outputs_match_recomputation():
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    try:
+        la, sa = _run("1")
+        lb, sb = _run("0")
+    finally:
+        os.environ.pop("BDLLM_SAVE_CORES", None)
+        Cu.ActStore.clear()
+    assert max(abs(a - b) for a, b in zip(la, lb)) < 1e-4 * max(1.0, abs(la[0]))
+    assert max(float((sa[k] - sb[k]).abs().max()) for k in sa) < 1e-3

@@ -1013,6 +1013,7 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   BDLLM_GEMM_CASE(256, true, true, EPI_F32)
   BDLLM_GEMM_CASE(256, true, true, EPI_ACC_F32)
   BDLLM_GEMM_CASE(256, true, true, EPI_BF16)
+  BDLLM_GEMM_CASE(256, true, true, EPI_ADD_BF16)
   BDLLM_GEMM_CASE(128, false, false, EPI_BF16)
   BDLLM_GEMM_CASE(128, false, false, EPI_F32)
   BDLLM_GEMM_CASE(128, false, true, EPI_BF16)

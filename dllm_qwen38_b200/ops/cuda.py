@@ -122,6 +122,22 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
     return out
 
 
+def wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor):
+    """Weight gradient dy^T x for leaf weight `w`. When `w.grad` is a preset bf16 buffer (the
+    sharded engine's flat gradient views) the GEMM epilogue adds into it in place (one rounding,
+    no fp32 temporary) and None is returned; otherwise the gradient tensor."""
+    g = w.grad if (w.is_leaf and w.requires_grad) else None
+    if g is not None and g.dtype == torch.bfloat16 and g.shape == w.shape and g.stride(-1) == 1 \
+            and g.dim() == 2 and g.stride(0) % 8 == 0 and g.data_ptr() % 16 == 0:
+        K, M = dy2.shape
+        N = x2.shape[1]
+        _C.gemm(dy2, True, dy2.stride(0), x2, True, x2.stride(0), M, N, K, g, g.stride(0), EPI_ADD_BF16, g,
+                g.stride(0), None, 256, 1.0)
+        _count()
+        return None
+    return gemm_tn(dy2, x2, out_dtype=torch.float32).to(w.dtype)
+
+
 def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, F: int, store_gu: bool):
     """act[M, F] = silu(x Wg^T) * (x Wu^T) with w_gate_up = [Wg; Wu] ([2F, K], contiguous rows).
     Returns (act, gu) where gu [M, 2F] holds the bf16 (gate | up) when store_gu."""
@@ -156,7 +172,7 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[0]:
             dx = gemm_nn(dy2, w).reshape(x.shape)
         if ctx.needs_input_grad[1]:
-            dw = gemm_tn(dy2, _c2(x), out_dtype=torch.float32).to(w.dtype)
+            dw = wgrad(dy2, _c2(x), w)
         return dx, dw
 
 
@@ -260,8 +276,8 @@ class _SwiGLUMLP(torch.autograd.Function):
         dgu = _C.dswiglu(dact, gu)
         _count()
         dx = gemm_nn(dgu, w_gu).reshape(x.shape)
-        dw_gu = gemm_tn(dgu, x2, out_dtype=torch.float32).to(w_gu.dtype)
-        dw_down = gemm_tn(dy2, act, out_dtype=torch.float32).to(w_down.dtype)
+        dw_gu = wgrad(dgu, x2, w_gu) if ctx.needs_input_grad[1] else None
+        dw_down = wgrad(dy2, act, w_down) if ctx.needs_input_grad[2] else None
         return dx, dw_gu, dw_down
 
 

@@ -194,6 +194,143 @@ __device__ bool ag_wait_range(const GemmArgs& a, int64_t lo, int64_t hi, volatil
   return true;
 }
 
+// Epilogue of one accumulator tile for the thread's row: TMEM columns -> the epilogue op -> global.
+// t_row: this warp's TMEM lane quadrant at the accumulator's first column; n0: first output
+// column; split_off / t / mn_tiles / ksplit: the k-split bookkeeping of the tile.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_row, int row, bool row_ok, int n0,
+                                              int64_t split_off, int t, int mn_tiles, int ksplit, int lane) {
+  constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  (void)lane;
+#pragma unroll 1
+  for (int c = 0; c < BN_OUT / 32; ++c) {
+    float v[32];
+    tmem_ld32(t_row + c * 32, v);
+    if (args.alpha != 1.f) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
+    }
+    const int col0 = n0 + c * 32;
+    if constexpr (EPI == EPI_SWIGLU) {
+      float u[32];
+      tmem_ld32(t_row + BN / 2 + c * 32, u);
+      if (row_ok) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
+        __nv_bfloat16* gu = args.GU ? args.GU + (size_t)row * args.ldgu + col0 : nullptr;
+        if (col0 + 32 <= args.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 pk, pg, pu;
+            __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+            __nv_bfloat162* g2 = reinterpret_cast<__nv_bfloat162*>(&pg);
+            __nv_bfloat162* u2 = reinterpret_cast<__nv_bfloat162*>(&pu);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              // the activation uses the bf16-rounded gate/up so that backward (which reads the
+              // stored bf16 gate/up) differentiates exactly the function forward computed
+              __nv_bfloat162 gb = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+              __nv_bfloat162 ub = __floats2bfloat162_rn(u[j + 2 * e], u[j + 2 * e + 1]);
+              float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
+              p2[e] = __floats2bfloat162_rn(silu_f(gf.x) * uf.x, silu_f(gf.y) * uf.y);
+              g2[e] = gb;
+              u2[e] = ub;
+            }
+            *reinterpret_cast<uint4*>(out + j) = pk;
+            if (gu) {
+              *reinterpret_cast<uint4*>(gu + j) = pg;
+              *reinterpret_cast<uint4*>(gu + args.N + j) = pu;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < args.N) {
+              float g = __bfloat162float(__float2bfloat16(v[j])), uu = __bfloat162float(__float2bfloat16(u[j]));
+              out[j] = __float2bfloat16(silu_f(g) * uu);
+              if (gu) {
+                gu[j] = __float2bfloat16(g);
+                gu[args.N + j] = __float2bfloat16(uu);
+              }
+            }
+          }
+        }
+      }
+    } else if constexpr (EPI == EPI_PEER_F32) {
+      // lane = row: 16-byte stores of this row's 32 columns into the owner's slot (a transposed,
+      // row-contiguous variant measured slower over NVLink)
+      if (row_ok) {
+        const int owner = row / args.rows_per_rank, lr = row - owner * args.rows_per_rank;
+        const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
+        float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
+                     (slot * args.rows_per_rank + lr) * args.ldc + col0;
+        if (col0 + 32 <= args.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < args.N) out[j] = v[j];
+        }
+      }
+    } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
+      if (row_ok) {
+        float* out = reinterpret_cast<float*>(args.C) + split_off + (size_t)row * args.ldc + col0;
+        if (col0 + 32 <= args.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            if constexpr (EPI == EPI_ACC_F32) {
+              float4 p = *reinterpret_cast<float4*>(out + j);
+              o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
+            }
+            *reinterpret_cast<float4*>(out + j) = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < args.N) out[j] = (EPI == EPI_ACC_F32 ? out[j] : 0.f) + v[j];
+        }
+      }
+    } else {  // EPI_BF16 / EPI_ADD_BF16
+      if (row_ok) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
+        const __nv_bfloat16* res =
+            (EPI == EPI_ADD_BF16) ? reinterpret_cast<const __nv_bfloat16*>(args.R) + (size_t)row * args.ldr + col0
+                                  : nullptr;
+        if (col0 + 32 <= args.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            uint4 pk;
+            __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+            if constexpr (EPI == EPI_ADD_BF16) {
+              uint4 rr = *reinterpret_cast<const uint4*>(res + j);
+              const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 rf = __bfloat1622float2(r2[e]);
+                p2[e] = __floats2bfloat162_rn(v[j + 2 * e] + rf.x, v[j + 2 * e + 1] + rf.y);
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
+            }
+            *reinterpret_cast<uint4*>(out + j) = pk;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (col0 + j < args.N) {
+              float r = (EPI == EPI_ADD_BF16) ? __bfloat162float(res[j]) : 0.f;
+              out[j] = __float2bfloat16(v[j] + r);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs args) {
@@ -397,133 +534,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int n0 = tn * C_::BN_OUT;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
       const bool row_ok = row < args.M;
-#pragma unroll 1
-      for (int c = 0; c < C_::BN_OUT / 32; ++c) {
-        float v[32];
-        tmem_ld32(t_row + c * 32, v);
-        if (args.alpha != 1.f) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
-        }
-        const int col0 = n0 + c * 32;
-        if constexpr (EPI == EPI_SWIGLU) {
-          float u[32];
-          tmem_ld32(t_row + BN / 2 + c * 32, u);
-          if (row_ok) {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
-            __nv_bfloat16* gu = args.GU ? args.GU + (size_t)row * args.ldgu + col0 : nullptr;
-            if (col0 + 32 <= args.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk, pg, pu;
-                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-                __nv_bfloat162* g2 = reinterpret_cast<__nv_bfloat162*>(&pg);
-                __nv_bfloat162* u2 = reinterpret_cast<__nv_bfloat162*>(&pu);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  // the activation uses the bf16-rounded gate/up so that backward (which reads the
-                  // stored bf16 gate/up) differentiates exactly the function forward computed
-                  __nv_bfloat162 gb = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
-                  __nv_bfloat162 ub = __floats2bfloat162_rn(u[j + 2 * e], u[j + 2 * e + 1]);
-                  float2 gf = __bfloat1622float2(gb), uf = __bfloat1622float2(ub);
-                  p2[e] = __floats2bfloat162_rn(silu_f(gf.x) * uf.x, silu_f(gf.y) * uf.y);
-                  g2[e] = gb;
-                  u2[e] = ub;
-                }
-                *reinterpret_cast<uint4*>(out + j) = pk;
-                if (gu) {
-                  *reinterpret_cast<uint4*>(gu + j) = pg;
-                  *reinterpret_cast<uint4*>(gu + args.N + j) = pu;
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (col0 + j < args.N) {
-                  float g = __bfloat162float(__float2bfloat16(v[j])), uu = __bfloat162float(__float2bfloat16(u[j]));
-                  out[j] = __float2bfloat16(silu_f(g) * uu);
-                  if (gu) {
-                    gu[j] = __float2bfloat16(g);
-                    gu[args.N + j] = __float2bfloat16(uu);
-                  }
-                }
-              }
-            }
-          }
-        } else if constexpr (EPI == EPI_PEER_F32) {
-          // lane = row: 16-byte stores of this row's 32 columns into the owner's slot (a transposed,
-          // row-contiguous variant measured slower over NVLink)
-          if (row_ok) {
-            const int owner = row / args.rows_per_rank, lr = row - owner * args.rows_per_rank;
-            const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
-            float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
-                         (slot * args.rows_per_rank + lr) * args.ldc + col0;
-            if (col0 + 32 <= args.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < args.N) out[j] = v[j];
-            }
-          }
-        } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
-          if (row_ok) {
-            float* out = reinterpret_cast<float*>(args.C) + split_off + (size_t)row * args.ldc + col0;
-            if (col0 + 32 <= args.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) {
-                float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                if constexpr (EPI == EPI_ACC_F32) {
-                  float4 p = *reinterpret_cast<float4*>(out + j);
-                  o.x += p.x, o.y += p.y, o.z += p.z, o.w += p.w;
-                }
-                *reinterpret_cast<float4*>(out + j) = o;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < args.N) out[j] = (EPI == EPI_ACC_F32 ? out[j] : 0.f) + v[j];
-            }
-          }
-        } else {  // EPI_BF16 / EPI_ADD_BF16
-          if (row_ok) {
-            __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
-            const __nv_bfloat16* res =
-                (EPI == EPI_ADD_BF16) ? reinterpret_cast<const __nv_bfloat16*>(args.R) + (size_t)row * args.ldr + col0
-                                      : nullptr;
-            if (col0 + 32 <= args.N) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 8) {
-                uint4 pk;
-                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
-                if constexpr (EPI == EPI_ADD_BF16) {
-                  uint4 rr = *reinterpret_cast<const uint4*>(res + j);
-                  const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&rr);
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    float2 rf = __bfloat1622float2(r2[e]);
-                    p2[e] = __floats2bfloat162_rn(v[j + 2 * e] + rf.x, v[j + 2 * e + 1] + rf.y);
-                  }
-                } else {
-#pragma unroll
-                  for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[j + 2 * e], v[j + 2 * e + 1]);
-                }
-                *reinterpret_cast<uint4*>(out + j) = pk;
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (col0 + j < args.N) {
-                  float r = (EPI == EPI_ADD_BF16) ? __bfloat162float(res[j]) : 0.f;
-                  out[j] = __float2bfloat16(v[j] + r);
-                }
-              }
-            }
-          }
-        }
-      }
+      epilogue_tile<BN, EPI>(args, t_row, row, row_ok, n0, split_off, t, mn_tiles, ksplit, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -553,6 +564,230 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tp_st_release(tp_flag(args.peers[p], args.flag_off, TP_SLOT_RS, args.rank), seq);
       }
     }
+  }
+}
+
+// ============================================================================== 2-CTA variant
+// A CTA pair (cluster of 2, cta_group::2) computes 256 x 256 tiles: CTA rank r of the pair loads A
+// rows [m0 + 128 r, +128) and B rows [n0 + 128 r, +128) (for SwiGLU: rank 0 the gate rows, rank 1
+// the up rows) into its own smem; the leader (rank 0) issues M = 256, N = 256 MMAs that read both
+// CTAs' tiles, and each CTA's TMEM receives its 128 rows x 256 columns. Per SM this halves the B
+// operand traffic of the one-CTA 128 x 256 tile and leaves room for 6 pipeline stages. K-major A
+// and B only (the forward projections). Both CTAs' TMA loads complete on the leader's full
+// barriers; the leader's MMA commits arrive on both CTAs' empty / tfull barriers; both CTAs'
+// epilogue warps arrive on the leader's tempty barriers. Every wait is bounded as in gemm_kernel;
+// all paths reach the final cluster barrier.
+constexpr int STAGES2 = 6;
+template <int EPI>
+struct Cfg2 {
+  static constexpr int BN = 256;  // MMA N (both CTAs' B halves)
+  static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? 128 : 256;
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SMEM = STAGES2 * STAGE_BYTES + 1024 + 256;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr uint32_t IDESC = idesc_bf16(256, 256, 0, 0);
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void commit2(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+__device__ __forceinline__ void arrive_remote(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t leader_bar, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs args) {
+  using C_ = Cfg2<EPI>;
+  constexpr int STAGES = STAGES2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * C_::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t crank = cluster_rank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_m = (args.M + 255) / 256;
+  const int tiles_n = (args.N + C_::BN_OUT - 1) / C_::BN_OUT;
+  const int num_tiles = tiles_m * tiles_n;
+  const int kblocks = (args.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s2 = 0; s2 < STAGES; ++s2) {
+      mbar_init(&full[s2], 1);
+      mbar_init(&empty[s2], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);  // four epilogue warps in each CTA of the pair
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&map_a);
+    prefetch_tmap(&map_b);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C_::TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full0 = map_to(smem_u32(full), 0);     // the leader's full barriers
+  const uint32_t tempty0 = map_to(smem_u32(tempty), 0);  // the leader's tempty barriers
+
+  if (warp == 0 && lane == 0) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    int stage = 0;
+    uint32_t round = 0;
+    uint32_t armed_mask = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += npairs) {
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int m0 = tm * 256 + (int)crank * 128;
+      const int n0 = tn * C_::BN_OUT;
+      const int bn0 = (EPI == EPI_SWIGLU) ? (crank ? args.N + n0 : n0) : n0 + (int)crank * 128;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);  // both CTAs' bytes
+        armed_mask |= 1u << stage;
+        const int k0 = kb * BK;
+        const uint32_t bar = full0 + stage * 8;
+        tma_load_2d_pair(sa + stage * C_::A_BYTES, &map_a, bar, k0, m0);
+        tma_load_2d_pair(sb + stage * C_::B_BYTES, &map_b, bar, k0, bn0);
+        if (++stage == STAGES) {
+          stage = 0;
+          ++round;
+        }
+      }
+    }
+    if (!ok && crank == 0) {  // drain the leader's in-flight stages (bounded)
+      for (int s2 = 0; s2 < STAGES; ++s2)
+        if (armed_mask & (1u << s2))
+          mbar_wait(&full[s2], (s2 < stage ? round : round - 1) & 1, args.err, ERR_GEMM_WAIT, nullptr);
+    }
+  } else if (warp == 1 && lane == 0 && crank == 0) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    int stage = 0;
+    uint32_t round = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < num_tiles && ok; t += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = it >> 1;
+      if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * C_::BN;
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait(&full[stage], round & 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sa + stage * C_::A_BYTES);
+        const uint32_t b_addr = smem_u32(sb + stage * C_::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)
+          mma_bf16_pair(d_tmem, smem_desc(a_addr + k * 32, 16, 1024), smem_desc(b_addr + k * 32, 16, 1024), C_::IDESC,
+                        (kb > 0 || k > 0) ? 1u : 0u);
+        const uint32_t e = smem_u32(&empty[stage]);
+        commit2(map_to(e, 0));  // frees this stage in both CTAs once the MMAs have read it
+        commit2(map_to(e, 1));
+        if (++stage == STAGES) {
+          stage = 0;
+          ++round;
+        }
+      }
+      if (ok) {
+        const uint32_t f = smem_u32(&tfull[acc]);
+        commit2(map_to(f, 0));
+        commit2(map_to(f, 1));
+      }
+    }
+    if (!ok) {
+      commit2(map_to(smem_u32(drain), 0));
+      mbar_wait(drain, 0, args.err, ERR_GEMM_WAIT, nullptr);
+    }
+  } else if (warp >= 2 && warp < 6) {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int it = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++it) {
+      const int acc = it & 1;
+      const uint32_t use = it >> 1;
+      if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      const int row = tm * 256 + (int)crank * 128 + row_in_tile;
+      const int n0 = tn * C_::BN_OUT;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * C_::BN;
+      epilogue_tile<256, EPI>(args, t_row, row, row < args.M, n0, 0, t, num_tiles, 1, lane);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_remote(tempty0 + acc * 8);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still read its smem or signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(C_::TMEM_COLS)
+                 : "memory");
   }
 }
 
@@ -633,6 +868,48 @@ static int num_sms() {
     C10_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
   }
   return n;
+}
+
+// CTA pairs: for K-major forward GEMMs large enough to give every pair a few 256 x 256 tiles
+// (BDLLM_GEMM_PAIR=0 keeps the one-CTA kernel)
+static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, const void* tp, const void* ag) {
+  static int env = -1;
+  if (env < 0) {
+    const char* e = getenv("BDLLM_GEMM_PAIR");
+    env = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  if (!env || a_mn || b_mn || tp != nullptr || ag != nullptr) return false;
+  if (!(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_ADD_BF16 || epi == EPI_SWIGLU)) return false;
+  const int64_t tiles = ((M + 255) / 256) * ((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256));
+  return M >= 512 && tiles >= 148;
+}
+
+template <int EPI>
+static void launch_pair(GemmLaunch* L, cudaStream_t st) {
+  using C_ = Cfg2<EPI>;
+  auto kern = gemm2_kernel<EPI>;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM));
+    attr = true;
+  }
+  const GemmArgs& args = L->args;
+  const int tiles = (int)(((args.M + 255) / 256) * ((args.N + C_::BN_OUT - 1) / C_::BN_OUT));
+  const int pairs = std::max(1, std::min(tiles, num_sms() / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.dynamicSmemBytes = C_::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  void* kargs[3] = {&L->ma, &L->mb, &L->args};
+  C10_CUDA_CHECK(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), kargs));
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -981,6 +1258,18 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   TORCH_CHECK(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31), "gemm: dims exceed int32");
 
   GTRACE("args ok");
+  // the CTA-pair kernel for large forward (K-major) GEMMs
+  if (use_pair(a_mn, b_mn, M, N, epi, tp, ag)) {
+    make_map_bf16(&L->ma, a.data_ptr(), K, M, lda, 64, 128);
+    make_map_bf16(&L->mb, b.data_ptr(), K, epi == EPI_SWIGLU ? 2 * N : N, ldb, 64, 128);
+    switch (epi) {
+      case EPI_BF16: launch_pair<EPI_BF16>(L, st); return;
+      case EPI_F32: launch_pair<EPI_F32>(L, st); return;
+      case EPI_ADD_BF16: launch_pair<EPI_ADD_BF16>(L, st); return;
+      case EPI_SWIGLU: launch_pair<EPI_SWIGLU>(L, st); return;
+      default: break;
+    }
+  }
   if (a_mn)
     make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);
   else

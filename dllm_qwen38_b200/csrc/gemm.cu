@@ -578,7 +578,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // epilogue warps arrive on the leader's tempty barriers. Every wait is bounded as in gemm_kernel;
 // all paths reach the final cluster barrier.
 constexpr int STAGES2 = 6;
-template <int EPI>
+template <int EPI, bool A_MN, bool B_MN>
 struct Cfg2 {
   static constexpr int BN = 256;  // MMA N (both CTAs' B halves)
   static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? 128 : 256;
@@ -587,7 +587,7 @@ struct Cfg2 {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int SMEM = STAGES2 * STAGE_BYTES + 1024 + 256;
   static constexpr int TMEM_COLS = 512;
-  static constexpr uint32_t IDESC = idesc_bf16(256, 256, 0, 0);
+  static constexpr uint32_t IDESC = idesc_bf16(256, 256, A_MN ? 1 : 0, B_MN ? 1 : 0);
 };
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -627,10 +627,10 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, u
       : "memory");
 }
 
-template <int EPI>
+template <int EPI, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs args) {
-  using C_ = Cfg2<EPI>;
+  using C_ = Cfg2<EPI, A_MN, B_MN>;
   constexpr int STAGES = STAGES2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -702,8 +702,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         armed_mask |= 1u << stage;
         const int k0 = kb * BK;
         const uint32_t bar = full0 + stage * 8;
-        tma_load_2d_pair(sa + stage * C_::A_BYTES, &map_a, bar, k0, m0);
-        tma_load_2d_pair(sb + stage * C_::B_BYTES, &map_b, bar, k0, bn0);
+        uint8_t* a_dst = sa + stage * C_::A_BYTES;
+        uint8_t* b_dst = sb + stage * C_::B_BYTES;
+        if constexpr (!A_MN) {
+          tma_load_2d_pair(a_dst, &map_a, bar, k0, m0);
+        } else {  // [K, M] operand: two 64-row (128-byte) swizzle atoms along M
+          tma_load_2d_pair(a_dst, &map_a, bar, m0, k0);
+          tma_load_2d_pair(a_dst + 8192, &map_a, bar, m0 + 64, k0);
+        }
+        if constexpr (!B_MN) {
+          tma_load_2d_pair(b_dst, &map_b, bar, k0, bn0);
+        } else {
+          tma_load_2d_pair(b_dst, &map_b, bar, bn0, k0);
+          tma_load_2d_pair(b_dst + 8192, &map_b, bar, bn0 + 64, k0);
+        }
         if (++stage == STAGES) {
           stage = 0;
           ++round;
@@ -739,9 +751,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t a_addr = smem_u32(sa + stage * C_::A_BYTES);
         const uint32_t b_addr = smem_u32(sb + stage * C_::B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k)
-          mma_bf16_pair(d_tmem, smem_desc(a_addr + k * 32, 16, 1024), smem_desc(b_addr + k * 32, 16, 1024), C_::IDESC,
-                        (kb > 0 || k > 0) ? 1u : 0u);
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, 8192, 1024) : smem_desc(a_addr + k * 32, 16, 1024);
+          const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, 8192, 1024) : smem_desc(b_addr + k * 32, 16, 1024);
+          mma_bf16_pair(d_tmem, ad, bd, C_::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
+        }
         const uint32_t e = smem_u32(&empty[stage]);
         commit2(map_to(e, 0));  // frees this stage in both CTAs once the MMAs have read it
         commit2(map_to(e, 1));
@@ -870,24 +884,25 @@ static int num_sms() {
   return n;
 }
 
-// CTA pairs: for K-major forward GEMMs large enough to give every pair a few 256 x 256 tiles
-// (BDLLM_GEMM_PAIR=0 keeps the one-CTA kernel)
+// CTA pairs: for GEMMs large enough to give every pair a few 256 x 256 tiles, any operand majors
+// (SwiGLU: K-major only) (BDLLM_GEMM_PAIR=0 keeps the one-CTA kernel)
 static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, const void* tp, const void* ag) {
   static int env = -1;
   if (env < 0) {
     const char* e = getenv("BDLLM_GEMM_PAIR");
     env = (e == nullptr || e[0] != '0') ? 1 : 0;
   }
-  if (!env || a_mn || b_mn || tp != nullptr || ag != nullptr) return false;
+  if (!env || tp != nullptr || ag != nullptr) return false;
+  if (epi == EPI_SWIGLU && (a_mn || b_mn)) return false;
   if (!(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_ADD_BF16 || epi == EPI_SWIGLU)) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256));
   return M >= 512 && tiles >= 148;
 }
 
-template <int EPI>
+template <int EPI, bool A_MN, bool B_MN>
 static void launch_pair(GemmLaunch* L, cudaStream_t st) {
-  using C_ = Cfg2<EPI>;
-  auto kern = gemm2_kernel<EPI>;
+  using C_ = Cfg2<EPI, A_MN, B_MN>;
+  auto kern = gemm2_kernel<EPI, A_MN, B_MN>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM));
@@ -1260,15 +1275,30 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   GTRACE("args ok");
   // the CTA-pair kernel for large forward (K-major) GEMMs
   if (use_pair(a_mn, b_mn, M, N, epi, tp, ag)) {
-    make_map_bf16(&L->ma, a.data_ptr(), K, M, lda, 64, 128);
-    make_map_bf16(&L->mb, b.data_ptr(), K, epi == EPI_SWIGLU ? 2 * N : N, ldb, 64, 128);
-    switch (epi) {
-      case EPI_BF16: launch_pair<EPI_BF16>(L, st); return;
-      case EPI_F32: launch_pair<EPI_F32>(L, st); return;
-      case EPI_ADD_BF16: launch_pair<EPI_ADD_BF16>(L, st); return;
-      case EPI_SWIGLU: launch_pair<EPI_SWIGLU>(L, st); return;
-      default: break;
-    }
+    if (a_mn)
+      make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);
+    else
+      make_map_bf16(&L->ma, a.data_ptr(), K, M, lda, 64, 128);
+    if (b_mn)
+      make_map_bf16(&L->mb, b.data_ptr(), N, K, ldb, 64, 64);
+    else
+      make_map_bf16(&L->mb, b.data_ptr(), K, epi == EPI_SWIGLU ? 2 * N : N, ldb, 64, 128);
+#define BDLLM_PAIR_CASE(E, AM, BMN)                   \
+  if (epi == E && a_mn == AM && b_mn == BMN) {        \
+    launch_pair<E, AM, BMN>(L, st);                   \
+    return;                                           \
+  }
+    BDLLM_PAIR_CASE(EPI_BF16, false, false)
+    BDLLM_PAIR_CASE(EPI_F32, false, false)
+    BDLLM_PAIR_CASE(EPI_ADD_BF16, false, false)
+    BDLLM_PAIR_CASE(EPI_SWIGLU, false, false)
+    BDLLM_PAIR_CASE(EPI_BF16, false, true)
+    BDLLM_PAIR_CASE(EPI_F32, false, true)
+    BDLLM_PAIR_CASE(EPI_ADD_BF16, false, true)
+    BDLLM_PAIR_CASE(EPI_BF16, true, true)
+    BDLLM_PAIR_CASE(EPI_F32, true, true)
+    BDLLM_PAIR_CASE(EPI_ADD_BF16, true, true)
+#undef BDLLM_PAIR_CASE
   }
   if (a_mn)
     make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);

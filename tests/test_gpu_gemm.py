@@ -51,6 +51,37 @@ def test_nn_and_tn(M, N, K):
     C.check_errors()
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 2560, 1024), (4104, 2568, 520)])
+def test_cta_pair_all_majors(M, N, K):
+    """Shapes with >= 148 256x256 tiles take the two-CTA (cta_group::2) kernel: K-major and
+    MN-major operands, bf16 / fp32 / in-place accumulate epilogues, M, N and K tails."""
+    from dllm_qwen38_b200 import _C
+
+    torch.manual_seed(5)
+    a_mk = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    a_km = a_mk.t().contiguous()
+    b_nk = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    b_kn = b_nk.t().contiguous()
+    ref = a_mk.float() @ b_nk.float().t()
+    for a_mn in (False, True):
+        for b_mn in (False, True):
+            if a_mn and not b_mn:
+                continue
+            a, lda = (a_km, M) if a_mn else (a_mk, K)
+            b, ldb = (b_kn, N) if b_mn else (b_nk, K)
+            c32 = torch.empty(M, N, device="cuda", dtype=torch.float32)
+            _C.gemm(a, a_mn, lda, b, b_mn, ldb, M, N, K, c32, N, 1)
+            assert _rel(c32, ref) < 1e-5, (a_mn, b_mn)
+            c16 = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            _C.gemm(a, a_mn, lda, b, b_mn, ldb, M, N, K, c16, N, 0)
+            assert _rel(c16, ref) < 1e-2, (a_mn, b_mn)
+            acc = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+            want = acc.float() + ref
+            _C.gemm(a, a_mn, lda, b, b_mn, ldb, M, N, K, acc, N, 2, acc, N)  # in place, as wgrad runs it
+            assert _rel(acc, want) < 1e-2, (a_mn, b_mn)
+    _ops().check_errors()
+
+
 def test_bn128_variant():
     from dllm_qwen38_b200 import _C
 

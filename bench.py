@@ -31,6 +31,7 @@ from __future__ import annotations
 
 import argparse
 import datetime
+import faulthandler
 import json
 import math
 import os
@@ -288,6 +289,7 @@ def run_reference(a, rank, world):
 
 
 def main(argv=None) -> int:
+    faulthandler.enable()  # a fatal signal in any rank prints every thread's Python stack
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=8)

@@ -55,11 +55,27 @@ def timeit(fn, iters: int, warmup: int) -> float:
 
 
 def op_gemm(a):
+    """--layout nt: y[M,N] = x[M,K] w[N,K]^T (forward); nn: x[M,K] w[K,N] (input gradient, w read
+    N-contiguous); tn: g[M,N] += a[K,M]^T b[K,N] into bf16 (weight gradient, both operands
+    MN-major, accumulated in place as the training step runs it)."""
     from ..ops import cuda as Cu
 
-    x = torch.randn(a.M, a.K, device="cuda").bfloat16()
-    w = torch.randn(a.N, a.K, device="cuda").bfloat16()
-    fn = (lambda: torch.matmul(x, w.t())) if a.impl == "cublas" else (lambda: Cu.gemm_nt(x, w))
+    if a.layout == "nt":
+        x = torch.randn(a.M, a.K, device="cuda").bfloat16()
+        w = torch.randn(a.N, a.K, device="cuda").bfloat16()
+        fn = (lambda: torch.matmul(x, w.t())) if a.impl == "cublas" else (lambda: Cu.gemm_nt(x, w))
+    elif a.layout == "nn":
+        x = torch.randn(a.M, a.K, device="cuda").bfloat16()
+        w = torch.randn(a.K, a.N, device="cuda").bfloat16()
+        fn = (lambda: torch.matmul(x, w)) if a.impl == "cublas" else (lambda: Cu.gemm_nn(x, w))
+    else:
+        at = torch.randn(a.K, a.M, device="cuda").bfloat16()
+        bt = torch.randn(a.K, a.N, device="cuda").bfloat16()
+        g = torch.zeros(a.M, a.N, device="cuda").bfloat16()
+        if a.impl == "cublas":
+            fn = lambda: g.addmm_(at.t(), bt)  # noqa: E731
+        else:
+            fn = lambda: Cu._C.gemm(at, True, a.M, bt, True, a.N, a.M, a.N, a.K, g, a.N, Cu.EPI_ADD_BF16, g, a.N)  # noqa: E731
     return fn, 2.0 * a.M * a.N * a.K, 2.0 * (a.M * a.K + a.N * a.K + a.M * a.N)
 
 
@@ -188,6 +204,7 @@ def main(argv=None) -> int:
     p.add_argument("--M", type=int, default=8192)
     p.add_argument("--N", type=int, default=5120)
     p.add_argument("--K", type=int, default=5120)
+    p.add_argument("--layout", default="nt", choices=["nt", "nn", "tn"], help="gemm operand majors")
     p.add_argument("--B", type=int, default=1)
     p.add_argument("--L", type=int, default=4096)
     p.add_argument("--block", type=int, default=32)
@@ -206,7 +223,7 @@ def main(argv=None) -> int:
     out = {"op": a.op, "impl": a.impl, "ms": round(ms, 4), "tflops": round(flops / s / 1e12, 2),
            "gbs": round(byts / s / 1e9, 1), "frac_bf16_peak": round(flops / s / tf, 3),
            "frac_hbm_peak": round(byts / s / bw, 3), "peaks": src,
-           "shape": {k: getattr(a, k) for k in ("M", "N", "K", "B", "L", "block", "rows", "D", "vocab", "n")}}
+           "shape": {k: getattr(a, k) for k in ("M", "N", "K", "layout", "B", "L", "block", "rows", "D", "vocab", "n")}}
     print(json.dumps(out))
     return 0
 

@@ -146,6 +146,20 @@ def op_attn(a):
     return fn, flops, byts
 
 
+def op_attn_fwd(a):
+    """forward only (O and the row log2-sum-exp), same operands and pair count as `attn`"""
+    from ..ops import cuda as Cu
+
+    B, L, Hq, Hk, D = a.B, a.L, 24, 4, 256
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(B, 2 * L, Hq, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
+    fn = lambda: Cu._C.attn_fwd(q, k, v, L, a.block, D ** -0.5, False)  # noqa: E731
+    pairs = float(L) * L + L * a.block
+    return fn, B * Hq * pairs * D * 4.0, 2 * (q.numel() * 2 + k.numel() + v.numel())
+
+
 def op_ce(a):
     from ..ops import cuda as Cu
 
@@ -193,7 +207,7 @@ def op_adamw(a):
     return (lambda: Cu.adamw_flat(w, p, gr, m, v, 1e-5, 0.9, 0.95, 1e-8, 0.0, 1.0, 0.1, 0.05)), 12.0 * n, 30.0 * n
 
 
-OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm,
+OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm,
        "adamw": op_adamw}
 
 

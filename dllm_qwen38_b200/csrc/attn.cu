@@ -18,6 +18,9 @@
 #include "common.cuh"
 
 namespace bdllm {
+bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
+                 int64_t L, int64_t block, double scale, bool leak);
+
 namespace attn {
 
 constexpr int TILE = 64;
@@ -522,12 +525,24 @@ static at::Tensor prefix_t(const at::Tensor& q, const at::Tensor& k, const at::T
   return o;
 }
 
+// BDLLM_ATTN_TC=0 keeps the mma.sync forward for head dims the tcgen05 kernel covers
+static bool tc_forward_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("BDLLM_ATTN_TC");
+    on = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return on == 1;
+}
+
 template <int D>
 static std::vector<at::Tensor> fwd_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L,
                                      int64_t block, double scale, bool leak) {
   Args a = make_args(q, k, v, L, block, scale, leak);
   auto o = at::empty({a.B, a.T2, a.Hq, D}, q.options());
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
+  if ((D == 128 || D == 256) && tc_forward_enabled() && attn_fwd_tc(q, k, v, o, lse, L, block, scale, leak))
+    return {o, lse};
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse2 = lse.data_ptr<float>();
   go(fwd_kernel<D>, dim3((a.T2 + TILE - 1) / TILE, a.B * a.Hq), 3 * TILE * D * 2, a);

@@ -20,6 +20,9 @@
 namespace bdllm {
 bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                  int64_t L, int64_t block, double scale, bool leak);
+bool attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                 const at::Tensor& o, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+                 at::Tensor& dv, int64_t L, int64_t block, double scale, bool leak);
 
 namespace attn {
 
@@ -535,6 +538,16 @@ static bool tc_forward_enabled() {
   return on == 1;
 }
 
+// BDLLM_ATTN_TC_BWD=0 keeps the mma.sync backward
+static bool tc_backward_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("BDLLM_ATTN_TC_BWD");
+    on = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return on == 1 && tc_forward_enabled();
+}
+
 template <int D>
 static std::vector<at::Tensor> fwd_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L,
                                      int64_t block, double scale, bool leak) {
@@ -567,6 +580,9 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
   a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
   a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  if ((D == 128 || D == 256) && tc_backward_enabled() &&
+      attn_bwd_tc(d, q, k, v, oc, lse, delta, dq, dk, dv, L, block, scale, leak))
+    return {dq, dk, dv};
   const int nt = (a.T2 + TILE - 1) / TILE;
   go(bwd_dq_kernel<D>, dim3(nt, a.B * a.Hq), (2 * TILE + 2 * TK) * D * 2, a);
   constexpr int DA = D > 128 ? D / 2 : D;

@@ -415,6 +415,572 @@ __global__ void __launch_bounds__(NTHR, 1)
   }
 }
 
+// ================================================================== backward: dQ
+// One CTA = 128 query rows of one (batch, query head), key tiles of 32 (two-stage K/V ring):
+//   S = Q K^T and dP = dO V^T (M 128, N 32, K D) into double-buffered TMEM;
+//   warps 0-3 (thread = query row): P = 2^(S log2e scale - lse2), dS = P (dP - Delta), dS (bf16)
+//   into a 128-byte-swizzled smem tile (the first 64 bytes of each 128-byte row);
+//   dQ += dS K (M 128, N D, K 32) in TMEM, with K read N(=d)-contiguous.
+// Delta = rowsum(dO * O) is computed by the row's thread at the start and stored for the dK/dV
+// kernel.
+constexpr int BK2 = 32;
+
+template <int D>
+struct QCfg {
+  static constexpr int Q_BYTES = BQ * D * 2;    // Q, then dO: D/64 boxes of [128 rows][128 B]
+  static constexpr int K_BYTES = BK2 * D * 2;   // D/64 boxes of [32 rows][128 B]
+  static constexpr int STAGE = 2 * K_BYTES;     // K then V
+  static constexpr int DS_BYTES = BQ * 128;     // [128 rows][128 B] (64 B used per row)
+  static constexpr int SMEM = 2 * Q_BYTES + 2 * STAGE + 2 * DS_BYTES + 1024 + 256;
+  static constexpr int S_COL = 0, DP_COL = 64;  // two buffers of 32 columns each
+  static constexpr int DQ_COL = (D == 256) ? 256 : 128;
+  static constexpr int TMEM_COLS = (D == 256) ? 512 : 256;
+  static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BK2, 0, 0);
+  static constexpr uint32_t IDESC_DQ = idesc_bf16(BQ, D, 0, 1);
+};
+
+struct BArgs {
+  const __nv_bfloat16* o;     // forward output [B, T2, Hq, D]
+  const __nv_bfloat16* dout;  // [B, T2, Hq, D]
+  const float* lse2;          // [B, Hq, T2]
+  float* delta;               // [B, Hq, T2]
+  __nv_bfloat16* dq;          // [B, T2, Hq, D]
+  __nv_bfloat16* dk;          // [B, T2, Hk, D]
+  __nv_bfloat16* dv;          // [B, T2, Hk, D]
+  int B, T2, L, Hq, Hk, block, leak;
+  float scale, scale_log2;
+  int* err;
+};
+
+template <int W>
+__device__ __forceinline__ int next_tile_w(int jt, int nkt, int i0, int i1, int T2, int L, int block, int leak) {
+  for (; jt < nkt; ++jt)
+    if (tile_may(i0, i1, jt * W, min(jt * W + W - 1, T2 - 1), L, block, leak)) return jt;
+  return nkt;
+}
+
+template <int D>
+__global__ void __launch_bounds__(NTHR, 1)
+    bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
+                     const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
+  using C = QCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sdO = smem + C::Q_BYTES;
+  uint8_t* sKV = smem + 2 * C::Q_BYTES;
+  uint8_t* sdS = sKV + 2 * C::STAGE;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + 2 * C::DS_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* sd_full = bars + 5;
+  uint64_t* ds_full = bars + 7;
+  uint64_t* dq_done = bars + 9;
+  uint64_t* drain = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int qt = gridDim.x - 1 - blockIdx.x;
+  const int i0 = qt * BQ, i1 = min(i0 + BQ - 1, a.T2 - 1);
+  const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
+  const int nkt = (a.T2 + BK2 - 1) / BK2;
+  const int row0 = b * a.T2;
+  auto next = [&](int jt) { return next_tile_w<BK2>(jt, nkt, i0, i1, a.T2, a.L, a.block, a.leak); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&sd_full[s], 1);
+      mbar_init(&ds_full[s], 4);
+      mbar_init(&dq_done[s], 1);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&mq);
+    prefetch_tmap(&mdo);
+    prefetch_tmap(&mk);
+    prefetch_tmap(&mv);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sQ + c * BQ * 128, &mq, q_full, h * D + c * 64, row0 + i0);
+        tma_load_2d(sdO + c * BQ * 128, &mdo, q_full, h * D + c * 64, row0 + i0);
+      }
+      uint32_t armed = 0;
+      int it = 0;
+      for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&kv_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
+        armed |= 1u << s;
+        uint8_t* dk = sKV + s * C::STAGE;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_2d(dk + c * BK2 * 128, &mk, &kv_full[s], hk * D + c * 64, row0 + jt * BK2);
+          tma_load_2d(dk + C::K_BYTES + c * BK2 * 128, &mv, &kv_full[s], hk * D + c * 64, row0 + jt * BK2);
+        }
+      }
+      mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
+      for (int s = 0; s < 2; ++s)
+        if (armed & (1u << s)) {
+          const int last = ((it - 1) & 1) == s ? it - 1 : it - 2;
+          if (last >= 0) mbar_wait(&kv_full[s], (last >> 1) & 1, a.err, ERR_ATTN_WAIT, nullptr);
+        }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      bool ok = mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
+      tc_fence_after();
+      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sdO);
+      auto issue_sdp = [&](int it) {
+        const int s = it & 1;
+        const uint32_t k_addr = smem_u32(sKV + s * C::STAGE), v_addr = k_addr + C::K_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+          const uint32_t ok_ = (kk >> 2) * (BK2 * 128) + (kk & 3) * 32;
+          mma_bf16(tmem + C::S_COL + s * BK2, smem_desc(q_addr + oq, 16, 1024), smem_desc(k_addr + ok_, 16, 1024),
+                   C::IDESC_S, kk > 0 ? 1u : 0u);
+          mma_bf16(tmem + C::DP_COL + s * BK2, smem_desc(do_addr + oq, 16, 1024), smem_desc(v_addr + ok_, 16, 1024),
+                   C::IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&sd_full[s]);
+      };
+      int jt = ok ? next(0) : nkt;
+      if (jt < nkt) {
+        if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
+          tc_fence_after();
+          issue_sdp(0);
+        } else {
+          ok = false;
+        }
+      }
+      for (int it = 0; ok && jt < nkt; ++it) {
+        const int nx = next(jt + 1);
+        if (nx < nkt) {
+          if (!mbar_wait(&kv_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+          tc_fence_after();
+          issue_sdp(it + 1);
+        }
+        const int s = it & 1;
+        if (!mbar_wait(&ds_full[s], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t ds_addr = smem_u32(sdS + s * C::DS_BYTES);
+        const uint32_t k_addr = smem_u32(sKV + s * C::STAGE);
+#pragma unroll
+        for (int kk = 0; kk < BK2 / 16; ++kk)
+          mma_bf16(tmem + C::DQ_COL, smem_desc(ds_addr + kk * 32, 16, 1024),
+                   smem_desc(k_addr + kk * 2048, BK2 * 128, 1024), C::IDESC_DQ, (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&dq_done[s]);
+        mma_commit(&kv_empty[s]);
+        jt = nx;
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
+    }
+  } else {
+    // -------------------------------------------------------------- dS (warps 0-3)
+    const int r = warp * 32 + lane;
+    const int row = i0 + r;
+    const bool valid = row < a.T2;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const int64_t otok = (int64_t)a.Hq * D;
+    float lse = 0.f, dlt = 0.f;
+    if (valid) {
+      const uint4* po = reinterpret_cast<const uint4*>(a.o + ((int64_t)b * a.T2 + row) * otok + h * D);
+      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + ((int64_t)b * a.T2 + row) * otok + h * D);
+#pragma unroll 4
+      for (int c = 0; c < D / 8; ++c) {
+        const uint4 x = po[c], y = pd[c];
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&x);
+        const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 xf = __bfloat1622float2(x2[e]), yf = __bfloat1622float2(y2[e]);
+          dlt += xf.x * yf.x + xf.y * yf.y;
+        }
+      }
+      lse = a.lse2[((int64_t)b * a.Hq + h) * a.T2 + row];
+      a.delta[((int64_t)b * a.Hq + h) * a.T2 + row] = dlt;
+    }
+    const bool live = valid && lse != NEG_INF;
+    int it = 0;
+    bool ok = true;
+    for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+      const int s = it & 1;
+      const int j0 = jt * BK2;
+      if (!warp_wait(&sd_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t rs[32], rp[32];
+      tmem_ld32_async(tmem + lane_base + C::S_COL + s * BK2, rs);
+      tmem_ld32_async(tmem + lane_base + C::DP_COL + s * BK2, rp);
+      tmem_wait_ld(rs);
+      tmem_wait_ld(rp);
+      const bool full = tile_all(i0, i0 + BQ - 1, j0, j0 + BK2 - 1, a.T2, a.L, a.block, a.leak);
+      uint32_t pk[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float d2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = 2 * c + e, col = j0 + cc;
+          const bool vis = live && (full || (col < a.T2 && allowed(row, col, a.L, a.block, a.leak)));
+          const float p = vis ? exp2f(__uint_as_float(rs[cc]) * a.scale_log2 - lse) : 0.f;
+          d2[e] = p * (__uint_as_float(rp[cc]) - dlt);
+        }
+        pk[c] = pack_bf16(d2[0], d2[1]);
+      }
+      if (it >= 2 && !warp_wait(&dq_done[s], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      uint8_t* drow = sdS + s * C::DS_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        *reinterpret_cast<uint4*>(drow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ds_full[s]);
+    }
+    if (ok && it > 0 && !warp_wait(&dq_done[(it - 1) & 1], ((it - 1) >> 1) & 1, a.err, abort_flag)) ok = false;
+    tc_fence_after();
+    __nv_bfloat16* qrow = a.dq + ((int64_t)b * a.T2 + row) * otok + h * D;
+#pragma unroll 1
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t ro[32];
+      if (ok && it > 0) {
+        tmem_ld32_async(tmem + lane_base + C::DQ_COL + c * 32, ro);
+        tmem_wait_ld(ro);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ro[e] = 0u;
+      }
+      if (valid) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[e] = pack_bf16(__uint_as_float(ro[2 * e]) * a.scale, __uint_as_float(ro[2 * e + 1]) * a.scale);
+        uint4* dst = reinterpret_cast<uint4*>(qrow + c * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ================================================================== backward: dK, dV
+// One CTA = 128 keys of one (batch, kv head) and one 128-column slice z of dK / dV (D 256 runs
+// two CTAs per key tile); it loops over the query heads of the GQA group and their 32-row query
+// tiles that may see the key tile (two-stage Q / dO ring):
+//   S^T = K Q^T and dP^T = V dO^T (M 128 keys, N 32, K D) into double-buffered TMEM;
+//   warps 0-3 (thread = key): P^T = 2^(S^T log2e scale - lse2[q]), dS^T = P^T (dP^T - Delta[q]),
+//   both (bf16) into 128-byte-swizzled smem tiles;
+//   dV += P^T dO[:, z] and dK += dS^T Q[:, z] (M 128, N 128, K 32) in TMEM.
+constexpr int BQ2 = 32;
+
+template <int D>
+struct KCfg {
+  static constexpr int KV_BYTES = BQ * D * 2;   // K, then V: D/64 boxes of [128 rows][128 B]
+  static constexpr int T_BYTES = BQ2 * D * 2;   // Q tile, then dO tile: D/64 boxes of [32 rows][128 B]
+  static constexpr int STAGE = 2 * T_BYTES;
+  static constexpr int PT_BYTES = BQ * 128;     // [128 keys][128 B] (64 B used per row)
+  static constexpr int SMEM = 2 * KV_BYTES + 2 * STAGE + 2 * PT_BYTES + 1024 + 256;
+  static constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 256;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BQ2, 0, 0);
+  static constexpr uint32_t IDESC_G = idesc_bf16(BQ, 128, 0, 1);
+};
+
+template <int D>
+__global__ void __launch_bounds__(NTHR, 1)
+    bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
+                      const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
+  using C = KCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = smem + C::KV_BYTES;
+  uint8_t* sT = smem + 2 * C::KV_BYTES;  // stage s: Q tile at sT + s * STAGE, dO tile + T_BYTES
+  uint8_t* sPT = sT + 2 * C::STAGE;
+  uint8_t* sDST = sPT + C::PT_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDST + C::PT_BYTES);
+  uint64_t* kv_full = bars;
+  uint64_t* t_full = bars + 1;
+  uint64_t* t_empty = bars + 3;
+  uint64_t* st_full = bars + 5;
+  uint64_t* pt_full = bars + 7;
+  uint64_t* g_done = bars + 8;
+  uint64_t* drain = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = gridDim.x;
+  const int kt = (blockIdx.x + nkt / 2) % nkt;  // clean-stream key tiles (the most work) first
+  const int j0 = kt * BQ, j1 = min(j0 + BQ - 1, a.T2 - 1);
+  const int b = blockIdx.y / a.Hk, hk = blockIdx.y % a.Hk;
+  const int z = blockIdx.z;
+  const int rep = a.Hq / a.Hk;
+  const int nqt = (a.T2 + BQ2 - 1) / BQ2;
+  const int total = rep * nqt;  // (query head, query tile) pairs, head-major
+  const int row0 = b * a.T2;
+  auto vis = [&](int t) {
+    const int i0 = (t % nqt) * BQ2;
+    return tile_may(i0, min(i0 + BQ2 - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak);
+  };
+  auto next = [&](int t) {
+    for (; t < total; ++t)
+      if (vis(t)) return t;
+    return total;
+  };
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&t_full[s], 1);
+      mbar_init(&t_empty[s], 1);
+      mbar_init(&st_full[s], 1);
+    }
+    mbar_init(pt_full, 4);
+    mbar_init(g_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&mq);
+    prefetch_tmap(&mdo);
+    prefetch_tmap(&mk);
+    prefetch_tmap(&mv);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_2d(sK + c * BQ * 128, &mk, kv_full, hk * D + c * 64, row0 + j0);
+        tma_load_2d(sV + c * BQ * 128, &mv, kv_full, hk * D + c * 64, row0 + j0);
+      }
+      uint32_t armed = 0;
+      int it = 0;
+      for (int t = next(0); t < total; t = next(t + 1), ++it) {
+        const int s = it & 1;
+        if (!mbar_wait(&t_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        mbar_arrive_expect_tx(&t_full[s], C::STAGE);
+        armed |= 1u << s;
+        const int hq = hk * rep + t / nqt, i0 = (t % nqt) * BQ2;
+        uint8_t* dst = sT + s * C::STAGE;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_2d(dst + c * BQ2 * 128, &mq, &t_full[s], hq * D + c * 64, row0 + i0);
+          tma_load_2d(dst + C::T_BYTES + c * BQ2 * 128, &mdo, &t_full[s], hq * D + c * 64, row0 + i0);
+        }
+      }
+      mbar_wait(kv_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
+      for (int s = 0; s < 2; ++s)
+        if (armed & (1u << s)) {
+          const int last = ((it - 1) & 1) == s ? it - 1 : it - 2;
+          if (last >= 0) mbar_wait(&t_full[s], (last >> 1) & 1, a.err, ERR_ATTN_WAIT, nullptr);
+        }
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      bool ok = mbar_wait(kv_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
+      tc_fence_after();
+      const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
+      auto issue_s = [&](int it) {
+        const int s = it & 1;
+        const uint32_t q_addr = smem_u32(sT + s * C::STAGE), do_addr = q_addr + C::T_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t okv = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+          const uint32_t ot = (kk >> 2) * (BQ2 * 128) + (kk & 3) * 32;
+          mma_bf16(tmem + C::ST_COL + s * BQ2, smem_desc(k_addr + okv, 16, 1024), smem_desc(q_addr + ot, 16, 1024),
+                   C::IDESC_S, kk > 0 ? 1u : 0u);
+          mma_bf16(tmem + C::DPT_COL + s * BQ2, smem_desc(v_addr + okv, 16, 1024),
+                   smem_desc(do_addr + ot, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&st_full[s]);
+      };
+      int t = ok ? next(0) : total;
+      if (t < total) {
+        if (mbar_wait(&t_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
+          tc_fence_after();
+          issue_s(0);
+        } else {
+          ok = false;
+        }
+      }
+      const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sDST);
+      for (int it = 0; ok && t < total; ++it) {
+        const int nx = next(t + 1);
+        if (nx < total) {
+          if (!mbar_wait(&t_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+          tc_fence_after();
+          issue_s(it + 1);
+        }
+        const int s = it & 1;
+        if (!mbar_wait(pt_full, it & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(sT + s * C::STAGE) + z * 2 * (BQ2 * 128);
+        const uint32_t do_addr = smem_u32(sT + s * C::STAGE + C::T_BYTES) + z * 2 * (BQ2 * 128);
+#pragma unroll
+        for (int kk = 0; kk < BQ2 / 16; ++kk) {
+          const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
+          mma_bf16(tmem + C::DV_COL, smem_desc(pt_addr + kk * 32, 16, 1024),
+                   smem_desc(do_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
+          mma_bf16(tmem + C::DK_COL, smem_desc(dst_addr + kk * 32, 16, 1024),
+                   smem_desc(q_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
+        }
+        mma_commit(g_done);
+        mma_commit(&t_empty[s]);
+        t = nx;
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
+    }
+  } else {
+    // -------------------------------------------------------------- P^T, dS^T (warps 0-3)
+    const int r = warp * 32 + lane;
+    const int key = j0 + r;
+    const bool kvalid = key < a.T2;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int it = 0;
+    bool ok = true;
+    for (int t = next(0); t < total; t = next(t + 1), ++it) {
+      const int s = it & 1;
+      const int hq = hk * rep + t / nqt, i0 = (t % nqt) * BQ2;
+      // lane c holds lse2 / Delta of query row i0 + c
+      const int qr = i0 + lane;
+      const int64_t hoff = ((int64_t)b * a.Hq + hq) * a.T2;
+      const float lse_l = qr < a.T2 ? a.lse2[hoff + qr] : NEG_INF;
+      const float dl_l = qr < a.T2 ? a.delta[hoff + qr] : 0.f;
+      if (!warp_wait(&st_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t rs[32], rp[32];
+      tmem_ld32_async(tmem + lane_base + C::ST_COL + s * BQ2, rs);
+      tmem_ld32_async(tmem + lane_base + C::DPT_COL + s * BQ2, rp);
+      tmem_wait_ld(rs);
+      tmem_wait_ld(rp);
+      const bool full = tile_all(i0, i0 + BQ2 - 1, j0, j0 + BQ - 1, a.T2, a.L, a.block, a.leak);
+      uint32_t pp[16], pd[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float p2[2], d2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int cc = 2 * c + e, qrow = i0 + cc;
+          const float lq = __shfl_sync(0xffffffffu, lse_l, cc);
+          const float dq = __shfl_sync(0xffffffffu, dl_l, cc);
+          const bool vis = kvalid && lq != NEG_INF && (full || (qrow < a.T2 && allowed(qrow, key, a.L, a.block, a.leak)));
+          const float p = vis ? exp2f(__uint_as_float(rs[cc]) * a.scale_log2 - lq) : 0.f;
+          p2[e] = p;
+          d2[e] = p * (__uint_as_float(rp[cc]) - dq);
+        }
+        pp[c] = pack_bf16(p2[0], p2[1]);
+        pd[c] = pack_bf16(d2[0], d2[1]);
+      }
+      // the P^T / dS^T tiles were read by the gradient MMAs of iteration it-1
+      if (it >= 1 && !warp_wait(g_done, (it - 1) & 1, a.err, abort_flag)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = sPT + r * 128;
+      uint8_t* drow = sDST + r * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pp[4 * c], pp[4 * c + 1], pp[4 * c + 2], pp[4 * c + 3]);
+        *reinterpret_cast<uint4*>(drow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pd[4 * c], pd[4 * c + 1], pd[4 * c + 2], pd[4 * c + 3]);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pt_full);
+    }
+    if (ok && it > 0 && !warp_wait(g_done, (it - 1) & 1, a.err, abort_flag)) ok = false;
+    tc_fence_after();
+    const int64_t ktok = (int64_t)a.Hk * D;
+    __nv_bfloat16* krow = a.dk + ((int64_t)b * a.T2 + key) * ktok + hk * D + z * 128;
+    __nv_bfloat16* vrow = a.dv + ((int64_t)b * a.T2 + key) * ktok + hk * D + z * 128;
+#pragma unroll 1
+    for (int g = 0; g < 2; ++g) {
+      const uint32_t col = g == 0 ? C::DV_COL : C::DK_COL;
+      const float mul = g == 0 ? 1.f : a.scale;
+      __nv_bfloat16* dst_row = g == 0 ? vrow : krow;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ro[32];
+        if (ok && it > 0) {
+          tmem_ld32_async(tmem + lane_base + col + c * 32, ro);
+          tmem_wait_ld(ro);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ro[e] = 0u;
+        }
+        if (kvalid) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            pk[e] = pack_bf16(__uint_as_float(ro[2 * e]) * mul, __uint_as_float(ro[2 * e + 1]) * mul);
+          uint4* dst = reinterpret_cast<uint4*>(dst_row + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) dst[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 struct alignas(64) Maps {
   CUtensorMap q, k, v;
 };
@@ -446,6 +1012,61 @@ static void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int D>
+static void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                       const at::Tensor& o, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+                       at::Tensor& dv, int64_t L, int64_t block, double scale, bool leak) {
+  const int B = q.size(0), T2 = q.size(1), Hq = q.size(2), Hk = k.size(2);
+  BArgs a{};
+  a.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  a.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  a.lse2 = lse.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  a.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  a.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  a.B = B, a.T2 = T2, a.L = (int)L, a.Hq = Hq, a.Hk = Hk, a.block = (int)block, a.leak = leak ? 1 : 0;
+  a.scale = (float)scale;
+  a.scale_log2 = (float)(scale * 1.4426950408889634);
+  a.err = error_word_ptr();
+  const int64_t otok = (int64_t)Hq * D;
+  auto st = at::cuda::getCurrentCUDAStream();
+  {  // dQ (and Delta)
+    using C = QCfg<D>;
+    Maps m;
+    alignas(64) CUtensorMap mdo_al;
+    make_map_bf16(&m.q, q.data_ptr(), (uint64_t)Hq * D, (uint64_t)B * T2, q.stride(1), 64, BQ);
+    make_map_bf16(&mdo_al, dout.data_ptr(), (uint64_t)Hq * D, (uint64_t)B * T2, otok, 64, BQ);
+    make_map_bf16(&m.k, k.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, k.stride(1), 64, BK2);
+    make_map_bf16(&m.v, v.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, v.stride(1), 64, BK2);
+    auto kern = bwd_dq_tc_kernel<D>;
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      attr = true;
+    }
+    kern<<<dim3((T2 + BQ - 1) / BQ, B * Hq), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+  {  // dK, dV
+    using C = KCfg<D>;
+    Maps m;
+    alignas(64) CUtensorMap mdo_al;
+    make_map_bf16(&m.q, q.data_ptr(), (uint64_t)Hq * D, (uint64_t)B * T2, q.stride(1), 64, BQ2);
+    make_map_bf16(&mdo_al, dout.data_ptr(), (uint64_t)Hq * D, (uint64_t)B * T2, otok, 64, BQ2);
+    make_map_bf16(&m.k, k.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, k.stride(1), 64, BQ);
+    make_map_bf16(&m.v, v.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, v.stride(1), 64, BQ);
+    auto kern = bwd_dkv_tc_kernel<D>;
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+      attr = true;
+    }
+    kern<<<dim3((T2 + BQ - 1) / BQ, B * Hk, D / 128), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
 }  // namespace attn_tc
 
 // tcgen05 forward for head dims 128 / 256 (returns false when the shape is not covered)
@@ -458,6 +1079,20 @@ bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
     attn_tc::launch<128>(q, k, v, o, lse, L, block, scale, leak);
   else
     attn_tc::launch<256>(q, k, v, o, lse, L, block, scale, leak);
+  return true;
+}
+
+// tcgen05 backward (dQ with Delta, then dK / dV) for head dims 128 / 256; dout and o contiguous
+bool attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                 const at::Tensor& o, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
+                 at::Tensor& dv, int64_t L, int64_t block, double scale, bool leak) {
+  const int64_t D = q.size(3);
+  if (D != 128 && D != 256) return false;
+  bind_context(q.get_device());
+  if (D == 128)
+    attn_tc::launch_bwd<128>(dout, q, k, v, o, lse, delta, dq, dk, dv, L, block, scale, leak);
+  else
+    attn_tc::launch_bwd<256>(dout, q, k, v, o, lse, delta, dq, dk, dv, L, block, scale, leak);
   return true;
 }
 

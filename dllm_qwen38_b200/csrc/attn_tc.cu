@@ -3,10 +3,10 @@
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and
 // 256. One CTA = 128 query rows of one (batch, query head); 6 warps:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 64 keys into a 2-stage ring
-//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 64, K D) into one of two TMEM score
-//               buffers, O += P V (M 128, N D, K 64) into the TMEM output accumulator
-//   warps 0-3   softmax: thread = query row = TMEM lane; reads its 64 scores with tcgen05.ld,
+//   warp 4      TMA producer: the Q tile once, then K and V tiles of 32 keys into a 4-stage ring
+//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 32, K D) into one of two TMEM score
+//               buffers, O += P V (M 128, N D, K 32) into the TMEM output accumulator
+//   warps 0-3   softmax: thread = query row = TMEM lane; reads its 32 scores with tcgen05.ld,
 //               masks, keeps a running max and sum, writes P (bf16) into a 128-byte-swizzled smem
 //               tile that the next MMA reads as its K-major A operand
 // The score MMA of tile j+1 is issued before the softmax of tile j, so the tensor pipe computes it
@@ -28,19 +28,20 @@ void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t out
 namespace attn_tc {
 
 constexpr int BQ = 128;   // query rows per CTA (MMA M)
-constexpr int BKV = 64;   // keys per tile
 constexpr int NTHR = 192;
 constexpr float NEG_INF = -INFINITY;
 constexpr float RESCALE_LOG2 = 8.f;
 
 template <int D>
 struct FCfg {
+  static constexpr int BKV = 32;               // keys per tile
+  static constexpr int NST = 4;                // K/V ring stages
   static constexpr int Q_BYTES = BQ * D * 2;   // D/64 boxes of [128 rows][128 B]
-  static constexpr int K_BYTES = BKV * D * 2;  // D/64 boxes of [64 rows][128 B]
+  static constexpr int K_BYTES = BKV * D * 2;  // D/64 boxes of [BKV rows][128 B]
   static constexpr int STAGE = 2 * K_BYTES;    // K then V
-  static constexpr int P_BYTES = BQ * BKV * 2;  // [128 rows][128 B], one swizzle atom column
-  static constexpr int SMEM = Q_BYTES + 2 * STAGE + 2 * P_BYTES + 1024 + 256;
-  static constexpr int O_COL = (D == 256) ? 256 : 128;  // TMEM column of O; S buffers at 0 and 64
+  static constexpr int P_BYTES = BQ * 128;     // [128 rows][128 B] swizzle atoms, 2*BKV bytes used per row
+  static constexpr int SMEM = Q_BYTES + NST * STAGE + 2 * P_BYTES + 1024 + 256;
+  static constexpr int O_COL = (D == 256) ? 256 : 128;  // TMEM column of O; S buffers at 0 and BKV
   static constexpr int TMEM_COLS = (D == 256) ? 512 : 256;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV, 0, 0);
   static constexpr uint32_t IDESC_O = idesc_bf16(BQ, D, 0, 1);  // V read N(=d)-contiguous
@@ -141,10 +142,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __all_sync(0xffffffffu, ok);
 }
 
-// next visible key tile at or after jt (nkt when none)
-__device__ __forceinline__ int next_tile(int jt, int nkt, int i0, int i1, const FArgs& a) {
+// next visible key tile (of W keys) at or after jt (nkt when none)
+template <int W>
+__device__ __forceinline__ int next_tile_w(int jt, int nkt, int i0, int i1, int T2, int L, int block, int leak) {
   for (; jt < nkt; ++jt)
-    if (tile_may(i0, i1, jt * BKV, min(jt * BKV + BKV - 1, a.T2 - 1), a.L, a.block, a.leak)) return jt;
+    if (tile_may(i0, i1, jt * W, min(jt * W + W - 1, T2 - 1), L, block, leak)) return jt;
   return nkt;
 }
 
@@ -153,20 +155,21 @@ __global__ void __launch_bounds__(NTHR, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, FArgs a) {
   using C = FCfg<D>;
+  constexpr int BKV = C::BKV, NST = C::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::Q_BYTES;
-  uint8_t* sP = sKV + 2 * C::STAGE;
+  uint8_t* sP = sKV + NST * C::STAGE;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 7;
-  uint64_t* o_done = bars + 9;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_empty = kv_full + NST;
+  uint64_t* s_full = kv_empty + NST;
+  uint64_t* p_full = s_full + 2;
+  uint64_t* o_done = p_full + 2;
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -177,12 +180,15 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
   const int nkt = (a.T2 + BKV - 1) / BKV;
   const int row0 = b * a.T2;  // first row of this batch in the [B*T2, H*D] maps
+  auto next = [&](int jt) { return next_tile_w<BKV>(jt, nkt, i0, i1, a.T2, a.L, a.block, a.leak); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);  // one arrive per softmax warp
       mbar_init(&o_done[s], 1);
@@ -209,17 +215,15 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) tma_load_2d(sQ + c * BQ * 128, &mq, q_full, h * D + c * 64, row0 + i0);
-      uint32_t armed = 0;
+      int last[NST];
+#pragma unroll
+      for (int s = 0; s < NST; ++s) last[s] = -1;
       int it = 0;
-      bool ok = true;
-      for (int jt = next_tile(0, nkt, i0, i1, a); jt < nkt; jt = next_tile(jt + 1, nkt, i0, i1, a), ++it) {
-        const int s = it & 1;
-        if (!mbar_wait(&kv_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
-          ok = false;
-          break;
-        }
+      for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+        const int s = it % NST;
+        if (!mbar_wait(&kv_empty[s], ((it / NST) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
-        armed |= 1u << s;
+        last[s] = it;
         uint8_t* dk = sKV + s * C::STAGE;
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
@@ -229,12 +233,9 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       // every load armed must land before the CTA exits (bounded): the last arming of each stage
       mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
-      for (int s = 0; s < 2; ++s)
-        if (armed & (1u << s)) {
-          const int last = ((it - 1) & 1) == s ? it - 1 : it - 2;
-          if (last >= 0) mbar_wait(&kv_full[s], (last >> 1) & 1, a.err, ERR_ATTN_WAIT, nullptr);
-        }
-      (void)ok;
+#pragma unroll
+      for (int s = 0; s < NST; ++s)
+        if (last[s] >= 0) mbar_wait(&kv_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -243,18 +244,17 @@ __global__ void __launch_bounds__(NTHR, 1)
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
       auto issue_s = [&](int it) {
-        const int s = it & 1;
-        const uint32_t k_addr = smem_u32(sKV + s * C::STAGE);
+        const uint32_t k_addr = smem_u32(sKV + (it % NST) * C::STAGE);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off_q = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
           const uint32_t off_k = (kk >> 2) * (BKV * 128) + (kk & 3) * 32;
-          mma_bf16(tmem + s * BKV, smem_desc(q_addr + off_q, 16, 1024), smem_desc(k_addr + off_k, 16, 1024),
+          mma_bf16(tmem + (it & 1) * BKV, smem_desc(q_addr + off_q, 16, 1024), smem_desc(k_addr + off_k, 16, 1024),
                    C::IDESC_S, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&s_full[s]);
+        mma_commit(&s_full[it & 1]);
       };
-      int jt = ok ? next_tile(0, nkt, i0, i1, a) : nkt;
+      int jt = ok ? next(0) : nkt;
       if (jt < nkt) {
         if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
           tc_fence_after();
@@ -264,29 +264,24 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       for (int it = 0; ok && jt < nkt; ++it) {
-        const int nxt = next_tile(jt + 1, nkt, i0, i1, a);
+        const int nxt = next(jt + 1);
         if (nxt < nkt) {
-          if (!mbar_wait(&kv_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
-            ok = false;
-            break;
-          }
+          const int s1 = (it + 1) % NST;
+          if (!mbar_wait(&kv_full[s1], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
           issue_s(it + 1);
         }
-        const int s = it & 1;
-        if (!mbar_wait(&p_full[s], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
-          ok = false;
-          break;
-        }
+        const int pb = it & 1;
+        if (!mbar_wait(&p_full[pb], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + s * C::P_BYTES);
-        const uint32_t v_addr = smem_u32(sKV + s * C::STAGE + C::K_BYTES);
+        const uint32_t p_addr = smem_u32(sP + pb * C::P_BYTES);
+        const uint32_t v_addr = smem_u32(sKV + (it % NST) * C::STAGE + C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_bf16(tmem + C::O_COL, smem_desc(p_addr + kk * 32, 16, 1024), smem_desc(v_addr + kk * 2048, 8192, 1024),
-                   C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&o_done[s]);
-        mma_commit(&kv_empty[s]);
+          mma_bf16(tmem + C::O_COL, smem_desc(p_addr + kk * 32, 16, 1024),
+                   smem_desc(v_addr + kk * 2048, BKV * 128, 1024), C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&o_done[pb]);
+        mma_commit(&kv_empty[it % NST]);
         jt = nxt;
       }
       // every MMA issued must complete before TMEM is freed (bounded)
@@ -302,7 +297,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     float m_used = NEG_INF, l = 0.f;
     int it = 0;
     bool ok = true;
-    for (int jt = next_tile(0, nkt, i0, i1, a); jt < nkt; jt = next_tile(jt + 1, nkt, i0, i1, a), ++it) {
+    for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
       const int s = it & 1;
       const int j0 = jt * BKV;
       if (!warp_wait(&s_full[s], (it >> 1) & 1, a.err, abort_flag)) {
@@ -310,27 +305,29 @@ __global__ void __launch_bounds__(NTHR, 1)
         break;
       }
       tc_fence_after();
-      uint32_t ra[32], rb[32];
-      tmem_ld32_async(tmem + lane_base + s * BKV, ra);
-      tmem_ld32_async(tmem + lane_base + s * BKV + 32, rb);
-      tmem_wait_ld(ra);
-      tmem_wait_ld(rb);
-      float x[64];
+      float x[BKV];
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        x[c] = __uint_as_float(ra[c]) * a.scale_log2;
-        x[32 + c] = __uint_as_float(rb[c]) * a.scale_log2;
+      for (int h2 = 0; h2 < BKV / 32; ++h2) {
+        uint32_t ra[32];
+        tmem_ld32_async(tmem + lane_base + s * BKV + h2 * 32, ra);
+        tmem_wait_ld(ra);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) x[h2 * 32 + c] = __uint_as_float(ra[c]) * a.scale_log2;
       }
       if (!tile_all(i0, i0 + BQ - 1, j0, j0 + BKV - 1, a.T2, a.L, a.block, a.leak)) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
+        for (int c = 0; c < BKV; ++c) {
           const int col = j0 + c;
           if (!valid || col >= a.T2 || !allowed(row, col, a.L, a.block, a.leak)) x[c] = NEG_INF;
         }
       }
-      float mx = NEG_INF;
+      float m8[8];  // eight independent chains, then a tree
 #pragma unroll
-      for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
+      for (int e = 0; e < 8; ++e) m8[e] = x[e];
+#pragma unroll
+      for (int c = 8; c < BKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       float alpha = 1.f;
       if (mx > m_used + RESCALE_LOG2) {
         if (m_used != NEG_INF) alpha = exp2f(m_used - mx);
@@ -356,15 +353,15 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       l *= alpha;
       const float mu = (m_used == NEG_INF) ? 0.f : m_used;
-      uint32_t pk[32];
-      float rs = 0.f;
+      uint32_t pk[BKV / 2];
+      float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
+      for (int c = 0; c < BKV / 2; ++c) {
         const float p0 = exp2f(x[2 * c] - mu), p1 = exp2f(x[2 * c + 1] - mu);
-        rs += p0 + p1;
+        r8[c & 7] += p0 + p1;
         pk[c] = pack_bf16(p0, p1);
       }
-      l += rs;
+      l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
       // the P buffer s was read by the O MMA of tile it-2
       if (it >= 2 && !warp_wait(&o_done[s], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
         ok = false;
@@ -372,7 +369,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       uint8_t* prow = sP + s * C::P_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
+      for (int c = 0; c < BKV / 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async();  // generic smem writes -> visible to the tensor core's async proxy
@@ -452,12 +449,6 @@ struct BArgs {
   int* err;
 };
 
-template <int W>
-__device__ __forceinline__ int next_tile_w(int jt, int nkt, int i0, int i1, int T2, int L, int block, int leak) {
-  for (; jt < nkt; ++jt)
-    if (tile_may(i0, i1, jt * W, min(jt * W + W - 1, T2 - 1), L, block, leak)) return jt;
-  return nkt;
-}
 
 template <int D>
 __global__ void __launch_bounds__(NTHR, 1)
@@ -993,8 +984,8 @@ static void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   Maps m;
   // [B*T2 rows, H*D cols] views with the tensors' token strides
   make_map_bf16(&m.q, q.data_ptr(), (uint64_t)Hq * D, (uint64_t)B * T2, q.stride(1), 64, BQ);
-  make_map_bf16(&m.k, k.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, k.stride(1), 64, BKV);
-  make_map_bf16(&m.v, v.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, v.stride(1), 64, BKV);
+  make_map_bf16(&m.k, k.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, k.stride(1), 64, C::BKV);
+  make_map_bf16(&m.v, v.data_ptr(), (uint64_t)Hk * D, (uint64_t)B * T2, v.stride(1), 64, C::BKV);
   FArgs a{};
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   a.lse2 = lse.data_ptr<float>();

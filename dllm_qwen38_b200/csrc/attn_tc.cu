@@ -3,10 +3,10 @@
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and
 // 256. One CTA = 128 query rows of one (batch, query head); 6 warps:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 32 keys into a 4-stage ring
-//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 32, K D) into one of two TMEM score
-//               buffers, O += P V (M 128, N D, K 32) into the TMEM output accumulator
-//   warps 0-3   softmax: thread = query row = TMEM lane; reads its 32 scores with tcgen05.ld,
+//   warp 4      TMA producer: the Q tile once, then K and V tiles of 64 (or 32) keys into a ring
+//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 64, K D) into one of two TMEM score
+//               buffers, O += P V (M 128, N D, K 64) into the TMEM output accumulator
+//   warps 0-3   softmax: thread = query row = TMEM lane; reads its 64 scores with tcgen05.ld,
 //               masks, keeps a running max and sum, writes P (bf16) into a 128-byte-swizzled smem
 //               tile that the next MMA reads as its K-major A operand
 // The score MMA of tile j+1 is issued before the softmax of tile j, so the tensor pipe computes it
@@ -32,19 +32,22 @@ constexpr int NTHR = 192;
 constexpr float NEG_INF = -INFINITY;
 constexpr float RESCALE_LOG2 = 8.f;
 
-template <int D>
+template <int D, int BKV_ = 64>
 struct FCfg {
-  static constexpr int BKV = 32;               // keys per tile
-  static constexpr int NST = 4;                // K/V ring stages
+  static constexpr int BKV = BKV_;             // keys per tile
   static constexpr int Q_BYTES = BQ * D * 2;   // D/64 boxes of [128 rows][128 B]
   static constexpr int K_BYTES = BKV * D * 2;  // D/64 boxes of [BKV rows][128 B]
   static constexpr int STAGE = 2 * K_BYTES;    // K then V
   static constexpr int P_BYTES = BQ * 128;     // [128 rows][128 B] swizzle atoms, 2*BKV bytes used per row
+  // as many K/V stages as fit next to Q and the two P tiles (<= 4)
+  static constexpr int NST_FIT = (227 * 1024 - Q_BYTES - 2 * P_BYTES - 1024 - 256) / STAGE;
+  static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;
   static constexpr int SMEM = Q_BYTES + NST * STAGE + 2 * P_BYTES + 1024 + 256;
   static constexpr int O_COL = (D == 256) ? 256 : 128;  // TMEM column of O; S buffers at 0 and BKV
   static constexpr int TMEM_COLS = (D == 256) ? 512 : 256;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV, 0, 0);
   static constexpr uint32_t IDESC_O = idesc_bf16(BQ, D, 0, 1);  // V read N(=d)-contiguous
+  static_assert(NST >= 2, "K/V ring needs two stages");
 };
 
 struct FArgs {
@@ -54,44 +57,6 @@ struct FArgs {
   float scale_log2;
   int* err;
 };
-
-__device__ __forceinline__ bool allowed(int i, int j, int L, int block, int leak) {
-  const bool it = i < L, jt = j < L;
-  const int bi = (it ? i : i - L) / block, bj = (jt ? j : j - L) / block;
-  if (it) return jt ? (leak ? bj <= bi : bj == bi) : (bj < bi);
-  return jt ? false : (bj <= bi);
-}
-
-// may any row in [i0, i1] see any key in [j0, j1]?
-__device__ __forceinline__ bool tile_may(int i0, int i1, int j0, int j1, int L, int block, int leak) {
-  bool any = false;
-  if (i0 < L) {
-    const int qb0 = i0 / block, qb1 = min(i1, L - 1) / block;
-    if (j0 < L) {
-      const int kb0 = j0 / block, kb1 = min(j1, L - 1) / block;
-      any |= leak ? (kb0 <= qb1) : (kb0 <= qb1 && kb1 >= qb0);
-    }
-    if (j1 >= L) any |= ((max(j0, L) - L) / block) < qb1;
-  }
-  if (i1 >= L && j1 >= L) any |= ((max(j0, L) - L) / block) <= (i1 - L) / block;
-  return any;
-}
-
-// does every row in [i0, i1] see every key in [j0, j1]? (then the tile needs no mask)
-__device__ __forceinline__ bool tile_all(int i0, int i1, int j0, int j1, int T2, int L, int block, int leak) {
-  if (i1 >= T2 || j1 >= T2) return false;
-  if ((i0 < L) != (i1 < L) || (j0 < L) != (j1 < L)) return false;
-  if (i1 < L) {
-    const int qb0 = i0 / block, qb1 = i1 / block;
-    if (j1 < L) {
-      const int kb0 = j0 / block, kb1 = j1 / block;
-      return leak ? (kb1 <= qb0) : (kb0 == kb1 && qb0 == qb1 && kb0 == qb0);
-    }
-    return (j1 - L) / block < qb0;
-  }
-  if (j1 < L) return false;
-  return (j1 - L) / block <= (i0 - L) / block;
-}
 
 __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
@@ -135,6 +100,117 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// ex2 on the SFU (approximate, flush-to-zero): the softmax exponentials in base 2
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Up to two runs of tiles: [a0, a0 + na) then [b0, b0 + nb); k-th visible tile = at(k)
+struct Span2 {
+  int a0, na, b0, nb;
+  __device__ __forceinline__ int n() const { return na + nb; }
+  __device__ __forceinline__ int at(int k) const { return k < na ? a0 + k : b0 + (k - na); }
+};
+
+// tiles of W covering [lo1, hi1) and [lo2, hi2) (hi1 <= lo2 or an empty first range)
+__device__ __forceinline__ Span2 span_of(int lo1, int hi1, int lo2, int hi2, int W) {
+  Span2 s;
+  s.a0 = lo1 / W;
+  s.na = hi1 > lo1 ? (hi1 + W - 1) / W - s.a0 : 0;
+  s.b0 = lo2 / W;
+  int b1 = hi2 > lo2 ? (hi2 + W - 1) / W : s.b0;
+  if (s.na > 0 && s.b0 < s.a0 + s.na) s.b0 = s.a0 + s.na;  // a tile straddling L is listed once
+  s.nb = max(0, b1 - s.b0);
+  return s;
+}
+
+// key tiles of width W that some row of the query rows [i0, i1] may see (exactly the tiles
+// tile_may accepts): x_t keys of the rows' blocks (all earlier x_t blocks with the leak fault),
+// and the clean keys before the last block of the x_t rows / up to the last x_0 row's block
+__device__ __forceinline__ Span2 key_tiles(int i0, int i1, int L, int block, int leak, int W) {
+  int k1lo = 0, k1hi = 0, c = 0;
+  if (i0 < L) {
+    const int qb0 = i0 / block, qb1 = min(i1, L - 1) / block;
+    k1lo = leak ? 0 : qb0 * block;
+    k1hi = min((qb1 + 1) * block, L);
+    c = qb1 * block;
+  }
+  if (i1 >= L) c = max(c, min(((i1 - L) / block + 1) * block, L));
+  return span_of(k1lo, k1hi, L, L + c, W);
+}
+
+// query-row tiles of width W that may see some key of [j0, j1] (a hull: tiles it adds are fully
+// masked and contribute zeros)
+__device__ __forceinline__ Span2 row_tiles(int j0, int j1, int L, int T2, int block, int leak, int W) {
+  int r1lo = L, r1hi = 0, r2lo = T2;
+  if (j0 < L) {
+    const int kb0 = j0 / block, kb1 = min(j1, L - 1) / block;
+    r1lo = kb0 * block;
+    r1hi = leak ? L : min((kb1 + 1) * block, L);
+  }
+  if (j1 >= L) {
+    const int kb0 = (max(j0, L) - L) / block;
+    if ((kb0 + 1) * block < L) {
+      r1lo = min(r1lo, (kb0 + 1) * block);
+      r1hi = L;
+    }
+    r2lo = L + kb0 * block;
+  }
+  if (r1hi <= r1lo) r1lo = r1hi = 0;
+  return span_of(r1lo, r1hi, r2lo, T2, W);
+}
+
+// keys visible to one query row i: x_t keys [lo_t, hi_t), x_0 keys [L, L + hi_0)
+struct RowVis {
+  int lo_t, hi_t, hi_0;
+  __device__ __forceinline__ bool sees(int j, int L) const { return j < L ? (j >= lo_t && j < hi_t) : (j < L + hi_0); }
+  // every key of [j0, j1] (one stream) visible?
+  __device__ __forceinline__ bool sees_all(int j0, int j1, int L) const {
+    return j1 < L ? (j0 >= lo_t && j1 < hi_t) : (j0 >= L && j1 < L + hi_0);
+  }
+};
+__device__ __forceinline__ RowVis row_vis(int i, int L, int T2, int block, int leak) {
+  RowVis r{0, 0, 0};
+  if (i >= T2) return r;
+  if (i < L) {
+    const int bi = i / block;
+    r.lo_t = leak ? 0 : bi * block;
+    r.hi_t = min((bi + 1) * block, L);
+    r.hi_0 = bi * block;
+  } else {
+    r.hi_0 = min(((i - L) / block + 1) * block, L);
+  }
+  return r;
+}
+
+// query rows that see one key j: x_t rows [lo_t, hi_t), x_0 rows [lo_0, T2)
+struct KeyVis {
+  int lo_t, hi_t, lo_0;
+  __device__ __forceinline__ bool seen_by(int i, int L, int T2) const {
+    return i < L ? (i >= lo_t && i < hi_t) : (i >= lo_0 && i < T2);
+  }
+  __device__ __forceinline__ bool seen_by_all(int i0, int i1, int L, int T2) const {
+    return i1 < L ? (i0 >= lo_t && i1 < hi_t) : (i0 >= lo_0 && i0 >= L && i1 < T2);
+  }
+};
+__device__ __forceinline__ KeyVis key_vis(int j, int L, int T2, int block, int leak) {
+  KeyVis k{0, 0, T2};
+  if (j >= T2) return k;
+  if (j < L) {
+    const int bj = j / block;
+    k.lo_t = bj * block;
+    k.hi_t = leak ? L : min((bj + 1) * block, L);
+  } else {
+    const int bj = (j - L) / block;
+    k.lo_t = (bj + 1) * block;
+    k.hi_t = L;
+    k.lo_0 = L + bj * block;
+  }
+  return k;
+}
+
 // a bounded wait whose outcome is the same in every lane of the warp (the tcgen05.ld / st that
 // follow are warp-collective)
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* err, volatile int* abort) {
@@ -142,19 +218,11 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* e
   return __all_sync(0xffffffffu, ok);
 }
 
-// next visible key tile (of W keys) at or after jt (nkt when none)
-template <int W>
-__device__ __forceinline__ int next_tile_w(int jt, int nkt, int i0, int i1, int T2, int L, int block, int leak) {
-  for (; jt < nkt; ++jt)
-    if (tile_may(i0, i1, jt * W, min(jt * W + W - 1, T2 - 1), L, block, leak)) return jt;
-  return nkt;
-}
-
-template <int D>
+template <int D, int BKV_>
 __global__ void __launch_bounds__(NTHR, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, FArgs a) {
-  using C = FCfg<D>;
+  using C = FCfg<D, BKV_>;
   constexpr int BKV = C::BKV, NST = C::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -178,9 +246,9 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int qt = nqt - 1 - blockIdx.x;
   const int i0 = qt * BQ, i1 = min(i0 + BQ - 1, a.T2 - 1);
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
-  const int nkt = (a.T2 + BKV - 1) / BKV;
+  const Span2 sp = key_tiles(i0, i1, a.L, a.block, a.leak, BKV);  // visible key tiles, in order
+  const int nt = sp.n();
   const int row0 = b * a.T2;  // first row of this batch in the [B*T2, H*D] maps
-  auto next = [&](int jt) { return next_tile_w<BKV>(jt, nkt, i0, i1, a.T2, a.L, a.block, a.leak); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -218,8 +286,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       int last[NST];
 #pragma unroll
       for (int s = 0; s < NST; ++s) last[s] = -1;
-      int it = 0;
-      for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+      for (int it = 0; it < nt; ++it) {
+        const int jt = sp.at(it);
         const int s = it % NST;
         if (!mbar_wait(&kv_empty[s], ((it / NST) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
@@ -254,8 +322,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
         mma_commit(&s_full[it & 1]);
       };
-      int jt = ok ? next(0) : nkt;
-      if (jt < nkt) {
+      if (ok && nt > 0) {
         if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
           tc_fence_after();
           issue_s(0);
@@ -263,9 +330,8 @@ __global__ void __launch_bounds__(NTHR, 1)
           ok = false;
         }
       }
-      for (int it = 0; ok && jt < nkt; ++it) {
-        const int nxt = next(jt + 1);
-        if (nxt < nkt) {
+      for (int it = 0; ok && it < nt; ++it) {
+        if (it + 1 < nt) {
           const int s1 = (it + 1) % NST;
           if (!mbar_wait(&kv_full[s1], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
@@ -282,7 +348,6 @@ __global__ void __launch_bounds__(NTHR, 1)
                    smem_desc(v_addr + kk * 2048, BKV * 128, 1024), C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&o_done[pb]);
         mma_commit(&kv_empty[it % NST]);
-        jt = nxt;
       }
       // every MMA issued must complete before TMEM is freed (bounded)
       mma_commit(drain);
@@ -294,32 +359,32 @@ __global__ void __launch_bounds__(NTHR, 1)
     const int row = i0 + r;
     const bool valid = row < a.T2;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    float m_used = NEG_INF, l = 0.f;
+    const RowVis vis = row_vis(row, a.L, a.T2, a.block, a.leak);
+    const float c2 = a.scale_log2;
+    float m_used = NEG_INF, l = 0.f;  // m_used in the scaled log2 domain
     int it = 0;
     bool ok = true;
-    for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+    for (; it < nt; ++it) {
       const int s = it & 1;
-      const int j0 = jt * BKV;
+      const int j0 = sp.at(it) * BKV;
       if (!warp_wait(&s_full[s], (it >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float x[BKV];
+      float x[BKV];  // raw scores; masked ones -inf
 #pragma unroll
       for (int h2 = 0; h2 < BKV / 32; ++h2) {
         uint32_t ra[32];
         tmem_ld32_async(tmem + lane_base + s * BKV + h2 * 32, ra);
         tmem_wait_ld(ra);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) x[h2 * 32 + c] = __uint_as_float(ra[c]) * a.scale_log2;
+        for (int c = 0; c < 32; ++c) x[h2 * 32 + c] = __uint_as_float(ra[c]);
       }
-      if (!tile_all(i0, i0 + BQ - 1, j0, j0 + BKV - 1, a.T2, a.L, a.block, a.leak)) {
+      if (!__all_sync(0xffffffffu, vis.sees_all(j0, j0 + BKV - 1, a.L))) {
 #pragma unroll
-        for (int c = 0; c < BKV; ++c) {
-          const int col = j0 + c;
-          if (!valid || col >= a.T2 || !allowed(row, col, a.L, a.block, a.leak)) x[c] = NEG_INF;
-        }
+        for (int c = 0; c < BKV; ++c)
+          if (!vis.sees(j0 + c, a.L)) x[c] = NEG_INF;
       }
       float m8[8];  // eight independent chains, then a tree
 #pragma unroll
@@ -327,7 +392,7 @@ __global__ void __launch_bounds__(NTHR, 1)
 #pragma unroll
       for (int c = 8; c < BKV; ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
       const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * c2;
       float alpha = 1.f;
       if (mx > m_used + RESCALE_LOG2) {
         if (m_used != NEG_INF) alpha = exp2f(m_used - mx);
@@ -352,12 +417,12 @@ __global__ void __launch_bounds__(NTHR, 1)
         tmem_wait_st();
       }
       l *= alpha;
-      const float mu = (m_used == NEG_INF) ? 0.f : m_used;
+      const float nmu = (m_used == NEG_INF) ? 0.f : -m_used;
       uint32_t pk[BKV / 2];
       float r8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BKV / 2; ++c) {
-        const float p0 = exp2f(x[2 * c] - mu), p1 = exp2f(x[2 * c + 1] - mu);
+        const float p0 = ex2(fmaf(x[2 * c], c2, nmu)), p1 = ex2(fmaf(x[2 * c + 1], c2, nmu));
         r8[c & 7] += p0 + p1;
         pk[c] = pack_bf16(p0, p1);
       }
@@ -476,9 +541,9 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int qt = gridDim.x - 1 - blockIdx.x;
   const int i0 = qt * BQ, i1 = min(i0 + BQ - 1, a.T2 - 1);
   const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
-  const int nkt = (a.T2 + BK2 - 1) / BK2;
+  const Span2 sp = key_tiles(i0, i1, a.L, a.block, a.leak, BK2);
+  const int nt = sp.n();
   const int row0 = b * a.T2;
-  auto next = [&](int jt) { return next_tile_w<BK2>(jt, nkt, i0, i1, a.T2, a.L, a.block, a.leak); };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -517,7 +582,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       uint32_t armed = 0;
       int it = 0;
-      for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+      for (; it < nt; ++it) {
+        const int jt = sp.at(it);
         const int s = it & 1;
         if (!mbar_wait(&kv_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
@@ -556,8 +622,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
         mma_commit(&sd_full[s]);
       };
-      int jt = ok ? next(0) : nkt;
-      if (jt < nkt) {
+      if (ok && nt > 0) {
         if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
           tc_fence_after();
           issue_sdp(0);
@@ -565,9 +630,8 @@ __global__ void __launch_bounds__(NTHR, 1)
           ok = false;
         }
       }
-      for (int it = 0; ok && jt < nkt; ++it) {
-        const int nx = next(jt + 1);
-        if (nx < nkt) {
+      for (int it = 0; ok && it < nt; ++it) {
+        if (it + 1 < nt) {
           if (!mbar_wait(&kv_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
           issue_sdp(it + 1);
@@ -583,7 +647,6 @@ __global__ void __launch_bounds__(NTHR, 1)
                    smem_desc(k_addr + kk * 2048, BK2 * 128, 1024), C::IDESC_DQ, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&dq_done[s]);
         mma_commit(&kv_empty[s]);
-        jt = nx;
       }
       mma_commit(drain);
       mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
@@ -614,11 +677,13 @@ __global__ void __launch_bounds__(NTHR, 1)
       a.delta[((int64_t)b * a.Hq + h) * a.T2 + row] = dlt;
     }
     const bool live = valid && lse != NEG_INF;
+    const RowVis vis = row_vis(live ? row : a.T2, a.L, a.T2, a.block, a.leak);  // nothing visible when dead
+    const float c2 = a.scale_log2, nl = live ? -lse : 0.f;
     int it = 0;
     bool ok = true;
-    for (int jt = next(0); jt < nkt; jt = next(jt + 1), ++it) {
+    for (; it < nt; ++it) {
       const int s = it & 1;
-      const int j0 = jt * BK2;
+      const int j0 = sp.at(it) * BK2;
       if (!warp_wait(&sd_full[s], (it >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
@@ -629,16 +694,16 @@ __global__ void __launch_bounds__(NTHR, 1)
       tmem_ld32_async(tmem + lane_base + C::DP_COL + s * BK2, rp);
       tmem_wait_ld(rs);
       tmem_wait_ld(rp);
-      const bool full = tile_all(i0, i0 + BQ - 1, j0, j0 + BK2 - 1, a.T2, a.L, a.block, a.leak);
+      const bool full = __all_sync(0xffffffffu, vis.sees_all(j0, j0 + BK2 - 1, a.L));
       uint32_t pk[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         float d2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e, col = j0 + cc;
-          const bool vis = live && (full || (col < a.T2 && allowed(row, col, a.L, a.block, a.leak)));
-          const float p = vis ? exp2f(__uint_as_float(rs[cc]) * a.scale_log2 - lse) : 0.f;
+          const int cc = 2 * c + e;
+          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, nl));
+          if (!full && !vis.sees(j0 + cc, a.L)) p = 0.f;
           d2[e] = p * (__uint_as_float(rp[cc]) - dlt);
         }
         pk[c] = pack_bf16(d2[0], d2[1]);
@@ -742,18 +807,10 @@ __global__ void __launch_bounds__(NTHR, 1)
   const int b = blockIdx.y / a.Hk, hk = blockIdx.y % a.Hk;
   const int z = blockIdx.z;
   const int rep = a.Hq / a.Hk;
-  const int nqt = (a.T2 + BQ2 - 1) / BQ2;
-  const int total = rep * nqt;  // (query head, query tile) pairs, head-major
+  const Span2 sp = row_tiles(j0, j1, a.L, a.T2, a.block, a.leak, BQ2);  // query tiles that may see a key
+  const int nqv = sp.n();
+  const int total = rep * nqv;  // (query head, query tile) pairs, head-major
   const int row0 = b * a.T2;
-  auto vis = [&](int t) {
-    const int i0 = (t % nqt) * BQ2;
-    return tile_may(i0, min(i0 + BQ2 - 1, a.T2 - 1), j0, j1, a.L, a.block, a.leak);
-  };
-  auto next = [&](int t) {
-    for (; t < total; ++t)
-      if (vis(t)) return t;
-    return total;
-  };
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -792,12 +849,12 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       uint32_t armed = 0;
       int it = 0;
-      for (int t = next(0); t < total; t = next(t + 1), ++it) {
+      for (; it < total; ++it) {
         const int s = it & 1;
         if (!mbar_wait(&t_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&t_full[s], C::STAGE);
         armed |= 1u << s;
-        const int hq = hk * rep + t / nqt, i0 = (t % nqt) * BQ2;
+        const int hq = hk * rep + it / nqv, i0 = sp.at(it % nqv) * BQ2;
         uint8_t* dst = sT + s * C::STAGE;
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
@@ -832,8 +889,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
         mma_commit(&st_full[s]);
       };
-      int t = ok ? next(0) : total;
-      if (t < total) {
+      if (ok && total > 0) {
         if (mbar_wait(&t_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
           tc_fence_after();
           issue_s(0);
@@ -842,9 +898,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sDST);
-      for (int it = 0; ok && t < total; ++it) {
-        const int nx = next(t + 1);
-        if (nx < total) {
+      for (int it = 0; ok && it < total; ++it) {
+        if (it + 1 < total) {
           if (!mbar_wait(&t_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
           issue_s(it + 1);
@@ -864,7 +919,6 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
         mma_commit(g_done);
         mma_commit(&t_empty[s]);
-        t = nx;
       }
       mma_commit(drain);
       mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
@@ -875,15 +929,18 @@ __global__ void __launch_bounds__(NTHR, 1)
     const int key = j0 + r;
     const bool kvalid = key < a.T2;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const KeyVis kv = key_vis(key, a.L, a.T2, a.block, a.leak);
+    const float c2 = a.scale_log2;
     int it = 0;
     bool ok = true;
-    for (int t = next(0); t < total; t = next(t + 1), ++it) {
+    for (; it < total; ++it) {
       const int s = it & 1;
-      const int hq = hk * rep + t / nqt, i0 = (t % nqt) * BQ2;
+      const int hq = hk * rep + it / nqv, i0 = sp.at(it % nqv) * BQ2;
       // lane c holds lse2 / Delta of query row i0 + c
       const int qr = i0 + lane;
       const int64_t hoff = ((int64_t)b * a.Hq + hq) * a.T2;
-      const float lse_l = qr < a.T2 ? a.lse2[hoff + qr] : NEG_INF;
+      float lse_l = qr < a.T2 ? a.lse2[hoff + qr] : INFINITY;
+      if (lse_l == NEG_INF) lse_l = INFINITY;  // a row that sees nothing: every p is 0
       const float dl_l = qr < a.T2 ? a.delta[hoff + qr] : 0.f;
       if (!warp_wait(&st_full[s], (it >> 1) & 1, a.err, abort_flag)) {
         ok = false;
@@ -895,18 +952,18 @@ __global__ void __launch_bounds__(NTHR, 1)
       tmem_ld32_async(tmem + lane_base + C::DPT_COL + s * BQ2, rp);
       tmem_wait_ld(rs);
       tmem_wait_ld(rp);
-      const bool full = tile_all(i0, i0 + BQ2 - 1, j0, j0 + BQ - 1, a.T2, a.L, a.block, a.leak);
+      const bool full = __all_sync(0xffffffffu, kv.seen_by_all(i0, i0 + BQ2 - 1, a.L, a.T2));
       uint32_t pp[16], pd[16];
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
         float p2[2], d2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e, qrow = i0 + cc;
+          const int cc = 2 * c + e;
           const float lq = __shfl_sync(0xffffffffu, lse_l, cc);
           const float dq = __shfl_sync(0xffffffffu, dl_l, cc);
-          const bool vis = kvalid && lq != NEG_INF && (full || (qrow < a.T2 && allowed(qrow, key, a.L, a.block, a.leak)));
-          const float p = vis ? exp2f(__uint_as_float(rs[cc]) * a.scale_log2 - lq) : 0.f;
+          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, -lq));  // lse -inf (dead row): masked below
+          if (!full && !kv.seen_by(i0 + cc, a.L, a.T2)) p = 0.f;
           p2[e] = p;
           d2[e] = p * (__uint_as_float(rp[cc]) - dq);
         }
@@ -976,10 +1033,10 @@ struct alignas(64) Maps {
   CUtensorMap q, k, v;
 };
 
-template <int D>
+template <int D, int BKV>
 static void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& o, at::Tensor& lse,
                    int64_t L, int64_t block, double scale, bool leak) {
-  using C = FCfg<D>;
+  using C = FCfg<D, BKV>;
   const int B = q.size(0), T2 = q.size(1), Hq = q.size(2), Hk = k.size(2);
   Maps m;
   // [B*T2 rows, H*D cols] views with the tensors' token strides
@@ -992,7 +1049,7 @@ static void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
   a.B = B, a.T2 = T2, a.L = (int)L, a.Hq = Hq, a.Hk = Hk, a.block = (int)block, a.leak = leak ? 1 : 0;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
   a.err = error_word_ptr();
-  auto kern = fwd_tc_kernel<D>;
+  auto kern = fwd_tc_kernel<D, BKV>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
@@ -1066,10 +1123,17 @@ bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   const int64_t D = q.size(3);
   if (D != 128 && D != 256) return false;
   bind_context(q.get_device());
+  static int bkv = -1;  // BDLLM_ATTN_BKV=32 selects 32-key tiles (more ring stages)
+  if (bkv < 0) {
+    const char* e = getenv("BDLLM_ATTN_BKV");
+    bkv = (e != nullptr && atoi(e) == 32) ? 32 : 64;
+  }
   if (D == 128)
-    attn_tc::launch<128>(q, k, v, o, lse, L, block, scale, leak);
+    bkv == 32 ? attn_tc::launch<128, 32>(q, k, v, o, lse, L, block, scale, leak)
+              : attn_tc::launch<128, 64>(q, k, v, o, lse, L, block, scale, leak);
   else
-    attn_tc::launch<256>(q, k, v, o, lse, L, block, scale, leak);
+    bkv == 32 ? attn_tc::launch<256, 32>(q, k, v, o, lse, L, block, scale, leak)
+              : attn_tc::launch<256, 64>(q, k, v, o, lse, L, block, scale, leak);
   return true;
 }
 

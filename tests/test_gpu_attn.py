@@ -14,7 +14,7 @@ def _rel(a, b):
 
 @pytest.mark.parametrize("leak", [False, True])
 @pytest.mark.parametrize("B,L,block,Hq,Hk,D", [(2, 64, 16, 4, 2, 32), (1, 96, 32, 6, 2, 128), (1, 128, 32, 4, 1, 256),
-                                               (2, 24, 8, 4, 2, 16)])
+                                               (2, 24, 8, 4, 2, 16), (1, 100, 20, 4, 2, 128), (2, 192, 32, 6, 1, 256)])
 def test_attention_fwd_bwd(leak, B, L, block, Hq, Hk, D):
     from dllm_qwen38_b200.ops import cuda as Cu
 
@@ -41,7 +41,7 @@ def test_attention_fwd_bwd(leak, B, L, block, Hq, Hk, D):
 
 @pytest.mark.parametrize("leak", [False, True])
 @pytest.mark.parametrize("B,L,block,Hq,Hk,D,qscale", [(2, 320, 32, 6, 1, 256, 1.0), (1, 200, 8, 4, 2, 128, 6.0),
-                                                      (1, 256, 32, 2, 1, 256, 12.0)])
+                                                      (1, 256, 32, 2, 1, 256, 12.0), (1, 100, 20, 2, 1, 128, 3.0)])
 def test_attention_forward_many_tiles(leak, B, L, block, Hq, Hk, D, qscale):
     """Many key tiles per query tile (the tcgen05 forward's pipeline, tile skipping, masks inside
     partial tiles, row tails) and large score ranges (the running max moves by more than 2^8, so

@@ -147,6 +147,22 @@ class ModelConfig:
             name=name,
         )
 
+    def to_hf_dict(self) -> dict:
+        """HF Qwen3.5 text `config.json` for this config (the inverse of `from_hf_dict`)."""
+        return {"model_type": "qwen3_5_text", "architectures": ["Qwen3_5ForCausalLM"],
+                "vocab_size": self.vocab_size, "hidden_size": self.hidden_size,
+                "intermediate_size": self.intermediate_size, "num_hidden_layers": self.num_hidden_layers,
+                "layer_types": list(self.layer_types), "num_attention_heads": self.num_attention_heads,
+                "num_key_value_heads": self.num_key_value_heads, "head_dim": self.head_dim,
+                "rope_parameters": {"rope_type": "default", "rope_theta": self.rope_theta,
+                                    "partial_rotary_factor": self.partial_rotary_factor},
+                "linear_num_key_heads": self.linear_num_key_heads,
+                "linear_num_value_heads": self.linear_num_value_heads,
+                "linear_key_head_dim": self.linear_key_head_dim, "linear_value_head_dim": self.linear_value_head_dim,
+                "linear_conv_kernel_dim": self.linear_conv_kernel_dim, "rms_norm_eps": self.rms_norm_eps,
+                "tie_word_embeddings": self.tie_word_embeddings, "initializer_range": self.initializer_range,
+                "torch_dtype": "bfloat16"}
+
     @classmethod
     def from_pretrained_dir(cls, path: str) -> "ModelConfig":
         with open(os.path.join(path, "config.json")) as f:

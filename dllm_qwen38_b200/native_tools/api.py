@@ -36,7 +36,8 @@ def load(spec: str, layers: int = 0):
     if os.path.isdir(spec):
         from ..io.hf_load import load_model
 
-        return load_model(spec, dtype=dtype, device=dev, layers=layers or None)
+        model, _ = load_model(spec, dtype=dtype, device=dev, layers=layers or None)
+        return model
     cfg = preset(spec, layers=layers or None)
     return build_model(cfg, seed=0, device=dev, dtype=dtype)
 

@@ -95,6 +95,26 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M 128 x K 16, bf16) is read from TMEM, row i in lane i,
+// consecutive K pairs packed in consecutive 32-bit columns (8 columns per instruction)
+__device__ __forceinline__ void mma_bf16_ta(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -478,11 +498,11 @@ __global__ void __launch_bounds__(NTHR, 1)
 }
 
 // ================================================================== backward: dQ
-// One CTA = 128 query rows of one (batch, query head), key tiles of 32 (two-stage K/V ring):
+// One CTA = 128 query rows of one (batch, query head), key tiles of 32:
 //   S = Q K^T and dP = dO V^T (M 128, N 32, K D) into double-buffered TMEM;
 //   warps 0-3 (thread = query row): P = 2^(S log2e scale - lse2), dS = P (dP - Delta), dS (bf16)
-//   into a 128-byte-swizzled smem tile (the first 64 bytes of each 128-byte row);
-//   dQ += dS K (M 128, N D, K 32) in TMEM, with K read N(=d)-contiguous.
+//   stored into TMEM (double-buffered), the A operand of the dQ MMA;
+//   dQ += dS K (M 128, N D, K 32) in TMEM, with K read N(=d)-contiguous, from a 3-stage K/V ring.
 // Delta = rowsum(dO * O) is computed by the row's thread at the start and stored for the dK/dV
 // kernel.
 constexpr int BK2 = 32;
@@ -492,13 +512,16 @@ struct QCfg {
   static constexpr int Q_BYTES = BQ * D * 2;    // Q, then dO: D/64 boxes of [128 rows][128 B]
   static constexpr int K_BYTES = BK2 * D * 2;   // D/64 boxes of [32 rows][128 B]
   static constexpr int STAGE = 2 * K_BYTES;     // K then V
-  static constexpr int DS_BYTES = BQ * 128;     // [128 rows][128 B] (64 B used per row)
-  static constexpr int SMEM = 2 * Q_BYTES + 2 * STAGE + 2 * DS_BYTES + 1024 + 256;
-  static constexpr int S_COL = 0, DP_COL = 64;  // two buffers of 32 columns each
-  static constexpr int DQ_COL = (D == 256) ? 256 : 128;
-  static constexpr int TMEM_COLS = (D == 256) ? 512 : 256;
+  static constexpr int NST_FIT = (227 * 1024 - 2 * Q_BYTES - 1024 - 256) / STAGE;
+  static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;  // K / V ring stages
+  static constexpr int SMEM = 2 * Q_BYTES + NST * STAGE + 1024 + 256;
+  // TMEM: S and dP (two buffers of 32 columns each), dS as the bf16 A operand of the dQ MMA (two
+  // buffers of 16 packed columns), dQ (D columns)
+  static constexpr int S_COL = 0, DP_COL = 64, DS_COL = 128, DQ_COL = 256;
+  static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BK2, 0, 0);
   static constexpr uint32_t IDESC_DQ = idesc_bf16(BQ, D, 0, 1);
+  static_assert(NST >= 2, "K / V ring needs two stages");
 };
 
 struct BArgs {
@@ -520,21 +543,21 @@ __global__ void __launch_bounds__(NTHR, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                      const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = QCfg<D>;
+  constexpr int NST = C::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sdO = smem + C::Q_BYTES;
   uint8_t* sKV = smem + 2 * C::Q_BYTES;
-  uint8_t* sdS = sKV + 2 * C::STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + 2 * C::DS_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NST * C::STAGE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 3;
-  uint64_t* sd_full = bars + 5;
-  uint64_t* ds_full = bars + 7;
-  uint64_t* dq_done = bars + 9;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* kv_empty = kv_full + NST;
+  uint64_t* sd_full = kv_empty + NST;
+  uint64_t* ds_full = sd_full + 2;
+  uint64_t* dq_done = ds_full + 2;
+  uint64_t* drain = dq_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -547,9 +570,11 @@ __global__ void __launch_bounds__(NTHR, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&sd_full[s], 1);
       mbar_init(&ds_full[s], 4);
       mbar_init(&dq_done[s], 1);
@@ -580,14 +605,15 @@ __global__ void __launch_bounds__(NTHR, 1)
         tma_load_2d(sQ + c * BQ * 128, &mq, q_full, h * D + c * 64, row0 + i0);
         tma_load_2d(sdO + c * BQ * 128, &mdo, q_full, h * D + c * 64, row0 + i0);
       }
-      uint32_t armed = 0;
-      int it = 0;
-      for (; it < nt; ++it) {
+      int last[NST];
+#pragma unroll
+      for (int s = 0; s < NST; ++s) last[s] = -1;
+      for (int it = 0; it < nt; ++it) {
         const int jt = sp.at(it);
-        const int s = it & 1;
-        if (!mbar_wait(&kv_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        const int s = it % NST;
+        if (!mbar_wait(&kv_empty[s], ((it / NST) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
-        armed |= 1u << s;
+        last[s] = it;
         uint8_t* dk = sKV + s * C::STAGE;
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
@@ -596,11 +622,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
-      for (int s = 0; s < 2; ++s)
-        if (armed & (1u << s)) {
-          const int last = ((it - 1) & 1) == s ? it - 1 : it - 2;
-          if (last >= 0) mbar_wait(&kv_full[s], (last >> 1) & 1, a.err, ERR_ATTN_WAIT, nullptr);
-        }
+#pragma unroll
+      for (int s = 0; s < NST; ++s)
+        if (last[s] >= 0) mbar_wait(&kv_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -609,8 +633,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sdO);
       auto issue_sdp = [&](int it) {
-        const int s = it & 1;
-        const uint32_t k_addr = smem_u32(sKV + s * C::STAGE), v_addr = k_addr + C::K_BYTES;
+        const int s = it & 1;  // TMEM buffer
+        const uint32_t k_addr = smem_u32(sKV + (it % NST) * C::STAGE), v_addr = k_addr + C::K_BYTES;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t oq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
@@ -632,21 +656,20 @@ __global__ void __launch_bounds__(NTHR, 1)
       }
       for (int it = 0; ok && it < nt; ++it) {
         if (it + 1 < nt) {
-          if (!mbar_wait(&kv_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+          if (!mbar_wait(&kv_full[(it + 1) % NST], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
           issue_sdp(it + 1);
         }
         const int s = it & 1;
         if (!mbar_wait(&ds_full[s], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
-        const uint32_t ds_addr = smem_u32(sdS + s * C::DS_BYTES);
-        const uint32_t k_addr = smem_u32(sKV + s * C::STAGE);
+        const uint32_t k_addr = smem_u32(sKV + (it % NST) * C::STAGE);
 #pragma unroll
         for (int kk = 0; kk < BK2 / 16; ++kk)
-          mma_bf16(tmem + C::DQ_COL, smem_desc(ds_addr + kk * 32, 16, 1024),
-                   smem_desc(k_addr + kk * 2048, BK2 * 128, 1024), C::IDESC_DQ, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ta(tmem + C::DQ_COL, tmem + C::DS_COL + s * 16 + kk * 8,
+                      smem_desc(k_addr + kk * 2048, BK2 * 128, 1024), C::IDESC_DQ, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&dq_done[s]);
-        mma_commit(&kv_empty[s]);
+        mma_commit(&kv_empty[it % NST]);
       }
       mma_commit(drain);
       mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
@@ -712,12 +735,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         ok = false;
         break;
       }
-      uint8_t* drow = sdS + s * C::DS_BYTES + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        *reinterpret_cast<uint4*>(drow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async();
+      tmem_st16(tmem + lane_base + C::DS_COL + s * 16, pk);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ds_full[s]);
@@ -757,10 +776,11 @@ __global__ void __launch_bounds__(NTHR, 1)
 // ================================================================== backward: dK, dV
 // One CTA = 128 keys of one (batch, kv head) and one 128-column slice z of dK / dV (D 256 runs
 // two CTAs per key tile); it loops over the query heads of the GQA group and their 32-row query
-// tiles that may see the key tile (two-stage Q / dO ring):
+// tiles that may see the key tile (Q / dO ring of up to 4 stages):
 //   S^T = K Q^T and dP^T = V dO^T (M 128 keys, N 32, K D) into double-buffered TMEM;
 //   warps 0-3 (thread = key): P^T = 2^(S^T log2e scale - lse2[q]), dS^T = P^T (dP^T - Delta[q]),
-//   both (bf16) into 128-byte-swizzled smem tiles;
+//   both (bf16) stored into TMEM (tcgen05.st, double-buffered), where the gradient MMAs read them
+//   as their A operand (so the smem holds K, V and a 3-stage Q / dO ring);
 //   dV += P^T dO[:, z] and dK += dS^T Q[:, z] (M 128, N 128, K 32) in TMEM.
 constexpr int BQ2 = 32;
 
@@ -769,12 +789,16 @@ struct KCfg {
   static constexpr int KV_BYTES = BQ * D * 2;   // K, then V: D/64 boxes of [128 rows][128 B]
   static constexpr int T_BYTES = BQ2 * D * 2;   // Q tile, then dO tile: D/64 boxes of [32 rows][128 B]
   static constexpr int STAGE = 2 * T_BYTES;
-  static constexpr int PT_BYTES = BQ * 128;     // [128 keys][128 B] (64 B used per row)
-  static constexpr int SMEM = 2 * KV_BYTES + 2 * STAGE + 2 * PT_BYTES + 1024 + 256;
-  static constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 256;
+  static constexpr int NST_FIT = (227 * 1024 - 2 * KV_BYTES - 1024 - 256) / STAGE;
+  static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;  // Q / dO ring stages
+  static constexpr int SMEM = 2 * KV_BYTES + NST * STAGE + 1024 + 256;
+  // TMEM: S^T and dP^T (two buffers of 32 columns each), dV and dK slices (128 each), and the bf16
+  // P^T / dS^T operands of the gradient MMAs (two buffers of 16 packed columns each)
+  static constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 256, PT_COL = 384, DST_COL = 416;
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BQ2, 0, 0);
   static constexpr uint32_t IDESC_G = idesc_bf16(BQ, 128, 0, 1);
+  static_assert(NST >= 2, "Q / dO ring needs two stages");
 };
 
 template <int D>
@@ -782,22 +806,21 @@ __global__ void __launch_bounds__(NTHR, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                       const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = KCfg<D>;
+  constexpr int NST = C::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + C::KV_BYTES;
   uint8_t* sT = smem + 2 * C::KV_BYTES;  // stage s: Q tile at sT + s * STAGE, dO tile + T_BYTES
-  uint8_t* sPT = sT + 2 * C::STAGE;
-  uint8_t* sDST = sPT + C::PT_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDST + C::PT_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sT + NST * C::STAGE);
   uint64_t* kv_full = bars;
   uint64_t* t_full = bars + 1;
-  uint64_t* t_empty = bars + 3;
-  uint64_t* st_full = bars + 5;
-  uint64_t* pt_full = bars + 7;
-  uint64_t* g_done = bars + 8;
-  uint64_t* drain = bars + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* t_empty = t_full + NST;
+  uint64_t* st_full = t_empty + NST;
+  uint64_t* pt_full = st_full + 2;
+  uint64_t* g_done = pt_full + 2;
+  uint64_t* drain = g_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -814,13 +837,15 @@ __global__ void __launch_bounds__(NTHR, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(&t_full[s], 1);
       mbar_init(&t_empty[s], 1);
-      mbar_init(&st_full[s], 1);
     }
-    mbar_init(pt_full, 4);
-    mbar_init(g_done, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&st_full[s], 1);
+      mbar_init(&pt_full[s], 4);
+      mbar_init(&g_done[s], 1);
+    }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -847,13 +872,14 @@ __global__ void __launch_bounds__(NTHR, 1)
         tma_load_2d(sK + c * BQ * 128, &mk, kv_full, hk * D + c * 64, row0 + j0);
         tma_load_2d(sV + c * BQ * 128, &mv, kv_full, hk * D + c * 64, row0 + j0);
       }
-      uint32_t armed = 0;
-      int it = 0;
-      for (; it < total; ++it) {
-        const int s = it & 1;
-        if (!mbar_wait(&t_empty[s], ((it >> 1) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+      int last[NST];
+#pragma unroll
+      for (int s = 0; s < NST; ++s) last[s] = -1;
+      for (int it = 0; it < total; ++it) {
+        const int s = it % NST;
+        if (!mbar_wait(&t_empty[s], ((it / NST) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         mbar_arrive_expect_tx(&t_full[s], C::STAGE);
-        armed |= 1u << s;
+        last[s] = it;
         const int hq = hk * rep + it / nqv, i0 = sp.at(it % nqv) * BQ2;
         uint8_t* dst = sT + s * C::STAGE;
 #pragma unroll
@@ -863,11 +889,9 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       mbar_wait(kv_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
-      for (int s = 0; s < 2; ++s)
-        if (armed & (1u << s)) {
-          const int last = ((it - 1) & 1) == s ? it - 1 : it - 2;
-          if (last >= 0) mbar_wait(&t_full[s], (last >> 1) & 1, a.err, ERR_ATTN_WAIT, nullptr);
-        }
+#pragma unroll
+      for (int s = 0; s < NST; ++s)
+        if (last[s] >= 0) mbar_wait(&t_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -876,18 +900,18 @@ __global__ void __launch_bounds__(NTHR, 1)
       tc_fence_after();
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       auto issue_s = [&](int it) {
-        const int s = it & 1;
-        const uint32_t q_addr = smem_u32(sT + s * C::STAGE), do_addr = q_addr + C::T_BYTES;
+        const uint32_t q_addr = smem_u32(sT + (it % NST) * C::STAGE), do_addr = q_addr + C::T_BYTES;
+        const int sb = it & 1;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t okv = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
           const uint32_t ot = (kk >> 2) * (BQ2 * 128) + (kk & 3) * 32;
-          mma_bf16(tmem + C::ST_COL + s * BQ2, smem_desc(k_addr + okv, 16, 1024), smem_desc(q_addr + ot, 16, 1024),
+          mma_bf16(tmem + C::ST_COL + sb * BQ2, smem_desc(k_addr + okv, 16, 1024), smem_desc(q_addr + ot, 16, 1024),
                    C::IDESC_S, kk > 0 ? 1u : 0u);
-          mma_bf16(tmem + C::DPT_COL + s * BQ2, smem_desc(v_addr + okv, 16, 1024),
+          mma_bf16(tmem + C::DPT_COL + sb * BQ2, smem_desc(v_addr + okv, 16, 1024),
                    smem_desc(do_addr + ot, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&st_full[s]);
+        mma_commit(&st_full[sb]);
       };
       if (ok && total > 0) {
         if (mbar_wait(&t_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
@@ -897,27 +921,27 @@ __global__ void __launch_bounds__(NTHR, 1)
           ok = false;
         }
       }
-      const uint32_t pt_addr = smem_u32(sPT), dst_addr = smem_u32(sDST);
       for (int it = 0; ok && it < total; ++it) {
         if (it + 1 < total) {
-          if (!mbar_wait(&t_full[(it + 1) & 1], ((it + 1) >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+          if (!mbar_wait(&t_full[(it + 1) % NST], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
           tc_fence_after();
           issue_s(it + 1);
         }
-        const int s = it & 1;
-        if (!mbar_wait(pt_full, it & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        const int pb = it & 1;
+        if (!mbar_wait(&pt_full[pb], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
+        const int s = it % NST;
         const uint32_t q_addr = smem_u32(sT + s * C::STAGE) + z * 2 * (BQ2 * 128);
         const uint32_t do_addr = smem_u32(sT + s * C::STAGE + C::T_BYTES) + z * 2 * (BQ2 * 128);
 #pragma unroll
         for (int kk = 0; kk < BQ2 / 16; ++kk) {
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          mma_bf16(tmem + C::DV_COL, smem_desc(pt_addr + kk * 32, 16, 1024),
-                   smem_desc(do_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
-          mma_bf16(tmem + C::DK_COL, smem_desc(dst_addr + kk * 32, 16, 1024),
-                   smem_desc(q_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
+          mma_bf16_ta(tmem + C::DV_COL, tmem + C::PT_COL + pb * 16 + kk * 8,
+                      smem_desc(do_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
+          mma_bf16_ta(tmem + C::DK_COL, tmem + C::DST_COL + pb * 16 + kk * 8,
+                      smem_desc(q_addr + kk * 2048, BQ2 * 128, 1024), C::IDESC_G, acc);
         }
-        mma_commit(g_done);
+        mma_commit(&g_done[pb]);
         mma_commit(&t_empty[s]);
       }
       mma_commit(drain);
@@ -934,7 +958,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     int it = 0;
     bool ok = true;
     for (; it < total; ++it) {
-      const int s = it & 1;
+      const int sb = it & 1;
       const int hq = hk * rep + it / nqv, i0 = sp.at(it % nqv) * BQ2;
       // lane c holds lse2 / Delta of query row i0 + c
       const int qr = i0 + lane;
@@ -942,14 +966,14 @@ __global__ void __launch_bounds__(NTHR, 1)
       float lse_l = qr < a.T2 ? a.lse2[hoff + qr] : INFINITY;
       if (lse_l == NEG_INF) lse_l = INFINITY;  // a row that sees nothing: every p is 0
       const float dl_l = qr < a.T2 ? a.delta[hoff + qr] : 0.f;
-      if (!warp_wait(&st_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+      if (!warp_wait(&st_full[sb], (it >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t rs[32], rp[32];
-      tmem_ld32_async(tmem + lane_base + C::ST_COL + s * BQ2, rs);
-      tmem_ld32_async(tmem + lane_base + C::DPT_COL + s * BQ2, rp);
+      tmem_ld32_async(tmem + lane_base + C::ST_COL + sb * BQ2, rs);
+      tmem_ld32_async(tmem + lane_base + C::DPT_COL + sb * BQ2, rp);
       tmem_wait_ld(rs);
       tmem_wait_ld(rp);
       const bool full = __all_sync(0xffffffffu, kv.seen_by_all(i0, i0 + BQ2 - 1, a.L, a.T2));
@@ -962,7 +986,7 @@ __global__ void __launch_bounds__(NTHR, 1)
           const int cc = 2 * c + e;
           const float lq = __shfl_sync(0xffffffffu, lse_l, cc);
           const float dq = __shfl_sync(0xffffffffu, dl_l, cc);
-          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, -lq));  // lse -inf (dead row): masked below
+          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, -lq));
           if (!full && !kv.seen_by(i0 + cc, a.L, a.T2)) p = 0.f;
           p2[e] = p;
           d2[e] = p * (__uint_as_float(rp[cc]) - dq);
@@ -970,26 +994,19 @@ __global__ void __launch_bounds__(NTHR, 1)
         pp[c] = pack_bf16(p2[0], p2[1]);
         pd[c] = pack_bf16(d2[0], d2[1]);
       }
-      // the P^T / dS^T tiles were read by the gradient MMAs of iteration it-1
-      if (it >= 1 && !warp_wait(g_done, (it - 1) & 1, a.err, abort_flag)) {
+      // the TMEM operand buffers sb were read by the gradient MMAs of iteration it-2
+      if (it >= 2 && !warp_wait(&g_done[sb], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
-      uint8_t* prow = sPT + r * 128;
-      uint8_t* drow = sDST + r * 128;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pp[4 * c], pp[4 * c + 1], pp[4 * c + 2], pp[4 * c + 3]);
-        *reinterpret_cast<uint4*>(drow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pd[4 * c], pd[4 * c + 1], pd[4 * c + 2], pd[4 * c + 3]);
-      }
-      fence_proxy_async();
+      tmem_st16(tmem + lane_base + C::PT_COL + sb * 16, pp);
+      tmem_st16(tmem + lane_base + C::DST_COL + sb * 16, pd);
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(pt_full);
+      if (lane == 0) mbar_arrive(&pt_full[sb]);
     }
-    if (ok && it > 0 && !warp_wait(g_done, (it - 1) & 1, a.err, abort_flag)) ok = false;
+    if (ok && it > 0 && !warp_wait(&g_done[(it - 1) & 1], ((it - 1) >> 1) & 1, a.err, abort_flag)) ok = false;
     tc_fence_after();
     const int64_t ktok = (int64_t)a.Hk * D;
     __nv_bfloat16* krow = a.dk + ((int64_t)b * a.T2 + key) * ktok + hk * D + z * 128;

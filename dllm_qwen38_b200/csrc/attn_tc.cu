@@ -3,14 +3,16 @@
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and
 // 256. One CTA = 128 query rows of one (batch, query head); 6 warps:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 64 (or 32) keys into a ring
-//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 64, K D) into one of two TMEM score
-//               buffers, O += P V (M 128, N D, K 64) into the TMEM output accumulator
-//   warps 0-3   softmax: thread = query row = TMEM lane; reads its 64 scores with tcgen05.ld,
-//               masks, keeps a running max and sum, writes P (bf16) into a 128-byte-swizzled smem
-//               tile that the next MMA reads as its K-major A operand
-// The score MMA of tile j+1 is issued before the softmax of tile j, so the tensor pipe computes it
-// while the softmax runs. O is rescaled lazily: a row's reference max moves only when a new score
+//   warp 4      TMA producer: the Q tile once, then K and V tiles of 32 (or 64) keys into a ring
+//               of as many stages as fit (5 at D 256)
+//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 32, K D) into one of three TMEM score
+//               buffers, up to two tiles ahead, and O += P V (M 128, N D, K 32) into the TMEM output
+//               accumulator, with P read from TMEM as the A operand
+//   warps 0-3   softmax: thread = query row = TMEM lane; reads its scores with tcgen05.ld, masks,
+//               keeps a running max and sum, and stores P (bf16, packed pairs) into TMEM
+//               (tcgen05.st, double-buffered)
+// Score MMAs run ahead of the softmax, so the tensor pipe computes the next tiles' scores while the
+// softmax of this one runs. O is rescaled lazily: a row's reference max moves only when a new score
 // exceeds it by more than 2^8 (the probabilities stay <= 256, exact in fp32 / bf16 range), and the
 // rescale reads O from TMEM, scales it and stores it back (tcgen05.st) after the previous O MMA
 // has completed. Every mbarrier wait is bounded; on expiry the CTA records ERR_ATTN_WAIT, drains
@@ -32,22 +34,25 @@ constexpr int NTHR = 192;
 constexpr float NEG_INF = -INFINITY;
 constexpr float RESCALE_LOG2 = 8.f;
 
-template <int D, int BKV_ = 64>
+template <int D, int BKV_ = 32>
 struct FCfg {
   static constexpr int BKV = BKV_;             // keys per tile
   static constexpr int Q_BYTES = BQ * D * 2;   // D/64 boxes of [128 rows][128 B]
   static constexpr int K_BYTES = BKV * D * 2;  // D/64 boxes of [BKV rows][128 B]
   static constexpr int STAGE = 2 * K_BYTES;    // K then V
-  static constexpr int P_BYTES = BQ * 128;     // [128 rows][128 B] swizzle atoms, 2*BKV bytes used per row
-  // as many K/V stages as fit next to Q and the two P tiles (<= 4)
-  static constexpr int NST_FIT = (227 * 1024 - Q_BYTES - 2 * P_BYTES - 1024 - 256) / STAGE;
-  static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;
-  static constexpr int SMEM = Q_BYTES + NST * STAGE + 2 * P_BYTES + 1024 + 256;
-  static constexpr int O_COL = (D == 256) ? 256 : 128;  // TMEM column of O; S buffers at 0 and BKV
-  static constexpr int TMEM_COLS = (D == 256) ? 512 : 256;
+  static constexpr int NST_FIT = (227 * 1024 - Q_BYTES - 1024 - 256) / STAGE;
+  static constexpr int NST = NST_FIT > 6 ? 6 : NST_FIT;  // K/V ring stages
+  static constexpr int NS = 3;                 // TMEM score buffers
+  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // score MMAs issued ahead
+  static constexpr int SMEM = Q_BYTES + NST * STAGE + 1024 + 256;
+  // TMEM: NS score buffers of BKV columns, two bf16 P buffers of BKV/2 packed columns (the A
+  // operand of the PV MMA), and O (D columns)
+  static constexpr int S_COL = 0, P_COL = NS * BKV;
+  static constexpr int O_COL = (P_COL + BKV <= 128 && D <= 128) ? 128 : 256;
+  static constexpr int TMEM_COLS = (O_COL + D <= 256) ? 256 : 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV, 0, 0);
   static constexpr uint32_t IDESC_O = idesc_bf16(BQ, D, 0, 1);  // V read N(=d)-contiguous
-  static_assert(NST >= 2, "K/V ring needs two stages");
+  static_assert(NST >= 2 && P_COL + BKV <= O_COL && O_COL + D <= 512, "attention forward resources");
 };
 
 struct FArgs {
@@ -243,18 +248,17 @@ __global__ void __launch_bounds__(NTHR, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, FArgs a) {
   using C = FCfg<D, BKV_>;
-  constexpr int BKV = C::BKV, NST = C::NST;
+  constexpr int BKV = C::BKV, NST = C::NST, NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::Q_BYTES;
-  uint8_t* sP = sKV + NST * C::STAGE;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * C::P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NST * C::STAGE);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + NST;
   uint64_t* s_full = kv_empty + NST;
-  uint64_t* p_full = s_full + 2;
+  uint64_t* p_full = s_full + NS;
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -276,8 +280,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int s = 0; s < NS; ++s) mbar_init(&s_full[s], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 4);  // one arrive per softmax warp
       mbar_init(&o_done[s], 1);
     }
@@ -331,41 +335,35 @@ __global__ void __launch_bounds__(NTHR, 1)
       bool ok = mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ);
-      auto issue_s = [&](int it) {
-        const uint32_t k_addr = smem_u32(sKV + (it % NST) * C::STAGE);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off_q = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
-          const uint32_t off_k = (kk >> 2) * (BKV * 128) + (kk & 3) * 32;
-          mma_bf16(tmem + (it & 1) * BKV, smem_desc(q_addr + off_q, 16, 1024), smem_desc(k_addr + off_k, 16, 1024),
-                   C::IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&s_full[it & 1]);
-      };
-      if (ok && nt > 0) {
-        if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
-          tc_fence_after();
-          issue_s(0);
-        } else {
-          ok = false;
-        }
-      }
+      int issued = 0;  // score MMAs issued so far; up to AHEAD tiles ahead of the PV being waited
       for (int it = 0; ok && it < nt; ++it) {
-        if (it + 1 < nt) {
-          const int s1 = (it + 1) % NST;
-          if (!mbar_wait(&kv_full[s1], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        while (issued < nt && issued <= it + C::AHEAD) {
+          if (!mbar_wait(&kv_full[issued % NST], (issued / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_s(it + 1);
+          const uint32_t k_addr = smem_u32(sKV + (issued % NST) * C::STAGE);
+          const uint32_t d_s = tmem + C::S_COL + (issued % NS) * BKV;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off_q = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+            const uint32_t off_k = (kk >> 2) * (BKV * 128) + (kk & 3) * 32;
+            mma_bf16(d_s, smem_desc(q_addr + off_q, 16, 1024), smem_desc(k_addr + off_k, 16, 1024), C::IDESC_S,
+                     kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&s_full[issued % NS]);
+          ++issued;
         }
+        if (!ok) break;
         const int pb = it & 1;
         if (!mbar_wait(&p_full[pb], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
-        const uint32_t p_addr = smem_u32(sP + pb * C::P_BYTES);
         const uint32_t v_addr = smem_u32(sKV + (it % NST) * C::STAGE + C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          mma_bf16(tmem + C::O_COL, smem_desc(p_addr + kk * 32, 16, 1024),
-                   smem_desc(v_addr + kk * 2048, BKV * 128, 1024), C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ta(tmem + C::O_COL, tmem + C::P_COL + pb * (BKV / 2) + kk * 8,
+                      smem_desc(v_addr + kk * 2048, BKV * 128, 1024), C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&o_done[pb]);
         mma_commit(&kv_empty[it % NST]);
       }
@@ -385,9 +383,9 @@ __global__ void __launch_bounds__(NTHR, 1)
     int it = 0;
     bool ok = true;
     for (; it < nt; ++it) {
-      const int s = it & 1;
+      const int sb = it % NS, pb = it & 1;
       const int j0 = sp.at(it) * BKV;
-      if (!warp_wait(&s_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+      if (!warp_wait(&s_full[sb], (it / NS) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -396,7 +394,7 @@ __global__ void __launch_bounds__(NTHR, 1)
 #pragma unroll
       for (int h2 = 0; h2 < BKV / 32; ++h2) {
         uint32_t ra[32];
-        tmem_ld32_async(tmem + lane_base + s * BKV + h2 * 32, ra);
+        tmem_ld32_async(tmem + lane_base + C::S_COL + sb * BKV + h2 * 32, ra);
         tmem_wait_ld(ra);
 #pragma unroll
         for (int c = 0; c < 32; ++c) x[h2 * 32 + c] = __uint_as_float(ra[c]);
@@ -447,20 +445,22 @@ __global__ void __launch_bounds__(NTHR, 1)
         pk[c] = pack_bf16(p0, p1);
       }
       l += ((r8[0] + r8[1]) + (r8[2] + r8[3])) + ((r8[4] + r8[5]) + (r8[6] + r8[7]));
-      // the P buffer s was read by the O MMA of tile it-2
-      if (it >= 2 && !warp_wait(&o_done[s], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
+      // the P buffer pb was read by the O MMA of tile it-2
+      if (it >= 2 && !warp_wait(&o_done[pb], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
-      uint8_t* prow = sP + s * C::P_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < BKV / 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async();  // generic smem writes -> visible to the tensor core's async proxy
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t q16[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) q16[e] = pk[c * 16 + e];
+        tmem_st16(tmem + lane_base + C::P_COL + pb * (BKV / 2) + c * 16, q16);
+      }
+      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[s]);
+      if (lane == 0) mbar_arrive(&p_full[pb]);
     }
     // epilogue: O / l (bf16) and the row's log2-sum-exp
     if (ok && it > 0 && !warp_wait(&o_done[(it - 1) & 1], ((it - 1) >> 1) & 1, a.err, abort_flag)) ok = false;
@@ -1140,10 +1140,10 @@ bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   const int64_t D = q.size(3);
   if (D != 128 && D != 256) return false;
   bind_context(q.get_device());
-  static int bkv = -1;  // BDLLM_ATTN_BKV=32 selects 32-key tiles (more ring stages)
+  static int bkv = -1;  // BDLLM_ATTN_BKV=64 selects 64-key tiles (fewer ring stages)
   if (bkv < 0) {
     const char* e = getenv("BDLLM_ATTN_BKV");
-    bkv = (e != nullptr && atoi(e) == 32) ? 32 : 64;
+    bkv = (e != nullptr && atoi(e) == 64) ? 64 : 32;
   }
   if (D == 128)
     bkv == 32 ? attn_tc::launch<128, 32>(q, k, v, o, lse, L, block, scale, leak)

@@ -515,9 +515,11 @@ struct QCfg {
   static constexpr int NST_FIT = (227 * 1024 - 2 * Q_BYTES - 1024 - 256) / STAGE;
   static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;  // K / V ring stages
   static constexpr int SMEM = 2 * Q_BYTES + NST * STAGE + 1024 + 256;
-  // TMEM: S and dP (two buffers of 32 columns each), dS as the bf16 A operand of the dQ MMA (two
+  // TMEM: S and dP (NS buffers of 32 columns each), dS as the bf16 A operand of the dQ MMA (two
   // buffers of 16 packed columns), dQ (D columns)
-  static constexpr int S_COL = 0, DP_COL = 64, DS_COL = 128, DQ_COL = 256;
+  static constexpr int NS = 3;
+  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // S / dP MMAs issued ahead
+  static constexpr int S_COL = 0, DP_COL = NS * BK2, DS_COL = 2 * NS * BK2, DQ_COL = 256;
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BK2, 0, 0);
   static constexpr uint32_t IDESC_DQ = idesc_bf16(BQ, D, 0, 1);
@@ -543,7 +545,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                      const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = QCfg<D>;
-  constexpr int NST = C::NST;
+  constexpr int NST = C::NST, NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -554,7 +556,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + NST;
   uint64_t* sd_full = kv_empty + NST;
-  uint64_t* ds_full = sd_full + 2;
+  uint64_t* ds_full = sd_full + NS;
   uint64_t* dq_done = ds_full + 2;
   uint64_t* drain = dq_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -574,8 +576,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
+    for (int s = 0; s < NS; ++s) mbar_init(&sd_full[s], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&sd_full[s], 1);
       mbar_init(&ds_full[s], 4);
       mbar_init(&dq_done[s], 1);
     }
@@ -632,34 +634,29 @@ __global__ void __launch_bounds__(NTHR, 1)
       bool ok = mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
       tc_fence_after();
       const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sdO);
-      auto issue_sdp = [&](int it) {
-        const int s = it & 1;  // TMEM buffer
-        const uint32_t k_addr = smem_u32(sKV + (it % NST) * C::STAGE), v_addr = k_addr + C::K_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t oq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
-          const uint32_t ok_ = (kk >> 2) * (BK2 * 128) + (kk & 3) * 32;
-          mma_bf16(tmem + C::S_COL + s * BK2, smem_desc(q_addr + oq, 16, 1024), smem_desc(k_addr + ok_, 16, 1024),
-                   C::IDESC_S, kk > 0 ? 1u : 0u);
-          mma_bf16(tmem + C::DP_COL + s * BK2, smem_desc(do_addr + oq, 16, 1024), smem_desc(v_addr + ok_, 16, 1024),
-                   C::IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&sd_full[s]);
-      };
-      if (ok && nt > 0) {
-        if (mbar_wait(&kv_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
-          tc_fence_after();
-          issue_sdp(0);
-        } else {
-          ok = false;
-        }
-      }
+      int issued = 0;  // S / dP MMA pairs issued; up to AHEAD tiles ahead of the dQ MMA being waited
       for (int it = 0; ok && it < nt; ++it) {
-        if (it + 1 < nt) {
-          if (!mbar_wait(&kv_full[(it + 1) % NST], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        while (issued < nt && issued <= it + C::AHEAD) {
+          if (!mbar_wait(&kv_full[issued % NST], (issued / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_sdp(it + 1);
+          const uint32_t k_addr = smem_u32(sKV + (issued % NST) * C::STAGE), v_addr = k_addr + C::K_BYTES;
+          const int sb = issued % NS;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oq = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+            const uint32_t ok_ = (kk >> 2) * (BK2 * 128) + (kk & 3) * 32;
+            mma_bf16(tmem + C::S_COL + sb * BK2, smem_desc(q_addr + oq, 16, 1024), smem_desc(k_addr + ok_, 16, 1024),
+                     C::IDESC_S, kk > 0 ? 1u : 0u);
+            mma_bf16(tmem + C::DP_COL + sb * BK2, smem_desc(do_addr + oq, 16, 1024),
+                     smem_desc(v_addr + ok_, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&sd_full[sb]);
+          ++issued;
         }
+        if (!ok) break;
         const int s = it & 1;
         if (!mbar_wait(&ds_full[s], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
@@ -705,16 +702,16 @@ __global__ void __launch_bounds__(NTHR, 1)
     int it = 0;
     bool ok = true;
     for (; it < nt; ++it) {
-      const int s = it & 1;
+      const int s = it & 1, sb = it % NS;
       const int j0 = sp.at(it) * BK2;
-      if (!warp_wait(&sd_full[s], (it >> 1) & 1, a.err, abort_flag)) {
+      if (!warp_wait(&sd_full[sb], (it / NS) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t rs[32], rp[32];
-      tmem_ld32_async(tmem + lane_base + C::S_COL + s * BK2, rs);
-      tmem_ld32_async(tmem + lane_base + C::DP_COL + s * BK2, rp);
+      tmem_ld32_async(tmem + lane_base + C::S_COL + sb * BK2, rs);
+      tmem_ld32_async(tmem + lane_base + C::DP_COL + sb * BK2, rp);
       tmem_wait_ld(rs);
       tmem_wait_ld(rp);
       const bool full = __all_sync(0xffffffffu, vis.sees_all(j0, j0 + BK2 - 1, a.L));
@@ -792,10 +789,14 @@ struct KCfg {
   static constexpr int NST_FIT = (227 * 1024 - 2 * KV_BYTES - 1024 - 256) / STAGE;
   static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;  // Q / dO ring stages
   static constexpr int SMEM = 2 * KV_BYTES + NST * STAGE + 1024 + 256;
-  // TMEM: S^T and dP^T (two buffers of 32 columns each), dV and dK slices (128 each), and the bf16
-  // P^T / dS^T operands of the gradient MMAs (two buffers of 16 packed columns each)
-  static constexpr int ST_COL = 0, DPT_COL = 64, DV_COL = 128, DK_COL = 256, PT_COL = 384, DST_COL = 416;
+  // TMEM: S^T and dP^T (NS buffers of 32 columns each), the bf16 P^T / dS^T operands of the
+  // gradient MMAs (two buffers of 16 packed columns each), dV and dK slices (128 columns each)
+  static constexpr int NS = 3;
+  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // S^T / dP^T MMAs issued ahead
+  static constexpr int ST_COL = 0, DPT_COL = NS * BQ2, PT_COL = 2 * NS * BQ2, DST_COL = PT_COL + BQ2,
+                       DV_COL = 256, DK_COL = 384;
   static constexpr int TMEM_COLS = 512;
+  static_assert(DST_COL + BQ2 <= DV_COL, "TMEM layout");
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BQ2, 0, 0);
   static constexpr uint32_t IDESC_G = idesc_bf16(BQ, 128, 0, 1);
   static_assert(NST >= 2, "Q / dO ring needs two stages");
@@ -806,7 +807,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                       const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = KCfg<D>;
-  constexpr int NST = C::NST;
+  constexpr int NST = C::NST, NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -817,7 +818,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* t_full = bars + 1;
   uint64_t* t_empty = t_full + NST;
   uint64_t* st_full = t_empty + NST;
-  uint64_t* pt_full = st_full + 2;
+  uint64_t* pt_full = st_full + NS;
   uint64_t* g_done = pt_full + 2;
   uint64_t* drain = g_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -841,8 +842,8 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_init(&t_full[s], 1);
       mbar_init(&t_empty[s], 1);
     }
+    for (int s = 0; s < NS; ++s) mbar_init(&st_full[s], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&st_full[s], 1);
       mbar_init(&pt_full[s], 4);
       mbar_init(&g_done[s], 1);
     }
@@ -899,34 +900,29 @@ __global__ void __launch_bounds__(NTHR, 1)
       bool ok = mbar_wait(kv_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
       tc_fence_after();
       const uint32_t k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      auto issue_s = [&](int it) {
-        const uint32_t q_addr = smem_u32(sT + (it % NST) * C::STAGE), do_addr = q_addr + C::T_BYTES;
-        const int sb = it & 1;
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t okv = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
-          const uint32_t ot = (kk >> 2) * (BQ2 * 128) + (kk & 3) * 32;
-          mma_bf16(tmem + C::ST_COL + sb * BQ2, smem_desc(k_addr + okv, 16, 1024), smem_desc(q_addr + ot, 16, 1024),
-                   C::IDESC_S, kk > 0 ? 1u : 0u);
-          mma_bf16(tmem + C::DPT_COL + sb * BQ2, smem_desc(v_addr + okv, 16, 1024),
-                   smem_desc(do_addr + ot, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(&st_full[sb]);
-      };
-      if (ok && total > 0) {
-        if (mbar_wait(&t_full[0], 0, a.err, ERR_ATTN_WAIT, abort_flag)) {
-          tc_fence_after();
-          issue_s(0);
-        } else {
-          ok = false;
-        }
-      }
+      int issued = 0;  // S^T / dP^T MMA pairs issued; up to AHEAD ahead of the gradient MMAs being waited
       for (int it = 0; ok && it < total; ++it) {
-        if (it + 1 < total) {
-          if (!mbar_wait(&t_full[(it + 1) % NST], ((it + 1) / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        while (issued < total && issued <= it + C::AHEAD) {
+          if (!mbar_wait(&t_full[issued % NST], (issued / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          issue_s(it + 1);
+          const uint32_t q_addr = smem_u32(sT + (issued % NST) * C::STAGE), do_addr = q_addr + C::T_BYTES;
+          const int sb = issued % NS;
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t okv = (kk >> 2) * (BQ * 128) + (kk & 3) * 32;
+            const uint32_t ot = (kk >> 2) * (BQ2 * 128) + (kk & 3) * 32;
+            mma_bf16(tmem + C::ST_COL + sb * BQ2, smem_desc(k_addr + okv, 16, 1024),
+                     smem_desc(q_addr + ot, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
+            mma_bf16(tmem + C::DPT_COL + sb * BQ2, smem_desc(v_addr + okv, 16, 1024),
+                     smem_desc(do_addr + ot, 16, 1024), C::IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          mma_commit(&st_full[sb]);
+          ++issued;
         }
+        if (!ok) break;
         const int pb = it & 1;
         if (!mbar_wait(&pt_full[pb], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
@@ -958,7 +954,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     int it = 0;
     bool ok = true;
     for (; it < total; ++it) {
-      const int sb = it & 1;
+      const int sb = it % NS, pb = it & 1;
       const int hq = hk * rep + it / nqv, i0 = sp.at(it % nqv) * BQ2;
       // lane c holds lse2 / Delta of query row i0 + c
       const int qr = i0 + lane;
@@ -966,7 +962,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       float lse_l = qr < a.T2 ? a.lse2[hoff + qr] : INFINITY;
       if (lse_l == NEG_INF) lse_l = INFINITY;  // a row that sees nothing: every p is 0
       const float dl_l = qr < a.T2 ? a.delta[hoff + qr] : 0.f;
-      if (!warp_wait(&st_full[sb], (it >> 1) & 1, a.err, abort_flag)) {
+      if (!warp_wait(&st_full[sb], (it / NS) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
@@ -994,17 +990,17 @@ __global__ void __launch_bounds__(NTHR, 1)
         pp[c] = pack_bf16(p2[0], p2[1]);
         pd[c] = pack_bf16(d2[0], d2[1]);
       }
-      // the TMEM operand buffers sb were read by the gradient MMAs of iteration it-2
-      if (it >= 2 && !warp_wait(&g_done[sb], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
+      // the TMEM operand buffers pb were read by the gradient MMAs of iteration it-2
+      if (it >= 2 && !warp_wait(&g_done[pb], ((it - 2) >> 1) & 1, a.err, abort_flag)) {
         ok = false;
         break;
       }
-      tmem_st16(tmem + lane_base + C::PT_COL + sb * 16, pp);
-      tmem_st16(tmem + lane_base + C::DST_COL + sb * 16, pd);
+      tmem_st16(tmem + lane_base + C::PT_COL + pb * 16, pp);
+      tmem_st16(tmem + lane_base + C::DST_COL + pb * 16, pd);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&pt_full[sb]);
+      if (lane == 0) mbar_arrive(&pt_full[pb]);
     }
     if (ok && it > 0 && !warp_wait(&g_done[(it - 1) & 1], ((it - 1) >> 1) & 1, a.err, abort_flag)) ok = false;
     tc_fence_after();

@@ -10,6 +10,7 @@ at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64
 std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
                                  int64_t block, int64_t mode);
 at::Tensor ce_rows_(at::Tensor& logits, const at::Tensor& tgt);
+void sumsq_(const at::Tensor& x, at::Tensor& sq, const c10::optional<at::Tensor>& dst);
 void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
                 double b2, double eps, double wd, double coef, const c10::optional<at::Tensor>& coef_dev, double bc1,
                 double bc2);
@@ -98,6 +99,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv_bwd", &bdllm::conv_bwd);
   m.def("ce_rows_", &bdllm::ce_rows_);
   m.def("adamw_step", &bdllm::adamw_step);
+  m.def("sumsq_", &bdllm::sumsq_, "sq += ||x||^2 (optionally writing x as fp32)", py::arg("x"), py::arg("sq"),
+        py::arg("dst") = c10::nullopt);
   m.def("gdn_fwd", &bdllm::gdn_fwd, "state-fork chunked gated delta rule forward");
   m.def("gdn_bwd", &bdllm::gdn_bwd, "state-fork chunked gated delta rule backward");
   m.def("attn_fwd", &bdllm::attn_fwd, "complementary-mask flash attention forward");

@@ -99,16 +99,37 @@ __device__ __forceinline__ void load_taps(const float* __restrict__ w, int c, fl
   }
 }
 
+// the K source rows of output row t (same rule as source_of, one division per row)
+template <int K>
+__device__ __forceinline__ void sources_of(int t, int L, int block, int mode, int (&src)[K]) {
+  if (mode == CONV_CONCAT || t >= L) {
+    const int lo = (mode == CONV_CONCAT) ? 0 : L;  // first row of the stream
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+      const int q = t + j - (K - 1);
+      src[j] = q >= lo ? q : -1;
+    }
+    return;
+  }
+  const int s = (t / block) * block;  // noised stream: own block, then the clean prefix (fork)
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int q = t + j - (K - 1);
+    src[j] = q >= s ? q : ((mode == CONV_FORK && q >= 0) ? L + q : -1);
+  }
+}
+
 template <int K>
 __device__ __forceinline__ void conv_row(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float (&wr)[8][K],
                                          int b, int t, int c, int T2, int L, int block, int mode, float (&acc)[8]) {
 #pragma unroll
   for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+  int src[K];
+  sources_of<K>(t, L, block, mode, src);
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    const int src = source_of(t, j - (K - 1), L, block, mode);
-    if (src < 0) continue;
-    const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src) * ld + c);
+    if (src[j] < 0) continue;
+    const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src[j]) * ld + c);
     const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -176,68 +197,91 @@ __global__ void conv_dpre_kernel(const __nv_bfloat16* __restrict__ raw, int64_t 
 }
 
 // draw[b, q, c] = sum over (t, j) with source_of(t, j-(K-1)) == q of dpre[b, t, c] * w[c, j].
-// A source row q is read only by output rows t in [q, q + K - 1] (its own stream) and, in fork
-// mode, by noised rows t in [q - L, q - L + K - 1] (clean source q >= L read as a block prefix).
+// A source row r is read by the rows t = r + d (d < K, tap K-1-d) of its own stream -- within its
+// block in the noised stream -- and, in fork mode, a clean row r = L + q also by the noised rows
+// t = q + d of later blocks (it is their clean prefix). Grid and threads as in the forward: 8
+// channels per thread, CONV_ROWS consecutive source rows per block row.
+template <int K>
+__device__ __forceinline__ void add_consumer(const float* __restrict__ dpre, int64_t row, int C, int c,
+                                             const float (&wr)[8][K], int j, float (&acc)[8]) {
+  const float4* p = reinterpret_cast<const float4*>(dpre + row * C + c);
+  const float4 u = p[0], v = p[1];
+  acc[0] += u.x * wr[0][j], acc[1] += u.y * wr[1][j], acc[2] += u.z * wr[2][j], acc[3] += u.w * wr[3][j];
+  acc[4] += v.x * wr[4][j], acc[5] += v.y * wr[5][j], acc[6] += v.z * wr[6][j], acc[7] += v.w * wr[7][j];
+}
+
 template <int K>
 __global__ void conv_dx_kernel(const float* __restrict__ dpre, const float* __restrict__ w,
                                __nv_bfloat16* __restrict__ draw, int64_t ldd, int B, int T2, int C, int L, int block,
                                int mode) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c >= C) return;
-  for (int row = blockIdx.y; row < B * T2; row += gridDim.y) {
-    const int q = row % T2, b = row / T2;
-    float acc = 0.f;
+  float wr[8][K];
+  load_taps<K>(w, c, wr);
+  const int r1 = min(B * T2, (int)(blockIdx.y + 1) * CONV_ROWS);
+  for (int row = blockIdx.y * CONV_ROWS; row < r1; ++row) {
+    const int b = row / T2, r = row - b * T2;
+    const int64_t base = (int64_t)b * T2;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    const int tend = (mode == CONV_CONCAT || r >= L) ? T2 : min(L, (r / block + 1) * block);
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      const int t = q + (K - 1) - j;  // same-stream consumer
-      if (t < T2 && source_of(t, j - (K - 1), L, block, mode) == q)
-        acc += dpre[((int64_t)b * T2 + t) * C + c] * w[c * K + j];
-      if (mode == CONV_FORK && q >= L) {  // noised consumer reading this clean row as a prefix
-        const int tn = q - L + (K - 1) - j;
-        if (tn < L && source_of(tn, j - (K - 1), L, block, mode) == q)
-          acc += dpre[((int64_t)b * T2 + tn) * C + c] * w[c * K + j];
+    for (int d = 0; d < K; ++d)
+      if (r + d < tend) add_consumer<K>(dpre, base + r + d, C, c, wr, K - 1 - d, acc);
+    if (mode == CONV_FORK && r >= L) {
+      const int q = r - L, later = (q / block + 1) * block;  // noised rows of later blocks
+#pragma unroll
+      for (int d = 0; d < K; ++d) {
+        const int t = q + d;
+        if (t < L && t >= later) add_consumer<K>(dpre, base + t, C, c, wr, K - 1 - d, acc);
       }
     }
-    draw[((int64_t)b * T2 + q) * ldd + c] = __float2bfloat16(acc);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+    *reinterpret_cast<uint4*>(draw + (base + r) * ldd + c) = o;
   }
 }
 
-// dw partials: block handles a token range for 32 channels x K taps; grid.y over channel groups.
+// dw partials: thread = 8 channels x K taps over `tokens_per_block` consecutive rows (grid.y);
+// part[chunk, c, j] is summed over chunks afterwards.
 template <int K>
 __global__ void conv_dw_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld, const float* __restrict__ dpre,
                                float* __restrict__ part, int B, int T2, int C, int L, int block, int mode,
                                int tokens_per_block) {
-  const int c = blockIdx.y * 32 + (threadIdx.x & 31);
-  const int sub = threadIdx.x >> 5;  // 8 token lanes
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c >= C) return;
-  float acc[K];
+  float acc[8][K];
 #pragma unroll
-  for (int j = 0; j < K; ++j) acc[j] = 0.f;
-  const int64_t total = (int64_t)B * T2;
-  const int64_t r0 = (int64_t)blockIdx.x * tokens_per_block;
-  const int64_t r1 = min(total, r0 + tokens_per_block);
-  for (int64_t r = r0 + sub; r < r1; r += 8) {
-    const int t = (int)(r % T2);
-    const int b = (int)(r / T2);
-    const float d = dpre[r * C + c];
+  for (int e = 0; e < 8; ++e)
 #pragma unroll
-    for (int j = 0; j < K; ++j) {
-      int src = source_of(t, j - (K - 1), L, block, mode);
-      if (src >= 0) acc[j] += d * __bfloat162float(raw[((int64_t)b * T2 + src) * ld + c]);
-    }
-  }
-  __shared__ float red[8][32][K];
-#pragma unroll
-  for (int j = 0; j < K; ++j) red[sub][threadIdx.x & 31][j] = acc[j];
-  __syncthreads();
-  if (sub == 0) {
+    for (int j = 0; j < K; ++j) acc[e][j] = 0.f;
+  const int total = B * T2;
+  const int r0 = blockIdx.y * tokens_per_block, r1 = min(total, r0 + tokens_per_block);
+  for (int row = r0; row < r1; ++row) {
+    const int b = row / T2, t = row - b * T2;
+    const float4* pd = reinterpret_cast<const float4*>(dpre + (int64_t)row * C + c);
+    const float4 u = pd[0], v = pd[1];
+    const float dv[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+    int src[K];
+    sources_of<K>(t, L, block, mode, src);
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      float s = 0.f;
-      for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x & 31][j];
-      part[((int64_t)blockIdx.x * C + c) * K + j] = s;
+      if (src[j] < 0) continue;
+      const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src[j]) * ld + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(p2[e]);
+        acc[2 * e][j] += dv[2 * e] * f.x;
+        acc[2 * e + 1][j] += dv[2 * e + 1] * f.y;
+      }
     }
   }
+  float* dst = part + ((int64_t)blockIdx.y * C + c) * K;
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    *reinterpret_cast<float4*>(dst + e * K) = make_float4(acc[e][0], acc[e][1], acc[e][2], acc[e][3]);
 }
 
 __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int64_t n, float* __restrict__ out) {
@@ -249,7 +293,6 @@ __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int
 }
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
-static dim3 row_grid(int per_row, int rows) { return dim3((per_row + 255) / 256, std::min(rows, 65535)); }
 
 at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode) {
   TORCH_CHECK(raw.dim() == 3 && raw.stride(-1) == 1 && raw.scalar_type() == at::kBFloat16, "conv: raw [B, 2L, C] bf16");
@@ -279,15 +322,16 @@ std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, co
                                                                     (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto draw = at::empty({B, T2, C}, raw.options());
-  conv_dx_kernel<4><<<row_grid(C, B * T2), 256, 0, stream()>>>(dpre.data_ptr<float>(), wf.data_ptr<float>(),
-                                                                bfp(draw), C, B, T2, C, (int)L, (int)block, (int)mode);
+  conv_dx_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(
+      dpre.data_ptr<float>(), wf.data_ptr<float>(), bfp(draw), C, B, T2, C, (int)L, (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const int64_t total = (int64_t)B * T2;
-  const int tpb = (int)std::max<int64_t>(64, (total + 127) / 128);
+  // enough (channel-group x token-chunk) threads to fill the GPU: chunks of >= 32 rows
+  const int tpb = (int)std::max<int64_t>(32, (total + 255) / 256);
   const int nb = (int)((total + tpb - 1) / tpb);
   auto part = at::empty({nb, C, K}, raw.options().dtype(at::kFloat));
-  dim3 grid(nb, (C + 31) / 32);
-  conv_dw_kernel<4><<<grid, 256, 0, stream()>>>(cbf(raw), raw.stride(1), dpre.data_ptr<float>(), part.data_ptr<float>(),
+  dim3 grid((C / 8 + 127) / 128, nb);
+  conv_dw_kernel<4><<<grid, 128, 0, stream()>>>(cbf(raw), raw.stride(1), dpre.data_ptr<float>(), part.data_ptr<float>(),
                                                 B, T2, C, (int)L, (int)block, (int)mode, tpb);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto dw = at::empty({C, K}, raw.options().dtype(at::kFloat));
@@ -438,6 +482,81 @@ void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m
     else ADAMW(__nv_bfloat16, float, bfp(p), g.data_ptr<float>());
   }
 #undef ADAMW
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------- grad norm
+// sq += sum_i x_i^2 over an fp32 or bf16 vector (16-byte vectors, one fp32 atomic per block);
+// with dst set (bf16 input), dst = float(x) is written in the same pass.
+template <typename T>
+__global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restrict__ dst, float* __restrict__ sq) {
+  constexpr int V = 16 / sizeof(T);
+  float acc = 0.f;
+  const int64_t nv = n / V;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 raw = reinterpret_cast<const uint4*>(x)[i];
+    float f[V];
+    if constexpr (sizeof(T) == 4) {
+      const float4 q = *reinterpret_cast<const float4*>(&raw);
+      f[0] = q.x, f[1] = q.y, f[2] = q.z, f[3] = q.w;
+    } else {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 t = __bfloat1622float2(h[e]);
+        f[2 * e] = t.x, f[2 * e + 1] = t.y;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc += f[e] * f[e];
+    if (dst != nullptr) {
+      float4* d = reinterpret_cast<float4*>(dst + i * V);
+#pragma unroll
+      for (int e = 0; e < V / 4; ++e) d[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
+    }
+  }
+  // tail (n not a multiple of the vector width)
+  for (int64_t i = nv * V + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const float f = to_f(x[i]);
+    acc += f * f;
+    if (dst != nullptr) dst[i] = f;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ float part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) atomicAdd(sq, t);
+  }
+}
+
+// sq += ||x||^2 (x fp32 or bf16, contiguous); with dst (fp32, x bf16): dst = float(x) as well
+void sumsq_(const at::Tensor& x, at::Tensor& sq, const c10::optional<at::Tensor>& dst) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
+              "sumsq: contiguous 16-byte aligned input");
+  TORCH_CHECK(sq.scalar_type() == at::kFloat && sq.numel() >= 1, "sumsq: fp32 accumulator");
+  float* d = nullptr;
+  if (dst.has_value()) {
+    TORCH_CHECK(dst->scalar_type() == at::kFloat && dst->is_contiguous() && dst->numel() >= x.numel() &&
+                    reinterpret_cast<uintptr_t>(dst->data_ptr()) % 16 == 0,
+                "sumsq: fp32 destination");
+    d = dst->data_ptr<float>();
+  }
+  const int64_t n = x.numel();
+  if (n == 0) return;
+  c10::cuda::CUDAGuard gd(x.device());
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n / 8 + 255) / 256, 148 * 8));
+  if (x.scalar_type() == at::kFloat)
+    sumsq_kernel<float><<<grid, 256, 0, stream()>>>(x.data_ptr<float>(), n, d, sq.data_ptr<float>());
+  else if (x.scalar_type() == at::kBFloat16)
+    sumsq_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(cbf(x), n, d, sq.data_ptr<float>());
+  else
+    TORCH_CHECK(false, "sumsq: fp32 or bf16 input");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -147,6 +147,15 @@ def adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
     p.copy_(w)
 
 
+def sumsq_(x, sq, dst=None):
+    """sq += ||x||^2 in fp32 (one read of x); with `dst` (fp32, same size) also dst = float(x)."""
+    if x.is_cuda:
+        return _nat().sumsq_(x, sq, dst)
+    if dst is not None:
+        dst.copy_(x)
+    sq += x.float().pow(2).sum()
+
+
 def gated_rmsnorm(x, z, w, eps: float):
     if use_native(x, op="gated_rmsnorm"):
         _record("gated_rmsnorm", "native")

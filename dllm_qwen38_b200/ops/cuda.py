@@ -536,6 +536,11 @@ def adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2):
     _count()
 
 
+def sumsq_(x, sq, dst=None):
+    _C.sumsq_(x, sq, dst)
+    _count()
+
+
 def error_word(reset: bool = False) -> int:
     return int(_C.read_error_word(reset))
 

@@ -214,11 +214,13 @@ class FSDPEngine:
             # the next layer's backward fills the other
             self.grads, self.grad_offs = zip(*[self.peer.alloc(gmax, self.dtype) for _ in range(2)])
             self.table_grad, self.table_off = self.peer.alloc(self.embed.padded, torch.float32)
-            self.sq = torch.zeros(1, dtype=torch.float32, device=self.device)
-            self.sq_all = torch.zeros(1, dtype=torch.float32, device=self.device)
         else:
             self.grads = (torch.empty(gmax, dtype=self.dtype, device=self.device),)
             self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
+        # sum of squares of this rank's reduced gradient shards (the clip norm), filled as each unit's
+        # gradient is reduced; summed over ranks once per step
+        self.sq = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.sq_all = torch.zeros(1, dtype=torch.float32, device=self.device)
         self.grad_i = 0
         self.rs_done = [None] * len(self.grads)
         self.epoch = 0
@@ -383,7 +385,11 @@ class FSDPEngine:
 
     def reduce_scatter(self, unit: Unit, flat_grad: torch.Tensor) -> None:
         if self.peer is None:
-            unit.reduce_scatter_from(flat_grad)
+            if self.world == 1:  # the fp32 shard copy and its sum of squares in one pass
+                ops.sumsq_(flat_grad[: unit.shard], self.sq, unit.g)
+            else:
+                unit.reduce_scatter_from(flat_grad)
+                ops.sumsq_(unit.g, self.sq)
             return
         if flat_grad.data_ptr() == self.table_grad.data_ptr():
             j, off, f32 = None, self.table_off, True
@@ -453,8 +459,7 @@ class FSDPEngine:
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
-        if self.peer is not None:
-            self.sq.zero_()
+        self.sq.zero_()
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
         loss.backward()
         self._optimizer_step()
@@ -471,12 +476,9 @@ class FSDPEngine:
                 self.invalidate()
                 return
         else:
-            sq = torch.zeros((), device=self.device, dtype=torch.float32)
-            for u in self.units:
-                sq += u.g.pow(2).sum()
             if self.world > 1:
-                dist.all_reduce(sq)
-            norm = sq.sqrt()
+                dist.all_reduce(self.sq)
+            norm = self.sq.sqrt()
         coef = torch.clamp(self.grad_clip / (norm + 1e-6), max=1.0) if self.grad_clip > 0 else torch.ones_like(norm)
         b1, b2 = self.betas
         bc1, bc2 = 1 - b1 ** self.step_count, 1 - b2 ** self.step_count

@@ -13,7 +13,7 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("mode", ["fork", "no-prefix", "concat"])
-@pytest.mark.parametrize("L,block,C", [(64, 16, 64), (96, 32, 40 * 8)])
+@pytest.mark.parametrize("L,block,C", [(64, 16, 64), (96, 32, 40 * 8), (100, 20, 64)])
 def test_conv_fwd_bwd(mode, L, block, C):
     from dllm_qwen38_b200.ops import cuda as Cu
 

@@ -3,11 +3,12 @@
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and
 // 256. One CTA = 128 query rows of one (batch, query head); 6 warps:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 32 (or 64) keys into a ring
-//               of as many stages as fit (5 at D 256)
-//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 32, K D) into one of three TMEM score
-//               buffers, up to two tiles ahead, and O += P V (M 128, N D, K 32) into the TMEM output
-//               accumulator, with P read from TMEM as the A operand
+//   warp 4      TMA producer: the Q tile once, then K and V tiles of 64 (or 32) keys into a ring
+//               of as many stages as fit (2 at D 256 with 64-key tiles, 5 with 32-key tiles)
+//   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 64, K D) into one of three TMEM score
+//               buffers, ahead of the softmax by as many tiles as the ring allows, and
+//               O += P V (M 128, N D, K 64) into the TMEM output accumulator, with P read from TMEM
+//               as the A operand
 //   warps 0-3   softmax: thread = query row = TMEM lane; reads its scores with tcgen05.ld, masks,
 //               keeps a running max and sum, and stores P (bf16, packed pairs) into TMEM
 //               (tcgen05.st, double-buffered)
@@ -1136,10 +1137,10 @@ bool attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, 
   const int64_t D = q.size(3);
   if (D != 128 && D != 256) return false;
   bind_context(q.get_device());
-  static int bkv = -1;  // BDLLM_ATTN_BKV=64 selects 64-key tiles (fewer ring stages)
+  static int bkv = -1;  // 64-key tiles (measured faster); BDLLM_ATTN_BKV=32 selects 32-key tiles
   if (bkv < 0) {
     const char* e = getenv("BDLLM_ATTN_BKV");
-    bkv = (e != nullptr && atoi(e) == 64) ? 64 : 32;
+    bkv = (e != nullptr && atoi(e) == 32) ? 32 : 64;
   }
   if (D == 128)
     bkv == 32 ? attn_tc::launch<128, 32>(q, k, v, o, lse, L, block, scale, leak)

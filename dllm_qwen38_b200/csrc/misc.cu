@@ -487,9 +487,12 @@ void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m
 
 // ------------------------------------------------------------------------------- grad norm
 // sq += sum_i x_i^2 over an fp32 or bf16 vector (16-byte vectors, one fp32 atomic per block);
-// with dst set (bf16 input), dst = float(x) is written in the same pass.
-template <typename T>
-__global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restrict__ dst, float* __restrict__ sq) {
+// with dst set, dst = x (converted to dst's type, fp32 or bf16) is written in the same pass.
+__device__ __forceinline__ void put(float* d, int64_t i, float f) { d[i] = f; }
+__device__ __forceinline__ void put(__nv_bfloat16* d, int64_t i, float f) { d[i] = __float2bfloat16(f); }
+
+template <typename T, typename TD>
+__global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, TD* __restrict__ dst, float* __restrict__ sq) {
   constexpr int V = 16 / sizeof(T);
   float acc = 0.f;
   const int64_t nv = n / V;
@@ -510,9 +513,12 @@ __global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restri
 #pragma unroll
     for (int e = 0; e < V; ++e) acc += f[e] * f[e];
     if (dst != nullptr) {
-      float4* d = reinterpret_cast<float4*>(dst + i * V);
+      if constexpr (sizeof(T) == sizeof(TD)) {  // same type: copy the 16 bytes
+        reinterpret_cast<uint4*>(dst)[i] = raw;
+      } else {
 #pragma unroll
-      for (int e = 0; e < V / 4; ++e) d[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
+        for (int e = 0; e < V; ++e) put(dst, i * V + e, f[e]);
+      }
     }
   }
   // tail (n not a multiple of the vector width)
@@ -520,7 +526,7 @@ __global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restri
        i += (int64_t)gridDim.x * blockDim.x) {
     const float f = to_f(x[i]);
     acc += f * f;
-    if (dst != nullptr) dst[i] = f;
+    if (dst != nullptr) put(dst, i, f);
   }
 #pragma unroll
   for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -535,28 +541,36 @@ __global__ void sumsq_kernel(const T* __restrict__ x, int64_t n, float* __restri
   }
 }
 
-// sq += ||x||^2 (x fp32 or bf16, contiguous); with dst (fp32, x bf16): dst = float(x) as well
+// sq += ||x||^2 (x fp32 or bf16, contiguous); with dst (fp32 or bf16): dst = x as well
 void sumsq_(const at::Tensor& x, at::Tensor& sq, const c10::optional<at::Tensor>& dst) {
   TORCH_CHECK(x.is_cuda() && x.is_contiguous() && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0,
               "sumsq: contiguous 16-byte aligned input");
+  TORCH_CHECK(x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16, "sumsq: fp32 or bf16 input");
   TORCH_CHECK(sq.scalar_type() == at::kFloat && sq.numel() >= 1, "sumsq: fp32 accumulator");
-  float* d = nullptr;
-  if (dst.has_value()) {
-    TORCH_CHECK(dst->scalar_type() == at::kFloat && dst->is_contiguous() && dst->numel() >= x.numel() &&
-                    reinterpret_cast<uintptr_t>(dst->data_ptr()) % 16 == 0,
-                "sumsq: fp32 destination");
-    d = dst->data_ptr<float>();
-  }
+  const bool has_dst = dst.has_value();
+  if (has_dst)
+    TORCH_CHECK((dst->scalar_type() == at::kFloat || dst->scalar_type() == at::kBFloat16) && dst->is_contiguous() &&
+                    dst->numel() >= x.numel() && reinterpret_cast<uintptr_t>(dst->data_ptr()) % 16 == 0,
+                "sumsq: fp32 or bf16 contiguous destination");
   const int64_t n = x.numel();
   if (n == 0) return;
   c10::cuda::CUDAGuard gd(x.device());
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n / 8 + 255) / 256, 148 * 8));
-  if (x.scalar_type() == at::kFloat)
-    sumsq_kernel<float><<<grid, 256, 0, stream()>>>(x.data_ptr<float>(), n, d, sq.data_ptr<float>());
-  else if (x.scalar_type() == at::kBFloat16)
-    sumsq_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(cbf(x), n, d, sq.data_ptr<float>());
+  float* sqp = sq.data_ptr<float>();
+  const bool xf = x.scalar_type() == at::kFloat;
+  const bool df = !has_dst || dst->scalar_type() == at::kFloat;
+  if (xf && df)
+    sumsq_kernel<float, float><<<grid, 256, 0, stream()>>>(x.data_ptr<float>(), n,
+                                                           has_dst ? dst->data_ptr<float>() : nullptr, sqp);
+  else if (xf)
+    sumsq_kernel<float, __nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        x.data_ptr<float>(), n, reinterpret_cast<__nv_bfloat16*>(dst->data_ptr()), sqp);
+  else if (df)
+    sumsq_kernel<__nv_bfloat16, float><<<grid, 256, 0, stream()>>>(cbf(x), n, has_dst ? dst->data_ptr<float>() : nullptr,
+                                                                   sqp);
   else
-    TORCH_CHECK(false, "sumsq: fp32 or bf16 input");
+    sumsq_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, stream()>>>(
+        cbf(x), n, reinterpret_cast<__nv_bfloat16*>(dst->data_ptr()), sqp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -123,3 +123,22 @@ def test_embedding_fwd_bwd_against_torch():
     h.backward(dh)
     want = torch.zeros(300, 64, device="cuda").index_add_(0, ids.reshape(-1), dh.reshape(-1, 64).float())
     assert torch.allclose(table.grad.float(), want, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("xdt,ddt", [(torch.float32, None), (torch.bfloat16, None), (torch.bfloat16, torch.float32),
+                                     (torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
+@pytest.mark.parametrize("n", [8, 1000003, 4096 * 33])
+def test_sumsq_with_copy(xdt, ddt, n):
+    """sq += ||x||^2 (fp32 accumulate) with the optional fused copy into dst, vector tails included."""
+    from dllm_qwen38_b200 import _C
+
+    torch.manual_seed(4)
+    x = torch.randn(n, device="cuda").to(xdt)
+    sq = torch.full((1,), 2.5, device="cuda")
+    dst = torch.empty(n, device="cuda", dtype=ddt) if ddt is not None else None
+    _C.sumsq_(x, sq, dst)
+    torch.cuda.synchronize()
+    want = 2.5 + float(x.double().pow(2).sum())
+    assert abs(float(sq[0]) - want) < 1e-4 * want
+    if dst is not None:
+        assert torch.equal(dst, x.to(ddt))

@@ -3,8 +3,8 @@
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and
 // 256. One CTA = 128 query rows of one (batch, query head); 6 warps:
-//   warp 4      TMA producer: the Q tile once, then K and V tiles of 64 (or 32) keys into a ring
-//               of as many stages as fit (2 at D 256 with 64-key tiles, 5 with 32-key tiles)
+//   warp 4      TMA producers: the Q tile once, then K and V tiles of 64 (or 32) keys into two
+//               rings (K released by its score MMA, V by the PV MMA; 3 K and 2 V stages at D 256)
 //   warp 5      MMA issuer (one thread): S = Q K^T (M 128, N 64, K D) into one of three TMEM score
 //               buffers, ahead of the softmax by as many tiles as the ring allows, and
 //               O += P V (M 128, N D, K 64) into the TMEM output accumulator, with P read from TMEM
@@ -35,17 +35,20 @@ constexpr int NTHR = 192;
 constexpr float NEG_INF = -INFINITY;
 constexpr float RESCALE_LOG2 = 8.f;
 
-template <int D, int BKV_ = 32>
+template <int D, int BKV_ = 64>
 struct FCfg {
   static constexpr int BKV = BKV_;             // keys per tile
   static constexpr int Q_BYTES = BQ * D * 2;   // D/64 boxes of [128 rows][128 B]
-  static constexpr int K_BYTES = BKV * D * 2;  // D/64 boxes of [BKV rows][128 B]
-  static constexpr int STAGE = 2 * K_BYTES;    // K then V
-  static constexpr int NST_FIT = (227 * 1024 - Q_BYTES - 1024 - 256) / STAGE;
-  static constexpr int NST = NST_FIT > 6 ? 6 : NST_FIT;  // K/V ring stages
+  static constexpr int K_BYTES = BKV * D * 2;  // one K or V tile: D/64 boxes of [BKV rows][128 B]
+  // separate K and V rings: a K stage is released as soon as its score MMA completes, a V stage
+  // only after the PV MMA that follows the softmax, so K can run further ahead
+  static constexpr int NTILE_FIT = (227 * 1024 - Q_BYTES - 1024 - 256) / K_BYTES;
+  static constexpr int NV = NTILE_FIT >= 6 ? 3 : 2;
+  static constexpr int NK_FIT = NTILE_FIT - NV;
+  static constexpr int NK = NK_FIT > 4 ? 4 : NK_FIT;
   static constexpr int NS = 3;                 // TMEM score buffers
-  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // score MMAs issued ahead
-  static constexpr int SMEM = Q_BYTES + NST * STAGE + 1024 + 256;
+  static constexpr int AHEAD = (NS - 1) < (NK - 1) ? (NS - 1) : (NK - 1);  // score MMAs issued ahead
+  static constexpr int SMEM = Q_BYTES + (NK + NV) * K_BYTES + 1024 + 256;
   // TMEM: NS score buffers of BKV columns, two bf16 P buffers of BKV/2 packed columns (the A
   // operand of the PV MMA), and O (D columns)
   static constexpr int S_COL = 0, P_COL = NS * BKV;
@@ -53,7 +56,7 @@ struct FCfg {
   static constexpr int TMEM_COLS = (O_COL + D <= 256) ? 256 : 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BKV, 0, 0);
   static constexpr uint32_t IDESC_O = idesc_bf16(BQ, D, 0, 1);  // V read N(=d)-contiguous
-  static_assert(NST >= 2 && P_COL + BKV <= O_COL && O_COL + D <= 512, "attention forward resources");
+  static_assert(NK >= 2 && NV >= 2 && P_COL + BKV <= O_COL && O_COL + D <= 512, "attention forward resources");
 };
 
 struct FArgs {
@@ -249,16 +252,19 @@ __global__ void __launch_bounds__(NTHR, 1)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                   const __grid_constant__ CUtensorMap mv, FArgs a) {
   using C = FCfg<D, BKV_>;
-  constexpr int BKV = C::BKV, NST = C::NST, NS = C::NS;
+  constexpr int BKV = C::BKV, NK = C::NK, NV = C::NV, NS = C::NS;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = smem + C::Q_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + NST * C::STAGE);
+  uint8_t* sK = smem + C::Q_BYTES;
+  uint8_t* sV = sK + NK * C::K_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sV + NV * C::K_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + NST;
-  uint64_t* s_full = kv_empty + NST;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = k_full + NK;
+  uint64_t* v_full = k_empty + NK;
+  uint64_t* v_empty = v_full + NV;
+  uint64_t* s_full = v_empty + NV;
   uint64_t* p_full = s_full + NS;
   uint64_t* o_done = p_full + 2;
   uint64_t* drain = o_done + 2;
@@ -277,9 +283,13 @@ __global__ void __launch_bounds__(NTHR, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < NST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < NV; ++s) {
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < NS; ++s) mbar_init(&s_full[s], 1);
     for (int s = 0; s < 2; ++s) {
@@ -303,32 +313,36 @@ __global__ void __launch_bounds__(NTHR, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 4) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+    if (lane == 0 || lane == 1) {
+      // ------------------------------------------------------------ TMA producers: lane 0 the Q
+      // tile and the K ring, lane 1 the V ring (independent waits, so K runs ahead of V)
+      const bool isk = lane == 0;
+      const int nst = isk ? NK : NV;
+      uint8_t* ring = isk ? sK : sV;
+      uint64_t* full = isk ? k_full : v_full;
+      uint64_t* empty = isk ? k_empty : v_empty;
+      const CUtensorMap* map = isk ? &mk : &mv;
+      if (isk) {
+        mbar_arrive_expect_tx(q_full, C::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c) tma_load_2d(sQ + c * BQ * 128, &mq, q_full, h * D + c * 64, row0 + i0);
-      int last[NST];
-#pragma unroll
-      for (int s = 0; s < NST; ++s) last[s] = -1;
+        for (int c = 0; c < D / 64; ++c) tma_load_2d(sQ + c * BQ * 128, &mq, q_full, h * D + c * 64, row0 + i0);
+      }
+      int last[4] = {-1, -1, -1, -1};
       for (int it = 0; it < nt; ++it) {
         const int jt = sp.at(it);
-        const int s = it % NST;
-        if (!mbar_wait(&kv_empty[s], ((it / NST) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
-        mbar_arrive_expect_tx(&kv_full[s], C::STAGE);
+        const int s = it % nst;
+        if (!mbar_wait(&empty[s], ((it / nst) & 1) ^ 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], C::K_BYTES);
         last[s] = it;
-        uint8_t* dk = sKV + s * C::STAGE;
+        uint8_t* dst = ring + s * C::K_BYTES;
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(dk + c * BKV * 128, &mk, &kv_full[s], hk * D + c * 64, row0 + jt * BKV);
-          tma_load_2d(dk + C::K_BYTES + c * BKV * 128, &mv, &kv_full[s], hk * D + c * 64, row0 + jt * BKV);
-        }
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(dst + c * BKV * 128, map, &full[s], hk * D + c * 64, row0 + jt * BKV);
       }
       // every load armed must land before the CTA exits (bounded): the last arming of each stage
-      mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
-#pragma unroll
-      for (int s = 0; s < NST; ++s)
-        if (last[s] >= 0) mbar_wait(&kv_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
+      if (isk) mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, nullptr);
+      for (int s = 0; s < nst; ++s)
+        if (last[s] >= 0) mbar_wait(&full[s], (last[s] / nst) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else if (warp == 5) {
     if (lane == 0) {
@@ -339,12 +353,12 @@ __global__ void __launch_bounds__(NTHR, 1)
       int issued = 0;  // score MMAs issued so far; up to AHEAD tiles ahead of the PV being waited
       for (int it = 0; ok && it < nt; ++it) {
         while (issued < nt && issued <= it + C::AHEAD) {
-          if (!mbar_wait(&kv_full[issued % NST], (issued / NST) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
+          if (!mbar_wait(&k_full[issued % NK], (issued / NK) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t k_addr = smem_u32(sKV + (issued % NST) * C::STAGE);
+          const uint32_t k_addr = smem_u32(sK + (issued % NK) * C::K_BYTES);
           const uint32_t d_s = tmem + C::S_COL + (issued % NS) * BKV;
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
@@ -354,19 +368,21 @@ __global__ void __launch_bounds__(NTHR, 1)
                      kk > 0 ? 1u : 0u);
           }
           mma_commit(&s_full[issued % NS]);
+          mma_commit(&k_empty[issued % NK]);  // the K stage is free once these MMAs have read it
           ++issued;
         }
         if (!ok) break;
         const int pb = it & 1;
         if (!mbar_wait(&p_full[pb], (it >> 1) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
+        if (!mbar_wait(&v_full[it % NV], (it / NV) & 1, a.err, ERR_ATTN_WAIT, abort_flag)) break;
         tc_fence_after();
-        const uint32_t v_addr = smem_u32(sKV + (it % NST) * C::STAGE + C::K_BYTES);
+        const uint32_t v_addr = smem_u32(sV + (it % NV) * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
           mma_bf16_ta(tmem + C::O_COL, tmem + C::P_COL + pb * (BKV / 2) + kk * 8,
                       smem_desc(v_addr + kk * 2048, BKV * 128, 1024), C::IDESC_O, (it > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&o_done[pb]);
-        mma_commit(&kv_empty[it % NST]);
+        mma_commit(&v_empty[it % NV]);
       }
       // every MMA issued must complete before TMEM is freed (bounded)
       mma_commit(drain);
@@ -519,7 +535,10 @@ struct QCfg {
   // TMEM: S and dP (NS buffers of 32 columns each), dS as the bf16 A operand of the dQ MMA (two
   // buffers of 16 packed columns), dQ (D columns)
   static constexpr int NS = 3;
-  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // S / dP MMAs issued ahead
+  // S / dP MMAs issued ahead; the K/V stage they need must have been released two gradient MMAs
+  // earlier (a stage released by the previous one is still loading)
+  static constexpr int AHEAD_R = (NS - 1) < (NST - 2) ? (NS - 1) : (NST - 2);
+  static constexpr int AHEAD = AHEAD_R < 1 ? 1 : AHEAD_R;
   static constexpr int S_COL = 0, DP_COL = NS * BK2, DS_COL = 2 * NS * BK2, DQ_COL = 256;
   static constexpr int TMEM_COLS = 512;
   static constexpr uint32_t IDESC_S = idesc_bf16(BQ, BK2, 0, 0);
@@ -793,7 +812,9 @@ struct KCfg {
   // TMEM: S^T and dP^T (NS buffers of 32 columns each), the bf16 P^T / dS^T operands of the
   // gradient MMAs (two buffers of 16 packed columns each), dV and dK slices (128 columns each)
   static constexpr int NS = 3;
-  static constexpr int AHEAD = (NS - 1) < (NST - 1) ? (NS - 1) : (NST - 1);  // S^T / dP^T MMAs issued ahead
+  // S^T / dP^T MMAs issued ahead (same rule as the dQ kernel)
+  static constexpr int AHEAD_R = (NS - 1) < (NST - 2) ? (NS - 1) : (NST - 2);
+  static constexpr int AHEAD = AHEAD_R < 1 ? 1 : AHEAD_R;
   static constexpr int ST_COL = 0, DPT_COL = NS * BQ2, PT_COL = 2 * NS * BQ2, DST_COL = PT_COL + BQ2,
                        DV_COL = 256, DK_COL = 384;
   static constexpr int TMEM_COLS = 512;

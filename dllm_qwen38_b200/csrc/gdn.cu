@@ -232,6 +232,13 @@ __device__ __forceinline__ int64_t tok(const Args& a, int b, int stream, int c, 
   return (int64_t)b * 2 * a.L + ((stream && !a.concat) ? a.L : 0) + (int64_t)c * a.C + i;
 }
 
+// 16-byte asynchronous global -> shared copies (operand prefetch in the recurrences)
+__device__ __forceinline__ void cp16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // ------------------------------------------------------------------ shared-tile strides
 // Row strides of the fp32 shared tiles are padded by 4 floats: with that, every TF32 fragment read
 // pattern of mm_tc (lanes spanning 8 rows x 4 columns or 4 rows x 8 columns) hits 32 distinct banks.
@@ -384,44 +391,64 @@ __global__ void __launch_bounds__(NT) fwd_prep_kernel(Args a) {
   if (threadIdx.x == 0) a.Ec[base] = __expf(s.gam[C - 1]);
 }
 
-// sequential state recurrence: CTA per (b, h, 32 value columns); the chunk operands stream
-// through smem.
+// sequential state recurrence: CTA per (b, h, 32 value columns). The chunk operands (W, K~ and
+// the U columns) are double-buffered: chunk c+1's are copied in (cp.async) while chunk c is
+// computed.
 template <int Dk, int Dv>
 __global__ void __launch_bounds__(NT) fwd_recur_kernel(Args a) {
   extern __shared__ float sm[];
   constexpr int KD = Ld<Dk>::v;
   const int C = a.C;
-  float* sW = sm;               // [C][KD]
-  float* sKt = sW + 32 * KD;    // [C][KD]
-  float* sVp = sKt + 32 * KD;   // [C][LDC]
-  float* sS = sVp + 32 * LDC;   // [Dk][LDC]
+  // buffer k: W and K~ [C][KD] each, then the U columns [C][LDC]
+  constexpr int BUF = 2 * 32 * KD + 32 * LDC;
+  auto sWb = [&](int k) { return sm + k * BUF; };
+  auto sKtb = [&](int k) { return sm + k * BUF + 32 * KD; };
+  auto sUb = [&](int k) { return sm + k * BUF + 2 * 32 * KD; };
+  float* sVp = sm + 2 * BUF;       // [C][LDC]
+  float* sS = sVp + 32 * LDC;      // [Dk][LDC]
   const int bh = blockIdx.x, b = bh / a.Hv, h = bh % a.Hv;
   const int col0 = blockIdx.y * 32;
   const int ncols = min(32, Dv - col0);
+  auto prefetch = [&](int c, int buf) {
+    const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
+    const float* Wg = a.W + base * C * Dk;
+    const float* Kt = a.Kt + base * C * Dk;
+    const float* U = a.U + base * C * Dv;
+    for (int idx = threadIdx.x; idx < C * (Dk / 4); idx += NT) {
+      const int i = idx / (Dk / 4), q = (idx % (Dk / 4)) * 4;
+      cp16(sWb(buf) + i * KD + q, Wg + i * Dk + q);
+      cp16(sKtb(buf) + i * KD + q, Kt + i * Dk + q);
+    }
+    for (int idx = threadIdx.x; idx < C * 8; idx += NT) {
+      const int i = idx / 8, q = (idx % 8) * 4;
+      if (q < ncols) cp16(sUb(buf) + i * LDC + q, U + i * Dv + col0 + q);
+    }
+    cp_commit();
+  };
   for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) {
     const int r = idx / LDC, cc = idx % LDC;
     sS[idx] = (a.S0 != nullptr && cc < ncols) ? a.S0[((int64_t)bh * Dk + r) * Dv + col0 + cc] : 0.f;
   }
+  if (a.nb > 0) prefetch(0, 0);
   __syncthreads();
   for (int c = 0; c < a.nb; ++c) {
+    const int buf = c & 1;
     const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
     float* Sin = a.S_in + base * Dk * Dv;
     for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
       const int r = idx / 32, cc = idx % 32;
       if (cc < ncols) Sin[r * Dv + col0 + cc] = sS[r * LDC + cc];
     }
-    const float* Wg = a.W + base * C * Dk;
-    const float* Kt = a.Kt + base * C * Dk;
-    const float* U = a.U + base * C * Dv;
-    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-      const int i = idx / Dk, d = idx % Dk;
-      sW[i * KD + d] = Wg[idx], sKt[i * KD + d] = Kt[idx];
-    }
-    __syncthreads();
+    cp_wait_all();
+    __syncthreads();  // chunk c's operands are in buffer buf; buffer buf^1 is no longer read
+    if (c + 1 < a.nb) prefetch(c + 1, buf ^ 1);
+    const float* sW = sWb(buf);
+    const float* sKt = sKtb(buf);
+    const float* sU = sUb(buf);
     float* Vp = a.Vp + base * C * Dv;
     matmul<false, false>(C, 32, Dk, sW, KD, sS, LDC, [&](int i, int j, float x) {  // V' = U - W S
       if (j < ncols) {
-        const float v = U[i * Dv + col0 + j] - x;
+        const float v = sU[i * LDC + j] - x;
         sVp[i * LDC + j] = v;
         Vp[i * Dv + col0 + j] = v;
       } else {
@@ -435,6 +462,7 @@ __global__ void __launch_bounds__(NT) fwd_recur_kernel(Args a) {
     });
     __syncthreads();
   }
+  cp_wait_all();
   if (a.S_final != nullptr)
     for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
       const int r = idx / 32, cc = idx % 32;
@@ -809,42 +837,70 @@ __global__ void __launch_bounds__(NT) bwd_recur_kernel(Args a, int has_inj) {
   extern __shared__ float sm[];
   constexpr int KD = Ld<Dk>::v;
   const int C = a.C;
-  float* sW = sm;                // [C][KD]
-  float* sKt = sW + 32 * KD;     // [C][KD]
-  float* sQt = sKt + 32 * KD;    // [C][KD]
-  float* sdVp = sQt + 32 * KD;   // [C][LDC]
+  // double-buffered chunk operands: W, K~, q~ [C][KD], P^T dO columns [C][LDC] (fp32) and the dO
+  // columns as raw bf16 [C][32]
+  constexpr int BUF = 3 * 32 * KD + 32 * LDC + 32 * 16;
+  auto sWb = [&](int k) { return sm + k * BUF; };
+  auto sKtb = [&](int k) { return sm + k * BUF + 32 * KD; };
+  auto sQtb = [&](int k) { return sm + k * BUF + 2 * 32 * KD; };
+  auto sPb = [&](int k) { return sm + k * BUF + 3 * 32 * KD; };
+  auto sOb = [&](int k) { return reinterpret_cast<__nv_bfloat16*>(sm + k * BUF + 3 * 32 * KD + 32 * LDC); };
+  float* p = sm + 2 * BUF;
+  float* sdVp = p;               // [C][LDC]
   float* sdO = sdVp + 32 * LDC;  // [C][LDC]
   float* sS = sdO + 32 * LDC;    // [Dk][LDC]
   const int bh = blockIdx.x, b = bh / a.Hv, h = bh % a.Hv;
   const int col0 = blockIdx.y * 32;
   const int ncols = min(32, Dv - col0);
+  auto prefetch = [&](int c, int buf) {
+    const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
+    const float* Wg = a.W + base * C * Dk;
+    const float* Kt = a.Kt + base * C * Dk;
+    const float* Qt = a.Qt + base * C * Dk;
+    const float* Pt = a.PtdO + base * C * Dv;
+    for (int idx = threadIdx.x; idx < C * (Dk / 4); idx += NT) {
+      const int i = idx / (Dk / 4), q = (idx % (Dk / 4)) * 4;
+      cp16(sWb(buf) + i * KD + q, Wg + i * Dk + q);
+      cp16(sKtb(buf) + i * KD + q, Kt + i * Dk + q);
+      cp16(sQtb(buf) + i * KD + q, Qt + i * Dk + q);
+    }
+    for (int idx = threadIdx.x; idx < C * 8; idx += NT) {
+      const int i = idx / 8, q = (idx % 8) * 4;
+      if (q < ncols) cp16(sPb(buf) + i * LDC + q, Pt + i * Dv + col0 + q);
+    }
+    for (int idx = threadIdx.x; idx < C * 4; idx += NT) {
+      const int i = idx / 4, q = (idx % 4) * 8;
+      if (q < ncols)
+        cp16(sOb(buf) + i * 32 + q, a.dout + tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + col0 + q);
+    }
+    cp_commit();
+  };
   for (int idx = threadIdx.x; idx < Dk * LDC; idx += NT) sS[idx] = 0.f;
+  if (a.nb > 0) prefetch(a.nb - 1, (a.nb - 1) & 1);
   __syncthreads();
   for (int c = a.nb - 1; c >= 0; --c) {
+    const int buf = c & 1;
     const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
     float* dSo = a.dS_out + base * Dk * Dv;
     for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
       const int r = idx / 32, cc = idx % 32;
       if (cc < ncols) dSo[r * Dv + col0 + cc] = sS[r * LDC + cc];
     }
-    const float* Wg = a.W + base * C * Dk;
-    const float* Kt = a.Kt + base * C * Dk;
-    const float* Qt = a.Qt + base * C * Dk;
-    for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
-      const int i = idx / Dk, d = idx % Dk;
-      sW[i * KD + d] = Wg[idx], sKt[i * KD + d] = Kt[idx], sQt[i * KD + d] = Qt[idx];
-    }
+    cp_wait_all();
+    __syncthreads();  // chunk c's operands are in buffer buf; buffer buf^1 is no longer read
+    if (c > 0) prefetch(c - 1, buf ^ 1);
     for (int idx = threadIdx.x; idx < C * 32; idx += NT) {
       const int i = idx / 32, cc = idx % 32;
-      sdO[i * LDC + cc] =
-          cc < ncols ? __bfloat162float(a.dout[tok(a, b, 1, c, i) * (int64_t)a.Hv * Dv + h * Dv + col0 + cc]) : 0.f;
+      sdO[i * LDC + cc] = cc < ncols ? __bfloat162float(sOb(buf)[i * 32 + cc]) : 0.f;
     }
-    __syncthreads();
-    const float* PtdO = a.PtdO + base * C * Dv;
+    const float* sW = sWb(buf);
+    const float* sKt = sKtb(buf);
+    const float* sQt = sQtb(buf);
+    const float* sP = sPb(buf);
     float* dVp = a.dVp + base * C * Dv;
     matmul<false, false>(C, 32, Dk, sKt, KD, sS, LDC, [&](int i, int j, float x) {
       if (j < ncols) {
-        const float v = PtdO[i * Dv + col0 + j] + x;
+        const float v = sP[i * LDC + j] + x;
         sdVp[i * LDC + j] = v;
         dVp[i * Dv + col0 + j] = v;
       } else {
@@ -865,6 +921,7 @@ __global__ void __launch_bounds__(NT) bwd_recur_kernel(Args a, int has_inj) {
     });
     __syncthreads();
   }
+  cp_wait_all();
 }
 
 // ------------------------------------------------------------------------------------- host
@@ -941,7 +998,7 @@ static std::vector<at::Tensor> forward_t(const at::Tensor& q, const at::Tensor& 
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
   const int BH = a.B * a.Hv;
   launch(fwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
-  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 2 * 32 * Ld<Dk>::v + 32 * LDC + Dk * LDC, a);
+  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 4 * 32 * Ld<Dk>::v + 3 * 32 * LDC + Dk * LDC, a);
   // noised blocks (x < nb) only exist with the fork
   const int ngrid = concat ? a.nb : 2 * a.nb;
   launch(fwd_out_kernel<Dk, Dv>, dim3(ngrid, BH), Smem<Dk, Dv>::floats, a);
@@ -983,7 +1040,7 @@ static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, 
   }
   const int BH = a.B * a.Hv;
   launch(fwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
-  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 2 * 32 * Ld<Dk>::v + 32 * LDC + Dk * LDC, a);
+  launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 4 * 32 * Ld<Dk>::v + 3 * 32 * LDC + Dk * LDC, a);
   launch(fwd_out_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
   return {o};
 }
@@ -1027,7 +1084,8 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   const int BH = a.B * a.Hv;
   if (!concat) launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
   launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
-  launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 3 * 32 * Ld<Dk>::v + 2 * 32 * LDC + Dk * LDC, a,
+  launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
+          2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a,
           concat ? 0 : 1);
   launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
   return {dq, dk, dv, dg, db};
@@ -1117,7 +1175,7 @@ int noalloc_run(bdllm::gdn::Args a, unsigned char* base, size_t cap, cudaStream_
   }
   const int BH = a.B * a.Hv;
   const int big = Smem<D, D>::floats * 4;
-  const int rec = (2 * 32 * Ld<D>::v + 32 * LDC + D * LDC) * 4;
+  const int rec = (4 * 32 * Ld<D>::v + 3 * 32 * LDC + D * LDC) * 4;
   if (cudaFuncSetAttribute(fwd_prep_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess ||
       cudaFuncSetAttribute(fwd_recur_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, rec) != cudaSuccess ||
       cudaFuncSetAttribute(fwd_out_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess)

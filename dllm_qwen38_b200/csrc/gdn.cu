@@ -208,79 +208,6 @@ __device__ __forceinline__ void matmul_rowsum(int M, int N, int K, const float* 
 }
 
 // out[i] += sum_d X[i][d] * Y[i][d] over C rows of D, warp per row
-// Split-K tensor-core product for shapes with fewer 16 x 32 output tiles than warps: each warp
-// computes one (tile, k-slice) partial and calls add(m, n, partial), which must accumulate (shared
-// atomics), so the summation order of the slices is not fixed. Shapes that do not tile go through
-// matmul() (one call per output with the full sum).
-__device__ __forceinline__ int ksplit_for(int tiles, int K) {
-  int ks = 1;
-  while (tiles * ks * 2 <= NT / 32 && K % (16 * ks) == 0) ks *= 2;
-  return ks;
-}
-
-template <bool AT, bool BT, typename Add>
-__device__ __forceinline__ void matmul_add(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
-                                           Add add) {
-  if (!(M % 16 == 0 && N % 32 == 0 && K % 8 == 0)) {
-    matmul<AT, BT>(M, N, K, A, lda, B, ldb, add);
-    return;
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int tiles_n = N / 32, tiles = (M / 16) * tiles_n;
-  const int ks = ksplit_for(tiles, K), kl = K / ks;
-  for (int w = warp; w < tiles * ks; w += NT / 32) {
-    const int tile = w % tiles, ksl = w / tiles;
-    const int m0 = (tile / tiles_n) * 16, n0 = (tile % tiles_n) * 32;
-    float c[4][4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
-    for (int k0 = ksl * kl; k0 < (ksl + 1) * kl; k0 += 8) {
-      auto Aget = [&](int m, int k) { return AT ? A[k * lda + m] : A[m * lda + k]; };
-      const uint32_t a0 = tf32(Aget(m0 + g, k0 + t)), a1 = tf32(Aget(m0 + g + 8, k0 + t));
-      const uint32_t a2 = tf32(Aget(m0 + g, k0 + t + 4)), a3 = tf32(Aget(m0 + g + 8, k0 + t + 4));
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int n = n0 + j * 8 + g;
-        const uint32_t b0 = tf32(BT ? B[n * ldb + k0 + t] : B[(k0 + t) * ldb + n]);
-        const uint32_t b1 = tf32(BT ? B[n * ldb + k0 + t + 4] : B[(k0 + t + 4) * ldb + n]);
-        asm volatile(
-            "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-            "{%0,%1,%2,%3};"
-            : "+f"(c[j][0]), "+f"(c[j][1]), "+f"(c[j][2]), "+f"(c[j][3])
-            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + j * 8 + 2 * t;
-      add(m0 + g, n, c[j][0]);
-      add(m0 + g, n + 1, c[j][1]);
-      add(m0 + g + 8, n, c[j][2]);
-      add(m0 + g + 8, n + 1, c[j][3]);
-    }
-  }
-}
-
-// out[m] += sum_n f(m, n, (A B)_mn) with f linear in its last argument: split-K partials are
-// reduced through the same shared atomics
-template <bool AT, bool BT, typename F>
-__device__ __forceinline__ void matmul_rowsum_sk(int M, int N, int K, const float* A, int lda, const float* B,
-                                                 int ldb, F f, float* out) {
-  if (!(M % 16 == 0 && N % 32 == 0 && K % 8 == 0)) {
-    matmul_rowsum<AT, BT>(M, N, K, A, lda, B, ldb, f, out);
-    return;
-  }
-  const int lane = threadIdx.x & 31;
-  // accumulate the row sum of each warp tile's contributions lane-locally, then one atomic per row
-  matmul_add<AT, BT>(M, N, K, A, lda, B, ldb, [&](int m, int n, float x) {
-    float v = f(m, n, x);
-    // lanes sharing row m (same g) are t = 0..3 of one quad: reduce over the quad
-    v += __shfl_xor_sync(0xffffffffu, v, 1);
-    v += __shfl_xor_sync(0xffffffffu, v, 2);
-    if ((lane & 3) == 0) atomicAdd(&out[m], v);
-  });
-}
-
 __device__ __forceinline__ void rowdot(int C, int D, const float* X, int ldx, const float* Y, int ldy, float* out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = warp; i < C; i += NT / 32) {
@@ -678,21 +605,16 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     const int i = idx / Dk, d = idx % Dk;
     s.dK[i * KD + d] = 0.f;
   }
-  for (int idx = threadIdx.x; idx < 32 * LDC; idx += NT) s.KK[idx] = 0.f, s.P[idx] = 0.f;
-  __syncthreads();
-  // ---- KK, P (with Gam, incl), T: split-K over all warps (2 output tiles of 16 x 32 each)
-  matmul_add<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { atomicAdd(&s.KK[i * LDC + j], x); });
-  matmul_add<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) { atomicAdd(&s.P[i * LDC + j], x); });
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
-    const int i = idx / C, j = idx % C;
-    s.P[i * LDC + j] = j <= i ? s.P[i * LDC + j] * __expf(s.gam[i] - s.gam[j]) : 0.f;
-  }
+  // ---- KK, P (with Gam, incl), T
+  matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
+  matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {
+    s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
+  });
   __syncthreads();
   ut_transform(C, s.KK, s.gam, s.beta, s.X, s.T);  // X is scratch for A here
   // ---- R0 = V - diag(E) k^ S (in place over V)
-  matmul_add<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
-    atomicAdd(&s.R0[i * VD + d], -__expf(s.gam[i]) * x);
+  matmul<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
+    s.R0[i * VD + d] -= __expf(s.gam[i]) * x;
   });
   __syncthreads();
   // ---- V' = (T diag(beta)) R0
@@ -720,12 +642,9 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     a.dv[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(s.beta[i] * x);
   });
   // ---- T-path: dT = dV' R^T (R = diag(beta) R0) -> Y ; dA = strict_lower(-T^T dT T^T) -> Y
-  for (int idx = threadIdx.x; idx < 32 * LDC; idx += NT) s.Y[idx] = 0.f, s.X[idx] = 0.f;
+  matmul<false, true>(C, C, Dv, s.dVp, VD, s.R0, VD, [&](int i, int j, float x) { s.Y[i * LDC + j] = x * s.beta[j]; });
   __syncthreads();
-  matmul_add<false, true>(C, C, Dv, s.dVp, VD, s.R0, VD,
-                          [&](int i, int j, float x) { atomicAdd(&s.Y[i * LDC + j], x * s.beta[j]); });
-  __syncthreads();
-  matmul_add<false, true>(C, C, C, s.Y, LDC, s.T, LDC, [&](int i, int j, float x) { atomicAdd(&s.X[i * LDC + j], x); });
+  matmul<false, true>(C, C, C, s.Y, LDC, s.T, LDC, [&](int i, int j, float x) { s.X[i * LDC + j] = x; });
   __syncthreads();
   matmul<true, false>(C, C, C, s.T, LDC, s.X, LDC, [&](int i, int j, float x) { s.Y[i * LDC + j] = j < i ? -x : 0.f; });
   __syncthreads();
@@ -748,34 +667,33 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   }
   __syncthreads();
   // dK += dKK k^ + dKK^T k^ ; dV' is dead from here on: its tile becomes the dq^ accumulator
-  matmul_add<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { atomicAdd(&s.dK[i * KD + d], x); });
-  matmul_add<true, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { atomicAdd(&s.dK[i * KD + d], x); });
+  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  __syncthreads();
+  matmul<true, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
     const int i = idx / Dk, d = idx % Dk;
     s.dQ[i * KD + d] = 0.f;
   }
   __syncthreads();
   // ---- products with S: dQ += diag(E) dO S^T ; dK -= diag(beta E) dR S^T ; dE terms ; dbeta part
-  matmul_add<false, true>(C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) {
-    atomicAdd(&s.dQ[i * KD + d], __expf(s.gam[i]) * x);
+  matmul<false, true>(C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) {
+    s.dQ[i * KD + d] += __expf(s.gam[i]) * x;
   });
-  matmul_add<false, true>(C, Dk, Dv, s.dR, VD, s.S, VD, [&](int i, int d, float x) {
-    atomicAdd(&s.dK[i * KD + d], -s.beta[i] * __expf(s.gam[i]) * x);
+  matmul<false, true>(C, Dk, Dv, s.dR, VD, s.S, VD, [&](int i, int d, float x) {
+    s.dK[i * KD + d] -= s.beta[i] * __expf(s.gam[i]) * x;
   });
-  matmul_rowsum_sk<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD,
-                                  [&](int i, int d, float x) { return x * s.dO[i * VD + d]; }, s.dE);
-  matmul_rowsum_sk<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
-                                  [&](int i, int d, float x) { return -s.beta[i] * x * s.dR[i * VD + d]; }, s.dE);
+  matmul_rowsum<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD,
+                               [&](int i, int d, float x) { return x * s.dO[i * VD + d]; }, s.dE);
+  matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
+                               [&](int i, int d, float x) { return -s.beta[i] * x * s.dR[i * VD + d]; }, s.dE);
   __syncthreads();
   rowdot(C, Dv, s.dR, VD, s.R0, VD, s.red);
   __syncthreads();
   // ---- dP = dO V'^T ; dPm = dP * Gam (incl) -> X ; G1 = dP * P -> Y ; dgam += rowsum(G1) - colsum(G1)
-  for (int idx = threadIdx.x; idx < 32 * LDC; idx += NT) s.X[idx] = 0.f, s.Y[idx] = 0.f;
-  __syncthreads();
-  matmul_add<false, true>(C, C, Dv, s.dO, VD, s.Vp, VD, [&](int i, int j, float x) {
+  matmul<false, true>(C, C, Dv, s.dO, VD, s.Vp, VD, [&](int i, int j, float x) {
     const float gm = j <= i ? __expf(s.gam[i] - s.gam[j]) : 0.f;
-    atomicAdd(&s.X[i * LDC + j], x * gm);
-    atomicAdd(&s.Y[i * LDC + j], x * s.P[i * LDC + j]);
+    s.X[i * LDC + j] = x * gm;
+    s.Y[i * LDC + j] = x * s.P[i * LDC + j];
   });
   __syncthreads();
   if (threadIdx.x < C) {
@@ -785,8 +703,8 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.dgam[i] += rs - cs;
   }
   __syncthreads();
-  matmul_add<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { atomicAdd(&s.dQ[i * KD + d], x); });
-  matmul_add<true, false>(C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { atomicAdd(&s.dK[i * KD + d], x); });
+  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dQ[i * KD + d] += x; });
+  matmul<true, false>(C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   __syncthreads();
   // ---- state gradient
   if (mode == 0) {
@@ -819,11 +737,11 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     }
     __syncthreads();
     // dK += diag(F) V' dS_out^T ; dF_i = sum_b (k^ dS_out)_ib V'_ib
-    matmul_add<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
-      atomicAdd(&s.dK[i * KD + d], __expf(s.gam[C - 1] - s.gam[i]) * x);
+    matmul<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
+      s.dK[i * KD + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
     });
-    matmul_rowsum_sk<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
-                                    [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
+    matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
+                                 [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
     __syncthreads();
   }
   // ---- gates: dgam += dE E - dF F ; dgam[C-1] += sum dF F ; dg = reverse cumsum ; dbeta

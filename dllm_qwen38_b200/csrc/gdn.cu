@@ -64,7 +64,13 @@ struct Args {
   __nv_bfloat16* dv;  // [B, 2L, Hv, Dv]
   float* dg;          // [B, 2L, Hv]
   float* dbeta;       // [B, 2L, Hv]
+  long long* phase;   // optional: clock64() at phase boundaries of CTA (0, 0) (BDLLM_GDN_PHASES=1)
 };
+
+// records the SM clock at phase boundary `k` (thread 0 of CTA (0, 0) only; no-op without a buffer)
+__device__ __forceinline__ void mark(const Args& a, int k) {
+  if (a.phase != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) a.phase[k] = clock64();
+}
 
 // ------------------------------------------------------------------ small matmul in smem
 // For every output (m, n) of an M x N product sum_k A(m,k) B(k,n), call epi(m, n, value).
@@ -587,6 +593,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   const int c = blockIdx.x;
   const int bh = blockIdx.y, b = bh / a.Hv, h = bh % a.Hv;
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
+  mark(a, 0);
   // ---- loads: q^, k^, V (into R0), gam, beta, S, dO
   load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.R0, s.gam, s.beta, true, true);
   const float* Sin = a.S_in + base * Dk * Dv;
@@ -605,13 +612,17 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     const int i = idx / Dk, d = idx % Dk;
     s.dK[i * KD + d] = 0.f;
   }
+  __syncthreads();
+  mark(a, 1);  // loads done
   // ---- KK, P (with Gam, incl), T
   matmul<false, true>(C, C, Dk, s.K, KD, s.K, KD, [&](int i, int j, float x) { s.KK[i * LDC + j] = x; });
   matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {
     s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
   });
   __syncthreads();
+  mark(a, 2);  // KK, P
   ut_transform(C, s.KK, s.gam, s.beta, s.X, s.T);  // X is scratch for A here
+  mark(a, 3);  // UT transform
   // ---- R0 = V - diag(E) k^ S (in place over V)
   matmul<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
     s.R0[i * VD + d] -= __expf(s.gam[i]) * x;
@@ -625,6 +636,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   __syncthreads();
   matmul<false, false>(C, Dv, C, s.X, LDC, s.R0, VD, [&](int i, int d, float x) { s.Vp[i * VD + d] = x; });
   __syncthreads();
+  mark(a, 4);  // R0, V'
   // ---- dV'
   if (mode == 0) {
     matmul<true, false>(C, Dv, C, s.P, LDC, s.dO, VD, [&](int i, int d, float x) { s.dVp[i * VD + d] = x; });
@@ -641,6 +653,8 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.dR[i * VD + d] = x;
     a.dv[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(s.beta[i] * x);
   });
+  __syncthreads();
+  mark(a, 5);  // dV', dR, dv
   // ---- T-path: dT = dV' R^T (R = diag(beta) R0) -> Y ; dA = strict_lower(-T^T dT T^T) -> Y
   matmul<false, true>(C, C, Dv, s.dVp, VD, s.R0, VD, [&](int i, int j, float x) { s.Y[i * LDC + j] = x * s.beta[j]; });
   __syncthreads();
@@ -666,6 +680,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.dgam[i] += s.beta[i] * rs - cs;
   }
   __syncthreads();
+  mark(a, 6);  // T-path, dKK, dbeta / dgam rows
   // dK += dKK k^ + dKK^T k^ ; dV' is dead from here on: its tile becomes the dq^ accumulator
   matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   __syncthreads();
@@ -675,6 +690,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.dQ[i * KD + d] = 0.f;
   }
   __syncthreads();
+  mark(a, 7);  // dK from dKK
   // ---- products with S: dQ += diag(E) dO S^T ; dK -= diag(beta E) dR S^T ; dE terms ; dbeta part
   matmul<false, true>(C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) {
     s.dQ[i * KD + d] += __expf(s.gam[i]) * x;
@@ -689,6 +705,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   __syncthreads();
   rowdot(C, Dv, s.dR, VD, s.R0, VD, s.red);
   __syncthreads();
+  mark(a, 8);  // products with S
   // ---- dP = dO V'^T ; dPm = dP * Gam (incl) -> X ; G1 = dP * P -> Y ; dgam += rowsum(G1) - colsum(G1)
   matmul<false, true>(C, C, Dv, s.dO, VD, s.Vp, VD, [&](int i, int j, float x) {
     const float gm = j <= i ? __expf(s.gam[i] - s.gam[j]) : 0.f;
@@ -706,6 +723,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dQ[i * KD + d] += x; });
   matmul<true, false>(C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   __syncthreads();
+  mark(a, 9);  // dP path
   // ---- state gradient
   if (mode == 0) {
     // dS_inj = (diag(E) q^)^T dO - k^T diag(beta E) dR ; dO and dR are consumed (scaled in place)
@@ -744,6 +762,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
                                  [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
     __syncthreads();
   }
+  mark(a, 10);  // state gradient
   // ---- gates: dgam += dE E - dF F ; dgam[C-1] += sum dF F ; dg = reverse cumsum ; dbeta
   if (threadIdx.x < 32) {
     const int i = threadIdx.x;
@@ -767,6 +786,7 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
       a.dbeta[t * a.Hv + h] = s.red[i];
     }
   }
+  mark(a, 11);  // gates
   // ---- l2norm backward (warp per row): dq = l2_bwd(q_raw, scale * dQ), dk = l2_bwd(k_raw, dK)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int hk = h / (a.Hv / a.Hk);
@@ -792,7 +812,10 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
       out[d] = __float2bfloat16(rr * dy[d] * sc - x * rr * rr * rr * xd);
     }
   }
+  __syncthreads();
+  mark(a, 12);  // l2norm backward, stores
 }
+
 
 // clean chunks: what the reverse recurrence needs -> PtdO [C][Dv], Kt [C][Dk], Qt [C][Dk], W [C][Dk], Ec
 template <int Dk, int Dv>
@@ -1082,12 +1105,34 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   a.W = W.data_ptr<float>();
   a.Ec = Ec.data_ptr<float>();
   const int BH = a.B * a.Hv;
-  if (!concat) launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
-  launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
+  // BDLLM_GDN_PHASES=1: clock64() at the phase boundaries of the chunk kernel's first CTA, printed
+  // per launch (diagnostics; one device-to-host read per launch)
+  static const bool phases = getenv("BDLLM_GDN_PHASES") != nullptr;
+  at::Tensor ph;
+  auto report = [&](const char* what) {
+    if (!phases) return;
+    auto h = ph.cpu();
+    const long long* t = h.data_ptr<long long>();
+    fprintf(stderr, "[gdn phases] %s:", what);
+    for (int i = 1; i < 13; ++i) fprintf(stderr, " %lld", t[i] - t[i - 1]);
+    fprintf(stderr, " | total %lld cycles\n", t[12] - t[0]);
+  };
+  if (phases) {
+    ph = at::zeros({16}, q.options().dtype(at::kLong));
+    a.phase = ph.data_ptr<long long>();
+  }
+  if (!concat) {
+    launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
+    report("noised");
+  }
+  Args a2 = a;
+  a2.phase = nullptr;
+  launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a2);
   launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
-          2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a,
+          2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a2,
           concat ? 0 : 1);
   launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
+  report("clean");
   return {dq, dk, dv, dg, db};
 }
 

@@ -1112,14 +1112,14 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto report = [&](const char* what) {
     if (!phases) return;
     auto h = ph.cpu();
-    const long long* t = h.data_ptr<long long>();
+    const int64_t* t = h.data_ptr<int64_t>();
     fprintf(stderr, "[gdn phases] %s:", what);
-    for (int i = 1; i < 13; ++i) fprintf(stderr, " %lld", t[i] - t[i - 1]);
-    fprintf(stderr, " | total %lld cycles\n", t[12] - t[0]);
+    for (int i = 1; i < 13; ++i) fprintf(stderr, " %lld", (long long)(t[i] - t[i - 1]));
+    fprintf(stderr, " | total %lld cycles\n", (long long)(t[12] - t[0]));
   };
   if (phases) {
     ph = at::zeros({16}, q.options().dtype(at::kLong));
-    a.phase = ph.data_ptr<long long>();
+    a.phase = reinterpret_cast<long long*>(ph.data_ptr<int64_t>());
   }
   if (!concat) {
     launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);

@@ -329,14 +329,31 @@ __device__ void ut_transform(int C, const float* sKK, const float* sgam, const f
     sA[i * LDC + j] = j < i ? sbeta[i] * sKK[i * LDC + j] * __expf(sgam[i] - sgam[j]) : 0.f;
   }
   __syncthreads();
-  if (threadIdx.x < 32) {  // forward substitution, lane = column (C <= 32)
+  if (threadIdx.x < 32) {
+    // forward substitution, lane = column of T: the column lives in registers (t[i] for rows i),
+    // row i needs sum_{j<i} A_ij t_j: fully unrolled with four independent partial sums, A read as
+    // broadcast shared loads. Rows / columns >= C have A = 0 and are not stored.
     const int col = threadIdx.x;
-    for (int i = 0; i < C; ++i) {
-      float v = (i == col) ? 1.f : 0.f;
-      for (int j = 0; j < i; ++j) v -= sA[i * LDC + j] * sT[j * LDC + col];
-      if (col < C) sT[i * LDC + col] = v;
-      __syncwarp();
+    float t[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+      const float* Ai = sA + i * LDC;
+#pragma unroll
+      for (int j = 0; j + 3 < i; j += 4) {
+        p0 += Ai[j] * t[j];
+        p1 += Ai[j + 1] * t[j + 1];
+        p2 += Ai[j + 2] * t[j + 2];
+        p3 += Ai[j + 3] * t[j + 3];
+      }
+#pragma unroll
+      for (int j = i & ~3; j < i; ++j) p0 += Ai[j] * t[j];
+      t[i] = (i < C ? ((i == col) ? 1.f : 0.f) - ((p0 + p1) + (p2 + p3)) : 0.f);
     }
+    if (col < C)
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < C) sT[i * LDC + col] = t[i];
   }
   __syncthreads();
 }
@@ -532,9 +549,16 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
   float* sO = s.Y;
   matmul<false, false>(C, Dv, C, s.P, LDC, sVp, VD, [&](int i, int d, float x) { sO[i * VD + d] = x; });
   __syncthreads();
-  matmul<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD, [&](int i, int d, float x) {
-    a.o[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(x + sO[i * VD + d]);
-  });
+  matmul<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD, [&](int i, int d, float x) { sO[i * VD + d] += x; });
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < C * (Dv / 8); idx += NT) {  // 16-byte bf16 stores
+    const int i = idx / (Dv / 8), d = (idx % (Dv / 8)) * 8;
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(sO[i * VD + d + 2 * e], sO[i * VD + d + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(a.o + tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d) = o;
+  }
 }
 
 // ================================================================== backward
@@ -601,9 +625,15 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
     *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(Sin + r * Dv + d);
   }
-  for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
-    const int i = idx / Dv, d = idx % Dv;
-    s.dO[i * VD + d] = __bfloat162float(a.dout[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d]);
+  for (int idx = threadIdx.x; idx < C * (Dv / 8); idx += NT) {  // 16-byte loads
+    const int i = idx / (Dv / 8), d = (idx % (Dv / 8)) * 8;
+    const uint4 raw = *reinterpret_cast<const uint4*>(a.dout + tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d);
+    const __nv_bfloat162* r2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(r2[e]);
+      s.dO[i * VD + d + 2 * e] = f.x, s.dO[i * VD + d + 2 * e + 1] = f.y;
+    }
   }
   if (threadIdx.x < 32) {
     s.dgam[threadIdx.x] = 0.f, s.dE[threadIdx.x] = 0.f, s.dF[threadIdx.x] = 0.f, s.red[threadIdx.x] = 0.f;
@@ -649,10 +679,17 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   }
   __syncthreads();
   // ---- dR = T^T dV' ; dV = diag(beta) dR -> global
-  matmul<true, false>(C, Dv, C, s.T, LDC, s.dVp, VD, [&](int i, int d, float x) {
-    s.dR[i * VD + d] = x;
-    a.dv[tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d] = __float2bfloat16(s.beta[i] * x);
-  });
+  matmul<true, false>(C, Dv, C, s.T, LDC, s.dVp, VD, [&](int i, int d, float x) { s.dR[i * VD + d] = x; });
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < C * (Dv / 8); idx += NT) {  // dv = diag(beta) dR, 16-byte stores
+    const int i = idx / (Dv / 8), d = (idx % (Dv / 8)) * 8;
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+    const float bi = s.beta[i];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(bi * s.dR[i * VD + d + 2 * e], bi * s.dR[i * VD + d + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(a.dv + tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d) = o;
+  }
   __syncthreads();
   mark(a, 5);  // dV', dR, dv
   // ---- T-path: dT = dV' R^T (R = diag(beta) R0) -> Y ; dA = strict_lower(-T^T dT T^T) -> Y
@@ -737,9 +774,12 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     matmul<true, false>(Dk, Dv, C, s.Q, KD, s.dO, VD, [&](int r, int d, float x) { s.S[r * VD + d] = x; });
     __syncthreads();
     float* dSi = a.dS_inj + base * Dk * Dv;
-    matmul<true, false>(Dk, Dv, C, s.K, KD, s.dR, VD, [&](int r, int d, float x) {
-      dSi[r * Dv + d] = s.S[r * VD + d] - x;
-    });
+    matmul<true, false>(Dk, Dv, C, s.K, KD, s.dR, VD, [&](int r, int d, float x) { s.S[r * VD + d] -= x; });
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {  // 16-byte stores
+      const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
+      *reinterpret_cast<float4*>(dSi + r * Dv + d) = *reinterpret_cast<const float4*>(s.S + r * VD + d);
+    }
     __syncthreads();
   } else {
     // dEc = sum S * dS_out (S still in smem, dS_out from global) ; then S <- dS_out

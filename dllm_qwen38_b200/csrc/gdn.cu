@@ -503,13 +503,14 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
   const int stream = (a.concat || blockIdx.x >= a.nb) ? 1 : 0;
   const int c = blockIdx.x - ((stream && !a.concat) ? a.nb : 0);
   const int bh = blockIdx.y, b = bh / a.Hv, h = bh % a.Hv;
-  load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.V, s.gam, s.beta, true, stream == 0);
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
   const float* Sin = a.S_in + base * Dk * Dv;
-  for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
+  for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {  // asynchronous: first used for V' / O
     const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
-    *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(Sin + r * Dv + d);
+    cp16(s.S + r * VD + d, Sin + r * Dv + d);
   }
+  cp_commit();
+  load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.V, s.gam, s.beta, true, stream == 0);
   matmul<false, true>(C, C, Dk, s.Q, KD, s.K, KD, [&](int i, int j, float x) {  // P = q^ k^T * Gam (incl)
     s.P[i * LDC + j] = j <= i ? x * __expf(s.gam[i] - s.gam[j]) : 0.f;
   });
@@ -530,6 +531,7 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
     __syncthreads();
     matmul<false, false>(C, Dk, C, s.T, LDC, s.Y, KD, [&](int i, int d, float x) { s.W[i * KD + d] = x; });
     matmul<false, false>(C, Dv, C, s.T, LDC, s.V, VD, [&](int i, int d, float x) { sVp[i * VD + d] = x; });
+    cp_wait_all();
     __syncthreads();
     matmul<false, false>(C, Dv, Dk, s.W, KD, s.S, VD, [&](int i, int d, float x) { sVp[i * VD + d] -= x; });
   } else {
@@ -539,6 +541,7 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
       sVp[i * VD + d] = Vp[idx];
     }
   }
+  cp_wait_all();
   __syncthreads();
   // O = diag(E) q^ S + P V'
   for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
@@ -618,13 +621,15 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   const int bh = blockIdx.y, b = bh / a.Hv, h = bh % a.Hv;
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
   mark(a, 0);
-  // ---- loads: q^, k^, V (into R0), gam, beta, S, dO
-  load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.R0, s.gam, s.beta, true, true);
+  // ---- loads: S (asynchronously: first needed after the UT transform), q^, k^, V (into R0), gam,
+  // beta, dO
   const float* Sin = a.S_in + base * Dk * Dv;
   for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
     const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
-    *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(Sin + r * Dv + d);
+    cp16(s.S + r * VD + d, Sin + r * Dv + d);
   }
+  cp_commit();
+  load_chunk<Dk, Dv>(a, b, stream, c, h, s.Q, s.K, s.R0, s.gam, s.beta, true, true);
   for (int idx = threadIdx.x; idx < C * (Dv / 8); idx += NT) {  // 16-byte loads
     const int i = idx / (Dv / 8), d = (idx % (Dv / 8)) * 8;
     const uint4 raw = *reinterpret_cast<const uint4*>(a.dout + tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d);
@@ -652,7 +657,9 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   __syncthreads();
   mark(a, 2);  // KK, P
   ut_transform(C, s.KK, s.gam, s.beta, s.X, s.T);  // X is scratch for A here
-  mark(a, 3);  // UT transform
+  cp_wait_all();
+  __syncthreads();
+  mark(a, 3);  // UT transform (and the state tile landed)
   // ---- R0 = V - diag(E) k^ S (in place over V)
   matmul<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
     s.R0[i * VD + d] -= __expf(s.gam[i]) * x;

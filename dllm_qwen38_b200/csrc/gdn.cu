@@ -149,6 +149,45 @@ __device__ __forceinline__ void mm_tc(int M, int N, int K, const float* A, int l
   }
 }
 
+// mm_tc over warps [w0, w0 + nw) only (the other warps skip it)
+template <bool AT, bool BT, typename Epi>
+__device__ __forceinline__ void mm_tc_part(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
+                                           Epi epi, int w0, int nw) {
+  const int warp = (threadIdx.x >> 5) - w0, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  if (warp < 0 || warp >= nw) return;
+  const int tiles_n = N / 32, tiles = (M / 16) * tiles_n;
+  for (int tile = warp; tile < tiles; tile += nw) {
+    const int m0 = (tile / tiles_n) * 16, n0 = (tile % tiles_n) * 32;
+    float c[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) c[j][0] = c[j][1] = c[j][2] = c[j][3] = 0.f;
+    for (int k0 = 0; k0 < K; k0 += 8) {
+      auto Aget = [&](int m, int k) { return AT ? A[k * lda + m] : A[m * lda + k]; };
+      const uint32_t a0 = tf32(Aget(m0 + g, k0 + t)), a1 = tf32(Aget(m0 + g + 8, k0 + t));
+      const uint32_t a2 = tf32(Aget(m0 + g, k0 + t + 4)), a3 = tf32(Aget(m0 + g + 8, k0 + t + 4));
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int n = n0 + j * 8 + g;
+        const uint32_t b0 = tf32(BT ? B[n * ldb + k0 + t] : B[(k0 + t) * ldb + n]);
+        const uint32_t b1 = tf32(BT ? B[n * ldb + k0 + t + 4] : B[(k0 + t + 4) * ldb + n]);
+        asm volatile(
+            "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(c[j][0]), "+f"(c[j][1]), "+f"(c[j][2]), "+f"(c[j][3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + j * 8 + 2 * t;
+      epi(m0 + g, n, c[j][0]);
+      epi(m0 + g, n + 1, c[j][1]);
+      epi(m0 + g + 8, n, c[j][2]);
+      epi(m0 + g + 8, n + 1, c[j][3]);
+    }
+  }
+}
+
 // tensor cores when the shape tiles into 16 x 32 x 8, else fp32 CUDA cores (4x4 register tiles)
 template <bool AT, bool BT, typename Epi>
 __device__ __forceinline__ void matmul(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
@@ -214,6 +253,50 @@ __device__ __forceinline__ void matmul_rowsum(int M, int N, int K, const float* 
 }
 
 // out[i] += sum_d X[i][d] * Y[i][d] over C rows of D, warp per row
+// Two independent products at once, each on half of the warps (for shapes whose tile count is at
+// most half the warps, so neither half idles); sequential when a shape does not tile.
+template <bool AT1, bool BT1, bool AT2, bool BT2, typename E1, typename E2>
+__device__ __forceinline__ void matmul_pair(int M1, int N1, int K1, const float* A1, int lda1, const float* B1,
+                                            int ldb1, E1 e1, int M2, int N2, int K2, const float* A2, int lda2,
+                                            const float* B2, int ldb2, E2 e2) {
+  const bool tc = M1 % 16 == 0 && N1 % 32 == 0 && K1 % 8 == 0 && M2 % 16 == 0 && N2 % 32 == 0 && K2 % 8 == 0;
+  if (!tc) {
+    matmul<AT1, BT1>(M1, N1, K1, A1, lda1, B1, ldb1, e1);
+    matmul<AT2, BT2>(M2, N2, K2, A2, lda2, B2, ldb2, e2);
+    return;
+  }
+  constexpr int H = NT / 64;
+  mm_tc_part<AT1, BT1>(M1, N1, K1, A1, lda1, B1, ldb1, e1, 0, H);
+  mm_tc_part<AT2, BT2>(M2, N2, K2, A2, lda2, B2, ldb2, e2, H, H);
+}
+
+// matmul_rowsum for two products at once (each on half of the warps)
+template <bool AT1, bool BT1, bool AT2, bool BT2, typename F1, typename F2>
+__device__ __forceinline__ void matmul_rowsum_pair(int M1, int N1, int K1, const float* A1, int lda1, const float* B1,
+                                                   int ldb1, F1 f1, float* out1, int M2, int N2, int K2,
+                                                   const float* A2, int lda2, const float* B2, int ldb2, F2 f2,
+                                                   float* out2) {
+  const bool tc = M1 % 16 == 0 && N1 % 32 == 0 && K1 % 8 == 0 && M2 % 16 == 0 && N2 % 32 == 0 && K2 % 8 == 0;
+  if (!tc) {
+    matmul_rowsum<AT1, BT1>(M1, N1, K1, A1, lda1, B1, ldb1, f1, out1);
+    matmul_rowsum<AT2, BT2>(M2, N2, K2, A2, lda2, B2, ldb2, f2, out2);
+    return;
+  }
+  constexpr int H = NT / 64;
+  const int lane = threadIdx.x & 31;
+  auto row_acc = [&](auto f, float* out) {
+    return [&, f, out](int m, int n, float x) {
+      // the four lanes of a quad share row m: reduce over the quad, one atomic per row and column pair
+      float v = f(m, n, x);
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if ((lane & 3) == 0) atomicAdd(&out[m], v);
+    };
+  };
+  mm_tc_part<AT1, BT1>(M1, N1, K1, A1, lda1, B1, ldb1, row_acc(f1, out1), 0, H);
+  mm_tc_part<AT2, BT2>(M2, N2, K2, A2, lda2, B2, ldb2, row_acc(f2, out2), H, H);
+}
+
 __device__ __forceinline__ void rowdot(int C, int D, const float* X, int ldx, const float* Y, int ldy, float* out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = warp; i < C; i += NT / 32) {
@@ -671,13 +754,17 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.X[i * LDC + j] = s.T[i * LDC + j] * s.beta[j];
   }
   __syncthreads();
-  matmul<false, false>(C, Dv, C, s.X, LDC, s.R0, VD, [&](int i, int d, float x) { s.Vp[i * VD + d] = x; });
-  __syncthreads();
-  mark(a, 4);  // R0, V'
-  // ---- dV'
+  // ---- V' and dV' (noised blocks: P^T dO, computed next to V' on the other half of the warps)
   if (mode == 0) {
-    matmul<true, false>(C, Dv, C, s.P, LDC, s.dO, VD, [&](int i, int d, float x) { s.dVp[i * VD + d] = x; });
+    matmul_pair<false, false, true, false>(
+        C, Dv, C, s.X, LDC, s.R0, VD, [&](int i, int d, float x) { s.Vp[i * VD + d] = x; },
+        C, Dv, C, s.P, LDC, s.dO, VD, [&](int i, int d, float x) { s.dVp[i * VD + d] = x; });
+    __syncthreads();
+    mark(a, 4);  // R0, V', dV'
   } else {
+    matmul<false, false>(C, Dv, C, s.X, LDC, s.R0, VD, [&](int i, int d, float x) { s.Vp[i * VD + d] = x; });
+    __syncthreads();
+    mark(a, 4);  // R0, V'
     const float* gdv = a.dVp + base * C * Dv;
     for (int idx = threadIdx.x; idx < C * Dv; idx += NT) {
       const int i = idx / Dv, d = idx % Dv;
@@ -725,10 +812,14 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   }
   __syncthreads();
   mark(a, 6);  // T-path, dKK, dbeta / dgam rows
-  // dK += dKK k^ + dKK^T k^ ; dV' is dead from here on: its tile becomes the dq^ accumulator
-  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  // dK += dKK k^ + dKK^T k^ = (dKK + dKK^T) k^ (Y is free again); dV' is dead from here on: its
+  // tile becomes the dq^ accumulator
+  for (int idx = threadIdx.x; idx < C * C; idx += NT) {
+    const int i = idx / C, j = idx % C;
+    s.Y[i * LDC + j] = s.X[i * LDC + j] + s.X[j * LDC + i];
+  }
   __syncthreads();
-  matmul<true, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  matmul<false, false>(C, Dk, C, s.Y, LDC, s.K, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   for (int idx = threadIdx.x; idx < C * Dk; idx += NT) {
     const int i = idx / Dk, d = idx % Dk;
     s.dQ[i * KD + d] = 0.f;
@@ -736,16 +827,13 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
   __syncthreads();
   mark(a, 7);  // dK from dKK
   // ---- products with S: dQ += diag(E) dO S^T ; dK -= diag(beta E) dR S^T ; dE terms ; dbeta part
-  matmul<false, true>(C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) {
-    s.dQ[i * KD + d] += __expf(s.gam[i]) * x;
-  });
-  matmul<false, true>(C, Dk, Dv, s.dR, VD, s.S, VD, [&](int i, int d, float x) {
-    s.dK[i * KD + d] -= s.beta[i] * __expf(s.gam[i]) * x;
-  });
-  matmul_rowsum<false, false>(C, Dv, Dk, s.Q, KD, s.S, VD,
-                               [&](int i, int d, float x) { return x * s.dO[i * VD + d]; }, s.dE);
-  matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
-                               [&](int i, int d, float x) { return -s.beta[i] * x * s.dR[i * VD + d]; }, s.dE);
+  matmul_pair<false, true, false, true>(
+      C, Dk, Dv, s.dO, VD, s.S, VD, [&](int i, int d, float x) { s.dQ[i * KD + d] += __expf(s.gam[i]) * x; },
+      C, Dk, Dv, s.dR, VD, s.S, VD,
+      [&](int i, int d, float x) { s.dK[i * KD + d] -= s.beta[i] * __expf(s.gam[i]) * x; });
+  matmul_rowsum_pair<false, false, false, false>(
+      C, Dv, Dk, s.Q, KD, s.S, VD, [&](int i, int d, float x) { return x * s.dO[i * VD + d]; }, s.dE,
+      C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) { return -s.beta[i] * x * s.dR[i * VD + d]; }, s.dE);
   __syncthreads();
   rowdot(C, Dv, s.dR, VD, s.R0, VD, s.red);
   __syncthreads();
@@ -764,8 +852,9 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     s.dgam[i] += rs - cs;
   }
   __syncthreads();
-  matmul<false, false>(C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dQ[i * KD + d] += x; });
-  matmul<true, false>(C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
+  matmul_pair<false, false, true, false>(
+      C, Dk, C, s.X, LDC, s.K, KD, [&](int i, int d, float x) { s.dQ[i * KD + d] += x; },
+      C, Dk, C, s.X, LDC, s.Q, KD, [&](int i, int d, float x) { s.dK[i * KD + d] += x; });
   __syncthreads();
   mark(a, 9);  // dP path
   // ---- state gradient

@@ -149,6 +149,8 @@ __device__ __forceinline__ void mm_tc(int M, int N, int K, const float* A, int l
   }
 }
 
+#define M_TILES_OK(M, N, K) ((M) % 16 == 0 && (N) % 32 == 0 && (K) % 8 == 0)
+
 // mm_tc over warps [w0, w0 + nw) only (the other warps skip it)
 template <bool AT, bool BT, typename Epi>
 __device__ __forceinline__ void mm_tc_part(int M, int N, int K, const float* A, int lda, const float* B, int ldb,
@@ -878,24 +880,41 @@ __global__ void __launch_bounds__(NT) bwd_chunk_kernel(Args a, int mode) {
     }
     __syncthreads();
   } else {
-    // dEc = sum S * dS_out (S still in smem, dS_out from global) ; then S <- dS_out
+    // dEc = sum S * dS_out and S <- dS_out in one pass (each thread reads its four S values before
+    // overwriting them)
     const float* dSo = a.dS_out + base * Dk * Dv;
     float part = 0.f;
-    for (int idx = threadIdx.x; idx < Dk * Dv; idx += NT) part += s.S[(idx / Dv) * VD + idx % Dv] * dSo[idx];
+    for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
+      const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
+      float4* sp = reinterpret_cast<float4*>(s.S + r * VD + d);
+      const float4 o = *reinterpret_cast<const float4*>(dSo + r * Dv + d);
+      const float4 v = *sp;
+      part += v.x * o.x + v.y * o.y + v.z * o.z + v.w * o.w;
+      *sp = o;
+    }
     part = wsum(part);
     if ((threadIdx.x & 31) == 0) atomicAdd(&s.dgam[C - 1], part * __expf(s.gam[C - 1]));  // dEc * Ec
     __syncthreads();
-    for (int idx = threadIdx.x; idx < Dk * (Dv / 4); idx += NT) {
-      const int r = idx / (Dv / 4), d = (idx % (Dv / 4)) * 4;
-      *reinterpret_cast<float4*>(s.S + r * VD + d) = *reinterpret_cast<const float4*>(dSo + r * Dv + d);
+    // dK += diag(F) V' dS_out^T ; dF_i = sum_b (k^ dS_out)_ib V'_ib (on the two halves of the warps)
+    if (M_TILES_OK(C, Dk, Dv) && M_TILES_OK(C, Dv, Dk)) {
+      constexpr int H = NT / 64;
+      const int lane = threadIdx.x & 31;
+      mm_tc_part<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
+        s.dK[i * KD + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
+      }, 0, H);
+      mm_tc_part<false, false>(C, Dv, Dk, s.K, KD, s.S, VD, [&](int i, int d, float x) {
+        float v = x * s.Vp[i * VD + d];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        if ((lane & 3) == 0) atomicAdd(&s.dF[i], v);
+      }, H, H);
+    } else {
+      matmul<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
+        s.dK[i * KD + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
+      });
+      matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
+                                   [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
     }
-    __syncthreads();
-    // dK += diag(F) V' dS_out^T ; dF_i = sum_b (k^ dS_out)_ib V'_ib
-    matmul<false, true>(C, Dk, Dv, s.Vp, VD, s.S, VD, [&](int i, int d, float x) {
-      s.dK[i * KD + d] += __expf(s.gam[C - 1] - s.gam[i]) * x;
-    });
-    matmul_rowsum<false, false>(C, Dv, Dk, s.K, KD, s.S, VD,
-                                 [&](int i, int d, float x) { return x * s.Vp[i * VD + d]; }, s.dF);
     __syncthreads();
   }
   mark(a, 10);  // state gradient

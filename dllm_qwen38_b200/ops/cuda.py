@@ -161,8 +161,13 @@ class _Linear(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w):
         ctx.save_for_backward(x, w)
-        y = gemm_nt(x, w)
-        return y.reshape(*x.shape[:-1], w.shape[0])
+        saved = ActStore.take() if ActStore.gemms else None
+        if saved is not None:
+            return saved[0]
+        y = gemm_nt(x, w).reshape(*x.shape[:-1], w.shape[0])
+        if ActStore.gemms:
+            ActStore.put(y)
+        return y
 
     @staticmethod
     def backward(ctx, dy):
@@ -261,11 +266,18 @@ class _SwiGLUMLP(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_gu, w_down):
         F = w_gu.shape[0] // 2
-        need = any(ctx.needs_input_grad)
-        act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
-        y = gemm_nt(act, w_down)
+        saved = ActStore.take() if ActStore.gemms else None
+        if saved is not None:
+            y, act, gu = saved
+        else:
+            # the saving forward (no grad) keeps gate|up for the backward it will serve
+            need = any(ctx.needs_input_grad) or (ActStore.gemms and ActStore.mode == "save")
+            act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
+            y = gemm_nt(act, w_down).reshape(*x.shape[:-1], w_down.shape[0])
+            if ActStore.gemms:
+                ActStore.put(y, act, gu)
         ctx.save_for_backward(x, w_gu, w_down, act, gu)
-        return y.reshape(*x.shape[:-1], w_down.shape[0])
+        return y
 
     @staticmethod
     def backward(ctx, dy):
@@ -353,9 +365,12 @@ class ActStore:
     """Selective activation saving across activation checkpointing: in "save" mode the GDN core
     and attention forwards keep their outputs (and the state snapshots / log-sum-exps their
     backward needs) per layer; in "reuse" mode the recomputation inside the backward returns them
-    instead of running those kernels again. Keyed by layer, consumed in call order."""
+    instead of running those kernels again. Keyed by layer, consumed in call order. With `gemms`
+    set, the projection GEMMs and the SwiGLU MLP keep their outputs too (the MLP also its gate|up
+    and activation), so the recomputation runs only the cheap elementwise / norm kernels."""
 
     mode = None
+    gemms = False
     key = None
     data: dict = {}
     pos = 0

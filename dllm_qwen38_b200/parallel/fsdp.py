@@ -240,6 +240,9 @@ class FSDPEngine:
             from ..ops import cuda as Cu
 
             self.act_store = Cu.ActStore
+        # also keep the GEMM outputs of the checkpointed forward ("1", "0", or "auto": when the
+        # estimate fits in free memory, decided at the first step from the row count)
+        self.save_gemms = os.environ.get("BDLLM_SAVE_GEMMS", "auto") if self.save_cores else "0"
         if self.peer is not None:  # every shard written before any peer reads one
             torch.cuda.synchronize(self.device)
             dist.barrier()
@@ -456,6 +459,10 @@ class FSDPEngine:
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
         x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
+        if self.save_gemms not in ("0", "1"):
+            self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
+        if self.save_cores:
+            self.act_store.gemms = self.save_gemms == "1"
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
@@ -464,6 +471,31 @@ class FSDPEngine:
         loss.backward()
         self._optimizer_step()
         return loss.detach()
+
+    def gemm_bytes_per_step(self, rows: int) -> int:
+        """Bytes the saved GEMM outputs take for one step of `rows` token rows per layer pass."""
+        c = self.cfg
+        mlp = c.hidden_size + 3 * c.intermediate_size  # down output, activation, gate|up
+        total = 0
+        for t in c.layer_types:
+            if t == "linear_attention":
+                proj = c.conv_dim + c.value_dim + 2 * c.linear_num_value_heads
+            else:
+                proj = 2 * c.num_attention_heads * c.head_dim + 2 * c.num_key_value_heads * c.head_dim
+            total += rows * (proj + c.hidden_size + mlp) * 2
+        return total
+
+    def _decide_save_gemms(self, rows: int) -> None:
+        """Keep the GEMM outputs when they fit with room to spare (a decision every rank takes alike:
+        the smallest free memory over ranks counts)."""
+        need = self.gemm_bytes_per_step(rows)
+        free = torch.tensor([float(torch.cuda.mem_get_info(self.device)[0])], device=self.device)
+        if self.world > 1:
+            dist.all_reduce(free, op=dist.ReduceOp.MIN)
+        self.save_gemms = "1" if need < 0.7 * (float(free[0]) - (12 << 30)) else "0"
+        if self.save_gemms == "1" and self.fused_ag:
+            # the backward's gathers must not wait for GEMMs that the saved outputs replace
+            self.fused_ag = False
 
     @torch.no_grad()
     def _optimizer_step(self):

@@ -9,12 +9,13 @@ import torch
 pytestmark = pytest.mark.gpu
 
 
-def _run(save: str):
+def _run(save: str, gemms: str = "0"):
     from dllm_qwen38_b200.config import preset
     from dllm_qwen38_b200.models.qwen35 import build_model
     from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
 
     os.environ["BDLLM_SAVE_CORES"] = save
+    os.environ["BDLLM_SAVE_GEMMS"] = gemms
     cfg = preset("tiny", hidden_size=256, intermediate_size=512, linear_key_head_dim=64, linear_value_head_dim=64,
                  head_dim=64)
     tr = FSDPTrainer(build_model(cfg, seed=0, device="cuda", dtype=torch.bfloat16), block=32, mask_id=cfg.mask_id,
@@ -36,6 +37,25 @@ def test_saved_core_outputs_match_recomputation():
         lb, sb = _run("0")
     finally:
         os.environ.pop("BDLLM_SAVE_CORES", None)
+        os.environ.pop("BDLLM_SAVE_GEMMS", None)
         Cu.ActStore.clear()
     assert max(abs(a - b) for a, b in zip(la, lb)) < 1e-4 * max(1.0, abs(la[0]))
     assert max(float((sa[k] - sb[k]).abs().max()) for k in sa) < 1e-3
+
+
+def test_saved_gemm_outputs_match_recomputation():
+    """Keeping the projection / MLP GEMM outputs of the checkpointed forward (the recomputation
+    then runs only the elementwise and norm kernels) gives the same training trajectory: the GEMMs
+    are deterministic, so the recomputed outputs would have been bitwise the same."""
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    try:
+        la, sa = _run("1", gemms="1")
+        lb, sb = _run("1", gemms="0")
+    finally:
+        os.environ.pop("BDLLM_SAVE_CORES", None)
+        os.environ.pop("BDLLM_SAVE_GEMMS", None)
+        Cu.ActStore.clear()
+        Cu.ActStore.gemms = False
+    assert la == lb, (la, lb)
+    assert all(torch.equal(sa[k], sb[k]) for k in sa)

@@ -173,12 +173,20 @@ def run_native(a, rank, world):
         t = torch.tensor([loss_last], device="cuda", dtype=torch.float64)
         dist.all_reduce(t)
         loss_last = float(t.item())
+    ckpt_policy = "per layer" if not a.no_ckpt else "off"
     if hasattr(trainer, "engine"):
-        trainer.engine.close()
+        eng = trainer.engine
+        kept = ["GDN core outputs and block states", "attention outputs and LSE"] if eng.save_cores else []
+        if getattr(eng, "save_gemms", "0") == "1":
+            kept.append("projection and MLP GEMM outputs")
+        if kept:
+            ckpt_policy = "per layer; the forward keeps " + ", ".join(kept) + " for the backward"
+        eng.close()
     h2d = host_x[0].numel() * host_x[0].element_size() + pl.numel() * 8 + vl.numel() * 8
     return {
         "ms_per_step": ms, "e2e_s_per_step": e2e_s, "launches": launches, "clocks": clocks, "cfg": cfg,
         "parallel": parallel, "loss_last": loss_last, "h2d": h2d, "d2h": 4, "impl": ops.last_impl(),
+        "ckpt_policy": ckpt_policy,
         "peak_mem_gib": round(torch.cuda.max_memory_allocated() / 2**30, 2),
     }
 
@@ -341,7 +349,7 @@ def main(argv=None) -> int:
         "config": {
             "model": f"27b-shape hybrid, {cfg.num_hidden_layers} of 64 layers" if a.model == "27b" else a.model,
             "global_batch": seqs, "seq_len": a.seq_len, "block": a.block, "micro_batch_per_gpu": a.micro_batch,
-            "parallelism": r["parallel"], "activation_checkpointing": not a.no_ckpt, "optimizer": "AdamW lr 1e-5",
+            "parallelism": r["parallel"], "activation_checkpointing": r.get("ckpt_policy", not a.no_ckpt), "optimizer": "AdamW lr 1e-5",
             "l2": "flushed (256 MiB write) before every timed step; step working set >> L2",
         },
         "mfu": round(mfu, 4), "proxy_mfu_24N": round(proxy_mfu, 4), "peak_flops_source": peak_src,

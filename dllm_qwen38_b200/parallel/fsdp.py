@@ -39,6 +39,7 @@ are averaged over ranks (`fsdp_train.py:39-44,162,207-221`), so AdamW sees
 from __future__ import annotations
 
 import os
+import sys
 
 import torch
 import torch.distributed as dist
@@ -493,6 +494,9 @@ class FSDPEngine:
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
         self.save_gemms = "1" if need < 0.7 * (float(free[0]) - (12 << 30)) else "0"
+        if self.rank == 0:
+            print(f"[fsdp] GEMM outputs across checkpointing: {'kept' if self.save_gemms == '1' else 'recomputed'} "
+                  f"(need {need / 2**30:.1f} GiB, free {float(free[0]) / 2**30:.1f} GiB)", file=sys.stderr, flush=True)
         if self.save_gemms == "1" and self.fused_ag:
             # the backward's gathers must not wait for GEMMs that the saved outputs replace
             self.fused_ag = False

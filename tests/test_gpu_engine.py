@@ -46,8 +46,8 @@ def test_saved_core_outputs_match_recomputation():
 def test_saved_gemm_outputs_match_recomputation():
     """Keeping the projection / MLP GEMM outputs of the checkpointed forward (the recomputation
     then runs only the elementwise and norm kernels) gives the same training trajectory: the GEMMs
-    are deterministic, so the recomputed outputs would be bitwise the same (the losses are); the
-    parameters agree to the run-to-run noise of the kernels that reduce with atomics."""
+    are deterministic, so the recomputed outputs would be bitwise the same; what differs is the
+    run-to-run noise of the kernels that reduce with atomics (clip norm, GDN row sums)."""
     from dllm_qwen38_b200.ops import cuda as Cu
 
     try:
@@ -58,5 +58,6 @@ def test_saved_gemm_outputs_match_recomputation():
         os.environ.pop("BDLLM_SAVE_GEMMS", None)
         Cu.ActStore.clear()
         Cu.ActStore.gemms = False
-    assert la == lb, (la, lb)
+    assert la[0] == lb[0], (la, lb)  # the first step's loss precedes any update
+    assert max(abs(a - b) for a, b in zip(la, lb)) < 1e-5 * max(1.0, abs(la[0]))
     assert max(float((sa[k] - sb[k]).abs().max()) for k in sa) < 1e-3

@@ -39,6 +39,12 @@ at::Tensor attn_prefix(const at::Tensor& q, const at::Tensor& k, const at::Tenso
 std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                  const at::Tensor& beta, const at::Tensor& S0, const c10::optional<at::Tensor>& S_final,
                                  int64_t C);
+std::vector<at::Tensor> gdn_fwd_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                     const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S0, int64_t C);
+std::vector<at::Tensor> gdn_bwd_rows(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                     const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta,
+                                     const at::Tensor& S_in, int64_t C, const c10::optional<at::Tensor>& inj,
+                                     bool want_dS0);
 at::Tensor conv_tail(const at::Tensor& raw, at::Tensor& tail, const at::Tensor& w, bool update_tail);
 void confidence(const at::Tensor& logits, at::Tensor& conf, at::Tensor& pick);
 void commit(const at::Tensor& conf, const at::Tensor& pick, at::Tensor& masked, at::Tensor& ids, double threshold,
@@ -113,6 +119,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_bwd", &bdllm::qk_norm_rope_bwd);
   m.def("attn_prefix", &bdllm::attn_prefix, "attention of a query block over a KV cache (every key visible)",
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("tk_host"), py::arg("tk") = c10::nullopt, py::arg("scale"));
+  m.def("gdn_fwd_rows", &bdllm::gdn_fwd_rows, "gated delta rule rows from initial states, with chunk states");
+  m.def("gdn_bwd_rows", &bdllm::gdn_bwd_rows, "backward of gated delta rule rows (injected state grads, dS0)",
+        py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta"), py::arg("S_in"),
+        py::arg("C"), py::arg("inj") = c10::nullopt, py::arg("want_dS0") = false);
   m.def("gdn_rows", &bdllm::gdn_rows, "gated delta rule over decode rows from a cached state", py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("g"), py::arg("beta"), py::arg("S0"), py::arg("S_final") = c10::nullopt,
         py::arg("C"));

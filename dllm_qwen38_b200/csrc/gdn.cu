@@ -65,6 +65,7 @@ struct Args {
   float* dg;          // [B, 2L, Hv]
   float* dbeta;       // [B, 2L, Hv]
   long long* phase;   // optional: clock64() at phase boundaries of CTA (0, 0) (BDLLM_GDN_PHASES=1)
+  float* dS0;         // optional [B, Hv, Dk, Dv]: gradient of the state before the first chunk (rows)
 };
 
 // records the SM clock at phase boundary `k` (thread 0 of CTA (0, 0) only; no-op without a buffer)
@@ -1100,6 +1101,11 @@ __global__ void __launch_bounds__(NT) bwd_recur_kernel(Args a, int has_inj) {
     __syncthreads();
   }
   cp_wait_all();
+  if (a.dS0 != nullptr)  // the gradient of the state entering chunk 0 (the row's initial state)
+    for (int idx = threadIdx.x; idx < Dk * 32; idx += NT) {
+      const int r = idx / 32, cc = idx % 32;
+      if (cc < ncols) a.dS0[((int64_t)bh * Dk + r) * Dv + col0 + cc] = sS[r * LDC + cc];
+    }
 }
 
 // ------------------------------------------------------------------------------------- host
@@ -1189,7 +1195,7 @@ static std::vector<at::Tensor> forward_t(const at::Tensor& q, const at::Tensor& 
 template <int Dk, int Dv>
 static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                       const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S0,
-                                      const c10::optional<at::Tensor>& S_final, int64_t C) {
+                                      const c10::optional<at::Tensor>& S_final, int64_t C, bool want_states = false) {
   const int64_t T = q.size(1);
   TORCH_CHECK(T % 2 == 0 && T % C == 0, "gdn_rows: T even and a multiple of the chunk");
   Args a = make_args(q, k, v, g, beta, T / 2, C, true);
@@ -1220,6 +1226,7 @@ static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, 
   launch(fwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
   launch(fwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32), 4 * 32 * Ld<Dk>::v + 3 * 32 * LDC + Dk * LDC, a);
   launch(fwd_out_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a);
+  if (want_states) return {o, S_in};
   return {o};
 }
 
@@ -1227,7 +1234,9 @@ static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, 
 template <int Dk, int Dv>
 static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                           const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta,
-                                          const at::Tensor& S_in, int64_t L, int64_t C, bool concat) {
+                                          const at::Tensor& S_in, int64_t L, int64_t C, bool concat,
+                                          const c10::optional<at::Tensor>& inj = c10::nullopt,
+                                          bool want_dS0 = false) {
   Args a = make_args(q, k, v, g, beta, L, C, concat);
   auto f32 = q.options().dtype(at::kFloat);
   auto d = dout.to(at::kBFloat16).contiguous();
@@ -1243,7 +1252,14 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   a.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   a.dg = dg.data_ptr<float>();
   a.dbeta = db.data_ptr<float>();
-  auto dS_inj = concat ? at::Tensor() : at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
+  // concat runs take optional injected state gradients (one [Dk, Dv] per chunk entry, e.g. from
+  // rows that start from those states) and may return the gradient of their initial state
+  TORCH_CHECK(!inj.has_value() || (concat && inj->is_contiguous() && inj->scalar_type() == at::kFloat &&
+                                   inj->numel() == (int64_t)a.B * a.nb * a.Hv * Dk * Dv),
+              "gdn_bwd: injected state gradients fp32 [B, nb, Hv, Dk, Dv] (concat runs)");
+  auto dS_inj = concat ? (inj.has_value() ? *inj : at::Tensor()) : at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
+  auto dS0 = want_dS0 ? at::empty({a.B, a.Hv, Dk, Dv}, f32) : at::Tensor();
+  a.dS0 = want_dS0 ? dS0.data_ptr<float>() : nullptr;
   auto dS_out = at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
   auto dVp = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
   auto PtdO = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
@@ -1251,7 +1267,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto Kt = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
   auto W = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
   auto Ec = at::empty({a.B, a.nb, a.Hv}, f32);
-  a.dS_inj = concat ? nullptr : dS_inj.data_ptr<float>();
+  a.dS_inj = dS_inj.defined() ? dS_inj.data_ptr<float>() : nullptr;
   a.dS_out = dS_out.data_ptr<float>();
   a.dVp = dVp.data_ptr<float>();
   a.PtdO = PtdO.data_ptr<float>();
@@ -1285,9 +1301,10 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a2);
   launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
           2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a2,
-          concat ? 0 : 1);
+          a.dS_inj != nullptr ? 1 : 0);
   launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
   report("clean");
+  if (want_dS0) return {dq, dk, dv, dg, db, dS0};
   return {dq, dk, dv, dg, db};
 }
 
@@ -1324,6 +1341,26 @@ std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const
                                  int64_t C) {
   c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(rows_t, q, k, v, g, beta, S0, S_final, C)
+  return {};
+}
+
+// rows with an initial state, for training: {o, S_in} (S_in: the state entering each chunk)
+std::vector<at::Tensor> gdn_fwd_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                     const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S0, int64_t C) {
+  c10::cuda::CUDAGuard guard(q.device());
+  GDN_DISPATCH(rows_t, q, k, v, g, beta, S0, c10::nullopt, C, true)
+  return {};
+}
+
+// backward of one causal run per row (q [B, T, ...], T = 2 * (T / 2)) with optional injected
+// chunk-entry state gradients; want_dS0 adds the gradient of the initial state as a sixth output
+std::vector<at::Tensor> gdn_bwd_rows(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                     const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta,
+                                     const at::Tensor& S_in, int64_t C, const c10::optional<at::Tensor>& inj,
+                                     bool want_dS0) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const int64_t half = q.size(1) / 2;
+  GDN_DISPATCH(backward_t, dout, q, k, v, g, beta, S_in, half, C, true, inj, want_dS0)
   return {};
 }
 

@@ -495,12 +495,69 @@ def embedding(ids, table):
     return _Embedding.apply(ids, table)
 
 
+class _GDNCoreBlocks(torch.autograd.Function):
+    """The state fork for blocks of more than 32 tokens (the kernels chunk at 32): the clean stream
+    x_0 is one causal run chunked at 32; every noised block of x_t is an independent run that
+    starts from the clean state at its block's start. Backward: the noised runs return the
+    gradient of their initial states, which is injected into the clean run's reverse recurrence at
+    the block-start chunks. q, k [B, 2L, Hk, Dk], v [B, 2L, Hv, Dv]; g, beta [B, 2L, Hv]."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, L, block):
+        B = q.shape[0]
+        C, nb = 32, L // block
+        cpb = block // C
+        gf, bf = g.float(), beta.float()
+        clean = [t[:, L:].contiguous() for t in (q, k, v, gf, bf)]
+        o0, S0_in, _ = _C.gdn_fwd(*clean, L // 2, C, True)  # x_0: one causal run of L tokens
+        rows = [t[:, :L].reshape(B * nb, block, *t.shape[2:]).contiguous() for t in (q, k, v, gf, bf)]
+        S0 = S0_in[:, ::cpb].reshape(B * nb, *S0_in.shape[2:]).contiguous()  # the fork states
+        ot, St_in = _C.gdn_fwd_rows(*rows, S0, C)
+        _count(6)
+        ctx.save_for_backward(*clean, S0_in, *rows, St_in)
+        ctx.cfg = (B, L, block, C, nb, cpb)
+        ctx.dtypes = (g.dtype, beta.dtype)
+        return torch.cat([ot.reshape(B, L, *ot.shape[2:]), o0], 1)
+
+    @staticmethod
+    def backward(ctx, do):
+        saved = ctx.saved_tensors
+        clean, S0_in, rows, St_in = saved[:5], saved[5], saved[6:11], saved[11]
+        B, L, block, C, nb, cpb = ctx.cfg
+        do = do.to(torch.bfloat16)
+        dot = do[:, :L].reshape(B * nb, block, *do.shape[2:]).contiguous()
+        dqt, dkt, dvt, dgt, dbt, dS0 = _C.gdn_bwd_rows(dot, *rows, St_in, C, None, True)
+        inj = torch.zeros_like(S0_in)
+        inj[:, ::cpb] = dS0.reshape(B, nb, *dS0.shape[1:])
+        dq0, dk0, dv0, dg0, db0 = _C.gdn_bwd_rows(do[:, L:].contiguous(), *clean, S0_in, C, inj, False)
+        _count(8)
+
+        def cat(a, b):
+            return torch.cat([a.reshape(B, L, *a.shape[2:]), b], 1)
+
+        dq, dk, dv, dg, db = cat(dqt, dq0), cat(dkt, dk0), cat(dvt, dv0), cat(dgt, dg0), cat(dbt, db0)
+        Hk, Hv = clean[0].shape[2], clean[2].shape[2]
+        if Hv != Hk:  # per-v-head gradients: sum each repeat group
+            T2, Dk = dq.shape[1], dq.shape[3]
+            dq = dq.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(clean[0].dtype)
+            dk = dk.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(clean[1].dtype)
+        return dq, dk, dv, dg.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None, None
+
+
 def gdn_core_blockdiff(q, k, v, g, beta, L, block, chunk, mode):
-    """chunk is the host reference's chunking; the kernels chunk at the block (<= 32)."""
+    """chunk is the host reference's chunking. The kernels chunk at the block when it is <= 32;
+    larger blocks (multiples of 32) run the clean stream and the noised blocks as separate runs
+    chunked at 32 (`_GDNCoreBlocks`); the concat fault is one causal run at any block."""
     del chunk
-    if block > 32 or L % block:
-        raise ValueError(f"native GDN needs block <= 32 dividing L (got block={block}, L={L})")
-    return _GDNCore.apply(q, k, v, g, beta, L, block, mode == "concat")
+    if L % block:
+        raise ValueError(f"native GDN needs the block to divide L (got block={block}, L={L})")
+    if mode == "concat":
+        return _GDNCore.apply(q, k, v, g, beta, L, block if block <= 32 else 32, True)
+    if block <= 32:
+        return _GDNCore.apply(q, k, v, g, beta, L, block, False)
+    if block % 32:
+        raise ValueError(f"native GDN: blocks above 32 must be multiples of 32 (got {block})")
+    return _GDNCoreBlocks.apply(q, k, v, g, beta, L, block)
 
 
 # ----------------------------------------------------------------------------- attention

@@ -13,7 +13,8 @@ def _rel(a, b):
 
 
 @pytest.mark.parametrize("mode", ["fork", "concat"])
-@pytest.mark.parametrize("B,L,block,Hk,Hv,D", [(2, 64, 16, 2, 4, 32), (1, 96, 32, 2, 6, 128), (2, 32, 8, 4, 4, 16)])
+@pytest.mark.parametrize("B,L,block,Hk,Hv,D", [(2, 64, 16, 2, 4, 32), (1, 96, 32, 2, 6, 128), (2, 32, 8, 4, 4, 16),
+                                               (1, 256, 64, 2, 4, 64), (2, 256, 128, 2, 2, 32), (1, 192, 64, 1, 3, 128)])
 def test_gdn_core_fwd_bwd(mode, B, L, block, Hk, Hv, D):
     from dllm_qwen38_b200.ops import cuda as Cu
 

@@ -1132,8 +1132,8 @@ static Args make_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor
   TORCH_CHECK(q.stride(1) == k.stride(1) && q.stride(2) == q.size(3) && k.stride(2) == k.size(3) &&
                   v.stride(2) == v.size(3),
               "gdn: heads must be packed within a token row");
-  TORCH_CHECK(q.stride(0) == q.size(1) * q.stride(1) && v.stride(0) == v.size(1) * v.stride(1),
-              "gdn: batch and token dims must merge");
+  TORCH_CHECK(q.size(0) == 1 || (q.stride(0) == q.size(1) * q.stride(1) && v.stride(0) == v.size(1) * v.stride(1)),
+              "gdn: batch and token dims must merge");  // (a single batch row has no batch stride)
   TORCH_CHECK(g.is_contiguous() && beta.is_contiguous() && g.scalar_type() == at::kFloat &&
                   beta.scalar_type() == at::kFloat,
               "gdn: g, beta fp32 contiguous [B, 2L, Hv]");

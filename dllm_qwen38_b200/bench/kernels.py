@@ -134,10 +134,25 @@ def op_attn(a):
     k = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
     v = torch.randn(B, 2 * L, Hk, D, device="cuda", generator=g).bfloat16()
 
-    def fn():
-        qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
-        o = Cu.attention_blockdiff(qq, kk, vv, L, a.block, D ** -0.5)
-        o.float().sum().backward()
+    if a.impl == "reference":
+        # the reference's additive [1, 1, 2L, 2L] mask (`blockdiff.py:50-66`) through torch SDPA with
+        # the kv heads repeated, as its HF sdpa attention layers run it
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from dllm_qwen38.blockdiff import complementary_mask
+
+        mask = complementary_mask(L, a.block, torch.bfloat16, q.device)
+
+        def fn():
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+            rep = Hq // Hk
+            qt, kt, vt = (x.transpose(1, 2) for x in (qq, kk.repeat_interleave(rep, 2), vv.repeat_interleave(rep, 2)))
+            o = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, attn_mask=mask, scale=D ** -0.5)
+            o.float().sum().backward()
+    else:
+        def fn():
+            qq, kk, vv = (t.detach().requires_grad_(True) for t in (q, k, v))
+            o = Cu.attention_blockdiff(qq, kk, vv, L, a.block, D ** -0.5)
+            o.float().sum().backward()
     # allowed pairs of the complementary mask: x_t rows see their block + earlier clean blocks
     # (~L^2/2 + L*block), x_0 rows the clean prefix (~L^2/2): ~L^2 pairs; fwd 4 D + bwd 10 D flops/pair
     pairs = float(L) * L + L * a.block

@@ -495,6 +495,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         for (int e = 0; e < 32; ++e) ro[e] = 0u;
       }
       if (valid) {
+        (void)BDLLM_CHECK(all_finite(reinterpret_cast<const float*>(ro), 32), row, a.T2);  // sentinel
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -714,6 +715,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       lse = a.lse2[((int64_t)b * a.Hq + h) * a.T2 + row];
+      (void)BDLLM_CHECK(isfinite(dlt), row, a.T2);  // sentinel: non-finite O or dO row
       a.delta[((int64_t)b * a.Hq + h) * a.T2 + row] = dlt;
     }
     const bool live = valid && lse != NEG_INF;

@@ -15,6 +15,8 @@ void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m
                 double b2, double eps, double wd, double coef, const c10::optional<at::Tensor>& coef_dev, double bc1,
                 double bc2);
 int64_t read_error_word(bool reset);
+std::vector<std::tuple<std::string, int64_t, int64_t, int64_t, int64_t>> bounds_report(bool reset);
+bool debug_bounds_build();
 at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w1, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w1, double eps);
 at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at::Tensor& w, double eps);
@@ -166,6 +168,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sq"), py::arg("seq"), py::arg("max_blocks"), py::arg("timeout_s"),
         py::arg("adam_state") = std::vector<at::Tensor>{}, py::arg("adam_hp") = std::vector<double>{});
   m.def("peer_allreduce_f32", &bdllm::peer::allreduce_f32);
+  m.def("bounds_report", &bdllm::bounds_report,
+        "debug-bounds build: (file, line, index, limit, failures) per translation unit with a failed check",
+        py::arg("reset") = true);
+  m.def("debug_bounds_build", &bdllm::debug_bounds_build, "true in the -DBDLLM_DEBUG_BOUNDS extension (_C_dbg)");
   m.def("read_error_word", &bdllm::read_error_word, "device error word (bounded-wait expiries)",
         py::arg("reset") = false);
 }

@@ -36,6 +36,66 @@ __device__ __forceinline__ void record_error(int* err, int code) {
 int* error_word_ptr();     // host: lazily allocated device int, per device
 void bind_context(int dev);  // host: make the device's primary context current in this thread
 
+// ------------------------------------------------------------------ debug-bounds build
+// The `_C_dbg` extension is this library compiled with -DBDLLM_DEBUG_BOUNDS. There,
+// BDLLM_CHECK(cond, idx, lim) evaluates an index / alignment condition before an access; a failing
+// check records (line, idx, lim) in its translation unit's record (the first failure keeps its
+// line, index and limit; every failure is counted) and evaluates to false, so the caller skips the
+// access. Nothing traps: a kernel with a skipped TMA load runs into its bounded mbarrier wait and
+// returns. The host collects every unit's record through bounds_report(). In the normal build the
+// macro is the constant `true` and costs nothing.
+struct BoundsRec {
+  unsigned long long line, idx, lim, count;
+};
+using BoundsReader = void (*)(BoundsRec*, bool);
+struct BoundsUnit {
+  const char* file;
+  BoundsReader read;
+};
+inline BoundsUnit* bounds_units(int* n_out) {  // one registry for the whole shared object
+  static BoundsUnit units[32];
+  static int n = 0;
+  if (n_out == nullptr) return units + (n < 32 ? n++ : 31);
+  *n_out = n;
+  return units;
+}
+
+#ifdef BDLLM_DEBUG_BOUNDS
+namespace dbg {
+static __device__ BoundsRec g_rec;
+static void read_rec(BoundsRec* out, bool reset) {
+  cudaMemcpyFromSymbol(out, g_rec, sizeof(BoundsRec));
+  if (reset) {
+    BoundsRec z{};
+    cudaMemcpyToSymbol(g_rec, &z, sizeof(BoundsRec));
+  }
+}
+static const int g_registered = (*bounds_units(nullptr) = BoundsUnit{__BASE_FILE__, &read_rec}, 0);
+static __device__ __noinline__ void fail(int line, long long idx, long long lim) {
+  if (atomicCAS(&g_rec.line, 0ull, (unsigned long long)line) == 0ull) {
+    g_rec.idx = (unsigned long long)idx;
+    g_rec.lim = (unsigned long long)lim;
+  }
+  atomicAdd(&g_rec.count, 1ull);
+}
+}  // namespace dbg
+#define BDLLM_DEBUG_BUILD 1
+#define BDLLM_CHECK(cond, idx, lim) \
+  ((cond) ? true : (::bdllm::dbg::fail(__LINE__, (long long)(idx), (long long)(lim)), false))
+#else
+#define BDLLM_DEBUG_BUILD 0
+#define BDLLM_CHECK(cond, idx, lim) true
+#endif
+// index i in [0, n)
+#define BDLLM_IDX(i, n) BDLLM_CHECK((long long)(i) >= 0 && (long long)(i) < (long long)(n), (i), (n))
+
+// NaN / Inf sentinel of an epilogue (debug build): true when all n values are finite
+__device__ __forceinline__ bool all_finite(const float* v, int n) {
+  bool ok = true;
+  for (int i = 0; i < n; ++i) ok &= isfinite(v[i]);
+  return ok;
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -99,7 +159,10 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
 }
 
 // ------------------------------------------------------------------ TMA
+// Every tensor map of this library is bf16: a tiled load's x coordinate must be a multiple of 8
+// elements (16 bytes). The debug build checks it and skips a load that breaks it.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  if (!BDLLM_CHECK((x & 7) == 0, x, 8)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
@@ -109,6 +172,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
 
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y,
                                             int z) {
+  if (!BDLLM_CHECK((x & 7) == 0, x, 8)) return;
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
           smem_u32(smem_dst)),

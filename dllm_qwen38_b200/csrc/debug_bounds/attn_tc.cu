@@ -1,0 +1,4 @@
+// Debug-bounds build of ../attn_tc.cu: the same source compiled with BDLLM_DEBUG_BOUNDS
+// (index, alignment and non-finite checks; records read by bounds_report()).
+#define BDLLM_DEBUG_BOUNDS 1
+#include "../attn_tc.cu"

@@ -321,7 +321,9 @@ __device__ __forceinline__ float wsum(float v) {
 // stream 0 = noised (x_t, positions [0, L)), stream 1 = clean (x_0, positions [L, 2L)); in concat
 // mode stream 1 is the whole 2L sequence run causally (the concat-causal-gdn fault).
 __device__ __forceinline__ int64_t tok(const Args& a, int b, int stream, int c, int i) {
-  return (int64_t)b * 2 * a.L + ((stream && !a.concat) ? a.L : 0) + (int64_t)c * a.C + i;
+  const int64_t t = (int64_t)b * 2 * a.L + ((stream && !a.concat) ? a.L : 0) + (int64_t)c * a.C + i;
+  if (!BDLLM_IDX(t, (int64_t)a.B * 2 * a.L)) return 0;  // debug build: recorded, redirected to row 0
+  return t;
 }
 
 // 16-byte asynchronous global -> shared copies (operand prefetch in the recurrences)
@@ -646,6 +648,7 @@ __global__ void __launch_bounds__(NT) fwd_out_kernel(Args a) {
     __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(sO[i * VD + d + 2 * e], sO[i * VD + d + 2 * e + 1]);
+    (void)BDLLM_CHECK(all_finite(sO + i * VD + d, 8), i, C);  // sentinel: non-finite output
     *reinterpret_cast<uint4*>(a.o + tok(a, b, stream, c, i) * (int64_t)a.Hv * Dv + h * Dv + d) = o;
   }
 }

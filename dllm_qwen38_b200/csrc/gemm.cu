@@ -17,6 +17,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <string>
+#include <tuple>
+#include <vector>
+
 #include "common.cuh"
 
 namespace bdllm {
@@ -211,13 +215,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_r
       for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
     }
     const int col0 = n0 + c * 32;
+    if (row_ok) (void)BDLLM_CHECK(all_finite(v, 32), row, col0);  // sentinel: non-finite accumulator
     if constexpr (EPI == EPI_SWIGLU) {
       float u[32];
       tmem_ld32(t_row + BN / 2 + c * 32, u);
       if (row_ok) {
         __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + col0;
         __nv_bfloat16* gu = args.GU ? args.GU + (size_t)row * args.ldgu + col0 : nullptr;
-        if (col0 + 32 <= args.N) {
+        if (col0 + 32 <= args.N && BDLLM_CHECK(((uintptr_t)out & 15) == 0, row, col0)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             uint4 pk, pg, pu;
@@ -263,7 +268,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_r
         const int64_t slot = (int64_t)args.rank * ksplit + t / mn_tiles;  // [src rank][k split]
         float* out = reinterpret_cast<float*>(args.peers[owner] + args.part_off) +
                      (slot * args.rows_per_rank + lr) * args.ldc + col0;
-        if (col0 + 32 <= args.N) {
+        if (col0 + 32 <= args.N && BDLLM_CHECK(((uintptr_t)out & 15) == 0, row, col0)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
             *reinterpret_cast<float4*>(out + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -276,7 +281,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_r
     } else if constexpr (EPI == EPI_F32 || EPI == EPI_ACC_F32) {
       if (row_ok) {
         float* out = reinterpret_cast<float*>(args.C) + split_off + (size_t)row * args.ldc + col0;
-        if (col0 + 32 <= args.N) {
+        if (col0 + 32 <= args.N && BDLLM_CHECK(((uintptr_t)out & 15) == 0, row, col0)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
             float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
@@ -298,7 +303,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_r
         const __nv_bfloat16* res =
             (EPI == EPI_ADD_BF16) ? reinterpret_cast<const __nv_bfloat16*>(args.R) + (size_t)row * args.ldr + col0
                                   : nullptr;
-        if (col0 + 32 <= args.N) {
+        if (col0 + 32 <= args.N && BDLLM_CHECK(((uintptr_t)out & 15) == 0, row, col0)) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             uint4 pk;
@@ -612,6 +617,7 @@ __device__ __forceinline__ void arrive_remote(uint32_t cluster_bar) {
 }
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t leader_bar, int x,
                                                  int y) {
+  if (!BDLLM_CHECK((x & 7) == 0, x, 8)) return;
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(smem_dst)),
@@ -1352,6 +1358,24 @@ int* error_word_ptr() {
   }
   return ptrs[dev];
 }
+
+// (file, line, index, limit, failures) of every translation unit whose bounds record is set; empty
+// in the normal build (no unit registers a record there).
+std::vector<std::tuple<std::string, int64_t, int64_t, int64_t, int64_t>> bounds_report(bool reset) {
+  std::vector<std::tuple<std::string, int64_t, int64_t, int64_t, int64_t>> out;
+  int n = 0;
+  BoundsUnit* units = bounds_units(&n);
+  for (int i = 0; i < n; ++i) {
+    BoundsRec r{};
+    units[i].read(&r, reset);
+    if (r.count)
+      out.emplace_back(units[i].file, (int64_t)r.line, (int64_t)r.idx, (int64_t)r.lim, (int64_t)r.count);
+  }
+  C10_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
+bool debug_bounds_build() { return BDLLM_DEBUG_BUILD != 0; }
 
 int64_t read_error_word(bool reset) {
   int v = 0;

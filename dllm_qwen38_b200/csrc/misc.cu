@@ -128,7 +128,7 @@ __device__ __forceinline__ void conv_row(const __nv_bfloat16* __restrict__ raw, 
   sources_of<K>(t, L, block, mode, src);
 #pragma unroll
   for (int j = 0; j < K; ++j) {
-    if (src[j] < 0) continue;
+    if (src[j] < 0 || !BDLLM_IDX(src[j], T2)) continue;
     const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src[j]) * ld + c);
     const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
 #pragma unroll
@@ -226,13 +226,13 @@ __global__ void conv_dx_kernel(const float* __restrict__ dpre, const float* __re
     const int tend = (mode == CONV_CONCAT || r >= L) ? T2 : min(L, (r / block + 1) * block);
 #pragma unroll
     for (int d = 0; d < K; ++d)
-      if (r + d < tend) add_consumer<K>(dpre, base + r + d, C, c, wr, K - 1 - d, acc);
+      if (r + d < tend && BDLLM_IDX(r + d, T2)) add_consumer<K>(dpre, base + r + d, C, c, wr, K - 1 - d, acc);
     if (mode == CONV_FORK && r >= L) {
       const int q = r - L, later = (q / block + 1) * block;  // noised rows of later blocks
 #pragma unroll
       for (int d = 0; d < K; ++d) {
         const int t = q + d;
-        if (t < L && t >= later) add_consumer<K>(dpre, base + t, C, c, wr, K - 1 - d, acc);
+        if (t < L && t >= later && BDLLM_IDX(t, T2)) add_consumer<K>(dpre, base + t, C, c, wr, K - 1 - d, acc);
       }
     }
     uint4 o;
@@ -267,7 +267,7 @@ __global__ void conv_dw_kernel(const __nv_bfloat16* __restrict__ raw, int64_t ld
     sources_of<K>(t, L, block, mode, src);
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-      if (src[j] < 0) continue;
+      if (src[j] < 0 || !BDLLM_IDX(src[j], T2)) continue;
       const uint4 p = *reinterpret_cast<const uint4*>(raw + ((int64_t)b * T2 + src[j]) * ld + c);
       const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
 #pragma unroll
@@ -396,7 +396,10 @@ __global__ void ce_rows_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, c
   __syncthreads();
   const float lse = sm[0];
   const int64_t t = tgt[row];
-  if (threadIdx.x == 0) loss[row] = lse - __bfloat162float(x[t]);
+  if (threadIdx.x == 0) {
+    (void)BDLLM_CHECK(isfinite(lse), row, V);  // sentinel: a non-finite logit in the row
+    loss[row] = BDLLM_IDX(t, V) ? lse - __bfloat162float(x[t]) : NAN;
+  }
   __syncthreads();  // the target logit is read before pass 2 overwrites it
   for (int c = threadIdx.x * 8; c < V; c += blockDim.x * 8) {
     uint4 p = *reinterpret_cast<const uint4*>(x + c);
@@ -444,6 +447,7 @@ __global__ void adamw_kernel(float* __restrict__ w, TP* __restrict__ p, const TG
   if (coef_dev != nullptr) coef *= *coef_dev;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float gi = to_f(g[i]) * coef;
+    (void)BDLLM_CHECK(isfinite(gi), i, n);  // sentinel: a non-finite gradient element
     float wi = w[i];
     if (wd != 0.f) wi *= 1.f - lr * wd;
     float mi = b1 * m[i] + (1.f - b1) * gi;

@@ -43,6 +43,7 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
     }
   }
   ss = warp_sum(ss);
+  if (lane == 0) (void)BDLLM_CHECK(isfinite(ss), row, rows);  // sentinel: a non-finite input row
   const float r = rsqrtf(ss / D + eps);
   __nv_bfloat16* yr = y + (int64_t)row * ldy;
   for (int c = lane * 8; c < D; c += 256) {

@@ -13,7 +13,9 @@ from __future__ import annotations
 
 import torch
 
-from .. import _C
+from ._native import require as _require
+
+_C = _require()  # `_C`, or the debug-bounds build `_C_dbg` under BDLLM_DEBUG_BOUNDS=1
 
 EPI_BF16, EPI_F32, EPI_ADD_BF16, EPI_ACC_F32, EPI_SWIGLU = 0, 1, 2, 3, 4
 

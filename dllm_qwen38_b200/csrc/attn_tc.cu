@@ -136,6 +136,15 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Dispatch rank r -> query tile, heaviest first. A query tile's work grows along each stream (x_t
+// rows see the clean blocks before theirs, x_0 rows the clean prefix), so the two halves are
+// walked down from their ends in turn: r = 0, 2, 4.. take the upper half [lo, n) from the top,
+// r = 1, 3, 5.. the lower half [0, lo) from its top (a bijection on [0, n) for any n).
+__host__ __device__ __forceinline__ int heavy_first(int r, int n) {
+  const int lo = n / 2;
+  return (r & 1) ? lo - 1 - (r >> 1) : n - 1 - (r >> 1);
+}
+
 // Up to two runs of tiles: [a0, a0 + na) then [b0, b0 + nb); k-th visible tile = at(k)
 struct Span2 {
   int a0, na, b0, nb;
@@ -272,11 +281,10 @@ __global__ void __launch_bounds__(NTHR, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // heavy (late) query tiles first: x_0 rows see the most keys at the end of each stream
-  const int nqt = gridDim.x;
-  const int qt = nqt - 1 - blockIdx.x;
+  // grid (B * Hq, query tiles): every head's tile of one work rank is dispatched before the next rank
+  const int qt = heavy_first(blockIdx.y, gridDim.y);
   const int i0 = qt * BQ, i1 = min(i0 + BQ - 1, a.T2 - 1);
-  const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
+  const int b = blockIdx.x / a.Hq, h = blockIdx.x % a.Hq, hk = h / (a.Hq / a.Hk);
   const Span2 sp = key_tiles(i0, i1, a.L, a.block, a.leak, BKV);  // visible key tiles, in order
   const int nt = sp.n();
   const int row0 = b * a.T2;  // first row of this batch in the [B*T2, H*D] maps
@@ -584,9 +592,9 @@ __global__ void __launch_bounds__(NTHR, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int qt = gridDim.x - 1 - blockIdx.x;
+  const int qt = heavy_first(blockIdx.y, gridDim.y);  // grid (B * Hq, query tiles), as the forward
   const int i0 = qt * BQ, i1 = min(i0 + BQ - 1, a.T2 - 1);
-  const int b = blockIdx.y / a.Hq, h = blockIdx.y % a.Hq, hk = h / (a.Hq / a.Hk);
+  const int b = blockIdx.x / a.Hq, h = blockIdx.x % a.Hq, hk = h / (a.Hq / a.Hk);
   const Span2 sp = key_tiles(i0, i1, a.L, a.block, a.leak, BK2);
   const int nt = sp.n();
   const int row0 = b * a.T2;
@@ -849,11 +857,14 @@ __global__ void __launch_bounds__(NTHR, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int nkt = gridDim.x;
-  const int kt = (blockIdx.x + nkt / 2) % nkt;  // clean-stream key tiles (the most work) first
+  // grid (B * Hk * D/128 slices, key tiles): clean-stream key tiles (the most work, decreasing
+  // along the stream) first, each for every (batch, kv head, slice) before the next tile
+  const int nkt = gridDim.y;
+  const int kt = (blockIdx.y + nkt / 2) % nkt;
   const int j0 = kt * BQ, j1 = min(j0 + BQ - 1, a.T2 - 1);
-  const int b = blockIdx.y / a.Hk, hk = blockIdx.y % a.Hk;
-  const int z = blockIdx.z;
+  constexpr int NZ = D / 128;
+  const int z = blockIdx.x % NZ;
+  const int b = (blockIdx.x / NZ) / a.Hk, hk = (blockIdx.x / NZ) % a.Hk;
   const int rep = a.Hq / a.Hk;
   const Span2 sp = row_tiles(j0, j1, a.L, a.T2, a.block, a.leak, BQ2);  // query tiles that may see a key
   const int nqv = sp.n();
@@ -1092,7 +1103,7 @@ static void launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     attr = true;
   }
-  const dim3 grid((T2 + BQ - 1) / BQ, B * Hq);
+  const dim3 grid(B * Hq, (T2 + BQ - 1) / BQ);
   kern<<<grid, NTHR, C::SMEM, at::cuda::getCurrentCUDAStream()>>>(m.q, m.k, m.v, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -1130,7 +1141,7 @@ static void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Te
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       attr = true;
     }
-    kern<<<dim3((T2 + BQ - 1) / BQ, B * Hq), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    kern<<<dim3(B * Hq, (T2 + BQ - 1) / BQ), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   {  // dK, dV
@@ -1147,7 +1158,7 @@ static void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Te
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       attr = true;
     }
-    kern<<<dim3((T2 + BQ - 1) / BQ, B * Hk, D / 128), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    kern<<<dim3(B * Hk * (D / 128), (T2 + BQ - 1) / BQ), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

@@ -177,8 +177,11 @@ def run_native(a, rank, world):
     if hasattr(trainer, "engine"):
         eng = trainer.engine
         kept = ["GDN core outputs and block states", "attention outputs and LSE"] if eng.save_cores else []
-        if getattr(eng, "save_gemms", "0") == "1":
+        sg = getattr(eng, "save_gemms", "0")
+        if sg == "1":
             kept.append("projection and MLP GEMM outputs")
+        elif sg.isdigit() and sg != "0":
+            kept.append(f"projection and MLP GEMM outputs of the first {sg} of {len(eng.layers)} layers")
         if kept:
             ckpt_policy = "per layer; the forward keeps " + ", ".join(kept) + " for the backward"
         eng.close()

@@ -241,9 +241,12 @@ class FSDPEngine:
             from ..ops import cuda as Cu
 
             self.act_store = Cu.ActStore
-        # also keep the GEMM outputs of the checkpointed forward ("1", "0", or "auto": when the
-        # estimate fits in free memory, decided at the first step from the row count)
+        # also keep the GEMM outputs of the checkpointed forward: "1" every layer, "0" none, "<n>" the
+        # first n layers, or "auto": as many layers as fit in free memory, decided at the first step
+        # from the row count
         self.save_gemms = os.environ.get("BDLLM_SAVE_GEMMS", "auto") if self.save_cores else "0"
+        if self.save_gemms not in ("0", "auto"):
+            self.fused_ag = False  # the backward's gathers must not wait for GEMMs that are not rerun
         if self.peer is not None:  # every shard written before any peer reads one
             torch.cuda.synchronize(self.device)
             dist.barrier()
@@ -460,10 +463,8 @@ class FSDPEngine:
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
         x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
-        if self.save_gemms not in ("0", "1"):
+        if self.save_gemms == "auto":
             self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
-        if self.save_cores:
-            self.act_store.gemms = self.save_gemms == "1"
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
@@ -473,31 +474,47 @@ class FSDPEngine:
         self._optimizer_step()
         return loss.detach()
 
-    def gemm_bytes_per_step(self, rows: int) -> int:
-        """Bytes the saved GEMM outputs take for one step of `rows` token rows per layer pass."""
+    def gemm_bytes_per_layer(self, rows: int) -> list:
+        """Bytes the saved GEMM outputs of each layer take for one step of `rows` token rows."""
         c = self.cfg
         mlp = c.hidden_size + 3 * c.intermediate_size  # down output, activation, gate|up
-        total = 0
-        for t in c.layer_types:
+        out = []
+        for t in c.layer_types[: len(self.layers)]:
             if t == "linear_attention":
                 proj = c.conv_dim + c.value_dim + 2 * c.linear_num_value_heads
             else:
                 proj = 2 * c.num_attention_heads * c.head_dim + 2 * c.num_key_value_heads * c.head_dim
-            total += rows * (proj + c.hidden_size + mlp) * 2
-        return total
+            out.append(rows * (proj + c.hidden_size + mlp) * 2)
+        return out
+
+    def gemm_bytes_per_step(self, rows: int) -> int:
+        """Bytes the saved GEMM outputs of every layer take for one step of `rows` token rows."""
+        return sum(self.gemm_bytes_per_layer(rows))
+
+    def gemm_saved(self, i: int) -> bool:
+        """Whether layer i keeps its GEMM outputs across checkpointing."""
+        s = self.save_gemms
+        return s == "1" or (s.isdigit() and s != "0" and i < int(s))
 
     def _decide_save_gemms(self, rows: int) -> None:
-        """Keep the GEMM outputs when they fit with room to spare (a decision every rank takes alike:
-        the smallest free memory over ranks counts)."""
-        need = self.gemm_bytes_per_step(rows)
+        """Keep the GEMM outputs of as many layers (from the first) as fit in 70 % of the free memory
+        beyond a 12 GiB margin (a decision every rank takes alike: the smallest free memory over
+        ranks counts)."""
+        per = self.gemm_bytes_per_layer(rows)
         free = torch.tensor([float(torch.cuda.mem_get_info(self.device)[0])], device=self.device)
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
-        self.save_gemms = "1" if need < 0.7 * (float(free[0]) - (12 << 30)) else "0"
+        budget = 0.7 * (float(free[0]) - (12 << 30))
+        n, used = 0, 0
+        while n < len(per) and used + per[n] < budget:
+            used += per[n]
+            n += 1
+        self.save_gemms = "1" if n == len(per) else str(n)
         if self.rank == 0:
-            print(f"[fsdp] GEMM outputs across checkpointing: {'kept' if self.save_gemms == '1' else 'recomputed'} "
-                  f"(need {need / 2**30:.1f} GiB, free {float(free[0]) / 2**30:.1f} GiB)", file=sys.stderr, flush=True)
-        if self.save_gemms == "1" and self.fused_ag:
+            print(f"[fsdp] GEMM outputs across checkpointing: kept for {n} of {len(per)} layers "
+                  f"({used / 2**30:.1f} of {sum(per) / 2**30:.1f} GiB; free {float(free[0]) / 2**30:.1f} GiB)",
+                  file=sys.stderr, flush=True)
+        if n and self.fused_ag:
             # the backward's gathers must not wait for GEMMs that the saved outputs replace
             self.fused_ag = False
 
@@ -623,6 +640,7 @@ class _LayerFn(torch.autograd.Function):
         save = engine.save_cores and h.is_cuda
         try:
             if save:
+                engine.act_store.gemms = engine.gemm_saved(i)
                 engine.act_store.begin("save", i)
             with nvtx(f"layer{i}.fwd"), torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], h, L, block, engine.cfg.gdn_chunk_size, cos, sin,
@@ -652,6 +670,7 @@ class _LayerFn(torch.autograd.Function):
         reuse = engine.save_cores and hx.is_cuda
         try:
             if reuse:  # the recomputation takes the saved core outputs instead of rerunning them
+                engine.act_store.gemms = engine.gemm_saved(i)
                 engine.act_store.begin("reuse", i)
             with nvtx(f"layer{i}.bwd"), torch.enable_grad(), \
                     torch.nn.utils.stateless._reparametrize_module(layer, params):

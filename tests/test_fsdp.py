@@ -92,3 +92,13 @@ def test_world2_fsdp_matches_replicated_dp_on_gloo():
         for a, b in losses:
             assert abs(a - b) < 1e-4 * max(1.0, abs(a)), (rank, losses)
         assert worst < 1e-4, (rank, worst)
+
+
+def test_partial_gemm_saving_policy():
+    """gemm_saved: "1" every layer, "0" none, "<n>" the first n layers."""
+    from dllm_qwen38_b200.parallel.fsdp import FSDPEngine
+
+    e = object.__new__(FSDPEngine)
+    for s, want in (("1", [True] * 4), ("0", [False] * 4), ("2", [True, True, False, False])):
+        e.save_gemms = s
+        assert [e.gemm_saved(i) for i in range(4)] == want, s

@@ -463,8 +463,10 @@ class FSDPEngine:
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
         x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
-        if self.save_gemms == "auto":
-            self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
+        probe = self.save_gemms == "auto"  # this step keeps no GEMM outputs and measures the peak
+        if probe:
+            torch.cuda.synchronize(self.device)
+            torch.cuda.reset_peak_memory_stats(self.device)
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
@@ -472,6 +474,8 @@ class FSDPEngine:
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
         loss.backward()
         self._optimizer_step()
+        if probe:
+            self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
         return loss.detach()
 
     def gemm_bytes_per_layer(self, rows: int) -> list:
@@ -497,14 +501,17 @@ class FSDPEngine:
         return s == "1" or (s.isdigit() and s != "0" and i < int(s))
 
     def _decide_save_gemms(self, rows: int) -> None:
-        """Keep the GEMM outputs of as many layers (from the first) as fit in 70 % of the free memory
-        beyond a 12 GiB margin (a decision every rank takes alike: the smallest free memory over
-        ranks counts)."""
+        """After a step that kept no GEMM outputs: keep those of as many layers (from the first,
+        whose outputs live longest) as fit in 85 % of the device memory that the step's peak left
+        unreserved, less 2 GiB. The caching allocator keeps its peak reservation, so what the saved
+        outputs add has to come from memory that is still free now. Every rank takes the same
+        decision: the smallest headroom over ranks counts."""
         per = self.gemm_bytes_per_layer(rows)
+        torch.cuda.synchronize(self.device)
         free = torch.tensor([float(torch.cuda.mem_get_info(self.device)[0])], device=self.device)
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
-        budget = 0.7 * (float(free[0]) - (12 << 30))
+        budget = 0.85 * (float(free[0]) - (2 << 30))
         n, used = 0, 0
         while n < len(per) and used + per[n] < budget:
             used += per[n]

@@ -222,7 +222,118 @@ def op_adamw(a):
     return (lambda: Cu.adamw_flat(w, p, gr, m, v, 1e-5, 0.9, 0.95, 1e-8, 0.0, 1.0, 0.1, 0.05)), 12.0 * n, 30.0 * n
 
 
-OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm,
+def op_qknorm(a):
+    """q and k RMSNorm(1+w) + partial RoPE, forward + backward (`_C.qk_norm_rope_fwd/bwd`), 27B
+    attention shapes: q [B, 2L, 24, 256], k [B, 2L, 4, 256], rotary dim 64"""
+    from ..config import preset
+    from ..models.blockdiff import rope_tables
+    from ..ops import cuda as Cu
+
+    cfg = preset("27b")
+    B, T2, D = a.B, 2 * a.L, 256
+    q = torch.randn(B, T2, 24, D, device="cuda").bfloat16()
+    k = torch.randn(B, T2, 4, D, device="cuda").bfloat16()
+    w1 = torch.ones(D, device="cuda")
+    cos, sin = rope_tables(cfg, a.L, torch.bfloat16, "cuda")
+    cos, sin = torch.cat([cos, cos]), torch.cat([sin, sin])  # both streams share positions 0..L-1
+    dq, dk = torch.randn_like(q), torch.randn_like(k)
+
+    def fn():
+        Cu._C.qk_norm_rope_fwd(q, w1, cos, sin, 1e-6)
+        Cu._C.qk_norm_rope_fwd(k, w1, cos, sin, 1e-6)
+        Cu._C.qk_norm_rope_bwd(dq, q, w1, cos, sin, 1e-6)
+        Cu._C.qk_norm_rope_bwd(dk, k, w1, cos, sin, 1e-6)
+    n = q.numel() + k.numel()
+    return fn, 20.0 * n, 2.0 * n * 5  # fwd: read x, write y; bwd: read dy, x, write dx
+
+
+def op_gnorm(a):
+    """gated RMSNorm of the GDN output, forward + backward (`_C.gated_rmsnorm_fwd/bwd`): rows =
+    B x 2L x 48 heads of 128"""
+    from ..ops import cuda as Cu
+
+    rows = a.B * 2 * a.L * 48
+    x = torch.randn(rows, 128, device="cuda").bfloat16()
+    z = torch.randn(rows, 128, device="cuda").bfloat16()
+    w = torch.ones(128, device="cuda").bfloat16()
+    dy = torch.randn_like(x)
+
+    def fn():
+        Cu._C.gated_rmsnorm_fwd(x, z, w, 1e-6)
+        Cu._C.gated_rmsnorm_bwd(dy, x, z, w, 1e-6)
+    n = x.numel()
+    return fn, 24.0 * n, 2.0 * n * 8  # fwd: x, z -> y; bwd: dy, x, z -> dx, dz
+
+
+def op_dswiglu(a):
+    """SwiGLU backward elementwise (`_C.dswiglu`): d(gate|up) from d(act) and the stored gate|up,
+    rows = B x 2L, F = 17408"""
+    from ..ops import cuda as Cu
+
+    rows, F = a.B * 2 * a.L, 17408
+    dact = torch.randn(rows, F, device="cuda").bfloat16()
+    gu = torch.randn(rows, 2 * F, device="cuda").bfloat16()
+    return (lambda: Cu._C.dswiglu(dact, gu)), 10.0 * rows * F, 2.0 * rows * F * 5
+
+
+def op_gates(a):
+    """GDN gates forward + backward (`_C.gdn_gates_fwd/bwd`): beta = sigmoid(b), g = -exp(A_log)
+    softplus(a + dt_bias), rows = B x 2L, 48 heads"""
+    from ..ops import cuda as Cu
+
+    rows, H = a.B * 2 * a.L, 48
+    av = torch.randn(rows, H, device="cuda").bfloat16()
+    bv = torch.randn(rows, H, device="cuda").bfloat16()
+    A_log = torch.randn(H, device="cuda")
+    dt = torch.randn(H, device="cuda")
+    dg, db = torch.randn(rows, H, device="cuda"), torch.randn(rows, H, device="cuda")
+
+    def fn():
+        Cu._C.gdn_gates_fwd(av, bv, A_log, dt)
+        Cu._C.gdn_gates_bwd(dg, db, av, bv, A_log, dt)
+    return fn, 30.0 * rows * H, rows * H * (2 * 2 + 4 * 2 + 4 * 2 + 2 * 2 * 2)
+
+
+def op_decode(a):
+    """decode confidence (softmax max probability + argmax over the vocab per row) and the
+    threshold commit rule (`_C.confidence`, `_C.commit`): batch 32 x block 32 rows"""
+    from ..ops import cuda as Cu
+
+    Bd, T = 32, 32
+    logits = torch.randn(Bd * T, a.vocab, device="cuda").bfloat16()
+    conf = torch.zeros(Bd * T, device="cuda")
+    pick = torch.zeros(Bd * T, dtype=torch.long, device="cuda")
+    ids = torch.zeros(Bd, T, dtype=torch.long, device="cuda")
+    masked = torch.ones(Bd, T, dtype=torch.bool, device="cuda")
+    fw = torch.zeros(Bd, dtype=torch.int32, device="cuda")
+    left = torch.zeros(Bd, dtype=torch.int32, device="cuda")
+
+    def fn():
+        masked.fill_(True)
+        Cu._C.confidence(logits, conf, pick)
+        Cu._C.commit(conf, pick, masked, ids, 0.9, 8, fw, left)
+    return fn, 4.0 * logits.numel(), 2.0 * logits.numel()
+
+
+def op_embed(a):
+    """embedding rows forward + gradient scatter-add (`_C.embed_fwd`, `_C.embed_bwd_`): B x 2L ids
+    into a [vocab, 5120] table"""
+    from ..ops import cuda as Cu
+
+    D = 5120
+    table = torch.randn(a.vocab, D, device="cuda").bfloat16()
+    ids = torch.randint(0, a.vocab, (a.B * 2 * a.L,), device="cuda")
+    dh = torch.randn(ids.numel(), D, device="cuda").bfloat16()
+    grad = torch.zeros(a.vocab, D, device="cuda")
+
+    def fn():
+        Cu._C.embed_fwd(ids, table)
+        Cu._C.embed_bwd_(grad, ids, dh)
+    return fn, 1.0 * ids.numel() * D, ids.numel() * D * (2 + 2 + 2 + 8)
+
+
+OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
+       "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed,
        "adamw": op_adamw}
 
 

@@ -429,7 +429,8 @@ std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tenso
   auto dsrc = at::empty({B, T2, H, Dh}, src.options());
   const int T = B * T2;
   const int64_t items = (int64_t)T * H;
-  const int per_block = 256;
+  // about four 8-warp blocks per SM whatever the head count (the k side has 6x fewer rows than q)
+  const int per_block = (int)std::min<int64_t>(256, std::max<int64_t>(8, (items + 4 * 148 - 1) / (4 * 148)));
   const int nblk = std::max<int64_t>(1, (items + per_block - 1) / per_block);
   auto part = at::empty({nblk, Dh}, src.options().dtype(at::kFloat));
   auto dw = at::zeros({Dh}, src.options().dtype(at::kFloat));

@@ -100,11 +100,44 @@ __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) {
   return __bfloat162float(x);
 }
 
+// one 16-byte vector of 8 bf16 logits starting at index i0: a single rescale of the running sum
+// per vector (at the vector's first maximum) instead of a dependent update per element
+__device__ __forceinline__ void absorb8(Best& b, uint4 p, int i0) {
+  const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+  float x[8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(p2[e]);
+    x[2 * e] = f.x, x[2 * e + 1] = f.y;
+  }
+  float mx = x[0];
+  int am = 0;
+#pragma unroll
+  for (int e = 1; e < 8; ++e)
+    if (x[e] > mx) mx = x[e], am = e;  // strict: the first index of the vector's max
+  if (mx > b.m) {  // strict: an equal max keeps the thread's earlier index
+    b.s = b.m == -INFINITY ? 0.f : b.s * __expf(b.m - mx);
+    b.m = mx;
+    b.idx = i0 + am;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) b.s += __expf(x[e] - b.m);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(512) confidence_kernel(const T* __restrict__ logits, int64_t ld, int V,
-                                                         float* __restrict__ conf, int64_t* __restrict__ pick) {
+                                                         float* __restrict__ conf, int64_t* __restrict__ pick,
+                                                         int vec) {
   const T* row = logits + (int64_t)blockIdx.x * ld;
   Best b{-INFINITY, 0.f, 0x7fffffff};
+  if constexpr (sizeof(T) == 2) {
+    if (vec) {  // bf16 rows of a multiple of 8 logits, 16-byte aligned
+      const uint4* rv = reinterpret_cast<const uint4*>(row);
+#pragma unroll 4
+      for (int j = threadIdx.x; j < V / 8; j += blockDim.x) absorb8(b, rv[j], j * 8);
+      V = 0;  // nothing left for the element loop
+    }
+  }
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float x = to_f<T>(row[i]);
     if (x > b.m) {
@@ -214,12 +247,13 @@ void confidence(const at::Tensor& logits, at::Tensor& conf, at::Tensor& pick) {
   c10::cuda::CUDAGuard g(logits.device());
   if (logits.scalar_type() == at::kFloat)
     dec::confidence_kernel<float><<<R, 512, 0, dec::stream()>>>(logits.data_ptr<float>(), logits.stride(0), V,
-                                                                 conf.data_ptr<float>(), pick.data_ptr<int64_t>());
+                                                                 conf.data_ptr<float>(), pick.data_ptr<int64_t>(), 0);
   else {
     TORCH_CHECK(logits.scalar_type() == at::kBFloat16, "confidence: fp32 or bf16 logits");
+    const int vec = V % 8 == 0 && logits.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0;
     dec::confidence_kernel<__nv_bfloat16><<<R, 512, 0, dec::stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0), V, conf.data_ptr<float>(),
-        pick.data_ptr<int64_t>());
+        pick.data_ptr<int64_t>(), vec);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -88,10 +88,11 @@ def test_confidence_and_commit_rule_match_golden():
     conf = torch.empty(B * T, device="cuda")
     pick = torch.empty(B * T, dtype=torch.long, device="cuda")
     lb = (torch.randn(B * T, V, device="cuda") * 3).bfloat16()  # bf16 rows: ties possible
-    C.confidence(lb, conf, pick)
-    cm = torch.softmax(lb.float(), -1).max(-1).values
-    assert torch.allclose(conf, cm, rtol=1e-4, atol=1e-6)
-    assert torch.equal(lb.float().gather(1, pick[:, None])[:, 0], lb.float().max(-1).values)
+    for rows in (lb, lb[:, :4999]):  # the 16-byte vector path, and the element path (V % 8 != 0)
+        C.confidence(rows, conf, pick)
+        cm = torch.softmax(rows.float(), -1).max(-1).values
+        assert torch.allclose(conf, cm, rtol=1e-4, atol=1e-6)
+        assert torch.equal(pick, rows.float().argmax(-1))  # the first index of the maximum
     logits = torch.randn(B * T, V, device="cuda") * 3  # fp32 rows: the argmax is unique
     C.confidence(logits, conf, pick)
     cm, pm = torch.softmax(logits, -1).max(-1)

@@ -17,6 +17,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <string>
 #include <tuple>
 #include <vector>
@@ -81,6 +82,9 @@ struct GemmArgs {
   unsigned* ag_ready;
   unsigned* ag_claim;
   unsigned ag_seq, ag_epoch;
+  // tile raster: groups of raster_g tile rows along M (raster_n = 0) or tile columns along N
+  // (raster_n = 1); 0 = 8 along M
+  int raster_g, raster_n;
 };
 
 __device__ __forceinline__ void tp_st_release(unsigned* p, unsigned v) {
@@ -107,15 +111,26 @@ struct Cfg {
   static constexpr uint32_t IDESC = idesc_bf16(BM, BN, A_MN ? 1 : 0, B_MN ? 1 : 0);
 };
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
-  constexpr int G = 8;  // m-tiles per raster group
-  int group_size = G * tiles_n;
-  int g = t / group_size;
-  int first_m = g * G;
-  int rows = min(G, tiles_m - first_m);
-  int r = t % group_size;
-  tm = first_m + r % rows;
-  tn = r / rows;
+// Tile t -> (tm, tn). Tiles run in groups of G tile rows (or, along N, G tile columns); within a
+// group the short side varies fastest, so the CTAs resident at one time share the group's
+// operand tiles through L2 and the other operand streams once per group.
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int G, int along_n, int& tm, int& tn) {
+  if (G <= 0) G = 8;
+  if (!along_n) {
+    const int group_size = G * tiles_n;
+    const int first_m = (t / group_size) * G;
+    const int rows = min(G, tiles_m - first_m);
+    const int r = t % group_size;
+    tm = first_m + r % rows;
+    tn = r / rows;
+  } else {
+    const int group_size = G * tiles_m;
+    const int first_n = (t / group_size) * G;
+    const int cols = min(G, tiles_n - first_n);
+    const int r = t % group_size;
+    tn = first_n + r % cols;
+    tm = r / cols;
+  }
 }
 
 __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
@@ -411,7 +426,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
       int tm, tn;
-      tile_coords(t % mn_tiles, tiles_m, tiles_n, tm, tn);
+      tile_coords(t % mn_tiles, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
       const int m0 = tm * BM, n0 = tn * C_::BN_OUT;
       const int kb0 = (t / mn_tiles) * kbs, kb1 = min(kblocks_all, kb0 + kbs);
       if constexpr (!B_MN) {
@@ -533,7 +548,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t % mn_tiles, tiles_m, tiles_n, tm, tn);
+      tile_coords(t % mn_tiles, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
       const int64_t split_off = (int64_t)(t / mn_tiles) * args.split_stride;
       const int row = tm * BM + row_in_tile;
       const int n0 = tn * C_::BN_OUT;
@@ -695,7 +710,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     bool ok = true;
     for (int t = pair; t < num_tiles && ok; t += npairs) {
       int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      tile_coords(t, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
       const int m0 = tm * 256 + (int)crank * 128;
       const int n0 = tn * C_::BN_OUT;
       const int bn0 = (EPI == EPI_SWIGLU) ? (crank ? args.N + n0 : n0) : n0 + (int)crank * 128;
@@ -791,7 +806,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, tm, tn);
+      tile_coords(t, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
       const int row = tm * 256 + (int)crank * 128 + row_in_tile;
       const int n0 = tn * C_::BN_OUT;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * C_::BN;
@@ -903,6 +918,37 @@ static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, co
   if (!(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_ADD_BF16 || epi == EPI_SWIGLU)) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256));
   return M >= 512 && tiles >= 148;
+}
+
+// Tile raster of the pair kernel. BDLLM_GEMM_RASTER: "m<G>" / "n<G>" fixes G tile rows along M /
+// tile columns along N; "auto" picks, from a DRAM-traffic model, the orientation and G for which
+// the grouped operand (G tiles x K, bf16) fits in 48 MB of L2 and (operand read once) + (other
+// operand x number of groups) is smallest; unset = "m8".
+static void choose_raster(GemmArgs& g, int64_t M, int64_t NB, int64_t K, int tiles_m, int tiles_n) {
+  static int mode = -1, fixed_g = 8;  // 0: fixed along M, 1: fixed along N, 2: auto
+  if (mode < 0) {
+    const char* e = getenv("BDLLM_GEMM_RASTER");
+    mode = 0;
+    if (e != nullptr && strcmp(e, "auto") == 0) {
+      mode = 2;
+    } else if (e != nullptr && (e[0] == 'm' || e[0] == 'n') && atoi(e + 1) > 0) {
+      mode = e[0] == 'n' ? 1 : 0;
+      fixed_g = atoi(e + 1);
+    }
+  }
+  if (mode < 2) {
+    g.raster_g = fixed_g;
+    g.raster_n = mode;
+    return;
+  }
+  const double tile_bytes = 256.0 * (double)K * 2.0;
+  const int gmax = std::max(1, (int)(48e6 / tile_bytes));
+  const double a = (double)M * K * 2.0, b = (double)NB * K * 2.0;
+  const int gm = std::min(gmax, tiles_m), gn = std::min(gmax, tiles_n);
+  const double tm = a + b * (double)((tiles_m + gm - 1) / gm);
+  const double tn = b + a * (double)((tiles_n + gn - 1) / gn);
+  g.raster_n = tn < tm ? 1 : 0;
+  g.raster_g = tn < tm ? gn : gm;
 }
 
 template <int EPI, bool A_MN, bool B_MN>
@@ -1281,6 +1327,8 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   GTRACE("args ok");
   // the CTA-pair kernel for large forward (K-major) GEMMs
   if (use_pair(a_mn, b_mn, M, N, epi, tp, ag)) {
+    choose_raster(args, M, epi == EPI_SWIGLU ? 2 * N : N, K, (int)((M + 255) / 256),
+                  (int)((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256)));
     if (a_mn)
       make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);
     else

@@ -42,7 +42,7 @@ import torch
 import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-BASELINE_SEQ_TOK_S = 1233.12  # 27B FSDP, 8 x H200, production run
+BASELINE_SEQ_TOK_S = 1233.12  # the reference's published 27B FSDP production run (8 x H200, full 64 layers)
 METRIC = "block-diff train tok/s & MFU, 27B FSDP 1/2/4/8 B200"
 
 

@@ -6,10 +6,12 @@
 Metric: unique sequence tokens per second (batch x L per step; neither the two complementary
 views nor the x_t||x_0 doubling counted, the reference's unit), whole job, plus MFU.
 Config: 27B-shape hybrid (hidden 5120, FFN 17408, GDN 16/48 heads of 128, attention 24/4 of 256,
-vocab 248320), truncated to --layers (default 16: 12 GDN + 4 attention, the depth that fits one
-B200 with fp32 master weights and moments) at every N, seq 4096 per stream (x_t||x_0 = 8192),
-block 32, micro-batch 1 sequence per GPU (global batch = N: weak scaling), activation
-checkpointing, AdamW, bf16 compute, random init, synthetic uniform token ids.
+vocab 248320). Depth per N (`--layers`, default `auto`): all 64 layers (48 GDN + 16 attention) at
+N >= 4, the full BASELINE config; 32 layers at N = 2 and 16 at N = 1, the deepest 3:1 truncations
+whose fp32 master weights and AdamW moments fit in the GPUs' memory (27B parameters need 14 bytes
+each of sharded state, 378 GB). Seq 4096 per stream (x_t||x_0 = 8192), block 32, micro-batch 1
+sequence per GPU (global batch = N: per-GPU tokens fixed), activation checkpointing, AdamW, bf16
+compute, random init, synthetic uniform token ids.
 
 Timing: W untimed warm-up steps; then K steps between a barrier + synchronize on both sides,
 timed with CUDA events on the compute stream; the reported time is the max over ranks. L2 is
@@ -220,8 +222,39 @@ def _install_fsdp_state_adapter():
             lambda self: [self._fsdp_param_group] if self._fsdp_param_group is not None else [])
 
 
+def _install_reference(ref_root: str, rank: int) -> None:
+    """Offline install of the reference package into `ref_root` when it is missing and its source
+    tree is named by BDLLM_REFERENCE_SRC: pip from a scratch copy (the build writes into its
+    source tree), no index, no dependency resolution (every dependency is already importable).
+    Rank 0 installs; the other ranks wait for its marker file."""
+    src = os.environ.get("BDLLM_REFERENCE_SRC", "")
+    if not src or not os.path.isfile(os.path.join(src, "pyproject.toml")):
+        return
+    done = ref_root + ".installed"
+    if rank == 0:
+        import shutil
+        import subprocess
+        import tempfile
+
+        with tempfile.TemporaryDirectory() as tmp:
+            copy = os.path.join(tmp, "src")
+            shutil.copytree(src, copy)
+            cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                   "--find-links", "/opt/wheelhouse", "--target", ref_root, copy]
+            rc = subprocess.run(cmd, stdout=subprocess.DEVNULL, stderr=subprocess.PIPE, text=True).returncode
+        with open(done, "w") as f:
+            f.write(str(rc))
+    else:
+        for _ in range(600):
+            if os.path.exists(done):
+                break
+            time.sleep(1.0)
+
+
 def run_reference(a, rank, world):
     ref_root = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_root, "dllm_qwen38")):
+        _install_reference(ref_root, rank)
     if not os.path.isdir(os.path.join(ref_root, "dllm_qwen38")):
         return {"unavailable": "baseline/_ref not installed (pip install --no-deps --target baseline/_ref)"}
     sys.path.insert(0, ref_root)
@@ -307,7 +340,8 @@ def main(argv=None) -> int:
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--model", default="27b")
-    p.add_argument("--layers", type=int, default=16)
+    p.add_argument("--layers", default="auto",
+                   help="decoder layers: an int, or auto = 64 at >= 4 GPUs, 32 at 2, 16 at 1 (27b model)")
     p.add_argument("--seq-len", type=int, default=4096)
     p.add_argument("--block", type=int, default=32)
     p.add_argument("--micro-batch", type=int, default=1)
@@ -319,6 +353,10 @@ def main(argv=None) -> int:
     a = p.parse_args(argv)
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    if a.layers == "auto":
+        a.layers = (64 if a.gpus >= 4 else 32 if a.gpus == 2 else 16) if a.model == "27b" else None
+    else:
+        a.layers = int(a.layers)
     rank, world, _ = _dist_setup(a.gpus)
     try:
         r = run_reference(a, rank, world) if a.impl == "reference" else run_native(a, rank, world)

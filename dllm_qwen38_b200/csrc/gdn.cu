@@ -1371,7 +1371,9 @@ std::vector<at::Tensor> gdn_bwd_rows(const at::Tensor& dout, const at::Tensor& q
 
 // ============================================================================ no-allocation entry
 // The forward above, with its working memory taken from a fixed array instead of allocated
-// tensors. Declared (and its contract described) in gdn_noalloc.h.
+// tensors. Declared (and its contract described) in gdn_noalloc.h. Left out of the debug-bounds
+// build (_C_dbg), so a process that loads both libraries holds one scratch array, not two.
+#ifndef BDLLM_DEBUG_BOUNDS
 #include <atomic>
 #include <cstdio>
 
@@ -1420,11 +1422,16 @@ int noalloc_run(bdllm::gdn::Args a, unsigned char* base, size_t cap, cudaStream_
       cudaFuncSetAttribute(fwd_recur_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, rec) != cudaSuccess ||
       cudaFuncSetAttribute(fwd_out_kernel<D, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, big) != cudaSuccess)
     return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "cudaFuncSetAttribute failed");
+  // no error was pending on entry, so one seen after a launch is that launch's own
   fwd_prep_kernel<D, D><<<dim3(a.nb, BH), NT, big, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "launch of the chunk-preparation kernel failed");
   fwd_recur_kernel<D, D><<<dim3(BH, (D + 31) / 32), NT, rec, stream>>>(a);
+  if (cudaGetLastError() != cudaSuccess)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "launch of the state recurrence kernel failed");
   fwd_out_kernel<D, D><<<dim3(2 * a.nb, BH), NT, big, stream>>>(a);
   if (cudaGetLastError() != cudaSuccess)
-    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "kernel launch failed");
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "launch of the output kernel failed");
   return BDLLM_NOALLOC_OK;
 }
 
@@ -1439,8 +1446,18 @@ extern "C" __attribute__((visibility("default"))) int bdllm_gdn_forward_noalloc(
     return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "need block <= 32 dividing L and Hv % Hk == 0");
   if (D != 16 && D != 32 && D != 64 && D != 128)
     return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "head dim must be 16, 32, 64 or 128");
-  if (ld_qk % 8 != 0 || ld_v % 8 != 0 || ld_qk < 2 * (int64_t)Hk * D || ld_v < (int64_t)Hv * D)
+  if (ld_qk % 8 != 0 || ld_v % 8 != 0 || ld_qk < (int64_t)Hk * D || ld_v < (int64_t)Hv * D)
     return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "token strides too small or not multiples of 8");
+  // the kernels move q, k, v and o in 16-byte vectors and g, beta as 4-byte floats
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+       reinterpret_cast<uintptr_t>(o)) & 15u)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "q, k, v and o must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(g) | reinterpret_cast<uintptr_t>(beta)) & 3u)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_BAD_ARGUMENT, "g and beta must be 4-byte aligned");
+  // an error left pending by earlier work on this thread belongs to its owner: report it without
+  // consuming it, and launch nothing
+  if (cudaPeekAtLastError() != cudaSuccess)
+    return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "a CUDA error was already pending on entry");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
     return noalloc_fail(err, err_len, BDLLM_NOALLOC_CUDA_ERROR, "cudaGetDevice failed");
@@ -1476,3 +1493,4 @@ extern "C" __attribute__((visibility("default"))) int bdllm_gdn_forward_noalloc(
     default: return noalloc_run<128>(a, s, cap, stream, err, err_len);
   }
 }
+#endif  // BDLLM_DEBUG_BOUNDS

@@ -21,6 +21,13 @@
 //     it. Nothing in it has to start at zero: every element a call reads was written earlier in
 //     the same call.
 //   * The call allocates nothing: no cudaMalloc, no cudaFree, no allocating library routine.
+//   * Pointer rules: q, k, v and o 16-byte aligned, g and beta 4-byte aligned; anything else is
+//     refused with BDLLM_NOALLOC_BAD_ARGUMENT before a launch. q and k may be separate buffers or
+//     slices of one packed row; they share the token stride ld_qk (>= Hk * D).
+//   * A CUDA error already pending on the calling thread when the call starts is left in place
+//     (not consumed) and the call returns BDLLM_NOALLOC_CUDA_ERROR without launching.
+//   * Only the main library (_C) exports this symbol; the debug-bounds build (_C_dbg) leaves it
+//     out, so loading both still holds one scratch array per GPU.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -45,8 +52,8 @@ extern "C" {
 //   g    : fp32 [B, 2L, Hv] log-decay gates;  beta : fp32 [B, 2L, Hv]
 //   o    : bf16 [B, 2L, Hv, D] output (written)
 // Supported: D in {16, 32, 64, 128}, block <= 32 dividing L, Hv a multiple of Hk, ld_* multiples
-// of 8. Returns one of the BDLLM_NOALLOC_* codes; on a non-zero code `err` (if not null, of
-// `err_len` bytes) receives a one-line reason.
+// of 8 with ld_qk >= Hk * D and ld_v >= Hv * D. Returns one of the BDLLM_NOALLOC_* codes; on a
+// non-zero code `err` (if not null, of `err_len` bytes) receives a one-line reason.
 int bdllm_gdn_forward_noalloc(const void* q, const void* k, const void* v, int64_t ld_qk, int64_t ld_v,
                               const float* g, const float* beta, void* o, int B, int L, int Hk, int Hv, int D,
                               int block, cudaStream_t stream, char* err, int err_len);

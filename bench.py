@@ -7,10 +7,11 @@ Metric: unique sequence tokens per second (batch x L per step; neither the two c
 views nor the x_t||x_0 doubling counted, the reference's unit), whole job, plus MFU.
 Config: 27B-shape hybrid (hidden 5120, FFN 17408, GDN 16/48 heads of 128, attention 24/4 of 256,
 vocab 248320). Depth per N (`--layers`, default `auto`): all 64 layers (48 GDN + 16 attention) at
-N >= 4, the full BASELINE config; 32 layers at N = 2 and 16 at N = 1, the deepest 3:1 truncations
-whose fp32 master weights and AdamW moments fit in the GPUs' memory (27B parameters need 14 bytes
-each of sharded state, 378 GB). Seq 4096 per stream (x_t||x_0 = 8192), block 32, micro-batch 1
-sequence per GPU (global batch = N: per-GPU tokens fixed), activation checkpointing, AdamW, bf16
+N = 8, the full 27B configuration; 16 layers (12 GDN + 4 attention) at N = 1, 2 and 4, a 3:1
+truncation that fits one GPU (27B parameters need 378 GB of fp32 master weights, AdamW moments and
+bf16 shards, more than one GPU holds), so N = 1 -> 4 is a clean weak-scaling curve at fixed
+per-GPU work and N = 8 is the headline configuration. Seq 4096 per stream (x_t||x_0 = 8192),
+block 32, micro-batch 1 sequence per GPU (global batch = N), activation checkpointing, AdamW, bf16
 compute, random init, synthetic uniform token ids.
 
 Timing: W untimed warm-up steps; then K steps between a barrier + synchronize on both sides,
@@ -341,7 +342,7 @@ def main(argv=None) -> int:
     p.add_argument("--impl", default="native", choices=["native", "reference"])
     p.add_argument("--model", default="27b")
     p.add_argument("--layers", default="auto",
-                   help="decoder layers: an int, or auto = 64 at >= 4 GPUs, 32 at 2, 16 at 1 (27b model)")
+                   help="decoder layers: an int, or auto = 64 at 8 GPUs, else 16 (27b model)")
     p.add_argument("--seq-len", type=int, default=4096)
     p.add_argument("--block", type=int, default=32)
     p.add_argument("--micro-batch", type=int, default=1)
@@ -354,7 +355,7 @@ def main(argv=None) -> int:
     if a.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if a.layers == "auto":
-        a.layers = (64 if a.gpus >= 4 else 32 if a.gpus == 2 else 16) if a.model == "27b" else None
+        a.layers = (64 if a.gpus >= 8 else 16) if a.model == "27b" else None
     else:
         a.layers = int(a.layers)
     rank, world, _ = _dist_setup(a.gpus)
@@ -389,6 +390,7 @@ def main(argv=None) -> int:
         "data": "synthetic uniform token ids, random-init weights (seed 0)",
         "config": {
             "model": f"27b-shape hybrid, {cfg.num_hidden_layers} of 64 layers" if a.model == "27b" else a.model,
+            "depth_per_n": "64 layers at 8 GPUs, 16 at 1, 2 and 4 (per-GPU work grows 4x at 8 GPUs)",
             "global_batch": seqs, "seq_len": a.seq_len, "block": a.block, "micro_batch_per_gpu": a.micro_batch,
             "parallelism": r["parallel"], "activation_checkpointing": r.get("ckpt_policy", not a.no_ckpt), "optimizer": "AdamW lr 1e-5",
             "l2": "flushed (256 MiB write) before every timed step; step working set >> L2",

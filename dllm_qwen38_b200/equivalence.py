@@ -1,19 +1,33 @@
-"""The state-fork visibility equivalence check with fault injection.
+"""Equivalence gate for the state fork, with deliberate faults as negative controls.
 
-Answers with numbers (the reference's `equivalence.py:1-12` contract):
+The state fork computes every noised block from the clean stream's recurrent state at the block's
+start instead of running the block-causal mask over the whole x_t||x_0 sequence. This module
+measures whether that shortcut is exact. It builds an oracle that knows nothing about forking:
+for each block it reruns an ordinary, unforked forward over the clean prefix followed by that
+block's noised tokens (fp32 reference ops, delta rule one token at a time, on an fp32 copy of
+the weights), then reports
 
-  1. does the noised stream equal the oracle (an unforked forward per block, block-causal mask)?
-  2. does the clean stream equal the unforked block-causal forward?
-  3. perturbation: does x_t block k ignore x_t block k-1 and x_0 block k, and react to x_0 block k-1?
-  4. does every deliberate fault (concat-causal-gdn / mask-leak / no-conv-prefix) turn check 1 red?
+  * the largest logit difference between the candidate's noised stream and that oracle, and the
+    same for the clean stream against a plain causal forward;
+  * three visibility probes made by editing the input: a noised block must not change when the
+    previous noised block or its own clean block is rewritten, and must change (by at least a
+    floor, 10x the tolerance by default) when the previous clean block is rewritten;
+  * for each fault in `FAULTS` (run the DeltaNet causally over the concatenation, let noised
+    tokens see their own clean block, start each block's convolution without the clean prefix),
+    whether the first measure moves beyond the tolerance. A fault that stays inside it means the
+    gate could not have caught that bug.
 
-Exit 0 = every check passed AND every fault was detected; 1 = a check failed or a fault went
-undetected; 2 = could not measure. The candidate runs through the op layer (the sm_100a kernels
-for ``--device cuda --dtype bfloat16``; fp32 torch ops on the device for ``--dtype float32``,
-since the kernels compute in bf16); the oracle always runs the fp32 reference ops with the
-token-by-token delta rule on its own fp32 copy (``--oracle-device``, default the candidate's).
+The process status is the verdict: 0 when every measure is within bounds and every fault is
+caught, 1 otherwise, 2 when the run itself failed (model not loadable, bad arguments). With
+``--device cuda --dtype bfloat16`` the candidate runs on the sm_100a kernels, which carry the
+fault switches themselves; ``--dtype float32`` on a GPU runs the candidate through the fp32 torch
+ops there (the kernels compute in bf16). Tolerances follow the dtype: 1e-3 for fp32, 0.25 for
+bf16.
 
     python -m dllm_qwen38_b200.equivalence [--model tiny] [--block 32 --nblocks 4] [--device cuda]
+
+Contract kept with the reference (`src/dllm_qwen38/equivalence.py:75-219`): check and fault
+names, output lines, tolerances and exit codes.
 """
 
 from __future__ import annotations

@@ -697,6 +697,11 @@ class _LayerFn(torch.autograd.Function):
 
 def _head_loss(engine, ht, m, x0, norm_w, head_w, n_global, n_local):
     hn = ops.rmsnorm(ht, norm_w, engine.cfg.rms_norm_eps)
+    if n_local == 0:
+        # no scored target on this rank: a zero that still depends on the hidden states, so the
+        # backward runs every layer and this rank joins every gather and reduce-scatter with zero
+        # gradients (the reference's rule, `fsdp_train.py:618-629`)
+        return hn.float().sum() * 0.0
     flat = m.reshape(-1)
     idx = torch.nonzero_static(flat, size=n_local).squeeze(1) if n_local is not None else flat.nonzero().squeeze(1)
     rows = hn.reshape(-1, hn.shape[-1]).index_select(0, idx)
@@ -762,8 +767,13 @@ class FSDPTrainer:
         self.gstep = 0
         self.world, self.rank = self.engine.world, self.engine.rank
 
-    def step(self, x0, prompt_len, valid_len, n_targets: int | None = None):
-        """x0 [b, L] this rank's rows (host or device); returns this rank's loss contribution."""
+    def step(self, x0, prompt_len, valid_len, n_targets: int | None = None, n_global=None):
+        """x0 [b, L] this rank's rows (host or device); returns this rank's loss contribution.
+
+        n_targets: this rank's scored-target count; n_global: the count over all ranks (host
+        number), when the caller already has it. A rank with no scored target still runs the whole
+        step (zero loss and zero gradients) so its collectives stay in step with the others; a
+        step whose GLOBAL count is zero must be skipped by every rank (the caller's decision)."""
         self.gstep += 1
         if n_targets is None:
             n_targets = int((valid_len - prompt_len).clamp(min=0).sum())
@@ -771,12 +781,13 @@ class FSDPTrainer:
         x0 = x0.to(dev, non_blocking=True)
         prompt_len = prompt_len.to(dev, non_blocking=True)
         valid_len = valid_len.to(dev, non_blocking=True)
-        if self.world == 1 or self.uniform_rows:
-            n_global = n_targets * self.world  # every rank scores the same count (no communication)
-        else:
-            n_global = torch.tensor(float(n_targets), device=dev)
-            dist.all_reduce(n_global)
-        if n_targets == 0:
-            raise ValueError("a step with zero scored targets on this rank; pass uniform rows or skip it")
+        if n_global is None:
+            if self.world == 1 or self.uniform_rows:
+                n_global = n_targets * self.world  # every rank scores the same count (no communication)
+            else:
+                n_global = torch.tensor(float(n_targets), device=dev)
+                dist.all_reduce(n_global)
+        if self.world == 1 and n_targets == 0:
+            raise ValueError("a step with zero scored targets; skip it")
         return self.engine.step(x0, prompt_len, valid_len, block=self.block, mask_id=self.mask_id,
                                 n_local=n_targets, n_global=n_global, gstep=self.gstep)

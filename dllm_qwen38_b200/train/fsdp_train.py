@@ -112,13 +112,11 @@ def train_window(trainer, batches, *, n_steps: int, start_step: int, seq_tokens_
             skipped += 1
             trainer.gstep += 1
             continue
-        try:
-            contrib = trainer.step(xr, pr, vr, n_targets=n_local) if n_local else None
+        try:  # a rank with no local target still steps (zero loss, zero gradients, same collectives)
+            contrib = trainer.step(xr, pr, vr, n_targets=n_local, n_global=n_global)
         except torch.OutOfMemoryError:
             mem.on_oom(engine, rank, mem_history and rank == 0)
             raise
-        if contrib is None:
-            raise ValueError("a rank with zero local targets is not supported by the step API")
         loss = contrib.detach().float().reshape(1)
         if world > 1:
             dist.all_reduce(loss)

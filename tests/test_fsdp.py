@@ -102,3 +102,64 @@ def test_partial_gemm_saving_policy():
     for s, want in (("1", [True] * 4), ("0", [False] * 4), ("2", [True, True, False, False])):
         e.save_gemms = s
         assert [e.gemm_saved(i) for i in range(4)] == want, s
+
+
+def _zero_target_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+
+        cfg = preset("tiny_ref")
+        fs = FSDPTrainer(build_model(cfg, seed=0), block=8, mask_id=cfg.mask_id, lr=1e-3, grad_clip=0.0)
+        losses = []
+        for x0, pl, vl in _batches(2 * world, 32, cfg.vocab_size, 3):
+            sl = slice(rank * 2, (rank + 1) * 2)
+            pr = pl[sl].clone()
+            if rank == 1:
+                pr[:] = 32  # every row of this rank is prompt: no scored target here
+            n_local = int((vl[sl] - pr).clamp(min=0).sum())
+            counts = torch.tensor([float(n_local)])
+            dist.all_reduce(counts)
+            loss = fs.step(x0[sl], pr, vl[sl], n_targets=n_local, n_global=int(counts.item()))
+            t = loss.detach().float().reshape(1)
+            dist.all_reduce(t)
+            losses.append(float(t))
+        # numpy copies travel by value (a tensor would be shared by a handle that dies with the rank)
+        out.put((rank, losses, {k: v.numpy().copy() for k, v in _flat(fs.engine.full_state()).items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_world2_rank_with_zero_targets_keeps_collectives_in_step():
+    """Rank 1 holds only prompt rows. It must still run the step (a graph-connected zero loss, zero
+    gradients, the same gathers and reduce-scatters), and the result must equal training on rank
+    0's rows alone with the loss divided by twice its target count (the world-2 gradient average
+    halves rank 0's gradient)."""
+    from dllm_qwen38_b200.parallel.fsdp import FSDPTrainer
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29000 + (os.getpid() + 777) % 2000
+    procs = [ctx.Process(target=_zero_target_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in procs], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    cfg = preset("tiny_ref")
+    solo = FSDPTrainer(build_model(cfg, seed=0), block=8, mask_id=cfg.mask_id, lr=1e-3, grad_clip=0.0)
+    want = []
+    for x0, pl, vl in _batches(4, 32, cfg.vocab_size, 3):
+        n = int((vl[:2] - pl[:2]).clamp(min=0).sum())
+        # divided by twice the count: the gradient AdamW sees is then the world-2 average exactly
+        want.append(2 * float(solo.step(x0[:2], pl[:2], vl[:2], n_targets=n, n_global=2 * n)))
+    ref = _flat(solo.engine.full_state())
+    res = [(r, ls, {k: torch.from_numpy(v) for k, v in st.items()}) for r, ls, st in res]
+    for rank, losses, state in res:
+        for a, b in zip(losses, want):
+            assert abs(a - b) < 1e-4 * max(1.0, abs(b)), (rank, losses, want)
+        worst = max(float((v - ref[k]).abs().max()) for k, v in state.items())
+        assert worst < 1e-4, (rank, worst)
+    assert all(torch.equal(res[0][2][k], res[1][2][k]) for k in res[0][2])

@@ -17,7 +17,11 @@ Exports/imports:
   * `export_safetensors`: full parameters under our keys (``text_model.<HF text key>``,
     ``lm_head.weight``) -- the reference's single-device layout (`train.py:270-276`);
   * `reference_dcp_tensors` + `plain_fqn`: read a reference FSDP checkpoint (per-parameter
-    DTensors named ``text_model.layers.N.layer.<...>``, `gsm8k_eval.py:249-285`) as plain tensors.
+    DTensors named ``text_model.layers.N.layer.<...>``, `gsm8k_eval.py:249-285`) as plain tensors;
+  * `convert_to_reference`: rewrite one of this engine's checkpoints in the reference's layout
+    (`fsdp_train.py:408-464`) so the reference's tools (`gsm8k_eval.py:264-328`) read it.
+
+    python -m dllm_qwen38_b200.io.ckpt to-reference <step dir> <out dir> --model 27b [--layers N]
 """
 
 from __future__ import annotations
@@ -307,3 +311,97 @@ def restore_into(model, tensors: dict, ctx: str = "ckpt") -> None:
     bad += ["model:" + k for k in missing]
     if bad:
         raise ValueError(f"{ctx}: restore incomplete ({len(bad)} problems, first 10: {bad[:10]})")
+
+
+def reference_fqn(key: str) -> str:
+    """Our key -> the reference's checkpoint FQN: decoder-layer parameters sit under the
+    reference's per-layer wrapper (`text_model.layers.N.layer.<...>`); the rest is unchanged."""
+    m = re.match(r"^text_model\.(layers\.\d+)\.(.+)$", key)
+    return f"text_model.{m.group(1)}.layer.{m.group(2)}" if m else key
+
+
+def _optimizer_tensors(path: str, cfg) -> tuple[dict, int]:
+    """{our key: (master fp32, exp_avg fp32, exp_avg_sq fp32)} and the AdamW step count of one of
+    this engine's checkpoints."""
+    from torch.distributed.checkpoint import FileSystemReader, load as dcp_load
+
+    md = FileSystemReader(path).read_metadata()
+    flat = {}
+    for k, meta in md.state_dict_metadata.items():
+        if k.startswith("optim.") and hasattr(meta, "size") and k != "optim.step":
+            flat[k[len("optim."):]] = torch.empty(tuple(meta.size), dtype=meta.properties.dtype)
+    step = torch.zeros((), dtype=torch.int64)
+    dcp_load({"optim": {**flat, "step": step}}, storage_reader=FileSystemReader(path), no_dist=True)
+    out = {}
+    for unit, entries in engine_unit_layout(cfg).items():
+        parts = [flat.get(f"{unit}.{x}") for x in ("master", "exp_avg", "exp_avg_sq")]
+        if any(t is None for t in parts):
+            raise ValueError(f"{path}: optimizer state of unit {unit} missing")
+        for key, shape, off, n in entries:
+            out[key] = tuple(t[off : off + n].view(shape).clone() for t in parts)
+    return out, int(step)
+
+
+@torch.no_grad()
+def convert_to_reference(src: str, dst: str, cfg, *, lr: float = 1e-5, betas=(0.9, 0.95), eps: float = 1e-8,
+                         weight_decay: float = 0.0) -> dict:
+    """Write checkpoint `src` of this engine as a checkpoint in the reference's layout at `dst`.
+
+    Layout written (`fsdp_train.py:408-464` there): {"model": {FQN: bf16}, "optim": {"state":
+    {FQN: {"exp_avg", "exp_avg_sq": bf16, "step": fp32}}, "param_groups": [AdamW hyper-parameters
+    with the FQN list]}, "step", "seq_tokens"}, FQNs as `reference_fqn` spells them. The reference
+    trains bf16 parameters with bf16 moments and no master copy, so the fp32 master weights are
+    rounded to bf16 for "model" and the fp32 moments to bf16 for "optim". A tied head is written
+    as its own `lm_head.weight` entry too (the reference's restore requires the key). Single
+    process; the full model passes through host memory once."""
+    import torch.distributed.checkpoint as dcp
+
+    params, step, seq = any_dcp_tensors(src, cfg)
+    opt, adam_step = _optimizer_tensors(src, cfg)
+    if cfg.tie_word_embeddings and "lm_head.weight" not in params:
+        params["lm_head.weight"] = params["text_model.embed_tokens.weight"]
+    model, state = {}, {}
+    for key, t in params.items():
+        fqn = reference_fqn(key)
+        src_key = "text_model.embed_tokens.weight" if (key == "lm_head.weight" and key not in opt) else key
+        master, m, v = opt[src_key]
+        model[fqn] = master.to(torch.bfloat16)
+        state[fqn] = {"exp_avg": m.to(torch.bfloat16), "exp_avg_sq": v.to(torch.bfloat16),
+                      "step": torch.tensor(float(adam_step))}
+    groups = [{"lr": lr, "betas": list(betas), "eps": eps, "weight_decay": weight_decay, "amsgrad": False,
+               "foreach": False, "maximize": False, "capturable": False, "differentiable": False, "fused": None,
+               "params": sorted(model)}]
+    dcp.save({"model": model, "optim": {"state": state, "param_groups": groups},
+              "step": torch.tensor(step, dtype=torch.int64), "seq_tokens": torch.tensor(seq, dtype=torch.int64)},
+             checkpoint_id=dst, no_dist=True)
+    return {"params": len(model), "step": step, "seq_tokens": seq}
+
+
+def main(argv=None) -> int:
+    import argparse
+
+    import json
+
+    from ..config import PRESETS, ModelConfig, preset
+
+    p = argparse.ArgumentParser(description="checkpoint conversion")
+    sub = p.add_subparsers(dest="cmd", required=True)
+    c = sub.add_parser("to-reference", help="rewrite an engine checkpoint in the reference's DCP layout")
+    c.add_argument("src")
+    c.add_argument("dst")
+    c.add_argument("--model", default="27b", help="preset name or HF checkpoint directory (its config.json)")
+    c.add_argument("--layers", type=int, default=None)
+    c.add_argument("--lr", type=float, default=1e-5)
+    a = p.parse_args(argv)
+    if a.model in PRESETS:
+        cfg = preset(a.model, layers=a.layers)
+    else:
+        with open(os.path.join(a.model, "config.json")) as f:
+            cfg = ModelConfig.from_hf_dict(json.load(f)).truncated(a.layers)
+    rep = convert_to_reference(a.src, a.dst, cfg, lr=a.lr)
+    print(f"CONVERTED\t{a.src} -> {a.dst}\tparams {rep['params']}\tstep {rep['step']}\tseq_tokens {rep['seq_tokens']}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

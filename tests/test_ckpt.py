@@ -94,3 +94,71 @@ def test_export_safetensors_roundtrip(tmp_path):
     load_state_into(m, [path])
     full = a.engine.full_state()
     assert torch.equal(m.text_model.norm.weight.detach(), full["text_model.norm.weight"])
+
+
+def _reference_pkg():
+    """The reference package installed offline under baseline/_ref (skipped when absent)."""
+    import sys
+
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.isdir(os.path.join(root, "dllm_qwen38")):
+        pytest.skip("reference package not installed under baseline/_ref")
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    import dllm_qwen38.blockdiff as rbd
+    import dllm_qwen38.gsm8k_eval as rge
+
+    return rbd, rge
+
+
+def test_convert_to_reference_layout_reads_back_through_the_reference_tools(tmp_path):
+    """An engine checkpoint rewritten in the reference's DCP layout: per-parameter entries named
+    `text_model.layers.N.layer.*`, bf16 model and moments, step / seq_tokens. The reference's own
+    eval reader (`gsm8k_eval.dcp_model_tensors` + `restore_into`) loads it into its HF model with
+    no missing or unexpected key, and the weights are our master weights rounded to bf16."""
+    a = _trainer()
+    for x, p, v in _batches(2):
+        a.step(x, p, v)
+    ckpt.save_engine(a.engine, str(tmp_path / "ours"), gstep=2, seq_tokens=256)
+    cfg = preset("tiny_ref")
+    rep = ckpt.convert_to_reference(ckpt.ckpt_path(str(tmp_path / "ours"), 2), str(tmp_path / "ref"), cfg)
+    assert rep["step"] == 2 and rep["seq_tokens"] == 256
+    tensors, step, seq = ckpt.reference_dcp_tensors(str(tmp_path / "ref"))
+    assert step == 2 and seq == 256
+    assert any(k.startswith("text_model.layers.3.layer.") for k in tensors)
+    assert all(t.dtype == torch.bfloat16 for t in tensors.values())
+    full = a.engine.full_state()
+    for k, t in tensors.items():
+        ours = ckpt.plain_fqn(k)
+        assert torch.equal(t, full[ours].to(torch.bfloat16)), k
+
+    rbd, rge = _reference_pkg()
+    model, lm_head = rbd.tiny_text_model(seed=1)
+    got, rstep, rseq = rge.dcp_model_tensors(str(tmp_path / "ref"))
+    assert (rstep, rseq) == (2, 256)
+    model, lm_head = model.to(torch.bfloat16), lm_head.to(torch.bfloat16)
+    rge.restore_into(model, lm_head, got, ctx="converted")  # raises on any missing/unexpected key
+    sd = model.state_dict()
+    for k, t in full.items():
+        if k == "lm_head.weight":
+            assert torch.equal(lm_head.weight, t.to(torch.bfloat16))
+        else:
+            assert torch.equal(sd[k[len("text_model."):]], t.to(torch.bfloat16)), k
+
+
+def test_convert_cli_round_trip_into_our_loader(tmp_path):
+    a = _trainer()
+    x, p, v = _batches(1)[0]
+    a.step(x, p, v)
+    ckpt.save_engine(a.engine, str(tmp_path / "ours"), gstep=1, seq_tokens=64)
+    rc = ckpt.main(["to-reference", ckpt.ckpt_path(str(tmp_path / "ours"), 1), str(tmp_path / "ref"),
+                    "--model", "tiny_ref"])
+    assert rc == 0
+    m = build_model(preset("tiny_ref"), seed=9)
+    tensors, _, _ = ckpt.any_dcp_tensors(str(tmp_path / "ref"), m.config)
+    ckpt.restore_into(m, tensors)
+    full = a.engine.full_state()
+    for k, t in m.state_dict().items():
+        key = "text_model." + k if not k.startswith("lm_head") else k
+        if key in full:
+            assert torch.equal(t, full[key].to(torch.bfloat16).float()), k

@@ -30,20 +30,27 @@ from .optim import MasterAdamW
 
 
 def synthetic_rule(start: int, n: int, vocab: int, a: int = 7, c: int = 3) -> list:
-    out, x = [], start
-    for _ in range(n):
-        out.append(x)
-        x = (x * a + c) % vocab
-    return out
+    """The affine token rule x_{i+1} = (a x_i + c) mod vocab from `start`, n tokens (the
+    reference's synthetic task, `train.py:33-38`)."""
+    return _affine_rows(torch.tensor([start]), n, vocab, a, c)[0].tolist()
+
+
+def _affine_rows(starts: torch.Tensor, n: int, vocab: int, a: int = 7, c: int = 3) -> torch.Tensor:
+    """[len(starts), n] int64: every row follows the affine rule from its start, all rows at once."""
+    cols = [starts.to(torch.int64)]
+    for _ in range(n - 1):
+        cols.append((cols[-1] * a + c) % vocab)
+    return torch.stack(cols, 1)
 
 
 def synthetic_batches(B: int, L: int, vocab: int, block: int, seed: int):
-    """Yields (x0 [B, L], prompt_len [B] = block, valid_len [B] = L) forever."""
+    """Yields (x0 [B, L], prompt_len [B] = block, valid_len [B] = L) forever: one start id per row
+    from a generator seeded with `seed` (the same seed gives the reference's rows), the first
+    block as the unscored prompt."""
     g = torch.Generator().manual_seed(seed)
+    prompt, valid = torch.full((B,), block), torch.full((B,), L)
     while True:
-        starts = torch.randint(0, vocab, (B,), generator=g).tolist()
-        x0 = torch.tensor([synthetic_rule(s, L, vocab) for s in starts])
-        yield x0, torch.full((B,), block), torch.full((B,), L)
+        yield _affine_rows(torch.randint(0, vocab, (B,), generator=g), L, vocab), prompt, valid
 
 
 def random_batches(B: int, L: int, vocab: int, seed: int, prompt: int = 0):
@@ -53,61 +60,106 @@ def random_batches(B: int, L: int, vocab: int, seed: int, prompt: int = 0):
         yield torch.randint(0, vocab, (B, L), generator=g), torch.full((B,), prompt), torch.full((B,), L)
 
 
+# ---------------------------------------------------------------------------- chat data
+
+
+def _literal_list(text: str):
+    """A message list written as a Python literal (single quotes), or None."""
+    import ast
+
+    try:
+        val = ast.literal_eval(text)
+    except (ValueError, SyntaxError):
+        return None
+    return val if isinstance(val, list) else None
+
+
 def _messages(row: dict):
-    """Chat rows: a `messages` list, or Nemotron-style `input` (a Python-literal message list or a
-    string) plus `output` (`train.py:94-111`)."""
+    """Normalise one dataset row to a chat message list ending with the assistant turn, or None.
+
+    Accepted shapes: {"messages": [...]}; {"input": <message list, or that list as a Python
+    literal string, or a plain user string>, "output": <assistant text>} (the Nemotron SFT rows
+    the reference trains on, `train.py:94-111`)."""
     if isinstance(row.get("messages"), list):
         return row["messages"]
-    inp, out = row.get("input"), row.get("output")
-    if isinstance(inp, str) and inp.lstrip().startswith("[{"):
-        import ast
-
-        try:
-            inp = ast.literal_eval(inp)
-        except (ValueError, SyntaxError):
+    reply = row.get("output")
+    if not isinstance(reply, str):
+        return None
+    turns = row.get("input")
+    if isinstance(turns, str) and turns.lstrip().startswith("[{"):
+        turns = _literal_list(turns)
+        if turns is None:
             return None
-    if isinstance(inp, list) and isinstance(out, str):
-        return list(inp) + [{"role": "assistant", "content": out}]
-    if isinstance(inp, str) and isinstance(out, str):
-        return [{"role": "user", "content": inp}, {"role": "assistant", "content": out}]
-    return None
+    if isinstance(turns, str):
+        turns = [{"role": "user", "content": turns}]
+    if not isinstance(turns, list):
+        return None
+    return [*turns, {"role": "assistant", "content": reply}]
+
+
+def _token_list(encoded) -> list:
+    """apply_chat_template may return a list of ids or a mapping holding them."""
+    return list(encoded["input_ids"]) if hasattr(encoded, "keys") else list(encoded)
+
+
+def encode_chat(tokenizer, msgs: list, L: int):
+    """(ids truncated to L, prompt token count) for one conversation; None when the prompt alone
+    fills L or the reply adds no token (nothing to score)."""
+    prompt = _token_list(tokenizer.apply_chat_template(msgs[:-1], tokenize=True, add_generation_prompt=True))
+    full = _token_list(tokenizer.apply_chat_template(msgs, tokenize=True))
+    if len(prompt) >= L or len(full) <= len(prompt):
+        return None
+    return full[:L], len(prompt)
+
+
+def _chat_rows(dataset: str, split: str, tokenizer, L: int, seed: int, streaming: bool):
+    """Encoded (ids, prompt_len) rows forever, one shuffled pass of the split after another (pass
+    p shuffled with seed + p, 2000-row buffer); yields None at the end of each pass so the batcher
+    can tell whether a pass produced anything."""
+    from datasets import load_dataset  # optional dependency
+
+    name = "SFT" if "Nemotron" in dataset else None
+    p = 0
+    while True:
+        ds = load_dataset(dataset, name, split=split, streaming=streaming)
+        if streaming:
+            ds = ds.shuffle(seed=seed + p, buffer_size=2000)
+        for row in ds:
+            msgs = _messages(row)
+            enc = encode_chat(tokenizer, msgs, L) if msgs else None
+            if enc is not None:
+                yield enc
+        yield None
+        p += 1
 
 
 def chat_batches(dataset: str, split: str, tokenizer, B: int, L: int, block: int, seed: int, streaming: bool = True):
-    """Cycling chat-data batches (`train.py:50-91`): (x0, prompt_len, valid_len)."""
-    from datasets import load_dataset  # optional dependency
-
+    """Cycling chat-data batches (x0 [B, L] right-padded, prompt_len [B], valid_len [B]): the
+    prompt tokens stay clean and unscored. Stops with RuntimeError when a whole pass has no usable
+    row, or when a second pass still has not filled one batch (the split is too small for B)."""
     pad = tokenizer.pad_token_id if tokenizer.pad_token_id is not None else 0
-    buf_x, buf_p, buf_v = [], [], []
-    pass_n = 0
-    while True:
-        ds = load_dataset(dataset, "SFT" if "Nemotron" in dataset else None, split=split, streaming=streaming)
-        if streaming:
-            ds = ds.shuffle(seed=seed + pass_n, buffer_size=2000)
-        added = yielded = 0
-        for row in ds:
-            msgs = _messages(row)
-            if msgs is None:
-                continue
-            prompt = tokenizer.apply_chat_template(msgs[:-1], tokenize=True, add_generation_prompt=True)
-            full = tokenizer.apply_chat_template(msgs, tokenize=True)
-            if hasattr(prompt, "get"):
-                prompt, full = prompt.get("input_ids", prompt), full.get("input_ids", full)
-            if len(prompt) >= L or len(full) <= len(prompt):
-                continue
-            ids = list(full[:L])
-            valid = len(ids)
-            buf_x.append(ids + [pad] * (L - valid))
-            buf_p.append(len(prompt))
-            buf_v.append(valid)
-            added += 1
-            if len(buf_x) == B:
-                yield torch.tensor(buf_x), torch.tensor(buf_p), torch.tensor(buf_v)
-                buf_x, buf_p, buf_v = [], [], []
-                yielded += 1
-        if added == 0 or (yielded == 0 and pass_n >= 1):
-            raise RuntimeError(f"{dataset}/{split}: usable rows can't fill one batch (added {added}, yielded {yielded})")
-        pass_n += 1
+    x0 = torch.full((B, L), pad, dtype=torch.long)
+    plen = torch.zeros(B, dtype=torch.long)
+    vlen = torch.zeros(B, dtype=torch.long)
+    fill = usable = batches = passes = 0
+    for item in _chat_rows(dataset, split, tokenizer, L, seed, streaming):
+        if item is None:  # end of a pass
+            if usable == 0 or (batches == 0 and passes >= 1):
+                raise RuntimeError(f"{dataset}/{split}: not enough usable rows for a batch of {B} "
+                                   f"({usable} usable rows, {batches} batches in pass {passes})")
+            usable = batches = 0
+            passes += 1
+            continue
+        ids, n_prompt = item
+        x0[fill].fill_(pad)
+        x0[fill, : len(ids)] = torch.tensor(ids)
+        plen[fill], vlen[fill] = n_prompt, len(ids)
+        fill += 1
+        usable += 1
+        if fill == B:
+            yield x0.clone(), plen.clone(), vlen.clone()
+            fill = 0
+            batches += 1
 
 
 def train(model, batches, *, block: int, mask_id: int, steps: int, lr: float, device: str, log_every: int = 10,

@@ -2,6 +2,7 @@
 checkpointing changes nothing but memory (mirrors tests/test_equivalence.py:50-121 of the
 reference)."""
 
+import pytest
 import torch
 
 from dllm_qwen38_b200.config import preset
@@ -87,3 +88,69 @@ def test_trained_tiny_model_decodes_the_rule():
     ev = synthetic_eval(m, block=8, mask_id=255, vocab=255, seed=0, threshold=0.9, n_prompts=4, n_blocks=2)
     assert ev["tokens_per_forward"] >= 1.0
     assert ev["generated"] == 4 * 16
+
+
+class _FakeTok:
+    """Chat template = role markers + one token per character; pad id 0."""
+
+    pad_token_id = 0
+
+    def apply_chat_template(self, msgs, tokenize=True, add_generation_prompt=False):
+        ids = []
+        for m in msgs:
+            ids += [1 if m["role"] == "user" else 2] + [3 + (ord(c) % 50) for c in m["content"]]
+        if add_generation_prompt:
+            ids.append(2)
+        return {"input_ids": ids}
+
+
+def _fake_datasets(monkeypatch, rows):
+    import sys
+    import types
+
+    mod = types.ModuleType("datasets")
+
+    class _DS(list):
+        def shuffle(self, seed, buffer_size):
+            g = torch.Generator().manual_seed(seed)
+            return _DS(self[i] for i in torch.randperm(len(self), generator=g).tolist())
+
+    mod.load_dataset = lambda name, cfg, split, streaming: _DS(rows)
+    monkeypatch.setitem(sys.modules, "datasets", mod)
+
+
+def test_chat_batches_normalise_rows_pad_and_cycle(monkeypatch):
+    from dllm_qwen38_b200.train.single import _messages, chat_batches
+
+    rows = [
+        {"messages": [{"role": "user", "content": "hi"}, {"role": "assistant", "content": "yo"}]},
+        {"input": "[{'role': 'user', 'content': 'abc'}]", "output": "d"},  # Nemotron literal list
+        {"input": "plain", "output": "ok"},
+        {"input": "[{'role': 'user', broken", "output": "x"},  # unparsable literal: dropped
+        {"input": "q" * 40, "output": "a"},  # prompt longer than L: dropped
+        {"other": 1},  # unknown shape: dropped
+    ]
+    assert _messages(rows[3]) is None and _messages(rows[5]) is None
+    assert _messages(rows[2]) == [{"role": "user", "content": "plain"}, {"role": "assistant", "content": "ok"}]
+    _fake_datasets(monkeypatch, rows)
+    it = chat_batches("some/chat", "train", _FakeTok(), B=2, L=16, block=4, seed=0)
+    seen = []
+    for _ in range(4):  # 3 usable rows per pass: batches straddle passes
+        x0, pl, vl = next(it)
+        assert x0.shape == (2, 16)
+        for r in range(2):
+            assert int(pl[r]) < int(vl[r]) <= 16
+            assert bool((x0[r, int(vl[r]):] == 0).all())  # right padding
+            seen.append(int(vl[r]))
+    assert len(set(seen)) > 1
+
+
+def test_chat_batches_stop_when_the_split_cannot_fill_a_batch(monkeypatch):
+    from dllm_qwen38_b200.train.single import chat_batches
+
+    _fake_datasets(monkeypatch, [{"input": "u", "output": "v"}])
+    with pytest.raises(RuntimeError):
+        next(chat_batches("x", "train", _FakeTok(), B=4, L=16, block=4, seed=0))
+    _fake_datasets(monkeypatch, [{"other": 1}])
+    with pytest.raises(RuntimeError):
+        next(chat_batches("x", "train", _FakeTok(), B=1, L=16, block=4, seed=0))

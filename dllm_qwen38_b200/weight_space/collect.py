@@ -1,23 +1,23 @@
 """Collect completed launched runs under an explicit comparison plan into one verified bundle
-(the reference's `tools/weight-space/collect.py` role; no inference, no regrading).
+(the role of the reference's `tools/weight-space/collect.py`; no inference, no regrading).
 
     python -m dllm_qwen38_b200.weight_space.collect PLAN.json --output BUNDLE.json
 
 PLAN: {"qualification": str, "conditions": [{"name", "run": RUN_DIR relative to the plan}],
        "paired": [[baseline, candidate], ...], "no_op": [[baseline, candidate], ...]}
-Each run must be completed with its server stopped; its launch config and manifest must agree
-on the model digest and backend; its dataset must still hash to the manifest's digest; its
-results must be the manifest's full case list in order; its stored summary must equal the one
-recomputed from the results. Paired runs must share the scorer revision and the engine identity
-and arguments. Every file read is hashed, and re-hashed at the end: a run that changes while it
-is collected fails the collection.
+
+A bundle is only as good as the runs under it, so each run is admitted by `admit_run`, which
+fails on the first of these it finds: the run did not complete or its server is still up; the
+launch configuration and the manifest name different models or backends; the dataset moved or
+changed; the results are not the manifest's full case list in order; the stored summary is not
+the one the results give. Paired runs must also share the scorer revision and the engine's
+identity and arguments. Every file the collector reads goes through one `Ledger` that records its
+digest; the ledger is checked again at the end, so a run that changes during collection fails it.
 """
 
 from __future__ import annotations
 
 import argparse
-import contextlib
-import io
 import json
 import math
 import pathlib
@@ -25,83 +25,114 @@ import pathlib
 from . import bench
 from .common import digest, read_jsonl, write_new
 
-FILES = ("manifest.json", "launch.json", "process-status.json", "results.jsonl", "summary.json")
+RUN_FILES = ("manifest.json", "launch.json", "process-status.json", "results.jsonl", "summary.json")
 ENGINE_KEYS = ("tokenizer", "block", "threshold", "sub_block", "n_ctx", "backend_commit")
+LIMITATIONS = ["stored grades and timings are aggregated; no new inference or regrading",
+               "model files are not re-hashed by the collector (the launcher checked them)",
+               "small or selected development subsets do not establish a held-out improvement"]
+
+
+class Ledger:
+    """Digests of every file read, for the end-of-collection re-check."""
+
+    def __init__(self):
+        self.seen = {}
+
+    def note(self, path, expected: str | None = None) -> str:
+        h = digest(path)
+        if expected is not None and h != expected:
+            raise ValueError(f"{path}: checksum differs from the manifest's")
+        self.seen[pathlib.Path(path)] = h
+        return h
+
+    def verify(self) -> None:
+        changed = [str(p) for p, h in self.seen.items() if digest(p) != h]
+        if changed:
+            raise ValueError(f"a run changed while it was being collected: {changed[:3]}")
+
+
+def _same_summary(stored: dict, recomputed: dict) -> str | None:
+    """The first summary key whose stored value disagrees with the recomputed one (floats to a
+    relative 1e-10 / absolute 1e-8), or None."""
+    for k, v in recomputed.items():
+        s = stored.get(k)
+        ok = (isinstance(s, (int, float)) and math.isclose(v, s, rel_tol=1e-10, abs_tol=1e-8)) \
+            if isinstance(v, float) else s == v
+        if not ok:
+            return k
+    return None
+
+
+def admit_run(name: str, root: pathlib.Path, ledger: Ledger) -> dict:
+    """Verify one run directory and return its bundle entry plus what the pairing needs."""
+    files = {f: root / f for f in RUN_FILES}
+    hashes = {f: ledger.note(p) for f, p in files.items()}
+    status = json.loads(files["process-status.json"].read_text())
+    if not (status.get("state") == "completed" and status.get("engine_stopped")
+            and type(status.get("engine_exit_code")) is int):
+        raise ValueError(f"{name}: run not completed with its server stopped")
+    ident = json.loads(files["manifest.json"].read_text())["identity"]
+    launch = json.loads(files["launch.json"].read_text())
+    cfg = launch["config"]
+    if not launch.get("engine_sha256") or (cfg.get("model_sha256"), cfg.get("backend_commit")) != (
+            ident["model_sha256"], ident["backend_commit"]):
+        raise ValueError(f"{name}: launch and manifest provenance disagree")
+    data = pathlib.Path(cfg["data"])
+    if not data.is_absolute():
+        raise ValueError(f"{name}: dataset path not absolute")
+    try:
+        ledger.note(data, ident["data_sha256"])
+    except ValueError:
+        raise ValueError(f"{name}: dataset checksum changed") from None
+    rows = read_jsonl(files["results.jsonl"])
+    if not rows or [r["id"] for r in rows] != ident["case_ids"]:
+        raise ValueError(f"{name}: incomplete or reordered results")
+    recomputed = bench.summary(rows)
+    bad = _same_summary(json.loads(files["summary.json"].read_text()), recomputed)
+    if bad is not None:
+        raise ValueError(f"{name}: stored summary differs at {bad}")
+    if not ident.get("bench_sha256"):
+        raise ValueError(f"{name}: scorer revision missing")
+    entry = {"identity": ident, "summary": recomputed, "artifact_sha256": hashes,
+             "engine": {"engine_sha256": launch["engine_sha256"], **{k: cfg.get(k) for k in ENGINE_KEYS}},
+             "engine_exit_code": status["engine_exit_code"], "engine_stopped": True}
+    return {"entry": entry, "root": root, "rows": rows}
 
 
 def collect(plan_path) -> dict:
     plan_path = pathlib.Path(plan_path).resolve()
     plan = json.loads(plan_path.read_text())
-    runs, ids, launches, records, roots, frozen = {}, {}, {}, {}, {}, {}
-    for item in plan["conditions"]:
-        name = item["name"]
-        if name in runs:
-            raise ValueError(f"duplicate condition {name}")
-        root = (plan_path.parent / item["run"]).resolve()
-        paths = [root / f for f in FILES]
-        hashes = {p.name: digest(p) for p in paths}
-        proc = json.loads(paths[2].read_text())
-        if proc.get("state") != "completed" or not proc.get("engine_stopped") or type(
-                proc.get("engine_exit_code")) is not int:
-            raise ValueError(f"{name}: run not completed with its server stopped")
-        ident = json.loads(paths[0].read_text())["identity"]
-        launch = json.loads(paths[1].read_text())
-        lcfg = launch["config"]
-        if (lcfg.get("model_sha256") != ident["model_sha256"] or lcfg.get("backend_commit") != ident["backend_commit"]
-                or not launch.get("engine_sha256")):
-            raise ValueError(f"{name}: launch and manifest provenance disagree")
-        data = pathlib.Path(lcfg["data"])
-        if not data.is_absolute() or digest(data) != ident["data_sha256"]:
-            raise ValueError(f"{name}: dataset path not absolute or its checksum changed")
-        frozen[data] = ident["data_sha256"]
-        rows = read_jsonl(paths[3])
-        if not rows or [r["id"] for r in rows] != ident["case_ids"]:
-            raise ValueError(f"{name}: incomplete or reordered results")
-        got, stored = bench.summary(rows), json.loads(paths[4].read_text())
-        for k, v in got.items():
-            sv = stored.get(k)
-            if isinstance(v, float):
-                if not isinstance(sv, (int, float)) or not math.isclose(v, sv, rel_tol=1e-10, abs_tol=1e-8):
-                    raise ValueError(f"{name}: stored summary differs at {k}")
-            elif sv != v:
-                raise ValueError(f"{name}: stored summary differs at {k}")
-        if not ident.get("bench_sha256"):
-            raise ValueError(f"{name}: scorer revision missing")
-        roots[name], ids[name], launches[name], records[name] = root, ident, launch, rows
-        runs[name] = {"identity": ident, "summary": got, "artifact_sha256": hashes,
-                      "engine": {"engine_sha256": launch["engine_sha256"],
-                                 **{k: lcfg.get(k) for k in ENGINE_KEYS}},
-                      "engine_exit_code": proc["engine_exit_code"], "engine_stopped": True}
-        frozen.update({p: hashes[p.name] for p in paths})
+    ledger = Ledger()
+    admitted = {}
+    for cond in plan["conditions"]:
+        if cond["name"] in admitted:
+            raise ValueError(f"duplicate condition {cond['name']}")
+        admitted[cond["name"]] = admit_run(cond["name"], (plan_path.parent / cond["run"]).resolve(), ledger)
+    entries = {k: v["entry"] for k, v in admitted.items()}
     paired = []
-    for left, right in plan["paired"]:
-        if ids[left]["bench_sha256"] != ids[right]["bench_sha256"]:
-            raise ValueError(f"{left}/{right}: scorer revisions differ")
-        if runs[left]["engine"] != runs[right]["engine"]:
-            raise ValueError(f"{left}/{right}: engine identity or arguments differ")
-        buf = io.StringIO()
-        with contextlib.redirect_stdout(buf):
-            res = bench.compare(argparse.Namespace(baseline=str(roots[left]), candidate=str(roots[right]), output=None))
-        paired.append({"baseline": left, "candidate": right, "result": res})
+    for base, cand in plan["paired"]:
+        if entries[base]["identity"]["bench_sha256"] != entries[cand]["identity"]["bench_sha256"]:
+            raise ValueError(f"{base}/{cand}: scorer revisions differ")
+        if entries[base]["engine"] != entries[cand]["engine"]:
+            raise ValueError(f"{base}/{cand}: engine identity or arguments differ")
+        paired.append({"baseline": base, "candidate": cand,
+                       "result": bench.compare_runs(admitted[base]["root"], admitted[cand]["root"])})
     no_ops = []
-    for left, right in plan.get("no_op", []):
-        if [left, right] not in plan["paired"]:
+    for base, cand in plan.get("no_op", []):
+        if [base, cand] not in plan["paired"]:
             raise ValueError("a no-op pair must also be a paired comparison")
-        if ids[left]["case_ids"] != ids[right]["case_ids"]:
+        bi, ci = entries[base]["identity"], entries[cand]["identity"]
+        if bi["case_ids"] != ci["case_ids"]:
             raise ValueError("no-op case lists differ")
-        a, b = records[left], records[right]
-        no_ops.append({"baseline": left, "candidate": right,
-                       "checkpoint_hash_equal": ids[left]["model_sha256"] == ids[right]["model_sha256"],
-                       "exact_response_text_matches": sum(x["response"]["content"] == y["response"]["content"]
-                                                          for x, y in zip(a, b)), "n": len(a)})
-    if any(digest(p) != h for p, h in frozen.items()):
-        raise ValueError("a run changed while it was being collected")
+        same_text = sum(x["response"]["content"] == y["response"]["content"]
+                        for x, y in zip(admitted[base]["rows"], admitted[cand]["rows"]))
+        no_ops.append({"baseline": base, "candidate": cand,
+                       "checkpoint_hash_equal": bi["model_sha256"] == ci["model_sha256"],
+                       "exact_response_text_matches": same_text, "n": len(admitted[base]["rows"])})
+    ledger.verify()
     return {"schema": "bdllm.ws.bundle/v1", "plan_sha256": digest(plan_path), "collector_sha256": digest(__file__),
-            "comparison_code_sha256": digest(bench.__file__), "qualification": plan["qualification"], "runs": runs,
-            "paired": paired, "no_op": no_ops,
-            "limitations": ["stored grades and timings are aggregated; no new inference or regrading",
-                            "model files are not re-hashed by the collector (the launcher checked them)",
-                            "small or selected development subsets do not establish a held-out improvement"]}
+            "comparison_code_sha256": digest(bench.__file__), "qualification": plan["qualification"], "runs": entries,
+            "paired": paired, "no_op": no_ops, "limitations": LIMITATIONS}
 
 
 def main(argv=None) -> int:

@@ -125,6 +125,23 @@ def op_gdn(a):
     return fn, flops, byts
 
 
+def op_gdn_fwd(a):
+    """forward only of the state-fork delta rule (the tcgen05 kernels when eligible; BDLLM_GDN_TC=0
+    selects the mma.sync kernels)."""
+    q, k, v, lg, beta = _gdn_inputs(a)
+    from ..ops import cuda as Cu
+
+    def fn():
+        with torch.no_grad():
+            Cu.gdn_core_blockdiff(q, k, v, lg, beta, a.L, a.block, 64, "fork")
+
+    B, L, Hv, D, C = a.B, a.L, 48, 128, a.block
+    chunks = B * (2 * L // C)
+    flops = chunks * Hv * (6.0 * C * D * D + 10.0 * C * C * D)
+    byts = (q.numel() + k.numel() + v.numel()) * 2 + v.numel() * 2 + B * (L // C) * Hv * D * D * 4
+    return fn, flops, byts
+
+
 def op_attn(a):
     from ..ops import cuda as Cu
 
@@ -332,7 +349,7 @@ def op_embed(a):
     return fn, 1.0 * ids.numel() * D, ids.numel() * D * (2 + 2 + 2 + 8)
 
 
-OPS = {"gemm": op_gemm, "gdn": op_gdn, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
+OPS = {"gemm": op_gemm, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
        "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed,
        "adamw": op_adamw}
 

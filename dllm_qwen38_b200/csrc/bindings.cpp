@@ -4,7 +4,8 @@
 namespace bdllm {
 void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
           int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
-          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha);
+          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha,
+          const c10::optional<at::Tensor>& alpha_t);
 at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu);
 at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode);
 std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
@@ -28,6 +29,10 @@ std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tenso
                                          const at::Tensor& cs, const at::Tensor& sn, double eps);
 std::vector<at::Tensor> gdn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                 const at::Tensor& beta, int64_t L, int64_t C, bool concat);
+bool gdn_tc_eligible(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L, int64_t C,
+                     bool concat);
+std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                                   const at::Tensor& beta, int64_t L);
 std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                 const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S_in, int64_t L,
                                 int64_t C, bool concat);
@@ -101,7 +106,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &bdllm::gemm, "tcgen05 bf16 GEMM with fused epilogues", py::arg("a"), py::arg("a_mn"),
         py::arg("lda"), py::arg("b"), py::arg("b_mn"), py::arg("ldb"), py::arg("M"), py::arg("N"), py::arg("K"),
         py::arg("c"), py::arg("ldc"), py::arg("epi"), py::arg("r") = c10::nullopt, py::arg("ldr") = 0,
-        py::arg("gu") = c10::nullopt, py::arg("bn") = 256, py::arg("alpha") = 1.0);
+        py::arg("gu") = c10::nullopt, py::arg("bn") = 256, py::arg("alpha") = 1.0,
+        py::arg("alpha_t") = c10::nullopt);
   m.def("dswiglu", &bdllm::dswiglu);
   m.def("conv_fwd", &bdllm::conv_fwd);
   m.def("conv_bwd", &bdllm::conv_bwd);
@@ -110,6 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sumsq_", &bdllm::sumsq_, "sq += ||x||^2 (optionally writing x as fp32)", py::arg("x"), py::arg("sq"),
         py::arg("dst") = c10::nullopt);
   m.def("gdn_fwd", &bdllm::gdn_fwd, "state-fork chunked gated delta rule forward");
+  m.def("gdn_tc_eligible", &bdllm::gdn_tc_eligible, "whether the tcgen05 GDN forward takes this problem");
+  m.def("gdn_fwd_tc", &bdllm::gdn_fwd_tc, "state-fork GDN forward on tcgen05 / TMEM / TMA (head dim 128, chunk 32)");
   m.def("gdn_bwd", &bdllm::gdn_bwd, "state-fork chunked gated delta rule backward");
   m.def("attn_fwd", &bdllm::attn_fwd, "complementary-mask flash attention forward");
   m.def("attn_bwd", &bdllm::attn_bwd, "complementary-mask flash attention backward");

@@ -85,6 +85,7 @@ struct GemmArgs {
   // tile raster: groups of raster_g tile rows along M (raster_n = 0) or tile columns along N
   // (raster_n = 1); 0 = 8 along M
   int raster_g, raster_n;
+  const float* alpha_dev;  // optional device scalar multiplying alpha (read once per tile)
 };
 
 __device__ __forceinline__ void tp_st_release(unsigned* p, unsigned v) {
@@ -221,13 +222,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t t_r
                                               int64_t split_off, int t, int mn_tiles, int ksplit, int lane) {
   constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   (void)lane;
+  const float alpha = args.alpha_dev != nullptr ? args.alpha * __ldg(args.alpha_dev) : args.alpha;
 #pragma unroll 1
   for (int c = 0; c < BN_OUT / 32; ++c) {
     float v[32];
     tmem_ld32(t_row + c * 32, v);
-    if (args.alpha != 1.f) {
+    if (alpha != 1.f) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
+      for (int j = 0; j < 32; ++j) v[j] *= alpha;
     }
     const int col0 = n0 + c * 32;
     if (row_ok) (void)BDLLM_CHECK(all_finite(v, 32), row, col0);  // sentinel: non-finite accumulator
@@ -1068,13 +1070,20 @@ struct AgHook {
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
                       int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
                       const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
-                      double alpha, const TpHook* tp, const AgHook* ag = nullptr);
+                      double alpha, const TpHook* tp, const AgHook* ag = nullptr, const float* alpha_dev = nullptr);
 
 void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb, int64_t M,
           int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi, const c10::optional<at::Tensor>& r,
-          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha) {
+          int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha,
+          const c10::optional<at::Tensor>& alpha_t) {
   TORCH_CHECK(epi != EPI_PEER_F32, "gemm: the peer epilogue goes through gemm_tp");
-  gemm_impl(a, a_mn, lda, b, b_mn, ldb, M, N, K, c, ldc, epi, r, ldr, gu, bn, alpha, nullptr);
+  const float* ad = nullptr;
+  if (alpha_t.has_value()) {
+    TORCH_CHECK(alpha_t->is_cuda() && alpha_t->scalar_type() == at::kFloat && alpha_t->numel() == 1,
+                "gemm: alpha_t must be one fp32 element on the device");
+    ad = alpha_t->data_ptr<float>();
+  }
+  gemm_impl(a, a_mn, lda, b, b_mn, ldb, M, N, K, c, ldc, epi, r, ldr, gu, bn, alpha, nullptr, nullptr, ad);
 }
 
 // Split-K GEMM for skinny problems (few output tiles): out[M, N] (bf16) = a b^T (+ residual), both
@@ -1254,7 +1263,7 @@ void gemm_ag(const at::Tensor& a, const at::Tensor& w, at::Tensor& c, int64_t ep
 static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool b_mn, int64_t ldb,
                       int64_t M, int64_t N, int64_t K, at::Tensor& c, int64_t ldc, int64_t epi,
                       const c10::optional<at::Tensor>& r, int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn,
-                      double alpha, const TpHook* tp, const AgHook* ag) {
+                      double alpha, const TpHook* tp, const AgHook* ag, const float* alpha_dev) {
   GTRACE("enter");
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors expected");
   bind_context(a.get_device());
@@ -1267,6 +1276,7 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   L->args = GemmArgs{(int)M, (int)N, (int)K, c.data_ptr(), (int)ldc, nullptr, (int)ldr, nullptr, 0, error_word_ptr(),
                      (float)alpha};
   GemmArgs& args = L->args;
+  args.alpha_dev = alpha_dev;
   if (epi == EPI_ADD_BF16) {
     TORCH_CHECK(r.has_value(), "EPI_ADD_BF16 needs a residual");
     args.R = r->data_ptr();

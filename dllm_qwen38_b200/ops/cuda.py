@@ -93,8 +93,10 @@ def gemm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
 
 
 def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
-            residual: torch.Tensor | None = None, alpha: float = 1.0) -> torch.Tensor:
-    """out[M, N] = a[M, K] @ b[K, N] (b MN-major: row-major [K, N])."""
+            residual: torch.Tensor | None = None, alpha: float = 1.0,
+            alpha_t: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M, N] = a[M, K] @ b[K, N] (b MN-major: row-major [K, N]). alpha_t: a one-element fp32
+    device tensor that also scales the product (read by the epilogue: no host synchronisation)."""
     a2, b2 = _c2(a), _c2(b)
     M, K = a2.shape
     N = b2.shape[1]
@@ -103,13 +105,13 @@ def gemm_nn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
     epi = EPI_ADD_BF16 if residual is not None else (EPI_F32 if out.dtype == torch.float32 else EPI_BF16)
     r = _c2(residual) if residual is not None else None
     _C.gemm(a2, False, a2.stride(0), b2, True, b2.stride(0), M, N, K, out, out.stride(0), epi,
-            r, r.stride(0) if r is not None else 0, None, 256, alpha)
+            r, r.stride(0) if r is not None else 0, None, 256, alpha, alpha_t)
     _count()
     return out
 
 
 def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, out_dtype=torch.float32,
-            accumulate: bool = False, alpha: float = 1.0) -> torch.Tensor:
+            accumulate: bool = False, alpha: float = 1.0, alpha_t: torch.Tensor | None = None) -> torch.Tensor:
     """out[M, N] = a[K, M]^T @ b[K, N] (both MN-major) -- the weight-gradient GEMM."""
     a2, b2 = _c2(a), _c2(b)
     K, M = a2.shape
@@ -119,25 +121,27 @@ def gemm_tn(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, o
             M, N, device=a.device, dtype=out_dtype)
     epi = EPI_ACC_F32 if accumulate else (EPI_F32 if out.dtype == torch.float32 else EPI_BF16)
     _C.gemm(a2, True, a2.stride(0), b2, True, b2.stride(0), M, N, K, out, out.stride(0), epi, None, 0, None, 256,
-            alpha)
+            alpha, alpha_t)
     _count()
     return out
 
 
-def wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor):
-    """Weight gradient dy^T x for leaf weight `w`. When `w.grad` is a preset bf16 buffer (the
-    sharded engine's flat gradient views) the GEMM epilogue adds into it in place (one rounding,
-    no fp32 temporary) and None is returned; otherwise the gradient tensor."""
+def wgrad(dy2: torch.Tensor, x2: torch.Tensor, w: torch.Tensor, alpha_t: torch.Tensor | None = None):
+    """Weight gradient (alpha_t *) dy^T x for leaf weight `w`. When `w.grad` is a preset bf16
+    buffer (the sharded engine's flat gradient views) the GEMM epilogue adds into it in place (one
+    rounding, no fp32 temporary) and None is returned; otherwise the gradient tensor."""
     g = w.grad if (w.is_leaf and w.requires_grad) else None
     if g is not None and g.dtype == torch.bfloat16 and g.shape == w.shape and g.stride(-1) == 1 \
             and g.dim() == 2 and g.stride(0) % 8 == 0 and g.data_ptr() % 16 == 0:
         K, M = dy2.shape
         N = x2.shape[1]
         _C.gemm(dy2, True, dy2.stride(0), x2, True, x2.stride(0), M, N, K, g, g.stride(0), EPI_ADD_BF16, g,
-                g.stride(0), None, 256, 1.0)
+                g.stride(0), None, 256, 1.0, alpha_t)
         _count()
         return None
-    return gemm_tn(dy2, x2, out_dtype=torch.float32).to(w.dtype)
+    if w.dtype == torch.bfloat16:  # bf16 result straight from the epilogue
+        return gemm_tn(dy2, x2, out_dtype=torch.bfloat16, alpha_t=alpha_t)
+    return gemm_tn(dy2, x2, out_dtype=torch.float32, alpha_t=alpha_t).to(w.dtype)
 
 
 def gemm_swiglu(x: torch.Tensor, w_gate_up: torch.Tensor, F: int, store_gu: bool):
@@ -335,8 +339,10 @@ def conv_blockdiff(raw, w, L, block, mode):
 
 class _MaskedCE(torch.autograd.Function):
     """sum_rows CE(h W^T, t). Forward: logits by GEMM (bf16, [n, V]), one row kernel writes the
-    per-row loss and overwrites the logits with (softmax - onehot). Backward: dh = g * dlogits W,
-    dW = g * dlogits^T h (the GEMM epilogue applies g)."""
+    per-row loss and overwrites the logits with (softmax - onehot), which the backward keeps as
+    dlogits (n x V bf16: 2 GiB at n = 4096, V = 248,320; the cost of not recomputing the logits
+    GEMM). Backward: dh = g * dlogits W, dW = g * dlogits^T h; g stays a device scalar that the
+    GEMM epilogues read, and dW is added in place into a preset bf16 gradient when there is one."""
 
     @staticmethod
     def forward(ctx, h, w, tgt):
@@ -350,9 +356,11 @@ class _MaskedCE(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         h2, w, dlogits = ctx.saved_tensors
-        gs = float(g)
-        dh = gemm_nn(dlogits, w, alpha=gs) if ctx.needs_input_grad[0] else None
-        dw = gemm_tn(dlogits, h2, out_dtype=torch.float32, alpha=gs).to(w.dtype) if ctx.needs_input_grad[1] else None
+        # the upstream scale stays on the device: both GEMM epilogues read it (no host sync)
+        gt = g.detach().float().reshape(1).contiguous()
+        dh = gemm_nn(dlogits, w, alpha_t=gt) if ctx.needs_input_grad[0] else None
+        # dW accumulates into a preset bf16 gradient buffer in place when the engine set one
+        dw = wgrad(dlogits, h2, w, alpha_t=gt) if ctx.needs_input_grad[1] else None
         return dh, dw, None
 
 
@@ -423,8 +431,12 @@ class _GDNCore(torch.autograd.Function):
         if saved is not None:
             o, S_in = saved
         else:
-            o, S_in, _ = _C.gdn_fwd(q, k, v, gf, bf, L, block, concat)
-            _count(3)
+            if _C.gdn_tc_eligible(q, k, v, L, block, concat):  # tcgen05 / TMEM / TMA forward
+                o, S_in = _C.gdn_fwd_tc(q, k, v, gf, bf, L)
+                _count(2)
+            else:
+                o, S_in, _ = _C.gdn_fwd(q, k, v, gf, bf, L, block, concat)
+                _count(3)
             ActStore.put(o, S_in)
         ctx.save_for_backward(q, k, v, gf, bf, S_in)
         ctx.cfg = (L, block, concat)

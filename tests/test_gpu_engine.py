@@ -61,6 +61,6 @@ def test_saved_gemm_outputs_match_recomputation():
         Cu.ActStore.gemms = False
     for lx, sx in ((la, sa), (lc, sc)):
         assert lx[0] == lb[0], (lx, lb)  # the first step's loss precedes any update
-        assert max(abs(a - b) for a, b in zip(lx, lb)) < 1e-5 * max(1.0, abs(lx[0]))
+        assert max(abs(a - b) for a, b in zip(lx, lb)) < 1e-4 * max(1.0, abs(lx[0]))
         assert max(float((sx[k] - sb[k]).abs().max()) for k in sx) < 1e-3
 

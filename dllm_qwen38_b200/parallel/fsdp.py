@@ -245,8 +245,10 @@ class FSDPEngine:
         # first n layers, or "auto": as many layers as fit in free memory, decided at the first step
         # from the row count
         self.save_gemms = os.environ.get("BDLLM_SAVE_GEMMS", "auto") if self.save_cores else "0"
-        if self.save_gemms not in ("0", "auto"):
-            self.fused_ag = False  # the backward's gathers must not wait for GEMMs that are not rerun
+        # which pass is gathering: in the backward, a layer whose GEMM outputs were kept reruns none
+        # of its GEMMs, so its gather cannot ride on one and takes the prefetched peer gather instead
+        self.phase = "fwd"
+        self.layer_index = {id(u): j for j, u in enumerate(self.layers)}
         if self.peer is not None:  # every shard written before any peer reads one
             torch.cuda.synchronize(self.device)
             dist.barrier()
@@ -280,10 +282,19 @@ class FSDPEngine:
             unit._ag_plan = plan
         return plan
 
+    def _fused_for(self, unit: Unit) -> bool:
+        """Gather `unit` inside its first GEMM? Every layer in the forward (it runs all its GEMMs);
+        in the backward only layers whose GEMM outputs were not kept (their recomputation reruns
+        the projection GEMMs)."""
+        if not self.fused_ag or self._fused_plan(unit) is None:
+            return False
+        j = self.layer_index.get(id(unit))
+        return not (self.phase == "bwd" and j is not None and self.gemm_saved(j))
+
     def gather(self, unit: Unit, prefetch: bool = False) -> torch.Tensor:
         if self.world == 1:  # the shard is the whole unit
             return unit.p
-        if self.fused_ag and self._fused_plan(unit) is not None:
+        if self._fused_for(unit):
             return self._gather_fused(unit, prefetch)
         for i in range(2):
             if self.owner[i] is unit:
@@ -467,6 +478,7 @@ class FSDPEngine:
         if probe:
             torch.cuda.synchronize(self.device)
             torch.cuda.reset_peak_memory_stats(self.device)
+        self.phase = "fwd"
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
         self.table_grad.zero_()
@@ -521,9 +533,6 @@ class FSDPEngine:
             print(f"[fsdp] GEMM outputs across checkpointing: kept for {n} of {len(per)} layers "
                   f"({used / 2**30:.1f} of {sum(per) / 2**30:.1f} GiB; free {float(free[0]) / 2**30:.1f} GiB)",
                   file=sys.stderr, flush=True)
-        if n and self.fused_ag:
-            # the backward's gathers must not wait for GEMMs that the saved outputs replace
-            self.fused_ag = False
 
     @torch.no_grad()
     def _optimizer_step(self):
@@ -732,6 +741,7 @@ class _HeadFn(torch.autograd.Function):
     def backward(ctx, g):
         engine, n_global, n_local = ctx.meta
         ht, m, x0 = ctx.saved_tensors
+        engine.phase = "bwd"  # the head's backward opens the backward pass
         u = engine.head
         grad = engine.grad_buffer(u)
         buf = engine.gather(u)

@@ -69,6 +69,30 @@ def test_masked_ce_fwd_bwd():
     assert _rel(h.grad, hf.grad) < 2e-2 and _rel(w.grad, wf.grad) < 2e-2
 
 
+def test_masked_ce_full_vocab_preset_grad_and_device_scale():
+    """4096 target rows over the full 248,320-row vocabulary against fp32, with the upstream
+    gradient scale kept on the device and dW added in place into a preset bf16 gradient (the
+    sharded engine's layout: no fp32 [V, D] temporary, no host synchronisation in the backward)."""
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(4)
+    n, D, V = 4096, 256, 248320
+    h = torch.randn(n, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(V, D, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    w.grad = torch.zeros_like(w)  # preset gradient buffer: the CE backward accumulates into it
+    t = torch.randint(0, V, (n,), device="cuda")
+    scale = torch.tensor(1.0 / n, device="cuda")
+    loss = Cu.masked_ce_sum(h, w, t) * scale
+    loss.backward()
+    hf, wf = h.detach().float().requires_grad_(True), w.detach().float().requires_grad_(True)
+    lr = ref.masked_ce_sum(hf, wf, t) / n
+    lr.backward()
+    assert abs(float(loss) - float(lr)) < 1e-2 * float(lr)
+    assert _rel(h.grad, hf.grad) < 2e-2 and _rel(w.grad, wf.grad) < 2e-2
+    m = float((w.grad.float() - wf.grad).abs().max()) / float(wf.grad.abs().max())
+    assert m < 3e-2, m
+
+
 def test_adamw_matches_reference_update():
     from dllm_qwen38_b200.train.optim import MasterAdamW
 

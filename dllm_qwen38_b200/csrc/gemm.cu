@@ -716,6 +716,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int m0 = tm * 256 + (int)crank * 128;
       const int n0 = tn * C_::BN_OUT;
       const int bn0 = (EPI == EPI_SWIGLU) ? (crank ? args.N + n0 : n0) : n0 + (int)crank * 128;
+      if constexpr (!B_MN) {
+        if (args.ag_nchunks > 0) {  // fused all-gather: this CTA's 128 weight rows must have landed
+          const int64_t rb = (int64_t)args.K * 2;
+          const int64_t rows_total = (EPI == EPI_SWIGLU) ? 2 * (int64_t)args.N : (int64_t)args.N;
+          const int64_t r1 = min((int64_t)bn0 + 128, rows_total);
+          if (r1 > bn0 && !ag_wait_range(args, args.ag_b_off + (int64_t)bn0 * rb, args.ag_b_off + r1 * rb, abort_flag)) {
+            ok = false;
+            break;
+          }
+        }
+      }
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
@@ -817,6 +828,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
       if (lane == 0) arrive_remote(tempty0 + acc * 8);
     }
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------------- fused all-gather copies
+    if (args.ag_nchunks > 0) ag_copy_warp(args, lane, abort_flag);
   }
   tc_fence_before();
   __syncthreads();
@@ -908,14 +922,17 @@ static int num_sms() {
 }
 
 // CTA pairs: for GEMMs large enough to give every pair a few 256 x 256 tiles, any operand majors
-// (SwiGLU: K-major only) (BDLLM_GEMM_PAIR=0 keeps the one-CTA kernel)
+// (SwiGLU: K-major only), with or without the fused all-gather (warps 6-7 of both CTAs copy the
+// weight's chunks; each CTA's producer waits for its own 128 weight rows) (BDLLM_GEMM_PAIR=0 keeps
+// the one-CTA kernel)
 static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, const void* tp, const void* ag) {
   static int env = -1;
   if (env < 0) {
     const char* e = getenv("BDLLM_GEMM_PAIR");
     env = (e == nullptr || e[0] != '0') ? 1 : 0;
   }
-  if (!env || tp != nullptr || ag != nullptr) return false;
+  if (!env || tp != nullptr) return false;
+  if (ag != nullptr && b_mn) return false;  // the fused all-gather waits on K-major weight rows
   if (epi == EPI_SWIGLU && (a_mn || b_mn)) return false;
   if (!(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_ADD_BF16 || epi == EPI_SWIGLU)) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256));

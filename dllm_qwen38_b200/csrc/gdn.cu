@@ -27,6 +27,8 @@
 #include "common.cuh"
 
 namespace bdllm {
+void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
+                   uint32_t box_outer);
 namespace gdn {
 
 constexpr int NT = 512;
@@ -1111,6 +1113,9 @@ __global__ void __launch_bounds__(NT) bwd_recur_kernel(Args a, int has_inj) {
     }
 }
 
+// ------------------------------------------------------------------------------------- tcgen05 backward
+#include "gdn_bwd_tc.cuh"
+
 // ------------------------------------------------------------------------------------- host
 
 template <typename K>
@@ -1295,8 +1300,42 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
     ph = at::zeros({16}, q.options().dtype(at::kLong));
     a.phase = reinterpret_cast<long long*>(ph.data_ptr<int64_t>());
   }
+  // the chunk kernels on tcgen05 (head dim 128, chunk 32, the fork layout; BDLLM_GDN_TC=0 keeps the
+  // mma.sync ones): q, k, v, dO tiles of 32 tokens by TMA
+  static const bool tc_off = getenv("BDLLM_GDN_TC") != nullptr && getenv("BDLLM_GDN_TC")[0] == '0';
+  const bool tc = Dk == 128 && Dv == 128 && !concat && C == 32 && !tc_off && !phases &&
+                  reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0 && a.ldqk % 8 == 0 && a.ldv % 8 == 0;
+  struct alignas(64) TcMaps {
+    CUtensorMap mq, mk, mv, mdo;
+  };
+  static thread_local TcMaps tm;
+  auto chunk_tc = [&](int mode) {
+    void* kargs[7];
+    int* err = error_word_ptr();
+    kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &a, kargs[5] = &mode,
+    kargs[6] = &err;
+    C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(bwd_chunk_tc_kernel), dim3(a.nb, BH),
+                                    dim3(btc::NTH), kargs, btc::L::BYTES, at::cuda::getCurrentCUDAStream()));
+  };
+  if (tc) {
+    static bool attr = false;
+    if (!attr) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(bwd_chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          btc::L::BYTES));
+      attr = true;
+    }
+    const uint64_t rows = (uint64_t)a.B * 2 * L;
+    make_map_bf16(&tm.mq, q.data_ptr(), (uint64_t)a.Hk * Dk, rows, a.ldqk, 64, 32);
+    make_map_bf16(&tm.mk, k.data_ptr(), (uint64_t)a.Hk * Dk, rows, a.ldqk, 64, 32);
+    make_map_bf16(&tm.mv, v.data_ptr(), (uint64_t)a.Hv * Dv, rows, a.ldv, 64, 32);
+    make_map_bf16(&tm.mdo, d.data_ptr(), (uint64_t)a.Hv * Dv, rows, (uint64_t)a.Hv * Dv, 64, 32);
+  }
   if (!concat) {
-    launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
+    if (tc)
+      chunk_tc(0);
+    else
+      launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
     report("noised");
   }
   Args a2 = a;
@@ -1305,7 +1344,10 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
           2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a2,
           a.dS_inj != nullptr ? 1 : 0);
-  launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
+  if (tc)
+    chunk_tc(1);
+  else
+    launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 1);
   report("clean");
   if (want_dS0) return {dq, dk, dv, dg, db, dS0};
   return {dq, dk, dv, dg, db};

@@ -94,3 +94,30 @@ def test_gdn_tc_op_forward_backward_against_autograd():
     assert _rel(gate.grad, gf.grad) < 2e-2, _rel(gate.grad, gf.grad)
     assert _rel(beta.grad, bf.grad) < 2e-2, _rel(beta.grad, bf.grad)
     Cu.check_errors()
+
+
+@pytest.mark.parametrize("B,L,Hk,Hv", [(2, 128, 1, 2), (1, 1024, 16, 48)])
+def test_gdn_tc_backward_matches_fp32_autograd(B, L, Hk, Hv):
+    """The tensor-core backward chunk kernels (noised blocks and clean chunks) through the op, on
+    the 27B head shape at L 1024 and a small batched case, against autograd of the fp32 reference."""
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    mixed, q, k, v, gate, beta = _inputs(B, L, Hk, Hv, seed=L + Hv, grad=True)
+    o = Cu.gdn_core_blockdiff(q, k, v, gate, beta, L, 32, 64, "fork")
+    do = torch.randn_like(o)
+    o.backward(do)
+    Cu.check_errors()
+    mf = mixed.detach().float().requires_grad_(True)
+    gf, bf = gate.detach().clone().requires_grad_(True), beta.detach().clone().requires_grad_(True)
+    D = 128
+    qf = mf[..., : Hk * D].reshape(B, 2 * L, Hk, D)
+    kf = mf[..., Hk * D : 2 * Hk * D].reshape(B, 2 * L, Hk, D)
+    vf = mf[..., 2 * Hk * D :].reshape(B, 2 * L, Hv, D)
+    orf = ref.gdn_core_blockdiff(qf, kf, vf, gf, bf, L, 32, 32, "fork")
+    orf.backward(do.float())
+    for name, got, want in (("q", mixed.grad[..., : Hk * D], mf.grad[..., : Hk * D]),
+                            ("k", mixed.grad[..., Hk * D : 2 * Hk * D], mf.grad[..., Hk * D : 2 * Hk * D]),
+                            ("v", mixed.grad[..., 2 * Hk * D :], mf.grad[..., 2 * Hk * D :]),
+                            ("g", gate.grad, gf.grad), ("beta", beta.grad, bf.grad)):
+        r = _rel(got, want)
+        assert r < 2e-2, (name, r)

@@ -29,6 +29,8 @@
 namespace bdllm {
 void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                    uint32_t box_outer);
+void gdn_bwd_recurrence_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, float* dS_out, float* dVp);
 namespace gdn {
 
 constexpr int NT = 512;
@@ -1303,7 +1305,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   // the chunk kernels on tcgen05 (head dim 128, chunk 32, the fork layout; BDLLM_GDN_TC=0 keeps the
   // mma.sync ones): q, k, v, dO tiles of 32 tokens by TMA
   static const bool tc_off = getenv("BDLLM_GDN_TC") != nullptr && getenv("BDLLM_GDN_TC")[0] == '0';
-  const bool tc = Dk == 128 && Dv == 128 && !concat && C == 32 && !tc_off && !phases &&
+  const bool tc = Dk == 128 && Dv == 128 && !concat && C == 32 && !tc_off &&
                   reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
                   reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0 && a.ldqk % 8 == 0 && a.ldv % 8 == 0;
   struct alignas(64) TcMaps {
@@ -1313,7 +1315,9 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto chunk_tc = [&](int mode) {
     void* kargs[7];
     int* err = error_word_ptr();
-    kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &a, kargs[5] = &mode,
+    Args ac = a;
+    if (mode == 1) ac.phase = a.phase;  // (phase stamps: both launches, like the mma.sync kernels)
+    kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &ac, kargs[5] = &mode,
     kargs[6] = &err;
     C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(bwd_chunk_tc_kernel), dim3(a.nb, BH),
                                     dim3(btc::NTH), kargs, btc::L::BYTES, at::cuda::getCurrentCUDAStream()));
@@ -1331,19 +1335,30 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
     make_map_bf16(&tm.mv, v.data_ptr(), (uint64_t)a.Hv * Dv, rows, a.ldv, 64, 32);
     make_map_bf16(&tm.mdo, d.data_ptr(), (uint64_t)a.Hv * Dv, rows, (uint64_t)a.Hv * Dv, 64, 32);
   }
+  // the sequential part on tcgen05 too (prep tiles of 4 chunks: L a multiple of 128): it adds the
+  // noised blocks' state gradients itself, so their chunk kernel stores none
+  const bool tc_rec = tc && L % 128 == 0 && (int64_t)a.B * 2 * a.Hv * a.nb * C * 4 < ((int64_t)1 << 31);
   if (!concat) {
-    if (tc)
+    if (tc) {
+      float* keep = a.dS_inj;
+      if (tc_rec) a.dS_inj = nullptr;
       chunk_tc(0);
-    else
+      a.dS_inj = keep;
+    } else {
       launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
+    }
     report("noised");
   }
-  Args a2 = a;
-  a2.phase = nullptr;
-  launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a2);
-  launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
-          2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a2,
-          a.dS_inj != nullptr ? 1 : 0);
+  if (tc_rec) {
+    gdn_bwd_recurrence_tc(q, k, v, g, beta, d, L, a.dS_out, a.dVp);
+  } else {
+    Args a2 = a;
+    a2.phase = nullptr;
+    launch(bwd_prep_kernel<Dk, Dv>, dim3(a.nb, BH), Smem<Dk, Dv>::floats, a2);
+    launch2(bwd_recur_kernel<Dk, Dv>, dim3(BH, (Dv + 31) / 32),
+            2 * (3 * 32 * Ld<Dk>::v + 32 * LDC + 32 * 16) + 2 * 32 * LDC + Dk * LDC, a2,
+            a.dS_inj != nullptr ? 1 : 0);
+  }
   if (tc)
     chunk_tc(1);
   else

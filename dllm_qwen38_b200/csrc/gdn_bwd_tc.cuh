@@ -43,7 +43,8 @@ struct L {
   static constexpr int RED = DS + ST;         // fp32 [128][33] reduction buffer
   static constexpr int TB = RED + 128 * 33 * 4;   // fp32 [96][33]: KK rows, P rows, dKK rows (token warp)
   static constexpr int SC = TB + 96 * 33 * 4;     // fp32 scalars per token: gam, beta, E, F, rq, rk, dE, dF, ...
-  static constexpr int BAR = SC + 16 * 32 * 4;
+  static constexpr int PART = SC + 16 * 32 * 4;   // fp32 [3][4 warps][32]: per-warp partials of token sums
+  static constexpr int BAR = PART + 3 * 128 * 4;
   static constexpr int BYTES = BAR + 128 + 1024;
 };
 static_assert(L::BYTES <= 227 * 1024, "gdn bwd tc smem");
@@ -105,6 +106,21 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// Warp transpose-reduce: every lane holds 32 per-token values; after 31 shuffles lane l holds the
+// sum over the warp's lanes of value l.
+__device__ __forceinline__ float fold32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = hi ? v[i] : v[i + o];
+      const float keep = hi ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
 __device__ __forceinline__ uint32_t pk2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -132,6 +148,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   float* red = reinterpret_cast<float*>(sm + L::RED);
   float* tb = reinterpret_cast<float*>(sm + L::TB);  // rows 0-31 KK, 32-63 P, 64-95 dKK
+  float* part = reinterpret_cast<float*>(sm + L::PART);  // [3][4][32]
   float* sc = reinterpret_cast<float*>(sm + L::SC);
   float *sgam = sc, *sbeta = sc + 32, *sE = sc + 64, *sF = sc + 96, *srq = sc + 128, *srk = sc + 160, *sdE = sc + 192,
         *sdF = sc + 224, *sdgam = sc + 256, *sdb = sc + 288, *sdEc = sc + 320;
@@ -148,6 +165,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   const int64_t base = (((int64_t)b * a.nb + c) * a.Hv + h);
   const int64_t tok0 = (int64_t)b * 2 * a.L + (stream ? a.L : 0) + (int64_t)c * C;  // first token row
   const bool clean = mode == 1;
+  mark(a, 0);
 
   if (threadIdx.x == 0) {
     mbar_init(ld_bar, 1);
@@ -255,6 +273,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   __syncthreads();
   tc_fence_after();
 
+  mark(a, 1);  // state tiles converted, q / k normalised, gates
   uint32_t rnd = 0;  // completed MMA rounds (mma_bar phase)
   auto round_wait = [&]() -> bool {
     bool w = mbar_wait(mma_bar, rnd & 1, err, ERR_GDN_WAIT, abort_flag);
@@ -298,22 +317,18 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int t = 0; t < 32; t += 2) {
       const float r00 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[t];
       const float r01 = get(sm + L::V, off2<32>(t + 1, f)) - sE[t + 1] * f1[t + 1];
-      red[f * 33 + t] = f2[t] * get(sm + L::DO, off2<32>(t, f));
-      red[f * 33 + t + 1] = f2[t + 1] * get(sm + L::DO, off2<32>(t + 1, f));
+      f2[t] *= get(sm + L::DO, off2<32>(t, f));
+      f2[t + 1] *= get(sm + L::DO, off2<32>(t + 1, f));
       const float rb0 = sbeta[t] * r00, rb1 = sbeta[t + 1] * r01;
       put(sm + L::R, off2<32>(t, f), rb0);
       put(sm + L::R, off2<32>(t + 1, f), rb1);
       ra[t >> 1] = pk2(rb0, rb1);
     }
     st16(tmem + lane_base + RA, ra);
-  }
-  __syncthreads();  // dE_a partials are in red[f][t] (warps 0-3); fold them before reuse
-  if (ok && warp == 4) {
-    float s = 0.f;
-    for (int v = 0; v < 128; ++v) s += red[v * 33 + lane];
-    sdE[lane] = s;
+    part[warp * 32 + lane] = fold32(f2, lane);  // dE_a partial of token `lane` over this warp's features
   }
   __syncthreads();
+  if (ok && warp == 4) sdE[lane] = part[lane] + part[32 + lane] + part[64 + lane] + part[96 + lane];
   if (ok && warp == 4) {
     float kk[32], qk[32];
     ld32(tmem + KK, kk);
@@ -354,6 +369,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int t = 0; t < 32; ++t) put(sm + L::QT, off2<32>(t, f), sE[t] * get(sm + L::Q, off2<32>(t, f)));
   }
   round_end();
+  mark(a, 2);
 
   // ================================================================ R2
   if (ok && ctl) {
@@ -387,6 +403,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     st16(tmem + lane_base + DVA, da);
   }
   round_end();
+  mark(a, 3);
 
   // ================================================================ R3
   if (ok && ctl) {
@@ -411,9 +428,10 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     ld32(tmem + lane_base + DRT, dr);
     float vp[32];
     ld32(tmem + lane_base + VPT, vp);  // V'^T row v (still in TMEM)
-    // dv = beta dR (global), dR tile, -beta E dR tile (noised), dbeta_a / dE_b partials
+    // dv = beta dR (global), dR tile, -beta E dR tile (noised); per-token sums over the features:
+    // dbeta_a = sum_v dR R0, dE_b = -beta sum_v F1 dR, dF = sum_v F7 V'
     __nv_bfloat16* dvg = a.dv + (tok0 * a.Hv + h) * (int64_t)D + f;
-    float f7[32];
+    float f7[32], pb[32];
     if (clean) ld32(tmem + lane_base + F7, f7);
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
@@ -421,24 +439,13 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       dvg[(int64_t)t * a.Hv * D] = __float2bfloat16_rn(sbeta[t] * dr[t]);
       put(sm + L::DR, off2<32>(t, f), dr[t]);
       if (!clean) put(sm + L::DRS, off2<32>(t, f), -sbeta[t] * sE[t] * dr[t]);
-      // red[f][t] = dbeta_a partial; dE_b and dF go to the second buffer half via atomics below
-      red[f * 33 + t] = dr[t] * r0;
+      pb[t] = dr[t] * r0;
+      f1[t] *= dr[t];
+      f7[t] = clean ? f7[t] * vp[t] : 0.f;
     }
-    // dE_b = -beta sum_v F1 dR ; dF = sum_v F7 V' : warp-reduce per token, one atomic per warp
-#pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      float e = f1[t] * dr[t];
-      float d = clean ? f7[t] * vp[t] : 0.f;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        e += __shfl_xor_sync(0xffffffffu, e, o);
-        d += __shfl_xor_sync(0xffffffffu, d, o);
-      }
-      if (lane == 0) {
-        atomicAdd(&sdE[t], -sbeta[t] * e);
-        if (clean) atomicAdd(&sdF[t], d);
-      }
-    }
+    part[warp * 32 + lane] = fold32(pb, lane);
+    part[128 + warp * 32 + lane] = fold32(f1, lane);
+    part[256 + warp * 32 + lane] = fold32(f7, lane);
     // dK^T (row k = f): clean F * (V' dS_out^T)^T ; dQ^T = E * F3
     float f3[32];
     ld32(tmem + lane_base + F3, f3);
@@ -482,12 +489,20 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     sdgam[lane] += rs - cs_mine;
   }
   __syncthreads();
-  if (ok && warp == 4) {  // dbeta_a: fold the feature partials
-    float s = 0.f;
-    for (int v = 0; v < 128; ++v) s += red[v * 33 + lane];
-    sdb[lane] += s;
+  if (ok && warp == 4) {  // combine the four warps' partials
+    float sb_ = 0.f, se = 0.f, sf = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      sb_ += part[w * 32 + lane];
+      se += part[128 + w * 32 + lane];
+      sf += part[256 + w * 32 + lane];
+    }
+    sdb[lane] += sb_;
+    sdE[lane] -= sbeta[lane] * se;
+    sdF[lane] = sf;
   }
   round_end();
+  mark(a, 4);
 
   // ================================================================ R4
   if (ok && ctl) {
@@ -501,7 +516,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int kk = 0; kk < 2; ++kk) {
       mma_s(tmem + DQB, d_tok_mn(sb + L::K, kk), d_tt_k(sb + L::DPM, kk), ID_A_MN, kk > 0);
       mma_s(tmem + DKB, d_tok_mn(sb + L::Q, kk), d_tt_k(sb + L::DPMT, kk), ID_A_MN, kk > 0);
-      if (!clean) {
+      if (!clean && a.dS_inj != nullptr) {
         mma_s(tmem + DSI, d_tok_mn(sb + L::QT, kk), d_tok_mn(sb + L::DO, kk), ID_SINJ, kk > 0);
         mma_s(tmem + DSI, d_tok_mn(sb + L::K, kk), d_tok_mn(sb + L::DRS, kk), ID_SINJ, 1u);
       }
@@ -520,7 +535,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     ld32(tmem + lane_base + DKB, x);
 #pragma unroll
     for (int t = 0; t < 32; ++t) dK[t] += x[t];
-    if (!clean) {  // dS_inj row k = f, 128 columns v
+    if (!clean && a.dS_inj != nullptr) {  // dS_inj row k = f, 128 columns v
       float* dst = a.dS_inj + base * D * D + (int64_t)f * D;
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
@@ -537,6 +552,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int j = 0; j < 32; ++j) put(sm + L::DT, off1(lane, j), dt[j]);  // dT = dV' R^T (R = beta R0)
   }
   round_end();
+  mark(a, 5);
 
   // ================================================================ R5: Z = dT T^T
   if (ok && ctl) {
@@ -552,6 +568,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int j = 0; j < 32; ++j) put(sm + L::ZT, off1(j, lane), z[j]);  // Z^T[j][lane] = Z[lane][j]
   }
   round_end();
+  mark(a, 6);
 
   // ================================================================ R6: dA' = T^T Z
   if (ok && ctl) {
@@ -596,6 +613,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int j = 0; j < 32; ++j) put(sm + L::SYM, off1(lane, j), dkk[j] + tb[(64 + j) * 33 + lane]);
   }
   round_end();
+  mark(a, 7);
 
   // ================================================================ R7: dKc = (sym k^)^T
   if (ok && ctl) {
@@ -604,33 +622,29 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
+  mark(a, 8);  // R7 MMA
   if (ok && warp < 4) {
     float x[32];
     ld32(tmem + lane_base + DKC, x);
 #pragma unroll
     for (int t = 0; t < 32; ++t) dK[t] += x[t];
-    // l2norm backward needs per-token dots <x^, dy> over the 128 features: reduce through red
+    // l2norm backward needs per-token dots <k^, dk^> and <q^, dq^> over the 128 features
+    float xk[32], xq[32];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) red[f * 33 + t] = get(sm + L::K, off2<32>(t, f)) * dK[t];
+    for (int t = 0; t < 32; ++t) {
+      xk[t] = get(sm + L::K, off2<32>(t, f)) * dK[t];
+      xq[t] = get(sm + L::Q, off2<32>(t, f)) * dQ[t];
+    }
+    part[warp * 32 + lane] = fold32(xk, lane);
+    part[128 + warp * 32 + lane] = fold32(xq, lane);
   }
   __syncthreads();
   if (ok && warp == 4) {
-    float s = 0.f;
-    for (int v = 0; v < 128; ++v) s += red[v * 33 + lane];
-    sc[352 + lane] = s;  // <k^, dk^>
+    sc[352 + lane] = part[lane] + part[32 + lane] + part[64 + lane] + part[96 + lane];  // <k^, dk^>
+    sc[384 + lane] = part[128 + lane] + part[160 + lane] + part[192 + lane] + part[224 + lane];  // <q^, dq^>
   }
   __syncthreads();
-  if (ok && warp < 4) {
-#pragma unroll
-    for (int t = 0; t < 32; ++t) red[f * 33 + t] = get(sm + L::Q, off2<32>(t, f)) * dQ[t];
-  }
-  __syncthreads();
-  if (ok && warp == 4) {
-    float s = 0.f;
-    for (int v = 0; v < 128; ++v) s += red[v * 33 + lane];
-    sc[384 + lane] = s;  // <q^, dq^>
-  }
-  __syncthreads();
+  mark(a, 9);  // R7 and the l2 folds
   if (ok && warp < 4) {
     // dk = rk (dk^ - k^ <k^, dk^>); dq = rq scale (dq^ - q^n <q^n, dq^>) with q^ = q^n scale
     __nv_bfloat16* dkg = a.dk + (tok0 * a.Hv + h) * (int64_t)D + f;
@@ -663,7 +677,11 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     a.dg[t * a.Hv + h] = v;
     a.dbeta[t * a.Hv + h] = sdb[i];
   }
+  __syncthreads();
+  mark(a, 10);
+  mark(a, 11);
   tc_fence_before();
   __syncthreads();
+  mark(a, 12);
   if (warp == 0) tmem_dealloc(tmem, 512);
 }

@@ -128,8 +128,9 @@ struct PArgs {
   __nv_bfloat16* W;
   __nv_bfloat16* Q;   // q~
   __nv_bfloat16* K;   // K~ (clean stream only)
-  __nv_bfloat16* P;   // [NCH * 32, 64]
+  __nv_bfloat16* P;   // [NCH * 32, 64] (optional)
   float* Ec;          // [NCH] e^gam_C
+  __nv_bfloat16* Pt;  // [NCH * 32, 64] P transposed per chunk (optional: the backward's operand)
   int B, L, Hk, Hv, nb;
   float scale;
   int* err;
@@ -298,9 +299,21 @@ __global__ void __launch_bounds__(P_THREADS, 1)
           const float p1 = j1 <= lane ? __uint_as_float(r[j1]) * __expf(gi - sgam[ch * 32 + j1]) : 0.f;
           pk[jj] = pack2(p0, p1);
         }
-        uint4* dst = reinterpret_cast<uint4*>(a.P + (chrow + t) * 64);
+        if (a.P != nullptr) {
+          uint4* dst = reinterpret_cast<uint4*>(a.P + (chrow + t) * 64);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+          for (int q4 = 0; q4 < 4; ++q4)
+            dst[q4] = make_uint4(pk[4 * q4], pk[4 * q4 + 1], pk[4 * q4 + 2], pk[4 * q4 + 3]);
+        }
+        if (a.Pt != nullptr) {  // Pt[chunk row j][lane] = P[lane][j]
+          __nv_bfloat16* dt = a.Pt + (chrow + ch * 32) * 64 + lane;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            const __nv_bfloat162 two = *reinterpret_cast<const __nv_bfloat162*>(&pk[jj]);
+            dt[(2 * jj) * 64] = two.x;
+            dt[(2 * jj + 1) * 64] = two.y;
+          }
+        }
       }
     }
     __syncthreads();
@@ -406,6 +419,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
       const uint32_t lane_base = (uint32_t)(q * 32) << 16;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
+        if (which == 0 && a.U == nullptr) continue;  // the backward needs W only
         __nv_bfloat16* dst = (which == 0 ? a.U : a.W) + (chrow + t) * D + hf * 64;
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
@@ -680,6 +694,233 @@ __global__ void __launch_bounds__(R_THREADS, 1)
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ============================================================================ kernel 3: reverse recurrence
+// The backward's sequential part, one CTA per (batch, v-head), chunks in reverse order. The state
+// gradient is kept transposed, dS^T [v = 128 TMEM lanes x k], as fp32 registers of 8 epilogue
+// warps and as a bf16 copy in TMEM (the A operand). With dS = dS_{c+1} (the gradient of the state
+// after clean chunk c) at step c:
+//   MMA 1: dV'^T = dS^T K~^T + dO_c^T P_c   (clean, N 32)    dV'_n^T = dO_n^T P_n  (noised block c)
+//   E1   : dV' of the clean chunk to global (fp32, for the chunk kernel); -dV'^T and -dV'_n^T as
+//          bf16 A operands into TMEM
+//   MMA 2: G^T = dO_c^T q~_c - dV'^T W_c + dO_n^T q~_n - dV'_n^T W_n   (N 128, K 32)
+//   E2   : dS_c^T = e^gam_C dS^T + G^T; dS_out[c - 1] = dS_c (fp32, for the chunk kernel)
+// The noised block's gradient of its starting state (q~_n^T dO_n - W_n^T dV'_n) is added here, so
+// the noised chunk kernel need not store it. dO tiles are the M-contiguous A operands (dO^T) as
+// TMA loads them; P enters transposed (K-major B).
+struct BArgs {
+  const float* Ec;  // [NCH]
+  float* dS_out;    // [B, nb, Hv, 128, 128]
+  float* dVp;       // [B, nb, Hv, 32, 128]
+  int B, L, Hv, nb;
+  int* err;
+};
+struct BStage {
+  // clean dO, K~, q~, W, Pt; noised dO, q~, W, Pt
+  static constexpr int DO = 0, K = T8, Q = 2 * T8, W = 3 * T8, DON = 4 * T8, QN = 5 * T8, WN = 6 * T8;
+  static constexpr int PT = 7 * T8, PTN = 7 * T8 + 4096;
+  static constexpr int BYTES = 7 * T8 + 2 * 4096;  // 64 KB
+};
+constexpr uint32_t IDESC_N32_AMN = idesc_bf16(128, 32, 1, 0);
+constexpr uint32_t IDESC_N128_ABMN = idesc_bf16(128, 128, 1, 1);
+
+__global__ void __launch_bounds__(R_THREADS, 1)
+    bwd_recur_kernel(const __grid_constant__ CUtensorMap mt, const __grid_constant__ CUtensorMap mp,
+                     const __grid_constant__ CUtensorMap mdo, BArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + NSTAGE * BStage::BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NSTAGE;
+  uint64_t* d1_full = bars + 2 * NSTAGE;
+  uint64_t* d2_full = d1_full + 1;
+  uint64_t* va_ready = d1_full + 2;
+  uint64_t* sa_ready = d1_full + 3;
+  uint64_t* drain = d1_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d1_full + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x / a.Hv, h = blockIdx.x % a.Hv;
+  const int nb = a.nb;
+  const int64_t chc = (((int64_t)(b * 2 + 1) * a.Hv + h) * nb) * C;
+  const int64_t chn = (((int64_t)(b * 2 + 0) * a.Hv + h) * nb) * C;
+  const int64_t tok_n = (int64_t)b * 2 * a.L, tok_c = tok_n + a.L;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(d1_full, 1);
+    mbar_init(d2_full, 1);
+    mbar_init(va_ready, 8);
+    mbar_init(sa_ready, 8);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&mt);
+    prefetch_tmap(&mp);
+    prefetch_tmap(&mdo);
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer (reverse order)
+      int last[NSTAGE];
+      for (int s = 0; s < NSTAGE; ++s) last[s] = -1;
+      const int nrow = a.B * 2 * a.Hv * nb * C;
+      for (int i = 0; i < nb; ++i) {
+        const int c = nb - 1 - i, s = i % NSTAGE;
+        if (!mbar_wait(&empty[s], ((i / NSTAGE) & 1) ^ 1, a.err, ERR_GDN_WAIT, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[s], BStage::BYTES);
+        last[s] = i;
+        uint8_t* st = sm + s * BStage::BYTES;
+        const int yc = (int)(chc + (int64_t)c * C), yn = (int)(chn + (int64_t)c * C);
+        for (int x = 0; x < 2; ++x) {
+          tma_load_2d(st + BStage::DO + x * 4096, &mdo, &full[s], h * D + x * 64, (int)(tok_c + (int64_t)c * C));
+          tma_load_2d(st + BStage::DON + x * 4096, &mdo, &full[s], h * D + x * 64, (int)(tok_n + (int64_t)c * C));
+          tma_load_2d(st + BStage::K + x * 4096, &mt, &full[s], x * 64, yc + 3 * nrow);
+          tma_load_2d(st + BStage::Q + x * 4096, &mt, &full[s], x * 64, yc + 2 * nrow);
+          tma_load_2d(st + BStage::W + x * 4096, &mt, &full[s], x * 64, yc + 1 * nrow);
+          tma_load_2d(st + BStage::QN + x * 4096, &mt, &full[s], x * 64, yn + 2 * nrow);
+          tma_load_2d(st + BStage::WN + x * 4096, &mt, &full[s], x * 64, yn + 1 * nrow);
+        }
+        tma_load_2d(st + BStage::PT, &mp, &full[s], 0, yc);
+        tma_load_2d(st + BStage::PTN, &mp, &full[s], 0, yn);
+      }
+      for (int s = 0; s < NSTAGE; ++s)
+        if (last[s] >= 0) mbar_wait(&full[s], (last[s] / NSTAGE) & 1, a.err, ERR_GDN_WAIT, nullptr);
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ MMA issuer
+      for (int i = 0; i < nb; ++i) {
+        const int s = i % NSTAGE;
+        if (!mbar_wait(&full[s], (i / NSTAGE) & 1, a.err, ERR_GDN_WAIT, abort_flag)) break;
+        if (!mbar_wait(sa_ready, i & 1, a.err, ERR_GDN_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * BStage::BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)  // dS^T K~^T (K = k)
+          mma_ta(tmem + DW_COL, tmem + SA_COL + kk * 8,
+                 smem_desc(st + BStage::K + (kk >> 2) * 4096 + (kk & 3) * 32, 16, 1024), IDESC_N32, kk > 0);
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk) {  // dO^T P (K = t')
+          mma_bf16(tmem + DW_COL, smem_desc(st + BStage::DO + kk * 2048, 4096, 1024),
+                   smem_desc(st + BStage::PT + kk * 32, 16, 1024), IDESC_N32_AMN, 1u);
+          mma_bf16(tmem + DWN_COL, smem_desc(st + BStage::DON + kk * 2048, 4096, 1024),
+                   smem_desc(st + BStage::PTN + kk * 32, 16, 1024), IDESC_N32_AMN, kk > 0);
+        }
+        mma_commit(d1_full);
+        if (!mbar_wait(va_ready, i & 1, a.err, ERR_GDN_WAIT, abort_flag)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk) {  // K = t (32)
+          const uint32_t acc = kk > 0;
+          mma_bf16(tmem + DS_COL, smem_desc(st + BStage::DO + kk * 2048, 4096, 1024),
+                   smem_desc(st + BStage::Q + kk * 2048, 4096, 1024), IDESC_N128_ABMN, acc);
+          mma_ta(tmem + DS_COL, tmem + VA_COL + kk * 8, smem_desc(st + BStage::W + kk * 2048, 4096, 1024),
+                 IDESC_N128_BMN, 1u);
+          mma_bf16(tmem + DS_COL, smem_desc(st + BStage::DON + kk * 2048, 4096, 1024),
+                   smem_desc(st + BStage::QN + kk * 2048, 4096, 1024), IDESC_N128_ABMN, 1u);
+          mma_ta(tmem + DS_COL, tmem + VNA_COL + kk * 8, smem_desc(st + BStage::WN + kk * 2048, 4096, 1024),
+                 IDESC_N128_BMN, 1u);
+        }
+        mma_commit(d2_full);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_GDN_WAIT, nullptr);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue (warps 0-7)
+    const int q = warp & 3, hf = warp >> 2;
+    const int v = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float S[64];  // dS^T[v][64 hf + i]
+#pragma unroll
+    for (int i = 0; i < 64; ++i) S[i] = 0.f;
+    {
+      uint32_t z[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) z[i] = 0u;
+      tmem_st32r(tmem + lane_base + SA_COL + hf * 32, z);
+      float* dst = a.dS_out + ((((int64_t)b * nb + nb - 1) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) dst[i * D] = 0.f;  // nothing flows back from after the last chunk
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sa_ready);
+    }
+    for (int i = 0; i < nb; ++i) {
+      const int c = nb - 1 - i, s = i % NSTAGE;
+      // ---- E1: dV' (clean) to global; -dV'^T, -dV'_n^T into TMEM; t in [16 hf, 16 hf + 16)
+      if (!warp_wait(d1_full, i & 1, a.err, abort_flag)) break;
+      tc_fence_after();
+      {
+        uint32_t dv[16], dvn[16];
+        tmem_ld16r(tmem + lane_base + DW_COL + hf * 16, dv);
+        tmem_ld16r(tmem + lane_base + DWN_COL + hf * 16, dvn);
+        uint32_t pc[8], pn[8];
+        float* g = a.dVp + ((((int64_t)b * nb + c) * a.Hv + h) * C) * D + v;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float x0 = __uint_as_float(dv[2 * j]), x1 = __uint_as_float(dv[2 * j + 1]);
+          g[(hf * 16 + 2 * j) * D] = x0;
+          g[(hf * 16 + 2 * j + 1) * D] = x1;
+          pc[j] = pack2(-x0, -x1);
+          pn[j] = pack2(-__uint_as_float(dvn[2 * j]), -__uint_as_float(dvn[2 * j + 1]));
+        }
+        tmem_st8r(tmem + lane_base + VA_COL + hf * 8, pc);
+        tmem_st8r(tmem + lane_base + VNA_COL + hf * 8, pn);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(va_ready);
+      // ---- E2: dS_c = e^gam_C dS_{c+1} + G
+      if (!warp_wait(d2_full, i & 1, a.err, abort_flag)) break;
+      tc_fence_after();
+      const float ec = a.Ec[(((int64_t)(b * 2 + 1) * a.Hv + h) * nb + c)];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32r(tmem + lane_base + DS_COL + hf * 64, r0);
+        tmem_ld32r(tmem + lane_base + DS_COL + hf * 64 + 32, r1);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          S[j] = ec * S[j] + __uint_as_float(r0[j]);
+          S[32 + j] = ec * S[32 + j] + __uint_as_float(r1[j]);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pk[j] = pack2(S[2 * j], S[2 * j + 1]);
+        tmem_st32r(tmem + lane_base + SA_COL + hf * 32, pk);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sa_ready);
+      if (warp == 0 && lane == 0) mbar_arrive(&empty[s]);
+      if (c > 0) {
+        float* dst = a.dS_out + ((((int64_t)b * nb + c - 1) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+#pragma unroll
+        for (int j = 0; j < 64; ++j) dst[j * D] = S[j];
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
 // ------------------------------------------------------------------------------------- host
 struct alignas(64) PrepLaunch {
   CUtensorMap mq, mk, mv;
@@ -743,8 +984,8 @@ std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, con
   auto* tb = reinterpret_cast<__nv_bfloat16*>(tiles.data_ptr());
   const int64_t tsz = nch * C * 128;
   pl.args = PArgs{g.data_ptr<float>(), beta.data_ptr<float>(), tb, tb + tsz, tb + 2 * tsz, tb + 3 * tsz,
-                  reinterpret_cast<__nv_bfloat16*>(P.data_ptr()), Ec.data_ptr<float>(), B, (int)L, Hk, Hv, nb,
-                  1.f / sqrtf(128.f), err};
+                  reinterpret_cast<__nv_bfloat16*>(P.data_ptr()), Ec.data_ptr<float>(), nullptr, B, (int)L, Hk, Hv,
+                  nb, 1.f / sqrtf(128.f), err};
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PSmem::BYTES));
@@ -767,6 +1008,56 @@ std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, con
                                     R_SMEM, st));
   }
   return {o, S_in};
+}
+
+// The backward's sequential part on tcgen05 for the fork layout (head dim 128, chunk 32): reruns the
+// prep kernel (W, q~, K~, P^T, e^gam_C of both streams) and the reverse recurrence. dout is bf16
+// contiguous [B, 2L, Hv, 128]; dS_out [B, nb, Hv, 128, 128] and dVp [B, nb, Hv, 32, 128] (fp32) are
+// written: what the clean chunk kernel reads. The noised blocks' state gradients are included.
+void gdn_bwd_recurrence_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
+                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, float* dS_out, float* dVp) {
+  using namespace gdn_tc;
+  const int B = q.size(0), Hk = q.size(2), Hv = v.size(2);
+  const int nb = (int)(L / C);
+  const int64_t nch = (int64_t)B * 2 * Hv * nb;
+  auto bf = q.options().dtype(at::kBFloat16);
+  auto tiles = at::empty({4, nch * C, 128}, bf);  // (unused U slot), W, q~, K~
+  auto Pt = at::empty({nch * C, 64}, bf);
+  auto Ec = at::empty({nch}, q.options().dtype(at::kFloat));
+  int* err = error_word_ptr();
+  auto st = at::cuda::getCurrentCUDAStream();
+  static thread_local PrepLaunch pl;
+  make_map_bf16(&pl.mq, q.data_ptr(), (uint64_t)Hk * 128, (uint64_t)B * 2 * L, q.stride(1), 64, TT);
+  make_map_bf16(&pl.mk, k.data_ptr(), (uint64_t)Hk * 128, (uint64_t)B * 2 * L, k.stride(1), 64, TT);
+  make_map_bf16(&pl.mv, v.data_ptr(), (uint64_t)Hv * 128, (uint64_t)B * 2 * L, v.stride(1), 64, TT);
+  auto* tb = reinterpret_cast<__nv_bfloat16*>(tiles.data_ptr());
+  const int64_t tsz = nch * C * 128;
+  pl.args = PArgs{g.data_ptr<float>(), beta.data_ptr<float>(), nullptr, tb + tsz, tb + 2 * tsz, tb + 3 * tsz, nullptr,
+                  Ec.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(Pt.data_ptr()), B, (int)L, Hk, Hv, nb,
+                  1.f / sqrtf(128.f), err};
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PSmem::BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(bwd_recur_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, R_SMEM));
+    attr = true;
+  }
+  {
+    void* kargs[4] = {&pl.mq, &pl.mk, &pl.mv, &pl.args};
+    C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(prep_kernel), dim3(nb / 4, Hk, B * 2),
+                                    dim3(P_THREADS), kargs, PSmem::BYTES, st));
+  }
+  struct alignas(64) BLaunch {
+    CUtensorMap mt, mp, mdo;
+    BArgs args;
+  };
+  static thread_local BLaunch bl;
+  make_map_bf16(&bl.mt, tiles.data_ptr(), 128, (uint64_t)4 * nch * C, 128, 64, C);
+  make_map_bf16(&bl.mp, Pt.data_ptr(), 64, (uint64_t)nch * C, 64, 64, C);
+  make_map_bf16(&bl.mdo, dout.data_ptr(), (uint64_t)Hv * 128, (uint64_t)B * 2 * L, (uint64_t)Hv * 128, 64, C);
+  bl.args = BArgs{Ec.data_ptr<float>(), dS_out, dVp, B, (int)L, Hv, nb, err};
+  void* kargs[4] = {&bl.mt, &bl.mp, &bl.mdo, &bl.args};
+  C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(bwd_recur_kernel), dim3(B * Hv), dim3(R_THREADS), kargs,
+                                  R_SMEM, st));
 }
 
 }  // namespace bdllm

@@ -30,7 +30,8 @@ namespace bdllm {
 void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_inner,
                    uint32_t box_outer);
 void gdn_bwd_recurrence_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
-                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, float* dS_out, float* dVp);
+                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, __nv_bfloat16* dS_out,
+                           float* dVp);
 namespace gdn {
 
 constexpr int NT = 512;
@@ -1251,7 +1252,9 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto f32 = q.options().dtype(at::kFloat);
   auto d = dout.to(at::kBFloat16).contiguous();
   a.dout = reinterpret_cast<const __nv_bfloat16*>(d.data_ptr());
-  a.S_in = const_cast<float*>(S_in.data_ptr<float>());
+  // bf16 S_in: the tensor-core forward's S^T rows; the whole backward then runs on tcgen05
+  const bool bf16_states = S_in.scalar_type() == at::kBFloat16;
+  a.S_in = bf16_states ? nullptr : const_cast<float*>(S_in.data_ptr<float>());
   auto dq = at::empty({a.B, 2 * L, a.Hv, Dk}, q.options());
   auto dk = at::empty({a.B, 2 * L, a.Hv, Dk}, q.options());
   auto dv = at::empty({a.B, 2 * L, a.Hv, Dv}, q.options());
@@ -1270,7 +1273,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto dS_inj = concat ? (inj.has_value() ? *inj : at::Tensor()) : at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
   auto dS0 = want_dS0 ? at::empty({a.B, a.Hv, Dk, Dv}, f32) : at::Tensor();
   a.dS0 = want_dS0 ? dS0.data_ptr<float>() : nullptr;
-  auto dS_out = at::empty({a.B, a.nb, a.Hv, Dk, Dv}, f32);
+  auto dS_out = at::empty({a.B, a.nb, a.Hv, Dk, Dv}, bf16_states ? q.options().dtype(at::kBFloat16) : f32);
   auto dVp = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
   auto PtdO = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
   auto Qt = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
@@ -1278,7 +1281,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   auto W = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
   auto Ec = at::empty({a.B, a.nb, a.Hv}, f32);
   a.dS_inj = dS_inj.defined() ? dS_inj.data_ptr<float>() : nullptr;
-  a.dS_out = dS_out.data_ptr<float>();
+  a.dS_out = bf16_states ? nullptr : dS_out.data_ptr<float>();
   a.dVp = dVp.data_ptr<float>();
   a.PtdO = PtdO.data_ptr<float>();
   a.Qt = Qt.data_ptr<float>();
@@ -1302,23 +1305,26 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
     ph = at::zeros({16}, q.options().dtype(at::kLong));
     a.phase = reinterpret_cast<long long*>(ph.data_ptr<int64_t>());
   }
-  // the chunk kernels on tcgen05 (head dim 128, chunk 32, the fork layout; BDLLM_GDN_TC=0 keeps the
-  // mma.sync ones): q, k, v, dO tiles of 32 tokens by TMA
-  static const bool tc_off = getenv("BDLLM_GDN_TC") != nullptr && getenv("BDLLM_GDN_TC")[0] == '0';
-  const bool tc = Dk == 128 && Dv == 128 && !concat && C == 32 && !tc_off &&
-                  reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
-                  reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0 && a.ldqk % 8 == 0 && a.ldv % 8 == 0;
+  // the whole backward on tcgen05 when the forward saved bf16 S^T rows (head dim 128, chunk 32, the
+  // fork layout, L a multiple of 128: the tensor-core forward's domain): chunk kernels fed by TMA
+  // (q, k, v, dO tiles of 32 tokens; S^T and dS_out^T tiles) and the reverse recurrence, which adds
+  // the noised blocks' state gradients itself
+  const bool tc = bf16_states;
+  TORCH_CHECK(!tc || (Dk == 128 && Dv == 128 && !concat && C == 32 && L % 128 == 0 && a.ldqk % 8 == 0 &&
+                      a.ldv % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(k.data_ptr()) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0),
+              "gdn_bwd: bf16 states come from the tensor-core forward (head dim 128, block 32, L % 128 == 0)");
   struct alignas(64) TcMaps {
-    CUtensorMap mq, mk, mv, mdo;
+    CUtensorMap mq, mk, mv, mdo, ms, mds;
   };
   static thread_local TcMaps tm;
   auto chunk_tc = [&](int mode) {
-    void* kargs[7];
+    void* kargs[9];
     int* err = error_word_ptr();
     Args ac = a;
-    if (mode == 1) ac.phase = a.phase;  // (phase stamps: both launches, like the mma.sync kernels)
-    kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &ac, kargs[5] = &mode,
-    kargs[6] = &err;
+    kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &tm.ms,
+    kargs[5] = &tm.mds, kargs[6] = &ac, kargs[7] = &mode, kargs[8] = &err;
     C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(bwd_chunk_tc_kernel), dim3(a.nb, BH),
                                     dim3(btc::NTH), kargs, btc::L::BYTES, at::cuda::getCurrentCUDAStream()));
   };
@@ -1334,23 +1340,19 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
     make_map_bf16(&tm.mk, k.data_ptr(), (uint64_t)a.Hk * Dk, rows, a.ldqk, 64, 32);
     make_map_bf16(&tm.mv, v.data_ptr(), (uint64_t)a.Hv * Dv, rows, a.ldv, 64, 32);
     make_map_bf16(&tm.mdo, d.data_ptr(), (uint64_t)a.Hv * Dv, rows, (uint64_t)a.Hv * Dv, 64, 32);
+    const uint64_t srows = (uint64_t)a.B * a.nb * a.Hv * Dk;
+    make_map_bf16(&tm.ms, S_in.data_ptr(), Dv, srows, Dv, 64, 128);
+    make_map_bf16(&tm.mds, dS_out.data_ptr(), Dv, srows, Dv, 64, 128);
   }
-  // the sequential part on tcgen05 too (prep tiles of 4 chunks: L a multiple of 128): it adds the
-  // noised blocks' state gradients itself, so their chunk kernel stores none
-  const bool tc_rec = tc && L % 128 == 0 && (int64_t)a.B * 2 * a.Hv * a.nb * C * 4 < ((int64_t)1 << 31);
   if (!concat) {
-    if (tc) {
-      float* keep = a.dS_inj;
-      if (tc_rec) a.dS_inj = nullptr;
+    if (tc)
       chunk_tc(0);
-      a.dS_inj = keep;
-    } else {
+    else
       launch2(bwd_chunk_kernel<Dk, Dv>, dim3(a.nb, BH), BSmem<Dk, Dv>::floats, a, 0);
-    }
     report("noised");
   }
-  if (tc_rec) {
-    gdn_bwd_recurrence_tc(q, k, v, g, beta, d, L, a.dS_out, a.dVp);
+  if (tc) {
+    gdn_bwd_recurrence_tc(q, k, v, g, beta, d, L, reinterpret_cast<__nv_bfloat16*>(dS_out.data_ptr()), a.dVp);
   } else {
     Args a2 = a;
     a2.phase = nullptr;

@@ -1,7 +1,9 @@
 // State-fork GDN backward, chunk kernel, on tcgen05 / TMEM with TMA-staged tiles (head dim 128,
 // chunk 32). Included by gdn.cu inside namespace bdllm::gdn: a drop-in for bwd_chunk_kernel<128,
-// 128> in both modes (0: noised block, dV' = P^T dO, writes dS_inj; 1: clean chunk, dV' and
-// dS_out from the reverse recurrence), same Args, same outputs.
+// 128> for the fork layout in both modes (0: noised block, dV' = P^T dO; 1: clean chunk, dV' and
+// dS_out from the reverse recurrence), used with the tensor-core recurrence, which adds the noised
+// blocks' state gradients itself (so no dS_inj is stored here). The states come as bf16 S^T rows
+// (the forward's S_in and the recurrence's dS_out, [v][k] per chunk) loaded by TMA.
 //
 // Per CTA = one chunk (32 tokens) of one v-head. Every product with a 128-wide operand (the state
 // S, dS_out, or a feature dimension) runs as an M = 128 MMA with the feature dimension on the 128
@@ -15,12 +17,11 @@
 //   dk^ = -diag(beta E) dR S^T + dPm^T q^ + diag(F) V' dS_out^T + (dKK + dKK^T) k^
 //   dE = rowsum(q^S * dO) - beta rowsum(k^S * dR),  dF = rowsum(k^ dS_out * V'),  dEc = <S, dS_out>
 //   dbeta = rowsum(dR * R0) + rowsum(dA * KK * Gam);  dKK = dA * beta_i * Gam
-//   dS_inj (noised) = (diag(E) q^)^T dO - k^T diag(beta E) dR
 // Rounds (MMA batch -> bounded wait -> epilogue -> barrier):
 //   R1  KK, QK (token x token); F1 = (k^S)^T, F2 = (q^S)^T [v x t]; F3 = (dO S^T)^T [k x t]
 //   R2  V'^T = R^T T^T (A = R^T from TMEM); noised: dV'^T = dO^T P
 //   R3  dR^T = dV'^T T; dP; clean: F6 = (V' dS_out^T)^T [k x t], F7 = (k^ dS_out)^T [v x t]
-//   R4  dT; F4 = (dR S^T)^T; dQb = (dPm k^)^T; dKb = (dPm^T q^)^T; noised: dS_inj [k x v]
+//   R4  dT; F4 = (dR S^T)^T; dQb = (dPm k^)^T; dKb = (dPm^T q^)^T
 //   R5  Z = dT T^T     R6  dA' = T^T Z     R7  dKc = ((dKK + dKK^T) k^)^T
 // Bounded waits as everywhere (ERR_GDN_WAIT); no multicast.
 
@@ -34,8 +35,8 @@ struct L {
   // token tiles (order matters: a token tile used as a padded A operand needs 12 KB of shared memory
   // after each of its boxes)
   static constexpr int Q = 0, K = TOK, DO = 2 * TOK, V = 3 * TOK, VP = 4 * TOK, DV = 5 * TOK, R = 6 * TOK,
-                       DR = 7 * TOK, QT = 8 * TOK, DRS = 9 * TOK;
-  static constexpr int TTB = 10 * TOK;  // token x token tiles
+                       DR = 7 * TOK;
+  static constexpr int TTB = 8 * TOK;  // token x token tiles
   static constexpr int T_ = TTB, TT_ = TTB + TT, PT = TTB + 2 * TT, DPM = TTB + 3 * TT, DPMT = TTB + 4 * TT,
                        DT = TTB + 5 * TT, ZT = TTB + 6 * TT, SYM = TTB + 7 * TT;
   static constexpr int S = TTB + 8 * TT;  // state tiles
@@ -51,10 +52,9 @@ static_assert(L::BYTES <= 227 * 1024, "gdn bwd tc smem");
 // TMEM columns
 constexpr uint32_t F1 = 0, F2 = 32, F3 = 64, KK = 96, QK = 128, VPT = 160, DVT = 192, RA = 224, DVA = 240,
                    DRT = 256, DP = 288, F6 = 320, F7 = 352, F4 = 384, DQB = 416, DKB = 448, DA = 480;
-constexpr uint32_t DT_C = 160, Z_C = 192, DKC = 224, DSI = 256;  // reuse after consumption
+constexpr uint32_t DT_C = 160, Z_C = 192, DKC = 224;  // reuse after consumption
 constexpr uint32_t ID_TT = idesc_bf16(128, 32, 0, 0);        // K-major A and B, N 32
 constexpr uint32_t ID_A_MN = idesc_bf16(128, 32, 1, 0);      // A M-contiguous, B K-major, N 32
-constexpr uint32_t ID_SINJ = idesc_bf16(128, 128, 1, 1);     // both MN-major, N 128
 
 // element (r, c) of a [R x 128] tile held as two 128-byte-swizzled boxes [R][64]
 template <int R>
@@ -140,7 +140,8 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint32_t a_tmem, uint64_t bd, 
 
 __global__ void __launch_bounds__(btc::NTH, 1)
     bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-                        const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, Args a,
+                        const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+                        const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mds, Args a,
                         int mode, int* err) {
   using namespace btc;
   constexpr int D = 128, C = 32;
@@ -182,36 +183,16 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sb = smem_u32(sm);
-  if (threadIdx.x == 160) {  // TMA: raw q, k, v rows and dO of this chunk
-    mbar_arrive_expect_tx(ld_bar, 4 * TOK);
+  if (threadIdx.x == 160) {  // TMA: raw q, k, v rows and dO of this chunk; S^T (and dS_out^T) tiles
+    mbar_arrive_expect_tx(ld_bar, 4 * TOK + (clean ? 2 : 1) * ST);
     for (int x = 0; x < 2; ++x) {
       tma_load_2d(sm + L::Q + x * 4096, &mq, ld_bar, hk * D + x * 64, (int)tok0);
       tma_load_2d(sm + L::K + x * 4096, &mk, ld_bar, hk * D + x * 64, (int)tok0);
       tma_load_2d(sm + L::V + x * 4096, &mv, ld_bar, h * D + x * 64, (int)tok0);
       tma_load_2d(sm + L::DO + x * 4096, &mdo, ld_bar, h * D + x * 64, (int)tok0);
+      tma_load_2d(sm + L::S + x * 16384, &ms, ld_bar, x * 64, (int)(base * D));
+      if (clean) tma_load_2d(sm + L::DS + x * 16384, &mds, ld_bar, x * 64, (int)(base * D));
     }
-  }
-  // ---- state tiles: S (and dS_out) fp32 -> bf16, thread = row k; <S, dS_out> partial per row
-  if (threadIdx.x < 128) {
-    const int k = threadIdx.x;
-    const float* Sg = a.S_in + base * D * D + (int64_t)k * D;
-    const float* Og = clean ? a.dS_out + base * D * D + (int64_t)k * D : nullptr;
-    float dot = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < 16; ++j) {
-      const float4 s0 = *reinterpret_cast<const float4*>(Sg + j * 8), s1 = *reinterpret_cast<const float4*>(Sg + j * 8 + 4);
-      uint4 u;
-      u.x = pk2(s0.x, s0.y), u.y = pk2(s0.z, s0.w), u.z = pk2(s1.x, s1.y), u.w = pk2(s1.z, s1.w);
-      *reinterpret_cast<uint4*>(sm + L::S + ((j >> 3) * 16384 + k * 128 + (((j & 7) ^ (k & 7)) << 4))) = u;
-      if (clean) {
-        const float4 o0 = *reinterpret_cast<const float4*>(Og + j * 8), o1 = *reinterpret_cast<const float4*>(Og + j * 8 + 4);
-        dot += s0.x * o0.x + s0.y * o0.y + s0.z * o0.z + s0.w * o0.w + s1.x * o1.x + s1.y * o1.y + s1.z * o1.z +
-               s1.w * o1.w;
-        u.x = pk2(o0.x, o0.y), u.y = pk2(o0.z, o0.w), u.z = pk2(o1.x, o1.y), u.w = pk2(o1.z, o1.w);
-        *reinterpret_cast<uint4*>(sm + L::DS + ((j >> 3) * 16384 + k * 128 + (((j & 7) ^ (k & 7)) << 4))) = u;
-      }
-    }
-    red[k * 33] = dot;
   }
   // ---- gates (token warp): gam = cumsum g, beta, E, F
   if (warp == 4) {
@@ -229,6 +210,23 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   }
   bool ok = mbar_wait(ld_bar, 0, err, ERR_GDN_WAIT, abort_flag);
   ok = __syncthreads_and(ok);
+  if (ok && clean && threadIdx.x < 128) {  // <S, dS_out> partial of row v = thread
+    const int v = threadIdx.x;
+    float dot = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t o = (j >> 3) * 16384 + v * 128 + (((j & 7) ^ (v & 7)) << 4);
+      const uint4 x = *reinterpret_cast<const uint4*>(sm + L::S + o), y = *reinterpret_cast<const uint4*>(sm + L::DS + o);
+      const __nv_bfloat162* px = reinterpret_cast<const __nv_bfloat162*>(&x);
+      const __nv_bfloat162* py = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fx = __bfloat1622float2(px[e]), fy = __bfloat1622float2(py[e]);
+        dot += fx.x * fy.x + fx.y * fy.y;
+      }
+    }
+    red[v * 33] = dot;
+  }
   // <S, dS_out> and the l2 normalisation of q, k rows (threads 0-63: k rows 0-31 then q rows)
   if (ok && threadIdx.x < 64) {
     const int r = threadIdx.x & 31;
@@ -261,6 +259,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       *reinterpret_cast<uint4*>(pp) = u;
     }
   }
+  __syncthreads();
   if (ok && warp == 4 && clean) {  // dEc = <S, dS_out>: sum the 128 row partials
     float s = 0.f;
     for (int k = lane; k < 128; k += 32) s += red[k * 33];
@@ -299,9 +298,9 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       const uint32_t acc = kk > 0;
       mma_s(tmem + KK, d_tok_k(sb + L::K, kk), d_tok_k(sb + L::K, kk), ID_TT, acc);
       mma_s(tmem + QK, d_tok_k(sb + L::Q, kk), d_tok_k(sb + L::K, kk), ID_TT, acc);
-      mma_s(tmem + F1, d_st_mn(sb + L::S, kk), d_tok_k(sb + L::K, kk), ID_A_MN, acc);
-      mma_s(tmem + F2, d_st_mn(sb + L::S, kk), d_tok_k(sb + L::Q, kk), ID_A_MN, acc);
-      mma_s(tmem + F3, d_st_k(sb + L::S, kk), d_tok_k(sb + L::DO, kk), ID_TT, acc);
+      mma_s(tmem + F1, d_st_k(sb + L::S, kk), d_tok_k(sb + L::K, kk), ID_TT, acc);
+      mma_s(tmem + F2, d_st_k(sb + L::S, kk), d_tok_k(sb + L::Q, kk), ID_TT, acc);
+      mma_s(tmem + F3, d_st_mn(sb + L::S, kk), d_tok_k(sb + L::DO, kk), ID_A_MN, acc);
     }
     mma_commit(mma_bar);
   }
@@ -363,11 +362,6 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       put(sm + L::TT_, off1(lane, i), tc[i]);  // T^T[lane][i]
     }
   }
-  if (ok && warp < 4 && !clean) {
-    // q~ = E q^ (rows = tokens): features f read column f of q^ for every token
-#pragma unroll 8
-    for (int t = 0; t < 32; ++t) put(sm + L::QT, off2<32>(t, f), sE[t] * get(sm + L::Q, off2<32>(t, f)));
-  }
   round_end();
   mark(a, 2);
 
@@ -414,8 +408,8 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       const uint32_t acc = kk > 0;
       mma_s(tmem + DP, d_tok_k(sb + L::DO, kk), d_tok_k(sb + L::VP, kk), ID_TT, acc);
       if (clean) {
-        mma_s(tmem + F6, d_st_k(sb + L::DS, kk), d_tok_k(sb + L::VP, kk), ID_TT, acc);
-        mma_s(tmem + F7, d_st_mn(sb + L::DS, kk), d_tok_k(sb + L::K, kk), ID_A_MN, acc);
+        mma_s(tmem + F6, d_st_mn(sb + L::DS, kk), d_tok_k(sb + L::VP, kk), ID_A_MN, acc);
+        mma_s(tmem + F7, d_st_k(sb + L::DS, kk), d_tok_k(sb + L::K, kk), ID_TT, acc);
       }
     }
     mma_commit(mma_bar);
@@ -438,7 +432,6 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       const float r0 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[t];
       dvg[(int64_t)t * a.Hv * D] = __float2bfloat16_rn(sbeta[t] * dr[t]);
       put(sm + L::DR, off2<32>(t, f), dr[t]);
-      if (!clean) put(sm + L::DRS, off2<32>(t, f), -sbeta[t] * sE[t] * dr[t]);
       pb[t] = dr[t] * r0;
       f1[t] *= dr[t];
       f7[t] = clean ? f7[t] * vp[t] : 0.f;
@@ -510,16 +503,12 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int kk = 0; kk < 8; ++kk) {
       const uint32_t acc = kk > 0;
       mma_s(tmem + DT_C, d_tok_k(sb + L::DV, kk), d_tok_k(sb + L::R, kk), ID_TT, acc);
-      mma_s(tmem + F4, d_st_k(sb + L::S, kk), d_tok_k(sb + L::DR, kk), ID_TT, acc);
+      mma_s(tmem + F4, d_st_mn(sb + L::S, kk), d_tok_k(sb + L::DR, kk), ID_A_MN, acc);
     }
 #pragma unroll
     for (int kk = 0; kk < 2; ++kk) {
       mma_s(tmem + DQB, d_tok_mn(sb + L::K, kk), d_tt_k(sb + L::DPM, kk), ID_A_MN, kk > 0);
       mma_s(tmem + DKB, d_tok_mn(sb + L::Q, kk), d_tt_k(sb + L::DPMT, kk), ID_A_MN, kk > 0);
-      if (!clean && a.dS_inj != nullptr) {
-        mma_s(tmem + DSI, d_tok_mn(sb + L::QT, kk), d_tok_mn(sb + L::DO, kk), ID_SINJ, kk > 0);
-        mma_s(tmem + DSI, d_tok_mn(sb + L::K, kk), d_tok_mn(sb + L::DRS, kk), ID_SINJ, 1u);
-      }
     }
     mma_commit(mma_bar);
   }
@@ -535,15 +524,6 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     ld32(tmem + lane_base + DKB, x);
 #pragma unroll
     for (int t = 0; t < 32; ++t) dK[t] += x[t];
-    if (!clean && a.dS_inj != nullptr) {  // dS_inj row k = f, 128 columns v
-      float* dst = a.dS_inj + base * D * D + (int64_t)f * D;
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        ld32(tmem + lane_base + DSI + c4 * 32, x);
-#pragma unroll
-        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + c4 * 32 + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
-      }
-    }
   }
   if (ok && warp == 4) {  // dT -> tile (A operand of Z = dT T^T)
     float dt[32];

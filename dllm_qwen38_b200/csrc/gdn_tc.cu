@@ -1,8 +1,10 @@
 // State-fork chunked gated delta rule, forward, on the 5th-generation tensor cores (tcgen05 +
 // TMEM, operands staged by TMA). Head dim 128, chunk = block = 32, the fork layout [B, 2L]
 // (positions [0, L) the noised stream x_t, [L, 2L) the clean stream x_0). Same contract as
-// gdn.cu's forward_t: returns o [B, 2L, Hv, 128] bf16 and S_in [B, nb, Hv, 128, 128] fp32 (the
-// state entering each clean chunk = the state each noised block forks from).
+// gdn.cu's forward_t for the output: returns o [B, 2L, Hv, 128] bf16, and the state entering each
+// clean chunk (= the state each noised block forks from) as S_in^T [B, nb, Hv, 128 (v), 128 (k)]
+// bf16, the layout the tensor-core backward loads by TMA (row v of S^T is what one epilogue
+// thread holds, so each thread stores one contiguous row).
 //
 // Math per chunk (one v-head; q^, k^ l2-normalised, q^ scaled by 128^-1/2; gam = cumsum g):
 //   A = strict_lower(beta_i k^_i.k^_j e^(gam_i - gam_j)), T = (I + A)^-1
@@ -458,7 +460,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 struct RArgs {
   const float* Ec;       // [NCH]
   const __nv_bfloat16* U;  // [NCH * 32, 128] (read by the epilogue through the TMA-staged tile)
-  float* S_in;           // [B, nb, Hv, 128, 128]
+  __nv_bfloat16* S_in;   // S^T per chunk entry: [B, nb, Hv, 128 (v), 128 (k)]
   __nv_bfloat16* o;      // [B, 2L, Hv, 128]
   int B, L, Hv, nb;
   int* err;
@@ -609,9 +611,9 @@ __global__ void __launch_bounds__(R_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 32; ++i) z[i] = 0u;
       tmem_st32r(tmem + lane_base + SA_COL + hf * 32, z);
-      float* dst = a.S_in + ((((int64_t)b * nb + 0) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+      uint4* dst = reinterpret_cast<uint4*>(a.S_in + ((((int64_t)b * nb + 0) * a.Hv + h) * D + v) * D + hf * 64);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) dst[i * D] = 0.f;
+      for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -652,6 +654,7 @@ __global__ void __launch_bounds__(R_THREADS, 1)
       if (!warp_wait(d2_full, c & 1, a.err, abort_flag)) break;
       tc_fence_after();
       const float ec = a.Ec[(((int64_t)(b * 2 + 1) * a.Hv + h) * nb + c)];
+      uint32_t spk[32];  // bf16 pairs of this thread's S^T row (k 64 hf + 2i, +1)
       {
         uint32_t r0[32], r1[32];
         tmem_ld32r(tmem + lane_base + DS_COL + hf * 64, r0);
@@ -661,10 +664,9 @@ __global__ void __launch_bounds__(R_THREADS, 1)
           S[i] = ec * S[i] + __uint_as_float(r0[i]);
           S[32 + i] = ec * S[32 + i] + __uint_as_float(r1[i]);
         }
-        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pk[i] = pack2(S[2 * i], S[2 * i + 1]);
-        tmem_st32r(tmem + lane_base + SA_COL + hf * 32, pk);
+        for (int i = 0; i < 32; ++i) spk[i] = pack2(S[2 * i], S[2 * i + 1]);
+        tmem_st32r(tmem + lane_base + SA_COL + hf * 32, spk);
       }
       {
         uint32_t oc[16], on[16];
@@ -683,9 +685,10 @@ __global__ void __launch_bounds__(R_THREADS, 1)
         }
       }
       if (c + 1 < nb) {
-        float* dst = a.S_in + ((((int64_t)b * nb + c + 1) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+        // row v of S^T (this thread's 64 k values, already packed as bf16 pairs for TMEM)
+        uint4* dst = reinterpret_cast<uint4*>(a.S_in + ((((int64_t)b * nb + c + 1) * a.Hv + h) * D + v) * D + hf * 64);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) dst[i * D] = S[i];
+        for (int i = 0; i < 8; ++i) dst[i] = make_uint4(spk[4 * i], spk[4 * i + 1], spk[4 * i + 2], spk[4 * i + 3]);
       }
     }
   }
@@ -709,7 +712,7 @@ __global__ void __launch_bounds__(R_THREADS, 1)
 // TMA loads them; P enters transposed (K-major B).
 struct BArgs {
   const float* Ec;  // [NCH]
-  float* dS_out;    // [B, nb, Hv, 128, 128]
+  __nv_bfloat16* dS_out;  // dS_out^T per chunk: [B, nb, Hv, 128 (v), 128 (k)]
   float* dVp;       // [B, nb, Hv, 32, 128]
   int B, L, Hv, nb;
   int* err;
@@ -852,9 +855,9 @@ __global__ void __launch_bounds__(R_THREADS, 1)
 #pragma unroll
       for (int i = 0; i < 32; ++i) z[i] = 0u;
       tmem_st32r(tmem + lane_base + SA_COL + hf * 32, z);
-      float* dst = a.dS_out + ((((int64_t)b * nb + nb - 1) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+      uint4* dst = reinterpret_cast<uint4*>(a.dS_out + ((((int64_t)b * nb + nb - 1) * a.Hv + h) * D + v) * D + hf * 64);
 #pragma unroll
-      for (int i = 0; i < 64; ++i) dst[i * D] = 0.f;  // nothing flows back from after the last chunk
+      for (int i = 0; i < 8; ++i) dst[i] = make_uint4(0, 0, 0, 0);  // nothing flows back after the last chunk
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -890,6 +893,7 @@ __global__ void __launch_bounds__(R_THREADS, 1)
       if (!warp_wait(d2_full, i & 1, a.err, abort_flag)) break;
       tc_fence_after();
       const float ec = a.Ec[(((int64_t)(b * 2 + 1) * a.Hv + h) * nb + c)];
+      uint32_t pk[32];  // bf16 pairs of this thread's dS^T row
       {
         uint32_t r0[32], r1[32];
         tmem_ld32r(tmem + lane_base + DS_COL + hf * 64, r0);
@@ -899,7 +903,6 @@ __global__ void __launch_bounds__(R_THREADS, 1)
           S[j] = ec * S[j] + __uint_as_float(r0[j]);
           S[32 + j] = ec * S[32 + j] + __uint_as_float(r1[j]);
         }
-        uint32_t pk[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) pk[j] = pack2(S[2 * j], S[2 * j + 1]);
         tmem_st32r(tmem + lane_base + SA_COL + hf * 32, pk);
@@ -910,9 +913,9 @@ __global__ void __launch_bounds__(R_THREADS, 1)
       if (lane == 0) mbar_arrive(sa_ready);
       if (warp == 0 && lane == 0) mbar_arrive(&empty[s]);
       if (c > 0) {
-        float* dst = a.dS_out + ((((int64_t)b * nb + c - 1) * a.Hv + h) * D) * D + (int64_t)(hf * 64) * D + v;
+        uint4* dst = reinterpret_cast<uint4*>(a.dS_out + ((((int64_t)b * nb + c - 1) * a.Hv + h) * D + v) * D + hf * 64);
 #pragma unroll
-        for (int j = 0; j < 64; ++j) dst[j * D] = S[j];
+        for (int j = 0; j < 8; ++j) dst[j] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
       }
     }
   }
@@ -972,7 +975,7 @@ std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, con
   auto tiles = at::empty({4, nch * C, 128}, bf);  // U, W, q~, K~
   auto P = at::empty({nch * C, 64}, bf);
   auto Ec = at::empty({nch}, f32);
-  auto S_in = at::empty({B, nb, Hv, 128, 128}, f32);
+  auto S_in = at::empty({B, nb, Hv, 128, 128}, bf);  // S^T rows (v, k)
   auto o = at::empty({B, 2 * L, Hv, 128}, q.options());
   int* err = error_word_ptr();
   auto st = at::cuda::getCurrentCUDAStream();
@@ -1000,7 +1003,8 @@ std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, con
   static thread_local RecurLaunch rl;
   make_map_bf16(&rl.mt, tiles.data_ptr(), 128, (uint64_t)4 * nch * C, 128, 64, C);
   make_map_bf16(&rl.mp, P.data_ptr(), 64, (uint64_t)nch * C, 64, 64, C);
-  rl.args = RArgs{Ec.data_ptr<float>(), tb, S_in.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(o.data_ptr()),
+  rl.args = RArgs{Ec.data_ptr<float>(), tb, reinterpret_cast<__nv_bfloat16*>(S_in.data_ptr()),
+                  reinterpret_cast<__nv_bfloat16*>(o.data_ptr()),
                   B, (int)L, Hv, nb, err};
   {
     void* kargs[3] = {&rl.mt, &rl.mp, &rl.args};
@@ -1013,9 +1017,11 @@ std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, con
 // The backward's sequential part on tcgen05 for the fork layout (head dim 128, chunk 32): reruns the
 // prep kernel (W, q~, K~, P^T, e^gam_C of both streams) and the reverse recurrence. dout is bf16
 // contiguous [B, 2L, Hv, 128]; dS_out [B, nb, Hv, 128, 128] and dVp [B, nb, Hv, 32, 128] (fp32) are
-// written: what the clean chunk kernel reads. The noised blocks' state gradients are included.
+// written: what the clean chunk kernel reads (dS_out as bf16 rows of dS_out^T, [v][k] per chunk).
+// The noised blocks' state gradients are included.
 void gdn_bwd_recurrence_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
-                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, float* dS_out, float* dVp) {
+                           const at::Tensor& beta, const at::Tensor& dout, int64_t L, __nv_bfloat16* dS_out,
+                           float* dVp) {
   using namespace gdn_tc;
   const int B = q.size(0), Hk = q.size(2), Hv = v.size(2);
   const int nb = (int)(L / C);

@@ -57,8 +57,9 @@ def test_gdn_tc_forward_matches_fp32(B, L, Hk, Hv):
         _, S_ref, _, _ = gdn_chunked.forward(qc, kc, v[:, L:].float(), gate[:, L:], beta[:, L:], 32)
     _close(o[:, :L], orf[:, :L])  # noised blocks (forked from the clean states)
     _close(o[:, L:], orf[:, L:])  # clean stream
-    # S_in [B, nb, Hv, Dk, Dv] vs the spec's [B, Hv, nb, Dk, Dv]
-    _close(S_in, S_ref.transpose(1, 2))
+    # S_in: bf16 S^T rows [B, nb, Hv, Dv, Dk]; the spec's states are [B, Hv, nb, Dk, Dv]
+    assert S_in.dtype == torch.bfloat16
+    _close(S_in.transpose(-1, -2), S_ref.transpose(1, 2))
 
 
 def test_gdn_tc_forward_matches_the_mma_sync_kernels():
@@ -69,7 +70,7 @@ def test_gdn_tc_forward_matches_the_mma_sync_kernels():
     o, S_in = _C.gdn_fwd_tc(q, k, v, gate.contiguous(), beta.contiguous(), L)
     o2, S2, _ = _C.gdn_fwd(q, k, v, gate.contiguous(), beta.contiguous(), L, 32, False)
     _close(o, o2)
-    _close(S_in, S2)
+    _close(S_in.transpose(-1, -2), S2)
 
 
 def test_gdn_tc_op_forward_backward_against_autograd():

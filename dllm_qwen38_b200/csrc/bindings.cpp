@@ -7,6 +7,7 @@ void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool
           int64_t ldr, const c10::optional<at::Tensor>& gu, int64_t bn, double alpha,
           const c10::optional<at::Tensor>& alpha_t);
 at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu);
+at::Tensor group_sum(const at::Tensor& x, int64_t groups);
 at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode);
 std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
                                  int64_t block, int64_t mode);
@@ -115,6 +116,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &bdllm::adamw_step);
   m.def("sumsq_", &bdllm::sumsq_, "sq += ||x||^2 (optionally writing x as fp32)", py::arg("x"), py::arg("sq"),
         py::arg("dst") = c10::nullopt);
+  m.def("group_sum", &bdllm::group_sum, "GQA: bf16 [..., H, D] summed over each of `groups` head groups");
   m.def("gdn_fwd", &bdllm::gdn_fwd, "state-fork chunked gated delta rule forward");
   m.def("gdn_tc_eligible", &bdllm::gdn_tc_eligible, "whether the tcgen05 GDN forward takes this problem");
   m.def("gdn_fwd_tc", &bdllm::gdn_fwd_tc, "state-fork GDN forward on tcgen05 / TMEM / TMA (head dim 128, chunk 32)");

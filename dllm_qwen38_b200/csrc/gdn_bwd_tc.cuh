@@ -470,15 +470,8 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       rs += g1;
       dp[j] = g1;
     }
-    // column sums of G1 across lanes: transpose through shuffles (token j's column total)
-    float cs_mine = 0.f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float v = dp[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == j) cs_mine = v;
-    }
+    // column sums of G1 across lanes (token `lane`'s column total)
+    const float cs_mine = fold32(dp, lane);
     sdgam[lane] += rs - cs_mine;
   }
   __syncthreads();
@@ -574,15 +567,8 @@ __global__ void __launch_bounds__(btc::NTH, 1)
       rsB += dA * kkv * gm;
       rsH += h2[j];
     }
-    // column sums of H2 and the transpose of dKK through shuffles
-    float csH = 0.f;
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float v = h2[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == j) csH = v;
-    }
+    // column sums of H2 (token `lane`'s column total)
+    const float csH = fold32(h2, lane);
     sdgam[lane] += rsH - csH;
     sdb[lane] += rsB;
     // sym = dKK + dKK^T (dKK rows through the token buffer for the transpose)

@@ -3,6 +3,7 @@
 //   conv_fwd/bwd   the state-fork short causal conv + SiLU over the [B, 2L, C] two-stream layout
 //   ce_rows        per-row log-sum-exp over the vocabulary, loss, and dlogits written in place
 //   adamw          fused clip-scale + AdamW on fp32 master weights, bf16 parameter write-back
+//   group_sum      GQA: per-v-head gradients summed over each k-head's group, bf16 in and out
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -738,6 +739,49 @@ std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& db
       dbc.data_ptr<float>(), H, rows, bfp(da), bfp(db), dA.data_ptr<float>(), ddt.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {da, db, dA, ddt};
+}
+
+// ------------------------------------------------------------------------------- group_sum
+// x [rows, G, R, D] bf16 -> out [rows, G, D] bf16, summed over R in fp32 (one pass, 16-byte vectors):
+// the GDN kernels give dq / dk per v-head, and each k-head's gradient is the sum over its group.
+__global__ void group_sum_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out, int64_t n8,
+                                 int R, int D8) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t rg = i / D8;  // (row, group)
+    const int c = (int)(i % D8);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < R; ++r) {
+      const uint4 u = *reinterpret_cast<const uint4*>(x + ((rg * R + r) * D8 + c) * 8);
+      const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(p[e]);
+        acc[2 * e] += f.x, acc[2 * e + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* po = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) po[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+    *reinterpret_cast<uint4*>(out + i * 8) = o;
+  }
+}
+
+at::Tensor group_sum(const at::Tensor& x, int64_t groups) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() >= 2,
+              "group_sum: contiguous bf16 [..., H, D]");
+  const int64_t D = x.size(-1), H = x.size(-2);
+  TORCH_CHECK(D % 8 == 0 && groups > 0 && H % groups == 0, "group_sum: D % 8 == 0 and H divisible by groups");
+  const int R = (int)(H / groups);
+  std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
+  shape[shape.size() - 2] = groups;
+  auto out = at::empty(shape, x.options());
+  const int64_t n8 = out.numel() / 8;
+  if (n8 == 0) return out;
+  c10::cuda::CUDAGuard gd(x.device());
+  group_sum_kernel<<<grid_for(n8), 256, 0, stream()>>>(cbf(x), bfp(out), n8, R, (int)(D / 8));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
 }
 
 }  // namespace bdllm

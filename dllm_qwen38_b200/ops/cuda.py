@@ -450,10 +450,10 @@ class _GDNCore(torch.autograd.Function):
         dq, dk, dv, dg, db = _C.gdn_bwd(do, q, k, v, gf, bf, S_in, L, block, concat)
         _count(3 if concat else 4)
         Hk, Hv = q.shape[2], v.shape[2]
-        if Hv != Hk:  # the kernel returns per-v-head gradients; sum each repeat group
-            B, T2, _, Dk = dq.shape
-            dq = dq.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(q.dtype)
-            dk = dk.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(k.dtype)
+        if Hv != Hk:  # the kernel returns per-v-head gradients; sum each repeat group (one pass each)
+            dq = _C.group_sum(dq, Hk)
+            dk = _C.group_sum(dk, Hk)
+            _count(2)
         return dq, dk, dv, dg.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None, None, None
 
 
@@ -551,10 +551,10 @@ class _GDNCoreBlocks(torch.autograd.Function):
 
         dq, dk, dv, dg, db = cat(dqt, dq0), cat(dkt, dk0), cat(dvt, dv0), cat(dgt, dg0), cat(dbt, db0)
         Hk, Hv = clean[0].shape[2], clean[2].shape[2]
-        if Hv != Hk:  # per-v-head gradients: sum each repeat group
-            T2, Dk = dq.shape[1], dq.shape[3]
-            dq = dq.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(clean[0].dtype)
-            dk = dk.view(B, T2, Hk, Hv // Hk, Dk).float().sum(3).to(clean[1].dtype)
+        if Hv != Hk:  # per-v-head gradients: sum each repeat group (one pass each)
+            dq = _C.group_sum(dq.to(torch.bfloat16).contiguous(), Hk).to(clean[0].dtype)
+            dk = _C.group_sum(dk.to(torch.bfloat16).contiguous(), Hk).to(clean[1].dtype)
+            _count(2)
         return dq, dk, dv, dg.to(ctx.dtypes[0]), db.to(ctx.dtypes[1]), None, None
 
 

@@ -8,6 +8,9 @@ void gemm(const at::Tensor& a, bool a_mn, int64_t lda, const at::Tensor& b, bool
           const c10::optional<at::Tensor>& alpha_t);
 at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu);
 at::Tensor group_sum(const at::Tensor& x, int64_t groups);
+std::vector<at::Tensor> mask_sample(const at::Tensor& x0, const at::Tensor& prompt_len,
+                                    const c10::optional<at::Tensor>& valid_len, int64_t block, int64_t mask_id,
+                                    int64_t seed);
 at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode);
 std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
                                  int64_t block, int64_t mode);
@@ -116,6 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &bdllm::adamw_step);
   m.def("sumsq_", &bdllm::sumsq_, "sq += ||x||^2 (optionally writing x as fp32)", py::arg("x"), py::arg("sq"),
         py::arg("dst") = c10::nullopt);
+  m.def("mask_sample", &bdllm::mask_sample, "complementary masks and both noised views of a step, one launch");
   m.def("group_sum", &bdllm::group_sum, "GQA: bf16 [..., H, D] summed over each of `groups` head groups");
   m.def("gdn_fwd", &bdllm::gdn_fwd, "state-fork chunked gated delta rule forward");
   m.def("gdn_tc_eligible", &bdllm::gdn_tc_eligible, "whether the tcgen05 GDN forward takes this problem");

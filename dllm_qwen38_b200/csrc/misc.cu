@@ -4,6 +4,7 @@
 //   ce_rows        per-row log-sum-exp over the vocabulary, loss, and dlogits written in place
 //   adamw          fused clip-scale + AdamW on fp32 master weights, bf16 parameter write-back
 //   group_sum      GQA: per-v-head gradients summed over each k-head's group, bf16 in and out
+//   mask_sample    the complementary masks of a step and both noised views, one launch
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -782,6 +783,62 @@ at::Tensor group_sum(const at::Tensor& x, int64_t groups) {
   group_sum_kernel<<<grid_for(n8), 256, 0, stream()>>>(cbf(x), bfp(out), n8, R, (int)(D / 8));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
+}
+
+// ------------------------------------------------------------------------------- mask_sample
+// Counter-based uniforms: the SplitMix64 output function (Steele, Lea and Flood, "Fast splittable
+// pseudorandom number generators", OOPSLA 2014) applied to a key made of (seed, row, position,
+// stream), top 24 bits as a float in [0, 1). No state: any thread draws any element.
+__device__ __forceinline__ float key_uniform(uint64_t seed, uint64_t a, uint64_t b) {
+  uint64_t z = seed + 0x9E3779B97F4A7C15ull * (a * 0x100000001B3ull + b + 1);
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  z ^= z >> 31;
+  return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+// One thread per (row, position): t = U(row, block) (the block's mask ratio), u = U(row, position);
+// m = u < t on scorable positions (prompt_len <= i < valid_len). Writes rows [0, B) of the outputs
+// for view m and rows [B, 2B) for the complement: x0_2 = x0 twice, xt_2 = x0 with [MASK] where
+// the view masks, m_2 the view's mask.
+__global__ void mask_sample_kernel(const int64_t* __restrict__ x0, const int64_t* __restrict__ plen,
+                                   const int64_t* __restrict__ vlen, int B, int L, int block, int64_t mask_id,
+                                   uint64_t seed, int64_t* __restrict__ x0_2, int64_t* __restrict__ xt_2,
+                                   bool* __restrict__ m_2) {
+  const int64_t n = (int64_t)B * L;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < n; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int b = (int)(idx / L), i = (int)(idx % L);
+    const float t = key_uniform(seed, (uint64_t)b, (uint64_t)(i / block) * 2 + 1);
+    const float u = key_uniform(seed, (uint64_t)b + (1ull << 32), (uint64_t)i * 2);
+    const bool scor = i >= plen[b] && (vlen == nullptr || i < vlen[b]);
+    const bool m = scor && u < t, mc = scor && !m;
+    const int64_t x = x0[idx], o = idx + n;
+    x0_2[idx] = x, x0_2[o] = x;
+    xt_2[idx] = m ? mask_id : x, xt_2[o] = mc ? mask_id : x;
+    m_2[idx] = m, m_2[o] = mc;
+  }
+}
+
+std::vector<at::Tensor> mask_sample(const at::Tensor& x0, const at::Tensor& prompt_len,
+                                    const c10::optional<at::Tensor>& valid_len, int64_t block, int64_t mask_id,
+                                    int64_t seed) {
+  TORCH_CHECK(x0.is_cuda() && x0.dim() == 2 && x0.scalar_type() == at::kLong, "mask_sample: int64 [B, L] on CUDA");
+  const int B = x0.size(0), L = x0.size(1);
+  TORCH_CHECK(block > 0 && L % block == 0, "mask_sample: block must divide L");
+  auto xc = x0.contiguous();
+  auto pl = prompt_len.to(x0.device(), at::kLong).contiguous();
+  at::Tensor vl;
+  if (valid_len.has_value()) vl = valid_len->to(x0.device(), at::kLong).contiguous();
+  TORCH_CHECK(pl.numel() == B && (!vl.defined() || vl.numel() == B), "mask_sample: one length per row");
+  auto x0_2 = at::empty({2 * B, L}, x0.options());
+  auto xt_2 = at::empty({2 * B, L}, x0.options());
+  auto m_2 = at::empty({2 * B, L}, x0.options().dtype(at::kBool));
+  c10::cuda::CUDAGuard gd(x0.device());
+  mask_sample_kernel<<<grid_for((int64_t)B * L), 256, 0, stream()>>>(
+      xc.data_ptr<int64_t>(), pl.data_ptr<int64_t>(), vl.defined() ? vl.data_ptr<int64_t>() : nullptr, B, L,
+      (int)block, mask_id, (uint64_t)seed, x0_2.data_ptr<int64_t>(), xt_2.data_ptr<int64_t>(), m_2.data_ptr<bool>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {x0_2, xt_2, m_2};
 }
 
 }  // namespace bdllm

@@ -473,7 +473,8 @@ class FSDPEngine:
 
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
-        x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len)
+        x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len,
+                                                    seed=gstep * 1000 + self.rank)
         probe = self.save_gemms == "auto"  # this step keeps no GEMM outputs and measures the peak
         if probe:
             torch.cuda.synchronize(self.device)

@@ -41,8 +41,15 @@ def apply_mask(x0, m, mask_id: int):
     return torch.where(m, torch.full_like(x0, mask_id), x0)
 
 
-def complementary_step_inputs(x0, prompt_len, block: int, mask_id: int, generator=None, valid_len=None):
-    """Both views stacked along batch: (x0_2B, xt_2B, m_2B) (`objective.py:72-76`)."""
+def complementary_step_inputs(x0, prompt_len, block: int, mask_id: int, generator=None, valid_len=None,
+                              seed: int | None = None):
+    """Both views stacked along batch: (x0_2B, xt_2B, m_2B) (`objective.py:72-76`). On CUDA with
+    an integer `seed`, one kernel draws the masks (counter-based: a pure function of the seed and
+    the element's (row, position)) and writes both views; otherwise torch's RNG with `generator`."""
+    if seed is not None and x0.is_cuda:
+        from ..ops import _native
+
+        return tuple(_native.require().mask_sample(x0, prompt_len, valid_len, block, mask_id, seed))
     m, mc = sample_complementary_masks(x0, prompt_len, block, generator, valid_len)
     return torch.cat([x0, x0], 0), torch.cat([apply_mask(x0, m, mask_id), apply_mask(x0, mc, mask_id)], 0), torch.cat([m, mc], 0)
 

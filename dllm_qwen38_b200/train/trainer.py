@@ -50,7 +50,8 @@ class Trainer:
         prompt_len = prompt_len.to(dev, non_blocking=True)
         valid_len = valid_len.to(dev, non_blocking=True)
         gen = torch.Generator(device=dev).manual_seed(self.gstep * 1000 + self.rank)
-        x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, self.block, self.mask_id, gen, valid_len)
+        x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, self.block, self.mask_id, gen, valid_len,
+                                                    seed=self.gstep * 1000 + self.rank)
         ht, _ = block_diffusion_forward(self.model, x0_2, xt_2, self.block, output="hidden",
                                         checkpointing=self.checkpointing)
         if n_targets == 0:

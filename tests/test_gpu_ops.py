@@ -166,3 +166,30 @@ def test_sumsq_with_copy(xdt, ddt, n):
     assert abs(float(sq[0]) - want) < 1e-4 * want
     if dst is not None:
         assert torch.equal(dst, x.to(ddt))
+
+
+def test_mask_sample_kernel_complementary_views():
+    """The fused mask kernel: both views partition the scorable positions, prompt and padding are
+    never noised, [MASK] sits exactly where a view masks, a seed reproduces its masks, and the
+    per-block ratios spread over (0, 1) with mean 1/2 (t ~ U(0, 1) per block)."""
+    from dllm_qwen38_b200.train.objective import complementary_step_inputs
+
+    B, L, block, mask_id = 4, 4096, 32, 999
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x0 = torch.randint(0, 900, (B, L), device="cuda", generator=g)
+    pl = torch.tensor([0, 17, 100, 0], device="cuda")
+    vl = torch.tensor([L, L, L - 50, L - 1], device="cuda")
+    x0_2, xt_2, m_2 = complementary_step_inputs(x0, pl, block, mask_id, None, vl, seed=1234)
+    pos = torch.arange(L, device="cuda")[None]
+    scor = (pos >= pl[:, None]) & (pos < vl[:, None])
+    m, mc = m_2[:B], m_2[B:]
+    assert torch.equal(x0_2[:B], x0) and torch.equal(x0_2[B:], x0)
+    assert not bool((m & mc).any()) and torch.equal(m | mc, scor)
+    assert torch.equal(xt_2, torch.where(m_2, torch.full_like(x0_2, mask_id), x0_2))
+    again = complementary_step_inputs(x0, pl, block, mask_id, None, vl, seed=1234)
+    assert torch.equal(again[2], m_2)
+    other = complementary_step_inputs(x0, pl, block, mask_id, None, vl, seed=1235)
+    assert not torch.equal(other[2], m_2)
+    ratio = m[0].float().view(-1, block).mean(1)  # row 0: every position scorable
+    assert 0.4 < float(ratio.mean()) < 0.6
+    assert float(ratio.min()) < 0.15 and float(ratio.max()) > 0.85

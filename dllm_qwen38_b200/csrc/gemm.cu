@@ -590,25 +590,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // ============================================================================== 2-CTA variant
-// A CTA pair (cluster of 2, cta_group::2) computes 256 x 256 tiles: CTA rank r of the pair loads A
-// rows [m0 + 128 r, +128) and B rows [n0 + 128 r, +128) (for SwiGLU: rank 0 the gate rows, rank 1
-// the up rows) into its own smem; the leader (rank 0) issues M = 256, N = 256 MMAs that read both
-// CTAs' tiles, and each CTA's TMEM receives its 128 rows x 256 columns. Per SM this halves the B
-// operand traffic of the one-CTA 128 x 256 tile and leaves room for 6 pipeline stages. K-major A
-// and B only (the forward projections). Both CTAs' TMA loads complete on the leader's full
-// barriers; the leader's MMA commits arrive on both CTAs' empty / tfull barriers; both CTAs'
-// epilogue warps arrive on the leader's tempty barriers. Every wait is bounded as in gemm_kernel;
-// all paths reach the final cluster barrier.
+// A CTA pair (cluster of 2, cta_group::2) computes 256 x NP tiles (NP = 256 or 512): CTA rank r
+// of the pair loads A rows [m0 + 128 r, +128) into its own smem, and for each of the NP / 256
+// MMAs h of a k step the B rows [n0 + 256 h + 128 r, +128) (for SwiGLU: rank 0 the gate rows,
+// rank 1 the up rows of activation columns [n0 + 128 h, +128)). The leader (rank 0) issues
+// M = 256, N = 256 MMAs that read both CTAs' tiles; each CTA's TMEM receives its 128 rows.
+//   NP = 256: 32 KB per stage, 6 stages, two TMEM accumulators (the epilogue of one tile overlaps
+//             the next tile's MMAs), 4 epilogue warps.
+//   NP = 512: 48 KB per stage (A 16 KB + B 2 x 16 KB), 4 stages, one 512-column accumulator,
+//             8 epilogue warps (warp 2 + e drains lane quadrant (2 + e) % 4 of MMA half e / 4).
+//             Each SM streams 48 instead of 64 bytes per 4096 MACs, a quarter less L2 -> SM
+//             traffic, which under the 1 kW power cap turns into clock. A last partial wave of
+//             tiles is split into half-tiles (one MMA half each) so that the tail takes half as
+//             long, and a tile whose second half lies beyond N skips it.
+// Both CTAs' TMA loads complete on the leader's full barriers; the leader's MMA commits arrive on
+// both CTAs' empty / tfull barriers; both CTAs' epilogue warps arrive on the leader's tempty
+// barriers. Every wait is bounded as in gemm_kernel; all paths reach the final cluster barrier.
 constexpr int STAGES2 = 6;
-template <int EPI, bool A_MN, bool B_MN>
+template <int EPI, bool A_MN, bool B_MN, int NP = 256>
 struct Cfg2 {
-  static constexpr int BN = 256;  // MMA N (both CTAs' B halves)
-  static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? 128 : 256;
+  static_assert(NP == 256 || EPI == EPI_BF16 || EPI == EPI_ADD_BF16, "256 x 512 tiles: bf16 epilogues only");
+  static constexpr int NH = NP / 256;                           // N = 256 MMAs per k step
+  static constexpr int BN = 256;                                // MMA N (both CTAs' B halves)
+  static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? NP / 2 : NP;  // output columns per tile
+  static constexpr int HALF_OUT = BN_OUT / NH;                  // output columns per MMA half
   static constexpr int A_BYTES = 128 * BK * 2;
-  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int B_HALF = 128 * BK * 2;                   // this CTA's rows of one MMA's B
+  static constexpr int B_BYTES = NH * B_HALF;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int SMEM = STAGES2 * STAGE_BYTES + 1024 + 256;
+  static constexpr int ST = (NP == 256) ? STAGES2 : 3;
+  // NP = 512: one MMA half of the output (128 rows x 256 bf16 columns) staged for TMA stores, as
+  // four 128-byte-swizzled blocks of 64 columns
+  static constexpr int STAGING = (NP == 256) ? 0 : 128 * 256 * 2;
+  static constexpr int SMEM = ST * STAGE_BYTES + STAGING + 1024 + 256;
+  static constexpr int NACC = (NP == 256) ? 2 : 1;
   static constexpr int TMEM_COLS = 512;
+  static constexpr int EPI_WARPS = 4 * NH;
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS + 64;  // TMA, MMA, epilogue, 2 all-gather copy warps
   static constexpr uint32_t IDESC = idesc_bf16(256, 256, A_MN ? 1 : 0, B_MN ? 1 : 0);
 };
 
@@ -650,19 +668,64 @@ __device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, u
       : "memory");
 }
 
-template <int EPI, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
-    gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs args) {
-  using C_ = Cfg2<EPI, A_MN, B_MN>;
-  constexpr int STAGES = STAGES2;
+// TMA store (or, with ADD, an element-wise bf16 add in L2) of a 2-D box from this CTA's smem
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  if (!BDLLM_CHECK((x & 7) == 0 && x >= 0 && y >= 0, x, 8)) return;
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  if (!BDLLM_CHECK((x & 7) == 0 && x >= 0 && y >= 0, x, 8)) return;
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void epi_bar_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+
+// Work unit u of the pair kernel -> tile (tm, tn) and the MMA halves [h0, h1) it computes. Units
+// below `full` are whole tiles; the tiles of the last partial wave come as one unit per half.
+// Returns false for a unit with nothing inside N (every role skips it alike).
+template <class C_>
+__device__ __forceinline__ bool pair_unit(int u, int full, int tiles_m, int tiles_n, const GemmArgs& args, int& t,
+                                          int& tm, int& tn, int& h0, int& h1) {
+  if (u < full) {
+    t = u, h0 = 0, h1 = C_::NH;
+  } else {
+    const int v = u - full;
+    t = full + v / C_::NH, h0 = v % C_::NH, h1 = h0 + 1;
+  }
+  tile_coords(t, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
+  const int left = args.N - tn * C_::BN_OUT;  // output columns of this tile inside N
+  const int nvalid = min(C_::NH, (left + C_::HALF_OUT - 1) / C_::HALF_OUT);
+  h1 = min(h1, nvalid);
+  return h0 < h1;
+}
+
+template <int EPI, bool A_MN, bool B_MN, int NP>
+__global__ void __launch_bounds__(Cfg2<EPI, A_MN, B_MN, NP>::THREADS, 1)
+    gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                 const __grid_constant__ CUtensorMap map_c, GemmArgs args) {
+  using C_ = Cfg2<EPI, A_MN, B_MN, NP>;
+  constexpr int STAGES = C_::ST;
+  constexpr bool WIDE = (NP == 512);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * C_::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * C_::STAGE_BYTES);
+  uint8_t* stg = smem + STAGES * C_::STAGE_BYTES;  // output staging (wide tiles), 1024-byte aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(stg + C_::STAGING);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
+  uint64_t* tempty = tfull + 2;  // per accumulator (256 x 256 tiles) or per MMA half (256 x 512)
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -673,6 +736,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int tiles_m = (args.M + 255) / 256;
   const int tiles_n = (args.N + C_::BN_OUT - 1) / C_::BN_OUT;
   const int num_tiles = tiles_m * tiles_n;
+  const int full_units = (C_::NH == 2) ? (num_tiles / npairs) * npairs : num_tiles;
+  const int num_units = full_units + (num_tiles - full_units) * C_::NH;
   const int kblocks = (args.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -682,13 +747,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);  // four epilogue warps in each CTA of the pair
+      mbar_init(&tempty[a], 2 * C_::EPI_WARPS);  // the epilogue warps of both CTAs of the pair
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&map_a);
     prefetch_tmap(&map_b);
+    if constexpr (WIDE) prefetch_tmap(&map_c);
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -710,29 +776,34 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint32_t round = 0;
     uint32_t armed_mask = 0;
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += npairs) {
-      int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
+    for (int u = pair; u < num_units && ok; u += npairs) {
+      int t, tm, tn, h0, h1;
+      if (!pair_unit<C_>(u, full_units, tiles_m, tiles_n, args, t, tm, tn, h0, h1)) continue;
       const int m0 = tm * 256 + (int)crank * 128;
       const int n0 = tn * C_::BN_OUT;
-      const int bn0 = (EPI == EPI_SWIGLU) ? (crank ? args.N + n0 : n0) : n0 + (int)crank * 128;
+      // this CTA's B rows of MMA half h
+      auto brow = [&](int h) {
+        return (EPI == EPI_SWIGLU) ? (crank ? args.N : 0) + n0 + h * 128 : n0 + h * 256 + (int)crank * 128;
+      };
       if constexpr (!B_MN) {
-        if (args.ag_nchunks > 0) {  // fused all-gather: this CTA's 128 weight rows must have landed
+        if (args.ag_nchunks > 0) {  // fused all-gather: this CTA's weight rows must have landed
           const int64_t rb = (int64_t)args.K * 2;
           const int64_t rows_total = (EPI == EPI_SWIGLU) ? 2 * (int64_t)args.N : (int64_t)args.N;
-          const int64_t r1 = min((int64_t)bn0 + 128, rows_total);
-          if (r1 > bn0 && !ag_wait_range(args, args.ag_b_off + (int64_t)bn0 * rb, args.ag_b_off + r1 * rb, abort_flag)) {
-            ok = false;
-            break;
+          for (int h = h0; h < h1 && ok; ++h) {
+            const int64_t r0 = brow(h), r1 = min(r0 + 128, rows_total);
+            if (r1 > r0 && !ag_wait_range(args, args.ag_b_off + r0 * rb, args.ag_b_off + r1 * rb, abort_flag))
+              ok = false;
           }
+          if (!ok) break;
         }
       }
+      const uint32_t tx = 2u * (uint32_t)(C_::A_BYTES + (h1 - h0) * C_::B_HALF);  // both CTAs' bytes
       for (int kb = 0; kb < kblocks; ++kb) {
         if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
           break;
         }
-        if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * C_::STAGE_BYTES);  // both CTAs' bytes
+        if (crank == 0) mbar_arrive_expect_tx(&full[stage], tx);
         armed_mask |= 1u << stage;
         const int k0 = kb * BK;
         const uint32_t bar = full0 + stage * 8;
@@ -744,11 +815,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           tma_load_2d_pair(a_dst, &map_a, bar, m0, k0);
           tma_load_2d_pair(a_dst + 8192, &map_a, bar, m0 + 64, k0);
         }
-        if constexpr (!B_MN) {
-          tma_load_2d_pair(b_dst, &map_b, bar, k0, bn0);
-        } else {
-          tma_load_2d_pair(b_dst, &map_b, bar, bn0, k0);
-          tma_load_2d_pair(b_dst + 8192, &map_b, bar, bn0 + 64, k0);
+        for (int h = h0; h < h1; ++h) {
+          uint8_t* bh = b_dst + h * C_::B_HALF;
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(bh, &map_b, bar, k0, brow(h));
+          } else {
+            tma_load_2d_pair(bh, &map_b, bar, brow(h), k0);
+            tma_load_2d_pair(bh + 8192, &map_b, bar, brow(h) + 64, k0);
+          }
         }
         if (++stage == STAGES) {
           stage = 0;
@@ -766,33 +840,88 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int stage = 0;
     uint32_t round = 0;
     int it = 0;
+    uint32_t hal_use0 = 0, hal_use1 = 0;  // wide tiles: units that used MMA half 0 / 1 so far
     bool ok = true;
-    for (int t = pair; t < num_tiles && ok; t += npairs, ++it) {
-      const int acc = it & 1;
-      const uint32_t use = it >> 1;
-      if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
-        ok = false;
-        break;
+    // the 4 k16 MMAs of one stage for MMA half h
+    auto mma_stage = [&](int s2, int h, uint32_t d_tmem, bool first) {
+      const uint32_t a_addr = smem_u32(sa + s2 * C_::A_BYTES);
+      const uint32_t bh = smem_u32(sb + s2 * C_::B_BYTES) + h * C_::B_HALF;
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, 8192, 1024) : smem_desc(a_addr + k * 32, 16, 1024);
+        const uint64_t bd = B_MN ? smem_desc(bh + k * 2048, 8192, 1024) : smem_desc(bh + k * 32, 16, 1024);
+        mma_bf16_pair(d_tmem + h * C_::BN, ad, bd, C_::IDESC, (!first || k > 0) ? 1u : 0u);
       }
-      tc_fence_after();
+    };
+    auto free_stage = [&](int s2) {
+      const uint32_t e = smem_u32(&empty[s2]);
+      commit2(map_to(e, 0));  // frees this stage in both CTAs once the MMAs have read it
+      commit2(map_to(e, 1));
+    };
+    for (int u = pair; u < num_units && ok; u += npairs) {
+      int t, tm, tn, h0, h1;
+      if (!pair_unit<C_>(u, full_units, tiles_m, tiles_n, args, t, tm, tn, h0, h1)) continue;
+      const int acc = (C_::NACC == 2) ? (it & 1) : 0;
+      const uint32_t use = (C_::NACC == 2) ? (uint32_t)(it >> 1) : (uint32_t)it;
+      ++it;
       const uint32_t d_tmem = tmem_base + acc * C_::BN;
-      for (int kb = 0; kb < kblocks; ++kb) {
+      int kb = 0;
+      if constexpr (WIDE) {
+        // Each MMA half is released by the epilogue on its own. A whole tile runs half 0 over the
+        // first stages while half 1 of the previous tile drains, then half 1 over the same stages
+        // (still resident), then both halves per stage.
+        if (!mbar_wait(&tempty[h0], ((h0 ? hal_use1 : hal_use0) & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (h1 - h0 == 2) {
+          const int P = min(STAGES, kblocks);
+          int s2 = stage;
+          uint32_t r2 = round;
+          for (int j = 0; j < P && ok; ++j) {
+            if (!mbar_wait(&full[s2], r2 & 1, args.err, ERR_GEMM_WAIT, abort_flag)) ok = false;
+            if (!ok) break;
+            tc_fence_after();
+            mma_stage(s2, 0, d_tmem, j == 0);
+            if (++s2 == STAGES) {
+              s2 = 0;
+              ++r2;
+            }
+          }
+          if (!ok) break;
+          if (!mbar_wait(&tempty[1], (hal_use1 & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int j = 0; j < P; ++j) {
+            mma_stage(stage, 1, d_tmem, j == 0);
+            free_stage(stage);
+            if (++stage == STAGES) {
+              stage = 0;
+              ++round;
+            }
+          }
+          kb = P;
+        }
+        hal_use0 += (h0 == 0);
+        hal_use1 += (h1 == 2);
+      } else {
+        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      for (; kb < kblocks; ++kb) {
         if (!mbar_wait(&full[stage], round & 1, args.err, ERR_GEMM_WAIT, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(sa + stage * C_::A_BYTES);
-        const uint32_t b_addr = smem_u32(sb + stage * C_::B_BYTES);
-#pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          const uint64_t ad = A_MN ? smem_desc(a_addr + k * 2048, 8192, 1024) : smem_desc(a_addr + k * 32, 16, 1024);
-          const uint64_t bd = B_MN ? smem_desc(b_addr + k * 2048, 8192, 1024) : smem_desc(b_addr + k * 32, 16, 1024);
-          mma_bf16_pair(d_tmem, ad, bd, C_::IDESC, (kb > 0 || k > 0) ? 1u : 0u);
-        }
-        const uint32_t e = smem_u32(&empty[stage]);
-        commit2(map_to(e, 0));  // frees this stage in both CTAs once the MMAs have read it
-        commit2(map_to(e, 1));
+        for (int h = h0; h < h1; ++h) mma_stage(stage, h, d_tmem, kb == 0);
+        free_stage(stage);
         if (++stage == STAGES) {
           stage = 0;
           ++round;
@@ -808,27 +937,93 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       commit2(map_to(smem_u32(drain), 0));
       mbar_wait(drain, 0, args.err, ERR_GEMM_WAIT, nullptr);
     }
-  } else if (warp >= 2 && warp < 6) {
+  } else if (warp >= 2 && warp < 2 + C_::EPI_WARPS) {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     const int quad = warp & 3;
     const int row_in_tile = quad * 32 + lane;
     int it = 0;
-    for (int t = pair; t < num_tiles; t += npairs, ++it) {
-      const int acc = it & 1;
-      const uint32_t use = it >> 1;
-      if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
-      tc_fence_after();
-      int tm, tn;
-      tile_coords(t, tiles_m, tiles_n, args.raster_g, args.raster_n, tm, tn);
-      const int row = tm * 256 + (int)crank * 128 + row_in_tile;
-      const int n0 = tn * C_::BN_OUT;
-      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * C_::BN;
-      epilogue_tile<256, EPI>(args, t_row, row, row < args.M, n0, 0, t, num_tiles, 1, lane);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) arrive_remote(tempty0 + acc * 8);
+    if constexpr (WIDE) {
+      // Per MMA half: TMEM -> registers -> bf16 -> the swizzled staging blocks (warp 2 + e takes
+      // lane quadrant quad and columns [128 (e / 4), +128) of the half), release the half's TMEM,
+      // then one thread stores (or adds) the staged half with four TMA box copies of 64 x 128.
+      const int cbase = ((warp - 2) / 4) * 128;
+      const bool leader_thread = (warp == 2 && lane == 0);
+      const float alpha_h = args.alpha;
+      for (int u = pair; u < num_units; u += npairs) {
+        int t, tm, tn, h0, h1;
+        if (!pair_unit<C_>(u, full_units, tiles_m, tiles_n, args, t, tm, tn, h0, h1)) continue;
+        const uint32_t use = (uint32_t)it;
+        ++it;
+        // every epilogue warp runs every unit and both named barriers, whatever its wait returned
+        // (a warp leaving the loop early would strand the others at a barrier); after a failed
+        // wait (the abort flag is set) the work is skipped and later waits return at once
+        const bool live = mbar_wait(&tfull[0], use & 1, args.err, ERR_GEMM_WAIT, abort_flag);
+        tc_fence_after();
+        const float alpha = args.alpha_dev != nullptr ? alpha_h * __ldg(args.alpha_dev) : alpha_h;
+        const int row0 = tm * 256 + (int)crank * 128;
+        for (int h = h0; h < h1; ++h) {
+          if (leader_thread) bulk_wait_read0();  // the previous half's stores have read the staging
+          epi_bar_sync(32 * C_::EPI_WARPS);
+          if (!live) {
+            epi_bar_sync(32 * C_::EPI_WARPS);
+            continue;
+          }
+          const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + h * C_::BN + cbase;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float v[32];
+            tmem_ld32(t_row + c * 32, v);
+            const int col = cbase + c * 32;  // column within the half
+            uint8_t* blk = stg + (col / 64) * 16384 + row_in_tile * 128;
+            const int ch0 = (col % 64) / 8;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 pk;
+              __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(v[8 * q + 2 * e] * alpha, v[8 * q + 2 * e + 1] * alpha);
+              *reinterpret_cast<uint4*>(blk + (((ch0 + q) ^ (row_in_tile & 7)) << 4)) = pk;
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) arrive_remote(tempty0 + h * 8);  // this half's TMEM may be overwritten
+          fence_proxy_async_smem();
+          epi_bar_sync(32 * C_::EPI_WARPS);
+          if (leader_thread && row0 < args.M) {
+            const int x0 = tn * C_::BN_OUT + h * C_::HALF_OUT;
+#pragma unroll 1
+            for (int b = 0; b < 4; ++b) {
+              if (x0 + b * 64 >= args.N) break;
+              if constexpr (EPI == EPI_ADD_BF16)
+                tma_reduce_add_2d(&map_c, stg + b * 16384, x0 + b * 64, row0);
+              else
+                tma_store_2d(&map_c, stg + b * 16384, x0 + b * 64, row0);
+            }
+            bulk_commit();
+          }
+        }
+      }
+      if (leader_thread) bulk_wait0();  // every store has landed before the CTA exits
+    } else {
+      for (int u = pair; u < num_units; u += npairs) {
+        int t, tm, tn, h0, h1;
+        if (!pair_unit<C_>(u, full_units, tiles_m, tiles_n, args, t, tm, tn, h0, h1)) continue;
+        const int acc = (C_::NACC == 2) ? (it & 1) : 0;
+        const uint32_t use = (C_::NACC == 2) ? (uint32_t)(it >> 1) : (uint32_t)it;
+        ++it;
+        if (!mbar_wait(&tfull[acc], use & 1, args.err, ERR_GEMM_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const int row = tm * 256 + (int)crank * 128 + row_in_tile;
+        const int n0 = tn * C_::BN_OUT;
+        const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * C_::BN;
+        epilogue_tile<256, EPI>(args, t_row, row, row < args.M, n0, 0, t, num_tiles, 1, lane);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) arrive_remote(tempty0 + acc * 8);
+      }
     }
-  } else if (warp >= 6) {
+  } else if (warp >= 2 + C_::EPI_WARPS) {
     // ---------------------------------------------------------------- fused all-gather copies
     if (args.ag_nchunks > 0) ag_copy_warp(args, lane, abort_flag);
   }
@@ -880,6 +1075,7 @@ void make_map_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t out
 struct alignas(64) GemmLaunch {
   CUtensorMap ma;
   CUtensorMap mb;
+  CUtensorMap mc;  // the output, for the TMA-store epilogue of the 256 x 512 pair kernel
   GemmArgs args;
 };
 static thread_local GemmLaunch tls_launch;
@@ -922,9 +1118,9 @@ static int num_sms() {
 }
 
 // CTA pairs: for GEMMs large enough to give every pair a few 256 x 256 tiles, any operand majors
-// (SwiGLU: K-major only), with or without the fused all-gather (warps 6-7 of both CTAs copy the
-// weight's chunks; each CTA's producer waits for its own 128 weight rows) (BDLLM_GEMM_PAIR=0 keeps
-// the one-CTA kernel)
+// (SwiGLU: K-major only), with or without the fused all-gather (the last two warps of both CTAs
+// copy the weight's chunks; each CTA's producer waits for its own weight rows) (BDLLM_GEMM_PAIR=0
+// keeps the one-CTA kernel)
 static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, const void* tp, const void* ag) {
   static int env = -1;
   if (env < 0) {
@@ -937,6 +1133,13 @@ static bool use_pair(bool a_mn, bool b_mn, int64_t M, int64_t N, int64_t epi, co
   if (!(epi == EPI_BF16 || epi == EPI_F32 || epi == EPI_ADD_BF16 || epi == EPI_SWIGLU)) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256));
   return M >= 512 && tiles >= 148;
+}
+
+// Tile width of the pair kernel: 256 x 512 (BDLLM_GEMM_WIDE unset or not "0") or 256 x 256.
+// Read at every call, so that a test can compare both in one process.
+static bool pair_wide() {
+  const char* e = getenv("BDLLM_GEMM_WIDE");
+  return e == nullptr || e[0] != '0';
 }
 
 // Tile raster of the pair kernel. BDLLM_GEMM_RASTER: "m<G>" / "n<G>" fixes G tile rows along M /
@@ -970,21 +1173,23 @@ static void choose_raster(GemmArgs& g, int64_t M, int64_t NB, int64_t K, int til
   g.raster_g = tn < tm ? gn : gm;
 }
 
-template <int EPI, bool A_MN, bool B_MN>
+template <int EPI, bool A_MN, bool B_MN, int NP>
 static void launch_pair(GemmLaunch* L, cudaStream_t st) {
-  using C_ = Cfg2<EPI, A_MN, B_MN>;
-  auto kern = gemm2_kernel<EPI, A_MN, B_MN>;
+  using C_ = Cfg2<EPI, A_MN, B_MN, NP>;
+  auto kern = gemm2_kernel<EPI, A_MN, B_MN, NP>;
   static bool attr = false;
   if (!attr) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C_::SMEM));
     attr = true;
   }
   const GemmArgs& args = L->args;
+  // at most one pair per work unit (a tile, or each half of a tile when there are fewer tiles
+  // than pairs)
   const int tiles = (int)(((args.M + 255) / 256) * ((args.N + C_::BN_OUT - 1) / C_::BN_OUT));
-  const int pairs = std::max(1, std::min(tiles, num_sms() / 2));
+  const int pairs = std::max(1, std::min(tiles * C_::NH, num_sms() / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(NUM_THREADS);
+  cfg.blockDim = dim3(C_::THREADS);
   cfg.dynamicSmemBytes = C_::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attrs[1];
@@ -994,7 +1199,7 @@ static void launch_pair(GemmLaunch* L, cudaStream_t st) {
   attrs[0].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  void* kargs[3] = {&L->ma, &L->mb, &L->args};
+  void* kargs[4] = {&L->ma, &L->mb, &L->mc, &L->args};
   C10_CUDA_CHECK(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), kargs));
 }
 
@@ -1354,8 +1559,10 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   GTRACE("args ok");
   // the CTA-pair kernel for large forward (K-major) GEMMs
   if (use_pair(a_mn, b_mn, M, N, epi, tp, ag)) {
-    choose_raster(args, M, epi == EPI_SWIGLU ? 2 * N : N, K, (int)((M + 255) / 256),
-                  (int)((N + (epi == EPI_SWIGLU ? 127 : 255)) / (epi == EPI_SWIGLU ? 128 : 256)));
+    // 256 x 512 tiles for bf16 outputs (an add only in place: the TMA reduce adds into C itself)
+    const bool wide = pair_wide() && (epi == EPI_BF16 || (epi == EPI_ADD_BF16 && args.R == c.data_ptr() && ldr == ldc));
+    const int64_t tile_out = (epi == EPI_SWIGLU ? 128 : 256) * (wide ? 2 : 1);
+    choose_raster(args, M, epi == EPI_SWIGLU ? 2 * N : N, K, (int)((M + 255) / 256), (int)((N + tile_out - 1) / tile_out));
     if (a_mn)
       make_map_bf16(&L->ma, a.data_ptr(), M, K, lda, 64, 64);
     else
@@ -1364,11 +1571,28 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
       make_map_bf16(&L->mb, b.data_ptr(), N, K, ldb, 64, 64);
     else
       make_map_bf16(&L->mb, b.data_ptr(), K, epi == EPI_SWIGLU ? 2 * N : N, ldb, 64, 128);
+    if (wide) {
+      TORCH_CHECK(reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0 && (ldc * 2) % 16 == 0,
+                  "gemm: TMA-store output must have 16-byte aligned rows");
+      make_map_bf16(&L->mc, c.data_ptr(), N, M, ldc, 64, 128);
+    }
 #define BDLLM_PAIR_CASE(E, AM, BMN)                   \
   if (epi == E && a_mn == AM && b_mn == BMN) {        \
-    launch_pair<E, AM, BMN>(L, st);                   \
+    launch_pair<E, AM, BMN, 256>(L, st);              \
     return;                                           \
   }
+#define BDLLM_WIDE_CASE(E, AM, BMN)                   \
+  if (wide && epi == E && a_mn == AM && b_mn == BMN) { \
+    launch_pair<E, AM, BMN, 512>(L, st);              \
+    return;                                           \
+  }
+    BDLLM_WIDE_CASE(EPI_BF16, false, false)
+    BDLLM_WIDE_CASE(EPI_ADD_BF16, false, false)
+    BDLLM_WIDE_CASE(EPI_BF16, false, true)
+    BDLLM_WIDE_CASE(EPI_ADD_BF16, false, true)
+    BDLLM_WIDE_CASE(EPI_BF16, true, true)
+    BDLLM_WIDE_CASE(EPI_ADD_BF16, true, true)
+#undef BDLLM_WIDE_CASE
     BDLLM_PAIR_CASE(EPI_BF16, false, false)
     BDLLM_PAIR_CASE(EPI_F32, false, false)
     BDLLM_PAIR_CASE(EPI_ADD_BF16, false, false)

@@ -51,10 +51,19 @@ def test_nn_and_tn(M, N, K):
     C.check_errors()
 
 
-@pytest.mark.parametrize("M,N,K", [(4096, 2560, 1024), (4104, 2568, 520)])
-def test_cta_pair_all_majors(M, N, K):
+@pytest.fixture(params=["1", "0"], ids=["256x512", "256x256"])
+def pair_width(request, monkeypatch):
+    """Both tile widths of the two-CTA kernel (the variable is read at every GEMM call)."""
+    monkeypatch.setenv("BDLLM_GEMM_WIDE", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("M,N,K", [(4096, 2560, 1024), (4104, 2568, 520), (8192, 5200, 256)])
+def test_cta_pair_all_majors(M, N, K, pair_width):
     """Shapes with >= 148 256x256 tiles take the two-CTA (cta_group::2) kernel: K-major and
-    MN-major operands, bf16 / fp32 / in-place accumulate epilogues, M, N and K tails."""
+    MN-major operands, bf16 / fp32 / in-place accumulate epilogues, M, N and K tails. In the
+    256 x 512 variant, 4096 x 2560 leaves a partial last wave (split into half-tiles), 2568 and
+    5200 leave a last tile column whose second half lies beyond N."""
     from dllm_qwen38_b200 import _C
 
     torch.manual_seed(5)
@@ -93,8 +102,8 @@ def test_bn128_variant():
     assert _rel(c, a.float() @ b.float().t()) < 1e-5
 
 
-@pytest.mark.parametrize("M,F,K", [(256, 384, 128), (1000, 1000, 520), (4096, 3584, 1024)])
-def test_swiglu_epilogue(M, F, K):
+@pytest.mark.parametrize("M,F,K", [(256, 384, 128), (1000, 1000, 520), (4096, 3584, 1024), (4096, 3600, 512)])
+def test_swiglu_epilogue(M, F, K, pair_width):
     C = _ops()
     torch.manual_seed(3)
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)

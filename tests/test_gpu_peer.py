@@ -62,18 +62,21 @@ def test_peer_wait_times_out_and_reports():
         dist.destroy_process_group()
 
 
-def test_fused_allgather_gemm_single_rank():
+@pytest.mark.parametrize("N,K,M,wide", [(1536, 1024, 300, "1"), (4096, 1024, 4096, "1"), (4096, 1024, 4096, "0")])
+def test_fused_allgather_gemm_single_rank(N, K, M, wide, monkeypatch):
     """gemm_ag with one rank: the copy warps fill the whole gathered buffer from the (own) shard
-    while the tiles wait per chunk; result and buffer against torch."""
+    while the tiles wait per chunk; result and buffer against torch. M 300 runs the one-CTA kernel,
+    M 4096 the two-CTA kernel in both tile widths."""
     from dllm_qwen38_b200.ops import _native
     from dllm_qwen38_b200.parallel.peer import SymmetricHeap
 
+    monkeypatch.setenv("BDLLM_GEMM_WIDE", wide)
     C = _native.require()
     torch.cuda.set_device(0)
     store = dist.TCPStore("127.0.0.1", _port(), 1, True)
     dist.init_process_group("gloo", store=store, rank=0, world_size=1)
     try:
-        N, K, M, extra = 1536, 1024, 300, 777 * 64
+        extra = 777 * 64
         numel = 4096 + N * K + extra  # [something | W | the rest of a unit]
         heap = SymmetricHeap(numel * 2 + (1 << 20), torch.device("cuda", 0))
         shard, off = heap.alloc(numel, torch.bfloat16)

@@ -10,6 +10,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <tuple>
+
 #include "common.cuh"
 
 namespace bdllm {
@@ -62,17 +64,19 @@ __global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
 }
 
-// dx = r * g - x * r^3 * mean(g * x), g = dy * (1 + w); the weight gradient sum_rows dy * x * r
-// accumulates in shared memory (one float per column) and each block writes one partial row.
+// dx = r * g - x * r^3 * mean(g * x), g = dy * (1 + w); weight gradient sum_rows dy * x * r.
+// A block takes RMS_BWD_ROWS rows. Phase 1: one warp per row computes r and mean(g * x) and writes
+// dx; the rows' r go to shared memory. Phase 2: thread t sums dy * x * r over the block's rows for
+// the 8-column groups t, t + 256, ... (16-byte loads of rows the block just read, mostly L2 hits)
+// and writes one partial row; no atomics, so the result is deterministic.
+constexpr int RMS_BWD_ROWS = 16;
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                                    const float* __restrict__ w1, __nv_bfloat16* __restrict__ dx,
-                                   float* __restrict__ dw_part, int rows, int D, float eps, int rows_per_block) {
-  extern __shared__ float wacc[];  // [D]
+                                   float* __restrict__ dw_part, int rows, int D, float eps) {
+  __shared__ float rr[RMS_BWD_ROWS];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  for (int c = threadIdx.x; c < D; c += blockDim.x) wacc[c] = 0.f;
-  __syncthreads();
-  const int r0 = blockIdx.x * rows_per_block;
-  const int r1 = min(rows, r0 + rows_per_block);
+  const int r0 = blockIdx.x * RMS_BWD_ROWS;
+  const int r1 = min(rows, r0 + RMS_BWD_ROWS);
   for (int row = r0 + warp; row < r1; row += NORM_ROWS_PER_BLOCK) {
     const __nv_bfloat16* xr = x + (int64_t)row * D;
     const __nv_bfloat16* dyr = dy + (int64_t)row * D;
@@ -80,23 +84,28 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
     for (int c = lane * 8; c < D; c += 256) {
       uint4 p = *reinterpret_cast<const uint4*>(xr + c);
       uint4 q = *reinterpret_cast<const uint4*>(dyr + c);
+      float4 wa = *reinterpret_cast<const float4*>(w1 + c), wb = *reinterpret_cast<const float4*>(w1 + c + 4);
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
       const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&q);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float2 a = __bfloat1622float2(p2[e]), b = __bfloat1622float2(q2[e]);
         ss += a.x * a.x + a.y * a.y;
-        gx += b.x * w1[c + 2 * e] * a.x + b.y * w1[c + 2 * e + 1] * a.y;
+        gx += b.x * wv[2 * e] * a.x + b.y * wv[2 * e + 1] * a.y;
       }
     }
     ss = warp_sum(ss);
     gx = warp_sum(gx);
     const float r = rsqrtf(ss / D + eps);
     const float k = r * r * r * gx / D;
+    if (lane == 0) rr[row - r0] = r;
     __nv_bfloat16* dxr = dx + (int64_t)row * D;
     for (int c = lane * 8; c < D; c += 256) {
       uint4 p = *reinterpret_cast<const uint4*>(xr + c);
       uint4 q = *reinterpret_cast<const uint4*>(dyr + c);
+      float4 wa = *reinterpret_cast<const float4*>(w1 + c), wb = *reinterpret_cast<const float4*>(w1 + c + 4);
+      const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
       const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
       const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&q);
       uint4 o;
@@ -104,95 +113,189 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const _
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         float2 a = __bfloat1622float2(p2[e]), b = __bfloat1622float2(q2[e]);
-        atomicAdd(&wacc[c + 2 * e], b.x * a.x * r);
-        atomicAdd(&wacc[c + 2 * e + 1], b.y * a.y * r);
-        o2[e] = __floats2bfloat162_rn(r * b.x * w1[c + 2 * e] - a.x * k, r * b.y * w1[c + 2 * e + 1] - a.y * k);
+        o2[e] = __floats2bfloat162_rn(r * b.x * wv[2 * e] - a.x * k, r * b.y * wv[2 * e + 1] - a.y * k);
       }
       *reinterpret_cast<uint4*>(dxr + c) = o;
     }
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) dw_part[(int64_t)blockIdx.x * D + c] = wacc[c];
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int row = r0; row < r1; ++row) {
+      uint4 p = *reinterpret_cast<const uint4*>(x + (int64_t)row * D + c);
+      uint4 q = *reinterpret_cast<const uint4*>(dy + (int64_t)row * D + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+      const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&q);
+      const float r = rr[row - r0];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 a = __bfloat1622float2(p2[e]), b = __bfloat1622float2(q2[e]);
+        acc[2 * e] += b.x * a.x * r;
+        acc[2 * e + 1] += b.y * a.y * r;
+      }
+    }
+    float* out = dw_part + (int64_t)blockIdx.x * D + c;
+    *reinterpret_cast<float4*>(out) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(out + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
 }
 
+// out[c] = sum_p part[p][c]: a block of 32 x 8 threads per 32 columns; thread (tx, ty) sums the
+// partial rows ty, ty + 8, ... of column tx (coalesced 128-byte row segments), then the 8 sums
+// of a column are added in shared memory in a fixed order.
 __global__ void colsum_kernel(const float* __restrict__ part, int nparts, int D, float* __restrict__ out) {
-  int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= D) return;
+  __shared__ float red[8][33];
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
+  const int c = blockIdx.x * 32 + tx;
   float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[(int64_t)p * D + c];
-  out[c] = s;
+  if (c < D)
+    for (int p = ty; p < nparts; p += 8) s += part[(int64_t)p * D + c];
+  red[ty][tx] = s;
+  __syncthreads();
+  if (ty == 0 && c < D) {
+    float t = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t += red[j][tx];
+    out[c] = t;
+  }
 }
 
 // --------------------------------------------------------------------------------- gated
-// rows of Dv (<= 256): x, z [rows, Dv] (z row stride ldz), w [Dv] (plain weight, not 1 + w)
-__global__ void gated_rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ z,
-                                         int64_t ldz, const float* __restrict__ w, __nv_bfloat16* __restrict__ y,
-                                         int rows, int D, float eps) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int row = blockIdx.x * NORM_ROWS_PER_BLOCK + warp;
-  if (row >= rows) return;
-  const int per = D / 32;  // elements per lane (D % 32 == 0, D <= 256)
-  float xv[8];
-  float ss = 0.f;
-  for (int e = 0; e < per; ++e) {
-    xv[e] = __bfloat162float(x[(int64_t)row * D + lane * per + e]);
-    ss += xv[e] * xv[e];
+// Rows of D = 32 * PER (<= 256) elements, one warp per row, lane l holding elements
+// [PER l, PER l + PER) as one 2 / 4 / 8 / 16-byte vector (PER 1, 2, 4, 8; other PER element-wise).
+// x, y, dy, dx, dz are [rows, D]; z is read in place from its projection: row = t * H + h lives at
+// z + t * ldzt + h * D (the z slice of the fused input projection, no copy).
+template <int PER>
+__device__ __forceinline__ void ld_row(const __nv_bfloat16* p, float (&f)[PER], bool vec) {
+  if constexpr (PER == 8) {
+    if (vec) {
+      uint4 u = *reinterpret_cast<const uint4*>(p);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 t = __bfloat1622float2(h[e]);
+        f[2 * e] = t.x, f[2 * e + 1] = t.y;
+      }
+      return;
+    }
+  } else if constexpr (PER == 4) {
+    if (vec) {
+      uint2 u = *reinterpret_cast<const uint2*>(p);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float2 t = __bfloat1622float2(h[e]);
+        f[2 * e] = t.x, f[2 * e + 1] = t.y;
+      }
+      return;
+    }
+  } else if constexpr (PER == 2) {
+    if (vec) {
+      float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+      f[0] = t.x, f[1] = t.y;
+      return;
+    }
   }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / D + eps);
-  for (int e = 0; e < per; ++e) {
-    int c = lane * per + e;
-    float n = __bfloat162float(__float2bfloat16(xv[e] * r));
-    float a = __bfloat162float(__float2bfloat16(w[c] * n));
-    float zz = __bfloat162float(z[(int64_t)row * ldz + c]);
-    y[(int64_t)row * D + c] = __float2bfloat16(a * silu_f(zz));
+#pragma unroll
+  for (int e = 0; e < PER; ++e) f[e] = __bfloat162float(p[e]);
+}
+template <int PER>
+__device__ __forceinline__ void st_row(__nv_bfloat16* p, const float (&f)[PER]) {
+  if constexpr (PER == 8) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  } else if constexpr (PER == 4) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) h[e] = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else if constexpr (PER == 2) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(f[0], f[1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < PER; ++e) p[e] = __float2bfloat16(f[e]);
   }
 }
 
-__global__ void gated_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
-                                         const __nv_bfloat16* __restrict__ z, int64_t ldz,
-                                         const float* __restrict__ w, __nv_bfloat16* __restrict__ dx,
-                                         __nv_bfloat16* __restrict__ dz, int64_t lddz, float* __restrict__ dw_part,
-                                         int rows, int D, float eps, int rows_per_block) {
+template <int PER>
+__global__ void gated_rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ z,
+                                         int64_t ldzt, int H, bool zvec, const float* __restrict__ w,
+                                         __nv_bfloat16* __restrict__ y, int rows, float eps) {
+  constexpr int D = 32 * PER;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int per = D / 32;
-  float wacc[8];
-  for (int e = 0; e < 8; ++e) wacc[e] = 0.f;
+  const int row = blockIdx.x * NORM_ROWS_PER_BLOCK + warp;
+  if (row >= rows) return;
+  float xv[PER], zv[PER], o[PER];
+  ld_row<PER>(x + (int64_t)row * D + lane * PER, xv, true);
+  ld_row<PER>(z + (int64_t)(row / H) * ldzt + (int64_t)(row % H) * D + lane * PER, zv, zvec);
+  float ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) ss += xv[e] * xv[e];
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / D + eps);
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int c = lane * PER + e;
+    const float n = __bfloat162float(__float2bfloat16(xv[e] * r));
+    const float a = __bfloat162float(__float2bfloat16(w[c] * n));
+    o[e] = a * silu_f(zv[e]);
+  }
+  st_row<PER>(y + (int64_t)row * D + lane * PER, o);
+}
+
+template <int PER>
+__global__ void gated_rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                         const __nv_bfloat16* __restrict__ z, int64_t ldzt, int H, bool zvec,
+                                         const float* __restrict__ w, __nv_bfloat16* __restrict__ dx,
+                                         __nv_bfloat16* __restrict__ dz, float* __restrict__ dw_part, int rows,
+                                         float eps, int rows_per_block) {
+  constexpr int D = 32 * PER;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float wv[PER], wacc[PER];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) wv[e] = w[lane * PER + e], wacc[e] = 0.f;
   const int r0 = blockIdx.x * rows_per_block, r1 = min(rows, r0 + rows_per_block);
   for (int row = r0 + warp; row < r1; row += NORM_ROWS_PER_BLOCK) {
-    float xv[8], g[8];
+    float xv[PER], zv[PER], dv[PER], g[PER], dzv[PER];
+    ld_row<PER>(x + (int64_t)row * D + lane * PER, xv, true);
+    ld_row<PER>(z + (int64_t)(row / H) * ldzt + (int64_t)(row % H) * D + lane * PER, zv, zvec);
+    ld_row<PER>(dy + (int64_t)row * D + lane * PER, dv, true);
     float ss = 0.f;
-    for (int e = 0; e < per; ++e) {
-      xv[e] = __bfloat162float(x[(int64_t)row * D + lane * per + e]);
-      ss += xv[e] * xv[e];
-    }
+#pragma unroll
+    for (int e = 0; e < PER; ++e) ss += xv[e] * xv[e];
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / D + eps);
     float gx = 0.f;
-    for (int e = 0; e < per; ++e) {
-      int c = lane * per + e;
-      float n = xv[e] * r;
-      float zz = __bfloat162float(z[(int64_t)row * ldz + c]);
-      float sg = sigmoid_f(zz);
-      float s = zz * sg;
-      float d = __bfloat162float(dy[(int64_t)row * D + c]);
-      float a = w[c] * n;
-      dz[(int64_t)row * lddz + c] = __float2bfloat16(d * a * sg * (1.f + zz * (1.f - sg)));
-      float da = d * s;
+#pragma unroll
+    for (int e = 0; e < PER; ++e) {
+      const float n = xv[e] * r;
+      const float zz = zv[e];
+      const float sg = sigmoid_f(zz);
+      const float a = wv[e] * n;
+      dzv[e] = dv[e] * a * sg * (1.f + zz * (1.f - sg));
+      const float da = dv[e] * zz * sg;
       wacc[e] += da * n;
-      g[e] = da * w[c];
+      g[e] = da * wv[e];
       gx += g[e] * xv[e];
     }
     gx = warp_sum(gx);
     const float k = r * r * r * gx / D;
-    for (int e = 0; e < per; ++e) dx[(int64_t)row * D + lane * per + e] = __float2bfloat16(r * g[e] - xv[e] * k);
+#pragma unroll
+    for (int e = 0; e < PER; ++e) g[e] = r * g[e] - xv[e] * k;
+    st_row<PER>(dz + (int64_t)row * D + lane * PER, dzv);
+    st_row<PER>(dx + (int64_t)row * D + lane * PER, g);
   }
-  __shared__ float red[NORM_ROWS_PER_BLOCK][256];
-  for (int e = 0; e < per; ++e) red[warp][lane * per + e] = wacc[e];
+  __shared__ float red[NORM_ROWS_PER_BLOCK][D];
+#pragma unroll
+  for (int e = 0; e < PER; ++e) red[warp][lane * PER + e] = wacc[e];
   __syncthreads();
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float s = 0.f;
-    for (int wv = 0; wv < NORM_ROWS_PER_BLOCK; ++wv) s += red[wv][c];
+    for (int wi = 0; wi < NORM_ROWS_PER_BLOCK; ++wi) s += red[wi][c];
     dw_part[(int64_t)blockIdx.x * D + c] = s;
   }
 }
@@ -337,15 +440,15 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, c
   auto dx = at::empty_like(x2);
   c10::cuda::CUDAGuard g(x.device());
   auto w = w1.to(at::kFloat).contiguous();
-  const int rows_per_block = std::max(64, (rows + 1023) / 1024);
-  const int nblk = std::max(1, (rows + rows_per_block - 1) / rows_per_block);
+  TORCH_CHECK(D % 8 == 0, "rmsnorm_bwd: D % 8 == 0");
+  const int nblk = std::max(1, (rows + RMS_BWD_ROWS - 1) / RMS_BWD_ROWS);
   auto part = at::empty({nblk, D}, x.options().dtype(at::kFloat));
   auto dw = at::empty({D}, x.options().dtype(at::kFloat));
   if (rows > 0) {
-    rmsnorm_bwd_kernel<<<nblk, 32 * NORM_ROWS_PER_BLOCK, D * sizeof(float), stream()>>>(
-        cbf(dy2), cbf(x2), w.data_ptr<float>(), bf(dx), part.data_ptr<float>(), rows, D, (float)eps, rows_per_block);
+    rmsnorm_bwd_kernel<<<nblk, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(
+        cbf(dy2), cbf(x2), w.data_ptr<float>(), bf(dx), part.data_ptr<float>(), rows, D, (float)eps);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    colsum_kernel<<<(D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, D, dw.data_ptr<float>());
+    colsum_kernel<<<(D + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, D, dw.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   } else {
     dw.zero_();
@@ -353,20 +456,51 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, c
   return {dx.view(x.sizes()), dw};
 }
 
+// z as [T, H, D] with unit inner stride and head stride D (any token stride): returns
+// (base pointer, token stride, H, whether PER-element vector loads are aligned); other layouts
+// are made contiguous first
+static std::tuple<at::Tensor, int64_t, int> gated_z(const at::Tensor& z, int D, int rows) {
+  at::Tensor zz = z;
+  if (z.dim() >= 3 && z.stride(-1) == 1 && z.stride(-2) == D) {
+    const int H = z.size(-2);
+    // the leading dims must merge into one token index with a single stride
+    int64_t ldt = z.dim() >= 3 ? z.stride(-3) : (int64_t)H * D;
+    bool ok = true;
+    for (int d = z.dim() - 4; d >= 0; --d)
+      if (z.size(d) > 1 && z.stride(d) != z.stride(d + 1) * z.size(d + 1)) ok = false;
+    if (ok && (int64_t)rows % H == 0) return {zz, ldt, H};
+  }
+  zz = z.reshape({-1, D}).contiguous();
+  return {zz, (int64_t)D, 1};
+}
+
+#define BDLLM_GATED_PER(PER_, ...) \
+  switch (per) {                   \
+    case 1: { constexpr int PER_ = 1; __VA_ARGS__; break; } \
+    case 2: { constexpr int PER_ = 2; __VA_ARGS__; break; } \
+    case 3: { constexpr int PER_ = 3; __VA_ARGS__; break; } \
+    case 4: { constexpr int PER_ = 4; __VA_ARGS__; break; } \
+    case 5: { constexpr int PER_ = 5; __VA_ARGS__; break; } \
+    case 6: { constexpr int PER_ = 6; __VA_ARGS__; break; } \
+    case 7: { constexpr int PER_ = 7; __VA_ARGS__; break; } \
+    default: { constexpr int PER_ = 8; __VA_ARGS__; break; } \
+  }
+
 at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at::Tensor& w, double eps) {
   const int D = x.size(-1);
   TORCH_CHECK(D % 32 == 0 && D <= 256, "gated_rmsnorm: D % 32 == 0 and D <= 256");
   auto x2 = x.reshape({-1, D}).contiguous();
-  auto z2 = z.reshape({-1, D});
-  if (z2.stride(-1) != 1) z2 = z2.contiguous();
   const int rows = x2.size(0);
   auto y = at::empty_like(x2);
   if (rows == 0) return y.view(x.sizes());
   c10::cuda::CUDAGuard g(x.device());
+  auto [zz, ldzt, H] = gated_z(z, D, rows);
+  const int per = D / 32;
+  const bool zvec = ((reinterpret_cast<uintptr_t>(zz.data_ptr()) | (uintptr_t)(ldzt * 2)) % (per * 2)) == 0;
   auto wf = w.to(at::kFloat).contiguous();
-  gated_rmsnorm_fwd_kernel<<<(rows + NORM_ROWS_PER_BLOCK - 1) / NORM_ROWS_PER_BLOCK, 32 * NORM_ROWS_PER_BLOCK, 0,
-                             stream()>>>(cbf(x2), cbf(z2), z2.stride(0), wf.data_ptr<float>(), bf(y), rows, D,
-                                         (float)eps);
+  const int nb = (rows + NORM_ROWS_PER_BLOCK - 1) / NORM_ROWS_PER_BLOCK;
+  BDLLM_GATED_PER(P, gated_rmsnorm_fwd_kernel<P><<<nb, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(
+                         cbf(x2), cbf(zz), ldzt, H, zvec, wf.data_ptr<float>(), bf(y), rows, (float)eps));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return y.view(x.sizes());
 }
@@ -374,9 +508,8 @@ at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at:
 std::vector<at::Tensor> gated_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& z,
                                           const at::Tensor& w, double eps) {
   const int D = x.size(-1);
+  TORCH_CHECK(D % 32 == 0 && D <= 256, "gated_rmsnorm: D % 32 == 0 and D <= 256");
   auto x2 = x.reshape({-1, D}).contiguous();
-  auto z2 = z.reshape({-1, D});
-  if (z2.stride(-1) != 1) z2 = z2.contiguous();
   auto dy2 = dy.to(at::kBFloat16).reshape({-1, D}).contiguous();
   const int rows = x2.size(0);
   auto dx = at::empty_like(x2);
@@ -388,11 +521,14 @@ std::vector<at::Tensor> gated_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor
   c10::cuda::CUDAGuard g(x.device());
   auto wf = w.to(at::kFloat).contiguous();
   if (rows > 0) {
-    gated_rmsnorm_bwd_kernel<<<nblk, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(
-        cbf(dy2), cbf(x2), cbf(z2), z2.stride(0), wf.data_ptr<float>(), bf(dx), bf(dz), D, part.data_ptr<float>(),
-        rows, D, (float)eps, rows_per_block);
+    auto [zz, ldzt, H] = gated_z(z, D, rows);
+    const int per = D / 32;
+    const bool zvec = ((reinterpret_cast<uintptr_t>(zz.data_ptr()) | (uintptr_t)(ldzt * 2)) % (per * 2)) == 0;
+    BDLLM_GATED_PER(P, gated_rmsnorm_bwd_kernel<P><<<nblk, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(
+                           cbf(dy2), cbf(x2), cbf(zz), ldzt, H, zvec, wf.data_ptr<float>(), bf(dx), bf(dz),
+                           part.data_ptr<float>(), rows, (float)eps, rows_per_block));
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    colsum_kernel<<<(D + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, D, dw.data_ptr<float>());
+    colsum_kernel<<<(D + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, D, dw.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   return {dx.view(x.sizes()), dz.view(z.sizes()), dw};
@@ -442,7 +578,7 @@ std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tenso
         cbf(d), cbf(src), src.stride(1), src.stride(2), w.data_ptr<float>(), cbf(c2), cbf(s2), bf(dsrc),
         dsrc.stride(1), dsrc.stride(2), part.data_ptr<float>(), T, H, Dh, T2, R, (float)eps, per_block);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
-    colsum_kernel<<<(Dh + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, Dh, dw.data_ptr<float>());
+    colsum_kernel<<<(Dh + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), nblk, Dh, dw.data_ptr<float>());
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   return {dsrc, dw};

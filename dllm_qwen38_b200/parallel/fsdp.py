@@ -215,6 +215,9 @@ class FSDPEngine:
             # the next layer's backward fills the other
             self.grads, self.grad_offs = zip(*[self.peer.alloc(gmax, self.dtype) for _ in range(2)])
             self.table_grad, self.table_off = self.peer.alloc(self.embed.padded, torch.float32)
+        elif self.world == 1:  # each unit's backward writes its own gradient (unit.g) in place
+            self.grads = ()
+            self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
         else:
             self.grads = (torch.empty(gmax, dtype=self.dtype, device=self.device),)
             self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
@@ -391,7 +394,11 @@ class FSDPEngine:
             unit.gather_into(out)
 
     def grad_buffer(self, unit: Unit) -> torch.Tensor:
-        """A zeroed flat gradient buffer for `unit` (waits until its previous reduce-scatter ended)."""
+        """A zeroed flat gradient buffer for `unit` (waits until its previous reduce-scatter ended).
+        One rank: the unit's own gradient tensor, which the optimizer reads directly."""
+        if not self.grads:
+            unit.g.zero_()
+            return unit.g
         j = self.grad_i
         self.grad_i = (j + 1) % len(self.grads)
         if self.rs_done[j] is not None:
@@ -403,7 +410,9 @@ class FSDPEngine:
 
     def reduce_scatter(self, unit: Unit, flat_grad: torch.Tensor) -> None:
         if self.peer is None:
-            if self.world == 1:  # the fp32 shard copy and its sum of squares in one pass
+            if flat_grad.data_ptr() == unit.g.data_ptr():  # one rank: the gradient is already in place
+                ops.sumsq_(flat_grad[: unit.shard], self.sq)
+            elif self.world == 1:  # the model-dtype copy and its sum of squares in one pass
                 ops.sumsq_(flat_grad[: unit.shard], self.sq, unit.g)
             else:
                 unit.reduce_scatter_from(flat_grad)

@@ -33,13 +33,15 @@ def test_rmsnorm_fwd_bwd(D):
     assert _rel(y, yr) < 1e-2 and _rel(x.grad, dxr) < 1e-2 and _rel(w.grad, dwr) < 1e-2
 
 
-@pytest.mark.parametrize("D", [32, 128])
-def test_gated_rmsnorm_fwd_bwd(D):
+@pytest.mark.parametrize("D,pad", [(32, 8), (64, 8), (96, 8), (128, 8), (128, 1), (256, 8)])
+def test_gated_rmsnorm_fwd_bwd(D, pad):
+    """z is read in place from a wider projection row (token stride 6 D + pad): pad 8 keeps the
+    per-lane vectors aligned, pad 1 takes the element-wise path."""
     from dllm_qwen38_b200.ops import cuda as C
 
     torch.manual_seed(1)
     x = torch.randn(2, 100, 6, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    zfull = torch.randn(2, 100, 6 * D + 8, device="cuda", dtype=torch.bfloat16)
+    zfull = torch.randn(2, 100, 6 * D + pad, device="cuda", dtype=torch.bfloat16)
     z = zfull[..., : 6 * D].reshape(2, 100, 6, D).detach().requires_grad_(True)
     w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16).requires_grad_(True)
     y = C.gated_rmsnorm(x, z, w, 1e-6)

@@ -109,6 +109,30 @@ def test_adamw_matches_reference_update():
     assert _rel(og.master[0].cpu(), p_cpu.detach()) < 1e-5
 
 
+@pytest.mark.parametrize("n,gdt", [(1003, torch.bfloat16), (4096 * 37 + 2, torch.bfloat16), (999, torch.float32)])
+def test_adamw_flat_vector_kernel_against_fp32(n, gdt):
+    """The flat AdamW (4 elements per thread, n % 4 tail) against the fp32 update with a device
+    clip coefficient."""
+    from dllm_qwen38_b200.ops import cuda as C
+
+    torch.manual_seed(4)
+    w = torch.randn(n, device="cuda")
+    m = torch.randn(n, device="cuda").abs() * 0.1
+    v = torch.randn(n, device="cuda").abs() * 0.01
+    g = torch.randn(n, device="cuda").to(gdt)
+    p = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    coef = torch.tensor(0.7, device="cuda")
+    lr, b1, b2, eps, wd, bc1, bc2 = 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.5, 0.3
+    gf = g.float() * 0.7
+    m_ref = b1 * m + (1 - b1) * gf
+    v_ref = b2 * v + (1 - b2) * gf * gf
+    w_ref = w * (1 - lr * wd) - lr * (m_ref / bc1) / ((v_ref / bc2).sqrt() + eps)
+    C.adamw_flat(w, p, g, m, v, lr, b1, b2, eps, wd, coef, bc1, bc2)
+    torch.cuda.synchronize()
+    assert _rel(m, m_ref) < 1e-6 and _rel(v, v_ref) < 1e-6 and _rel(w, w_ref) < 1e-6
+    assert torch.equal(p, w.to(torch.bfloat16))
+
+
 def test_gdn_gates_fwd_bwd_against_reference():
     from dllm_qwen38_b200.ops import cuda as Cu
 

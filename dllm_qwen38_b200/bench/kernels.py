@@ -79,6 +79,25 @@ def op_gemm(a):
     return fn, 2.0 * a.M * a.N * a.K, 2.0 * (a.M * a.K + a.N * a.K + a.M * a.N)
 
 
+def op_swiglu(a):
+    """act[M, N] = silu(x Wg^T) * (x Wu^T), x [M, K], [Wg; Wu] [2N, K] (the MLP's gate/up GEMM with
+    its SwiGLU epilogue); --layout tn also stores the bf16 (gate | up) [M, 2N], as the backward's
+    recomputation does. cublas: the [M, 2N] product, then torch's silu * up."""
+    from ..ops import cuda as Cu
+
+    x = torch.randn(a.M, a.K, device="cuda").bfloat16()
+    w = (torch.randn(2 * a.N, a.K, device="cuda") * a.K ** -0.5).bfloat16()
+    gu = a.layout == "tn"
+    if a.impl == "cublas":
+        def fn():
+            y = torch.matmul(x, w.t())
+            return torch.nn.functional.silu(y[:, : a.N]) * y[:, a.N :]
+    else:
+        def fn():
+            return Cu.gemm_swiglu(x, w, a.N, gu)
+    return fn, 4.0 * a.M * a.N * a.K, 2.0 * (a.M * a.K + 2 * a.N * a.K + a.M * a.N * (3 if gu else 1))
+
+
 def _gdn_inputs(a):
     B, L, Hk, Hv, D = a.B, a.L, 16, 48, 128
     g = torch.Generator(device="cuda").manual_seed(0)
@@ -349,7 +368,7 @@ def op_embed(a):
     return fn, 1.0 * ids.numel() * D, ids.numel() * D * (2 + 2 + 2 + 8)
 
 
-OPS = {"gemm": op_gemm, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
+OPS = {"gemm": op_gemm, "swiglu": op_swiglu, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
        "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed,
        "adamw": op_adamw}
 

@@ -32,6 +32,9 @@ namespace attn_tc {
 
 constexpr int BQ = 128;   // query rows per CTA (MMA M)
 constexpr int NTHR = 192;
+// backward kernels: warps 0-7 form dS (and P^T) from the score tiles (warp w: TMEM lane quadrant
+// w % 4, half w / 4 of each 32-column tile), warp 8 loads, warp 9 issues the MMAs
+constexpr int NTHR_K = 320;
 constexpr float NEG_INF = -INFINITY;
 constexpr float RESCALE_LOG2 = 8.f;
 
@@ -103,6 +106,26 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+               :
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
@@ -540,7 +563,8 @@ struct QCfg {
   static constexpr int STAGE = 2 * K_BYTES;     // K then V
   static constexpr int NST_FIT = (227 * 1024 - 2 * Q_BYTES - 1024 - 256) / STAGE;
   static constexpr int NST = NST_FIT > 4 ? 4 : NST_FIT;  // K / V ring stages
-  static constexpr int SMEM = 2 * Q_BYTES + NST * STAGE + 1024 + 256;
+  // + 1 KB for the two half-row partial sums of Delta
+  static constexpr int SMEM = 2 * Q_BYTES + NST * STAGE + 1024 + 256 + 1024;
   // TMEM: S and dP (NS buffers of 32 columns each), dS as the bf16 A operand of the dQ MMA (two
   // buffers of 16 packed columns), dQ (D columns)
   static constexpr int NS = 3;
@@ -570,7 +594,7 @@ struct BArgs {
 
 
 template <int D>
-__global__ void __launch_bounds__(NTHR, 1)
+__global__ void __launch_bounds__(NTHR_K, 1)
     bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                      const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = QCfg<D>;
@@ -590,6 +614,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   uint64_t* drain = dq_done + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* dpart = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);  // [2][128]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int qt = heavy_first(blockIdx.y, gridDim.y);  // grid (B * Hq, query tiles), as the forward
@@ -607,7 +632,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
     for (int s = 0; s < NS; ++s) mbar_init(&sd_full[s], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&ds_full[s], 4);
+      mbar_init(&ds_full[s], 8);  // the eight dS warps
       mbar_init(&dq_done[s], 1);
     }
     mbar_init(drain, 1);
@@ -627,7 +652,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer
       mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
@@ -657,7 +682,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       for (int s = 0; s < NST; ++s)
         if (last[s] >= 0) mbar_wait(&kv_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       bool ok = mbar_wait(q_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
@@ -701,18 +726,23 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else {
-    // -------------------------------------------------------------- dS (warps 0-3)
-    const int r = warp * 32 + lane;
+    // -------------------------------------------------------------- dS (warps 0-7)
+    // warp w: TMEM lane quadrant w % 4 (query row = thread), key columns [16 (w / 4), +16) of each
+    // 32-key tile; Delta = rowsum(dO * O) is summed over half the head dim by each of a row's two
+    // threads
+    const int quad = warp & 3, hc = warp >> 2;
+    const int r = quad * 32 + lane;
     const int row = i0 + r;
     const bool valid = row < a.T2;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const int64_t otok = (int64_t)a.Hq * D;
     float lse = 0.f, dlt = 0.f;
     if (valid) {
-      const uint4* po = reinterpret_cast<const uint4*>(a.o + ((int64_t)b * a.T2 + row) * otok + h * D);
-      const uint4* pd = reinterpret_cast<const uint4*>(a.dout + ((int64_t)b * a.T2 + row) * otok + h * D);
+      const uint4* po = reinterpret_cast<const uint4*>(a.o + ((int64_t)b * a.T2 + row) * otok + h * D) + hc * (D / 16);
+      const uint4* pd =
+          reinterpret_cast<const uint4*>(a.dout + ((int64_t)b * a.T2 + row) * otok + h * D) + hc * (D / 16);
 #pragma unroll 4
-      for (int c = 0; c < D / 8; ++c) {
+      for (int c = 0; c < D / 16; ++c) {
         const uint4 x = po[c], y = pd[c];
         const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&x);
         const __nv_bfloat162* y2 = reinterpret_cast<const __nv_bfloat162*>(&y);
@@ -723,6 +753,11 @@ __global__ void __launch_bounds__(NTHR, 1)
         }
       }
       lse = a.lse2[((int64_t)b * a.Hq + h) * a.T2 + row];
+    }
+    dpart[hc * 128 + r] = dlt;
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight dS warps
+    dlt = dpart[r] + dpart[128 + r];
+    if (valid && hc == 0) {
       (void)BDLLM_CHECK(isfinite(dlt), row, a.T2);  // sentinel: non-finite O or dO row
       a.delta[((int64_t)b * a.Hq + h) * a.T2 + row] = dlt;
     }
@@ -739,22 +774,22 @@ __global__ void __launch_bounds__(NTHR, 1)
         break;
       }
       tc_fence_after();
-      uint32_t rs[32], rp[32];
-      tmem_ld32_async(tmem + lane_base + C::S_COL + sb * BK2, rs);
-      tmem_ld32_async(tmem + lane_base + C::DP_COL + sb * BK2, rp);
-      tmem_wait_ld(rs);
-      tmem_wait_ld(rp);
+      uint32_t rs[16], rp[16];
+      tmem_ld16_async(tmem + lane_base + C::S_COL + sb * BK2 + 16 * hc, rs);
+      tmem_ld16_async(tmem + lane_base + C::DP_COL + sb * BK2 + 16 * hc, rp);
+      tmem_wait_ld16(rs);
+      tmem_wait_ld16(rp);
       const bool full = __all_sync(0xffffffffu, vis.sees_all(j0, j0 + BK2 - 1, a.L));
-      uint32_t pk[16];
+      uint32_t pk[8];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         float d2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e;
-          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, nl));
+          const int cl = 2 * c + e, cc = 16 * hc + cl;
+          float p = ex2(fmaf(__uint_as_float(rs[cl]), c2, nl));
           if (!full && !vis.sees(j0 + cc, a.L)) p = 0.f;
-          d2[e] = p * (__uint_as_float(rp[cc]) - dlt);
+          d2[e] = p * (__uint_as_float(rp[cl]) - dlt);
         }
         pk[c] = pack_bf16(d2[0], d2[1]);
       }
@@ -762,7 +797,7 @@ __global__ void __launch_bounds__(NTHR, 1)
         ok = false;
         break;
       }
-      tmem_st16(tmem + lane_base + C::DS_COL + s * 16, pk);
+      tmem_st8(tmem + lane_base + C::DS_COL + s * 16 + 8 * hc, pk);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -772,7 +807,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     tc_fence_after();
     __nv_bfloat16* qrow = a.dq + ((int64_t)b * a.T2 + row) * otok + h * D;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {  // this warp's half of the head dim
       uint32_t ro[32];
       if (ok && it > 0) {
         tmem_ld32_async(tmem + lane_base + C::DQ_COL + c * 32, ro);
@@ -835,7 +870,7 @@ struct KCfg {
 };
 
 template <int D>
-__global__ void __launch_bounds__(NTHR, 1)
+__global__ void __launch_bounds__(NTHR_K, 1)
     bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mdo,
                       const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, BArgs a) {
   using C = KCfg<D>;
@@ -879,7 +914,7 @@ __global__ void __launch_bounds__(NTHR, 1)
     }
     for (int s = 0; s < NS; ++s) mbar_init(&st_full[s], 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&pt_full[s], 4);
+      mbar_init(&pt_full[s], 8);  // the eight P^T / dS^T warps
       mbar_init(&g_done[s], 1);
     }
     mbar_init(drain, 1);
@@ -899,7 +934,7 @@ __global__ void __launch_bounds__(NTHR, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       // ------------------------------------------------------------ TMA producer
       mbar_arrive_expect_tx(kv_full, 2 * C::KV_BYTES);
@@ -929,7 +964,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       for (int s = 0; s < NST; ++s)
         if (last[s] >= 0) mbar_wait(&t_full[s], (last[s] / NST) & 1, a.err, ERR_ATTN_WAIT, nullptr);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       // ------------------------------------------------------------ MMA issuer
       bool ok = mbar_wait(kv_full, 0, a.err, ERR_ATTN_WAIT, abort_flag);
@@ -979,11 +1014,12 @@ __global__ void __launch_bounds__(NTHR, 1)
       mbar_wait(drain, 0, a.err, ERR_ATTN_WAIT, nullptr);
     }
   } else {
-    // -------------------------------------------------------------- P^T, dS^T (warps 0-3)
-    const int r = warp * 32 + lane;
+    // -------------------------------------------------------------- P^T, dS^T (warps 0-7)
+    const int quad = warp & 3, hc = warp >> 2;  // TMEM lane quadrant, half of the 32 query columns
+    const int r = quad * 32 + lane;
     const int key = j0 + r;
     const bool kvalid = key < a.T2;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const KeyVis kv = key_vis(key, a.L, a.T2, a.block, a.leak);
     const float c2 = a.scale_log2;
     int it = 0;
@@ -1002,25 +1038,25 @@ __global__ void __launch_bounds__(NTHR, 1)
         break;
       }
       tc_fence_after();
-      uint32_t rs[32], rp[32];
-      tmem_ld32_async(tmem + lane_base + C::ST_COL + sb * BQ2, rs);
-      tmem_ld32_async(tmem + lane_base + C::DPT_COL + sb * BQ2, rp);
-      tmem_wait_ld(rs);
-      tmem_wait_ld(rp);
+      uint32_t rs[16], rp[16];
+      tmem_ld16_async(tmem + lane_base + C::ST_COL + sb * BQ2 + 16 * hc, rs);
+      tmem_ld16_async(tmem + lane_base + C::DPT_COL + sb * BQ2 + 16 * hc, rp);
+      tmem_wait_ld16(rs);
+      tmem_wait_ld16(rp);
       const bool full = __all_sync(0xffffffffu, kv.seen_by_all(i0, i0 + BQ2 - 1, a.L, a.T2));
-      uint32_t pp[16], pd[16];
+      uint32_t pp[8], pd[8];
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c = 0; c < 8; ++c) {
         float p2[2], d2[2];
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int cc = 2 * c + e;
+          const int cl = 2 * c + e, cc = 16 * hc + cl;  // column within the half / within the tile
           const float lq = __shfl_sync(0xffffffffu, lse_l, cc);
           const float dq = __shfl_sync(0xffffffffu, dl_l, cc);
-          float p = ex2(fmaf(__uint_as_float(rs[cc]), c2, -lq));
+          float p = ex2(fmaf(__uint_as_float(rs[cl]), c2, -lq));
           if (!full && !kv.seen_by(i0 + cc, a.L, a.T2)) p = 0.f;
           p2[e] = p;
-          d2[e] = p * (__uint_as_float(rp[cc]) - dq);
+          d2[e] = p * (__uint_as_float(rp[cl]) - dq);
         }
         pp[c] = pack_bf16(p2[0], p2[1]);
         pd[c] = pack_bf16(d2[0], d2[1]);
@@ -1030,8 +1066,8 @@ __global__ void __launch_bounds__(NTHR, 1)
         ok = false;
         break;
       }
-      tmem_st16(tmem + lane_base + C::PT_COL + pb * 16, pp);
-      tmem_st16(tmem + lane_base + C::DST_COL + pb * 16, pd);
+      tmem_st8(tmem + lane_base + C::PT_COL + pb * 16 + 8 * hc, pp);
+      tmem_st8(tmem + lane_base + C::DST_COL + pb * 16 + 8 * hc, pd);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
@@ -1048,7 +1084,7 @@ __global__ void __launch_bounds__(NTHR, 1)
       const float mul = g == 0 ? 1.f : a.scale;
       __nv_bfloat16* dst_row = g == 0 ? vrow : krow;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * hc; c < 2 * hc + 2; ++c) {  // this warp's 64 of the slice's 128 columns
         uint32_t ro[32];
         if (ok && it > 0) {
           tmem_ld32_async(tmem + lane_base + col + c * 32, ro);
@@ -1141,7 +1177,7 @@ static void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Te
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       attr = true;
     }
-    kern<<<dim3(B * Hq, (T2 + BQ - 1) / BQ), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    kern<<<dim3(B * Hq, (T2 + BQ - 1) / BQ), NTHR_K, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
   {  // dK, dV
@@ -1158,7 +1194,7 @@ static void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Te
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
       attr = true;
     }
-    kern<<<dim3(B * Hk * (D / 128), (T2 + BQ - 1) / BQ), NTHR, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
+    kern<<<dim3(B * Hk * (D / 128), (T2 + BQ - 1) / BQ), NTHR_K, C::SMEM, st>>>(m.q, mdo_al, m.k, m.v, a);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

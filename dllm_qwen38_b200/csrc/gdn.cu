@@ -1316,15 +1316,16 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
                       reinterpret_cast<uintptr_t>(v.data_ptr()) % 16 == 0),
               "gdn_bwd: bf16 states come from the tensor-core forward (head dim 128, block 32, L % 128 == 0)");
   struct alignas(64) TcMaps {
-    CUtensorMap mq, mk, mv, mdo, ms, mds;
+    CUtensorMap mq, mk, mv, mdo, ms, mds, mdq, mdk, mdv;
   };
   static thread_local TcMaps tm;
   auto chunk_tc = [&](int mode) {
-    void* kargs[9];
+    void* kargs[12];
     int* err = error_word_ptr();
     Args ac = a;
     kargs[0] = &tm.mq, kargs[1] = &tm.mk, kargs[2] = &tm.mv, kargs[3] = &tm.mdo, kargs[4] = &tm.ms,
-    kargs[5] = &tm.mds, kargs[6] = &ac, kargs[7] = &mode, kargs[8] = &err;
+    kargs[5] = &tm.mds, kargs[6] = &tm.mdq, kargs[7] = &tm.mdk, kargs[8] = &tm.mdv, kargs[9] = &ac,
+    kargs[10] = &mode, kargs[11] = &err;
     C10_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(bwd_chunk_tc_kernel), dim3(a.nb, BH),
                                     dim3(btc::NTH), kargs, btc::L::BYTES, at::cuda::getCurrentCUDAStream()));
   };
@@ -1343,6 +1344,10 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
     const uint64_t srows = (uint64_t)a.B * a.nb * a.Hv * Dk;
     make_map_bf16(&tm.ms, S_in.data_ptr(), Dv, srows, Dv, 64, 128);
     make_map_bf16(&tm.mds, dS_out.data_ptr(), Dv, srows, Dv, 64, 128);
+    // outputs [B * 2L, Hv * D] (per v-head dq and dk): 32-row boxes stored from the staged tiles
+    make_map_bf16(&tm.mdq, dq.data_ptr(), (uint64_t)a.Hv * Dk, rows, (uint64_t)a.Hv * Dk, 64, 32);
+    make_map_bf16(&tm.mdk, dk.data_ptr(), (uint64_t)a.Hv * Dk, rows, (uint64_t)a.Hv * Dk, 64, 32);
+    make_map_bf16(&tm.mdv, dv.data_ptr(), (uint64_t)a.Hv * Dv, rows, (uint64_t)a.Hv * Dv, 64, 32);
   }
   if (!concat) {
     if (tc)

@@ -3,7 +3,8 @@
 // 128> for the fork layout in both modes (0: noised block, dV' = P^T dO; 1: clean chunk, dV' and
 // dS_out from the reverse recurrence), used with the tensor-core recurrence, which adds the noised
 // blocks' state gradients itself (so no dS_inj is stored here). The states come as bf16 S^T rows
-// (the forward's S_in and the recurrence's dS_out, [v][k] per chunk) loaded by TMA.
+// (the forward's S_in and the recurrence's dS_out, [v][k] per chunk) loaded by TMA; the dq, dk and
+// dv rows of the chunk are staged in dead token tiles and written by TMA stores.
 //
 // Per CTA = one chunk (32 tokens) of one v-head. Every product with a 128-wide operand (the state
 // S, dS_out, or a feature dimension) runs as an M = 128 MMA with the feature dimension on the 128
@@ -138,11 +139,19 @@ __device__ __forceinline__ void mma_t(uint32_t d, uint32_t a_tmem, uint64_t bd, 
 
 }  // namespace btc
 
+__device__ __forceinline__ void tma_store_tile(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+
 __global__ void __launch_bounds__(btc::NTH, 1)
     bwd_chunk_tc_kernel(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
                         const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
-                        const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mds, Args a,
-                        int mode, int* err) {
+                        const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mds,
+                        const __grid_constant__ CUtensorMap mdq, const __grid_constant__ CUtensorMap mdk,
+                        const __grid_constant__ CUtensorMap mdv, Args a, int mode, int* err) {
   using namespace btc;
   constexpr int D = 128, C = 32;
   extern __shared__ uint8_t smem_raw[];
@@ -424,13 +433,13 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     ld32(tmem + lane_base + VPT, vp);  // V'^T row v (still in TMEM)
     // dv = beta dR (global), dR tile, -beta E dR tile (noised); per-token sums over the features:
     // dbeta_a = sum_v dR R0, dE_b = -beta sum_v F1 dR, dF = sum_v F7 V'
-    __nv_bfloat16* dvg = a.dv + (tok0 * a.Hv + h) * (int64_t)D + f;
+    // (dv is staged in the V' tile, whose last reader was this round's MMAs, and TMA-stored)
     float f7[32], pb[32];
     if (clean) ld32(tmem + lane_base + F7, f7);
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       const float r0 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[t];
-      dvg[(int64_t)t * a.Hv * D] = __float2bfloat16_rn(sbeta[t] * dr[t]);
+      put(sm + L::VP, off2<32>(t, f), sbeta[t] * dr[t]);
       put(sm + L::DR, off2<32>(t, f), dr[t]);
       pb[t] = dr[t] * r0;
       f1[t] *= dr[t];
@@ -453,6 +462,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     }
 #pragma unroll
     for (int t = 0; t < 32; ++t) dQ[t] = sE[t] * f3[t];
+    fence_proxy_async();  // the staged dv tile -> the TMA store below
   }
   if (ok && warp == 4) {
     // dP -> dPm = dP Gam incl (tile, and transposed), G1 = dP * P -> dgam
@@ -475,6 +485,11 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     sdgam[lane] += rs - cs_mine;
   }
   __syncthreads();
+  if (ok && ctl) {  // dv rows of this chunk: two [32][64] boxes
+    tma_store_tile(&mdv, sm + L::VP, h * D, (int)tok0);
+    tma_store_tile(&mdv, sm + L::VP + 4096, h * D + 64, (int)tok0);
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
   if (ok && warp == 4) {  // combine the four warps' partials
     float sb_ = 0.f, se = 0.f, sf = 0.f;
 #pragma unroll
@@ -612,18 +627,18 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   __syncthreads();
   mark(a, 9);  // R7 and the l2 folds
   if (ok && warp < 4) {
-    // dk = rk (dk^ - k^ <k^, dk^>); dq = rq scale (dq^ - q^n <q^n, dq^>) with q^ = q^n scale
-    __nv_bfloat16* dkg = a.dk + (tok0 * a.Hv + h) * (int64_t)D + f;
-    __nv_bfloat16* dqg = a.dq + (tok0 * a.Hv + h) * (int64_t)D + f;
+    // dk = rk (dk^ - k^ <k^, dk^>); dq = rq scale (dq^ - q^n <q^n, dq^>) with q^ = q^n scale,
+    // staged in the V and dO tiles (no reader left) and TMA-stored
     const float s2 = a.scale * a.scale;
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       const float kn = get(sm + L::K, off2<32>(t, f));
       const float qh = get(sm + L::Q, off2<32>(t, f));
-      dkg[(int64_t)t * a.Hv * D] = __float2bfloat16_rn(srk[t] * (dK[t] - kn * sc[352 + t]));
+      put(sm + L::V, off2<32>(t, f), srk[t] * (dK[t] - kn * sc[352 + t]));
       // q^ = s qn: dq = r (s dq^ - qn <qn, s dq^>) = r s (dq^ - q^ <q^, dq^> / s^2)
-      dqg[(int64_t)t * a.Hv * D] = __float2bfloat16_rn(srq[t] * a.scale * (dQ[t] - qh * sc[384 + t] / s2));
+      put(sm + L::DO, off2<32>(t, f), srq[t] * a.scale * (dQ[t] - qh * sc[384 + t] / s2));
     }
+    fence_proxy_async();
   }
   if (ok && warp == 4) {
     // gates: dgam += dE E - dF F; last += sum dF F + dEc Ec; dg = reverse cumsum; dbeta
@@ -644,6 +659,16 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     a.dbeta[t * a.Hv + h] = sdb[i];
   }
   __syncthreads();
+  if (ctl) {
+    if (ok) {
+      tma_store_tile(&mdk, sm + L::V, h * D, (int)tok0);
+      tma_store_tile(&mdk, sm + L::V + 4096, h * D + 64, (int)tok0);
+      tma_store_tile(&mdq, sm + L::DO, h * D, (int)tok0);
+      tma_store_tile(&mdq, sm + L::DO + 4096, h * D + 64, (int)tok0);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the staged tiles have been read
+  }
   mark(a, 10);
   mark(a, 11);
   tc_fence_before();

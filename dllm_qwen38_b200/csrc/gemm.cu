@@ -609,7 +609,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 constexpr int STAGES2 = 6;
 template <int EPI, bool A_MN, bool B_MN, int NP = 256>
 struct Cfg2 {
-  static_assert(NP == 256 || EPI == EPI_BF16 || EPI == EPI_ADD_BF16, "256 x 512 tiles: bf16 epilogues only");
+  static_assert(NP == 256 || EPI == EPI_BF16 || EPI == EPI_ADD_BF16 || EPI == EPI_SWIGLU,
+                "256 x 512 tiles: bf16 epilogues only");
   static constexpr int NH = NP / 256;                           // N = 256 MMAs per k step
   static constexpr int BN = 256;                                // MMA N (both CTAs' B halves)
   static constexpr int BN_OUT = (EPI == EPI_SWIGLU) ? NP / 2 : NP;  // output columns per tile
@@ -713,7 +714,8 @@ __device__ __forceinline__ bool pair_unit(int u, int full, int tiles_m, int tile
 template <int EPI, bool A_MN, bool B_MN, int NP>
 __global__ void __launch_bounds__(Cfg2<EPI, A_MN, B_MN, NP>::THREADS, 1)
     gemm2_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                 const __grid_constant__ CUtensorMap map_c, GemmArgs args) {
+                 const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_g,
+                 const __grid_constant__ CUtensorMap map_u, GemmArgs args) {
   using C_ = Cfg2<EPI, A_MN, B_MN, NP>;
   constexpr int STAGES = C_::ST;
   constexpr bool WIDE = (NP == 512);
@@ -966,6 +968,85 @@ __global__ void __launch_bounds__(Cfg2<EPI, A_MN, B_MN, NP>::THREADS, 1)
           epi_bar_sync(32 * C_::EPI_WARPS);
           if (!live) {
             epi_bar_sync(32 * C_::EPI_WARPS);
+            if (EPI == EPI_SWIGLU && args.GU != nullptr) {  // round B's two barriers
+              epi_bar_sync(32 * C_::EPI_WARPS);
+              epi_bar_sync(32 * C_::EPI_WARPS);
+            }
+            continue;
+          }
+          if constexpr (EPI == EPI_SWIGLU) {
+            // half h holds gate (columns [0, 128)) and up ([128, 256)) of activation columns
+            // [a0, a0 + 128); warp 2 + e takes activation columns [64 (e / 4), +64). Round A stages
+            // act (blocks 0-1) and, with the gate / up store, gate (blocks 2-3); round B stages up.
+            const bool gu = args.GU != nullptr;
+            const int ab = ((warp - 2) / 4) * 64;
+            const uint32_t t_g = tmem_base + ((uint32_t)(quad * 32) << 16) + h * C_::BN + ab;
+            auto stage = [&](int blk, int c, const float (&f)[32]) {
+              uint8_t* bp = stg + blk * 16384 + row_in_tile * 128;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                uint4 pk;
+                __nv_bfloat162* p2 = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) p2[e] = __floats2bfloat162_rn(f[8 * q + 2 * e], f[8 * q + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(bp + (((4 * c + q) ^ (row_in_tile & 7)) << 4)) = pk;
+              }
+            };
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              float g[32], u[32], act[32];
+              tmem_ld32(t_g + c * 32, g);
+              tmem_ld32(t_g + 128 + c * 32, u);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                // the activation uses the bf16-rounded gate / up, which the backward reads back
+                g[j] = __bfloat162float(__float2bfloat16(g[j] * alpha));
+                u[j] = __bfloat162float(__float2bfloat16(u[j] * alpha));
+                act[j] = silu_f(g[j]) * u[j];
+              }
+              stage(ab / 64, c, act);
+              if (gu) stage(2 + ab / 64, c, g);
+            }
+            if (!gu) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) arrive_remote(tempty0 + h * 8);
+            }
+            fence_proxy_async_smem();
+            epi_bar_sync(32 * C_::EPI_WARPS);
+            const int a0 = tn * C_::BN_OUT + h * C_::HALF_OUT;
+            if (leader_thread && row0 < args.M) {
+              for (int b = 0; b < 2; ++b) {
+                if (a0 + b * 64 >= args.N) break;
+                tma_store_2d(&map_c, stg + b * 16384, a0 + b * 64, row0);
+                if (gu) tma_store_2d(&map_g, stg + (2 + b) * 16384, a0 + b * 64, row0);
+              }
+              bulk_commit();
+            }
+            if (gu) {  // round B: up
+              if (leader_thread) bulk_wait_read0();
+              epi_bar_sync(32 * C_::EPI_WARPS);
+#pragma unroll 1
+              for (int c = 0; c < 2; ++c) {
+                float u[32];
+                tmem_ld32(t_g + 128 + c * 32, u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) u[j] *= alpha;
+                stage(ab / 64, c, u);
+              }
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) arrive_remote(tempty0 + h * 8);
+              fence_proxy_async_smem();
+              epi_bar_sync(32 * C_::EPI_WARPS);
+              if (leader_thread && row0 < args.M) {
+                for (int b = 0; b < 2; ++b) {
+                  if (a0 + b * 64 >= args.N) break;
+                  tma_store_2d(&map_u, stg + b * 16384, a0 + b * 64, row0);
+                }
+                bulk_commit();
+              }
+            }
             continue;
           }
           const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + h * C_::BN + cbase;
@@ -1076,6 +1157,8 @@ struct alignas(64) GemmLaunch {
   CUtensorMap ma;
   CUtensorMap mb;
   CUtensorMap mc;  // the output, for the TMA-store epilogue of the 256 x 512 pair kernel
+  CUtensorMap mg;  // SwiGLU gate / up store: the gate half and the up half of [M, 2F]
+  CUtensorMap mu;
   GemmArgs args;
 };
 static thread_local GemmLaunch tls_launch;
@@ -1199,7 +1282,7 @@ static void launch_pair(GemmLaunch* L, cudaStream_t st) {
   attrs[0].val.clusterDim.z = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = 1;
-  void* kargs[4] = {&L->ma, &L->mb, &L->mc, &L->args};
+  void* kargs[6] = {&L->ma, &L->mb, &L->mc, &L->mg, &L->mu, &L->args};
   C10_CUDA_CHECK(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), kargs));
 }
 
@@ -1560,7 +1643,8 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
   // the CTA-pair kernel for large forward (K-major) GEMMs
   if (use_pair(a_mn, b_mn, M, N, epi, tp, ag)) {
     // 256 x 512 tiles for bf16 outputs (an add only in place: the TMA reduce adds into C itself)
-    const bool wide = pair_wide() && (epi == EPI_BF16 || (epi == EPI_ADD_BF16 && args.R == c.data_ptr() && ldr == ldc));
+    const bool wide = pair_wide() && (epi == EPI_BF16 || epi == EPI_SWIGLU ||
+                                      (epi == EPI_ADD_BF16 && args.R == c.data_ptr() && ldr == ldc));
     const int64_t tile_out = (epi == EPI_SWIGLU ? 128 : 256) * (wide ? 2 : 1);
     choose_raster(args, M, epi == EPI_SWIGLU ? 2 * N : N, K, (int)((M + 255) / 256), (int)((N + tile_out - 1) / tile_out));
     if (a_mn)
@@ -1575,6 +1659,10 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
       TORCH_CHECK(reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0 && (ldc * 2) % 16 == 0,
                   "gemm: TMA-store output must have 16-byte aligned rows");
       make_map_bf16(&L->mc, c.data_ptr(), N, M, ldc, 64, 128);
+      if (epi == EPI_SWIGLU && args.GU != nullptr) {
+        make_map_bf16(&L->mg, args.GU, N, M, 2 * N, 64, 128);
+        make_map_bf16(&L->mu, args.GU + N, N, M, 2 * N, 64, 128);
+      }
     }
 #define BDLLM_PAIR_CASE(E, AM, BMN)                   \
   if (epi == E && a_mn == AM && b_mn == BMN) {        \
@@ -1587,6 +1675,7 @@ static void gemm_impl(const at::Tensor& a, bool a_mn, int64_t lda, const at::Ten
     return;                                           \
   }
     BDLLM_WIDE_CASE(EPI_BF16, false, false)
+    BDLLM_WIDE_CASE(EPI_SWIGLU, false, false)
     BDLLM_WIDE_CASE(EPI_ADD_BF16, false, false)
     BDLLM_WIDE_CASE(EPI_BF16, false, true)
     BDLLM_WIDE_CASE(EPI_ADD_BF16, false, true)

@@ -54,6 +54,29 @@ def timeit(fn, iters: int, warmup: int) -> float:
     return statistics.median(ts)
 
 
+def sustained(fn, seconds: float):
+    """Mean ms of `fn` run back to back for about `seconds` (CUDA events around the whole loop),
+    with the SM clocks sampled during it."""
+    from ..utils.clocks import ClockSampler
+
+    for _ in range(5):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    n = max(10, int(seconds * 1000.0 / max(e0.elapsed_time(e1) / 10, 1e-3)))
+    sampler = ClockSampler(gpu=torch.cuda.current_device()).start()
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n, sampler.stop()
+
+
 def op_gemm(a):
     """--layout nt: y[M,N] = x[M,K] w[N,K]^T (forward); nn: x[M,K] w[K,N] (input gradient, w read
     N-contiguous); tn: g[M,N] += a[K,M]^T b[K,N] into bf16 (weight gradient, both operands
@@ -246,6 +269,17 @@ def op_rmsnorm(a):
     return (lambda: Cu.rmsnorm(x, w, 1e-6)), 4.0 * x.numel(), 4.0 * x.numel()
 
 
+def op_rmsnorm_bwd(a):
+    """RMSNorm(1+w) backward (`_C.rmsnorm_bwd`): dx and the weight-gradient partial rows, then
+    their column sum; algorithmic bytes = read x and dy, write dx."""
+    from ..ops import cuda as Cu
+
+    x = torch.randn(a.rows, a.D, device="cuda").bfloat16()
+    dy = torch.randn_like(x)
+    w1 = torch.ones(a.D, device="cuda")
+    return (lambda: Cu._C.rmsnorm_bwd(dy, x, w1, 1e-6)), 8.0 * x.numel(), 6.0 * x.numel()
+
+
 def op_adamw(a):
     from ..ops import cuda as Cu
 
@@ -368,7 +402,7 @@ def op_embed(a):
     return fn, 1.0 * ids.numel() * D, ids.numel() * D * (2 + 2 + 2 + 8)
 
 
-OPS = {"gemm": op_gemm, "swiglu": op_swiglu, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
+OPS = {"gemm": op_gemm, "swiglu": op_swiglu, "rmsnorm_bwd": op_rmsnorm_bwd, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
        "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed,
        "adamw": op_adamw}
 
@@ -390,16 +424,26 @@ def main(argv=None) -> int:
     p.add_argument("--n", type=int, default=400_000_000)
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--sustain", type=float, default=0.0,
+                   help="seconds: run the op back to back (no L2 flush) with the SM clocks sampled, "
+                        "the rate under the power cap rather than a burst")
     a = p.parse_args(argv)
     sys.path.insert(0, ROOT)
     fn, flops, byts = OPS[a.op](a)
-    ms = timeit(fn, a.iters, a.warmup)
+    clocks = None
+    if a.sustain > 0:
+        ms, clocks = sustained(fn, a.sustain)
+    else:
+        ms = timeit(fn, a.iters, a.warmup)
     bw, tf, src = peaks()
     s = ms / 1e3
     out = {"op": a.op, "impl": a.impl, "ms": round(ms, 4), "tflops": round(flops / s / 1e12, 2),
            "gbs": round(byts / s / 1e9, 1), "frac_bf16_peak": round(flops / s / tf, 3),
            "frac_hbm_peak": round(byts / s / bw, 3), "peaks": src,
            "shape": {k: getattr(a, k) for k in ("M", "N", "K", "layout", "B", "L", "block", "rows", "D", "vocab", "n")}}
+    if clocks is not None:
+        out["sustained_s"] = a.sustain
+        out["clocks"] = clocks
     print(json.dumps(out))
     return 0
 

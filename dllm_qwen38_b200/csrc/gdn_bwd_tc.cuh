@@ -565,33 +565,50 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  if (ok && warp == 4) {
-    // dA = strict_lower(-dA'); dKK = dA beta_i Gam; H2 = dA beta KK Gam -> dgam, dbeta; sym tile
+  // dA = strict_lower(-dA'); dKK = dA beta_i Gam; H2 = dA beta KK Gam -> dgam, dbeta; sym tile.
+  // Spread over the four feature warps (idle in this round): warp 0 moves the dA' rows out of
+  // TMEM lanes 0-31, then warp w takes rows [8 w, 8 w + 8) with lane = column.
+  if (ok && warp == 0) {
     float da[32];
     ld32(tmem + DA, da);
-    const float gi = sgam[lane], bi = sbeta[lane];
-    float rsH = 0.f, rsB = 0.f;
-    float dkk[32], h2[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float gm = j < lane ? __expf(gi - sgam[j]) : 0.f;
-      const float dA = j < lane ? -da[j] : 0.f;
-      const float kkv = tb[lane * 33 + j];
-      dkk[j] = dA * bi * gm;
-      h2[j] = dA * bi * kkv * gm;
-      rsB += dA * kkv * gm;
-      rsH += h2[j];
+    for (int j = 0; j < 32; ++j) red[lane * 33 + j] = da[j];
+  }
+  if (ok && warp < 4) {
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // the four feature warps
+    const int j = lane;
+    const float gj = sgam[j];
+    float csH = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int i = 8 * warp + r;
+      const float gm = j < i ? __expf(sgam[i] - gj) : 0.f;
+      const float dA = j < i ? -red[i * 33 + j] : 0.f;
+      const float kkv = tb[i * 33 + j];
+      const float dkk = dA * sbeta[i] * gm;
+      const float h2 = dkk * kkv;
+      float rb = dA * kkv * gm, rh = h2;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        rb += __shfl_xor_sync(0xffffffffu, rb, o);
+        rh += __shfl_xor_sync(0xffffffffu, rh, o);
+      }
+      if (lane == 0) part[128 + i] = rh, part[160 + i] = rb;  // row sums of H2 and dA KK Gam
+      csH += h2;
+      tb[(64 + i) * 33 + j] = dkk;
     }
-    // column sums of H2 (token `lane`'s column total)
-    const float csH = fold32(h2, lane);
-    sdgam[lane] += rsH - csH;
-    sdb[lane] += rsB;
-    // sym = dKK + dKK^T (dKK rows through the token buffer for the transpose)
+    part[warp * 32 + j] = csH;  // column partial of H2 over this warp's rows
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (warp == 0) {
+      const float cs = part[j] + part[32 + j] + part[64 + j] + part[96 + j];
+      sdgam[j] += part[128 + j] - cs;
+      sdb[j] += part[160 + j];
+    }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) tb[(64 + lane) * 33 + j] = dkk[j];
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 32; ++j) put(sm + L::SYM, off1(lane, j), dkk[j] + tb[(64 + j) * 33 + lane]);
+    for (int r = 0; r < 8; ++r) {  // sym = dKK + dKK^T
+      const int i = 8 * warp + r;
+      put(sm + L::SYM, off1(i, j), tb[(64 + i) * 33 + j] + tb[(64 + j) * 33 + i]);
+    }
   }
   round_end();
   mark(a, 7);
@@ -629,14 +646,14 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   if (ok && warp < 4) {
     // dk = rk (dk^ - k^ <k^, dk^>); dq = rq scale (dq^ - q^n <q^n, dq^>) with q^ = q^n scale,
     // staged in the V and dO tiles (no reader left) and TMA-stored
-    const float s2 = a.scale * a.scale;
+    const float inv_s2 = 1.f / (a.scale * a.scale);
 #pragma unroll
     for (int t = 0; t < 32; ++t) {
       const float kn = get(sm + L::K, off2<32>(t, f));
       const float qh = get(sm + L::Q, off2<32>(t, f));
       put(sm + L::V, off2<32>(t, f), srk[t] * (dK[t] - kn * sc[352 + t]));
       // q^ = s qn: dq = r (s dq^ - qn <qn, s dq^>) = r s (dq^ - q^ <q^, dq^> / s^2)
-      put(sm + L::DO, off2<32>(t, f), srq[t] * a.scale * (dQ[t] - qh * sc[384 + t] / s2));
+      put(sm + L::DO, off2<32>(t, f), srq[t] * a.scale * (dQ[t] - qh * sc[384 + t] * inv_s2));
     }
     fence_proxy_async();
   }

@@ -28,7 +28,11 @@
 
 namespace btc {
 
-constexpr int NTH = 192;  // warps 0-3 features, warp 4 tokens, warp 5 control (TMA + MMA)
+// warps 0-7 features (warp w: TMEM lane quadrant w % 4, tokens [16 (w / 4), +16) of the chunk),
+// warp 8 tokens, warp 9 control (TMA + MMA)
+constexpr int NTH = 320;
+constexpr int TOKW = 8;    // the token warp (reads TMEM lanes 0-31, where token x token products land)
+constexpr int CTL = 288;   // the control thread
 constexpr int TOK = 32 * 128 * 2;  // token tile [32 x 128] bf16, two [32][64] boxes (8 KB)
 constexpr int TT = 4096;           // token x token tile [32 x 64] bf16 (32 columns used)
 constexpr int ST = 128 * 128 * 2;  // state tile [128 x 128] bf16, two [128][64] boxes (32 KB)
@@ -106,6 +110,41 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
       "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// Half-width transpose-reduce: every lane holds 16 per-token values; after 31 shuffles lane l
+// holds the sum over all 32 lanes of value l % 16.
+__device__ __forceinline__ float fold16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], 16);
+#pragma unroll
+  for (int o = 8; o >= 1; o >>= 1) {
+    const bool hi = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      const float send = hi ? v[i] : v[i + o];
+      const float keep = hi ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
 }
 // Warp transpose-reduce: every lane holds 32 per-token values; after 31 shuffles lane l holds the
 // sum over the warp's lanes of value l.
@@ -192,7 +231,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t sb = smem_u32(sm);
-  if (threadIdx.x == 160) {  // TMA: raw q, k, v rows and dO of this chunk; S^T (and dS_out^T) tiles
+  if (threadIdx.x == CTL) {  // TMA: raw q, k, v rows and dO of this chunk; S^T (and dS_out^T) tiles
     mbar_arrive_expect_tx(ld_bar, 4 * TOK + (clean ? 2 : 1) * ST);
     for (int x = 0; x < 2; ++x) {
       tma_load_2d(sm + L::Q + x * 4096, &mq, ld_bar, hk * D + x * 64, (int)tok0);
@@ -204,7 +243,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     }
   }
   // ---- gates (token warp): gam = cumsum g, beta, E, F
-  if (warp == 4) {
+  if (warp == TOKW) {
     const int64_t t = tok0 + lane;
     float gv = a.g[t * a.Hv + h];
     const float bv = a.beta[t * a.Hv + h];
@@ -269,7 +308,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     }
   }
   __syncthreads();
-  if (ok && warp == 4 && clean) {  // dEc = <S, dS_out>: sum the 128 row partials
+  if (ok && warp == TOKW && clean) {  // dEc = <S, dS_out>: sum the 128 row partials
     float s = 0.f;
     for (int k = lane; k < 128; k += 32) s += red[k * 33];
 #pragma unroll
@@ -296,9 +335,10 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     __syncthreads();
     tc_fence_after();
   };
-  const bool ctl = threadIdx.x == 160;
+  const bool ctl = threadIdx.x == CTL;
   const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-  const int f = (warp & 3) * 32 + lane;  // feature row of warps 0-3
+  const int f = (warp & 3) * 32 + lane;  // feature row of the feature warps
+  const int q4 = warp & 3, hh = (warp >> 2) & 1, tb0 = 16 * hh;  // lane quadrant, token half
 
   // ================================================================ R1
   if (ok && ctl) {
@@ -314,30 +354,32 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  float f1[32];  // (k^ S)^T row v of this thread (kept for dE)
-  if (ok && warp < 4) {
+  float f1[16];  // (k^ S)^T row v of this thread, its 16 tokens (kept for dE)
+  if (ok && warp < 8) {
     // R0^T = V^T - E * F1 (v = f); R = beta R0 -> tile and TMEM A; dE_a = sum_v F2 * dO
-    float f2[32];
-    ld32(tmem + lane_base + F1, f1);
-    ld32(tmem + lane_base + F2, f2);
-    uint32_t ra[16];
+    float f2[16];
+    ld16(tmem + lane_base + F1 + tb0, f1);
+    ld16(tmem + lane_base + F2 + tb0, f2);
+    uint32_t ra[8];
 #pragma unroll
-    for (int t = 0; t < 32; t += 2) {
-      const float r00 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[t];
-      const float r01 = get(sm + L::V, off2<32>(t + 1, f)) - sE[t + 1] * f1[t + 1];
-      f2[t] *= get(sm + L::DO, off2<32>(t, f));
-      f2[t + 1] *= get(sm + L::DO, off2<32>(t + 1, f));
+    for (int u = 0; u < 16; u += 2) {
+      const int t = tb0 + u;
+      const float r00 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[u];
+      const float r01 = get(sm + L::V, off2<32>(t + 1, f)) - sE[t + 1] * f1[u + 1];
+      f2[u] *= get(sm + L::DO, off2<32>(t, f));
+      f2[u + 1] *= get(sm + L::DO, off2<32>(t + 1, f));
       const float rb0 = sbeta[t] * r00, rb1 = sbeta[t + 1] * r01;
       put(sm + L::R, off2<32>(t, f), rb0);
       put(sm + L::R, off2<32>(t + 1, f), rb1);
-      ra[t >> 1] = pk2(rb0, rb1);
+      ra[u >> 1] = pk2(rb0, rb1);
     }
-    st16(tmem + lane_base + RA, ra);
-    part[warp * 32 + lane] = fold32(f2, lane);  // dE_a partial of token `lane` over this warp's features
+    st8(tmem + lane_base + RA + 8 * hh, ra);
+    const float s0 = fold16(f2, lane);  // dE_a partial of token tb0 + lane % 16 over this warp's features
+    if (lane < 16) part[q4 * 32 + tb0 + lane] = s0;
   }
   __syncthreads();
-  if (ok && warp == 4) sdE[lane] = part[lane] + part[32 + lane] + part[64 + lane] + part[96 + lane];
-  if (ok && warp == 4) {
+  if (ok && warp == TOKW) sdE[lane] = part[lane] + part[32 + lane] + part[64 + lane] + part[96 + lane];
+  if (ok && warp == TOKW) {
     float kk[32], qk[32];
     ld32(tmem + KK, kk);
     ld32(tmem + QK, qk);
@@ -384,26 +426,27 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  if (ok && warp < 4) {
-    float vp[32], dv[32];
-    ld32(tmem + lane_base + VPT, vp);
+  if (ok && warp < 8) {
+    float vp[16], dv[16];
+    ld16(tmem + lane_base + VPT + tb0, vp);
     if (clean) {
-      const float* g = a.dVp + base * C * D + f;
+      const float* g = a.dVp + base * C * D + (int64_t)tb0 * D + f;
 #pragma unroll
-      for (int t = 0; t < 32; ++t) dv[t] = g[t * D];
+      for (int u = 0; u < 16; ++u) dv[u] = g[u * D];
     } else {
-      ld32(tmem + lane_base + DVT, dv);
+      ld16(tmem + lane_base + DVT + tb0, dv);
     }
-    uint32_t da[16];
+    uint32_t da[8];
 #pragma unroll
-    for (int t = 0; t < 32; t += 2) {
-      put(sm + L::VP, off2<32>(t, f), vp[t]);
-      put(sm + L::VP, off2<32>(t + 1, f), vp[t + 1]);
-      put(sm + L::DV, off2<32>(t, f), dv[t]);
-      put(sm + L::DV, off2<32>(t + 1, f), dv[t + 1]);
-      da[t >> 1] = pk2(dv[t], dv[t + 1]);
+    for (int u = 0; u < 16; u += 2) {
+      const int t = tb0 + u;
+      put(sm + L::VP, off2<32>(t, f), vp[u]);
+      put(sm + L::VP, off2<32>(t + 1, f), vp[u + 1]);
+      put(sm + L::DV, off2<32>(t, f), dv[u]);
+      put(sm + L::DV, off2<32>(t + 1, f), dv[u + 1]);
+      da[u >> 1] = pk2(dv[u], dv[u + 1]);
     }
-    st16(tmem + lane_base + DVA, da);
+    st8(tmem + lane_base + DVA + 8 * hh, da);
   }
   round_end();
   mark(a, 3);
@@ -424,47 +467,53 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  float dK[32];  // dk^ row k = f (transposed accumulation over the rounds), dQ likewise
-  float dQ[32];
-  if (ok && warp < 4) {
-    float dr[32];
-    ld32(tmem + lane_base + DRT, dr);
-    float vp[32];
-    ld32(tmem + lane_base + VPT, vp);  // V'^T row v (still in TMEM)
+  float dK[16];  // dk^ row k = f, this warp's 16 tokens (accumulated over the rounds), dQ likewise
+  float dQ[16];
+  if (ok && warp < 8) {
+    float dr[16];
+    ld16(tmem + lane_base + DRT + tb0, dr);
+    float vp[16];
+    ld16(tmem + lane_base + VPT + tb0, vp);  // V'^T row v (still in TMEM)
     // dv = beta dR (global), dR tile, -beta E dR tile (noised); per-token sums over the features:
     // dbeta_a = sum_v dR R0, dE_b = -beta sum_v F1 dR, dF = sum_v F7 V'
     // (dv is staged in the V' tile, whose last reader was this round's MMAs, and TMA-stored)
-    float f7[32], pb[32];
-    if (clean) ld32(tmem + lane_base + F7, f7);
+    float f7[16], pb[16];
+    if (clean) ld16(tmem + lane_base + F7 + tb0, f7);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      const float r0 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[t];
-      put(sm + L::VP, off2<32>(t, f), sbeta[t] * dr[t]);
-      put(sm + L::DR, off2<32>(t, f), dr[t]);
-      pb[t] = dr[t] * r0;
-      f1[t] *= dr[t];
-      f7[t] = clean ? f7[t] * vp[t] : 0.f;
+    for (int u = 0; u < 16; ++u) {
+      const int t = tb0 + u;
+      const float r0 = get(sm + L::V, off2<32>(t, f)) - sE[t] * f1[u];
+      put(sm + L::VP, off2<32>(t, f), sbeta[t] * dr[u]);
+      put(sm + L::DR, off2<32>(t, f), dr[u]);
+      pb[u] = dr[u] * r0;
+      f1[u] *= dr[u];
+      f7[u] = clean ? f7[u] * vp[u] : 0.f;
     }
-    part[warp * 32 + lane] = fold32(pb, lane);
-    part[128 + warp * 32 + lane] = fold32(f1, lane);
-    part[256 + warp * 32 + lane] = fold32(f7, lane);
+    {
+      const float s0 = fold16(pb, lane), s1 = fold16(f1, lane), s2 = fold16(f7, lane);
+      if (lane < 16) {
+        part[q4 * 32 + tb0 + lane] = s0;
+        part[128 + q4 * 32 + tb0 + lane] = s1;
+        part[256 + q4 * 32 + tb0 + lane] = s2;
+      }
+    }
     // dK^T (row k = f): clean F * (V' dS_out^T)^T ; dQ^T = E * F3
-    float f3[32];
-    ld32(tmem + lane_base + F3, f3);
+    float f3[16];
+    ld16(tmem + lane_base + F3 + tb0, f3);
     if (clean) {
-      float f6[32];
-      ld32(tmem + lane_base + F6, f6);
+      float f6[16];
+      ld16(tmem + lane_base + F6 + tb0, f6);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) dK[t] = sF[t] * f6[t];
+      for (int u = 0; u < 16; ++u) dK[u] = sF[tb0 + u] * f6[u];
     } else {
 #pragma unroll
-      for (int t = 0; t < 32; ++t) dK[t] = 0.f;
+      for (int u = 0; u < 16; ++u) dK[u] = 0.f;
     }
 #pragma unroll
-    for (int t = 0; t < 32; ++t) dQ[t] = sE[t] * f3[t];
+    for (int u = 0; u < 16; ++u) dQ[u] = sE[tb0 + u] * f3[u];
     fence_proxy_async();  // the staged dv tile -> the TMA store below
   }
-  if (ok && warp == 4) {
+  if (ok && warp == TOKW) {
     // dP -> dPm = dP Gam incl (tile, and transposed), G1 = dP * P -> dgam
     float dp[32];
     ld32(tmem + DP, dp);
@@ -490,7 +539,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     tma_store_tile(&mdv, sm + L::VP + 4096, h * D + 64, (int)tok0);
     asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   }
-  if (ok && warp == 4) {  // combine the four warps' partials
+  if (ok && warp == TOKW) {  // combine the four lane quadrants' partials
     float sb_ = 0.f, se = 0.f, sf = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
@@ -521,19 +570,19 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  if (ok && warp < 4) {
-    float x[32];
-    ld32(tmem + lane_base + F4, x);
+  if (ok && warp < 8) {
+    float x[16];
+    ld16(tmem + lane_base + F4 + tb0, x);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) dK[t] -= sbeta[t] * sE[t] * x[t];
-    ld32(tmem + lane_base + DQB, x);
+    for (int u = 0; u < 16; ++u) dK[u] -= sbeta[tb0 + u] * sE[tb0 + u] * x[u];
+    ld16(tmem + lane_base + DQB + tb0, x);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) dQ[t] += x[t];
-    ld32(tmem + lane_base + DKB, x);
+    for (int u = 0; u < 16; ++u) dQ[u] += x[u];
+    ld16(tmem + lane_base + DKB + tb0, x);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) dK[t] += x[t];
+    for (int u = 0; u < 16; ++u) dK[u] += x[u];
   }
-  if (ok && warp == 4) {  // dT -> tile (A operand of Z = dT T^T)
+  if (ok && warp == TOKW) {  // dT -> tile (A operand of Z = dT T^T)
     float dt[32];
     ld32(tmem + DT_C, dt);
 #pragma unroll
@@ -549,7 +598,7 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     mma_commit(mma_bar);
   }
   ok = ok && round_wait();
-  if (ok && warp == 4) {
+  if (ok && warp == TOKW) {
     float z[32];
     ld32(tmem + Z_C, z);
 #pragma unroll
@@ -621,43 +670,47 @@ __global__ void __launch_bounds__(btc::NTH, 1)
   }
   ok = ok && round_wait();
   mark(a, 8);  // R7 MMA
-  if (ok && warp < 4) {
-    float x[32];
-    ld32(tmem + lane_base + DKC, x);
+  if (ok && warp < 8) {
+    float x[16];
+    ld16(tmem + lane_base + DKC + tb0, x);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) dK[t] += x[t];
+    for (int u = 0; u < 16; ++u) dK[u] += x[u];
     // l2norm backward needs per-token dots <k^, dk^> and <q^, dq^> over the 128 features
-    float xk[32], xq[32];
+    float xk[16], xq[16];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
-      xk[t] = get(sm + L::K, off2<32>(t, f)) * dK[t];
-      xq[t] = get(sm + L::Q, off2<32>(t, f)) * dQ[t];
+    for (int u = 0; u < 16; ++u) {
+      xk[u] = get(sm + L::K, off2<32>(tb0 + u, f)) * dK[u];
+      xq[u] = get(sm + L::Q, off2<32>(tb0 + u, f)) * dQ[u];
     }
-    part[warp * 32 + lane] = fold32(xk, lane);
-    part[128 + warp * 32 + lane] = fold32(xq, lane);
+    const float s0 = fold16(xk, lane), s1 = fold16(xq, lane);
+    if (lane < 16) {
+      part[q4 * 32 + tb0 + lane] = s0;
+      part[128 + q4 * 32 + tb0 + lane] = s1;
+    }
   }
   __syncthreads();
-  if (ok && warp == 4) {
+  if (ok && warp == TOKW) {
     sc[352 + lane] = part[lane] + part[32 + lane] + part[64 + lane] + part[96 + lane];  // <k^, dk^>
     sc[384 + lane] = part[128 + lane] + part[160 + lane] + part[192 + lane] + part[224 + lane];  // <q^, dq^>
   }
   __syncthreads();
   mark(a, 9);  // R7 and the l2 folds
-  if (ok && warp < 4) {
+  if (ok && warp < 8) {
     // dk = rk (dk^ - k^ <k^, dk^>); dq = rq scale (dq^ - q^n <q^n, dq^>) with q^ = q^n scale,
     // staged in the V and dO tiles (no reader left) and TMA-stored
     const float inv_s2 = 1.f / (a.scale * a.scale);
 #pragma unroll
-    for (int t = 0; t < 32; ++t) {
+    for (int u = 0; u < 16; ++u) {
+      const int t = tb0 + u;
       const float kn = get(sm + L::K, off2<32>(t, f));
       const float qh = get(sm + L::Q, off2<32>(t, f));
-      put(sm + L::V, off2<32>(t, f), srk[t] * (dK[t] - kn * sc[352 + t]));
+      put(sm + L::V, off2<32>(t, f), srk[t] * (dK[u] - kn * sc[352 + t]));
       // q^ = s qn: dq = r (s dq^ - qn <qn, s dq^>) = r s (dq^ - q^ <q^, dq^> / s^2)
-      put(sm + L::DO, off2<32>(t, f), srq[t] * a.scale * (dQ[t] - qh * sc[384 + t] * inv_s2));
+      put(sm + L::DO, off2<32>(t, f), srq[t] * a.scale * (dQ[u] - qh * sc[384 + t] * inv_s2));
     }
     fence_proxy_async();
   }
-  if (ok && warp == 4) {
+  if (ok && warp == TOKW) {
     // gates: dgam += dE E - dF F; last += sum dF F + dEc Ec; dg = reverse cumsum; dbeta
     const int i = lane;
     float dgi = sdgam[i] + sdE[i] * sE[i] - sdF[i] * sF[i];

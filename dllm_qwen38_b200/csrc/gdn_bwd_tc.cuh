@@ -513,25 +513,39 @@ __global__ void __launch_bounds__(btc::NTH, 1)
     for (int u = 0; u < 16; ++u) dQ[u] = sE[tb0 + u] * f3[u];
     fence_proxy_async();  // the staged dv tile -> the TMA store below
   }
+  // dP -> dPm = dP Gam incl (tile, and transposed), G1 = dP * P -> dgam, on the token and the
+  // control warp (free after issuing this round): the token warp moves the dP rows out of TMEM
+  // lanes 0-31, then warp 8 + w takes rows [16 w, 16 w + 16) with lane = column.
+  float* dpr = red;                 // dP rows [32][33]
+  float* g1sum = red + 32 * 33;     // row sums of G1 [32], then the two column partials [2][32]
   if (ok && warp == TOKW) {
-    // dP -> dPm = dP Gam incl (tile, and transposed), G1 = dP * P -> dgam
     float dp[32];
     ld32(tmem + DP, dp);
-    const float gi = sgam[lane];
-    float rs = 0.f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float gm = j <= lane ? __expf(gi - sgam[j]) : 0.f;
-      const float x = dp[j] * gm;
-      put(sm + L::DPM, off1(lane, j), x);
-      put(sm + L::DPMT, off1(j, lane), x);
-      const float g1 = dp[j] * tb[(32 + lane) * 33 + j];
-      rs += g1;
-      dp[j] = g1;
+    for (int j = 0; j < 32; ++j) dpr[lane * 33 + j] = dp[j];
+  }
+  if (ok && warp >= TOKW) {
+    asm volatile("bar.sync 2, 64;" ::: "memory");  // warps 8 and 9
+    const int j = lane, w = warp - TOKW;
+    const float gj = sgam[j];
+    float cs = 0.f;
+#pragma unroll 4
+    for (int r = 0; r < 16; ++r) {
+      const int i = 16 * w + r;
+      const float dpv = dpr[i * 33 + j];
+      const float x = j <= i ? dpv * __expf(sgam[i] - gj) : 0.f;
+      put(sm + L::DPM, off1(i, j), x);
+      put(sm + L::DPMT, off1(j, i), x);
+      const float g1 = dpv * tb[(32 + i) * 33 + j];
+      float rs = g1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+      if (lane == 0) g1sum[i] = rs;
+      cs += g1;
     }
-    // column sums of G1 across lanes (token `lane`'s column total)
-    const float cs_mine = fold32(dp, lane);
-    sdgam[lane] += rs - cs_mine;
+    g1sum[32 + 32 * w + j] = cs;
+    asm volatile("bar.sync 2, 64;" ::: "memory");
+    if (w == 0) sdgam[j] += g1sum[j] - (g1sum[32 + j] + g1sum[64 + j]);  // row total - column total
   }
   __syncthreads();
   if (ok && ctl) {  // dv rows of this chunk: two [32][64] boxes

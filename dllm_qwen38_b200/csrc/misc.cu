@@ -66,6 +66,46 @@ at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu) {
   return out;
 }
 
+// act = silu(g) * u from the stored bf16 (gate | up), the value the SwiGLU GEMM epilogue wrote
+// (same rounding: the epilogue applies silu to the bf16-rounded gate and up)
+__global__ void swiglu_act_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ act,
+                                  int64_t rows, int F) {
+  const int64_t n = rows * (int64_t)(F / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (F / 8);
+    const int c = (int)(i % (F / 8)) * 8;
+    const uint4 gg = *reinterpret_cast<const uint4*>(gu + r * 2 * F + c);
+    const uint4 uu = *reinterpret_cast<const uint4*>(gu + r * 2 * F + F + c);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gg);
+    const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uu);
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 g = __bfloat1622float2(g2[e]), u = __bfloat1622float2(u2[e]);
+      o2[e] = __floats2bfloat162_rn(silu_f(g.x) * u.x, silu_f(g.y) * u.y);
+    }
+    *reinterpret_cast<uint4*>(act + r * F + c) = o;
+  }
+}
+
+at::Tensor swiglu_act(const at::Tensor& gu) {
+  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.is_contiguous() && gu.size(-1) % 16 == 0,
+              "swiglu_act: contiguous bf16 [..., 2F], F % 8 == 0");
+  const int F = gu.size(-1) / 2;
+  auto sizes = gu.sizes().vec();
+  sizes.back() = F;
+  auto out = at::empty(sizes, gu.options());
+  const int64_t rows = gu.numel() / (2 * F);
+  if (rows == 0) return out;
+  c10::cuda::CUDAGuard g(gu.device());
+  const int64_t n = rows * (F / 8);
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  swiglu_act_kernel<<<grid, 256, 0, stream()>>>(cbf(gu), bfp(out), rows, F);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return out;
+}
+
 // ------------------------------------------------------------------------------- conv
 // raw [B, 2L, C] (row stride ld), w [C, K] fp32. Source position of tap j for output token t:
 //   q = t - (K-1) + j in the stream's own coordinates; see source_of().
@@ -731,6 +771,55 @@ void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh) {
   c10::cuda::CUDAGuard g(grad.device());
   embed_bwd_kernel<<<(int)((N + 7) / 8), 256, 0, stream()>>>(ids.data_ptr<int64_t>(), cbf(d), D, V,
                                                              grad.data_ptr<float>(), N);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Sorted variant straight into a bf16 gradient (no fp32 [V, D] table): sid = the ids sorted, perm
+// their positions in dh. The warp at the first position of each run of equal ids sums that run's
+// dh rows in fp32, 8 columns per lane at a time, and writes the bf16 row; rows of ids absent from
+// the batch keep the zeros the caller wrote. Deterministic (fixed order within a run).
+__global__ void embed_bwd_sorted_kernel(const int64_t* __restrict__ sid, const int64_t* __restrict__ perm,
+                                        const __nv_bfloat16* __restrict__ dh, int D, int64_t V,
+                                        __nv_bfloat16* __restrict__ grad, int64_t N) {
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (i >= N) return;
+  const int64_t id = sid[i];
+  if ((i > 0 && sid[i - 1] == id) || id < 0 || id >= V) return;  // not the start of a run
+  int64_t end = i + 1;
+  while (end < N && sid[end] == id) ++end;
+  for (int c = (threadIdx.x & 31) * 8; c < D; c += 256) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int64_t j = i; j < end; ++j) {
+      const uint4 p = *reinterpret_cast<const uint4*>(dh + perm[j] * D + c);
+      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(p2[e]);
+        acc[2 * e] += f.x, acc[2 * e + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+    *reinterpret_cast<uint4*>(grad + id * D + c) = o;
+  }
+}
+
+void embed_bwd_sorted(at::Tensor& grad, const at::Tensor& sid, const at::Tensor& perm, const at::Tensor& dh) {
+  TORCH_CHECK(grad.dim() == 2 && grad.is_contiguous() && grad.scalar_type() == at::kBFloat16,
+              "embed_bwd_sorted: bf16 [V, D]");
+  TORCH_CHECK(sid.scalar_type() == at::kLong && perm.scalar_type() == at::kLong && sid.is_contiguous() &&
+                  perm.is_contiguous() && sid.numel() == perm.numel(),
+              "embed_bwd_sorted: int64 sorted ids and positions");
+  const int64_t N = sid.numel(), V = grad.size(0);
+  const int D = grad.size(1);
+  auto d = dh.to(at::kBFloat16).contiguous();
+  TORCH_CHECK(d.numel() == N * D && D % 8 == 0, "embed_bwd_sorted: dh [N, D]");
+  if (N == 0) return;
+  c10::cuda::CUDAGuard g(grad.device());
+  embed_bwd_sorted_kernel<<<(int)((N + 7) / 8), 256, 0, stream()>>>(sid.data_ptr<int64_t>(), perm.data_ptr<int64_t>(),
+                                                                    cbf(d), D, V, bfp(grad), N);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

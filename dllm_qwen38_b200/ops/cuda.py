@@ -275,13 +275,17 @@ class _SwiGLUMLP(torch.autograd.Function):
         saved = ActStore.take() if ActStore.gemms else None
         if saved is not None:
             y, act, gu = saved
+            if act is None:  # kept without the activation: rebuilt from the kept bf16 gate|up
+                act = _C.swiglu_act(gu)
+                _count()
         else:
-            # the saving forward (no grad) keeps gate|up for the backward it will serve
+            # the saving forward (no grad) keeps gate|up for the backward it will serve, and not the
+            # activation, which one element-wise pass rebuilds from it (a third less memory)
             need = any(ctx.needs_input_grad) or (ActStore.gemms and ActStore.mode == "save")
             act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
             y = gemm_nt(act, w_down).reshape(*x.shape[:-1], w_down.shape[0])
             if ActStore.gemms:
-                ActStore.put(y, act, gu)
+                ActStore.put(y, None if gu is not None else act, gu)
         ctx.save_for_backward(x, w_gu, w_down, act, gu)
         return y
 

@@ -217,7 +217,10 @@ class FSDPEngine:
             self.table_grad, self.table_off = self.peer.alloc(self.embed.padded, torch.float32)
         elif self.world == 1:  # each unit's backward writes its own gradient (unit.g) in place
             self.grads = ()
-            self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
+            # untied: the embedding gradient is written per token id straight into embed.g (sorted
+            # ids, fp32 sums per id), so no fp32 [V, D] table is needed (5 GB at the 27B shape)
+            self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device) \
+                if self.tied else None
         else:
             self.grads = (torch.empty(gmax, dtype=self.dtype, device=self.device),)
             self.table_grad = torch.zeros(self.embed.padded, dtype=torch.float32, device=self.device)
@@ -418,7 +421,7 @@ class FSDPEngine:
                 unit.reduce_scatter_from(flat_grad)
                 ops.sumsq_(unit.g, self.sq)
             return
-        if flat_grad.data_ptr() == self.table_grad.data_ptr():
+        if self.table_grad is not None and flat_grad.data_ptr() == self.table_grad.data_ptr():
             j, off, f32 = None, self.table_off, True
         else:
             j = next(k for k, g in enumerate(self.grads) if g.data_ptr() == flat_grad.data_ptr())
@@ -491,7 +494,8 @@ class FSDPEngine:
         self.phase = "fwd"
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
-        self.table_grad.zero_()
+        if self.table_grad is not None:
+            self.table_grad.zero_()
         self.sq.zero_()
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
         loss.backward()
@@ -503,7 +507,7 @@ class FSDPEngine:
     def gemm_bytes_per_layer(self, rows: int) -> list:
         """Bytes the saved GEMM outputs of each layer take for one step of `rows` token rows."""
         c = self.cfg
-        mlp = c.hidden_size + 3 * c.intermediate_size  # down output, activation, gate|up
+        mlp = c.hidden_size + 2 * c.intermediate_size  # down output, gate|up (the activation is rebuilt)
         out = []
         for t in c.layer_types[: len(self.layers)]:
             if t == "linear_attention":
@@ -630,6 +634,22 @@ class _EmbedFn(torch.autograd.Function):
         (ids,) = ctx.saved_tensors
         engine = ctx.engine
         V, D = engine.cfg.vocab_size, engine.cfg.hidden_size
+        if engine.table_grad is None:  # one rank, untied: per-id sums straight into embed.g
+            g = engine.embed.g
+            g.zero_()
+            gt = g[: V * D].view(V, D)
+            flat_ids = ids.reshape(-1)
+            if gt.is_cuda:
+                from ..ops import _native
+
+                sid, perm = torch.sort(flat_ids)
+                _native.require().embed_bwd_sorted(gt, sid, perm, dh.reshape(-1, D))
+            else:
+                acc = torch.zeros(V, D, dtype=torch.float32)
+                acc.index_add_(0, flat_ids, dh.reshape(-1, D).float())
+                gt.copy_(acc)
+            engine.reduce_scatter(engine.embed, g)
+            return None, None, None
         tg = engine.table_grad[: V * D].view(V, D)  # already holds the tied head's gradient, if any
         if tg.is_cuda:
             from ..ops import _native

@@ -37,7 +37,7 @@ def engine_census(engine) -> str:
         return sum(t.numel() * t.element_size() for t in ts) / 2**30
 
     shards = [t for u in engine.units for t in (u.p, u.master, u.m, u.v, u.g)]
-    bufs = list(engine.bufs) + list(engine.grads) + [engine.table_grad]
+    bufs = list(engine.bufs) + list(engine.grads) + ([engine.table_grad] if engine.table_grad is not None else [])
     owners = [o.name if o is not None else "-" for o in engine.owner]
     return (f"MEMCENSUS\tshards_gib={gib(shards):.2f}\tbuffers_gib={gib(bufs):.2f}\t"
             f"gathered_slots={owners}")

@@ -173,6 +173,38 @@ def test_embedding_fwd_bwd_against_torch():
     assert torch.allclose(table.grad.float(), want, rtol=1e-2, atol=1e-2)
 
 
+def test_embedding_sorted_gradient_into_bf16():
+    """Per-id sums of the sorted rows written as bf16 rows (the one-rank engine's embedding
+    gradient), against fp32 index_add; ids absent from the batch keep the zeros."""
+    from dllm_qwen38_b200 import _C
+
+    torch.manual_seed(1)
+    V, D = 1000, 5120
+    ids = torch.randint(0, V, (2 * 700,), device="cuda")
+    ids[:100] = 3  # one long run
+    dh = torch.randn(ids.numel(), D, device="cuda").bfloat16()
+    g = torch.zeros(V, D, device="cuda", dtype=torch.bfloat16)
+    sid, perm = torch.sort(ids)
+    _C.embed_bwd_sorted(g, sid, perm, dh)
+    want = torch.zeros(V, D, device="cuda").index_add_(0, ids, dh.float())
+    assert _rel(g, want) < 5e-3
+    absent = torch.ones(V, dtype=torch.bool, device="cuda")
+    absent[ids] = False
+    assert bool((g[absent] == 0).all())
+
+
+def test_swiglu_act_matches_the_gemm_epilogue():
+    """The activation rebuilt from the stored bf16 gate|up equals the one the SwiGLU GEMM wrote."""
+    from dllm_qwen38_b200 import _C
+    from dllm_qwen38_b200.ops import cuda as Cu
+
+    torch.manual_seed(2)
+    x = torch.randn(4096, 1024, device="cuda").bfloat16()
+    w = (torch.randn(2 * 3584, 1024, device="cuda") * 0.03).bfloat16()
+    act, gu = Cu.gemm_swiglu(x, w, 3584, store_gu=True)
+    assert torch.equal(_C.swiglu_act(gu), act)
+
+
 @pytest.mark.parametrize("xdt,ddt", [(torch.float32, None), (torch.bfloat16, None), (torch.bfloat16, torch.float32),
                                      (torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32)])
 @pytest.mark.parametrize("n", [8, 1000003, 4096 * 33])

@@ -279,13 +279,13 @@ class _SwiGLUMLP(torch.autograd.Function):
                 act = _C.swiglu_act(gu)
                 _count()
         else:
-            # the saving forward (no grad) keeps gate|up for the backward it will serve, and not the
-            # activation, which one element-wise pass rebuilds from it (a third less memory)
+            # the saving forward (no grad) keeps gate|up for the backward it will serve, and, when
+            # memory is short, not the activation, which one element-wise pass rebuilds from it
             need = any(ctx.needs_input_grad) or (ActStore.gemms and ActStore.mode == "save")
             act, gu = gemm_swiglu(x, w_gu, F, store_gu=need)
             y = gemm_nt(act, w_down).reshape(*x.shape[:-1], w_down.shape[0])
             if ActStore.gemms:
-                ActStore.put(y, None if gu is not None else act, gu)
+                ActStore.put(y, act if (ActStore.keep_act or gu is None) else None, gu)
         ctx.save_for_backward(x, w_gu, w_down, act, gu)
         return y
 
@@ -385,6 +385,7 @@ class ActStore:
 
     mode = None
     gemms = False
+    keep_act = False  # the MLP keeps its activation too (else the backward rebuilds it from gate|up)
     key = None
     data: dict = {}
     pos = 0

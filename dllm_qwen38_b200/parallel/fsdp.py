@@ -214,7 +214,10 @@ class FSDPEngine:
         if self.peer is not None:  # two alternating gradient buffers: one is reduce-scattered while
             # the next layer's backward fills the other
             self.grads, self.grad_offs = zip(*[self.peer.alloc(gmax, self.dtype) for _ in range(2)])
-            self.table_grad, self.table_off = self.peer.alloc(self.embed.padded, torch.float32)
+            # untied: the table gradient in the model dtype, written as sorted per-id sums (fp32 within
+            # a rank, fp32 across ranks in the reduce-scatter), like every other unit's gradient
+            self.table_grad, self.table_off = self.peer.alloc(self.embed.padded,
+                                                              torch.float32 if self.tied else self.dtype)
         elif self.world == 1:  # each unit's backward writes its own gradient (unit.g) in place
             self.grads = ()
             # untied: the embedding gradient is written per token id straight into embed.g (sorted
@@ -251,6 +254,7 @@ class FSDPEngine:
         # first n layers, or "auto": as many layers as fit in free memory, decided at the first step
         # from the row count
         self.save_gemms = os.environ.get("BDLLM_SAVE_GEMMS", "auto") if self.save_cores else "0"
+        self.keep_act = False  # whether the kept MLP outputs include the activation (decided with them)
         # which pass is gathering: in the backward, a layer whose GEMM outputs were kept reruns none
         # of its GEMMs, so its gather cannot ride on one and takes the prefetched peer gather instead
         self.phase = "fwd"
@@ -273,7 +277,7 @@ class FSDPEngine:
         shards = [shard(m) for m in modules]
         total = sum(a(s * esz) for s in shards)
         total += 2 * a(max(shards[1:]) * w * esz)
-        total += a(shards[0] * w * 4)
+        total += a(shards[0] * w * (4 if self.tied else esz))  # the embedding-table gradient
         return total + 4096
 
     # ------------------------------------------------------------------ gathers
@@ -422,7 +426,7 @@ class FSDPEngine:
                 ops.sumsq_(unit.g, self.sq)
             return
         if self.table_grad is not None and flat_grad.data_ptr() == self.table_grad.data_ptr():
-            j, off, f32 = None, self.table_off, True
+            j, off, f32 = None, self.table_off, self.table_grad.dtype == torch.float32
         else:
             j = next(k for k, g in enumerate(self.grads) if g.data_ptr() == flat_grad.data_ptr())
             off, f32 = self.grad_offs[j], False
@@ -494,7 +498,7 @@ class FSDPEngine:
         self.phase = "fwd"
         h = self.forward_hidden(x0_2, xt_2, block)
         L = x0.shape[1]
-        if self.table_grad is not None:
+        if self.table_grad is not None and self.table_grad.dtype == torch.float32:  # (others: zeroed in backward)
             self.table_grad.zero_()
         self.sq.zero_()
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
@@ -504,10 +508,11 @@ class FSDPEngine:
             self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
         return loss.detach()
 
-    def gemm_bytes_per_layer(self, rows: int) -> list:
-        """Bytes the saved GEMM outputs of each layer take for one step of `rows` token rows."""
+    def gemm_bytes_per_layer(self, rows: int, with_act: bool = False) -> list:
+        """Bytes the saved GEMM outputs of each layer take for one step of `rows` token rows (the MLP
+        activation included only with `with_act`; without it the backward rebuilds it)."""
         c = self.cfg
-        mlp = c.hidden_size + 2 * c.intermediate_size  # down output, gate|up (the activation is rebuilt)
+        mlp = c.hidden_size + (3 if with_act else 2) * c.intermediate_size  # down output, gate|up[, act]
         out = []
         for t in c.layer_types[: len(self.layers)]:
             if t == "linear_attention":
@@ -538,6 +543,12 @@ class FSDPEngine:
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
         budget = 0.85 * (float(free[0]) - (2 << 30))
+        # when every layer fits with its SwiGLU activation too, keep it (no rebuild in the backward);
+        # otherwise keep gate|up only, so that more layers skip their GEMM recomputation
+        per_act = self.gemm_bytes_per_layer(rows, with_act=True)
+        self.keep_act = sum(per_act) < budget
+        if self.keep_act:
+            per = per_act
         n, used = 0, 0
         while n < len(per) and used + per[n] < budget:
             used += per[n]
@@ -634,8 +645,10 @@ class _EmbedFn(torch.autograd.Function):
         (ids,) = ctx.saved_tensors
         engine = ctx.engine
         V, D = engine.cfg.vocab_size, engine.cfg.hidden_size
-        if engine.table_grad is None:  # one rank, untied: per-id sums straight into embed.g
-            g = engine.embed.g
+        if engine.table_grad is None or engine.table_grad.dtype != torch.float32:
+            # untied: per-id sums straight into the model-dtype gradient (one rank: embed.g; several
+            # ranks on peer memory: the table that the reduce-scatter reads)
+            g = engine.embed.g if engine.table_grad is None else engine.table_grad
             g.zero_()
             gt = g[: V * D].view(V, D)
             flat_ids = ids.reshape(-1)
@@ -687,6 +700,7 @@ class _LayerFn(torch.autograd.Function):
         try:
             if save:
                 engine.act_store.gemms = engine.gemm_saved(i)
+                engine.act_store.keep_act = engine.keep_act
                 engine.act_store.begin("save", i)
             with nvtx(f"layer{i}.fwd"), torch.no_grad(), torch.nn.utils.stateless._reparametrize_module(layer, params):
                 out = layer_step(layer, engine.cfg.layer_types[i], h, L, block, engine.cfg.gdn_chunk_size, cos, sin,
@@ -717,6 +731,7 @@ class _LayerFn(torch.autograd.Function):
         try:
             if reuse:  # the recomputation takes the saved core outputs instead of rerunning them
                 engine.act_store.gemms = engine.gemm_saved(i)
+                engine.act_store.keep_act = engine.keep_act
                 engine.act_store.begin("reuse", i)
             with nvtx(f"layer{i}.bwd"), torch.enable_grad(), \
                     torch.nn.utils.stateless._reparametrize_module(layer, params):

@@ -181,10 +181,12 @@ def run_native(a, rank, world):
         eng = trainer.engine
         kept = ["GDN core outputs and block states", "attention outputs and LSE"] if eng.save_cores else []
         sg = getattr(eng, "save_gemms", "0")
+        mlp = "MLP gate|up and activation" if getattr(eng, "keep_act", False) else \
+            "MLP gate|up (activation rebuilt in the backward)"
         if sg == "1":
-            kept.append("projection and MLP GEMM outputs")
+            kept.append(f"projection GEMM outputs and {mlp}")
         elif sg.isdigit() and sg != "0":
-            kept.append(f"projection and MLP GEMM outputs of the first {sg} of {len(eng.layers)} layers")
+            kept.append(f"projection GEMM outputs and {mlp} of the first {sg} of {len(eng.layers)} layers")
         if kept:
             ckpt_policy = "per layer; the forward keeps " + ", ".join(kept) + " for the backward"
         eng.close()

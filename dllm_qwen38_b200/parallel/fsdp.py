@@ -84,6 +84,20 @@ def _world():
     return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
 
 
+def choose_saved_layers(per: list, per_act: list, free: float):
+    """How many leading layers keep their GEMM outputs: the budget is 85 % of `free` bytes less
+    2 GiB. When every layer fits with its MLP activation too (`per_act` bytes each), keep it;
+    otherwise count with `per` (gate|up only). Returns (layers, bytes used, keep_act)."""
+    budget = 0.85 * (free - (2 << 30))
+    keep_act = sum(per_act) < budget
+    sizes = per_act if keep_act else per
+    n, used = 0, 0
+    while n < len(sizes) and used + sizes[n] < budget:
+        used += sizes[n]
+        n += 1
+    return n, used, keep_act
+
+
 class Unit:
     """A flat, sharded group of parameters of one module."""
 
@@ -542,21 +556,15 @@ class FSDPEngine:
         free = torch.tensor([float(torch.cuda.mem_get_info(self.device)[0])], device=self.device)
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
-        budget = 0.85 * (float(free[0]) - (2 << 30))
-        # when every layer fits with its SwiGLU activation too, keep it (no rebuild in the backward);
-        # otherwise keep gate|up only, so that more layers skip their GEMM recomputation
-        per_act = self.gemm_bytes_per_layer(rows, with_act=True)
-        self.keep_act = sum(per_act) < budget
+        n, used, self.keep_act = choose_saved_layers(per, self.gemm_bytes_per_layer(rows, with_act=True),
+                                                     float(free[0]))
         if self.keep_act:
-            per = per_act
-        n, used = 0, 0
-        while n < len(per) and used + per[n] < budget:
-            used += per[n]
-            n += 1
+            per = self.gemm_bytes_per_layer(rows, with_act=True)
         self.save_gemms = "1" if n == len(per) else str(n)
         if self.rank == 0:
             print(f"[fsdp] GEMM outputs across checkpointing: kept for {n} of {len(per)} layers "
-                  f"({used / 2**30:.1f} of {sum(per) / 2**30:.1f} GiB; free {float(free[0]) / 2**30:.1f} GiB)",
+                  f"({used / 2**30:.1f} of {sum(per) / 2**30:.1f} GiB; free {float(free[0]) / 2**30:.1f} GiB; "
+                  f"MLP activation {'kept' if self.keep_act else 'rebuilt from gate|up'})",
                   file=sys.stderr, flush=True)
 
     @torch.no_grad()

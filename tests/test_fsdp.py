@@ -104,6 +104,20 @@ def test_partial_gemm_saving_policy():
         assert [e.gemm_saved(i) for i in range(4)] == want, s
 
 
+def test_saved_layer_choice_keeps_the_activation_only_when_everything_fits():
+    from dllm_qwen38_b200.parallel.fsdp import choose_saved_layers
+
+    gib = 1 << 30
+    per, per_act = [2 * gib] * 4, [3 * gib] * 4
+    # 0.85 * (20 - 2) = 15.3 GiB: all four with the activation (12 GiB)
+    assert choose_saved_layers(per, per_act, 20 * gib) == (4, 12 * gib, True)
+    # 0.85 * (14 - 2) = 10.2 GiB: not all with it (12), so gate|up only: five would fit, four exist
+    assert choose_saved_layers(per, per_act, 14 * gib) == (4, 8 * gib, False)
+    # 0.85 * (8 - 2) = 5.1 GiB: two layers of gate|up
+    assert choose_saved_layers(per, per_act, 8 * gib) == (2, 4 * gib, False)
+    assert choose_saved_layers(per, per_act, gib)[0] == 0
+
+
 def _zero_target_worker(rank, world, port, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)

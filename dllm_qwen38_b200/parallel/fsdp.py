@@ -85,10 +85,10 @@ def _world():
 
 
 def choose_saved_layers(per: list, per_act: list, free: float):
-    """How many leading layers keep their GEMM outputs: the budget is 85 % of `free` bytes less
-    2 GiB. When every layer fits with its MLP activation too (`per_act` bytes each), keep it;
+    """How many leading layers keep their GEMM outputs: the budget is 92 % of `free` bytes less
+    3 GiB. When every layer fits with its MLP activation too (`per_act` bytes each), keep it;
     otherwise count with `per` (gate|up only). Returns (layers, bytes used, keep_act)."""
-    budget = 0.85 * (free - (2 << 30))
+    budget = 0.92 * (free - (3 << 30))
     keep_act = sum(per_act) < budget
     sizes = per_act if keep_act else per
     n, used = 0, 0
@@ -547,8 +547,8 @@ class FSDPEngine:
 
     def _decide_save_gemms(self, rows: int) -> None:
         """After a step that kept no GEMM outputs: keep those of as many layers (from the first,
-        whose outputs live longest) as fit in 85 % of the device memory that the step's peak left
-        unreserved, less 2 GiB. The caching allocator keeps its peak reservation, so what the saved
+        whose outputs live longest) as fit in 92 % of the device memory that the step's peak left
+        unreserved, less 3 GiB. The caching allocator keeps its peak reservation, so what the saved
         outputs add has to come from memory that is still free now. Every rank takes the same
         decision: the smallest headroom over ranks counts."""
         per = self.gemm_bytes_per_layer(rows)

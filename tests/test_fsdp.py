@@ -109,12 +109,12 @@ def test_saved_layer_choice_keeps_the_activation_only_when_everything_fits():
 
     gib = 1 << 30
     per, per_act = [2 * gib] * 4, [3 * gib] * 4
-    # 0.85 * (20 - 2) = 15.3 GiB: all four with the activation (12 GiB)
+    # 0.92 * (20 - 3) = 15.6 GiB: all four with the activation (12 GiB)
     assert choose_saved_layers(per, per_act, 20 * gib) == (4, 12 * gib, True)
-    # 0.85 * (14 - 2) = 10.2 GiB: not all with it (12), so gate|up only: five would fit, four exist
+    # 0.92 * (14 - 3) = 10.1 GiB: not all with it (12), so gate|up only: all four (8 GiB)
     assert choose_saved_layers(per, per_act, 14 * gib) == (4, 8 * gib, False)
-    # 0.85 * (8 - 2) = 5.1 GiB: two layers of gate|up
-    assert choose_saved_layers(per, per_act, 8 * gib) == (2, 4 * gib, False)
+    # 0.92 * (9 - 3) = 5.5 GiB: two layers of gate|up
+    assert choose_saved_layers(per, per_act, 9 * gib) == (2, 4 * gib, False)
     assert choose_saved_layers(per, per_act, gib)[0] == 0
 
 

@@ -498,9 +498,33 @@ class FSDPEngine:
         """One optimizer step on this rank's rows (already on the device). n_local: this rank's
         scored-target count (host int); n_global: the global count (python number or 0-d device
         tensor). Returns this rank's loss contribution (device tensor); summed over ranks it is the
-        global mean CE."""
+        global mean CE.
+
+        On one rank, when the number of layers keeping GEMM outputs was chosen from the probe step
+        and the step then runs out of memory before its update, the step is run again with two
+        layers fewer (the masks come from the step's seed, so it is the same step)."""
+        kw = dict(block=block, mask_id=mask_id, n_local=n_local, n_global=n_global, gstep=gstep)
+        try:
+            return self._step(x0, prompt_len, valid_len, **kw)
+        except torch.cuda.OutOfMemoryError:
+            if self.world > 1 or not self.save_gemms.isdigit() or not getattr(self, "_auto_saved", False) \
+                    or self._updated:
+                raise
+            n = len(self.layers) if self.save_gemms == "1" else int(self.save_gemms)
+            if n == 0:
+                raise
+            self.save_gemms = str(max(0, n - 2))
+            self.act_store.clear()
+            self.step_count -= 1
+            torch.cuda.empty_cache()
+            print(f"[fsdp] out of memory with GEMM outputs kept for {n} layers; retrying with "
+                  f"{self.save_gemms}", file=sys.stderr, flush=True)
+            return self._step(x0, prompt_len, valid_len, **kw)
+
+    def _step(self, x0, prompt_len, valid_len, *, block: int, mask_id: int, n_local: int, n_global, gstep: int):
         from ..train.objective import complementary_step_inputs
 
+        self._updated = False
         self.step_count += 1
         gen = torch.Generator(device=self.device).manual_seed(gstep * 1000 + self.rank)
         x0_2, xt_2, m_2 = complementary_step_inputs(x0, prompt_len, block, mask_id, gen, valid_len,
@@ -517,9 +541,11 @@ class FSDPEngine:
         self.sq.zero_()
         loss = _HeadFn.apply(h[:, :L], m_2, x0_2, self.anchor, self, n_global, n_local)
         loss.backward()
+        self._updated = True  # from here on the step has changed the weights: no retry
         self._optimizer_step()
         if probe:
             self._decide_save_gemms(x0_2.shape[0] * 2 * x0_2.shape[1])
+            self._auto_saved = True
         return loss.detach()
 
     def gemm_bytes_per_layer(self, rows: int, with_act: bool = False) -> list:

@@ -118,6 +118,54 @@ def test_saved_layer_choice_keeps_the_activation_only_when_everything_fits():
     assert choose_saved_layers(per, per_act, gib)[0] == 0
 
 
+def test_one_rank_out_of_memory_retries_with_fewer_kept_layers():
+    """An out-of-memory error before the update, after the probe chose the kept layers, reruns
+    the step with two layers fewer; a second failure, or one after the update, propagates."""
+    from dllm_qwen38_b200.parallel.fsdp import FSDPEngine
+
+    class Store:
+        cleared = 0
+
+        @classmethod
+        def clear(cls):
+            cls.cleared += 1
+
+    e = object.__new__(FSDPEngine)
+    e.world, e.layers, e.save_gemms, e._auto_saved, e.step_count = 1, [0] * 6, "5", True, 3
+    e.act_store = Store
+    calls = []
+
+    def failing_once(*a, **k):
+        calls.append(e.save_gemms)
+        e._updated = False
+        e.step_count += 1
+        if len(calls) == 1:
+            raise torch.cuda.OutOfMemoryError("test")
+        return "loss"
+
+    e._step = failing_once
+    kw = dict(block=8, mask_id=0, n_local=1, n_global=1, gstep=1)
+    assert e.step(None, None, None, **kw) == "loss"
+    assert calls == ["5", "3"] and e.save_gemms == "3" and e.step_count == 4 and Store.cleared == 1
+
+    def always_failing(*a, **k):
+        e._updated = False
+        raise torch.cuda.OutOfMemoryError("test")
+
+    e._step = always_failing
+    with pytest.raises(torch.cuda.OutOfMemoryError):
+        e.step(None, None, None, **kw)
+
+    def failing_after_update(*a, **k):
+        e._updated = True
+        raise torch.cuda.OutOfMemoryError("test")
+
+    e._step, e.save_gemms = failing_after_update, "5"
+    with pytest.raises(torch.cuda.OutOfMemoryError):
+        e.step(None, None, None, **kw)
+    assert e.save_gemms == "5"
+
+
 def _zero_target_worker(rank, world, port, out):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)

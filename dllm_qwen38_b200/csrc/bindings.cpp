@@ -80,6 +80,8 @@ at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& table);
 void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh);
 void embed_bwd_sorted(at::Tensor& grad, const at::Tensor& sid, const at::Tensor& perm, const at::Tensor& dh);
 at::Tensor swiglu_act(const at::Tensor& gu);
+at::Tensor out_gate_fwd(const at::Tensor& o, const at::Tensor& g);
+std::vector<at::Tensor> out_gate_bwd(const at::Tensor& dy, const at::Tensor& o, const at::Tensor& g);
 std::vector<at::Tensor> gdn_gates_fwd(const at::Tensor& a, const at::Tensor& b, const at::Tensor& A_log,
                                       const at::Tensor& dt_bias);
 std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& dbeta, const at::Tensor& a,
@@ -168,6 +170,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_bwd_sorted", &bdllm::embed_bwd_sorted,
         "embedding gradient as per-id sums of the sorted rows, written as bf16 rows (others untouched)");
   m.def("swiglu_act", &bdllm::swiglu_act, "act = silu(gate) * up from the stored bf16 (gate | up)");
+  m.def("out_gate_fwd", &bdllm::out_gate_fwd, "attention output gate y = o * sigmoid(gate)");
+  m.def("out_gate_bwd", &bdllm::out_gate_bwd, "output gate backward: (d o, d gate)");
   m.def("gdn_gates_fwd", &bdllm::gdn_gates_fwd, "beta = sigmoid(b), g = -exp(A_log) softplus(a + dt_bias)");
   m.def("gdn_gates_bwd", &bdllm::gdn_gates_bwd);
   m.def("gemm_splitk", &bdllm::gemm_splitk, "split-K tcgen05 GEMM for skinny problems (+ residual)",

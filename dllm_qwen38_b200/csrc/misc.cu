@@ -9,6 +9,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include <utility>
+
 #include "common.cuh"
 
 namespace bdllm {
@@ -104,6 +106,104 @@ at::Tensor swiglu_act(const at::Tensor& gu) {
   swiglu_act_kernel<<<grid, 256, 0, stream()>>>(cbf(gu), bfp(out), rows, F);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
+}
+
+// Attention output gate: y = o * sigmoid(g) over rows of D (o and y contiguous, g with row stride
+// ldg: the gate half of the q|gate projection read in place); backward do = dy s,
+// dg = dy o s (1 - s), s recomputed. 8 elements per thread.
+__global__ void out_gate_fwd_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g,
+                                    int64_t ldg, __nv_bfloat16* __restrict__ y, int64_t rows, int D) {
+  const int64_t n = rows * (int64_t)(D / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (D / 8);
+    const int c = (int)(i % (D / 8)) * 8;
+    const uint4 ov = *reinterpret_cast<const uint4*>(o + r * D + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(g + r * ldg + c);
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+    uint4 out;
+    __nv_bfloat162* y2 = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 of = __bfloat1622float2(o2[e]), gf = __bfloat1622float2(g2[e]);
+      y2[e] = __floats2bfloat162_rn(of.x * sigmoid_f(gf.x), of.y * sigmoid_f(gf.y));
+    }
+    *reinterpret_cast<uint4*>(y + r * D + c) = out;
+  }
+}
+
+__global__ void out_gate_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ o,
+                                    const __nv_bfloat16* __restrict__ g, int64_t ldg, __nv_bfloat16* __restrict__ dout,
+                                    __nv_bfloat16* __restrict__ dg, int64_t rows, int D) {
+  const int64_t n = rows * (int64_t)(D / 8);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / (D / 8);
+    const int c = (int)(i % (D / 8)) * 8;
+    const uint4 dv = *reinterpret_cast<const uint4*>(dy + r * D + c);
+    const uint4 ov = *reinterpret_cast<const uint4*>(o + r * D + c);
+    const uint4 gv = *reinterpret_cast<const uint4*>(g + r * ldg + c);
+    const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+    const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+    uint4 a, b;
+    __nv_bfloat162* a2 = reinterpret_cast<__nv_bfloat162*>(&a);
+    __nv_bfloat162* b2 = reinterpret_cast<__nv_bfloat162*>(&b);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 df = __bfloat1622float2(d2[e]), of = __bfloat1622float2(o2[e]), gf = __bfloat1622float2(g2[e]);
+      const float sx = sigmoid_f(gf.x), sy = sigmoid_f(gf.y);
+      a2[e] = __floats2bfloat162_rn(df.x * sx, df.y * sy);
+      b2[e] = __floats2bfloat162_rn(df.x * of.x * sx * (1.f - sx), df.y * of.y * sy * (1.f - sy));
+    }
+    *reinterpret_cast<uint4*>(dout + r * D + c) = a;
+    *reinterpret_cast<uint4*>(dg + r * D + c) = b;
+  }
+}
+
+// the gate as rows of D with one row stride (its leading dims must merge), or a contiguous copy
+static std::pair<at::Tensor, int64_t> gate_rows(const at::Tensor& g, int D) {
+  if (g.stride(-1) == 1 && g.dim() >= 2) {
+    bool ok = true;
+    for (int d = g.dim() - 3; d >= 0; --d)
+      if (g.size(d) > 1 && g.stride(d) != g.stride(d + 1) * g.size(d + 1)) ok = false;
+    const int64_t ld = g.stride(-2);
+    if (ok && ld % 8 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0) return {g, ld};
+  }
+  return {g.contiguous(), (int64_t)D};
+}
+
+at::Tensor out_gate_fwd(const at::Tensor& o, const at::Tensor& g) {
+  const int D = o.size(-1);
+  TORCH_CHECK(o.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16 && g.sizes() == o.sizes() &&
+                  D % 8 == 0,
+              "out_gate: bf16 o and gate of one shape, last dim % 8 == 0");
+  auto oc = o.contiguous();
+  auto [gr, ldg] = gate_rows(g, D);
+  auto y = at::empty_like(oc);
+  const int64_t rows = oc.numel() / D;
+  if (rows == 0) return y;
+  c10::cuda::CUDAGuard gd(o.device());
+  const int64_t n = rows * (D / 8);
+  out_gate_fwd_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, stream()>>>(
+      cbf(oc), cbf(gr), ldg, bfp(y), rows, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return y;
+}
+
+std::vector<at::Tensor> out_gate_bwd(const at::Tensor& dy, const at::Tensor& o, const at::Tensor& g) {
+  const int D = o.size(-1);
+  auto d = dy.to(at::kBFloat16).contiguous();
+  auto oc = o.contiguous();
+  auto [gr, ldg] = gate_rows(g, D);
+  auto dout = at::empty_like(oc), dg = at::empty_like(oc);
+  const int64_t rows = oc.numel() / D;
+  if (rows == 0) return {dout, dg};
+  c10::cuda::CUDAGuard gd(o.device());
+  const int64_t n = rows * (D / 8);
+  out_gate_bwd_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 148 * 16), 256, 0, stream()>>>(
+      cbf(d), cbf(oc), cbf(gr), ldg, bfp(dout), bfp(dg), rows, D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dout, dg};
 }
 
 // ------------------------------------------------------------------------------- conv

@@ -106,13 +106,13 @@ def attn_mixer(m, n: torch.Tensor, L: int, block: int, cos, sin, fault: BreakMod
     proj = ops.linear(n, w_qkv)
     qg, k, v = torch.split(proj, [2 * Hq * Dh, Hk * Dh, Hk * Dh], dim=-1)
     qg = qg.reshape(B, T2, Hq, 2 * Dh)
-    q, gate = qg[..., :Dh], qg[..., Dh:]
+    q, gate = torch.split(qg, Dh, dim=-1)  # one concatenation in backward, no zero-filled slice grads
     k = k.reshape(B, T2, Hk, Dh)
     v = v.reshape(B, T2, Hk, Dh)
     cos2, sin2 = torch.cat([cos, cos], 0), torch.cat([sin, sin], 0)
     q, k = ops.qk_norm_rope(q, k, m.q_norm.weight, m.k_norm.weight, m.q_norm.eps, cos2, sin2)
     o = ops.attention_blockdiff(q, k, v, L, block, Dh ** -0.5, fault.leak_xt_prefix)
-    o = o * torch.sigmoid(gate)
+    o = ops.output_gate(o, gate)
     return ops.linear(o.reshape(B, T2, Hq * Dh), m.o_proj.weight)
 
 

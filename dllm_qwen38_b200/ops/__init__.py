@@ -56,7 +56,7 @@ _LEVERS: set = set()
 # every op family with a native kernel (the native kernels compute in bf16; fp32 runs on a CUDA
 # device go through torch_on_cuda(*ALL_OPS))
 ALL_OPS = ("rmsnorm", "linear", "mlp", "gated_rmsnorm", "conv", "gdn_gates", "gdn_core", "attention",
-           "qk_norm_rope", "masked_ce", "embedding")
+           "qk_norm_rope", "output_gate", "masked_ce", "embedding")
 
 
 class torch_on_cuda:
@@ -221,6 +221,15 @@ def qk_norm_rope(q, k, wq, wk, eps: float, cos, sin):
         return _nat().qk_norm_rope(q, k, wq, wk, eps, cos, sin)
     _record_ref("qk_norm_rope")
     return ref.apply_rope(ref.rmsnorm(q, wq, eps), cos, sin), ref.apply_rope(ref.rmsnorm(k, wk, eps), cos, sin)
+
+
+def output_gate(o, gate):
+    """The attention output gate o * sigmoid(gate) (HF `Qwen3_5Attention`'s gated output)."""
+    if use_native(o, op="output_gate"):
+        _record("output_gate", "native")
+        return _nat().output_gate(o, gate)
+    _record_ref("output_gate")
+    return o * torch.sigmoid(gate)
 
 
 # ----------------------------------------------------------------------------- loss

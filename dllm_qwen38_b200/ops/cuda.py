@@ -237,6 +237,28 @@ def gated_rmsnorm(x, z, w, eps):
     return _GatedRMSNorm.apply(x, z, w, eps)
 
 
+class _OutputGate(torch.autograd.Function):
+    """o * sigmoid(gate), the gate read in place from the q|gate projection (one kernel each way,
+    sigmoid recomputed in the backward)."""
+
+    @staticmethod
+    def forward(ctx, o, gate):
+        ctx.save_for_backward(o, gate)
+        _count()
+        return _C.out_gate_fwd(o, gate)
+
+    @staticmethod
+    def backward(ctx, dy):
+        o, gate = ctx.saved_tensors
+        do, dg = _C.out_gate_bwd(dy, o, gate)
+        _count()
+        return do.view(o.shape), dg.view(gate.shape)
+
+
+def output_gate(o, gate):
+    return _OutputGate.apply(o, gate)
+
+
 class _QKNormRope(torch.autograd.Function):
     """q/k [B, T2, H, Dh] strided views (q is a slice of the q|gate projection)."""
 

@@ -22,7 +22,7 @@ from dllm_qwen38_b200.models.qwen35 import build_model
 pytestmark = pytest.mark.gpu
 
 NATIVE_OPS = ("rmsnorm", "linear", "mlp", "gated_rmsnorm", "conv", "gdn_gates", "gdn_core", "attention",
-              "qk_norm_rope", "embedding")
+              "qk_norm_rope", "output_gate", "embedding")
 
 
 def _gate(cfg, block, nblocks, batch=1, seed=0):

@@ -193,6 +193,28 @@ def test_embedding_sorted_gradient_into_bf16():
     assert bool((g[absent] == 0).all())
 
 
+def test_output_gate_fwd_bwd_with_the_gate_read_in_place():
+    """o * sigmoid(gate) with the gate a strided half of a q|gate projection, forward and
+    backward against fp32 autograd."""
+    from dllm_qwen38_b200 import ops
+
+    torch.manual_seed(3)
+    B, T, H, D = 2, 96, 6, 256
+    qg = torch.randn(B, T, H, 2 * D, device="cuda").bfloat16().requires_grad_(True)
+    _, gate = torch.split(qg, D, dim=-1)
+    o = torch.randn(B, T, H, D, device="cuda").bfloat16().requires_grad_(True)
+    y = ops.output_gate(o, gate)
+    assert ops.last_impl("output_gate") == "native"
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    of, qf = o.detach().float().requires_grad_(True), qg.detach().float().requires_grad_(True)
+    yf = of * torch.sigmoid(qf[..., D:])
+    yf.backward(dy.float())
+    assert _rel(y, yf) < 1e-2
+    assert _rel(o.grad, of.grad) < 1e-2 and _rel(qg.grad, qf.grad) < 1e-2
+    assert float(qg.grad[..., :D].abs().max()) == 0.0  # the q half gets nothing from the gate
+
+
 def test_swiglu_act_matches_the_gemm_epilogue():
     """The activation rebuilt from the stored bf16 gate|up equals the one the SwiGLU GEMM wrote."""
     from dllm_qwen38_b200 import _C

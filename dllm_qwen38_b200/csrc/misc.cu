@@ -875,35 +875,41 @@ void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh) {
 }
 
 // Sorted variant straight into a bf16 gradient (no fp32 [V, D] table): sid = the ids sorted, perm
-// their positions in dh. The warp at the first position of each run of equal ids sums that run's
-// dh rows in fp32, 8 columns per lane at a time, and writes the bf16 row; rows of ids absent from
-// the batch keep the zeros the caller wrote. Deterministic (fixed order within a run).
+// their positions in dh. Grid (positions / 8, column chunks of 256): the warp at the first
+// position of a run of equal ids finds the run's end by binary search and sums the run's dh rows
+// for its 256 columns in fp32 (8 per lane, 8 rows in flight), then writes the bf16 row chunk.
+// A long run (the mask token fills half the noised stream) is spread over the column chunks;
+// rows of ids absent from the batch keep the zeros the caller wrote. Deterministic.
 __global__ void embed_bwd_sorted_kernel(const int64_t* __restrict__ sid, const int64_t* __restrict__ perm,
                                         const __nv_bfloat16* __restrict__ dh, int D, int64_t V,
                                         __nv_bfloat16* __restrict__ grad, int64_t N) {
   const int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (i >= N) return;
+  const int c = blockIdx.y * 256 + (threadIdx.x & 31) * 8;
+  if (i >= N || c >= D) return;
   const int64_t id = sid[i];
   if ((i > 0 && sid[i - 1] == id) || id < 0 || id >= V) return;  // not the start of a run
-  int64_t end = i + 1;
-  while (end < N && sid[end] == id) ++end;
-  for (int c = (threadIdx.x & 31) * 8; c < D; c += 256) {
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int64_t j = i; j < end; ++j) {
-      const uint4 p = *reinterpret_cast<const uint4*>(dh + perm[j] * D + c);
-      const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __bfloat1622float2(p2[e]);
-        acc[2 * e] += f.x, acc[2 * e + 1] += f.y;
-      }
-    }
-    uint4 o;
-    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
-    *reinterpret_cast<uint4*>(grad + id * D + c) = o;
+  int64_t lo = i + 1, hi = N;  // first position past the run
+  while (lo < hi) {
+    const int64_t mid = lo + (hi - lo) / 2;
+    if (sid[mid] == id) lo = mid + 1;
+    else hi = mid;
   }
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+  for (int64_t j = i; j < lo; ++j) {
+    const uint4 p = *reinterpret_cast<const uint4*>(dh + perm[j] * D + c);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&p);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __bfloat1622float2(p2[e]);
+      acc[2 * e] += f.x, acc[2 * e + 1] += f.y;
+    }
+  }
+  uint4 o;
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) o2[e] = __floats2bfloat162_rn(acc[2 * e], acc[2 * e + 1]);
+  *reinterpret_cast<uint4*>(grad + id * D + c) = o;
 }
 
 void embed_bwd_sorted(at::Tensor& grad, const at::Tensor& sid, const at::Tensor& perm, const at::Tensor& dh) {
@@ -918,8 +924,9 @@ void embed_bwd_sorted(at::Tensor& grad, const at::Tensor& sid, const at::Tensor&
   TORCH_CHECK(d.numel() == N * D && D % 8 == 0, "embed_bwd_sorted: dh [N, D]");
   if (N == 0) return;
   c10::cuda::CUDAGuard g(grad.device());
-  embed_bwd_sorted_kernel<<<(int)((N + 7) / 8), 256, 0, stream()>>>(sid.data_ptr<int64_t>(), perm.data_ptr<int64_t>(),
-                                                                    cbf(d), D, V, bfp(grad), N);
+  const dim3 grid((unsigned)((N + 7) / 8), (unsigned)((D + 255) / 256));
+  embed_bwd_sorted_kernel<<<grid, 256, 0, stream()>>>(sid.data_ptr<int64_t>(), perm.data_ptr<int64_t>(), cbf(d), D, V,
+                                                      bfp(grad), N);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -180,8 +180,8 @@ def test_embedding_sorted_gradient_into_bf16():
 
     torch.manual_seed(1)
     V, D = 1000, 5120
-    ids = torch.randint(0, V, (2 * 700,), device="cuda")
-    ids[:100] = 3  # one long run
+    ids = torch.randint(0, V, (2 * 7000,), device="cuda")
+    ids[:6000] = 3  # one long run, as the mask token makes in the noised stream
     dh = torch.randn(ids.numel(), D, device="cuda").bfloat16()
     g = torch.zeros(V, D, device="cuda", dtype=torch.bfloat16)
     sid, perm = torch.sort(ids)

@@ -20,6 +20,14 @@ static inline const __nv_bfloat16* cbf(const at::Tensor& t) {
   return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
 }
 static inline __nv_bfloat16* bfp(at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+// the kernels below move bf16 / fp32 data in 16-byte vectors: base addresses must be 16-byte aligned
+static inline bool al16(const at::Tensor& t) { return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0; }
+// a contiguous input whose base is 16-byte aligned: the tensor itself, or a copy when a view's
+// offset breaks the alignment
+static inline at::Tensor vec_input(const at::Tensor& t) {
+  auto c = t.contiguous();
+  return al16(c) ? c : c.clone();
+}
 
 // ------------------------------------------------------------------------------- dswiglu
 // act = silu(g) * u; dg = dact * u * silu'(g), du = dact * silu(g). gu rows [g (F) | u (F)].
@@ -54,10 +62,11 @@ __global__ void dswiglu_kernel(const __nv_bfloat16* __restrict__ dact, const __n
 
 at::Tensor dswiglu(const at::Tensor& dact, const at::Tensor& gu) {
   const int F = dact.size(-1);
-  TORCH_CHECK(F % 8 == 0 && gu.size(-1) == 2 * F, "dswiglu: shapes");
-  auto d = dact.to(at::kBFloat16).contiguous();
-  auto g = gu.contiguous();
+  TORCH_CHECK(F % 8 == 0 && gu.size(-1) == 2 * F && gu.scalar_type() == at::kBFloat16, "dswiglu: shapes");
+  auto d = vec_input(dact.to(at::kBFloat16));
+  auto g = vec_input(gu);
   const int64_t rows = d.numel() / F;
+  TORCH_CHECK(g.numel() == rows * 2 * F, "dswiglu: d(act) and (gate | up) rows differ");
   auto out = at::empty({rows, 2 * F}, gu.options());
   if (rows == 0) return out;
   c10::cuda::CUDAGuard guard(gu.device());
@@ -92,9 +101,10 @@ __global__ void swiglu_act_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfl
 }
 
 at::Tensor swiglu_act(const at::Tensor& gu) {
-  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.is_contiguous() && gu.size(-1) % 16 == 0,
-              "swiglu_act: contiguous bf16 [..., 2F], F % 8 == 0");
+  TORCH_CHECK(gu.scalar_type() == at::kBFloat16 && gu.dim() >= 1 && gu.size(-1) % 16 == 0,
+              "swiglu_act: bf16 [..., 2F], F % 8 == 0");
   const int F = gu.size(-1) / 2;
+  auto gc = vec_input(gu);
   auto sizes = gu.sizes().vec();
   sizes.back() = F;
   auto out = at::empty(sizes, gu.options());
@@ -103,7 +113,7 @@ at::Tensor swiglu_act(const at::Tensor& gu) {
   c10::cuda::CUDAGuard g(gu.device());
   const int64_t n = rows * (F / 8);
   const int grid = (int)std::min<int64_t>((n + 255) / 256, 148 * 16);
-  swiglu_act_kernel<<<grid, 256, 0, stream()>>>(cbf(gu), bfp(out), rows, F);
+  swiglu_act_kernel<<<grid, 256, 0, stream()>>>(cbf(gc), bfp(out), rows, F);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -160,16 +170,23 @@ __global__ void out_gate_bwd_kernel(const __nv_bfloat16* __restrict__ dy, const 
   }
 }
 
-// the gate as rows of D with one row stride (its leading dims must merge), or a contiguous copy
+// the gate as rows of D at one row stride ld (row r at g + r * ld over the flattened leading dims,
+// so every leading dim longer than 1 must step by ld times the rows inside it), read in place;
+// otherwise a contiguous copy
 static std::pair<at::Tensor, int64_t> gate_rows(const at::Tensor& g, int D) {
-  if (g.stride(-1) == 1 && g.dim() >= 2) {
+  if (g.dim() >= 2 && g.stride(-1) == 1 && al16(g)) {
+    int64_t ld = -1, inner = 1;  // inner: rows spanned by the dims inside the current one
     bool ok = true;
-    for (int d = g.dim() - 3; d >= 0; --d)
-      if (g.size(d) > 1 && g.stride(d) != g.stride(d + 1) * g.size(d + 1)) ok = false;
-    const int64_t ld = g.stride(-2);
-    if (ok && ld % 8 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0) return {g, ld};
+    for (int d = g.dim() - 2; d >= 0 && ok; --d) {
+      if (g.size(d) == 1) continue;
+      if (ld < 0) ld = g.stride(d);
+      else ok = g.stride(d) == ld * inner;
+      inner *= g.size(d);
+    }
+    if (ld < 0) ld = D;  // a single row
+    if (ok && ld >= D && ld % 8 == 0) return {g, ld};
   }
-  return {g.contiguous(), (int64_t)D};
+  return {vec_input(g), (int64_t)D};
 }
 
 at::Tensor out_gate_fwd(const at::Tensor& o, const at::Tensor& g) {
@@ -177,7 +194,7 @@ at::Tensor out_gate_fwd(const at::Tensor& o, const at::Tensor& g) {
   TORCH_CHECK(o.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16 && g.sizes() == o.sizes() &&
                   D % 8 == 0,
               "out_gate: bf16 o and gate of one shape, last dim % 8 == 0");
-  auto oc = o.contiguous();
+  auto oc = vec_input(o);
   auto [gr, ldg] = gate_rows(g, D);
   auto y = at::empty_like(oc);
   const int64_t rows = oc.numel() / D;
@@ -192,8 +209,11 @@ at::Tensor out_gate_fwd(const at::Tensor& o, const at::Tensor& g) {
 
 std::vector<at::Tensor> out_gate_bwd(const at::Tensor& dy, const at::Tensor& o, const at::Tensor& g) {
   const int D = o.size(-1);
-  auto d = dy.to(at::kBFloat16).contiguous();
-  auto oc = o.contiguous();
+  TORCH_CHECK(o.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kBFloat16 && g.sizes() == o.sizes() &&
+                  dy.numel() == o.numel() && D % 8 == 0,
+              "out_gate: bf16 o and gate of one shape, dy of as many elements, last dim % 8 == 0");
+  auto d = vec_input(dy.to(at::kBFloat16));
+  auto oc = vec_input(o);
   auto [gr, ldg] = gate_rows(g, D);
   auto dout = at::empty_like(oc), dg = at::empty_like(oc);
   const int64_t rows = oc.numel() / D;
@@ -436,30 +456,40 @@ __global__ void sum_parts_kernel(const float* __restrict__ part, int nparts, int
 
 static int grid_for(int64_t n) { return (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32)); }
 
-at::Tensor conv_fwd(const at::Tensor& raw, const at::Tensor& w, int64_t L, int64_t block, int64_t mode) {
-  TORCH_CHECK(raw.dim() == 3 && raw.stride(-1) == 1 && raw.scalar_type() == at::kBFloat16, "conv: raw [B, 2L, C] bf16");
-  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2), K = w.size(1);
-  TORCH_CHECK(T2 == 2 * L && C % 8 == 0 && raw.stride(1) % 8 == 0 && raw.stride(0) == (int64_t)T2 * raw.stride(1),
-              "conv: layout");
-  TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
-  auto wf = w.to(at::kFloat).contiguous();
+// raw [B, 2L, C] read in place at token stride ld when its rows are 16-byte vectors and its batch
+// and token dims merge, else a contiguous copy; w [C, 4] as an aligned fp32 copy
+static std::pair<at::Tensor, int64_t> conv_raw(const at::Tensor& raw, const at::Tensor& w, int64_t L) {
+  TORCH_CHECK(raw.dim() == 3 && raw.scalar_type() == at::kBFloat16, "conv: raw [B, 2L, C] bf16");
+  TORCH_CHECK(raw.size(1) == 2 * L && raw.size(2) % 8 == 0, "conv: raw [B, 2L, C] with C % 8 == 0");
+  TORCH_CHECK(w.dim() == 2 && w.size(0) == raw.size(2) && w.size(1) == 4, "conv: weight [C, 4] (kernel size 4)");
+  if (raw.stride(-1) == 1 && raw.stride(1) % 8 == 0 && raw.stride(1) >= raw.size(2) &&
+      (raw.size(0) == 1 || raw.stride(0) == raw.size(1) * raw.stride(1)) && al16(raw))
+    return {raw, raw.stride(1)};
+  return {vec_input(raw), raw.size(2)};
+}
+
+at::Tensor conv_fwd(const at::Tensor& raw_in, const at::Tensor& w, int64_t L, int64_t block, int64_t mode) {
+  auto [raw, ld] = conv_raw(raw_in, w, L);
+  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2);
+  auto wf = vec_input(w.to(at::kFloat));
   auto y = at::empty({B, T2, C}, raw.options());
   c10::cuda::CUDAGuard g(raw.device());
-  conv_fwd_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(),
+  conv_fwd_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), ld, wf.data_ptr<float>(),
                                                                    bfp(y), B, T2, C, (int)L, (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return y;
 }
 
-std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, const at::Tensor& w, int64_t L,
+std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw_in, const at::Tensor& w, int64_t L,
                                  int64_t block, int64_t mode) {
-  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2), K = w.size(1);
-  TORCH_CHECK(K == 4, "conv: kernel size 4 supported");
-  auto wf = w.to(at::kFloat).contiguous();
-  auto d = dy.to(at::kBFloat16).contiguous();
+  auto [raw, ld] = conv_raw(raw_in, w, L);
+  const int B = raw.size(0), T2 = raw.size(1), C = raw.size(2), K = 4;
+  TORCH_CHECK(dy.numel() == raw.numel(), "conv: dy [B, 2L, C]");
+  auto wf = vec_input(w.to(at::kFloat));
+  auto d = vec_input(dy.to(at::kBFloat16));
   c10::cuda::CUDAGuard g(raw.device());
   auto dpre = at::empty({B, T2, C}, raw.options().dtype(at::kFloat));
-  conv_dpre_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), raw.stride(1), wf.data_ptr<float>(),
+  conv_dpre_kernel<4><<<dim3((C / 8 + 255) / 256, (B * T2 + CONV_ROWS - 1) / CONV_ROWS), 256, 0, stream()>>>(cbf(raw), ld, wf.data_ptr<float>(),
                                                                     cbf(d), dpre.data_ptr<float>(), B, T2, C, (int)L,
                                                                     (int)block, (int)mode);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -473,7 +503,7 @@ std::vector<at::Tensor> conv_bwd(const at::Tensor& dy, const at::Tensor& raw, co
   const int nb = (int)((total + tpb - 1) / tpb);
   auto part = at::empty({nb, C, K}, raw.options().dtype(at::kFloat));
   dim3 grid((C / 8 + 127) / 128, nb);
-  conv_dw_kernel<4><<<grid, 128, 0, stream()>>>(cbf(raw), raw.stride(1), dpre.data_ptr<float>(), part.data_ptr<float>(),
+  conv_dw_kernel<4><<<grid, 128, 0, stream()>>>(cbf(raw), ld, dpre.data_ptr<float>(), part.data_ptr<float>(),
                                                 B, T2, C, (int)L, (int)block, (int)mode, tpb);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   auto dw = at::empty({C, K}, raw.options().dtype(at::kFloat));
@@ -560,9 +590,11 @@ __global__ void ce_rows_kernel(__nv_bfloat16* __restrict__ logits, int64_t ld, c
 }
 
 at::Tensor ce_rows_(at::Tensor& logits, const at::Tensor& tgt) {
-  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1 && logits.size(1) % 8 == 0 && logits.stride(0) % 8 == 0,
-              "ce_rows: logits [n, V], V % 8 == 0");
+  TORCH_CHECK(logits.dim() == 2 && logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1 &&
+                  logits.size(1) % 8 == 0 && logits.stride(0) % 8 == 0 && al16(logits),
+              "ce_rows: bf16 logits [n, V] in 16-byte aligned rows, V % 8 == 0");
   const int64_t n = logits.size(0);
+  TORCH_CHECK(tgt.numel() == n, "ce_rows: one target per row");
   auto loss = at::empty({n}, logits.options().dtype(at::kFloat));
   if (n == 0) return loss;
   auto t = tgt.to(at::kLong).contiguous();
@@ -670,10 +702,16 @@ __global__ void __launch_bounds__(256) adamw4_kernel(float* __restrict__ w, TP* 
 void adamw_step(at::Tensor& w, at::Tensor& p, const at::Tensor& g, at::Tensor& m, at::Tensor& v, double lr, double b1,
                 double b2, double eps, double wd, double coef, const c10::optional<at::Tensor>& coef_dev, double bc1,
                 double bc2) {
+  TORCH_CHECK(!coef_dev.has_value() || (coef_dev->scalar_type() == at::kFloat && coef_dev->numel() >= 1),
+              "adamw: fp32 device clip coefficient");
   const float* cd = coef_dev.has_value() ? coef_dev->data_ptr<float>() : nullptr;
   TORCH_CHECK(w.is_contiguous() && g.is_contiguous() && m.is_contiguous() && v.is_contiguous(), "adamw: contiguous");
-  TORCH_CHECK(w.scalar_type() == at::kFloat, "adamw: fp32 master");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat,
+              "adamw: fp32 master and moments");
+  TORCH_CHECK(g.scalar_type() == at::kFloat || g.scalar_type() == at::kBFloat16, "adamw: fp32 or bf16 gradient");
   const int64_t n = w.numel();
+  TORCH_CHECK(p.numel() == n && g.numel() == n && m.numel() == n && v.numel() == n,
+              "adamw: master, parameter, gradient and moments of one length");
   if (n == 0) return;
   c10::cuda::CUDAGuard gd(w.device());
   const bool same = p.data_ptr() == w.data_ptr();
@@ -845,8 +883,8 @@ __global__ void embed_bwd_kernel(const int64_t* __restrict__ ids, const __nv_bfl
 at::Tensor embed_fwd(const at::Tensor& ids, const at::Tensor& table) {
   TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embed: int64 ids");
   TORCH_CHECK(table.dim() == 2 && table.is_contiguous() && table.scalar_type() == at::kBFloat16 &&
-                  table.size(1) % 8 == 0,
-              "embed: bf16 table [V, D], D % 8 == 0");
+                  table.size(1) % 8 == 0 && al16(table),
+              "embed: bf16 table [V, D] at a 16-byte aligned base, D % 8 == 0");
   const int64_t N = ids.numel(), V = table.size(0);
   const int D = table.size(1);
   auto sizes = ids.sizes().vec();
@@ -865,7 +903,7 @@ void embed_bwd_(at::Tensor& grad, const at::Tensor& ids, const at::Tensor& dh) {
   TORCH_CHECK(ids.scalar_type() == at::kLong && ids.is_contiguous(), "embed_bwd: int64 ids");
   const int64_t N = ids.numel(), V = grad.size(0);
   const int D = grad.size(1);
-  auto d = dh.to(at::kBFloat16).contiguous();
+  auto d = vec_input(dh.to(at::kBFloat16));
   TORCH_CHECK(d.numel() == N * D && D % 8 == 0, "embed_bwd: dh [N, D]");
   if (N == 0) return;
   c10::cuda::CUDAGuard g(grad.device());
@@ -913,14 +951,14 @@ __global__ void embed_bwd_sorted_kernel(const int64_t* __restrict__ sid, const i
 }
 
 void embed_bwd_sorted(at::Tensor& grad, const at::Tensor& sid, const at::Tensor& perm, const at::Tensor& dh) {
-  TORCH_CHECK(grad.dim() == 2 && grad.is_contiguous() && grad.scalar_type() == at::kBFloat16,
-              "embed_bwd_sorted: bf16 [V, D]");
+  TORCH_CHECK(grad.dim() == 2 && grad.is_contiguous() && grad.scalar_type() == at::kBFloat16 && al16(grad),
+              "embed_bwd_sorted: bf16 [V, D] at a 16-byte aligned base");
   TORCH_CHECK(sid.scalar_type() == at::kLong && perm.scalar_type() == at::kLong && sid.is_contiguous() &&
                   perm.is_contiguous() && sid.numel() == perm.numel(),
               "embed_bwd_sorted: int64 sorted ids and positions");
   const int64_t N = sid.numel(), V = grad.size(0);
   const int D = grad.size(1);
-  auto d = dh.to(at::kBFloat16).contiguous();
+  auto d = vec_input(dh.to(at::kBFloat16));
   TORCH_CHECK(d.numel() == N * D && D % 8 == 0, "embed_bwd_sorted: dh [N, D]");
   if (N == 0) return;
   c10::cuda::CUDAGuard g(grad.device());
@@ -991,6 +1029,8 @@ std::vector<at::Tensor> gdn_gates_fwd(const at::Tensor& a, const at::Tensor& b, 
   check_gate_view(a, "a");
   check_gate_view(b, "b");
   const int H = a.size(-1);
+  TORCH_CHECK(b.sizes() == a.sizes() && A_log.numel() == H && dt_bias.numel() == H,
+              "gdn_gates: a and b of one shape, A_log and dt_bias [H]");
   const int64_t rows = a.numel() / H;
   auto Af = A_log.to(at::kFloat).contiguous(), df = dt_bias.to(at::kFloat).contiguous();
   auto g = at::empty(a.sizes(), a.options().dtype(at::kFloat));
@@ -1008,6 +1048,9 @@ std::vector<at::Tensor> gdn_gates_bwd(const at::Tensor& dg, const at::Tensor& db
   check_gate_view(a, "a");
   check_gate_view(b, "b");
   const int H = a.size(-1);
+  TORCH_CHECK(b.sizes() == a.sizes() && A_log.numel() == H && dt_bias.numel() == H && dg.numel() == a.numel() &&
+                  dbeta.numel() == a.numel() && (int64_t)H * 2 * sizeof(float) <= 48 * 1024,
+              "gdn_gates: a, b, dg and dbeta of one shape, A_log and dt_bias [H], H <= 6144");
   const int64_t rows = a.numel() / H;
   auto Af = A_log.to(at::kFloat).contiguous(), df = dt_bias.to(at::kFloat).contiguous();
   auto dgc = dg.to(at::kFloat).contiguous(), dbc = dbeta.to(at::kFloat).contiguous();
@@ -1050,9 +1093,9 @@ __global__ void group_sum_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloa
   }
 }
 
-at::Tensor group_sum(const at::Tensor& x, int64_t groups) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() >= 2,
-              "group_sum: contiguous bf16 [..., H, D]");
+at::Tensor group_sum(const at::Tensor& x_in, int64_t groups) {
+  TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kBFloat16 && x_in.dim() >= 2, "group_sum: bf16 [..., H, D]");
+  auto x = vec_input(x_in);
   const int64_t D = x.size(-1), H = x.size(-2);
   TORCH_CHECK(D % 8 == 0 && groups > 0 && H % groups == 0, "group_sum: D % 8 == 0 and H divisible by groups");
   const int R = (int)(H / groups);

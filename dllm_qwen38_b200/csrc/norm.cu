@@ -407,11 +407,27 @@ static inline const __nv_bfloat16* cbf(const at::Tensor& t) {
   return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr());
 }
 static inline __nv_bfloat16* bf(at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+static inline bool al16(const at::Tensor& t) { return reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0; }
+
+// contiguous [rows, D] bf16 rows at a 16-byte aligned base (the kernels move rows in 16-byte
+// vectors): the input itself, or a copy when its layout or a view's offset does not allow that
+static at::Tensor vec_rows(const at::Tensor& x, int64_t D, const char* what) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, what, ": CUDA bf16 input expected");
+  auto x2 = x.reshape({-1, D}).contiguous();
+  return al16(x2) ? x2 : x2.clone();
+}
+
+// an fp32 weight of n elements at a 16-byte aligned base (read as float4)
+static at::Tensor fvec(const at::Tensor& w, int64_t n, const char* what) {
+  TORCH_CHECK(w.numel() == n, what, ": weight of ", n, " elements expected, got ", w.numel());
+  auto f = w.to(at::kFloat).contiguous();
+  return al16(f) ? f : f.clone();
+}
 
 static at::Tensor rows2d(const at::Tensor& x) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, "norm: CUDA bf16 input expected");
   auto x2 = x.reshape({-1, x.size(-1)});
-  if (x2.stride(-1) != 1 || x2.stride(0) % 8 || reinterpret_cast<uintptr_t>(x2.data_ptr()) % 16) x2 = x2.contiguous();
+  if (x2.stride(-1) != 1 || x2.stride(0) % 8 || !al16(x2)) x2 = vec_rows(x2, x.size(-1), "norm");
   return x2;
 }
 
@@ -424,7 +440,7 @@ at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w1, double eps) {
   auto y = at::empty({rows, D}, x.options());
   if (rows == 0) return y.view(x.sizes());
   c10::cuda::CUDAGuard g(x.device());
-  auto w = w1.to(at::kFloat).contiguous();
+  auto w = fvec(w1, D, "rmsnorm");
   dim3 grid((rows + NORM_ROWS_PER_BLOCK - 1) / NORM_ROWS_PER_BLOCK), block(32 * NORM_ROWS_PER_BLOCK);
   rmsnorm_fwd_kernel<<<grid, block, 0, stream()>>>(cbf(x2), x2.stride(0), w.data_ptr<float>(), bf(y), D, rows, D,
                                                    (float)eps);
@@ -434,13 +450,13 @@ at::Tensor rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w1, double eps) {
 
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w1, double eps) {
   const int D = x.size(-1);
-  auto x2 = x.reshape({-1, D}).contiguous();
-  auto dy2 = dy.to(at::kBFloat16).reshape({-1, D}).contiguous();
+  TORCH_CHECK(D % 8 == 0 && dy.numel() == x.numel(), "rmsnorm_bwd: D % 8 == 0, dy of x's size");
+  auto x2 = vec_rows(x, D, "rmsnorm_bwd");
+  auto dy2 = vec_rows(dy.to(at::kBFloat16), D, "rmsnorm_bwd");
   const int rows = x2.size(0);
   auto dx = at::empty_like(x2);
   c10::cuda::CUDAGuard g(x.device());
-  auto w = w1.to(at::kFloat).contiguous();
-  TORCH_CHECK(D % 8 == 0, "rmsnorm_bwd: D % 8 == 0");
+  auto w = fvec(w1, D, "rmsnorm_bwd");
   const int nblk = std::max(1, (rows + RMS_BWD_ROWS - 1) / RMS_BWD_ROWS);
   auto part = at::empty({nblk, D}, x.options().dtype(at::kFloat));
   auto dw = at::empty({D}, x.options().dtype(at::kFloat));
@@ -489,7 +505,8 @@ static std::tuple<at::Tensor, int64_t, int> gated_z(const at::Tensor& z, int D, 
 at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at::Tensor& w, double eps) {
   const int D = x.size(-1);
   TORCH_CHECK(D % 32 == 0 && D <= 256, "gated_rmsnorm: D % 32 == 0 and D <= 256");
-  auto x2 = x.reshape({-1, D}).contiguous();
+  TORCH_CHECK(z.numel() == x.numel() && z.scalar_type() == at::kBFloat16, "gated_rmsnorm: bf16 z of x's size");
+  auto x2 = vec_rows(x, D, "gated_rmsnorm");
   const int rows = x2.size(0);
   auto y = at::empty_like(x2);
   if (rows == 0) return y.view(x.sizes());
@@ -497,7 +514,7 @@ at::Tensor gated_rmsnorm_fwd(const at::Tensor& x, const at::Tensor& z, const at:
   auto [zz, ldzt, H] = gated_z(z, D, rows);
   const int per = D / 32;
   const bool zvec = ((reinterpret_cast<uintptr_t>(zz.data_ptr()) | (uintptr_t)(ldzt * 2)) % (per * 2)) == 0;
-  auto wf = w.to(at::kFloat).contiguous();
+  auto wf = fvec(w, D, "gated_rmsnorm");
   const int nb = (rows + NORM_ROWS_PER_BLOCK - 1) / NORM_ROWS_PER_BLOCK;
   BDLLM_GATED_PER(P, gated_rmsnorm_fwd_kernel<P><<<nb, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(
                          cbf(x2), cbf(zz), ldzt, H, zvec, wf.data_ptr<float>(), bf(y), rows, (float)eps));
@@ -509,8 +526,10 @@ std::vector<at::Tensor> gated_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor
                                           const at::Tensor& w, double eps) {
   const int D = x.size(-1);
   TORCH_CHECK(D % 32 == 0 && D <= 256, "gated_rmsnorm: D % 32 == 0 and D <= 256");
-  auto x2 = x.reshape({-1, D}).contiguous();
-  auto dy2 = dy.to(at::kBFloat16).reshape({-1, D}).contiguous();
+  TORCH_CHECK(z.numel() == x.numel() && dy.numel() == x.numel() && z.scalar_type() == at::kBFloat16,
+              "gated_rmsnorm: bf16 z and dy of x's size");
+  auto x2 = vec_rows(x, D, "gated_rmsnorm_bwd");
+  auto dy2 = vec_rows(dy.to(at::kBFloat16), D, "gated_rmsnorm_bwd");
   const int rows = x2.size(0);
   auto dx = at::empty_like(x2);
   auto dz = at::empty({rows, D}, x.options());
@@ -519,7 +538,7 @@ std::vector<at::Tensor> gated_rmsnorm_bwd(const at::Tensor& dy, const at::Tensor
   auto part = at::empty({nblk, D}, x.options().dtype(at::kFloat));
   auto dw = at::zeros({D}, x.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard g(x.device());
-  auto wf = w.to(at::kFloat).contiguous();
+  auto wf = fvec(w, D, "gated_rmsnorm_bwd");
   if (rows > 0) {
     auto [zz, ldzt, H] = gated_z(z, D, rows);
     const int per = D / 32;
@@ -542,13 +561,14 @@ at::Tensor qk_norm_rope_fwd(const at::Tensor& src, const at::Tensor& w1, const a
   TORCH_CHECK(Dh <= 256, "qk_norm_rope: Dh <= 256");
   TORCH_CHECK(src.stride(0) == (int64_t)T2 * src.stride(1), "qk_norm_rope: batch and token dims must merge");
   const int R = cs.size(-1);
+  TORCH_CHECK(cs.size(0) == T2 && cs.numel() == (int64_t)T2 * R && sn.numel() == cs.numel() && R % 2 == 0 && R <= Dh,
+              "qk_norm_rope: cos / sin [T2, R], R even and <= Dh");
   auto out = at::empty({B, T2, H, Dh}, src.options());
   const int T = B * T2;
   if (T == 0) return out;
   c10::cuda::CUDAGuard g(src.device());
-  auto w = w1.to(at::kFloat).contiguous();
+  auto w = fvec(w1, Dh, "qk_norm_rope");
   auto c2 = cs.to(at::kBFloat16).contiguous(), s2 = sn.to(at::kBFloat16).contiguous();
-  TORCH_CHECK(c2.size(0) == T2, "qk_norm_rope: cos/sin rows must equal T2");
   const int64_t items = (int64_t)T * H;
   qk_norm_rope_fwd_kernel<<<(items + NORM_ROWS_PER_BLOCK - 1) / NORM_ROWS_PER_BLOCK, 32 * NORM_ROWS_PER_BLOCK, 0,
                             stream()>>>(cbf(src), src.stride(1), src.stride(2), w.data_ptr<float>(), cbf(c2), cbf(s2),
@@ -559,8 +579,14 @@ at::Tensor qk_norm_rope_fwd(const at::Tensor& src, const at::Tensor& w1, const a
 
 std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& w1,
                                          const at::Tensor& cs, const at::Tensor& sn, double eps) {
+  TORCH_CHECK(src.dim() == 4 && src.stride(-1) == 1 && src.scalar_type() == at::kBFloat16,
+              "qk_norm_rope: src [B, T2, H, Dh] bf16 with unit inner stride");
   const int B = src.size(0), T2 = src.size(1), H = src.size(2), Dh = src.size(3);
+  TORCH_CHECK(Dh <= 256 && src.stride(0) == (int64_t)T2 * src.stride(1), "qk_norm_rope: Dh <= 256, batch and token dims merge");
   const int R = cs.size(-1);
+  TORCH_CHECK(dout.numel() == (int64_t)B * T2 * H * Dh, "qk_norm_rope: dout of src's size");
+  TORCH_CHECK(cs.size(0) == T2 && cs.numel() == (int64_t)T2 * R && sn.numel() == cs.numel() && R % 2 == 0 && R <= Dh,
+              "qk_norm_rope: cos / sin [T2, R], R even and <= Dh");
   auto d = dout.to(at::kBFloat16).contiguous();
   auto dsrc = at::empty({B, T2, H, Dh}, src.options());
   const int T = B * T2;
@@ -571,7 +597,7 @@ std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dout, const at::Tenso
   auto part = at::empty({nblk, Dh}, src.options().dtype(at::kFloat));
   auto dw = at::zeros({Dh}, src.options().dtype(at::kFloat));
   c10::cuda::CUDAGuard g(src.device());
-  auto w = w1.to(at::kFloat).contiguous();
+  auto w = fvec(w1, Dh, "qk_norm_rope_bwd");
   auto c2 = cs.to(at::kBFloat16).contiguous(), s2 = sn.to(at::kBFloat16).contiguous();
   if (items > 0) {
     qk_norm_rope_bwd_kernel<<<nblk, 32 * NORM_ROWS_PER_BLOCK, 0, stream()>>>(

@@ -1,0 +1,70 @@
+"""Host-side argument checks of the native element-wise, norm, conv, CE and optimizer entry points.
+
+The kernels move data in 16-byte vectors and index their inputs by the shapes they are given, so
+each wrapper checks that its tensors agree in shape and type before anything is launched (and
+copies an input whose view offset breaks the 16-byte alignment). These checks run on the host:
+CPU tensors with mismatched shapes must raise the wrapper's error, never reach a kernel. No GPU
+is needed.
+"""
+
+import pytest
+import torch
+
+bf = torch.bfloat16
+
+
+@pytest.fixture(scope="module")
+def C():
+    try:
+        from dllm_qwen38_b200 import _C
+    except ImportError as e:  # the extension is built by the package build; nothing to check without it
+        pytest.skip(f"native extension not built: {e}")
+    return _C
+
+
+def z(*shape, dtype=torch.float32):
+    return torch.zeros(*shape, dtype=dtype)
+
+
+CASES = [
+    ("out_gate_fwd", lambda C: C.out_gate_fwd(z(4, 8, dtype=bf), z(4, 16, dtype=bf)), "one shape"),
+    ("out_gate_bwd", lambda C: C.out_gate_bwd(z(4, 8, dtype=bf), z(4, 8, dtype=bf), z(4, 16, dtype=bf)), "one shape"),
+    ("out_gate_bwd dy", lambda C: C.out_gate_bwd(z(3, 8, dtype=bf), z(4, 8, dtype=bf), z(4, 8, dtype=bf)),
+     "as many elements"),
+    ("dswiglu rows", lambda C: C.dswiglu(z(4, 8, dtype=bf), z(3, 16, dtype=bf)), "rows differ"),
+    ("dswiglu width", lambda C: C.dswiglu(z(4, 8, dtype=bf), z(4, 12, dtype=bf)), "shapes"),
+    ("swiglu_act", lambda C: C.swiglu_act(z(4, 8, dtype=bf)), "F % 8"),
+    ("conv weight", lambda C: C.conv_fwd(z(1, 8, 16, dtype=bf), z(16, 3), 4, 2, 0), "kernel size 4"),
+    ("conv length", lambda C: C.conv_fwd(z(1, 6, 16, dtype=bf), z(16, 4), 4, 2, 0), "[B, 2L, C]"),
+    ("conv dy", lambda C: C.conv_bwd(z(1, 8, 8, dtype=bf), z(1, 8, 16, dtype=bf), z(16, 4), 4, 2, 0), "conv: dy"),
+    ("ce targets", lambda C: C.ce_rows_(z(4, 16, dtype=bf), z(3, dtype=torch.long)), "one target per row"),
+    ("ce dtype", lambda C: C.ce_rows_(z(4, 16), z(4, dtype=torch.long)), "bf16 logits"),
+    ("adamw lengths", lambda C: C.adamw_step(z(8), z(8, dtype=bf), z(7), z(8), z(8), 1e-3, 0.9, 0.95, 1e-8, 0.0,
+                                             1.0, None, 1.0, 1.0), "one length"),
+    ("adamw moments", lambda C: C.adamw_step(z(8), z(8, dtype=bf), z(8), z(8, dtype=bf), z(8), 1e-3, 0.9, 0.95,
+                                             1e-8, 0.0, 1.0, None, 1.0, 1.0), "moments"),
+    ("embed width", lambda C: C.embed_fwd(z(4, dtype=torch.long), z(16, 12, dtype=bf)), "D % 8"),
+    ("embed_bwd_sorted", lambda C: C.embed_bwd_sorted(z(16, 8, dtype=bf), z(4, dtype=torch.long),
+                                                      z(3, dtype=torch.long), z(4, 8, dtype=bf)), "sorted ids"),
+    ("gates heads", lambda C: C.gdn_gates_fwd(z(4, 6, dtype=bf), z(4, 6, dtype=bf), z(5), z(6)), "A_log"),
+    ("gates b", lambda C: C.gdn_gates_fwd(z(4, 6, dtype=bf), z(4, 5, dtype=bf), z(6), z(6)), "one shape"),
+    ("gates bwd", lambda C: C.gdn_gates_bwd(z(3, 6), z(4, 6), z(4, 6, dtype=bf), z(4, 6, dtype=bf), z(6), z(6)),
+     "one shape"),
+    ("rmsnorm_bwd", lambda C: C.rmsnorm_bwd(z(4, 16, dtype=bf), z(5, 16, dtype=bf), z(16), 1e-6), "dy of x's size"),
+    ("gated z", lambda C: C.gated_rmsnorm_fwd(z(4, 32, dtype=bf), z(3, 32, dtype=bf), z(32), 1e-6), "z of x's size"),
+    ("gated bwd", lambda C: C.gated_rmsnorm_bwd(z(3, 32, dtype=bf), z(4, 32, dtype=bf), z(4, 32, dtype=bf), z(32),
+                                                1e-6), "dy of x's size"),
+    ("qk cos", lambda C: C.qk_norm_rope_fwd(z(1, 4, 2, 16, dtype=bf), z(16), z(4, 3, dtype=bf), z(4, 3, dtype=bf),
+                                            1e-6), "R even"),
+    ("qk cos rows", lambda C: C.qk_norm_rope_fwd(z(1, 4, 2, 16, dtype=bf), z(16), z(5, 4, dtype=bf),
+                                                 z(5, 4, dtype=bf), 1e-6), "[T2, R]"),
+    ("qk dout", lambda C: C.qk_norm_rope_bwd(z(1, 4, 2, 8, dtype=bf), z(1, 4, 2, 16, dtype=bf), z(16),
+                                             z(4, 4, dtype=bf), z(4, 4, dtype=bf), 1e-6), "dout of src's size"),
+]
+
+
+@pytest.mark.parametrize("name,call,fragment", CASES, ids=[c[0] for c in CASES])
+def test_wrapper_rejects_mismatched_arguments(C, name, call, fragment):
+    with pytest.raises(RuntimeError) as e:
+        call(C)
+    assert fragment in str(e.value), (name, str(e.value).splitlines()[0])

@@ -444,6 +444,13 @@ __global__ void __launch_bounds__(NTH, 2) bwd_dkv_kernel(Args a) {
 }
 
 // ------------------------------------------------------------------------------------- host
+// a contiguous tensor at a 16-byte aligned base (rows move in 16-byte vectors and TMA tiles): the
+// input itself, or a copy when a view's offset breaks the alignment
+static at::Tensor aligned_rows(const at::Tensor& t) {
+  auto c = t.contiguous();
+  return reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0 ? c : c.clone();
+}
+
 static void check_qkv(const at::Tensor& t, int64_t D) {
   TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4, "attn: bf16 [B, T2, H, D]");
   TORCH_CHECK(t.stride(3) == 1 && t.stride(2) == D && t.stride(0) == t.size(1) * t.stride(1),
@@ -474,7 +481,10 @@ static Args make_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor
   a.leak = leak ? 1 : 0;
   a.scale = (float)scale;
   a.scale_log2 = (float)(scale * 1.4426950408889634);
-  TORCH_CHECK(a.T2 == 2 * L && a.Hq % a.Hk == 0, "attn: shapes");
+  TORCH_CHECK(a.T2 == 2 * L && a.Hq % a.Hk == 0 && block >= 1, "attn: shapes");
+  TORCH_CHECK(k.size(0) == a.B && v.size(0) == a.B && k.size(1) == a.T2 && v.size(1) == a.T2 &&
+                  v.size(2) == a.Hk && k.size(3) == D && v.size(3) == D,
+              "attn: q, k and v of one batch, length and head dim; k and v of one head count");
   a.Tk = a.T2;
   a.q_bat = (int64_t)a.T2 * a.q_tok;
   a.k_bat = (int64_t)a.T2 * a.k_tok;
@@ -519,7 +529,11 @@ static at::Tensor prefix_t(const at::Tensor& q, const at::Tensor& k, const at::T
   } else {
     TORCH_CHECK(tk_host >= 1 && tk_host <= k.size(1) && tk_host <= v.size(1), "attn_prefix: 1 <= Tk <= cache rows");
   }
-  TORCH_CHECK(a.Hq % a.Hk == 0 && k.size(0) == a.B && v.size(0) == a.B, "attn_prefix: shapes");
+  TORCH_CHECK(a.Hq % a.Hk == 0 && k.size(0) == a.B && v.size(0) == a.B && v.size(2) == a.Hk && q.size(3) == D &&
+                  k.size(3) == D && v.size(3) == D,
+              "attn_prefix: shapes");
+  for (const at::Tensor* t : {&q, &k, &v})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4, "attn_prefix: bf16 [B, T, H, D]");
   auto o = at::empty({a.B, a.T2, a.Hq, D}, q.options());
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
@@ -567,8 +581,11 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
                                      const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, int64_t L,
                                      int64_t block, double scale, bool leak) {
   Args a = make_args(q, k, v, L, block, scale, leak);
-  auto d = dout.to(at::kBFloat16).contiguous();
-  auto oc = o.contiguous();
+  TORCH_CHECK(dout.numel() == q.numel() && o.sizes() == q.sizes() && o.scalar_type() == at::kBFloat16 &&
+                  lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == (int64_t)a.B * a.Hq * a.T2,
+              "attn: dout and bf16 o of q's shape, fp32 lse [B, Hq, T2]");
+  auto d = aligned_rows(dout.to(at::kBFloat16));
+  auto oc = aligned_rows(o);
   auto delta = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   auto dq = at::empty({a.B, a.T2, a.Hq, D}, q.options());
   auto dk = at::empty({a.B, a.T2, a.Hk, D}, q.options());

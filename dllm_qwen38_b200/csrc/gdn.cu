@@ -1150,6 +1150,12 @@ static Args make_args(const at::Tensor& q, const at::Tensor& k, const at::Tensor
               "gdn: g, beta fp32 contiguous [B, 2L, Hv]");
   TORCH_CHECK(C <= 32 && C >= 1 && (2 * L) % C == 0 && (concat || L % C == 0),
               "gdn: chunk (= block) must be <= 32 and divide L");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
+              "gdn: bf16 q, k, v");
+  TORCH_CHECK(q.size(1) == 2 * L && k.sizes() == q.sizes() && v.size(0) == q.size(0) && v.size(1) == q.size(1) &&
+                  v.size(2) % q.size(2) == 0,
+              "gdn: q, k [B, 2L, Hk, Dk] and v [B, 2L, Hv, Dv] with Hv a multiple of Hk");
+  TORCH_CHECK(g.numel() == q.size(0) * q.size(1) * v.size(2) && beta.numel() == g.numel(), "gdn: g, beta [B, 2L, Hv]");
   Args a{};
   a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   a.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
@@ -1250,7 +1256,12 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
                                           bool want_dS0 = false) {
   Args a = make_args(q, k, v, g, beta, L, C, concat);
   auto f32 = q.options().dtype(at::kFloat);
+  TORCH_CHECK(dout.numel() == (int64_t)a.B * 2 * L * a.Hv * Dv, "gdn_bwd: dout [B, 2L, Hv, Dv]");
+  TORCH_CHECK(S_in.is_contiguous() && (S_in.scalar_type() == at::kFloat || S_in.scalar_type() == at::kBFloat16) &&
+                  S_in.numel() == (int64_t)a.B * a.nb * a.Hv * Dk * Dv,
+              "gdn_bwd: S_in [B, nb, Hv, Dk, Dv] (fp32, or bf16 from the tensor-core forward)");
   auto d = dout.to(at::kBFloat16).contiguous();
+  if (reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 != 0) d = d.clone();  // read in 16-byte vectors and TMA tiles
   a.dout = reinterpret_cast<const __nv_bfloat16*>(d.data_ptr());
   // bf16 S_in: the tensor-core forward's S^T rows; the whole backward then runs on tcgen05
   const bool bf16_states = S_in.scalar_type() == at::kBFloat16;

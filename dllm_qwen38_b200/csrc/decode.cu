@@ -228,7 +228,10 @@ at::Tensor conv_tail(const at::Tensor& raw, at::Tensor& tail, const at::Tensor& 
   TORCH_CHECK(tail.is_contiguous() && tail.scalar_type() == at::kBFloat16 && tail.size(0) == B &&
                   tail.size(1) == K - 1 && tail.size(2) == C,
               "conv_tail: tail [B, K-1, C] bf16 contiguous");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(raw.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(tail.data_ptr()) % 16 == 0,
+              "conv_tail: raw and tail at 16-byte aligned bases (read in 16-byte vectors)");
   auto wf = w.reshape({C, K}).to(at::kFloat).contiguous();
+  if (reinterpret_cast<uintptr_t>(wf.data_ptr()) % 16 != 0) wf = wf.clone();  // read as float4
   auto y = at::empty({B, T, C}, raw.options());
   c10::cuda::CUDAGuard g(raw.device());
   dec::conv_tail_kernel<4><<<dim3((C / 8 + 127) / 128, B), 128, 0, dec::stream()>>>(

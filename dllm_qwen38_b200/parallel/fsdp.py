@@ -84,11 +84,11 @@ def _world():
     return (dist.get_world_size(), dist.get_rank()) if dist.is_initialized() else (1, 0)
 
 
-def choose_saved_layers(per: list, per_act: list, free: float):
-    """How many leading layers keep their GEMM outputs: the budget is 92 % of `free` bytes less
-    3 GiB. When every layer fits with its MLP activation too (`per_act` bytes each), keep it;
+def choose_saved_layers(per: list, per_act: list, free: float, frac: float = 0.92, reserve: int = 3 << 30):
+    """How many leading layers keep their GEMM outputs: the budget is `frac` of `free` bytes less
+    `reserve`. When every layer fits with its MLP activation too (`per_act` bytes each), keep it;
     otherwise count with `per` (gate|up only). Returns (layers, bytes used, keep_act)."""
-    budget = 0.92 * (free - (3 << 30))
+    budget = frac * (free - reserve)
     keep_act = sum(per_act) < budget
     sizes = per_act if keep_act else per
     n, used = 0, 0
@@ -576,14 +576,17 @@ class FSDPEngine:
         whose outputs live longest) as fit in 92 % of the device memory that the step's peak left
         unreserved, less 3 GiB. The caching allocator keeps its peak reservation, so what the saved
         outputs add has to come from memory that is still free now. Every rank takes the same
-        decision: the smallest headroom over ranks counts."""
+        decision: the smallest headroom over ranks counts. With several ranks a step that runs out
+        of memory cannot be rerun (the other ranks are inside their collectives), so the budget
+        there is the wider-margin 85 % less 2 GiB."""
         per = self.gemm_bytes_per_layer(rows)
         torch.cuda.synchronize(self.device)
         free = torch.tensor([float(torch.cuda.mem_get_info(self.device)[0])], device=self.device)
         if self.world > 1:
             dist.all_reduce(free, op=dist.ReduceOp.MIN)
+        margin = dict(frac=0.85, reserve=2 << 30) if self.world > 1 else {}
         n, used, self.keep_act = choose_saved_layers(per, self.gemm_bytes_per_layer(rows, with_act=True),
-                                                     float(free[0]))
+                                                     float(free[0]), **margin)
         if self.keep_act:
             per = self.gemm_bytes_per_layer(rows, with_act=True)
         self.save_gemms = "1" if n == len(per) else str(n)

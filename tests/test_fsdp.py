@@ -116,6 +116,10 @@ def test_saved_layer_choice_keeps_the_activation_only_when_everything_fits():
     # 0.92 * (9 - 3) = 5.5 GiB: two layers of gate|up
     assert choose_saved_layers(per, per_act, 9 * gib) == (2, 4 * gib, False)
     assert choose_saved_layers(per, per_act, gib)[0] == 0
+    # several ranks (no rerun after an out-of-memory error): 0.85 * (9 - 2) = 5.95 GiB, two layers
+    assert choose_saved_layers(per, per_act, 9 * gib, frac=0.85, reserve=2 * gib) == (2, 4 * gib, False)
+    # 0.85 * (16 - 2) = 11.9 GiB: all four, gate|up only (12 GiB with the activation does not fit)
+    assert choose_saved_layers(per, per_act, 16 * gib, frac=0.85, reserve=2 * gib) == (4, 8 * gib, False)
 
 
 def test_one_rank_out_of_memory_retries_with_fewer_kept_layers():

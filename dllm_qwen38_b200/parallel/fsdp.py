@@ -692,7 +692,7 @@ class _EmbedFn(torch.autograd.Function):
             if gt.is_cuda:
                 from ..ops import _native
 
-                sid, perm = torch.sort(flat_ids)
+                sid, perm = torch.sort(flat_ids, stable=True)  # fixed summation order within a run
                 _native.require().embed_bwd_sorted(gt, sid, perm, dh.reshape(-1, D))
             else:
                 acc = torch.zeros(V, D, dtype=torch.float32)

@@ -279,7 +279,8 @@ class FSDPEngine:
 
     def _heap_bytes(self, modules) -> int:
         """Bytes of the symmetric heap: every unit's bf16 shard, two bf16 gradient buffers of the
-        largest layer/head unit and the fp32 embedding-table gradient (256-byte aligned each)."""
+        largest layer/head unit and the embedding-table gradient (fp32 when the head is tied to the
+        table, else the model dtype), each 256-byte aligned."""
         w = self.world
         esz = torch.empty(0, dtype=self.dtype).element_size()
 

@@ -241,3 +241,65 @@ def test_server_runs_compare_collect_uncertainty(tmp_path):
     u = uncertainty.analyze(tmp_path / "bundle.json")
     lo, hi = u["comparisons"][0]["interval"]
     assert -1.0 <= lo <= u["comparisons"][0]["observed_delta"] <= hi <= 1.0
+
+
+def test_capture_reader_checks_accounting(tmp_path):
+    from dllm_qwen38_b200.weight_space.capture_data import load_vectors
+
+    d = np.zeros(8, np.float32)
+    _synthetic_capture(tmp_path / "cap", 4, 2, 8, d)
+    vecs, acct = load_vectors(tmp_path / "cap", 4, [2], width=8)
+    assert acct["vectors"] == 4 and vecs[(0, 2)].shape == (8,)
+    with pytest.raises(ValueError, match="width"):
+        load_vectors(tmp_path / "cap", 4, [2], width=16)
+    with pytest.raises(ValueError, match="accounting"):  # a layer that was never captured
+        load_vectors(tmp_path / "cap", 4, [1, 2])
+    st = json.loads((tmp_path / "cap" / "status.json").read_text())
+    (tmp_path / "cap" / "status.json").write_text(json.dumps(dict(st, ok=False)))
+    with pytest.raises(ValueError, match="did not complete"):
+        load_vectors(tmp_path / "cap", 4, [2])
+    (tmp_path / "cap" / "status.json").write_text(json.dumps(st))
+    np.full(16, np.nan, "<f4").tofile(tmp_path / "cap" / "p3-l2.f32")  # same size, not finite
+    with pytest.raises(ValueError, match="non-finite"):
+        load_vectors(tmp_path / "cap", 4, [2])
+    np.zeros(15, "<f4").tofile(tmp_path / "cap" / "p3-l2.f32")  # one value short
+    with pytest.raises(ValueError, match="byte count"):
+        load_vectors(tmp_path / "cap", 4, [2])
+
+
+def test_prepare_math_selects_hard_single_integer_problems(tmp_path):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    from dllm_qwen38_b200.weight_space import prepare_math
+
+    rows = []
+    for i in range(10):  # eligible: level 4/5, exactly one boxed plain integer
+        rows.append({"problem": f"problem {i}", "level": "Level 5" if i % 2 else "Level 4",
+                     "solution": f"so \\boxed{{{1000 + i:,}}}", "type": "Algebra"})
+    rows += [
+        {"problem": "easy", "level": "Level 2", "solution": "\\boxed{3}", "type": "Algebra"},
+        {"problem": "two boxes", "level": "Level 5", "solution": "\\boxed{3} or \\boxed{4}", "type": "Algebra"},
+        {"problem": "fraction", "level": "Level 5", "solution": "\\boxed{\\frac{1}{2}}", "type": "Algebra"},
+        {"problem": "problem 3", "level": "Level 5", "solution": "\\boxed{7}", "type": "Algebra"},  # duplicate
+    ]
+    src = tmp_path / "src" / "algebra"
+    src.mkdir(parents=True)
+    pq.write_table(pa.Table.from_pylist(rows), src / "train.parquet")
+    out = tmp_path / "out"
+    assert prepare_math.main(["--source", str(tmp_path / "src"), "--output", str(out), "--size", "4"]) == 0
+    dev = json.loads((out / "dev.json").read_text())
+    val = json.loads((out / "validation.json").read_text())
+    cases = dev["cases"] + val["cases"]
+    assert len(dev["cases"]) == 4 and len(val["cases"]) == 4
+    assert [c["id"] for c in cases] == sorted(c["id"] for c in cases)  # hash order, dev first
+    assert {c["question"] for c in cases} <= {f"problem {i}" for i in range(10)}
+    assert all(c["answer"].isdigit() and "," not in c["answer"] for c in cases)
+    assert dev["sources"][0]["file"] == "algebra/train.parquet"
+    with pytest.raises(FileExistsError):  # outputs are never overwritten
+        prepare_math.main(["--source", str(tmp_path / "src"), "--output", str(out), "--size", "4"])
+    with pytest.raises(ValueError, match="not enough"):
+        prepare_math.main(["--source", str(tmp_path / "src"), "--output", str(tmp_path / "o2"), "--size", "6"])
+    pq.write_table(pa.Table.from_pylist(rows), src / "test.parquet")
+    with pytest.raises(ValueError, match="test split"):
+        prepare_math.main(["--source", str(tmp_path / "src"), "--output", str(tmp_path / "o3"), "--size", "2"])

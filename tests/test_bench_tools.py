@@ -44,3 +44,14 @@ def test_step_profile_families():
     # the first matching fragment wins, so each fragment is listed once
     frags = [f for f, _ in FAMILIES]
     assert len(frags) == len(set(frags))
+
+
+def test_lever_legs_name_real_op_families():
+    from dllm_qwen38_b200 import ops
+    from dllm_qwen38_b200.bench.levers import LEGS
+
+    names = [n for n, _, _ in LEGS]
+    assert names[0] == "native" and len(names) == len(set(names))
+    for _, off, opts in LEGS:
+        assert set(off) <= set(ops.ALL_OPS), off
+        assert set(opts) <= {"checkpointing", "batch_mult"}

@@ -1,4 +1,6 @@
 """Fused collective paths over 27B layer shapes, as fractions of their roofline (one rank per GPU).
+They replace the reference's FSDP2 per-unit all-gather and fp32 reduce-scatter
+(`src/dllm_qwen38/fsdp_train.py:133-171`), which NCCL runs as separate calls.
 
     torchrun --nproc-per-node N -m dllm_qwen38_b200.bench.collectives [--iters 10]
 

@@ -1,7 +1,7 @@
 """Native block-diffusion decode engine: static caches, device-side commit, CUDA-graph steps.
 
-The same decoding as `infer/cached.py` (and therefore the golden decoder's rule), organised for
-the GPU:
+The same decoding as `infer/cached.py` (and therefore the golden decoder's rule,
+`src/dllm_qwen38/decode.py:53-97`), organised for the GPU:
 
   * caches live in preallocated buffers: per attention layer K/V [B, max_len, Hk, Dh] (bf16),
     per GDN layer the fp32 state [B, Hv, Dk, Dv] and the conv tail [B, K-1, conv_dim];

@@ -1,4 +1,5 @@
-"""Tensor-parallel block-diffusion decoding (TP = 1, 2, 4, 8 GPUs of one node).
+"""Tensor-parallel block-diffusion decoding (TP = 1, 2, 4, 8 GPUs of one node). The reference
+decodes on one device only (`src/dllm_qwen38/decode.py:35-99`); the commit rule is the same.
 
 Layout (Megatron-style, with the residual stream sharded by rows between the layers):
   * GDN: q/k heads and v heads split evenly (Hk/world, Hv/world per rank), with their rows of

@@ -1,7 +1,8 @@
 """Write a model as an HF-layout checkpoint directory (`config.json` + `model.safetensors`, text
 tower under ``model.language_model.*``), readable by `io.hf_load.load_model` and by the
 weight-space tools. The inverse of `hf_load`; used to freeze a trained or edited model for the
-completion server and the weight-space bench."""
+completion server and the weight-space bench (the reference exports a trained model as one
+`model.safetensors` at `src/dllm_qwen38/train.py:270-276`)."""
 
 from __future__ import annotations
 

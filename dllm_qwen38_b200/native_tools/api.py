@@ -1,4 +1,6 @@
-"""Python half of the native tools (`capture`, `meter`): the engine calls they make.
+"""Python half of the native tools (`capture`, `meter`): the engine calls they make (the
+reference's tools make llama.cpp calls instead: `tools/weight-space/capture.cpp:27-57,124`,
+`tools/weight-space/meter.cpp:180-198`).
 
 The C++ programs own argument handling, limits, file formats, timing and accounting; these
 functions are the only way they touch the model:

@@ -1,5 +1,11 @@
 """Autograd-aware wrappers around the sm_100a kernels (``dllm_qwen38_b200._C``).
 
+Each wrapper replaces one library path of the reference: the chunked delta rule
+(`src/dllm_qwen38/gdn.py:48-123`) and its autograd backward, the GDN mixer's conv, gates and
+gated norm (`gdn.py:212-233`), the masked attention (`blockdiff.py:178-182`, HF eager or SDPA over
+a dense mask), the masked-row lm_head + CE (`objective.py:79-84`, `fsdp_train.py:618-623`) and
+single-tensor AdamW (`fsdp_train.py:779`).
+
 Conventions of the GEMM entry (``_C.gemm``): C[m, n] = sum_k A(m, k) B(n, k); A is K-major
 ([M, K]) or MN-major ([K, M]); B is K-major ([N, K]) or MN-major ([K, N]). With those two bits
 the three GEMMs of a linear layer need no transposes:

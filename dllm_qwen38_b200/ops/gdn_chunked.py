@@ -1,7 +1,9 @@
 """Explicit forward and backward of the chunked gated delta rule (fp32, vectorised over chunks).
 
 This is the specification the CUDA kernels in ``csrc/gdn.cu`` implement, kept as runnable
-torch code and checked against autograd in the tests. Per chunk of C tokens and one head
+torch code and checked against autograd in the tests. The reference computes the same rule with
+torch ops and two triangular solves per chunk and differentiates it by autograd
+(`src/dllm_qwen38/gdn.py:48-123`). Per chunk of C tokens and one head
 (q^, k^ are the l2-normalised query/key, q^ scaled by Dk^-1/2; S [Dk, Dv] the state entering the
 chunk):
 

@@ -1,5 +1,6 @@
 """NVTX ranges around layers, fused collectives and decode steps (`BDLLM_NVTX=1`), for Nsight
-timelines; a no-op otherwise (no per-call cost beyond one dict lookup)."""
+timelines; a no-op otherwise (no per-call cost beyond one dict lookup). The reference has no
+ranges of its own: it times loops with the host clock (`src/dllm_qwen38/train.py:145,165-166`)."""
 
 from __future__ import annotations
 

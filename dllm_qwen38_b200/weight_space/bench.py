@@ -1,5 +1,5 @@
 """GSM8K-train development runs against a loopback completion server, and the paired comparison
-of two runs (the role of the reference's `tools/weight-space/bench.py`; this one drives this
+of two runs (the role of the reference's `tools/weight-space/bench.py:39-185`; this one drives this
 framework's `server.py` instead of llama-server and reads the data from a local file).
 
     python -m dllm_qwen38_b200.weight_space.bench prepare --source train.jsonl --output DIR [--size 32]

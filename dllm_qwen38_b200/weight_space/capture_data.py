@@ -1,6 +1,6 @@
 """Read the output directory of this framework's `capture` tool (native_tools/capture.cpp) into
 final-position residual vectors, with the run's accounting checked first (the reference's
-`tools/weight-space/capture_data.py` role, for our capture format):
+`tools/weight-space/capture_data.py:8-37` role, for our capture format):
 
   DIR/status.json   {"ok", "prompts", "tensors", "layer_visits", "error"}
   DIR/index.jsonl   {"prompt", "layer", "file", "rows", "cols", "bytes"} per tensor

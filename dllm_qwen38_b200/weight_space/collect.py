@@ -1,5 +1,5 @@
 """Collect completed launched runs under an explicit comparison plan into one verified bundle
-(the role of the reference's `tools/weight-space/collect.py`; no inference, no regrading).
+(the role of the reference's `tools/weight-space/collect.py:13-99`; no inference, no regrading).
 
     python -m dllm_qwen38_b200.weight_space.collect PLAN.json --output BUNDLE.json
 

@@ -1,5 +1,5 @@
 """Exclusive ownership receipt for a controller's output directory (the reference's
-`tools/weight-space/controller_claim.py` role): `claim(dir, protocol_sha256)` creates
+`tools/weight-space/controller_claim.py:10-21` role): `claim(dir, protocol_sha256)` creates
 `controller-owner.json` with O_CREAT | O_EXCL, so two controllers can never both believe they own
 the directory; the receipt stays after completion, so a rerun needs a fresh directory."""
 

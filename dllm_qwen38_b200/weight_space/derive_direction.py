@@ -1,5 +1,5 @@
 """Derive one residual direction from captured development probes (the role of the reference's
-`tools/weight-space/derive_direction.py`).
+`tools/weight-space/derive_direction.py:13-74`).
 
     python -m dllm_qwen38_b200.weight_space.derive_direction --capture CAP_DIR --output OUT_DIR
            --layer L --prompts 8 --pairs 0:1 2:3 4:5 --reset 6:7 --min-mean-cosine 0.3

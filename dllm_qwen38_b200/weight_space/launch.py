@@ -1,6 +1,6 @@
 """Run one JSON-configured bench: start this framework's completion server on a loopback port,
 run `bench.run` against it, and stop only the server this run started (the reference's
-`tools/weight-space/launch.py` role, for our server instead of llama-server).
+`tools/weight-space/launch.py:14-91` role, for our server instead of llama-server).
 
     python -m dllm_qwen38_b200.weight_space.launch CONFIG.json
 

@@ -1,5 +1,5 @@
 """Hard MATH-train integer-answer subset from local parquet files (the reference's
-`tools/weight-space/prepare_math.py` role; no download: the parquet files are given).
+`tools/weight-space/prepare_math.py:21-62` role; no download: the parquet files are given).
 
     python -m dllm_qwen38_b200.weight_space.prepare_math --source DIR --output OUT [--size 32]
 

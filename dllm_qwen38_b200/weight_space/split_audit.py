@@ -1,4 +1,4 @@
-"""Lexical audit of dev vs validation splits (the reference's `tools/weight-space/split_audit.py`
+"""Lexical audit of dev vs validation splits (the reference's `tools/weight-space/split_audit.py:13-83`
 role). Every cross-split question pair is compared under a fixed profile:
 
   normalised   NFKC, casefold, whitespace collapsed

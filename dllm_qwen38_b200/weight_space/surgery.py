@@ -1,5 +1,5 @@
 """Projection edits on MLP down projections of a copy of a safetensors checkpoint (the
-reference's `tools/weight-space/surgery.py` role, for this framework's safetensors files instead
+reference's `tools/weight-space/surgery.py:20-160` role, for this framework's safetensors files instead
 of GGUF).
 
     python -m dllm_qwen38_b200.weight_space.surgery --source model.safetensors --source-sha256 H

@@ -1,5 +1,5 @@
 """The boxed-answer scorer behind a process boundary with a per-case deadline (the role of the
-reference's `tools/weight-space/symbolic_process.py`).
+reference's `tools/weight-space/symbolic_process.py:12-74`).
 
 A symbolic comparison can run away on a hostile prediction, so the scorer runs in a separate
 process. One long-lived child serves every case of a run through a pipe (starting a Python

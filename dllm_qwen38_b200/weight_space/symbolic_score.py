@@ -1,4 +1,4 @@
-"""Boxed-answer scorer for MATH-style runs (the reference's `tools/weight-space/symbolic_score.py`
+"""Boxed-answer scorer for MATH-style runs (the reference's `tools/weight-space/symbolic_score.py:13-79`
 role).
 
 Two profiles. When math-verify and its parser stack are installed at the versions the reference

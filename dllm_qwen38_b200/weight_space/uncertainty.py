@@ -1,5 +1,5 @@
 """Conservative paired-delta interval for a collected comparison bundle (supplementary to the
-frozen bootstrap / McNemar numbers; the reference's `tools/weight-space/uncertainty.py` role).
+frozen bootstrap / McNemar numbers; the reference's `tools/weight-space/uncertainty.py:12-99` role).
 
 For n paired problems with `wins` (candidate right, baseline wrong) and `losses` (the reverse),
 the win and loss rates each get an exact two-sided binomial (Clopper-Pearson) interval at

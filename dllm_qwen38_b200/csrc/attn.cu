@@ -4,6 +4,8 @@
 //   x_t row i sees x_0 key j iff block(j) <  block(i)
 //   x_0 row i sees x_0 key j iff block(j) <= block(i);   x_0 never sees x_t
 // Key tiles that no row of a query tile may see are skipped (about half of the 2L x 2L pairs).
+// (The reference builds a dense [2L, 2L] additive mask, `src/dllm_qwen38/blockdiff.py:50-66`, and runs
+// HF eager or SDPA attention over it, `blockdiff.py:178-182`.)
 //
 // Tiles of 64 query rows x 64 keys, 4 warps (16 rows each), bf16 mma.sync m16n8k16 with fp32
 // accumulation, online softmax in base 2. Shared tiles are 16-byte-chunk XOR-swizzled for

@@ -1,4 +1,5 @@
 // Complementary-mask attention forward on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+// (Reference path replaced: dense mask + HF eager / SDPA attention, `src/dllm_qwen38/blockdiff.py:50-66,178-182`.)
 //
 // Same contract as the mma.sync forward in attn.cu (O [B, T2, Hq, D] bf16 and the per-row
 // log2-sum-exp of the scaled scores), same analytic mask and tile skipping, for head dims 128 and

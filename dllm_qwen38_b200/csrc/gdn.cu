@@ -1,4 +1,6 @@
 // State-fork chunked gated delta rule, forward and backward, over the [B, 2L] two-stream layout.
+// (Reference: torch ops with triangular solves and a Python chunk loop, `src/dllm_qwen38/gdn.py:48-123`,
+// run twice for the fork, `blockdiff.py:159-177`, and differentiated by autograd.)
 //
 // Math (per chunk of C tokens and one v-head; the torch specification with the same names is
 // dllm_qwen38_b200/ops/gdn_chunked.py and is checked against autograd):

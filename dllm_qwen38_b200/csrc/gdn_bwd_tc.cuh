@@ -5,6 +5,7 @@
 // blocks' state gradients itself (so no dS_inj is stored here). The states come as bf16 S^T rows
 // (the forward's S_in and the recurrence's dS_out, [v][k] per chunk) loaded by TMA; the dq, dk and
 // dv rows of the chunk are staged in dead token tiles and written by TMA stores.
+// (Reference: autograd through `src/dllm_qwen38/gdn.py:48-123`.)
 //
 // Per CTA = one chunk (32 tokens) of one v-head. Every product with a 128-wide operand (the state
 // S, dS_out, or a feature dimension) runs as an M = 128 MMA with the feature dimension on the 128

@@ -5,6 +5,7 @@
 // clean chunk (= the state each noised block forks from) as S_in^T [B, nb, Hv, 128 (v), 128 (k)]
 // bf16, the layout the tensor-core backward loads by TMA (row v of S^T is what one epilogue
 // thread holds, so each thread stores one contiguous row).
+// (Reference path replaced: `src/dllm_qwen38/gdn.py:48-123` and the fork in `blockdiff.py:159-177`.)
 //
 // Math per chunk (one v-head; q^, k^ l2-normalised, q^ scaled by 128^-1/2; gam = cumsum g):
 //   A = strict_lower(beta_i k^_i.k^_j e^(gam_i - gam_j)), T = (I + A)^-1

@@ -1,5 +1,7 @@
 // Persistent warp-specialised bf16 GEMM for sm_100a: TMA -> shared memory -> tcgen05.mma with
 // the fp32 accumulator in TMEM -> tcgen05.ld epilogue with fused element-wise ops.
+// (Reference: nn.Linear / cuBLAS for every projection, `src/dllm_qwen38/gdn.py:212-215,233`,
+// `blockdiff.py:179-187`, and the masked-row lm_head, `objective.py:79-84`.)
 //
 //   C[m, n] = sum_k A(m, k) * B(n, k)
 //

@@ -5,6 +5,9 @@
 //   adamw          fused clip-scale + AdamW on fp32 master weights, bf16 parameter write-back
 //   group_sum      GQA: per-v-head gradients summed over each k-head's group, bf16 in and out
 //   mask_sample    the complementary masks of a step and both noised views, one launch
+// (Reference paths: mask sampling `src/dllm_qwen38/objective.py:26-57`, masked CE `objective.py:60-84`,
+// AdamW `fsdp_train.py:779`, conv + SiLU `gdn.py:217-219`, gates `gdn.py:225-226`, embedding
+// `blockdiff.py:140-141`.)
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>

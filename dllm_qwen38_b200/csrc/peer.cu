@@ -1,4 +1,6 @@
 // Symmetric peer memory over NVLink / NVSwitch and the collectives built on it.
+// (Reference: FSDP2's NCCL all-gather / fp32 reduce-scatter per unit, `src/dllm_qwen38/fsdp_train.py:133-171`,
+// and the all_reduce of replicated gradients, `fsdp_train.py:207-221`.)
 //
 // A symmetric heap is one cudaMalloc region of the same size on every rank of a node, exported
 // with a CUDA IPC handle and opened by every other rank; the ranks carve it up with identical

@@ -1,4 +1,5 @@
 // Tensor-parallel decode collectives over peer memory (the halves that are not inside the GEMM).
+// (The reference decodes on one device, `src/dllm_qwen38/decode.py:35-99`; tensor parallelism is new here.)
 //
 // The residual stream is sharded by rows: rank r owns rows [r*R, (r+1)*R) of the M = world*R
 // rows of a step. A row-parallel GEMM (csrc/gemm.cu, EPI_PEER_F32) stores each rank's fp32

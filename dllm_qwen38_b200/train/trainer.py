@@ -5,11 +5,13 @@ complementary masks (pure function of (global step, rank), `fsdp_train.py:607`),
 forward with per-layer activation checkpointing, masked CE over the 248k vocab on masked rows
 only, backward, global-norm clip, AdamW.
 
-The step never synchronises the host with the device: the number of scored targets is known
-on the host before any kernel runs, because the two complementary views together mask every
-scorable position exactly once (n = sum(valid_len - prompt_len)); the masked-row gather uses
-that count (`nonzero_static`) instead of reading it back. The returned loss is a device tensor;
-reading it is the caller's choice.
+The forward, the loss and the backward never synchronise the host with the device: the number
+of scored targets is known on the host before any kernel runs, because the two complementary
+views together mask every scorable position exactly once (n = sum(valid_len - prompt_len)); the
+masked-row gather uses that count (`nonzero_static`) instead of reading it back. The one host read
+per step is the global gradient norm, from which `MasterAdamW` computes the clip coefficient (the
+sharded engine, `parallel/fsdp.py`, keeps that coefficient on the device). The returned loss is a
+device tensor; reading it is the caller's choice.
 """
 
 from __future__ import annotations

@@ -20,6 +20,7 @@ Exit codes: 0 ok, 1 a gate failed, 2 could not measure.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import datetime
 import json
 import math
@@ -30,6 +31,7 @@ import time
 import torch
 import torch.distributed as dist
 
+from .. import ops
 from ..io import ckpt
 from ..utils import mem
 
@@ -173,8 +175,10 @@ def main(argv=None) -> int:
     p.add_argument("--layers", type=int, default=None)
     p.add_argument("--grad-checkpoint", action="store_true", help="accepted for compatibility: always on")
     p.add_argument("--mem-history", action="store_true")
-    p.add_argument("--gdn", default="native", choices=["native", "torch", "auto"],
-                   help="accepted for compatibility; the GDN core is the native kernel on CUDA")
+    p.add_argument("--gdn", default="native", choices=["native", "auto", "torch", "fla"],
+                   help="GDN core: native (= auto) runs the sm_100a kernels; torch runs the fp32 torch "
+                        "chunked rule on the device (the reference's default path, for comparison); fla is "
+                        "not part of this framework")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--out", default=None)
     p.add_argument("--ckpt-dir", default=None)
@@ -190,6 +194,17 @@ def main(argv=None) -> int:
     if a.resume_selftest and not a.ckpt_dir:
         print("COULD-NOT-MEASURE --resume-selftest needs --ckpt-dir", file=sys.stderr)
         return 2
+    if a.gdn == "fla":
+        print("COULD-NOT-MEASURE --gdn fla: fla's Triton kernel is not part of this framework (the native "
+              "tcgen05 kernel replaces it); use --gdn native, or --gdn torch for the torch chunked rule",
+              file=sys.stderr)
+        return 2
+    # the torch GDN path on the device for the whole run (host tensors take it anyway)
+    with ops.torch_on_cuda("gdn_core") if a.gdn == "torch" else contextlib.nullcontext():
+        return _run(a)
+
+
+def _run(a) -> int:
     rank, world = _init_dist()
     say = print if rank == 0 else (lambda *_a, **_k: None)
     try:
@@ -218,7 +233,8 @@ def main(argv=None) -> int:
                        fingerprint_saves="all" if a.resume_selftest else "window_end", log_every=a.log_every,
                        mem_history=a.mem_history, log=say)
     rep.update({"model": a.model, "data": a.data, "block": a.block, "seq_len": a.seq_len, "batch": a.batch,
-                "lr": a.lr, "layers": a.layers, "engine": "fsdp", "world": world})
+                "lr": a.lr, "layers": a.layers, "engine": "fsdp", "world": world,
+                "gdn": ops.last_impl("gdn_core")})  # the path that ran, as the reference reports it
     ok = rep["loss_last"] is not None and math.isfinite(rep["loss_last"]) and rep["weight_spread"] == 0.0
     if a.resume_selftest:
         mid = a.steps // 2

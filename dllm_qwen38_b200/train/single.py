@@ -12,6 +12,7 @@ not counting the two complementary views or the x_t||x_0 doubling (`train.py:164
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import math
 import os
@@ -255,7 +256,21 @@ def main(argv=None) -> int:
     p.add_argument("--out", default=None)
     p.add_argument("--no-eval", action="store_true")
     p.add_argument("--threads", type=int, default=None)
+    p.add_argument("--gdn", default="native", choices=["native", "auto", "torch", "fla"],
+                   help="GDN core: native (= auto) runs the sm_100a kernels on CUDA; torch runs the fp32 torch "
+                        "chunked rule on the device (the reference's torch path, for comparison); fla is not "
+                        "part of this framework")
     a = p.parse_args(argv)
+    if a.gdn == "fla":
+        print("COULD-NOT-MEASURE --gdn fla: fla's Triton kernel is not part of this framework (the native "
+              "tcgen05 kernel replaces it); use --gdn native, or --gdn torch for the torch chunked rule",
+              file=sys.stderr)
+        return 2
+    with ops.torch_on_cuda("gdn_core") if a.gdn == "torch" else contextlib.nullcontext():
+        return _run(a)
+
+
+def _run(a) -> int:
     if a.threads:
         torch.set_num_threads(a.threads)
     if a.seq_len % a.block:

@@ -154,3 +154,13 @@ def test_chat_batches_stop_when_the_split_cannot_fill_a_batch(monkeypatch):
     _fake_datasets(monkeypatch, [{"other": 1}])
     with pytest.raises(RuntimeError):
         next(chat_batches("x", "train", _FakeTok(), B=1, L=16, block=4, seed=0))
+
+
+def test_gdn_path_flag_refuses_fla_before_any_work(capsys):
+    """`--gdn` takes the reference's choices; fla (a Triton kernel this framework replaces) is
+    refused with the could-not-measure exit code before a model is built."""
+    from dllm_qwen38_b200.train import fsdp_train, single
+
+    assert single.main(["--gdn", "fla"]) == 2
+    assert fsdp_train.main(["--gdn", "fla"]) == 2
+    assert "COULD-NOT-MEASURE --gdn fla" in capsys.readouterr().err

@@ -3,13 +3,12 @@
 Semantics match the reference's optimizer (`train.py:140`: AdamW betas (0.9, 0.95), weight decay
 0; `train.py:160` clip_grad_norm_ 1.0; clip coefficient max_norm / (total + 1e-6) clamped at 1,
 `fsdp_train.py:224-252`). Differences by design: bf16 parameters get an fp32 master copy and
-fp32 moments (the reference steps bf16 params with bf16 moments); on CUDA the whole update is one
-fused kernel over a flat buffer (``csrc/adamw.cu``).
+fp32 moments (the reference steps bf16 params with bf16 moments); on CUDA each parameter's update
+(clip scale, moments, master step, bf16 write-back) is one fused kernel (``csrc/misc.cu``,
+``adamw_step``); the sharded engine runs the same kernel once per unit over its flat shard.
 """
 
 from __future__ import annotations
-
-import math
 
 import torch
 
@@ -83,7 +82,3 @@ class MasterAdamW:
         for dst, src in zip(self.master, sd["master"]):
             if dst is not None and src is not None:
                 dst.copy_(src)
-
-
-def lr_is_finite(x: float) -> bool:
-    return math.isfinite(x)

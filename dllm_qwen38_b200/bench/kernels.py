@@ -402,8 +402,28 @@ def op_embed(a):
     return fn, 1.0 * ids.numel() * D, ids.numel() * D * (2 + 2 + 2 + 8)
 
 
+def op_embed_sorted(a):
+    """embedding-table gradient as sorted per-id sums straight into a bf16 [vocab, 5120] gradient
+    (`_C.embed_bwd_sorted`, the one-rank untied path): --rows token rows (default B x 2L x 2, the
+    two views of both streams), of which --run carry one id (the mask token fills about half of
+    the noised rows, so its run is the longest one)"""
+    from ..ops import cuda as Cu
+
+    D, N = 5120, a.B * 4 * a.L if a.rows == 8192 else a.rows
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ids = torch.randint(0, a.vocab - 1, (N,), device="cuda", generator=g)
+    ids[: min(a.run, N)] = a.vocab - 1
+    dh = torch.randn(N, D, device="cuda", generator=g).bfloat16()
+    grad = torch.zeros(a.vocab, D, device="cuda", dtype=torch.bfloat16)
+    sid, perm = torch.sort(ids, stable=True)
+
+    def fn():
+        Cu._C.embed_bwd_sorted(grad, sid, perm, dh)
+    return fn, 1.0 * N * D, N * D * 2 + N * 16 + torch.unique(ids).numel() * D * 2
+
+
 OPS = {"gemm": op_gemm, "swiglu": op_swiglu, "rmsnorm_bwd": op_rmsnorm_bwd, "gdn": op_gdn, "gdn_fwd": op_gdn_fwd, "attn": op_attn, "attn_fwd": op_attn_fwd, "ce": op_ce, "conv": op_conv, "rmsnorm": op_rmsnorm, "qknorm": op_qknorm, "gnorm": op_gnorm,
-       "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed,
+       "dswiglu": op_dswiglu, "gates": op_gates, "decode": op_decode, "embed": op_embed, "embed_sorted": op_embed_sorted,
        "adamw": op_adamw}
 
 
@@ -421,6 +441,7 @@ def main(argv=None) -> int:
     p.add_argument("--rows", type=int, default=8192)
     p.add_argument("--D", type=int, default=5120)
     p.add_argument("--vocab", type=int, default=248320)
+    p.add_argument("--run", type=int, default=8000, help="embed_sorted: rows that carry one id")
     p.add_argument("--n", type=int, default=400_000_000)
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)

@@ -36,7 +36,6 @@ import argparse
 import datetime
 import faulthandler
 import json
-import math
 import os
 import sys
 import time

@@ -32,6 +32,7 @@ def _count() -> None:
 
     cuda.LAUNCHES[0] += 1
 
+
 HEADER_BYTES = 64 * 1024
 SLOT_EPOCH = 0
 

@@ -21,10 +21,8 @@ import time
 
 import torch
 
-from ..config import preset
 from ..infer.golden import generate
 from ..models.blockdiff import block_diffusion_forward
-from ..models.qwen35 import build_model
 from .. import ops
 from .objective import complementary_step_inputs, masked_ce_from_hidden
 from .optim import MasterAdamW

@@ -124,6 +124,9 @@ def main(argv=None) -> int:
     p.add_argument("--change-floor", type=float, default=None, help="default 10 x tol")
     p.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
     p.add_argument("--device", default="cpu")
+    p.add_argument("--attn", default="native", choices=["native", "sdpa", "eager"],
+                   help="candidate attention on a GPU: native (sm_100a kernel) or torch's attention over "
+                        "the boolean mask (sdpa / eager); on the CPU the candidate runs the fp32 torch ops")
     p.add_argument("--oracle-gdn", default="recurrent", choices=["recurrent", "chunk"])
     p.add_argument("--oracle-device", default=None, help="where the fp32 oracle runs (default: --device)")
     p.add_argument("--seed", type=int, default=0)
@@ -150,12 +153,11 @@ def main(argv=None) -> int:
     odev = a.oracle_device or a.device
     if a.device != "cpu" or dtype != torch.float32:  # the oracle: fp32 reference ops on its own copy
         oracle_model = copy.deepcopy(model).to(odev, torch.float32)
-    import contextlib
-
     from . import ops
 
     # the sm_100a kernels compute in bf16: an fp32 gate on a GPU runs the fp32 torch ops there
-    ctx = ops.torch_on_cuda(*ops.ALL_OPS) if (a.device != "cpu" and dtype == torch.float32) else contextlib.nullcontext()
+    ctx = ops.torch_on_cuda(*ops.ALL_OPS) if (a.device != "cpu" and dtype == torch.float32) else \
+        ops.torch_paths(attn=a.attn)
     with ctx:
         rep = run(model, block=a.block, nblocks=a.nblocks, layers=None, tol=tol, change_floor=floor, seed=a.seed,
                   device=a.device, oracle_model=oracle_model, batch=a.batch, oracle_gdn=a.oracle_gdn)

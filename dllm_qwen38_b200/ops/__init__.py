@@ -79,6 +79,21 @@ class torch_on_cuda:
         return False
 
 
+GDN_CHOICES = ("native", "auto", "torch")
+ATTN_CHOICES = ("native", "sdpa", "eager")
+
+
+def torch_paths(gdn: str = "native", attn: str = "native") -> torch_on_cuda:
+    """The command lines' `--gdn` / `--attn` choices (the reference's flags, `train.py:220-221`,
+    `equivalence.py:172`) as one context: gdn 'torch' runs the GDN core through the fp32 torch
+    chunked rule on the device; attn 'sdpa' or 'eager' runs the masked attention through torch's
+    scaled_dot_product_attention over the boolean complementary mask (one torch path stands for
+    both). 'native' / 'auto' keep the sm_100a kernels. Host tensors take the torch path anyway."""
+    if gdn not in GDN_CHOICES or attn not in ATTN_CHOICES:
+        raise ValueError(f"gdn must be one of {GDN_CHOICES}, attn one of {ATTN_CHOICES}")
+    return torch_on_cuda(*((("gdn_core",) if gdn == "torch" else ()) + (("attention",) if attn != "native" else ())))
+
+
 def use_native(*tensors: torch.Tensor, op: str | None = None) -> bool:
     """True when the op must run the CUDA kernel (any CUDA input). Raises if the extension is not
     built. An op listed in ``ops.cuda.TORCH_ON_CUDA`` has no kernel yet: it runs the reference on

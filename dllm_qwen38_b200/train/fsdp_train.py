@@ -20,7 +20,6 @@ Exit codes: 0 ok, 1 a gate failed, 2 could not measure.
 from __future__ import annotations
 
 import argparse
-import contextlib
 import datetime
 import json
 import math
@@ -179,6 +178,9 @@ def main(argv=None) -> int:
                    help="GDN core: native (= auto) runs the sm_100a kernels; torch runs the fp32 torch "
                         "chunked rule on the device (the reference's default path, for comparison); fla is "
                         "not part of this framework")
+    p.add_argument("--attn", default="native", choices=list(ops.ATTN_CHOICES),
+                   help="masked attention: native runs the sm_100a kernels; sdpa / eager run torch's "
+                        "attention over the boolean mask on the device (for comparison)")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--out", default=None)
     p.add_argument("--ckpt-dir", default=None)
@@ -199,8 +201,8 @@ def main(argv=None) -> int:
               "tcgen05 kernel replaces it); use --gdn native, or --gdn torch for the torch chunked rule",
               file=sys.stderr)
         return 2
-    # the torch GDN path on the device for the whole run (host tensors take it anyway)
-    with ops.torch_on_cuda("gdn_core") if a.gdn == "torch" else contextlib.nullcontext():
+    # the chosen GDN / attention paths for the whole run
+    with ops.torch_paths(a.gdn, a.attn):
         return _run(a)
 
 
@@ -234,7 +236,7 @@ def _run(a) -> int:
                        mem_history=a.mem_history, log=say)
     rep.update({"model": a.model, "data": a.data, "block": a.block, "seq_len": a.seq_len, "batch": a.batch,
                 "lr": a.lr, "layers": a.layers, "engine": "fsdp", "world": world,
-                "gdn": ops.last_impl("gdn_core")})  # the path that ran, as the reference reports it
+                "gdn": ops.last_impl("gdn_core"), "attn": ops.last_impl("attention")})  # the paths that ran
     ok = rep["loss_last"] is not None and math.isfinite(rep["loss_last"]) and rep["weight_spread"] == 0.0
     if a.resume_selftest:
         mid = a.steps // 2

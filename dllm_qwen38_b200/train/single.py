@@ -12,7 +12,6 @@ not counting the two complementary views or the x_t||x_0 doubling (`train.py:164
 from __future__ import annotations
 
 import argparse
-import contextlib
 import json
 import math
 import os
@@ -258,13 +257,16 @@ def main(argv=None) -> int:
                    help="GDN core: native (= auto) runs the sm_100a kernels on CUDA; torch runs the fp32 torch "
                         "chunked rule on the device (the reference's torch path, for comparison); fla is not "
                         "part of this framework")
+    p.add_argument("--attn", default="native", choices=list(ops.ATTN_CHOICES),
+                   help="masked attention: native runs the sm_100a kernels; sdpa / eager run torch's "
+                        "attention over the boolean mask on the device (for comparison)")
     a = p.parse_args(argv)
     if a.gdn == "fla":
         print("COULD-NOT-MEASURE --gdn fla: fla's Triton kernel is not part of this framework (the native "
               "tcgen05 kernel replaces it); use --gdn native, or --gdn torch for the torch chunked rule",
               file=sys.stderr)
         return 2
-    with ops.torch_on_cuda("gdn_core") if a.gdn == "torch" else contextlib.nullcontext():
+    with ops.torch_paths(a.gdn, a.attn):
         return _run(a)
 
 

@@ -164,3 +164,17 @@ def test_gdn_path_flag_refuses_fla_before_any_work(capsys):
     assert single.main(["--gdn", "fla"]) == 2
     assert fsdp_train.main(["--gdn", "fla"]) == 2
     assert "COULD-NOT-MEASURE --gdn fla" in capsys.readouterr().err
+
+
+def test_torch_paths_maps_the_reference_flags_to_op_families():
+    from dllm_qwen38_b200 import ops
+
+    assert ops.torch_paths().ops == set()
+    assert ops.torch_paths(gdn="auto", attn="native").ops == set()
+    assert ops.torch_paths(gdn="torch").ops == {"gdn_core"}
+    assert ops.torch_paths(attn="sdpa").ops == ops.torch_paths(attn="eager").ops == {"attention"}
+    with ops.torch_paths(gdn="torch", attn="sdpa"):
+        assert ops._LEVERS == {"gdn_core", "attention"}
+    assert ops._LEVERS == set()
+    with pytest.raises(ValueError):
+        ops.torch_paths(gdn="fla")

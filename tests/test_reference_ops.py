@@ -78,3 +78,13 @@ def test_kernel_diff_refuses_without_the_native_kernel():
     g = torch.zeros(1, 64, 1)
     with pytest.raises(RuntimeError, match="cannot run"):
         kernel_diff.core_diff(q, q, q, g, g, 32, 32)
+
+
+def test_no_states_requested_gives_the_same_output_and_no_states():
+    """Without `state_every` the chunked rule returns the same output and no snapshots (the
+    reference's need_states=False contract, `gdn.py:57,112,118-123`)."""
+    q, k, v, g, b = _gdn_inputs()
+    o_with, st = ref.chunk_gated_delta_rule(q, k, v, g, b, 8, state_every=8)
+    o_without, none = ref.chunk_gated_delta_rule(q, k, v, g, b, 8)
+    assert none is None and st is not None
+    assert torch.equal(o_with, o_without)

@@ -55,3 +55,26 @@ def test_lever_legs_name_real_op_families():
     for _, off, opts in LEGS:
         assert set(off) <= set(ops.ALL_OPS), off
         assert set(opts) <= {"checkpointing", "batch_mult"}
+
+
+def test_step_model_gemm_work_matches_the_bench_flop_count():
+    """The speed-of-light model's GEMM FLOPs (all GEMM outputs kept) agree with the FLOPs the
+    bench's MFU divides by, less its attention term; not keeping a layer adds its forward again."""
+    import importlib.util
+    import os
+
+    from dllm_qwen38_b200.bench.step_model import dense_params, step_work
+    from dllm_qwen38_b200.config import preset
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    spec = importlib.util.spec_from_file_location("bench_main", os.path.join(root, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = preset("27b", layers=16)
+    L = 4096
+    work = step_work(cfg, L, 32, kept=16)
+    n_attn = sum(1 for t in cfg.layer_types if t == "full_attention")
+    bench_gemm = bench.model_flops_per_step(cfg, L, 1) - 12.0 * cfg.head_dim * cfg.num_attention_heads * L * L * 2 * n_attn
+    assert abs(work["GEMM (tcgen05)"][0] / bench_gemm - 1) < 0.01
+    fewer = step_work(cfg, L, 32, kept=15)["GEMM (tcgen05)"][0] - work["GEMM (tcgen05)"][0]
+    assert fewer == 2 * 4 * L * dense_params(cfg, cfg.layer_types[15])

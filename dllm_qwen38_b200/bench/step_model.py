@@ -25,9 +25,15 @@ Counted work (no kernel detail, only what the math needs):
   CE rows    the [L, V] bf16 logits read twice and written once: 6 L V bytes.
   embedding  the backward's [R, D] row gradients read once and the table rows written once
              (at most min(R, V) distinct ids; all V when R >= V).
+  GDN core   the larger of two floors. FLOPs of the chunk algebra per (chunk of C tokens, v-head)
+             with Dk = Dv = D: 6 C D^2 (W S, Q S, the state update) + 10 C^2 D (K K^T, T V, T K,
+             Q K^T, its product with V') + 2/3 C^3 (the triangular inverse) for a clean chunk, less
+             the state update for a noised block; backward twice the forward. Bytes: q, k, v, g,
+             beta read and o written forward; those inputs, dO read and dq, dk, dv, dg, dbeta written
+             backward (no saved states counted).
 
-The GDN core and the causal conv are left out on purpose: their operands are small matrices in
-a long dependency chain, so neither FLOPs nor bytes bound them (their kernels are profiled in
+The causal conv is left out; the GDN floor ignores that each head's chunks form a chain of L / C
+dependent steps, which is what actually bounds its kernels (their per-phase profile is in
 `profiles/gdn_tc_27b_shapes.md`).
 """
 
@@ -91,9 +97,19 @@ def step_work(cfg, L: int, block: int, kept: int) -> dict:
     swiglu_b = 10.0 * R * F * len(kinds)
     ce_b = 6.0 * L * V
     embed_b = 2.0 * R * D + 2.0 * min(R, V) * D
+    n_gdn = sum(1 for k in kinds if k == "linear_attention")
+    C, Dg, Hv, Hk = block, cfg.linear_key_head_dim, cfg.linear_num_value_heads, cfg.linear_num_key_heads
+    clean = 6 * C * Dg * Dg + 10 * C * C * Dg + (2 / 3) * C ** 3
+    noised = clean - 2 * C * Dg * Dg
+    per_view = (L // C) * Hv * (clean + noised)
+    gdn_f = 3 * 2 * per_view * n_gdn  # two views, forward + backward (twice the forward)
+    T2 = 2 * L  # tokens per view
+    io_fwd = T2 * (2 * Hk * Dg * 2 + Hv * Dg * 2 + 2 * Hv * 4 + Hv * Dg * 2)  # q, k, v, g, beta in; o out
+    io_bwd = io_fwd + T2 * (2 * Hk * Dg * 2 + Hv * Dg * 2 + 2 * Hv * 4)  # + dq, dk, dv, dg, dbeta
+    gdn_b = 2 * (io_fwd + io_bwd) * n_gdn
     return {"GEMM (tcgen05)": (gemm, 0.0), "attention": (attn, 0.0), "AdamW": (0.0, adamw_b),
             "norms": (0.0, norm_b), "SwiGLU element-wise": (0.0, swiglu_b), "CE rows": (0.0, ce_b),
-            "embedding": (0.0, embed_b)}
+            "embedding": (0.0, embed_b), "GDN core": (gdn_f, gdn_b)}
 
 
 def main(argv=None) -> int:
@@ -116,10 +132,11 @@ def main(argv=None) -> int:
           f"({pk['source']}): {pk['tflops']:.1f} TF/s bf16 sustained, {pk['gbs']:.1f} GB/s copy")
     total = 0.0
     for fam, (flops, byts) in work.items():
-        ms = 1e3 * (flops / (pk["tflops"] * 1e12) if flops else byts / (pk["gbs"] * 1e9))
+        ms = 1e3 * max(flops / (pk["tflops"] * 1e12), byts / (pk["gbs"] * 1e9))
         total += ms
-        what = f"{flops / 1e12:9.2f} TFLOP" if flops else f"{byts / 1e9:9.2f} GB   "
-        print(f"  {ms:9.2f} ms  {what}  {fam}")
+        what = "  ".join(x for x in (f"{flops / 1e12:7.2f} TFLOP" if flops else "",
+                                     f"{byts / 1e9:7.2f} GB" if byts else "") if x)
+        print(f"  {ms:9.2f} ms  {what:24s}  {fam}")
     print(f"  {total:9.2f} ms  total of the modelled families")
     return 0
 

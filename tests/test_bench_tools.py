@@ -78,3 +78,13 @@ def test_step_model_gemm_work_matches_the_bench_flop_count():
     assert abs(work["GEMM (tcgen05)"][0] / bench_gemm - 1) < 0.01
     fewer = step_work(cfg, L, 32, kept=15)["GEMM (tcgen05)"][0] - work["GEMM (tcgen05)"][0]
     assert fewer == 2 * 4 * L * dense_params(cfg, cfg.layer_types[15])
+
+
+def test_step_model_gdn_floor_scales_with_gdn_layers():
+    from dllm_qwen38_b200.bench.step_model import step_work
+    from dllm_qwen38_b200.config import preset
+
+    w16 = step_work(preset("27b", layers=16), 4096, 32, kept=16)["GDN core"]
+    w8 = step_work(preset("27b", layers=8), 4096, 32, kept=8)["GDN core"]
+    assert 3.4e12 < w16[0] < 3.6e12 and w16[1] > 0
+    assert abs(w16[0] / w8[0] - 2.0) < 1e-9 and abs(w16[1] / w8[1] - 2.0) < 1e-9  # 12 vs 6 GDN layers

@@ -2,8 +2,9 @@
 
 Every op has exactly two implementations: the hand-written sm_100a kernel (``csrc/``, loaded
 through ``ops._native``) for CUDA tensors, and the fp32 PyTorch reference (``ops.reference``)
-for CPU tensors. There is no third path and no silent fallback: a CUDA tensor reaching an op
-whose extension is not built raises. Which path ran is recorded per op (``last_impl``), the
+for CPU tensors. There is no silent fallback: a CUDA tensor reaching an op whose extension is
+not built raises, and torch runs on the device only where a caller asks for it by name
+(`torch_on_cuda`, `torch_paths`: the lever benchmark, the fp32 gate on a GPU, `--gdn torch`). Which path ran is recorded per op (``last_impl``), the
 same contract as the reference's ``gdn.last_impl`` (`gdn.py:22-45`): reports name the path
 they measured instead of assuming it.
 """
@@ -37,7 +38,7 @@ def _record_ref(op: str) -> None:
 def last_impl(op: str | None = None):
     """Which implementation each op used on its most recent call: 'native' (sm_100a kernel),
     'reference' (fp32 torch on the host) or 'torch-cuda' (torch on the device: an op whose kernel
-    is not written yet)."""
+    is not written yet, or one routed there by `torch_on_cuda` / `torch_paths` for comparison)."""
     return dict(_LAST) if op is None else _LAST.get(op)
 
 

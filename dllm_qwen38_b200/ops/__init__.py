@@ -62,8 +62,8 @@ ALL_OPS = ("rmsnorm", "linear", "mlp", "gated_rmsnorm", "conv", "gdn_gates", "gd
 
 class torch_on_cuda:
     """Context manager: run the named ops through their torch path on the device (recorded as
-    'torch-cuda'). Used by the lever benchmark to measure what each native kernel buys; nothing
-    on a production path enters it."""
+    'torch-cuda'). Used by the lever benchmark to measure what each native kernel buys and by the
+    command lines' `--gdn torch` / `--attn sdpa`; no default path enters it."""
 
     def __init__(self, *ops: str):
         self.ops = set(ops)

@@ -68,3 +68,40 @@ def test_wrapper_rejects_mismatched_arguments(C, name, call, fragment):
     with pytest.raises(RuntimeError) as e:
         call(C)
     assert fragment in str(e.value), (name, str(e.value).splitlines()[0])
+
+
+def _views():
+    """Small tensors laid out like the training step's: the gate and q as strided halves of a
+    q|gate projection, the conv input as the leading columns of a wider projection row."""
+    qg = z(2, 8, 3, 32, dtype=bf)
+    q, gate = torch.split(qg, 16, dim=-1)
+    proj = z(2, 16, 48, dtype=bf)
+    return q, gate, proj[..., :32], proj[..., 32:38], proj[..., 38:44]
+
+
+ACCEPTED = [
+    ("out_gate_fwd", lambda C, v: C.out_gate_fwd(z(2, 8, 3, 16, dtype=bf), v[1])),
+    ("out_gate_bwd", lambda C, v: C.out_gate_bwd(z(2, 8, 3, 16), z(2, 8, 3, 16, dtype=bf), v[1])),
+    ("conv_fwd", lambda C, v: C.conv_fwd(v[2], z(32, 4, dtype=bf), 8, 4, 0)),
+    ("conv_bwd", lambda C, v: C.conv_bwd(z(2, 16, 32, dtype=bf), v[2], z(32, 4, dtype=bf), 8, 4, 0)),
+    ("dswiglu", lambda C, v: C.dswiglu(z(10, 16), z(10, 32, dtype=bf))),
+    ("swiglu_act", lambda C, v: C.swiglu_act(z(2, 5, 32, dtype=bf))),
+    ("ce_rows_", lambda C, v: C.ce_rows_(z(4, 16, dtype=bf), z(4, dtype=torch.long))),
+    ("adamw", lambda C, v: C.adamw_step(z(8), z(8, dtype=bf), z(8, dtype=bf), z(8), z(8), 1e-3, 0.9, 0.95, 1e-8,
+                                        0.0, 1.0, z(1), 1.0, 1.0)),
+    ("embed_fwd", lambda C, v: C.embed_fwd(z(6, dtype=torch.long), z(16, 8, dtype=bf))),
+    ("embed_bwd_sorted", lambda C, v: C.embed_bwd_sorted(z(16, 8, dtype=bf), z(6, dtype=torch.long),
+                                                         z(6, dtype=torch.long), z(6, 8, dtype=bf))),
+    ("gdn_gates_fwd", lambda C, v: C.gdn_gates_fwd(v[4], v[3], z(6), z(6))),
+    ("gdn_gates_bwd", lambda C, v: C.gdn_gates_bwd(z(2, 16, 6), z(2, 16, 6), v[4], v[3], z(6), z(6))),
+    ("qk_norm_rope_fwd", lambda C, v: C.qk_norm_rope_fwd(v[0], z(16), z(8, 4, dtype=bf), z(8, 4, dtype=bf), 1e-6)),
+]
+
+
+@pytest.mark.parametrize("name,call", ACCEPTED, ids=[c[0] for c in ACCEPTED])
+def test_wrapper_accepts_the_step_layouts(C, name, call):
+    """Well-formed host tensors with the step's layouts pass every check and only stop at the CUDA
+    device guard (these tensors are on the host), so no check rejects what the engine passes."""
+    with pytest.raises(RuntimeError) as e:
+        call(C, _views())
+    assert "CUDA" in str(e.value) and "Impl" in str(e.value), (name, str(e.value).splitlines()[0])

@@ -1097,7 +1097,7 @@ __global__ void group_sum_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloa
 }
 
 at::Tensor group_sum(const at::Tensor& x_in, int64_t groups) {
-  TORCH_CHECK(x_in.is_cuda() && x_in.scalar_type() == at::kBFloat16 && x_in.dim() >= 2, "group_sum: bf16 [..., H, D]");
+  TORCH_CHECK(x_in.scalar_type() == at::kBFloat16 && x_in.dim() >= 2, "group_sum: bf16 [..., H, D]");
   auto x = vec_input(x_in);
   const int64_t D = x.size(-1), H = x.size(-2);
   TORCH_CHECK(D % 8 == 0 && groups > 0 && H % groups == 0, "group_sum: D % 8 == 0 and H divisible by groups");

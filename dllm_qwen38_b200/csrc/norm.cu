@@ -412,7 +412,7 @@ static inline bool al16(const at::Tensor& t) { return reinterpret_cast<uintptr_t
 // contiguous [rows, D] bf16 rows at a 16-byte aligned base (the kernels move rows in 16-byte
 // vectors): the input itself, or a copy when its layout or a view's offset does not allow that
 static at::Tensor vec_rows(const at::Tensor& x, int64_t D, const char* what) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, what, ": CUDA bf16 input expected");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, what, ": bf16 input expected");
   auto x2 = x.reshape({-1, D}).contiguous();
   return al16(x2) ? x2 : x2.clone();
 }
@@ -425,7 +425,7 @@ static at::Tensor fvec(const at::Tensor& w, int64_t n, const char* what) {
 }
 
 static at::Tensor rows2d(const at::Tensor& x) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16, "norm: CUDA bf16 input expected");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "norm: bf16 input expected");
   auto x2 = x.reshape({-1, x.size(-1)});
   if (x2.stride(-1) != 1 || x2.stride(0) % 8 || !al16(x2)) x2 = vec_rows(x2, x.size(-1), "norm");
   return x2;

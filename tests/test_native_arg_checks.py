@@ -95,7 +95,18 @@ ACCEPTED = [
     ("gdn_gates_fwd", lambda C, v: C.gdn_gates_fwd(v[4], v[3], z(6), z(6))),
     ("gdn_gates_bwd", lambda C, v: C.gdn_gates_bwd(z(2, 16, 6), z(2, 16, 6), v[4], v[3], z(6), z(6))),
     ("qk_norm_rope_fwd", lambda C, v: C.qk_norm_rope_fwd(v[0], z(16), z(8, 4, dtype=bf), z(8, 4, dtype=bf), 1e-6)),
+    ("rmsnorm_fwd", lambda C, v: C.rmsnorm_fwd(z(2, 16, 32, dtype=bf), z(32), 1e-6)),
+    ("rmsnorm_bwd", lambda C, v: C.rmsnorm_bwd(z(2, 16, 32), z(2, 16, 32, dtype=bf), z(32), 1e-6)),
+    ("gated_rmsnorm_fwd", lambda C, v: C.gated_rmsnorm_fwd(z(2, 8, 3, 32, dtype=bf), _z_view(), z(32), 1e-6)),
+    ("gated_rmsnorm_bwd", lambda C, v: C.gated_rmsnorm_bwd(z(2, 8, 3, 32), z(2, 8, 3, 32, dtype=bf), _z_view(),
+                                                          z(32), 1e-6)),
+    ("group_sum", lambda C, v: C.group_sum(z(2, 8, 6, 16, dtype=bf), 2)),
 ]
+
+
+def _z_view():
+    """z as GDN's projection leaves it: [B, T, H, D] columns of a wider row (token stride > H D)."""
+    return z(2, 8, 3 * 32 + 40, dtype=bf)[..., 8 : 8 + 3 * 32].reshape(2, 8, 3, 32)
 
 
 @pytest.mark.parametrize("name,call", ACCEPTED, ids=[c[0] for c in ACCEPTED])

@@ -454,7 +454,7 @@ static at::Tensor aligned_rows(const at::Tensor& t) {
 }
 
 static void check_qkv(const at::Tensor& t, int64_t D) {
-  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 4, "attn: bf16 [B, T2, H, D]");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.dim() == 4, "attn: bf16 [B, T2, H, D]");
   TORCH_CHECK(t.stride(3) == 1 && t.stride(2) == D && t.stride(0) == t.size(1) * t.stride(1),
               "attn: heads packed in a token row, batch and token dims mergeable");
   TORCH_CHECK(t.stride(1) % 8 == 0 && reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0,
@@ -535,7 +535,8 @@ static at::Tensor prefix_t(const at::Tensor& q, const at::Tensor& k, const at::T
                   k.size(3) == D && v.size(3) == D,
               "attn_prefix: shapes");
   for (const at::Tensor* t : {&q, &k, &v})
-    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4, "attn_prefix: bf16 [B, T, H, D]");
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 4, "attn_prefix: bf16 [B, T, H, D]");
+  c10::cuda::CUDAGuard guard(q.device());
   auto o = at::empty({a.B, a.T2, a.Hq, D}, q.options());
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   a.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
@@ -568,6 +569,7 @@ template <int D>
 static std::vector<at::Tensor> fwd_t(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L,
                                      int64_t block, double scale, bool leak) {
   Args a = make_args(q, k, v, L, block, scale, leak);
+  c10::cuda::CUDAGuard guard(q.device());  // (after the host checks, which host tests reach)
   auto o = at::empty({a.B, a.T2, a.Hq, D}, q.options());
   auto lse = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
   if ((D == 128 || D == 256) && tc_forward_enabled() && attn_fwd_tc(q, k, v, o, lse, L, block, scale, leak))
@@ -586,6 +588,7 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
   TORCH_CHECK(dout.numel() == q.numel() && o.sizes() == q.sizes() && o.scalar_type() == at::kBFloat16 &&
                   lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == (int64_t)a.B * a.Hq * a.T2,
               "attn: dout and bf16 o of q's shape, fp32 lse [B, Hq, T2]");
+  c10::cuda::CUDAGuard guard(q.device());
   auto d = aligned_rows(dout.to(at::kBFloat16));
   auto oc = aligned_rows(o);
   auto delta = at::empty({a.B, a.Hq, a.T2}, q.options().dtype(at::kFloat));
@@ -623,7 +626,6 @@ static std::vector<at::Tensor> bwd_t(const at::Tensor& dout, const at::Tensor& q
 
 std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t L,
                                  int64_t block, double scale, bool leak) {
-  c10::cuda::CUDAGuard guard(q.device());
   ATTN_DISPATCH(fwd_t, q, k, v, L, block, scale, leak)
   return {};
 }
@@ -631,7 +633,6 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                  const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse, int64_t L,
                                  int64_t block, double scale, bool leak) {
-  c10::cuda::CUDAGuard guard(q.device());
   ATTN_DISPATCH(bwd_t, dout, q, k, v, o, lse, L, block, scale, leak)
   return {};
 }
@@ -641,7 +642,6 @@ std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, co
 namespace bdllm {
 at::Tensor attn_prefix(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, int64_t tk_host,
                        const c10::optional<at::Tensor>& tk, double scale) {
-  c10::cuda::CUDAGuard guard(q.device());
   ATTN_DISPATCH(prefix_t, q, k, v, tk_host, tk, scale)
   return {};
 }

@@ -1184,6 +1184,7 @@ static std::vector<at::Tensor> forward_t(const at::Tensor& q, const at::Tensor& 
                                          const at::Tensor& g, const at::Tensor& beta, int64_t L, int64_t C,
                                          bool concat) {
   Args a = make_args(q, k, v, g, beta, L, C, concat);
+  c10::cuda::CUDAGuard guard(q.device());  // (after the host checks, which host tests reach)
   auto f32 = q.options().dtype(at::kFloat);
   auto U = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
   auto W = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
@@ -1220,6 +1221,7 @@ static std::vector<at::Tensor> rows_t(const at::Tensor& q, const at::Tensor& k, 
   Args a = make_args(q, k, v, g, beta, T / 2, C, true);
   TORCH_CHECK(S0.is_contiguous() && S0.scalar_type() == at::kFloat && S0.numel() == (int64_t)a.B * a.Hv * Dk * Dv,
               "gdn_rows: S0 fp32 [B, Hv, Dk, Dv]");
+  c10::cuda::CUDAGuard guard(q.device());
   auto f32 = q.options().dtype(at::kFloat);
   auto U = at::empty({a.B, a.nb, a.Hv, C, Dv}, f32);
   auto W = at::empty({a.B, a.nb, a.Hv, C, Dk}, f32);
@@ -1262,6 +1264,7 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
   TORCH_CHECK(S_in.is_contiguous() && (S_in.scalar_type() == at::kFloat || S_in.scalar_type() == at::kBFloat16) &&
                   S_in.numel() == (int64_t)a.B * a.nb * a.Hv * Dk * Dv,
               "gdn_bwd: S_in [B, nb, Hv, Dk, Dv] (fp32, or bf16 from the tensor-core forward)");
+  c10::cuda::CUDAGuard guard(q.device());
   auto d = dout.to(at::kBFloat16).contiguous();
   if (reinterpret_cast<uintptr_t>(d.data_ptr()) % 16 != 0) d = d.clone();  // read in 16-byte vectors and TMA tiles
   a.dout = reinterpret_cast<const __nv_bfloat16*>(d.data_ptr());
@@ -1403,7 +1406,6 @@ static std::vector<at::Tensor> backward_t(const at::Tensor& dout, const at::Tens
 
 std::vector<at::Tensor> gdn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                 const at::Tensor& beta, int64_t L, int64_t C, bool concat) {
-  c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(forward_t, q, k, v, g, beta, L, C, concat)
   return {};
 }
@@ -1411,7 +1413,6 @@ std::vector<at::Tensor> gdn_fwd(const at::Tensor& q, const at::Tensor& k, const 
 std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                 const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S_in, int64_t L,
                                 int64_t C, bool concat) {
-  c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(backward_t, dout, q, k, v, g, beta, S_in, L, C, concat)
   return {};
 }
@@ -1419,7 +1420,6 @@ std::vector<at::Tensor> gdn_bwd(const at::Tensor& dout, const at::Tensor& q, con
 std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                  const at::Tensor& beta, const at::Tensor& S0, const c10::optional<at::Tensor>& S_final,
                                  int64_t C) {
-  c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(rows_t, q, k, v, g, beta, S0, S_final, C)
   return {};
 }
@@ -1427,7 +1427,6 @@ std::vector<at::Tensor> gdn_rows(const at::Tensor& q, const at::Tensor& k, const
 // rows with an initial state, for training: {o, S_in} (S_in: the state entering each chunk)
 std::vector<at::Tensor> gdn_fwd_rows(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                      const at::Tensor& g, const at::Tensor& beta, const at::Tensor& S0, int64_t C) {
-  c10::cuda::CUDAGuard guard(q.device());
   GDN_DISPATCH(rows_t, q, k, v, g, beta, S0, c10::nullopt, C, true)
   return {};
 }
@@ -1438,7 +1437,6 @@ std::vector<at::Tensor> gdn_bwd_rows(const at::Tensor& dout, const at::Tensor& q
                                      const at::Tensor& v, const at::Tensor& g, const at::Tensor& beta,
                                      const at::Tensor& S_in, int64_t C, const c10::optional<at::Tensor>& inj,
                                      bool want_dS0) {
-  c10::cuda::CUDAGuard guard(q.device());
   const int64_t half = q.size(1) / 2;
   GDN_DISPATCH(backward_t, dout, q, k, v, g, beta, S_in, half, C, true, inj, want_dS0)
   return {};

@@ -956,13 +956,13 @@ bool gdn_tc_eligible(const at::Tensor& q, const at::Tensor& k, const at::Tensor&
 std::vector<at::Tensor> gdn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& g,
                                    const at::Tensor& beta, int64_t L) {
   using namespace gdn_tc;
-  c10::cuda::CUDAGuard guard(q.device());
   const int B = q.size(0), Hk = q.size(2), Hv = v.size(2);
   TORCH_CHECK(Hv % Hk == 0, "gdn_tc: Hv % Hk == 0");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16 &&
                   q.size(1) == 2 * L && k.sizes() == q.sizes() && v.size(0) == B && v.size(1) == q.size(1),
               "gdn_tc: bf16 q, k [B, 2L, Hk, 128] and v [B, 2L, Hv, 128]");
   TORCH_CHECK(g.numel() == (int64_t)B * 2 * L * Hv && beta.numel() == g.numel(), "gdn_tc: g, beta [B, 2L, Hv]");
+  c10::cuda::CUDAGuard guard(q.device());
   TORCH_CHECK(q.stride(1) == k.stride(1) && q.stride(2) == 128 && k.stride(2) == 128 && v.stride(2) == 128 &&
                   q.stride(3) == 1 && k.stride(3) == 1 && v.stride(3) == 1,
               "gdn_tc: heads packed within a token row, unit inner stride");

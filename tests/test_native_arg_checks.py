@@ -116,3 +116,69 @@ def test_wrapper_accepts_the_step_layouts(C, name, call):
     with pytest.raises(RuntimeError) as e:
         call(C, _views())
     assert "CUDA" in str(e.value) and "Impl" in str(e.value), (name, str(e.value).splitlines()[0])
+
+
+def _gdn_views(B=1, L=64, Hk=2, Hv=4, D=16):
+    """q, k, v as the state-fork GDN reads them: head-packed column blocks of the post-conv row
+    [B, 2L, 2 Hk D + Hv D]; g, beta fp32 [B, 2L, Hv]."""
+    mixed = z(B, 2 * L, 2 * Hk * D + Hv * D, dtype=bf)
+    q = mixed[..., : Hk * D].reshape(B, 2 * L, Hk, D)
+    k = mixed[..., Hk * D : 2 * Hk * D].reshape(B, 2 * L, Hk, D)
+    v = mixed[..., 2 * Hk * D :].reshape(B, 2 * L, Hv, D)
+    return q, k, v, z(B, 2 * L, Hv), z(B, 2 * L, Hv)
+
+
+def _attn_views(B=1, L=64, Hq=4, Hk=2, D=64):
+    """q, k normalised copies [B, 2L, H, D]; v a column block of the q|gate, k, v projection row."""
+    proj = z(B, 2 * L, 2 * Hq * D + 2 * Hk * D, dtype=bf)
+    v = proj[..., 2 * Hq * D + Hk * D :].reshape(B, 2 * L, Hk, D)
+    return z(B, 2 * L, Hq, D, dtype=bf), z(B, 2 * L, Hk, D, dtype=bf), v
+
+
+DEVICE_CHECKED = [
+    ("gdn_fwd", lambda C: C.gdn_fwd(*_gdn_views(), 64, 32, False)),
+    ("gdn_fwd concat", lambda C: C.gdn_fwd(*_gdn_views(), 64, 32, True)),
+    ("gdn_bwd", lambda C: C.gdn_bwd(z(1, 128, 4, 16), *_gdn_views(), z(1, 2, 4, 16, 16), 64, 32, False)),
+    ("gdn_rows", lambda C: C.gdn_rows(*_gdn_views(B=2, L=16), z(2, 4, 16, 16), None, 32)),
+    ("gdn_fwd_tc", lambda C: C.gdn_fwd_tc(*_gdn_views(L=128, D=128), 128)),
+    ("attn_fwd", lambda C: C.attn_fwd(*_attn_views(), 64, 32, 0.125, False)),
+    ("attn_bwd", lambda C: C.attn_bwd(z(1, 128, 4, 64), *_attn_views(), z(1, 128, 4, 64, dtype=bf), z(1, 4, 128),
+                                      64, 32, 0.125, False)),
+    ("attn_prefix", lambda C: C.attn_prefix(z(2, 32, 4, 64, dtype=bf), z(2, 96, 2, 64, dtype=bf),
+                                            z(2, 96, 2, 64, dtype=bf), 64, None, 0.125)),
+]
+
+
+@pytest.mark.parametrize("name,call", DEVICE_CHECKED, ids=[c[0] for c in DEVICE_CHECKED])
+def test_gdn_and_attention_wrappers_accept_the_step_layouts(C, name, call):
+    with pytest.raises(RuntimeError) as e:
+        call(C)
+    assert "CUDA" in str(e.value) and "Impl" in str(e.value), (name, str(e.value).splitlines()[0])
+
+
+def _k_with_four_heads():
+    """k read from the same row as q (same token stride) but with four heads against q's two."""
+    q, _, v, g, b = _gdn_views()
+    mixed_row = q.as_strided((1, 128, 128), (q.stride(0), q.stride(1), 1))
+    return q, mixed_row[..., 32:96].reshape(1, 128, 4, 16), v, g, b
+
+
+MISMATCHED = [
+    ("gdn k heads", lambda C: C.gdn_fwd(*_k_with_four_heads(), 64, 32, False), "q, k [B, 2L, Hk, Dk]"),
+    ("gdn gates", lambda C: C.gdn_fwd(*_gdn_views()[:3], z(1, 128, 3), z(1, 128, 3), 64, 32, False), "g, beta"),
+    ("gdn dout", lambda C: C.gdn_bwd(z(1, 64, 4, 16), *_gdn_views(), z(1, 2, 4, 16, 16), 64, 32, False),
+     "gdn_bwd: dout"),
+    ("gdn states", lambda C: C.gdn_bwd(z(1, 128, 4, 16), *_gdn_views(), z(1, 3, 4, 16, 16), 64, 32, False),
+     "gdn_bwd: S_in"),
+    ("attn v length", lambda C: C.attn_fwd(*_attn_views()[:2], z(1, 64, 2, 64, dtype=bf), 64, 32, 0.125, False),
+     "one batch, length and head dim"),
+    ("attn lse", lambda C: C.attn_bwd(z(1, 128, 4, 64), *_attn_views(), z(1, 128, 4, 64, dtype=bf), z(1, 4, 64),
+                                      64, 32, 0.125, False), "fp32 lse"),
+]
+
+
+@pytest.mark.parametrize("name,call,fragment", MISMATCHED, ids=[c[0] for c in MISMATCHED])
+def test_gdn_and_attention_wrappers_reject_mismatches(C, name, call, fragment):
+    with pytest.raises(RuntimeError) as e:
+        call(C)
+    assert fragment in str(e.value), (name, str(e.value).splitlines()[0])

@@ -182,3 +182,14 @@ def test_gdn_and_attention_wrappers_reject_mismatches(C, name, call, fragment):
     with pytest.raises(RuntimeError) as e:
         call(C)
     assert fragment in str(e.value), (name, str(e.value).splitlines()[0])
+
+
+def test_decode_conv_tail_accepts_the_engine_layout(C):
+    """The decode engine's conv input: the conv columns of the in-projection row [B, T, C] (token
+    stride wider than C), a bf16 tail [B, 3, C] and fp32 taps [C, 4]."""
+    proj = z(2, 32, 64 + 24, dtype=bf)
+    with pytest.raises(RuntimeError) as e:
+        C.conv_tail(proj[..., :64], z(2, 3, 64, dtype=bf), z(64, 4), True)
+    assert "CUDA" in str(e.value) and "Impl" in str(e.value), str(e.value).splitlines()[0]
+    with pytest.raises(RuntimeError, match="tail"):
+        C.conv_tail(proj[..., :64], z(2, 2, 64, dtype=bf), z(64, 4), True)

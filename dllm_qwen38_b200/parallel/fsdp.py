@@ -661,6 +661,13 @@ class FSDPEngine:
 # ---------------------------------------------------------------------------- autograd units
 
 
+def _count_launch() -> None:
+    """One launch of this repository's kernels, for the step's launch count."""
+    from ..ops import cuda as Cu
+
+    Cu.LAUNCHES[0] += 1
+
+
 class _EmbedFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, ids, anchor, engine):
@@ -670,6 +677,7 @@ class _EmbedFn(torch.autograd.Function):
             from ..ops import _native
 
             h = _native.require().embed_fwd(ids.contiguous(), table)
+            _count_launch()
         else:
             h = torch.nn.functional.embedding(ids, table)
         ctx.save_for_backward(ids)
@@ -695,6 +703,7 @@ class _EmbedFn(torch.autograd.Function):
 
                 sid, perm = torch.sort(flat_ids, stable=True)  # fixed summation order within a run
                 _native.require().embed_bwd_sorted(gt, sid, perm, dh.reshape(-1, D))
+                _count_launch()
             else:
                 acc = torch.zeros(V, D, dtype=torch.float32)
                 acc.index_add_(0, flat_ids, dh.reshape(-1, D).float())
@@ -706,6 +715,7 @@ class _EmbedFn(torch.autograd.Function):
             from ..ops import _native
 
             _native.require().embed_bwd_(tg, ids.reshape(-1).contiguous(), dh.reshape(-1, D))
+            _count_launch()
         else:
             tg.index_add_(0, ids.reshape(-1), dh.reshape(-1, D).float())
         engine.reduce_scatter(engine.embed, engine.table_grad)

@@ -48,8 +48,11 @@ def complementary_step_inputs(x0, prompt_len, block: int, mask_id: int, generato
     the element's (row, position)) and writes both views; otherwise torch's RNG with `generator`."""
     if seed is not None and x0.is_cuda:
         from ..ops import _native
+        from ..ops import cuda as Cu
 
-        return tuple(_native.require().mask_sample(x0, prompt_len, valid_len, block, mask_id, seed))
+        out = tuple(_native.require().mask_sample(x0, prompt_len, valid_len, block, mask_id, seed))
+        Cu.LAUNCHES[0] += 1  # one launch of this repository's kernels
+        return out
     m, mc = sample_complementary_masks(x0, prompt_len, block, generator, valid_len)
     return torch.cat([x0, x0], 0), torch.cat([apply_mask(x0, m, mask_id), apply_mask(x0, mc, mask_id)], 0), torch.cat([m, mc], 0)
 

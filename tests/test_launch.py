@@ -26,3 +26,15 @@ def test_dry_run_prints_command(capsys):
     assert launch.main(["decode", "--gpus", "2", "--dry-run", "--", "--batch", "32"]) == 0
     out = capsys.readouterr().out
     assert "torch.distributed.run" in out and "dllm_qwen38_b200.bench.decode --batch 32" in out
+
+
+def test_package_command_list_names_importable_modules(capsys):
+    import importlib
+
+    from dllm_qwen38_b200.__main__ import COMMANDS, main
+
+    assert main([]) == 0
+    out = capsys.readouterr().out
+    for cmd, _ in COMMANDS:
+        assert cmd in out
+        importlib.import_module("dllm_qwen38_b200." + cmd)  # every listed command exists

@@ -32,6 +32,13 @@ Counted work (no kernel detail, only what the math needs):
              beta read and o written forward; those inputs, dO read and dq, dk, dv, dg, dbeta written
              backward (no saved states counted).
 
+With --gpus N (the sharded engine, one sequence per GPU) the per-GPU work above stays, AdamW
+covers 1/N of the parameters, and two NVLink rows are added: every unit's parameters gathered
+twice per step (forward, and again for the backward's GEMMs) and its gradient reduce-scattered
+once, (N - 1) / N of the bf16 bytes arriving at each GPU, at the pool's measured peer copy rate
+(770 GB/s per direction). Those transfers overlap the compute, so they are a floor of their own,
+not an addition to the step's.
+
 The causal conv is left out; the GDN floor ignores that each head's chunks form a chain of L / C
 dependent steps, which is what actually bounds its kernels (their per-phase profile is in
 `profiles/gdn_tc_27b_shapes.md`).
@@ -71,8 +78,8 @@ def dense_params(cfg, kind: str) -> int:
     return n
 
 
-def step_work(cfg, L: int, block: int, kept: int) -> dict:
-    """{family: (flops, bytes)} for one step of one sequence of length L."""
+def step_work(cfg, L: int, block: int, kept: int, gpus: int = 1) -> dict:
+    """{family: (flops, bytes)} for one GPU's share of one step (one sequence of length L per GPU)."""
     D, F, V = cfg.hidden_size, cfg.intermediate_size, cfg.vocab_size
     R = 4 * L
     kinds = list(cfg.layer_types)
@@ -85,7 +92,7 @@ def step_work(cfg, L: int, block: int, kept: int) -> dict:
     pairs = block * block * nb * (nb + 1)  # per view
     n_attn = sum(1 for k in kinds if k != "linear_attention")
     attn = 2 * pairs * cfg.num_attention_heads * cfg.head_dim * (4 + 10) * n_attn
-    adamw_b = 28.0 * cfg.param_count()
+    adamw_b = 28.0 * cfg.param_count() / gpus
     norm_b = 0.0
     for kind in kinds:
         norm_b += 2 * (4 + 6) * R * D  # input and post-attention RMSNorm
@@ -112,6 +119,15 @@ def step_work(cfg, L: int, block: int, kept: int) -> dict:
             "embedding": (0.0, embed_b), "GDN core": (gdn_f, gdn_b)}
 
 
+def comm_bytes(cfg, gpus: int) -> dict:
+    """Bytes arriving at each GPU over NVLink per step of the sharded engine (bf16 parameters and
+    gradients): {'all-gather': ..., 'reduce-scatter': ...}; empty on one GPU."""
+    if gpus <= 1:
+        return {}
+    share = (gpus - 1) / gpus * 2.0 * cfg.param_count()
+    return {"FSDP all-gather (NVLink, overlapped)": 2 * share, "FSDP reduce-scatter (NVLink, overlapped)": share}
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--model", default="27b")
@@ -120,6 +136,9 @@ def main(argv=None) -> int:
     p.add_argument("--block", type=int, default=32)
     p.add_argument("--kept", type=int, default=None, help="layers whose GEMM outputs are kept (default: all)")
     p.add_argument("--peaks", default=None, help="a MEASURED_PEAKS.json (default: the repository's)")
+    p.add_argument("--gpus", type=int, default=1, help="ranks of the sharded engine (one sequence each)")
+    p.add_argument("--nvlink-gbs", type=float, default=770.0,
+                   help="peer copy GB/s per direction (the pool's measured figure)")
     a = p.parse_args(argv)
     sys.path.insert(0, ROOT)
     from ..config import preset
@@ -127,7 +146,7 @@ def main(argv=None) -> int:
     cfg = preset(a.model, layers=a.layers)
     kept = cfg.num_hidden_layers if a.kept is None else a.kept
     pk = peaks(a.peaks)
-    work = step_work(cfg, a.seq_len, a.block, kept)
+    work = step_work(cfg, a.seq_len, a.block, kept, a.gpus)
     print(f"{a.model}, {cfg.num_hidden_layers} layers, seq {a.seq_len}, GEMM outputs kept for {kept}; peaks "
           f"({pk['source']}): {pk['tflops']:.1f} TF/s bf16 sustained, {pk['gbs']:.1f} GB/s copy")
     total = 0.0
@@ -137,7 +156,9 @@ def main(argv=None) -> int:
         what = "  ".join(x for x in (f"{flops / 1e12:7.2f} TFLOP" if flops else "",
                                      f"{byts / 1e9:7.2f} GB" if byts else "") if x)
         print(f"  {ms:9.2f} ms  {what:24s}  {fam}")
-    print(f"  {total:9.2f} ms  total of the modelled families")
+    print(f"  {total:9.2f} ms  total of the modelled families (per GPU, {a.gpus} GPU{'s' if a.gpus > 1 else ''})")
+    for what, byts in comm_bytes(cfg, a.gpus).items():
+        print(f"  {1e3 * byts / (a.nvlink_gbs * 1e9):9.2f} ms  {byts / 1e9:7.2f} GB{'':15s}  {what}")
     return 0
 
 

@@ -88,3 +88,19 @@ def test_step_model_gdn_floor_scales_with_gdn_layers():
     w8 = step_work(preset("27b", layers=8), 4096, 32, kept=8)["GDN core"]
     assert 3.4e12 < w16[0] < 3.6e12 and w16[1] > 0
     assert abs(w16[0] / w8[0] - 2.0) < 1e-9 and abs(w16[1] / w8[1] - 2.0) < 1e-9  # 12 vs 6 GDN layers
+
+
+def test_step_model_sharded_engine_terms():
+    from dllm_qwen38_b200.bench.step_model import comm_bytes, step_work
+    from dllm_qwen38_b200.config import preset
+
+    cfg = preset("27b", layers=16)
+    assert comm_bytes(cfg, 1) == {}
+    c2, c8 = comm_bytes(cfg, 2), comm_bytes(cfg, 8)
+    ag2, rs2 = c2.values()
+    ag8, rs8 = c8.values()
+    assert ag2 == 2 * rs2 and ag8 == 2 * rs8
+    assert abs(rs8 / rs2 - (7 / 8) / (1 / 2)) < 1e-12  # (N - 1) / N of the bf16 parameter bytes
+    assert abs(rs2 - cfg.param_count()) < 1  # half of 2 bytes per parameter arrives at each of 2 GPUs
+    one, eight = step_work(cfg, 4096, 32, 16, 1), step_work(cfg, 4096, 32, 16, 8)
+    assert eight["AdamW"][1] * 8 == one["AdamW"][1] and eight["GEMM (tcgen05)"] == one["GEMM (tcgen05)"]
